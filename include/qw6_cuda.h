@@ -1,0 +1,122 @@
+/* qw6_cuda.h -- device-resident API of libqw6cuda (B200 / sm_100a).
+ *
+ * The per-call qw6_vk_*_host entry points (qw6_vk.h) copy everything from
+ * and to host memory on every call.  This API is the persistent form the
+ * reference's pipeline uses (weights uploaded once, qw6_vk.c:2920-2958; one
+ * queue): a context owns a CUDA stream and a grow-only workspace, all
+ * tensors are DEVICE pointers, and calls only enqueue work on the context's
+ * stream (synchronize with qw6cu_synchronize).  No torch or C++ types cross
+ * this boundary.  Every function returns 0 or a negative error code;
+ * qw6cu_last_error() gives a message for the calling thread.
+ *
+ * Quant codes are qw6's qw6_quant_t values (qw6.h:77-92): Q4_K_M 4,
+ * Q4_K_S 5, Q5_K 6, Q6_K 7, IQ3_S 9, IQ2_S 11, IQ2_XXS 13.
+ *
+ * Weights for the quantized kernels live in the PACKED TILE layout: the
+ * GGUF super-blocks of every 16 consecutive rows, byte-permuted so that
+ * each GPU lane fetches its tensor-core fragments with 16-byte loads.  The
+ * permutation has the same size as the raw bytes, except that the row count
+ * is rounded up to a multiple of 16 (qw6cu_packed_bytes).  qw6cu_pack
+ * converts raw GGUF rows already on the device.
+ */
+#ifndef QW6_CUDA_H
+#define QW6_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QW6CU_OK 0
+#define QW6CU_ERR_ARG (-2)     /* bad shape / pointer / unsupported option */
+#define QW6CU_ERR_QUANT (-3)   /* quant type not handled */
+#define QW6CU_ERR_CUDA (-4)    /* CUDA runtime or launch failure */
+#define QW6CU_ERR_ALIGN (-5)   /* pointer or stride not 16-byte aligned */
+#define QW6CU_ERR_TIMEOUT (-6) /* a bounded device-side wait gave up */
+#define QW6CU_ERR_NOMEM (-7)   /* device allocation failed */
+
+typedef struct qw6cu_ctx qw6cu_ctx;
+
+/* Message describing the last error of the calling thread. */
+const char *qw6cu_last_error(void);
+
+/* Create a context on `device` (-1: $QW6_CUDA_DEVICE, else 0) with its own
+ * non-blocking stream. */
+int qw6cu_create(qw6cu_ctx **out, int device);
+void qw6cu_destroy(qw6cu_ctx *ctx);
+/* Make the context enqueue on an external cudaStream_t (NULL: its own). */
+int qw6cu_set_stream(qw6cu_ctx *ctx, void *stream);
+void *qw6cu_get_stream(qw6cu_ctx *ctx);
+int qw6cu_synchronize(qw6cu_ctx *ctx);
+
+/* ---- weights ---- */
+
+/* Bytes of the packed tile layout of one rows x cols matrix (0: invalid). */
+size_t qw6cu_packed_bytes(uint32_t quant, uint32_t rows, uint32_t cols);
+
+/* Pack `count` matrices: raw GGUF matrix i at raw + i*raw_stride, packed i
+ * written at packed + i*packed_stride (packed_stride >= packed_bytes). */
+int qw6cu_pack(qw6cu_ctx *ctx, uint32_t quant, const void *raw, void *packed, uint32_t rows, uint32_t cols,
+               uint32_t count, size_t raw_stride, size_t packed_stride);
+
+/* out[rows x cols] fp32 = exact dequantization of RAW GGUF rows, bit-equal
+ * to qw6_tensor_dequantize_row (qw6.c:1674-1724). */
+int qw6cu_dequantize(qw6cu_ctx *ctx, uint32_t quant, const void *raw, float *out, uint32_t rows, uint32_t cols);
+
+/* ---- matvec ---- */
+
+/* y[t*rows + r] = W[r] . x[t*cols ...] for t < ntok (1..32), W packed.
+ * x must be 16-byte aligned. */
+int qw6cu_matvec(qw6cu_ctx *ctx, uint32_t quant, const void *packed, const float *x, float *y, uint32_t rows,
+                 uint32_t cols, uint32_t ntok);
+
+/* fp32 weights, row-major rows x cols, one token. */
+int qw6cu_matvec_f32(qw6cu_ctx *ctx, const float *w, const float *x, float *y, uint32_t rows, uint32_t cols);
+
+/* ---- MoE pieces ---- */
+
+/* Per token t: indices idx[t*top_k ..] and softmax weights w[t*top_k ..]
+ * of the top_k largest of logits[t*n_experts ..] (n_experts <= 256,
+ * top_k <= 32); ties go to the lower expert index (qw6.c:2796-2827). */
+int qw6cu_moe_route(qw6cu_ctx *ctx, const float *logits, uint32_t ntok, uint32_t n_experts, uint32_t top_k,
+                    int32_t *idx, float *w);
+int qw6cu_silu_mul(qw6cu_ctx *ctx, const float *gate, const float *up, float *out, uint32_t n);
+int qw6cu_moe_gather(qw6cu_ctx *ctx, const float *expert_out, const float *w, const float *shared_out,
+                     float shared_weight, float *out, uint32_t dim, uint32_t top_k);
+/* argmax with qw6_cpu_argmax semantics; idx/val are device pointers. */
+int qw6cu_argmax(qw6cu_ctx *ctx, const float *x, uint32_t n, uint32_t *idx, float *val);
+
+/* ---- routed MoE FFN (decode batches) ---- */
+
+/* One GGUF expert pack in the packed tile layout: expert e's matrix starts at
+ * base + e*stride (qw6's bind_expert_pack keeps experts at a fixed stride,
+ * qw6.c:542-597).  quant is the pack's qw6_quant_t. */
+typedef struct {
+    uint32_t quant;
+    const void *base;
+    size_t stride;
+} qw6cu_expert_pack;
+
+/* out[t] = sum over the top_k experts e of token t (routing of
+ * logits[t*n_experts ..], qw6.c:2796-2827) of w_e * down_e(silu(gate_e x_t) *
+ * up_e x_t), composed as qw6_apply_layer_moe (qw6.c:2246-2264) without the
+ * shared expert.  gate/up are [inter x hidden], down [hidden x inter];
+ * gate and up must share one quant type.  ntok * top_k <= 4096; hidden and
+ * inter multiples of 512, hidden <= 4096; n_experts <= 256.  Routing,
+ * grouping and the expert matvecs all run on the device (no host sync).
+ * Uses the context workspace (grown on first use, which synchronizes). */
+int qw6cu_moe_decode(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
+                     const qw6cu_expert_pack *down, const float *logits, const float *x, float *out, uint32_t ntok,
+                     uint32_t hidden, uint32_t inter, uint32_t n_experts, uint32_t top_k);
+
+/* Device workspace qw6cu_moe_decode needs for these dimensions. */
+size_t qw6cu_moe_workspace_bytes(uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t n_experts,
+                                 uint32_t top_k);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QW6_CUDA_H */

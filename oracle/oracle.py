@@ -1,0 +1,249 @@
+"""ctypes front-end of the CPU checkers.  TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg import
+this module.  Two checkers are exposed with the same call shapes:
+
+* ``Oracle()``     -- liboracle.so, the C restatement of qw6's CPU path.
+* ``Reference()``  -- oracle/_ref/libqw6ref.so, qw6's own qw6.c compiled
+                      from its sources (present when it was built here).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ORACLE_SO = HERE / "liboracle.so"
+REF_SO = HERE / "_ref" / "libqw6ref.so"
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C")
+_f64p = np.ctypeslib.ndpointer(np.float64, flags="C")
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C")
+
+
+def build() -> None:
+    """Build liboracle.so (and _ref when the reference tree is present)."""
+    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+
+
+def _load(path: Path) -> C.CDLL:
+    if not path.exists():
+        build()
+    return C.CDLL(str(path))
+
+
+def _u8(a: np.ndarray) -> np.ndarray:
+    a = np.ascontiguousarray(a)
+    return a.view(np.uint8) if a.dtype != np.uint8 else a
+
+
+class _ExpertPack(C.Structure):
+    _fields_ = [("quant", C.c_uint32), ("base", C.c_void_p), ("stride", C.c_size_t)]
+
+
+class Oracle:
+    """C restatement (qw6_oracle.c)."""
+
+    kind = "port"
+
+    def __init__(self) -> None:
+        lib = _load(ORACLE_SO)
+        lib.qo_dequantize_row.argtypes = [C.c_uint32, C.c_void_p, C.c_uint32, C.c_uint32, _f32p]
+        lib.qo_matvec.argtypes = [C.c_uint32, C.c_void_p, _f32p, _f32p, C.c_uint32, C.c_uint32]
+        lib.qo_matvec_f64.argtypes = [C.c_uint32, C.c_void_p, _f32p, _f64p, C.c_uint32, C.c_uint32]
+        lib.qo_matvec_batch.argtypes = [C.c_uint32, C.c_void_p, _f32p, _f32p, C.c_uint32,
+                                        C.c_uint32, C.c_uint32]
+        lib.qo_moe_route.argtypes = [_f32p, C.c_uint32, C.c_uint32, _i32p, _f32p]
+        lib.qo_argmax.argtypes = [_f32p, C.c_uint32]
+        lib.qo_argmax.restype = C.c_int32
+        lib.qo_fp16_to_f32.argtypes = [C.c_uint16]
+        lib.qo_fp16_to_f32.restype = C.c_float
+        lib.qo_moe_gather.argtypes = [_f32p, _f32p, C.c_void_p, C.c_float, _f32p, C.c_uint32, C.c_uint32]
+        lib.qo_silu_mul.argtypes = [_f32p, _f32p, _f32p, C.c_uint32]
+        pk = C.POINTER(_ExpertPack)
+        lib.qo_moe_layer.argtypes = [pk, pk, pk, _f32p, _f32p, _f32p, C.c_uint32, C.c_uint32,
+                                     C.c_uint32, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p]
+        lib.qo_moe_layer_f64.argtypes = [pk, pk, pk, _f32p, _f32p, _f64p, C.c_uint32, C.c_uint32,
+                                         C.c_uint32, C.c_uint32, C.c_uint32]
+        self.lib = lib
+
+    def fp16_to_f32(self, h: int) -> float:
+        return self.lib.qo_fp16_to_f32(h)
+
+    def dequantize(self, quant: int, w: np.ndarray, rows: int, cols: int) -> np.ndarray:
+        w = _u8(w)
+        out = np.empty((rows, cols), np.float32)
+        for r in range(rows):
+            if self.lib.qo_dequantize_row(quant, w.ctypes.data, cols, r, out[r]):
+                raise ValueError("dequantize_row failed")
+        return out
+
+    def matvec(self, quant: int, w: np.ndarray, x: np.ndarray, rows: int, cols: int) -> np.ndarray:
+        w = _u8(w)
+        x = np.ascontiguousarray(x, np.float32).reshape(-1)
+        ntok = x.size // cols
+        y = np.empty(ntok * rows, np.float32)
+        if self.lib.qo_matvec_batch(quant, w.ctypes.data, x, y, rows, cols, ntok):
+            raise ValueError("matvec failed")
+        return y.reshape(ntok, rows) if ntok > 1 else y
+
+    def matvec_f64(self, quant: int, w: np.ndarray, x: np.ndarray, rows: int, cols: int) -> np.ndarray:
+        w = _u8(w)
+        x = np.ascontiguousarray(x, np.float32).reshape(-1)
+        y = np.empty(rows, np.float64)
+        if self.lib.qo_matvec_f64(quant, w.ctypes.data, x, y, rows, cols):
+            raise ValueError("matvec_f64 failed")
+        return y
+
+    def moe_route(self, logits: np.ndarray, top_k: int):
+        logits = np.ascontiguousarray(logits, np.float32)
+        idx = np.empty(top_k, np.int32)
+        w = np.empty(top_k, np.float32)
+        if self.lib.qo_moe_route(logits, logits.size, top_k, idx, w):
+            raise ValueError("moe_route failed")
+        return idx, w
+
+    def argmax(self, x: np.ndarray) -> int:
+        x = np.ascontiguousarray(x, np.float32)
+        return int(self.lib.qo_argmax(x, x.size))
+
+    def moe_gather(self, expert_out, w, shared, shared_weight, dim, top_k):
+        out = np.empty(dim, np.float32)
+        sh = None if shared is None else np.ascontiguousarray(shared, np.float32)
+        self.lib.qo_moe_gather(np.ascontiguousarray(expert_out, np.float32),
+                               np.ascontiguousarray(w, np.float32),
+                               None if sh is None else sh.ctypes.data, float(shared_weight),
+                               out, dim, top_k)
+        return out
+
+    def silu_mul(self, g, u):
+        g = np.ascontiguousarray(g, np.float32)
+        u = np.ascontiguousarray(u, np.float32)
+        out = np.empty_like(g)
+        self.lib.qo_silu_mul(g, u, out, g.size)
+        return out
+
+    @staticmethod
+    def _pack(quant, arr):
+        arr = _u8(arr)
+        return _ExpertPack(quant, arr.ctypes.data, arr[0].nbytes), arr
+
+    def moe_layer(self, gq, gate, up, dq, down, logits, x, top_k=8, f64=False):
+        """Routed MoE FFN (qw6.c:2246-2264) for every token row of x."""
+        logits = np.ascontiguousarray(logits, np.float32)
+        x = np.ascontiguousarray(x, np.float32)
+        ntok, hidden = x.shape
+        n_experts = logits.shape[1]
+        inter = gate.shape[1]
+        pg, _a = self._pack(gq, gate)
+        pu, _b = self._pack(gq, up)
+        pd, _c = self._pack(dq, down)
+        if f64:
+            out = np.empty((ntok, hidden), np.float64)
+            rc = self.lib.qo_moe_layer_f64(C.byref(pg), C.byref(pu), C.byref(pd), logits, x, out,
+                                           ntok, hidden, inter, n_experts, top_k)
+            if rc:
+                raise ValueError("moe_layer_f64 failed")
+            return out
+        out = np.empty((ntok, hidden), np.float32)
+        idx = np.empty((ntok, top_k), np.int32)
+        w = np.empty((ntok, top_k), np.float32)
+        rc = self.lib.qo_moe_layer(C.byref(pg), C.byref(pu), C.byref(pd), logits, x, out, ntok,
+                                   hidden, inter, n_experts, top_k, idx.ctypes.data, w.ctypes.data)
+        if rc:
+            raise ValueError("moe_layer failed")
+        return out, idx, w
+
+
+class Reference:
+    """qw6's own CPU functions, compiled from its sources (oracle/_ref)."""
+
+    kind = "reference"
+
+    @staticmethod
+    def available() -> bool:
+        return REF_SO.exists()
+
+    def __init__(self) -> None:
+        if not REF_SO.exists():
+            build()
+        lib = C.CDLL(str(REF_SO))
+        lib.ref_dequantize_row.argtypes = [C.c_int, C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32, _f32p]
+        lib.ref_matvec.argtypes = [C.c_int, C.c_void_p, _f32p, _f32p, C.c_uint32, C.c_uint32]
+        lib.ref_moe_route.argtypes = [_f32p, C.c_int, C.c_int, _i32p, _f32p]
+        lib.ref_argmax.argtypes = [_f32p, C.c_int]
+        lib.ref_silu.argtypes = [C.c_float]
+        lib.ref_silu.restype = C.c_float
+        self.lib = lib
+
+    def dequantize(self, quant, w, rows, cols):
+        w = _u8(w)
+        out = np.empty((rows, cols), np.float32)
+        for r in range(rows):
+            if self.lib.ref_dequantize_row(quant, w.ctypes.data, rows, cols, r, out[r]):
+                raise ValueError("ref dequantize failed")
+        return out
+
+    def matvec(self, quant, w, x, rows, cols):
+        w = _u8(w)
+        x = np.ascontiguousarray(x, np.float32).reshape(-1)
+        ntok = x.size // cols
+        y = np.empty((ntok, rows), np.float32)
+        for t in range(ntok):
+            if self.lib.ref_matvec(quant, w.ctypes.data, np.ascontiguousarray(x[t * cols:(t + 1) * cols]),
+                                   y[t], rows, cols):
+                raise ValueError("ref matvec failed")
+        return y if ntok > 1 else y[0]
+
+    def matvec_rows(self, quant, w_rows, x, rows, cols):
+        """matvec over a contiguous slice of rows (bounded CPU samples)."""
+        return self.matvec(quant, w_rows, x, rows, cols)
+
+    def moe_route(self, logits, top_k):
+        logits = np.ascontiguousarray(logits, np.float32)
+        idx = np.empty(top_k, np.int32)
+        w = np.empty(top_k, np.float32)
+        if self.lib.ref_moe_route(logits, logits.size, top_k, idx, w):
+            raise ValueError("ref moe_route failed")
+        return idx, w
+
+    def argmax(self, x):
+        x = np.ascontiguousarray(x, np.float32)
+        return int(self.lib.ref_argmax(x, x.size))
+
+    def silu(self, v: float) -> float:
+        return self.lib.ref_silu(v)
+
+    def moe_layer(self, gq, gate, up, dq, down, logits, x, top_k=8):
+        """qw6.c:2246-2264 composed from qw6's own public functions."""
+        logits = np.ascontiguousarray(logits, np.float32)
+        x = np.ascontiguousarray(x, np.float32)
+        ntok, hidden = x.shape
+        inter = gate.shape[1]
+        out = np.zeros((ntok, hidden), np.float32)
+        idxs = np.empty((ntok, top_k), np.int32)
+        ws = np.empty((ntok, top_k), np.float32)
+        for t in range(ntok):
+            idx, w = self.moe_route(logits[t], top_k)
+            idxs[t], ws[t] = idx, w
+            acc = np.zeros(hidden, np.float32)
+            for k in range(top_k):
+                e = int(idx[k])
+                g = self.matvec(gq, gate[e], x[t], inter, hidden)
+                u = self.matvec(gq, up[e], x[t], inter, hidden)
+                mid = np.array([self.silu(float(v)) for v in g], np.float32) * u
+                d = self.matvec(dq, down[e], mid.astype(np.float32), hidden, inter)
+                acc = (acc + np.float32(w[k]) * d).astype(np.float32)
+            out[t] = acc
+        return out, idxs, ws
+
+
+def cpu_count() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover
+        return os.cpu_count() or 1

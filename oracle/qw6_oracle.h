@@ -1,0 +1,99 @@
+/* qw6_oracle.h -- CPU restatement of qw6's quantized-matvec + MoE path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This is the checker the parity tests, smoke()
+ * and bench.py's cpu_baseline leg compare the CUDA library against; no
+ * product code path may link or call it.
+ *
+ * Every function restates one function of qw6's CPU reference (qw6.c) with
+ * the same floating-point evaluation order, so that dequantized weights are
+ * bit-identical and fp32 matvec results follow the same single-accumulator
+ * sequence.  Pinning: tests/test_oracle.py checks these functions against
+ * (a) qw6's own code compiled from its sources into oracle/_ref (bit-exact
+ * dequant, identical matvec/routing), (b) the committed fixtures in
+ * tests/golden/ that were produced by that build, and (c) the closed-form
+ * known-answer tests of qw6's Vulkan self-test (qw6_vk.c:1609-1954).
+ *
+ * Build: oracle/Makefile with -std=c11 -O2 -ffp-contract=off (no FMA
+ * contraction, as in the reference's x86-64 build).
+ */
+#ifndef QW6_ORACLE_H
+#define QW6_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* qw6_fp16_to_f32, qw6.c:1448-1471 (exact, subnormals normalised). */
+float qo_fp16_to_f32(uint16_t h);
+
+/* qw6_tensor_dequantize_row, qw6.c:1674-1724.  w is the whole matrix
+ * (rows x cols), row selects the row.  Returns 0, or -1 for an unsupported
+ * quant / bad shape (the reference returns -1 for Q8_0 and IQ2_M too). */
+int qo_dequantize_row(uint32_t quant, const void *w, uint32_t cols,
+                      uint32_t row, float *dst);
+
+/* qw6_tensor_matvec, qw6.c:1769-1791: per row, dequantize then a single
+ * sequential fp32 accumulator.  y[rows]. */
+int qo_matvec(uint32_t quant, const void *w, const float *x, float *y,
+              uint32_t rows, uint32_t cols);
+
+/* Same dequantized weights, double accumulation (error reference). */
+int qo_matvec_f64(uint32_t quant, const void *w, const float *x, double *y,
+                  uint32_t rows, uint32_t cols);
+
+/* Batched form: y[t*rows + r] = W[r] . x[t*cols : ...] for t < ntok. */
+int qo_matvec_batch(uint32_t quant, const void *w, const float *x, float *y,
+                    uint32_t rows, uint32_t cols, uint32_t ntok);
+
+/* qw6_cpu_moe_route, qw6.c:2796-2827: top_k by repeated strict-greater
+ * argmax (ties -> lower index), softmax over the selected logits. */
+int qo_moe_route(const float *logits, uint32_t n_experts, uint32_t top_k,
+                 int32_t *idx, float *w);
+
+/* qw6_cpu_argmax, qw6.c:2858-2863: strict '>' so the lowest index wins. */
+int32_t qo_argmax(const float *x, uint32_t n);
+
+/* moe_gather semantics (vulkan/moe_gather.comp:17-29):
+ * out[i] = sum_e w[e]*expert_out[e*dim+i] (+ shared_weight*shared[i]). */
+void qo_moe_gather(const float *expert_out, const float *w,
+                   const float *shared_out, float shared_weight, float *out,
+                   uint32_t dim, uint32_t top_k);
+
+/* silu_mul semantics (qw6.c:2258 with qw6_silu, qw6.h:292-294). */
+void qo_silu_mul(const float *gate, const float *up, float *out, uint32_t n);
+
+/* Routed MoE FFN for ntok tokens, composed as qw6_apply_layer_moe does
+ * (qw6.c:2246-2264) without the shared expert:
+ *   route(logits[t]) -> for each selected e in selection order:
+ *   g = Wg[e].x, u = Wu[e].x, mid = silu(g)*u, d = Wd[e].mid, out += w_e*d.
+ * Expert e's matrices start at base + e*stride (bind_expert_pack,
+ * qw6.c:542-597).  Gate/up are [inter x hidden], down is [hidden x inter].
+ * idx_out/w_out (optional, [ntok*top_k]) receive the routing. */
+typedef struct {
+    uint32_t quant;
+    const void *base;
+    size_t stride;
+} qo_expert_pack;
+
+int qo_moe_layer(const qo_expert_pack *gate, const qo_expert_pack *up,
+                 const qo_expert_pack *down, const float *logits,
+                 const float *x, float *out, uint32_t ntok,
+                 uint32_t hidden, uint32_t inter, uint32_t n_experts,
+                 uint32_t top_k, int32_t *idx_out, float *w_out);
+
+/* Same composition in double precision on the bit-exact weights (error
+ * reference for the fp32 and bf16 paths). Routing uses the fp32 rule. */
+int qo_moe_layer_f64(const qo_expert_pack *gate, const qo_expert_pack *up,
+                     const qo_expert_pack *down, const float *logits,
+                     const float *x, double *out, uint32_t ntok,
+                     uint32_t hidden, uint32_t inter, uint32_t n_experts,
+                     uint32_t top_k);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QW6_ORACLE_H */

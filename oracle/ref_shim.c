@@ -1,0 +1,71 @@
+/* ref_shim.c -- flat entry points into qw6's own CPU code.
+ *
+ * TEST INFRASTRUCTURE ONLY.  Compiled together with the unmodified
+ * reference sources (qw6.c, qw6_tok.c, where they lie) into
+ * oracle/_ref/libqw6ref.so by oracle/Makefile, so that tests and the
+ * CPU-baseline leg of bench.py can call qw6's real implementation:
+ *   qw6_tensor_dequantize_row (qw6.c:1674), qw6_tensor_matvec (qw6.c:1769),
+ *   qw6_cpu_moe_route (qw6.c:2796), qw6_cpu_argmax (qw6.c:2858).
+ * The shim only wraps raw block bytes in a qw6_tensor_t and validates
+ * arguments first, because the reference asserts (exit(1)) on bad input.
+ */
+#include <string.h>
+
+#include "qw6.h"
+
+static int block_ok(int quant, uint32_t cols) {
+    switch (quant) {
+    case QW6_Q_FP32:
+    case QW6_Q_FP16:
+    case QW6_Q_BF16: return cols > 0;
+    case QW6_Q_Q4_K_M:
+    case QW6_Q_Q4_K_S:
+    case QW6_Q_Q5_K:
+    case QW6_Q_Q6_K:
+    case QW6_Q_IQ2_XXS:
+    case QW6_Q_IQ2_S:
+    case QW6_Q_IQ3_S: return cols > 0 && cols % 256 == 0;
+    default: return 0;
+    }
+}
+
+static void wrap(qw6_tensor_t *t, int quant, const void *w, uint32_t rows,
+                 uint32_t cols) {
+    memset(t, 0, sizeof(*t));
+    t->rows = rows;
+    t->cols = cols;
+    t->quant = (qw6_quant_t)quant;
+    t->data = (void *)w;
+}
+
+int ref_dequantize_row(int quant, const void *w, uint32_t rows, uint32_t cols,
+                       uint32_t row, float *dst) {
+    if (!w || !dst || rows == 0 || row >= rows || !block_ok(quant, cols)) return -1;
+    qw6_tensor_t t;
+    wrap(&t, quant, w, rows, cols);
+    return qw6_tensor_dequantize_row(&t, row, dst);
+}
+
+int ref_matvec(int quant, const void *w, const float *x, float *y,
+               uint32_t rows, uint32_t cols) {
+    if (!w || !x || !y || rows == 0 || !block_ok(quant, cols)) return -1;
+    qw6_tensor_t t;
+    wrap(&t, quant, w, rows, cols);
+    return qw6_tensor_matvec(y, &t, x, 0);
+}
+
+int ref_moe_route(const float *logits, int n_experts, int top_k, int *idx,
+                  float *w) {
+    if (!logits || !idx || !w || n_experts <= 0 || n_experts > 256 ||
+        top_k <= 0 || top_k > n_experts)
+        return -1;
+    qw6_cpu_moe_route(idx, w, logits, n_experts, top_k);
+    return 0;
+}
+
+int ref_argmax(const float *x, int n) {
+    if (!x || n <= 0) return -1;
+    return qw6_cpu_argmax(x, n);
+}
+
+float ref_silu(float v) { return qw6_silu(v); }

@@ -1,0 +1,368 @@
+// k_matvec.cu -- GGUF super-block kernels: exact dequantization, repacking
+// into the tile layout, and the streaming int8 tensor-core matvec.
+//
+// Reference behaviour: qw6_tensor_dequantize_row (qw6.c:1674-1724) and
+// qw6_tensor_matvec (qw6.c:1769-1791); the Vulkan dispatch this replaces is
+// qw6_vk_pipe_matvec (qw6_vk.c:2386-2430) with the matmul_*.comp shaders.
+#include <cuda_runtime.h>
+
+#include "qw6_dev.cuh"
+#include "qw6_grids.cuh"
+#include "qw6_launch.h"
+
+namespace qw6 {
+
+// ======================================================= exact dequant ====
+// One thread per (row, super-block, 32-weight group).  Every product and
+// difference is rounded separately (no FMA) in qw6's evaluation order, so the
+// output is bit-identical to qw6_tensor_dequantize_row.
+
+__device__ __forceinline__ void k4_scale_min(const uint8_t* s, int j, uint32_t& sc, uint32_t& mn) {
+    if (j < 4) {
+        sc = s[j] & 63u;
+        mn = s[j + 4] & 63u;
+    } else {
+        sc = (s[j + 4] & 15u) | ((uint32_t)(s[j - 4] >> 6) << 4);
+        mn = (uint32_t)(s[j + 4] >> 4) | ((uint32_t)(s[j] >> 6) << 4);
+    }
+}
+
+__device__ __forceinline__ uint32_t rd16(const uint8_t* p) { return (uint32_t)p[0] | ((uint32_t)p[1] << 8); }
+
+__device__ __forceinline__ float sgnmul(float v, uint32_t bit) { return bit ? -v : v; }
+
+template <int F>
+__device__ void dequant_group(const uint8_t* blk, int j, float* o) {
+    if constexpr (F == QW6F_Q4_K_M || F == QW6F_Q5_K) {
+        const float d = f16_bits_exact(rd16(blk)), dm = f16_bits_exact(rd16(blk + 2));
+        uint32_t sc, mn;
+        k4_scale_min(blk + 4, j, sc, mn);
+        const float dl = __fmul_rn(d, (float)sc), ml = __fmul_rn(dm, (float)mn);
+        const int c = j >> 1, hh = j & 1;
+        const uint8_t* q = blk + (F == QW6F_Q5_K ? 48 : 16) + 32 * c;
+        for (int l = 0; l < 32; l++) {
+            uint32_t v = hh ? (q[l] >> 4) : (q[l] & 15u);
+            if constexpr (F == QW6F_Q5_K) v += (blk[16 + l] >> j) & 1u ? 16u : 0u;
+            o[l] = __fsub_rn(__fmul_rn(dl, (float)v), ml);
+        }
+    } else if constexpr (F == QW6F_Q6_K) {
+        const float d = f16_bits_exact(rd16(blk + 208));
+        const int n = j >> 2, kk = j & 3;
+        const uint8_t* ql = blk + 64 * n + ((kk & 1) ? 32 : 0);
+        const uint8_t* qh = blk + 128 + 32 * n;
+        const float ds = __fmul_rn(d, (float)(int8_t)blk[192 + 8 * n + 2 * kk]);
+        for (int l = 0; l < 32; l++) {
+            const int lo = (kk & 2) ? (ql[l] >> 4) : (ql[l] & 15);
+            const int q = (lo | (((qh[l] >> (2 * kk)) & 3) << 4)) - 32;
+            o[l] = __fmul_rn(ds, (float)q);
+        }
+    } else if constexpr (F == QW6F_IQ2_XXS) {
+        const float d = f16_bits_exact(rd16(blk));
+        const uint8_t* grp = blk + 2 + 8 * j;
+        const uint32_t aux = (uint32_t)grp[4] | ((uint32_t)grp[5] << 8) | ((uint32_t)grp[6] << 16) |
+                             ((uint32_t)grp[7] << 24);
+        const float db = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(aux >> 28))), 0.25f);
+        for (int l = 0; l < 4; l++) {
+            const uint8_t* gr = d_grid_iq2xxs + 8u * grp[l];
+            const uint32_t s = qw6_ksigns((aux >> (7 * l)) & 127u);
+            for (int jj = 0; jj < 8; jj++) o[8 * l + jj] = sgnmul(__fmul_rn(db, (float)gr[jj]), (s >> jj) & 1u);
+        }
+    } else if constexpr (F == QW6F_IQ2_S) {
+        const float d = f16_bits_exact(rd16(blk));
+        const uint8_t *qs = blk + 2, *sg = blk + 34, *qh = blk + 66, *sc = blk + 74;
+        const float d0 = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(sc[j] & 15u))), 0.25f);
+        const float d1 = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(sc[j] >> 4))), 0.25f);
+        for (int l = 0; l < 4; l++) {
+            const uint32_t gi = qs[4 * j + l] | (((uint32_t)qh[j] << (8 - 2 * l)) & 0x300u);
+            const uint8_t* gr = d_grid_iq2s + 8u * gi;
+            const float dl = l < 2 ? d0 : d1;
+            const uint32_t s = sg[4 * j + l];
+            for (int jj = 0; jj < 8; jj++) o[8 * l + jj] = sgnmul(__fmul_rn(dl, (float)gr[jj]), (s >> jj) & 1u);
+        }
+    } else if constexpr (F == QW6F_IQ3_S) {
+        const float d = f16_bits_exact(rd16(blk));
+        const uint8_t *qs = blk + 2 + 8 * j, *s = blk + 74 + 4 * j;
+        const uint32_t h = blk[66 + j], scb = blk[106 + (j >> 1)];
+        const uint32_t nib = (j & 1) ? (scb >> 4) : (scb & 15u);
+        const float db = __fmul_rn(d, (float)(int)(1 + 2 * nib));
+        for (int l = 0; l < 4; l++) {
+            const uint32_t i1 = qs[2 * l] | ((h << (8 - 2 * l)) & 256u);
+            const uint32_t i2 = qs[2 * l + 1] | ((h << (7 - 2 * l)) & 256u);
+            const uint8_t *g1 = d_grid_iq3s + 4u * i1, *g2 = d_grid_iq3s + 4u * i2;
+            for (int jj = 0; jj < 4; jj++) {
+                o[8 * l + jj] = sgnmul(__fmul_rn(db, (float)g1[jj]), (s[l] >> jj) & 1u);
+                o[8 * l + jj + 4] = sgnmul(__fmul_rn(db, (float)g2[jj]), (s[l] >> (jj + 4)) & 1u);
+            }
+        }
+    }
+}
+
+template <int F>
+__global__ void k_dequant(const uint8_t* __restrict__ w, float* __restrict__ out, int rows, int cols) {
+    const int nb = cols / 256;
+    const long long item = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long long total = (long long)rows * nb * 8;
+    if (item >= total) return;
+    const int j = (int)(item & 7), b = (int)((item >> 3) % nb);
+    const long long r = (item >> 3) / nb;
+    const uint8_t* blk = w + ((size_t)r * nb + b) * (size_t)Fmt<F>::BB;
+    dequant_group<F>(blk, j, out + (size_t)r * cols + 256 * b + 32 * j);
+}
+
+// =============================================================== repack ====
+// raw GGUF rows -> tile layout; one CTA per (tile-block, matrix).  Rows past
+// `rows` in the last m-tile are zero-filled (d = 0 makes them inert).
+
+template <int F>
+__global__ void k_pack(const uint8_t* __restrict__ raw, uint8_t* __restrict__ packed, int rows, int cols,
+                       size_t raw_stride, size_t pk_stride) {
+    constexpr int BB = Fmt<F>::BB, TB = Fmt<F>::TB;
+    __shared__ __align__(16) uint8_t s[TB];
+    const int nb = cols / 256;
+    const int tb = blockIdx.x, mt = tb / nb, b = tb % nb;
+    const uint8_t* src = raw + (size_t)blockIdx.y * raw_stride;
+    uint8_t* dst = packed + (size_t)blockIdx.y * pk_stride + (size_t)tb * TB;
+    const size_t rb = (size_t)nb * BB;
+    for (int i = threadIdx.x; i < TB; i += blockDim.x) {
+        const int r = i / BB, p = i % BB, row = mt * 16 + r;
+        s[Fmt<F>::dst(r, p)] = row < rows ? src[(size_t)row * rb + (size_t)b * BB + p] : 0;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < TB / 16; i += blockDim.x)
+        reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(s)[i];
+}
+
+// ============================================================== matvec ====
+// y[tok][r] = sum_c W[r][c] x[tok][c] for tok < ntok (<= 4*NQ).
+// Work item = (m-tile of 16 rows, k-split).  A CTA of 8 warps covers
+// 8/ks m-tiles x ks splits; the ks partial sums of an m-tile are combined in
+// shared memory in split order (deterministic).  Each warp double-buffers its
+// tile-block fragments in registers; the first block of the next item is
+// prefetched while the current one is consumed.
+
+struct MvArgs {
+    const uint8_t* w;
+    const float* x;
+    float* y;
+    int rows, cols, ntok, ldx, ldy, ks, nb, mtiles;
+};
+
+template <int F, int NQ>
+__global__ void __launch_bounds__(kThreads) k_matvec(const MvArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    using T = Tile<F, NQ>;
+    constexpr int TB = T::TB;
+    constexpr size_t tbl_bytes = IsIQ<F>::value ? sizeof(IQTables) : 0;
+    IQTables* tbl = reinterpret_cast<IQTables*>(smem);
+    XStage xs = xstage_carve(smem + tbl_bytes, 4 * NQ, a.cols);
+    float* red = reinterpret_cast<float*>(smem + tbl_bytes + xstage_bytes(4 * NQ, a.cols));
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ks = a.ks, wpm = kWarps / ks, ms = warp / ks, split = warp % ks, nbk = a.nb / ks;
+    const int ngrp = (a.mtiles + wpm - 1) / wpm;
+    const int n_iter = blockIdx.x < ngrp ? (ngrp - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int nsteps = n_iter * nbk;
+
+    auto item_mt = [&](int it) { return ((int)blockIdx.x + it * (int)gridDim.x) * wpm + ms; };
+    auto tile_ptr = [&](int step) {
+        const int it = step / nbk, i = step % nbk;
+        return a.w + ((size_t)item_mt(it) * a.nb + (size_t)split * nbk + i) * TB;
+    };
+    auto step_ok = [&](int step) { return step < nsteps && item_mt(step / nbk) < a.mtiles; };
+
+    typename T::Frag fa, fb;
+    if (step_ok(0)) T::load(fa, tile_ptr(0), lane);
+    if constexpr (IsIQ<F>::value) init_iq_tables(tbl, grid_ptr<F>(), GridBytes<F>::value);
+    xstage_fill(xs, a.x, a.ldx, a.ntok, 4 * NQ, a.cols);
+    __syncthreads();
+    const XView xv = xs.view();
+
+    float acc[2][NQ];
+#pragma unroll
+    for (int qt = 0; qt < NQ; qt++) acc[0][qt] = acc[1][qt] = 0.f;
+
+    auto epilogue = [&](int step) {
+        const int mt = item_mt(step / nbk);
+        const int g = lane >> 2, t = lane & 3;
+        if (ks > 1) {
+#pragma unroll
+            for (int qt = 0; qt < NQ; qt++) {
+                red[(warp * 32 + lane) * 2 * NQ + 2 * qt] = acc[0][qt];
+                red[(warp * 32 + lane) * 2 * NQ + 2 * qt + 1] = acc[1][qt];
+            }
+            __syncthreads();
+            if (split == 0) {
+#pragma unroll
+                for (int qt = 0; qt < NQ; qt++) {
+                    float s0 = 0.f, s1 = 0.f;
+                    for (int s = 0; s < ks; s++) {
+                        s0 += red[((warp + s) * 32 + lane) * 2 * NQ + 2 * qt];
+                        s1 += red[((warp + s) * 32 + lane) * 2 * NQ + 2 * qt + 1];
+                    }
+                    acc[0][qt] = s0;
+                    acc[1][qt] = s1;
+                }
+            }
+            __syncthreads();
+        }
+        if (split == 0 && mt < a.mtiles) {
+#pragma unroll
+            for (int qt = 0; qt < NQ; qt++) {
+                const int tok = 4 * qt + t;
+                if (tok < a.ntok) {
+                    const int r0 = mt * 16 + g;
+                    if (r0 < a.rows) a.y[(size_t)tok * a.ldy + r0] = acc[0][qt];
+                    if (r0 + 8 < a.rows) a.y[(size_t)tok * a.ldy + r0 + 8] = acc[1][qt];
+                }
+            }
+        }
+#pragma unroll
+        for (int qt = 0; qt < NQ; qt++) acc[0][qt] = acc[1][qt] = 0.f;
+    };
+
+    for (int s = 0; s < nsteps; s += 2) {
+        if (step_ok(s + 1)) T::load(fb, tile_ptr(s + 1), lane);
+        if (step_ok(s)) tile_dot<F, NQ>(fa, xv, split * nbk + s % nbk, acc, lane, tbl);
+        if (s % nbk == nbk - 1) epilogue(s);
+        if (s + 1 < nsteps) {
+            if (step_ok(s + 2)) T::load(fa, tile_ptr(s + 2), lane);
+            if (step_ok(s + 1)) tile_dot<F, NQ>(fb, xv, split * nbk + (s + 1) % nbk, acc, lane, tbl);
+            if ((s + 1) % nbk == nbk - 1) epilogue(s + 1);
+        }
+    }
+}
+
+// ---------------------------------------------------------- launchers ----
+
+static int g_num_sms = 0;
+
+static int num_sms() {
+    if (!g_num_sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (g_num_sms <= 0) g_num_sms = 148;
+    }
+    return g_num_sms;
+}
+
+template <int F, int NQ>
+static size_t mv_smem(int cols) {
+    return (IsIQ<F>::value ? sizeof(IQTables) : 0) + xstage_bytes(4 * NQ, cols) + (size_t)kThreads * 2 * NQ * 4;
+}
+
+template <int F, int NQ>
+static int launch_mv(const uint8_t* w, const float* x, float* y, int rows, int cols, int ntok, int ldx,
+                     int ldy, cudaStream_t st) {
+    const size_t smem = mv_smem<F, NQ>(cols);
+    static int configured = 0;
+    static int occ = 1;
+    if (!configured) {
+        if (cudaFuncSetAttribute(k_matvec<F, NQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
+            cudaSuccess)
+            return QW6K_ERR_CUDA;
+        configured = 1;
+    }
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_matvec<F, NQ>, kThreads, smem) != cudaSuccess ||
+        occ < 1)
+        return QW6K_ERR_CUDA;
+    MvArgs a;
+    a.w = w;
+    a.x = x;
+    a.y = y;
+    a.rows = rows;
+    a.cols = cols;
+    a.ntok = ntok;
+    a.ldx = ldx;
+    a.ldy = ldy;
+    a.nb = cols / 256;
+    a.mtiles = (rows + 15) / 16;
+    const int slots = num_sms() * occ * kWarps;  // resident warps
+    int ks = 1;
+    while (ks < 8 && a.nb % (ks * 2) == 0 && (long long)a.mtiles * ks < slots) ks *= 2;
+    a.ks = ks;
+    const int wpm = kWarps / ks;
+    const long long ngrp = (a.mtiles + wpm - 1) / wpm;
+    const int grid = (int)(ngrp < (long long)num_sms() * occ ? ngrp : (long long)num_sms() * occ);
+    k_matvec<F, NQ><<<grid, kThreads, smem, st>>>(a);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
+}
+
+template <int F>
+static int launch_mv_nq(const uint8_t* w, const float* x, float* y, int rows, int cols, int ntok, int ldx,
+                        int ldy, cudaStream_t st) {
+    if (ntok <= 4) return launch_mv<F, 1>(w, x, y, rows, cols, ntok, ldx, ldy, st);
+    if (ntok <= 8) return launch_mv<F, 2>(w, x, y, rows, cols, ntok, ldx, ldy, st);
+    if (ntok <= 32) return launch_mv<F, 8>(w, x, y, rows, cols, ntok, ldx, ldy, st);
+    return QW6K_ERR_ARG;
+}
+
+template <int F>
+static int launch_pack(const void* raw, void* packed, int rows, int cols, int nmat, size_t raw_stride,
+                       size_t pk_stride, cudaStream_t st) {
+    const int nb = cols / 256, mtiles = (rows + 15) / 16;
+    dim3 grid((unsigned)(mtiles * nb), (unsigned)nmat);
+    k_pack<F><<<grid, 256, 0, st>>>((const uint8_t*)raw, (uint8_t*)packed, rows, cols, raw_stride, pk_stride);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
+}
+
+template <int F>
+static int launch_dequant(const void* raw, float* out, int rows, int cols, cudaStream_t st) {
+    const long long total = (long long)rows * (cols / 256) * 8;
+    const int threads = 128;
+    const long long blocks = (total + threads - 1) / threads;
+    if (blocks > 0x7fffffffLL) return QW6K_ERR_ARG;
+    k_dequant<F><<<(unsigned)blocks, threads, 0, st>>>((const uint8_t*)raw, out, rows, cols);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
+}
+
+}  // namespace qw6
+
+using namespace qw6;
+
+#define QW6_DISPATCH_BLOCK(quant, CALL)             \
+    switch (quant) {                                \
+    case QW6F_Q4_K_M:                               \
+    case QW6F_Q4_K_S: return CALL(QW6F_Q4_K_M);     \
+    case QW6F_Q5_K: return CALL(QW6F_Q5_K);         \
+    case QW6F_Q6_K: return CALL(QW6F_Q6_K);         \
+    case QW6F_IQ2_XXS: return CALL(QW6F_IQ2_XXS);   \
+    case QW6F_IQ2_S: return CALL(QW6F_IQ2_S);       \
+    case QW6F_IQ3_S: return CALL(QW6F_IQ3_S);       \
+    default: return QW6K_ERR_QUANT;                 \
+    }
+
+extern "C" size_t qw6k_tile_bytes(uint32_t quant) { return (size_t)16 * qw6_block_bytes(quant); }
+
+extern "C" size_t qw6k_packed_bytes(uint32_t quant, uint32_t rows, uint32_t cols) {
+    if (!qw6_block_bytes(quant) || cols == 0 || cols % 256 || rows == 0) return 0;
+    return (size_t)((rows + 15) / 16) * (cols / 256) * qw6k_tile_bytes(quant);
+}
+
+extern "C" int qw6k_pack(uint32_t quant, const void* raw, void* packed, uint32_t rows, uint32_t cols,
+                         uint32_t nmat, size_t raw_stride, size_t packed_stride, cudaStream_t st) {
+    if (!raw || !packed || !rows || !cols || cols % 256 || !nmat || nmat > 65535) return QW6K_ERR_ARG;
+#define CALL(F) launch_pack<F>(raw, packed, (int)rows, (int)cols, (int)nmat, raw_stride, packed_stride, st)
+    QW6_DISPATCH_BLOCK(quant, CALL)
+#undef CALL
+}
+
+extern "C" int qw6k_dequant(uint32_t quant, const void* raw, float* out, uint32_t rows, uint32_t cols,
+                            cudaStream_t st) {
+    if (!raw || !out || !rows || !cols || cols % 256) return QW6K_ERR_ARG;
+#define CALL(F) launch_dequant<F>(raw, out, (int)rows, (int)cols, st)
+    QW6_DISPATCH_BLOCK(quant, CALL)
+#undef CALL
+}
+
+extern "C" int qw6k_matvec(uint32_t quant, const void* packed, const float* x, float* y, uint32_t rows,
+                           uint32_t cols, uint32_t ntok, uint32_t ldx, uint32_t ldy, cudaStream_t st) {
+    if (!packed || !x || !y || !rows || !cols || cols % 256 || !ntok || ntok > 32 || ldx < cols || ldy < rows ||
+        rows > (1u << 30) || cols > 65536)
+        return QW6K_ERR_ARG;
+    if ((reinterpret_cast<uintptr_t>(packed) & 15u) || (reinterpret_cast<uintptr_t>(x) & 15u) || (ldx & 3u))
+        return QW6K_ERR_ALIGN;
+#define CALL(F) launch_mv_nq<F>((const uint8_t*)packed, x, y, (int)rows, (int)cols, (int)ntok, (int)ldx, (int)ldy, st)
+    QW6_DISPATCH_BLOCK(quant, CALL)
+#undef CALL
+}

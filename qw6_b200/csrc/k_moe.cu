@@ -1,0 +1,386 @@
+// k_moe.cu -- routed MoE FFN for decode-sized batches, entirely on device.
+//
+// Reference composition (qw6_apply_layer_moe, qw6.c:2246-2264):
+//   route -> for each selected expert e (selection order):
+//   g = Wg[e].x, u = Wu[e].x, mid = silu(g)*u, t = Wd[e].mid, out += w_e*t.
+// The Vulkan pipeline runs this as a host readback of the routing plus 5
+// synchronous dispatches per expert (qw6_vk.c:3357-3407).  Here it is four
+// kernels with no host round trip:
+//   plan    route every token, group the (token, slot) assignments by
+//           expert (deterministic counting sort) and cut each expert's list
+//           into work items of <= 4*NQ tokens;
+//   gateup  per (work item, 16-row tile): gate and up tiles of the expert,
+//           int8 tensor-core matvec over the item's tokens, silu(g)*u;
+//   down    per (work item, 16-row tile of hidden): Wd[e] . mid;
+//   combine out[t] = sum_k w[t,k] * down[t,k] in slot order (fp32, rounded
+//           like the CPU loop).
+// Each expert's weights are read once per work item, i.e. once per layer
+// when an expert has <= 4*NQ tokens.
+#include <cuda_runtime.h>
+
+#include "qw6_dev.cuh"
+#include "qw6_grids.cuh"
+#include "qw6_launch.h"
+#include "qw6_route.cuh"
+
+namespace qw6 {
+
+struct MoeArgs {
+    const uint8_t* gate;
+    const uint8_t* up;
+    const uint8_t* down;
+    size_t gstride, ustride, dstride;  // bytes between experts (packed layout)
+    const float* logits;
+    const float* x;
+    float* out;
+    int ntok, hidden, inter, ne, topk, chunk;
+    int ks_gu, ks_dn;  // k-splits of the gate/up (K = hidden) and down (K = inter) tiles
+    // workspace
+    int32_t* idx;
+    float* w;
+    int32_t* order;
+    int4* items;
+    int* nitems;
+    float* mid;
+    float* dout;
+};
+
+// ------------------------------------------------------------------ plan --
+__global__ void __launch_bounds__(512) k_moe_plan(const MoeArgs a) {
+    __shared__ int cnt[256], off[257], ich[257];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
+    const int TK = a.ntok * a.topk;
+    for (int t = warp; t < a.ntok; t += nw)
+        route_token(a.logits + (size_t)t * a.ne, a.ne, a.topk, a.idx + (size_t)t * a.topk, a.w + (size_t)t * a.topk,
+                    lane);
+    for (int e = tid; e < 256; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    for (int i = tid; i < TK; i += blockDim.x) atomicAdd(&cnt[a.idx[i]], 1);
+    __syncthreads();
+    if (tid == 0) {
+        int o = 0, c = 0;
+        for (int e = 0; e < a.ne; e++) {
+            off[e] = o;
+            ich[e] = c;
+            o += cnt[e];
+            c += (cnt[e] + a.chunk - 1) / a.chunk;
+        }
+        off[a.ne] = o;
+        ich[a.ne] = c;
+        *a.nitems = c;
+    }
+    __syncthreads();
+    // stable counting sort: rank = earlier assignments with the same expert
+    for (int i = tid; i < TK; i += blockDim.x) {
+        const int e = a.idx[i];
+        int r = 0;
+        for (int j = 0; j < i; j++) r += a.idx[j] == e;
+        a.order[off[e] + r] = i;
+    }
+    for (int e = tid; e < a.ne; e += blockDim.x) {
+        const int n = cnt[e];
+        for (int c = 0; c * a.chunk < n; c++)
+            a.items[ich[e] + c] = make_int4(e, off[e] + c * a.chunk, min(a.chunk, n - c * a.chunk), 0);
+    }
+}
+
+__device__ __forceinline__ float silu_exact(float v) { return __fdiv_rn(v, __fadd_rn(1.0f, expf(-v))); }
+
+template <int F>
+__host__ __device__ constexpr size_t tbl_bytes_of() {
+    return IsIQ<F>::value ? sizeof(IQTables) : 0;
+}
+
+// ---------------------------------------------------------------- gateup --
+template <int F, int NQ>
+__global__ void __launch_bounds__(kThreads) k_moe_gateup(const MoeArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    using T = Tile<F, NQ>;
+    constexpr int TB = T::TB;
+    const int ks = a.ks_gu, mpc = kWarps / ks;
+    const int mgroups = (a.inter / 16) / mpc;
+    const int item = blockIdx.x / mgroups, mg = blockIdx.x % mgroups;
+    if (item >= *a.nitems) return;
+    const int4 it = a.items[item];
+    const int e = it.x, cnt = it.z;
+    const int32_t* sel = a.order + it.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ms = warp / ks, split = warp % ks, mt = mg * mpc + ms, nbh = a.hidden / 256, b0 = split * 2;
+
+    const uint8_t* gb = a.gate + (size_t)e * a.gstride + ((size_t)mt * nbh + b0) * TB;
+    const uint8_t* ub = a.up + (size_t)e * a.ustride + ((size_t)mt * nbh + b0) * TB;
+    typename T::Frag g0, g1, u0, u1;
+    T::load(g0, gb, lane);
+    T::load(g1, gb + TB, lane);
+    T::load(u0, ub, lane);
+    T::load(u1, ub + TB, lane);
+
+    IQTables* tbl = reinterpret_cast<IQTables*>(smem);
+    XStage xs = xstage_carve(smem + tbl_bytes_of<F>(), 4 * NQ, a.hidden);
+    float* red = reinterpret_cast<float*>(smem + tbl_bytes_of<F>() + xstage_bytes(4 * NQ, a.hidden));
+    if constexpr (IsIQ<F>::value) init_iq_tables(tbl, grid_ptr<F>(), GridBytes<F>::value);
+    xstage_fill(xs, a.x, a.hidden, cnt, 4 * NQ, a.hidden, sel, a.topk);
+    __syncthreads();
+    const XView xv = xs.view();
+
+    float ag[2][NQ], au[2][NQ];
+#pragma unroll
+    for (int q = 0; q < NQ; q++) ag[0][q] = ag[1][q] = au[0][q] = au[1][q] = 0.f;
+    tile_dot<F, NQ>(g0, xv, b0, ag, lane, tbl);
+    tile_dot<F, NQ>(g1, xv, b0 + 1, ag, lane, tbl);
+    tile_dot<F, NQ>(u0, xv, b0, au, lane, tbl);
+    tile_dot<F, NQ>(u1, xv, b0 + 1, au, lane, tbl);
+
+    if (ks > 1) {
+        float* r = red + (warp * 32 + lane) * 4 * NQ;
+#pragma unroll
+        for (int q = 0; q < NQ; q++) {
+            r[4 * q + 0] = ag[0][q];
+            r[4 * q + 1] = ag[1][q];
+            r[4 * q + 2] = au[0][q];
+            r[4 * q + 3] = au[1][q];
+        }
+        __syncthreads();
+        if (split == 0) {
+#pragma unroll
+            for (int q = 0; q < NQ; q++) {
+                float s[4] = {0.f, 0.f, 0.f, 0.f};
+                for (int p = 0; p < ks; p++) {
+                    const float* rp = red + ((warp + p) * 32 + lane) * 4 * NQ + 4 * q;
+                    s[0] += rp[0];
+                    s[1] += rp[1];
+                    s[2] += rp[2];
+                    s[3] += rp[3];
+                }
+                ag[0][q] = s[0];
+                ag[1][q] = s[1];
+                au[0][q] = s[2];
+                au[1][q] = s[3];
+            }
+        }
+    }
+    if (split == 0) {
+        const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+        for (int q = 0; q < NQ; q++) {
+            const int j = 4 * q + t;
+            if (j < cnt) {
+                float* m = a.mid + (size_t)sel[j] * a.inter + mt * 16 + g;
+                m[0] = __fmul_rn(silu_exact(ag[0][q]), au[0][q]);
+                m[8] = __fmul_rn(silu_exact(ag[1][q]), au[1][q]);
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------ down --
+template <int F, int NQ>
+__global__ void __launch_bounds__(kThreads) k_moe_down(const MoeArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    using T = Tile<F, NQ>;
+    constexpr int TB = T::TB;
+    const int ks = a.ks_dn, mpc = kWarps / ks;
+    const int mgroups = (a.hidden / 16) / mpc;
+    const int item = blockIdx.x / mgroups, mg = blockIdx.x % mgroups;
+    if (item >= *a.nitems) return;
+    const int4 it = a.items[item];
+    const int e = it.x, cnt = it.z;
+    const int32_t* sel = a.order + it.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ms = warp / ks, split = warp % ks, mt = mg * mpc + ms, nbi = a.inter / 256, b0 = split * 2;
+
+    const uint8_t* db = a.down + (size_t)e * a.dstride + ((size_t)mt * nbi + b0) * TB;
+    typename T::Frag d0, d1;
+    T::load(d0, db, lane);
+    T::load(d1, db + TB, lane);
+
+    IQTables* tbl = reinterpret_cast<IQTables*>(smem);
+    XStage xs = xstage_carve(smem + tbl_bytes_of<F>(), 4 * NQ, a.inter);
+    float* red = reinterpret_cast<float*>(smem + tbl_bytes_of<F>() + xstage_bytes(4 * NQ, a.inter));
+    if constexpr (IsIQ<F>::value) init_iq_tables(tbl, grid_ptr<F>(), GridBytes<F>::value);
+    xstage_fill(xs, a.mid, a.inter, cnt, 4 * NQ, a.inter, sel, 1);
+    __syncthreads();
+    const XView xv = xs.view();
+
+    float acc[2][NQ];
+#pragma unroll
+    for (int q = 0; q < NQ; q++) acc[0][q] = acc[1][q] = 0.f;
+    tile_dot<F, NQ>(d0, xv, b0, acc, lane, tbl);
+    tile_dot<F, NQ>(d1, xv, b0 + 1, acc, lane, tbl);
+
+    if (ks > 1) {
+        float* r = red + (warp * 32 + lane) * 2 * NQ;
+#pragma unroll
+        for (int q = 0; q < NQ; q++) {
+            r[2 * q] = acc[0][q];
+            r[2 * q + 1] = acc[1][q];
+        }
+        __syncthreads();
+        if (split == 0) {
+#pragma unroll
+            for (int q = 0; q < NQ; q++) {
+                float s0 = 0.f, s1 = 0.f;
+                for (int p = 0; p < ks; p++) {
+                    s0 += red[((warp + p) * 32 + lane) * 2 * NQ + 2 * q];
+                    s1 += red[((warp + p) * 32 + lane) * 2 * NQ + 2 * q + 1];
+                }
+                acc[0][q] = s0;
+                acc[1][q] = s1;
+            }
+        }
+    }
+    if (split == 0) {
+        const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+        for (int q = 0; q < NQ; q++) {
+            const int j = 4 * q + t;
+            if (j < cnt) {
+                float* o = a.dout + (size_t)sel[j] * a.hidden + mt * 16 + g;
+                o[0] = acc[0][q];
+                o[8] = acc[1][q];
+            }
+        }
+    }
+}
+
+// --------------------------------------------------------------- combine --
+__global__ void k_moe_combine(const MoeArgs a) {
+    const int t = blockIdx.y;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= a.hidden) return;
+    float acc = 0.f;
+    for (int k = 0; k < a.topk; k++) {
+        const int s = t * a.topk + k;
+        acc = __fadd_rn(acc, __fmul_rn(a.w[s], a.dout[(size_t)s * a.hidden + i]));
+    }
+    a.out[(size_t)t * a.hidden + i] = acc;
+}
+
+// -------------------------------------------------------------- launcher --
+
+template <int F, int NQ>
+static size_t gu_smem(int hidden) {
+    return tbl_bytes_of<F>() + xstage_bytes(4 * NQ, hidden) + (size_t)kThreads * 4 * NQ * 4;
+}
+
+template <int F, int NQ>
+static int launch_gateup(const MoeArgs& a, int max_items, cudaStream_t st) {
+    const size_t smem = gu_smem<F, NQ>(a.hidden);
+    if (smem > 200 * 1024) return QW6K_ERR_ARG;
+    static bool cfg = false;
+    if (!cfg && cudaFuncSetAttribute(k_moe_gateup<F, NQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
+                    cudaSuccess)
+        return QW6K_ERR_CUDA;
+    cfg = true;
+    const int mgroups = (a.inter / 16) / (kWarps / a.ks_gu);
+    k_moe_gateup<F, NQ><<<max_items * mgroups, kThreads, smem, st>>>(a);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
+}
+
+template <int F, int NQ>
+static int launch_down(const MoeArgs& a, int max_items, cudaStream_t st) {
+    const size_t smem = gu_smem<F, NQ>(a.inter);
+    if (smem > 200 * 1024) return QW6K_ERR_ARG;
+    static bool cfg = false;
+    if (!cfg && cudaFuncSetAttribute(k_moe_down<F, NQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
+                    cudaSuccess)
+        return QW6K_ERR_CUDA;
+    cfg = true;
+    const int mgroups = (a.hidden / 16) / (kWarps / a.ks_dn);
+    k_moe_down<F, NQ><<<max_items * mgroups, kThreads, smem, st>>>(a);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
+}
+
+#define QW6_MOE_DISPATCH(quant, FN, NQ, ...)                  \
+    switch (quant) {                                          \
+    case QW6F_Q4_K_M:                                         \
+    case QW6F_Q4_K_S: return FN<QW6F_Q4_K_M, NQ>(__VA_ARGS__); \
+    case QW6F_Q5_K: return FN<QW6F_Q5_K, NQ>(__VA_ARGS__);     \
+    case QW6F_Q6_K: return FN<QW6F_Q6_K, NQ>(__VA_ARGS__);     \
+    case QW6F_IQ2_XXS: return FN<QW6F_IQ2_XXS, NQ>(__VA_ARGS__); \
+    case QW6F_IQ2_S: return FN<QW6F_IQ2_S, NQ>(__VA_ARGS__);   \
+    case QW6F_IQ3_S: return FN<QW6F_IQ3_S, NQ>(__VA_ARGS__);   \
+    default: return QW6K_ERR_QUANT;                           \
+    }
+
+static int gateup_any(uint32_t q, int nq, const MoeArgs& a, int mi, cudaStream_t st) {
+    if (nq == 1) { QW6_MOE_DISPATCH(q, launch_gateup, 1, a, mi, st) }
+    QW6_MOE_DISPATCH(q, launch_gateup, 2, a, mi, st)
+}
+static int down_any(uint32_t q, int nq, const MoeArgs& a, int mi, cudaStream_t st) {
+    if (nq == 1) { QW6_MOE_DISPATCH(q, launch_down, 1, a, mi, st) }
+    QW6_MOE_DISPATCH(q, launch_down, 2, a, mi, st)
+}
+
+}  // namespace qw6
+
+using namespace qw6;
+
+static size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+static int moe_items_max(uint32_t ntok, uint32_t ne, uint32_t topk, uint32_t chunk) {
+    const uint32_t tk = ntok * topk;
+    return (int)((tk < ne ? tk : ne) + tk / chunk + 1);
+}
+
+static uint32_t moe_chunk(uint32_t ntok) { return ntok <= 4 ? 4u : 8u; }
+
+extern "C" size_t qw6k_moe_ws_bytes(uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t ne, uint32_t topk) {
+    const size_t tk = (size_t)ntok * topk;
+    const int mi = moe_items_max(ntok, ne, topk, moe_chunk(ntok));
+    return al256(tk * 4) * 3 + al256((size_t)mi * 16) + 256 + al256(tk * inter * 4) + al256(tk * hidden * 4);
+}
+
+extern "C" int qw6k_moe_decode(uint32_t gq, const void* gate, size_t gstride, const void* up, size_t ustride,
+                               uint32_t dq, const void* down, size_t dstride, const float* logits, const float* x,
+                               float* out, uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t ne,
+                               uint32_t topk, void* ws, size_t ws_bytes, cudaStream_t st) {
+    if (!gate || !up || !down || !logits || !x || !out || !ws || !ntok || !ne || ne > 256 || !topk || topk > 32 ||
+        topk > ne || (size_t)ntok * topk > 4096)
+        return QW6K_ERR_ARG;
+    const uint32_t nbh = hidden / 256, nbi = inter / 256;
+    if (hidden % 512 || inter % 512 || nbh > 16 || nbi > 16 || hidden > 4096) return QW6K_ERR_ARG;
+    if (ws_bytes < qw6k_moe_ws_bytes(ntok, hidden, inter, ne, topk)) return QW6K_ERR_ARG;
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up) |
+         reinterpret_cast<uintptr_t>(down) | gstride | ustride | dstride) & 15u)
+        return QW6K_ERR_ALIGN;
+    MoeArgs a;
+    a.gate = (const uint8_t*)gate;
+    a.up = (const uint8_t*)up;
+    a.down = (const uint8_t*)down;
+    a.gstride = gstride;
+    a.ustride = ustride;
+    a.dstride = dstride;
+    a.logits = logits;
+    a.x = x;
+    a.out = out;
+    a.ntok = (int)ntok;
+    a.hidden = (int)hidden;
+    a.inter = (int)inter;
+    a.ne = (int)ne;
+    a.topk = (int)topk;
+    a.chunk = (int)moe_chunk(ntok);
+    a.ks_gu = (int)nbh / 2;
+    a.ks_dn = (int)nbi / 2;
+    if ((inter / 16) % (kWarps / a.ks_gu) || (hidden / 16) % (kWarps / a.ks_dn)) return QW6K_ERR_ARG;
+    const size_t tk = (size_t)ntok * topk;
+    const int mi = moe_items_max(ntok, ne, topk, (uint32_t)a.chunk);
+    uint8_t* p = (uint8_t*)ws;
+    a.idx = (int32_t*)p; p += al256(tk * 4);
+    a.w = (float*)p; p += al256(tk * 4);
+    a.order = (int32_t*)p; p += al256(tk * 4);
+    a.items = (int4*)p; p += al256((size_t)mi * 16);
+    a.nitems = (int*)p; p += 256;
+    a.mid = (float*)p; p += al256(tk * inter * 4);
+    a.dout = (float*)p;
+    k_moe_plan<<<1, 512, 0, st>>>(a);
+    if (cudaPeekAtLastError() != cudaSuccess) return QW6K_ERR_CUDA;
+    const int nq = a.chunk / 4;
+    int rc = gateup_any(gq, nq, a, mi, st);
+    if (rc) return rc;
+    rc = down_any(dq, nq, a, mi, st);
+    if (rc) return rc;
+    dim3 cg((hidden + 255) / 256, ntok);
+    k_moe_combine<<<cg, 256, 0, st>>>(a);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
+}

@@ -1,0 +1,42 @@
+/* qw6_host_internal.h -- context struct and helpers shared by the host C
+ * files of libqw6cuda (not installed). */
+#ifndef QW6_HOST_INTERNAL_H
+#define QW6_HOST_INTERNAL_H
+
+#include <stddef.h>
+
+#include <cuda_runtime_api.h>
+
+#include "qw6_cuda.h"
+
+enum {
+    QW6H_BUF_RAW = 0, /* raw weights / first operand of a host call */
+    QW6H_BUF_PACKED,  /* packed weights of a host call */
+    QW6H_BUF_X,       /* activations */
+    QW6H_BUF_Y,       /* outputs */
+    QW6H_BUF_KEY,     /* small scratch (argmax key, routing weights) */
+    QW6H_BUF_WS,      /* workspace of the fused MoE / LM-head calls */
+    QW6H_NBUF
+};
+
+typedef struct {
+    void *p;
+    size_t n;
+} qw6h_buf_t;
+
+struct qw6cu_ctx {
+    int device;
+    int num_sms;
+    cudaStream_t own; /* stream created with the context */
+    cudaStream_t st;  /* stream work is enqueued on */
+    qw6h_buf_t buf[QW6H_NBUF];
+    void *pinned;     /* pinned host staging (unused unless requested) */
+};
+
+void qw6h_set_err(const char *fmt, ...);
+int qw6h_rc(int rc, const char *what);
+int qw6h_use(qw6cu_ctx *ctx);
+void *qw6h_buf(qw6cu_ctx *ctx, int i, size_t bytes);
+qw6cu_ctx *qw6h_default_locked(void);
+
+#endif /* QW6_HOST_INTERNAL_H */

@@ -1,0 +1,76 @@
+/* qw6_launch.h -- C-callable launchers of the CUDA kernels (internal).
+ *
+ * The host side of libqw6cuda is plain C (qw6_host.c); it reaches the
+ * kernels only through these functions, which take device pointers and a
+ * stream, validate shapes, and enqueue work without synchronizing.
+ * All return 0 or a negative QW6K_ERR_* code.
+ */
+#ifndef QW6_LAUNCH_H
+#define QW6_LAUNCH_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QW6K_ERR_ARG (-2)
+#define QW6K_ERR_QUANT (-3)
+#define QW6K_ERR_CUDA (-4)
+#define QW6K_ERR_ALIGN (-5)
+#define QW6K_ERR_TIMEOUT (-6)
+
+/* 16 * block bytes of the format (0 if not a super-block format). */
+size_t qw6k_tile_bytes(uint32_t quant);
+/* Device bytes of the packed tile layout of a rows x cols matrix. */
+size_t qw6k_packed_bytes(uint32_t quant, uint32_t rows, uint32_t cols);
+
+/* Raw GGUF rows -> packed tile layout, nmat matrices at the given strides. */
+int qw6k_pack(uint32_t quant, const void *raw, void *packed, uint32_t rows, uint32_t cols,
+              uint32_t nmat, size_t raw_stride, size_t packed_stride, cudaStream_t st);
+
+/* Bit-exact fp32 dequantization of raw GGUF rows (qw6.c:1674-1724). */
+int qw6k_dequant(uint32_t quant, const void *raw, float *out, uint32_t rows, uint32_t cols,
+                 cudaStream_t st);
+
+/* y[t*ldy + r] = W[r] . x[t*ldx ...] for t < ntok (<= 32); W packed. */
+int qw6k_matvec(uint32_t quant, const void *packed, const float *x, float *y, uint32_t rows,
+                uint32_t cols, uint32_t ntok, uint32_t ldx, uint32_t ldy, cudaStream_t st);
+
+/* fp32 weights (row-major rows x cols). */
+int qw6k_matvec_f32(const float *w, const float *x, float *y, uint32_t rows, uint32_t cols,
+                    cudaStream_t st);
+
+/* Top-k routing, one token per row of logits (qw6.c:2796-2827). */
+int qw6k_moe_route(const float *logits, uint32_t ntok, uint32_t n_experts, uint32_t top_k,
+                   int32_t *idx, float *w, cudaStream_t st);
+
+/* out[i] = sum_e w[e]*expert_out[e*dim+i] (+ shared_weight*shared[i]). */
+int qw6k_moe_gather(const float *expert_out, const float *w, const float *shared,
+                    float shared_weight, float *out, uint32_t dim, uint32_t top_k, cudaStream_t st);
+
+/* out[i] = silu(gate[i]) * up[i]. */
+int qw6k_silu_mul(const float *gate, const float *up, float *out, uint32_t n, cudaStream_t st);
+
+/* Greedy argmax (lowest index on ties; NaN handling as qw6_cpu_argmax).
+ * key64 is caller-provided device scratch of 8 bytes. */
+int qw6k_argmax(const float *x, uint32_t n, unsigned long long *key64, uint32_t *out_idx,
+                float *out_val, cudaStream_t st);
+
+/* Routed MoE FFN for ntok decode tokens (ntok*top_k <= 4096, hidden and
+ * inter multiples of 512, hidden <= 4096).  Expert e's packed matrices at
+ * base + e*stride.  ws: device workspace of qw6k_moe_ws_bytes(). */
+size_t qw6k_moe_ws_bytes(uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t ne, uint32_t topk);
+int qw6k_moe_decode(uint32_t gq, const void *gate, size_t gstride, const void *up, size_t ustride, uint32_t dq,
+                    const void *down, size_t dstride, const float *logits, const float *x, float *out,
+                    uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t ne, uint32_t topk, void *ws,
+                    size_t ws_bytes, cudaStream_t st);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QW6_LAUNCH_H */

@@ -1,0 +1,246 @@
+"""ctypes binding of libqw6cuda.so (the in-tree CUDA library).
+
+Two layers, mirroring the C headers in include/:
+
+* qw6_vk.h -- the drop-in per-call entry points of qw6's Vulkan backend
+  (host memory in and out, synchronous, 0 / -1).  Exposed as functions with
+  the same names minus the ``qw6_vk_`` prefix; -1 raises Qw6CudaError.
+* qw6_cuda.h -- the device-resident API (``Context``): device pointers (ints,
+  e.g. ``torch.Tensor.data_ptr()``), work enqueued on the context's stream.
+
+There is no CPU fallback: if the shared library is missing or no B200 is
+usable, the calls raise.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libqw6cuda.so"
+CSRC = PKG / "csrc"
+
+# qw6_quant_t (qw6.h:77-92)
+Q4_K, Q4_K_S, Q5_K, Q6_K, IQ3_S, IQ2_S, IQ2_XXS = 4, 5, 6, 7, 9, 11, 13
+FP32 = 0
+BLOCK_BYTES = {Q4_K: 144, Q4_K_S: 144, Q5_K: 176, Q6_K: 210, IQ2_XXS: 66, IQ2_S: 82, IQ3_S: 110}
+
+# Symbols include/*.h declare (checked by tests/test_abi.py).
+VK_SYMBOLS = (
+    "qw6_vk_selftest", "qw6_vk_matvec_f32_host", "qw6_vk_matmul_q4k_host", "qw6_vk_matmul_q5k_host",
+    "qw6_vk_matmul_q6k_host", "qw6_vk_matmul_iq2xxs_host", "qw6_vk_matmul_iq2s_host",
+    "qw6_vk_matmul_iq3s_host", "qw6_vk_silu_mul_host", "qw6_vk_argmax_host", "qw6_vk_sampling_greedy_host",
+    "qw6_vk_moe_route_host", "qw6_vk_moe_gather_host", "qw6_vk_rmsnorm_host", "qw6_vk_rmsnorm_chunked_host",
+    "qw6_vk_attention_gqa_host", "qw6_vk_deltanet_conv1d_host", "qw6_vk_deltanet_retrieve_host",
+    "qw6_vk_deltanet_update_host", "qw6_vk_mrope_host", "qw6_vk_mtp_draft_host", "qw6_vk_pipe_init",
+    "qw6_vk_pipe_forward", "qw6_vk_pipe_forward_greedy", "qw6_vk_pipe_free",
+)
+
+
+class Qw6CudaError(RuntimeError):
+    pass
+
+
+def build(jobs: int = 8) -> None:
+    """Compile libqw6cuda.so in-tree (sm_100a)."""
+    subprocess.run(["make", "-s", f"-j{jobs}", "-C", str(CSRC)], check=True)
+
+
+_lib = None
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C")
+_u32p = np.ctypeslib.ndpointer(np.uint32, flags="C")
+_u8p = np.ctypeslib.ndpointer(np.uint8, flags="C")
+_vp = C.c_void_p
+_u32 = C.c_uint32
+_sz = C.c_size_t
+
+
+class ExpertPack(C.Structure):
+    _fields_ = [("quant", C.c_uint32), ("base", C.c_void_p), ("stride", C.c_size_t)]
+
+
+def load() -> C.CDLL:
+    """Load the in-tree library (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise Qw6CudaError(f"{LIB_PATH} is missing; build it with `make -C {CSRC}` (or __graft_entry__.build())")
+    lib = C.CDLL(str(LIB_PATH))
+    for name in ("qw6_vk_matmul_q4k_host", "qw6_vk_matmul_q5k_host", "qw6_vk_matmul_q6k_host",
+                 "qw6_vk_matmul_iq2xxs_host", "qw6_vk_matmul_iq2s_host", "qw6_vk_matmul_iq3s_host"):
+        getattr(lib, name).argtypes = [_u8p, _f32p, _f32p, _u32, _u32]
+    lib.qw6_vk_matvec_f32_host.argtypes = [_f32p, _f32p, _f32p, _u32, _u32]
+    lib.qw6_vk_silu_mul_host.argtypes = [_f32p, _f32p, _f32p, _u32]
+    lib.qw6_vk_argmax_host.argtypes = [_f32p, _u32, C.POINTER(C.c_uint32), C.POINTER(C.c_float)]
+    lib.qw6_vk_sampling_greedy_host.argtypes = [_f32p, _u32, C.POINTER(C.c_uint32)]
+    lib.qw6_vk_moe_route_host.argtypes = [_f32p, _u32p, _f32p, _u32, _u32]
+    lib.qw6_vk_moe_gather_host.argtypes = [_f32p, _f32p, _vp, C.c_float, _f32p, _u32, _u32]
+    lib.qw6_vk_selftest.argtypes = []
+    lib.qw6cu_last_error.restype = C.c_char_p
+    lib.qw6cu_create.argtypes = [C.POINTER(_vp), C.c_int]
+    lib.qw6cu_destroy.argtypes = [_vp]
+    lib.qw6cu_destroy.restype = None
+    lib.qw6cu_set_stream.argtypes = [_vp, _vp]
+    lib.qw6cu_get_stream.argtypes = [_vp]
+    lib.qw6cu_get_stream.restype = _vp
+    lib.qw6cu_synchronize.argtypes = [_vp]
+    lib.qw6cu_packed_bytes.argtypes = [_u32, _u32, _u32]
+    lib.qw6cu_packed_bytes.restype = _sz
+    lib.qw6cu_pack.argtypes = [_vp, _u32, _vp, _vp, _u32, _u32, _u32, _sz, _sz]
+    lib.qw6cu_dequantize.argtypes = [_vp, _u32, _vp, _vp, _u32, _u32]
+    lib.qw6cu_matvec.argtypes = [_vp, _u32, _vp, _vp, _vp, _u32, _u32, _u32]
+    lib.qw6cu_matvec_f32.argtypes = [_vp, _vp, _vp, _vp, _u32, _u32]
+    lib.qw6cu_moe_route.argtypes = [_vp, _vp, _u32, _u32, _u32, _vp, _vp]
+    lib.qw6cu_silu_mul.argtypes = [_vp, _vp, _vp, _vp, _u32]
+    lib.qw6cu_moe_gather.argtypes = [_vp, _vp, _vp, _vp, C.c_float, _vp, _u32, _u32]
+    lib.qw6cu_argmax.argtypes = [_vp, _vp, _u32, _vp, _vp]
+    pk = C.POINTER(ExpertPack)
+    lib.qw6cu_moe_decode.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32]
+    lib.qw6cu_moe_workspace_bytes.argtypes = [_u32, _u32, _u32, _u32, _u32]
+    lib.qw6cu_moe_workspace_bytes.restype = _sz
+    _lib = lib
+    return lib
+
+
+def last_error() -> str:
+    msg = load().qw6cu_last_error()
+    return msg.decode() if msg else ""
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise Qw6CudaError(f"{what} failed (rc={rc}): {last_error()}")
+
+
+# ---------------------------------------------------------- qw6_vk.h -----
+
+_MATMUL = {Q4_K: "q4k", Q4_K_S: "q4k", Q5_K: "q5k", Q6_K: "q6k", IQ2_XXS: "iq2xxs", IQ2_S: "iq2s", IQ3_S: "iq3s"}
+
+
+def matmul_host(quant: int, w: np.ndarray, x: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    """qw6_vk_matmul_<fmt>_host: raw GGUF bytes + fp32 x -> fp32 y[rows]."""
+    fn = getattr(load(), f"qw6_vk_matmul_{_MATMUL[quant]}_host")
+    w = np.ascontiguousarray(w).view(np.uint8).reshape(-1)
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    y = np.empty(rows, np.float32)
+    _check(fn(w, x, y, rows, cols), f"qw6_vk_matmul_{_MATMUL[quant]}_host")
+    return y
+
+
+def matvec_f32_host(w: np.ndarray, x: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    y = np.empty(rows, np.float32)
+    _check(load().qw6_vk_matvec_f32_host(np.ascontiguousarray(w, np.float32).reshape(-1),
+                                         np.ascontiguousarray(x, np.float32), y, rows, cols),
+           "qw6_vk_matvec_f32_host")
+    return y
+
+
+def silu_mul_host(g: np.ndarray, u: np.ndarray) -> np.ndarray:
+    g = np.ascontiguousarray(g, np.float32)
+    out = np.empty_like(g)
+    _check(load().qw6_vk_silu_mul_host(g, np.ascontiguousarray(u, np.float32), out, g.size), "silu_mul_host")
+    return out
+
+
+def argmax_host(x: np.ndarray):
+    x = np.ascontiguousarray(x, np.float32)
+    i, v = C.c_uint32(), C.c_float()
+    _check(load().qw6_vk_argmax_host(x, x.size, C.byref(i), C.byref(v)), "argmax_host")
+    return int(i.value), float(v.value)
+
+
+def sampling_greedy_host(x: np.ndarray) -> int:
+    x = np.ascontiguousarray(x, np.float32)
+    t = C.c_uint32()
+    _check(load().qw6_vk_sampling_greedy_host(x, x.size, C.byref(t)), "sampling_greedy_host")
+    return int(t.value)
+
+
+def moe_route_host(logits: np.ndarray, top_k: int):
+    logits = np.ascontiguousarray(logits, np.float32)
+    idx = np.empty(top_k, np.uint32)
+    w = np.empty(top_k, np.float32)
+    _check(load().qw6_vk_moe_route_host(logits, idx, w, logits.size, top_k), "moe_route_host")
+    return idx, w
+
+
+def moe_gather_host(expert_out, w, shared, shared_weight, dim, top_k):
+    out = np.empty(dim, np.float32)
+    sh = None if shared is None else np.ascontiguousarray(shared, np.float32)
+    _check(load().qw6_vk_moe_gather_host(np.ascontiguousarray(expert_out, np.float32),
+                                         np.ascontiguousarray(w, np.float32),
+                                         None if sh is None else sh.ctypes.data, float(shared_weight), out,
+                                         dim, top_k), "moe_gather_host")
+    return out
+
+
+def selftest() -> int:
+    return int(load().qw6_vk_selftest())
+
+
+# -------------------------------------------------------- qw6_cuda.h -----
+
+class Context:
+    """A qw6cu_ctx: one device, one stream (optionally an external one)."""
+
+    def __init__(self, device: int = -1, stream: int | None = None) -> None:
+        self.lib = load()
+        h = _vp()
+        _check(self.lib.qw6cu_create(C.byref(h), device), "qw6cu_create")
+        self.h = h
+        if stream is not None:
+            self.set_stream(stream)
+
+    def close(self) -> None:
+        if self.h:
+            self.lib.qw6cu_destroy(self.h)
+            self.h = _vp()
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_stream(self, stream: int | None) -> None:
+        _check(self.lib.qw6cu_set_stream(self.h, stream or None), "qw6cu_set_stream")
+
+    def synchronize(self) -> None:
+        _check(self.lib.qw6cu_synchronize(self.h), "qw6cu_synchronize")
+
+    @staticmethod
+    def packed_bytes(quant: int, rows: int, cols: int) -> int:
+        return int(load().qw6cu_packed_bytes(quant, rows, cols))
+
+    def pack(self, quant, raw, packed, rows, cols, count=1, raw_stride=0, packed_stride=0):
+        _check(self.lib.qw6cu_pack(self.h, quant, raw, packed, rows, cols, count, raw_stride, packed_stride),
+               "qw6cu_pack")
+
+    def dequantize(self, quant, raw, out, rows, cols):
+        _check(self.lib.qw6cu_dequantize(self.h, quant, raw, out, rows, cols), "qw6cu_dequantize")
+
+    def matvec(self, quant, packed, x, y, rows, cols, ntok=1):
+        _check(self.lib.qw6cu_matvec(self.h, quant, packed, x, y, rows, cols, ntok), "qw6cu_matvec")
+
+    def matvec_f32(self, w, x, y, rows, cols):
+        _check(self.lib.qw6cu_matvec_f32(self.h, w, x, y, rows, cols), "qw6cu_matvec_f32")
+
+    def moe_route(self, logits, ntok, n_experts, top_k, idx, w):
+        _check(self.lib.qw6cu_moe_route(self.h, logits, ntok, n_experts, top_k, idx, w), "qw6cu_moe_route")
+
+    def argmax(self, x, n, idx, val):
+        _check(self.lib.qw6cu_argmax(self.h, x, n, idx, val), "qw6cu_argmax")
+
+    def moe_decode(self, gate: ExpertPack, up: ExpertPack, down: ExpertPack, logits, x, out, ntok, hidden, inter,
+                   n_experts, top_k):
+        _check(self.lib.qw6cu_moe_decode(self.h, C.byref(gate), C.byref(up), C.byref(down), logits, x, out, ntok,
+                                         hidden, inter, n_experts, top_k), "qw6cu_moe_decode")
+
+    @staticmethod
+    def moe_workspace_bytes(ntok, hidden, inter, n_experts, top_k) -> int:
+        return int(load().qw6cu_moe_workspace_bytes(ntok, hidden, inter, n_experts, top_k))

@@ -1,0 +1,52 @@
+"""CPU: the oracle reproduces the committed fixtures made by qw6's own code
+(tests/golden/gen_golden.py).  These run without the reference tree."""
+import hashlib
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from qw6_b200 import synth as S
+from tests.conftest import same_bits
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+@pytest.mark.parametrize("name", [S.QUANT_NAMES[q] for q in S.BLOCK_QUANTS])
+def test_golden_matvec(name, oracle):
+    g = np.load(GOLDEN / f"matvec_{name}.npz")
+    q, rows, cols = int(g["quant"]), int(g["rows"]), int(g["cols"])
+    assert same_bits(oracle.dequantize(q, g["w"], rows, cols), g["deq"])
+    assert same_bits(oracle.matvec(q, g["w"], g["x"], rows, cols), g["y"])
+    ns = g["w_special"].shape[0]
+    assert same_bits(oracle.dequantize(q, g["w_special"], ns, cols), g["deq_special"])
+
+
+def test_golden_route(oracle):
+    g = np.load(GOLDEN / "route.npz")
+    for lg, idx, w in zip(g["logits"], g["idx"], g["w"]):
+        i, ww = oracle.moe_route(lg, 8)
+        assert np.array_equal(i, idx) and same_bits(ww, w)
+
+
+def test_golden_argmax(oracle):
+    g = np.load(GOLDEN / "argmax.npz")
+    for x, n, idx in zip(g["x"], g["n"], g["idx"]):
+        assert oracle.argmax(x[:n]) == idx
+
+
+def golden_moe_weights():
+    g = np.load(GOLDEN / "moe_small.npz")
+    E, H, I, K, T = (int(v) for v in g["dims"])
+    rng = np.random.Generator(np.random.PCG64(int(g["seed"])))
+    gate, up, down = S.moe_weights(rng, E, S.Q4_K, S.Q6_K, H, I)
+    sha = hashlib.sha256(gate.tobytes() + up.tobytes() + down.tobytes()).hexdigest()
+    assert sha == str(g["sha"]), "synthetic generator drifted from the fixture"
+    return g, (E, H, I, K, T), (gate, up, down)
+
+
+def test_golden_moe(oracle):
+    g, (E, H, I, K, T), (gate, up, down) = golden_moe_weights()
+    out, idx, w = oracle.moe_layer(S.Q4_K, gate, up, S.Q6_K, down, g["logits"], g["x"], top_k=K)
+    assert np.array_equal(idx, g["idx"]) and same_bits(w, g["w"])
+    assert same_bits(out, g["out"])

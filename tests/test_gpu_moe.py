@@ -1,0 +1,76 @@
+"""GPU parity of the routed MoE FFN (qw6cu_moe_decode) against the oracle's
+composition of qw6_apply_layer_moe (qw6.c:2246-2264) and the golden fixture.
+Routing indices must match exactly; outputs within 1e-3 max relative error."""
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from qw6_b200 import lib as L
+from qw6_b200 import synth as S
+from tests.conftest import rel_err
+from tests.gpu_util import dev, empty_f32, host, pack, sync
+from tests.test_golden import golden_moe_weights
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+
+
+def run_moe(cuda, gq, gate, up, dq, down, logits, x, top_k):
+    E, I, H = gate.shape[0], gate.shape[1], x.shape[1]
+    T = x.shape[0]
+    pg, sg = pack(cuda, gq, gate, I, H, E)
+    pu, su = pack(cuda, gq, up, I, H, E)
+    pd, sd = pack(cuda, dq, down, H, I, E)
+    ld, xd = dev(logits), dev(x)
+    out = empty_f32(T, H)
+    sync(cuda)
+    cuda.moe_decode(L.ExpertPack(gq, pg.data_ptr(), sg), L.ExpertPack(gq, pu.data_ptr(), su),
+                    L.ExpertPack(dq, pd.data_ptr(), sd), ld.data_ptr(), xd.data_ptr(), out.data_ptr(), T, H, I, E,
+                    top_k)
+    cuda.synchronize()
+    return host(out)
+
+
+def test_moe_golden_small(cuda):
+    g, (E, H, I, K, T), (gate, up, down) = golden_moe_weights()
+    out = run_moe(cuda, S.Q4_K, gate, up, S.Q6_K, down, g["logits"], g["x"], K)
+    for t in range(T):
+        assert rel_err(out[t], g["out"][t]) <= TOL
+
+
+@pytest.mark.parametrize("ntok", [1, 2, 4, 5, 8, 17])
+def test_moe_small_experts_various_batches(ntok, cuda, oracle, rng):
+    E, H, I, K = 16, 2048, 512, 8
+    gate, up, down = S.moe_weights(rng, E, S.Q4_K, S.Q6_K, H, I)
+    logits = rng.standard_normal((ntok, E), dtype=np.float32)
+    x = rng.standard_normal((ntok, H), dtype=np.float32)
+    out = run_moe(cuda, S.Q4_K, gate, up, S.Q6_K, down, logits, x, K)
+    ref, _, _ = oracle.moe_layer(S.Q4_K, gate, up, S.Q6_K, down, logits, x, top_k=K)
+    for t in range(ntok):
+        assert rel_err(out[t], ref[t]) <= TOL, t
+
+
+def test_moe_config1_decode(cuda, oracle):
+    """Config 1: 256 experts, top-8, Q4_K gate/up, Q6_K down, one token."""
+    gate, up, down, logits, x = S.config1()
+    out = run_moe(cuda, S.Q4_K, gate, up, S.Q6_K, down, logits, x, 8)
+    ref, idx, w = oracle.moe_layer(S.Q4_K, gate, up, S.Q6_K, down, logits, x, top_k=8)
+    ref64 = oracle.moe_layer(S.Q4_K, gate, up, S.Q6_K, down, logits, x, top_k=8, f64=True)
+    assert rel_err(out[0], ref[0]) <= TOL
+    assert rel_err(out[0], ref64[0]) <= TOL
+
+
+def test_moe_config2_batched_iq2xxs(cuda, oracle):
+    """Config 2: 64 tokens, IQ2_XXS experts."""
+    gate, up, down, logits, x = S.config2()
+    out = run_moe(cuda, S.IQ2_XXS, gate, up, S.IQ2_XXS, down, logits, x, 8)
+    ref, _, _ = oracle.moe_layer(S.IQ2_XXS, gate, up, S.IQ2_XXS, down, logits, x, top_k=8)
+    errs = [rel_err(out[t], ref[t]) for t in range(x.shape[0])]
+    assert max(errs) <= TOL, max(errs)
+
+
+def test_moe_rejects_mixed_gate_up_quant(cuda):
+    with pytest.raises(L.Qw6CudaError):
+        cuda.moe_decode(L.ExpertPack(S.Q4_K, 16, 0), L.ExpertPack(S.Q5_K, 16, 0), L.ExpertPack(S.Q6_K, 16, 0),
+                        16, 16, 16, 1, 2048, 512, 8, 8)
