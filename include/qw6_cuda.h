@@ -111,9 +111,26 @@ int qw6cu_moe_decode(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu_
                      const qw6cu_expert_pack *down, const float *logits, const float *x, float *out, uint32_t ntok,
                      uint32_t hidden, uint32_t inter, uint32_t n_experts, uint32_t top_k);
 
+/* Same computation with HOST logits/x/out (copied in and out on the
+ * context stream); synchronous: returns after out is written. */
+int qw6cu_moe_decode_hostio(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
+                            const qw6cu_expert_pack *down, const float *logits, const float *x, float *out,
+                            uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t n_experts, uint32_t top_k);
+
 /* Device workspace qw6cu_moe_decode needs for these dimensions. */
 size_t qw6cu_moe_workspace_bytes(uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t n_experts,
                                  uint32_t top_k);
+
+/* ---- profiling ----
+ * Per-launch CUDA events around every kernel this context enqueues (the
+ * counterpart of qw6's QW6_PROFILE timestamp queries, qw6_vk.c:2315-2357).
+ * begin: allocate events for up to max_launches launches and start
+ * recording; end: synchronize, then write per-kernel-id total milliseconds
+ * and launch counts into arrays of QW6CU_NKERNELS entries and stop. */
+#define QW6CU_NKERNELS 9
+int qw6cu_profile_begin(qw6cu_ctx *ctx, uint32_t max_launches);
+int qw6cu_profile_end(qw6cu_ctx *ctx, double *ms_total, uint32_t *launches);
+const char *qw6cu_kernel_name(int kernel_id);
 
 #ifdef __cplusplus
 }

@@ -331,56 +331,74 @@ extern "C" size_t qw6k_moe_ws_bytes(uint32_t ntok, uint32_t hidden, uint32_t int
     return al256(tk * 4) * 3 + al256((size_t)mi * 16) + 256 + al256(tk * inter * 4) + al256(tk * hidden * 4);
 }
 
-extern "C" int qw6k_moe_decode(uint32_t gq, const void* gate, size_t gstride, const void* up, size_t ustride,
-                               uint32_t dq, const void* down, size_t dstride, const float* logits, const float* x,
-                               float* out, uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t ne,
-                               uint32_t topk, void* ws, size_t ws_bytes, cudaStream_t st) {
-    if (!gate || !up || !down || !logits || !x || !out || !ws || !ntok || !ne || ne > 256 || !topk || topk > 32 ||
-        topk > ne || (size_t)ntok * topk > 4096)
+static int moe_args(const qw6k_moe_desc* d, MoeArgs& a) {
+    if (!d || !d->gate || !d->up || !d->down || !d->logits || !d->x || !d->out || !d->ws || !d->ntok || !d->ne ||
+        d->ne > 256 || !d->topk || d->topk > 32 || d->topk > d->ne || (size_t)d->ntok * d->topk > 4096)
         return QW6K_ERR_ARG;
-    const uint32_t nbh = hidden / 256, nbi = inter / 256;
-    if (hidden % 512 || inter % 512 || nbh > 16 || nbi > 16 || hidden > 4096) return QW6K_ERR_ARG;
-    if (ws_bytes < qw6k_moe_ws_bytes(ntok, hidden, inter, ne, topk)) return QW6K_ERR_ARG;
-    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up) |
-         reinterpret_cast<uintptr_t>(down) | gstride | ustride | dstride) & 15u)
+    const uint32_t nbh = d->hidden / 256, nbi = d->inter / 256;
+    if (d->hidden % 512 || d->inter % 512 || nbh > 16 || nbi > 16 || d->hidden > 4096) return QW6K_ERR_ARG;
+    if (d->ws_bytes < qw6k_moe_ws_bytes(d->ntok, d->hidden, d->inter, d->ne, d->topk)) return QW6K_ERR_ARG;
+    if ((reinterpret_cast<uintptr_t>(d->x) | reinterpret_cast<uintptr_t>(d->gate) |
+         reinterpret_cast<uintptr_t>(d->up) | reinterpret_cast<uintptr_t>(d->down) | d->gstride | d->ustride |
+         d->dstride) & 15u)
         return QW6K_ERR_ALIGN;
-    MoeArgs a;
-    a.gate = (const uint8_t*)gate;
-    a.up = (const uint8_t*)up;
-    a.down = (const uint8_t*)down;
-    a.gstride = gstride;
-    a.ustride = ustride;
-    a.dstride = dstride;
-    a.logits = logits;
-    a.x = x;
-    a.out = out;
-    a.ntok = (int)ntok;
-    a.hidden = (int)hidden;
-    a.inter = (int)inter;
-    a.ne = (int)ne;
-    a.topk = (int)topk;
-    a.chunk = (int)moe_chunk(ntok);
+    a.gate = (const uint8_t*)d->gate;
+    a.up = (const uint8_t*)d->up;
+    a.down = (const uint8_t*)d->down;
+    a.gstride = d->gstride;
+    a.ustride = d->ustride;
+    a.dstride = d->dstride;
+    a.logits = d->logits;
+    a.x = d->x;
+    a.out = d->out;
+    a.ntok = (int)d->ntok;
+    a.hidden = (int)d->hidden;
+    a.inter = (int)d->inter;
+    a.ne = (int)d->ne;
+    a.topk = (int)d->topk;
+    a.chunk = (int)moe_chunk(d->ntok);
     a.ks_gu = (int)nbh / 2;
     a.ks_dn = (int)nbi / 2;
-    if ((inter / 16) % (kWarps / a.ks_gu) || (hidden / 16) % (kWarps / a.ks_dn)) return QW6K_ERR_ARG;
-    const size_t tk = (size_t)ntok * topk;
-    const int mi = moe_items_max(ntok, ne, topk, (uint32_t)a.chunk);
-    uint8_t* p = (uint8_t*)ws;
+    if ((a.inter / 16) % (kWarps / a.ks_gu) || (a.hidden / 16) % (kWarps / a.ks_dn)) return QW6K_ERR_ARG;
+    const size_t tk = (size_t)d->ntok * d->topk;
+    const int mi = moe_items_max(d->ntok, d->ne, d->topk, (uint32_t)a.chunk);
+    uint8_t* p = (uint8_t*)d->ws;
     a.idx = (int32_t*)p; p += al256(tk * 4);
     a.w = (float*)p; p += al256(tk * 4);
     a.order = (int32_t*)p; p += al256(tk * 4);
     a.items = (int4*)p; p += al256((size_t)mi * 16);
     a.nitems = (int*)p; p += 256;
-    a.mid = (float*)p; p += al256(tk * inter * 4);
+    a.mid = (float*)p; p += al256(tk * d->inter * 4);
     a.dout = (float*)p;
-    k_moe_plan<<<1, 512, 0, st>>>(a);
-    if (cudaPeekAtLastError() != cudaSuccess) return QW6K_ERR_CUDA;
+    return 0;
+}
+
+extern "C" int qw6k_moe_check(const qw6k_moe_desc* d) {
+    MoeArgs a;
+    return moe_args(d, a);
+}
+
+extern "C" int qw6k_moe_phase(const qw6k_moe_desc* d, int phase, cudaStream_t st) {
+    MoeArgs a;
+    const int rc = moe_args(d, a);
+    if (rc) return rc;
+    const int mi = moe_items_max(d->ntok, d->ne, d->topk, (uint32_t)a.chunk);
     const int nq = a.chunk / 4;
-    int rc = gateup_any(gq, nq, a, mi, st);
-    if (rc) return rc;
-    rc = down_any(dq, nq, a, mi, st);
-    if (rc) return rc;
-    dim3 cg((hidden + 255) / 256, ntok);
-    k_moe_combine<<<cg, 256, 0, st>>>(a);
+    switch (phase) {
+    case 0:
+        k_moe_plan<<<1, 512, 0, st>>>(a);
+        break;
+    case 1:
+        return gateup_any(d->gq, nq, a, mi, st);
+    case 2:
+        return down_any(d->dq, nq, a, mi, st);
+    case 3: {
+        dim3 cg((d->hidden + 255) / 256, d->ntok);
+        k_moe_combine<<<cg, 256, 0, st>>>(a);
+        break;
+    }
+    default:
+        return QW6K_ERR_ARG;
+    }
     return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
 }

@@ -106,10 +106,21 @@ int qw6cu_create(qw6cu_ctx **out, int device) {
     return 0;
 }
 
+static void prof_free(qw6cu_ctx *ctx) {
+    for (int i = 0; i < ctx->prof_cap; i++) {
+        cudaEventDestroy(ctx->prof[i].a);
+        cudaEventDestroy(ctx->prof[i].b);
+    }
+    free(ctx->prof);
+    ctx->prof = NULL;
+    ctx->prof_cap = ctx->prof_n = ctx->prof_on = 0;
+}
+
 void qw6cu_destroy(qw6cu_ctx *ctx) {
     if (!ctx) return;
     cudaSetDevice(ctx->device);
     cudaStreamSynchronize(ctx->st);
+    prof_free(ctx);
     for (int i = 0; i < QW6H_NBUF; i++) cudaFree(ctx->buf[i].p);
     cudaFreeHost(ctx->pinned);
     cudaStreamDestroy(ctx->own);
@@ -153,6 +164,74 @@ void *qw6h_buf(qw6cu_ctx *ctx, int i, size_t bytes) {
     return b->p;
 }
 
+/* --------------------------------------------------------- profiler --- */
+
+static const char *k_names[QW6H_K_COUNT] = {"matvec", "pack", "dequant", "route", "argmax",
+                                             "moe_plan", "moe_gateup", "moe_down", "moe_combine"};
+
+const char *qw6cu_kernel_name(int kid) { return kid >= 0 && kid < QW6H_K_COUNT ? k_names[kid] : "?"; }
+
+int qw6cu_profile_begin(qw6cu_ctx *ctx, uint32_t max_launches) {
+    int rc = qw6h_use(ctx);
+    if (rc) return rc;
+    prof_free(ctx);
+    if (max_launches == 0 || max_launches > (1u << 22)) {
+        qw6h_set_err("qw6cu_profile_begin: capacity %u out of range", max_launches);
+        return QW6CU_ERR_ARG;
+    }
+    ctx->prof = calloc(max_launches, sizeof *ctx->prof);
+    if (!ctx->prof) {
+        qw6h_set_err("qw6cu_profile_begin: out of host memory");
+        return QW6CU_ERR_NOMEM;
+    }
+    for (uint32_t i = 0; i < max_launches; i++) {
+        cudaError_t e1 = cudaEventCreate(&ctx->prof[i].a), e2 = cudaEventCreate(&ctx->prof[i].b);
+        if (e1 != cudaSuccess || e2 != cudaSuccess) {
+            ctx->prof_cap = (int)i;
+            prof_free(ctx);
+            return cuda_fail("cudaEventCreate", e1 != cudaSuccess ? e1 : e2);
+        }
+        ctx->prof_cap = (int)i + 1;
+    }
+    ctx->prof_n = 0;
+    ctx->prof_on = 1;
+    return 0;
+}
+
+int qw6h_prof_a(qw6cu_ctx *ctx, int kid) {
+    if (!ctx->prof_on || ctx->prof_n >= ctx->prof_cap) return -1;
+    qw6h_prof_rec *r = &ctx->prof[ctx->prof_n];
+    r->kid = kid;
+    cudaEventRecord(r->a, ctx->st);
+    return ctx->prof_n++;
+}
+
+void qw6h_prof_b(qw6cu_ctx *ctx, int rec) {
+    if (rec >= 0) cudaEventRecord(ctx->prof[rec].b, ctx->st);
+}
+
+int qw6cu_profile_end(qw6cu_ctx *ctx, double *ms_total, uint32_t *launches) {
+    int rc = qw6h_use(ctx);
+    if (rc) return rc;
+    for (int k = 0; k < QW6H_K_COUNT; k++) {
+        if (ms_total) ms_total[k] = 0.0;
+        if (launches) launches[k] = 0;
+    }
+    cudaError_t e = cudaStreamSynchronize(ctx->st);
+    if (e != cudaSuccess) return cuda_fail("cudaStreamSynchronize", e);
+    for (int i = 0; i < ctx->prof_n; i++) {
+        float ms = 0.f;
+        if ((e = cudaEventElapsedTime(&ms, ctx->prof[i].a, ctx->prof[i].b)) != cudaSuccess) {
+            prof_free(ctx);
+            return cuda_fail("cudaEventElapsedTime", e);
+        }
+        if (ms_total) ms_total[ctx->prof[i].kid] += ms;
+        if (launches) launches[ctx->prof[i].kid]++;
+    }
+    prof_free(ctx);
+    return 0;
+}
+
 /* ------------------------------------------------------- device API --- */
 
 size_t qw6cu_packed_bytes(uint32_t quant, uint32_t rows, uint32_t cols) { return qw6k_packed_bytes(quant, rows, cols); }
@@ -166,7 +245,10 @@ int qw6cu_pack(qw6cu_ctx *ctx, uint32_t quant, const void *raw, void *packed, ui
         qw6h_set_err("qw6cu_pack: bad shape/strides (quant %u, %u x %u)", quant, rows, cols);
         return QW6CU_ERR_ARG;
     }
-    return qw6h_rc(qw6k_pack(quant, raw, packed, rows, cols, count, raw_stride, packed_stride, ctx->st), "pack");
+    const int rec = qw6h_prof_a(ctx, QW6H_K_PACK);
+    rc = qw6h_rc(qw6k_pack(quant, raw, packed, rows, cols, count, raw_stride, packed_stride, ctx->st), "pack");
+    qw6h_prof_b(ctx, rec);
+    return rc;
 }
 
 int qw6cu_dequantize(qw6cu_ctx *ctx, uint32_t quant, const void *raw, float *out, uint32_t rows, uint32_t cols) {
@@ -179,7 +261,10 @@ int qw6cu_matvec(qw6cu_ctx *ctx, uint32_t quant, const void *packed, const float
                  uint32_t cols, uint32_t ntok) {
     int rc = qw6h_use(ctx);
     if (rc) return rc;
-    return qw6h_rc(qw6k_matvec(quant, packed, x, y, rows, cols, ntok, cols, rows, ctx->st), "matvec");
+    const int rec = qw6h_prof_a(ctx, QW6H_K_MATVEC);
+    rc = qw6h_rc(qw6k_matvec(quant, packed, x, y, rows, cols, ntok, cols, rows, ctx->st), "matvec");
+    qw6h_prof_b(ctx, rec);
+    return rc;
 }
 
 int qw6cu_matvec_f32(qw6cu_ctx *ctx, const float *w, const float *x, float *y, uint32_t rows, uint32_t cols) {

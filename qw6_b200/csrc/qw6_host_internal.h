@@ -24,6 +24,25 @@ typedef struct {
     size_t n;
 } qw6h_buf_t;
 
+/* Kernel ids of the profiler (names in qw6cu_kernel_name). */
+enum {
+    QW6H_K_MATVEC = 0,
+    QW6H_K_PACK,
+    QW6H_K_DEQUANT,
+    QW6H_K_ROUTE,
+    QW6H_K_ARGMAX,
+    QW6H_K_MOE_PLAN,
+    QW6H_K_MOE_GATEUP,
+    QW6H_K_MOE_DOWN,
+    QW6H_K_MOE_COMBINE,
+    QW6H_K_COUNT
+};
+
+typedef struct {
+    int kid;
+    cudaEvent_t a, b;
+} qw6h_prof_rec;
+
 struct qw6cu_ctx {
     int device;
     int num_sms;
@@ -31,6 +50,9 @@ struct qw6cu_ctx {
     cudaStream_t st;  /* stream work is enqueued on */
     qw6h_buf_t buf[QW6H_NBUF];
     void *pinned;     /* pinned host staging (unused unless requested) */
+    /* per-launch event profiler (qw6cu_profile_begin/end) */
+    int prof_on, prof_cap, prof_n;
+    qw6h_prof_rec *prof;
 };
 
 void qw6h_set_err(const char *fmt, ...);
@@ -38,5 +60,9 @@ int qw6h_rc(int rc, const char *what);
 int qw6h_use(qw6cu_ctx *ctx);
 void *qw6h_buf(qw6cu_ctx *ctx, int i, size_t bytes);
 qw6cu_ctx *qw6h_default_locked(void);
+/* Profiler hooks around one launch: rec = qw6h_prof_a(ctx, kid); launch;
+ * qw6h_prof_b(ctx, rec).  No-ops unless profiling is on. */
+int qw6h_prof_a(qw6cu_ctx *ctx, int kid);
+void qw6h_prof_b(qw6cu_ctx *ctx, int rec);
 
 #endif /* QW6_HOST_INTERNAL_H */

@@ -60,14 +60,24 @@ int qw6k_silu_mul(const float *gate, const float *up, float *out, uint32_t n, cu
 int qw6k_argmax(const float *x, uint32_t n, unsigned long long *key64, uint32_t *out_idx,
                 float *out_val, cudaStream_t st);
 
-/* Routed MoE FFN for ntok decode tokens (ntok*top_k <= 4096, hidden and
- * inter multiples of 512, hidden <= 4096).  Expert e's packed matrices at
- * base + e*stride.  ws: device workspace of qw6k_moe_ws_bytes(). */
+/* Routed MoE FFN for decode batches (ntok*top_k <= 4096, hidden and inter
+ * multiples of 512, hidden <= 4096).  Expert e's packed matrices live at
+ * base + e*stride.  The host runs the four phases in order on one stream:
+ * 0 plan (route + group by expert), 1 gate/up + silu, 2 down, 3 combine. */
+typedef struct {
+    uint32_t gq, dq;
+    const void *gate, *up, *down;
+    size_t gstride, ustride, dstride;
+    const float *logits, *x;
+    float *out;
+    uint32_t ntok, hidden, inter, ne, topk;
+    void *ws;
+    size_t ws_bytes;
+} qw6k_moe_desc;
+
 size_t qw6k_moe_ws_bytes(uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t ne, uint32_t topk);
-int qw6k_moe_decode(uint32_t gq, const void *gate, size_t gstride, const void *up, size_t ustride, uint32_t dq,
-                    const void *down, size_t dstride, const float *logits, const float *x, float *out,
-                    uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t ne, uint32_t topk, void *ws,
-                    size_t ws_bytes, cudaStream_t st);
+int qw6k_moe_check(const qw6k_moe_desc *d);
+int qw6k_moe_phase(const qw6k_moe_desc *d, int phase, cudaStream_t st);
 
 #ifdef __cplusplus
 }

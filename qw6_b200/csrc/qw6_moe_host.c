@@ -2,6 +2,9 @@
 #define _POSIX_C_SOURCE 200809L
 
 #include <stddef.h>
+#include <stdint.h>
+
+#include <cuda_runtime_api.h>
 
 #include "qw6_cuda.h"
 #include "qw6_host_internal.h"
@@ -12,20 +15,88 @@ size_t qw6cu_moe_workspace_bytes(uint32_t ntok, uint32_t hidden, uint32_t inter,
     return qw6k_moe_ws_bytes(ntok, hidden, inter, n_experts, top_k);
 }
 
+static int moe_desc(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
+                    const qw6cu_expert_pack *down, uint32_t ntok, uint32_t hidden, uint32_t inter,
+                    uint32_t n_experts, uint32_t top_k, qw6k_moe_desc *d) {
+    if (!gate || !up || !down || gate->quant != up->quant) {
+        qw6h_set_err("qw6cu_moe_decode: gate and up packs must be given and share one quant type");
+        return QW6CU_ERR_ARG;
+    }
+    d->gq = gate->quant;
+    d->dq = down->quant;
+    d->gate = gate->base;
+    d->up = up->base;
+    d->down = down->base;
+    d->gstride = gate->stride;
+    d->ustride = up->stride;
+    d->dstride = down->stride;
+    d->ntok = ntok;
+    d->hidden = hidden;
+    d->inter = inter;
+    d->ne = n_experts;
+    d->topk = top_k;
+    d->ws_bytes = qw6k_moe_ws_bytes(ntok, hidden, inter, n_experts, top_k);
+    d->ws = qw6h_buf(ctx, QW6H_BUF_WS, d->ws_bytes);
+    return d->ws ? 0 : QW6CU_ERR_NOMEM;
+}
+
+static int moe_run(qw6cu_ctx *ctx, const qw6k_moe_desc *d) {
+    int rc = qw6h_rc(qw6k_moe_check(d), "moe_decode");
+    static const int kid[4] = {QW6H_K_MOE_PLAN, QW6H_K_MOE_GATEUP, QW6H_K_MOE_DOWN, QW6H_K_MOE_COMBINE};
+    for (int ph = 0; ph < 4 && !rc; ph++) {
+        const int rec = qw6h_prof_a(ctx, kid[ph]);
+        rc = qw6h_rc(qw6k_moe_phase(d, ph, ctx->st), "moe_decode");
+        qw6h_prof_b(ctx, rec);
+    }
+    return rc;
+}
+
 int qw6cu_moe_decode(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
                      const qw6cu_expert_pack *down, const float *logits, const float *x, float *out, uint32_t ntok,
                      uint32_t hidden, uint32_t inter, uint32_t n_experts, uint32_t top_k) {
     int rc = qw6h_use(ctx);
     if (rc) return rc;
-    if (!gate || !up || !down || gate->quant != up->quant) {
-        qw6h_set_err("qw6cu_moe_decode: gate and up packs must be given and share one quant type");
+    qw6k_moe_desc d;
+    if ((rc = moe_desc(ctx, gate, up, down, ntok, hidden, inter, n_experts, top_k, &d))) return rc;
+    d.logits = logits;
+    d.x = x;
+    d.out = out;
+    return moe_run(ctx, &d);
+}
+
+int qw6cu_moe_decode_hostio(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
+                            const qw6cu_expert_pack *down, const float *logits, const float *x, float *out,
+                            uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t n_experts, uint32_t top_k) {
+    int rc = qw6h_use(ctx);
+    if (rc) return rc;
+    if (!logits || !x || !out) {
+        qw6h_set_err("qw6cu_moe_decode_hostio: null host buffer");
         return QW6CU_ERR_ARG;
     }
-    const size_t need = qw6k_moe_ws_bytes(ntok, hidden, inter, n_experts, top_k);
-    void *ws = qw6h_buf(ctx, QW6H_BUF_WS, need);
-    if (!ws) return QW6CU_ERR_NOMEM;
-    return qw6h_rc(qw6k_moe_decode(gate->quant, gate->base, gate->stride, up->base, up->stride, down->quant,
-                                   down->base, down->stride, logits, x, out, ntok, hidden, inter, n_experts, top_k,
-                                   ws, need, ctx->st),
-                   "moe_decode");
+    qw6k_moe_desc d;
+    if ((rc = moe_desc(ctx, gate, up, down, ntok, hidden, inter, n_experts, top_k, &d))) return rc;
+    const size_t lb = (size_t)ntok * n_experts * 4, xb = (size_t)ntok * hidden * 4;
+    uint8_t *in = qw6h_buf(ctx, QW6H_BUF_X, ((lb + 255) & ~(size_t)255) + xb);
+    float *dout = qw6h_buf(ctx, QW6H_BUF_Y, xb);
+    if (!in || !dout) return QW6CU_ERR_NOMEM;
+    d.logits = (const float *)in;
+    d.x = (const float *)(in + ((lb + 255) & ~(size_t)255));
+    d.out = dout;
+    cudaError_t e = cudaMemcpyAsync((void *)d.logits, logits, lb, cudaMemcpyHostToDevice, ctx->st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync((void *)d.x, x, xb, cudaMemcpyHostToDevice, ctx->st);
+    if (e != cudaSuccess) {
+        qw6h_set_err("qw6cu_moe_decode_hostio: H2D copy failed: %s", cudaGetErrorString(e));
+        return QW6CU_ERR_CUDA;
+    }
+    rc = moe_run(ctx, &d);
+    if (!rc && (e = cudaMemcpyAsync(out, dout, xb, cudaMemcpyDeviceToHost, ctx->st)) != cudaSuccess) {
+        qw6h_set_err("qw6cu_moe_decode_hostio: D2H copy failed: %s", cudaGetErrorString(e));
+        rc = QW6CU_ERR_CUDA;
+    }
+    e = cudaStreamSynchronize(ctx->st);
+    if (!rc && e != cudaSuccess) {
+        qw6h_set_err("qw6cu_moe_decode_hostio: %s", cudaGetErrorString(e));
+        rc = QW6CU_ERR_CUDA;
+    }
+    return rc;
 }
