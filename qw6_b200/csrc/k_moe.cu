@@ -57,17 +57,28 @@ __global__ void __launch_bounds__(512) k_moe_plan(const MoeArgs a) {
     __syncthreads();
     for (int i = tid; i < TK; i += blockDim.x) atomicAdd(&cnt[a.idx[i]], 1);
     __syncthreads();
-    if (tid == 0) {
-        int o = 0, c = 0;
-        for (int e = 0; e < a.ne; e++) {
-            off[e] = o;
-            ich[e] = c;
-            o += cnt[e];
-            c += (cnt[e] + a.chunk - 1) / a.chunk;
+    // exclusive scans of the per-expert counts and chunk counts: each of the
+    // first 8 warps scans 32 experts with shuffles, then the warp totals
+    __shared__ int wsum[2][8];
+    int v = 0, ch = 0;
+    if (tid < 256) {
+        v = tid < a.ne ? cnt[tid] : 0;
+        ch = (v + a.chunk - 1) / a.chunk;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int pv = __shfl_up_sync(0xffffffffu, v, o), pc = __shfl_up_sync(0xffffffffu, ch, o);
+            if (lane >= o) { v += pv; ch += pc; }
         }
-        off[a.ne] = o;
-        ich[a.ne] = c;
-        *a.nitems = c;
+        if (lane == 31) { wsum[0][warp] = v; wsum[1][warp] = ch; }
+    }
+    __syncthreads();
+    if (tid < 256) {
+        int bv = 0, bc = 0;
+        for (int w2 = 0; w2 < warp; w2++) { bv += wsum[0][w2]; bc += wsum[1][w2]; }
+        const int own = tid < a.ne ? cnt[tid] : 0;
+        off[tid] = bv + v - own;                           // exclusive
+        ich[tid] = bc + ch - (own + a.chunk - 1) / a.chunk;
+        if (tid == 255) { off[256] = bv + v; ich[256] = bc + ch; *a.nitems = bc + ch; }
     }
     __syncthreads();
     // stable counting sort: rank = earlier assignments with the same expert

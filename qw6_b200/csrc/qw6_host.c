@@ -198,16 +198,27 @@ int qw6cu_profile_begin(qw6cu_ctx *ctx, uint32_t max_launches) {
     return 0;
 }
 
+/* Inside stream capture an event must be recorded as an external node so
+ * that the graph replay timestamps it. */
+static void prof_record(cudaEvent_t ev, cudaStream_t st) {
+    enum cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(st, &cs);
+    if (cs == cudaStreamCaptureStatusActive)
+        cudaEventRecordWithFlags(ev, st, cudaEventRecordExternal);
+    else
+        cudaEventRecord(ev, st);
+}
+
 int qw6h_prof_a(qw6cu_ctx *ctx, int kid) {
     if (!ctx->prof_on || ctx->prof_n >= ctx->prof_cap) return -1;
     qw6h_prof_rec *r = &ctx->prof[ctx->prof_n];
     r->kid = kid;
-    cudaEventRecord(r->a, ctx->st);
+    prof_record(r->a, ctx->st);
     return ctx->prof_n++;
 }
 
 void qw6h_prof_b(qw6cu_ctx *ctx, int rec) {
-    if (rec >= 0) cudaEventRecord(ctx->prof[rec].b, ctx->st);
+    if (rec >= 0) prof_record(ctx->prof[rec].b, ctx->st);
 }
 
 int qw6cu_profile_end(qw6cu_ctx *ctx, double *ms_total, uint32_t *launches) {

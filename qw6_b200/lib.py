@@ -101,6 +101,11 @@ def load() -> C.CDLL:
     lib.qw6cu_argmax.argtypes = [_vp, _vp, _u32, _vp, _vp]
     pk = C.POINTER(ExpertPack)
     lib.qw6cu_moe_decode.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32]
+    lib.qw6cu_moe_decode_hostio.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32]
+    lib.qw6cu_profile_begin.argtypes = [_vp, _u32]
+    lib.qw6cu_profile_end.argtypes = [_vp, C.POINTER(C.c_double), C.POINTER(C.c_uint32)]
+    lib.qw6cu_kernel_name.argtypes = [C.c_int]
+    lib.qw6cu_kernel_name.restype = C.c_char_p
     lib.qw6cu_moe_workspace_bytes.argtypes = [_u32, _u32, _u32, _u32, _u32]
     lib.qw6cu_moe_workspace_bytes.restype = _sz
     _lib = lib
@@ -240,6 +245,23 @@ class Context:
                    n_experts, top_k):
         _check(self.lib.qw6cu_moe_decode(self.h, C.byref(gate), C.byref(up), C.byref(down), logits, x, out, ntok,
                                          hidden, inter, n_experts, top_k), "qw6cu_moe_decode")
+
+    def moe_decode_hostio(self, gate: ExpertPack, up: ExpertPack, down: ExpertPack, logits, x, out, ntok, hidden,
+                          inter, n_experts, top_k):
+        """Host pointers (ints) for logits/x/out; synchronous."""
+        _check(self.lib.qw6cu_moe_decode_hostio(self.h, C.byref(gate), C.byref(up), C.byref(down), logits, x, out,
+                                                ntok, hidden, inter, n_experts, top_k), "qw6cu_moe_decode_hostio")
+
+    def profile_begin(self, max_launches: int) -> None:
+        _check(self.lib.qw6cu_profile_begin(self.h, max_launches), "qw6cu_profile_begin")
+
+    def profile_end(self) -> dict:
+        """{kernel name: (total ms, launches)} for the kernels that ran."""
+        n = 9
+        ms = (C.c_double * n)()
+        cnt = (C.c_uint32 * n)()
+        _check(self.lib.qw6cu_profile_end(self.h, ms, cnt), "qw6cu_profile_end")
+        return {self.lib.qw6cu_kernel_name(i).decode(): (ms[i], cnt[i]) for i in range(n) if cnt[i]}
 
     @staticmethod
     def moe_workspace_bytes(ntok, hidden, inter, n_experts, top_k) -> int:
