@@ -364,7 +364,7 @@ def report(args, world, ms_max, prof, clk, e2e_steps, e2e_s, matvec, raw):
     # roofline of the dominant kernel (largest total time)
     per_launch = {
         "moe_gateup": TOPK * 2 * Q4K_BYTES_EXPERT + HIDDEN * 4 + TOPK * INTER * 4,
-        "moe_down": TOPK * Q6K_BYTES_EXPERT + TOPK * INTER * 4 + TOPK * HIDDEN * 4,
+        "moe_down": TOPK * Q6K_BYTES_EXPERT + TOPK * INTER * 4 + HIDDEN * 4,  # down + fused combine
     }
     dom = max((k for k in prof if k in per_launch), key=lambda k: prof[k][0])
     dom_ms = prof[dom][0] / prof[dom][1]

@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(kThreads) k_moe_gateup(const MoeArgs a) {
     IQTables* tbl = reinterpret_cast<IQTables*>(smem);
     XStage xs = xstage_carve(smem + tbl_bytes_of<F>(), 4 * NQ, a.hidden);
     float* red = reinterpret_cast<float*>(smem + tbl_bytes_of<F>() + xstage_bytes(4 * NQ, a.hidden));
-    if constexpr (IsIQ<F>::value) init_iq_tables(tbl, grid_ptr<F>(), GridBytes<F>::value);
+    if constexpr (IsIQ<F>::value) init_iq_tables(tbl, grid_ptr<F>(), GridBytes<F>::value, F == QW6F_IQ3_S);
     xstage_fill(xs, a.x, a.hidden, cnt, 4 * NQ, a.hidden, sel, a.topk);
     __syncthreads();
     const XView xv = xs.view();
@@ -208,7 +208,7 @@ __global__ void __launch_bounds__(kThreads) k_moe_down(const MoeArgs a) {
     IQTables* tbl = reinterpret_cast<IQTables*>(smem);
     XStage xs = xstage_carve(smem + tbl_bytes_of<F>(), 4 * NQ, a.inter);
     float* red = reinterpret_cast<float*>(smem + tbl_bytes_of<F>() + xstage_bytes(4 * NQ, a.inter));
-    if constexpr (IsIQ<F>::value) init_iq_tables(tbl, grid_ptr<F>(), GridBytes<F>::value);
+    if constexpr (IsIQ<F>::value) init_iq_tables(tbl, grid_ptr<F>(), GridBytes<F>::value, F == QW6F_IQ3_S);
     xstage_fill(xs, a.mid, a.inter, cnt, 4 * NQ, a.inter, sel, 1);
     __syncthreads();
     const XView xv = xs.view();
@@ -254,8 +254,200 @@ __global__ void __launch_bounds__(kThreads) k_moe_down(const MoeArgs a) {
     }
 }
 
+
+// ====================================================== small batches ====
+// ntok <= 4: every CTA routes the token(s) itself (no planner launch), lists
+// the distinct selected experts in ascending order, and takes expert
+// items[blockIdx / mgroups].  All ntok tokens share the 4 MMA columns, so an
+// expert chosen by several tokens is read once.  The down kernel is launched
+// with programmatic dependent launch: it routes and prefetches its weight
+// tiles while the gate/up kernel still runs, then waits for mid.
+
+struct SmallPlan {
+    int idx[32];
+    float w[32];
+    int items[32];      // distinct selected experts, ascending
+    int slot_item[32];  // assignment (t*topk + k) -> position in items
+    int nitems;
+    int rowsel[4];
+};
+
+__device__ __forceinline__ void small_plan(SmallPlan* P, const MoeArgs& a) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp < a.ntok)
+        route_token(a.logits + (size_t)warp * a.ne, a.ne, a.topk, P->idx + warp * a.topk, P->w + warp * a.topk,
+                    lane);
+    __syncthreads();
+    if (warp == 0) {
+        const int TK = a.ntok * a.topk;
+        const int e = lane < TK ? P->idx[lane] : 0x7fffffff;
+        bool first = lane < TK;
+        for (int j = 0; j < TK; j++)
+            if (j < lane && P->idx[j] == e) first = false;
+        const unsigned fm = __ballot_sync(0xffffffffu, first);
+        int rank = 0;
+        for (int j = 0; j < TK; j++)
+            if ((fm >> j) & 1u) rank += P->idx[j] < e;
+        if (first) P->items[rank] = e;
+        if (lane < TK) P->slot_item[lane] = rank;
+        if (lane == 0) P->nitems = __popc(fm);
+    }
+    __syncthreads();
+}
+
+template <int F, int NBW>
+__global__ void __launch_bounds__(kThreads) k_moe_small_gu(const MoeArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    using T = Tile<F, 1>;
+    constexpr int TB = T::TB;
+    __shared__ SmallPlan P;
+    pdl_trigger();
+    const int nbh = a.hidden / 256, ks = nbh / NBW, mpc = kWarps / ks;
+    const int mgroups = (a.inter / 16) / mpc;
+    const int item = blockIdx.x / mgroups, mg = blockIdx.x % mgroups;
+    small_plan(&P, a);
+    if (item >= P.nitems) return;
+    const int e = P.items[item];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ms = warp / ks, split = warp % ks, mt = mg * mpc + ms, b0 = split * NBW;
+    const uint8_t* gb = a.gate + (size_t)e * a.gstride + ((size_t)mt * nbh + b0) * TB;
+    const uint8_t* ub = a.up + (size_t)e * a.ustride + ((size_t)mt * nbh + b0) * TB;
+    typename T::Frag g[NBW], u[NBW];
+#pragma unroll
+    for (int i = 0; i < NBW; i++) {
+        T::load(g[i], gb + i * TB, lane);
+        T::load(u[i], ub + i * TB, lane);
+    }
+    if (blockIdx.x == 0 && threadIdx.x < a.ntok * a.topk) {
+        a.idx[threadIdx.x] = P.idx[threadIdx.x];
+        a.w[threadIdx.x] = P.w[threadIdx.x];
+    }
+    IQTables* tbl = reinterpret_cast<IQTables*>(smem);
+    XStage xs = xstage_carve(smem + tbl_bytes_of<F>(), 4, a.hidden);
+    float* red = reinterpret_cast<float*>(smem + tbl_bytes_of<F>() + xstage_bytes(4, a.hidden));
+    if constexpr (IsIQ<F>::value) init_iq_tables(tbl, grid_ptr<F>(), GridBytes<F>::value, F == QW6F_IQ3_S);
+    xstage_fill(xs, a.x, a.hidden, a.ntok, 4, a.hidden);
+    __syncthreads();
+    const XView xv = xs.view();
+    float ag[2][1] = {{0.f}, {0.f}}, au[2][1] = {{0.f}, {0.f}};
+#pragma unroll
+    for (int i = 0; i < NBW; i++) {
+        tile_dot<F, 1>(g[i], xv, b0 + i, ag, lane, tbl);
+        tile_dot<F, 1>(u[i], xv, b0 + i, au, lane, tbl);
+    }
+    if (ks > 1) {
+        float* r = red + (warp * 32 + lane) * 4;
+        r[0] = ag[0][0];
+        r[1] = ag[1][0];
+        r[2] = au[0][0];
+        r[3] = au[1][0];
+        __syncthreads();
+        if (split == 0) {
+            float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+            for (int p = 0; p < ks; p++) {
+                const float* rp = red + ((warp + p) * 32 + lane) * 4;
+                s0 += rp[0];
+                s1 += rp[1];
+                s2 += rp[2];
+                s3 += rp[3];
+            }
+            ag[0][0] = s0;
+            ag[1][0] = s1;
+            au[0][0] = s2;
+            au[1][0] = s3;
+        }
+    }
+    const int g8 = lane >> 2, t = lane & 3;
+    if (split == 0 && t < a.ntok) {
+        const float m0 = __fmul_rn(silu_exact(ag[0][0]), au[0][0]);
+        const float m1 = __fmul_rn(silu_exact(ag[1][0]), au[1][0]);
+        for (int k = 0; k < a.topk; k++)
+            if (P.idx[t * a.topk + k] == e) {
+                float* m = a.mid + (size_t)(t * a.topk + k) * a.inter + mt * 16 + g8;
+                m[0] = m0;
+                m[8] = m1;
+            }
+    }
+}
+
+// Down projection + routing-weighted combine, one CTA per 16 output rows:
+// warp w computes the rows for the selected experts items[w], items[w+8], ...
+// (all ntok tokens in the MMA columns), then the CTA sums
+// out[t][r] = sum_k w[t,k] * d_{e(t,k)}[t][r] in slot order k, rounded like
+// qw6's `out[i] += w[e] * tmp[i]` loop (qw6.c:2263).
+template <int F>
+__global__ void __launch_bounds__(kThreads) k_moe_small_down(const MoeArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    using T = Tile<F, 1>;
+    constexpr int TB = T::TB;
+    __shared__ SmallPlan P;
+    __shared__ int rs[32][4];
+    __shared__ float dres[32][4][16];
+    pdl_trigger();
+    small_plan(&P, a);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int mt = blockIdx.x, nbi = a.inter / 256, ni = P.nitems, TK = a.ntok * a.topk;
+    auto tptr = [&](int it, int b) {
+        return a.down + (size_t)P.items[it] * a.dstride + ((size_t)mt * nbi + b) * TB;
+    };
+    typename T::Frag fa, fb;
+    if (warp < ni) {  // prefetch while the gate/up kernel may still be running
+        T::load(fa, tptr(warp, 0), lane);
+        if (nbi > 1) T::load(fb, tptr(warp, 1), lane);
+    }
+    for (int i = threadIdx.x; i < ni * 4; i += blockDim.x) {
+        const int it = i >> 2, t = i & 3;
+        int r = -1;
+        if (t < a.ntok)
+            for (int k = a.topk - 1; k >= 0; k--)
+                if (P.idx[t * a.topk + k] == P.items[it]) r = t * a.topk + k;
+        rs[it][t] = r;
+    }
+    IQTables* tbl = reinterpret_cast<IQTables*>(smem);
+    uint8_t* stage0 = smem + tbl_bytes_of<F>();
+    const size_t sb = xstage_bytes(4, a.inter);
+    if constexpr (IsIQ<F>::value) init_iq_tables(tbl, grid_ptr<F>(), GridBytes<F>::value, F == QW6F_IQ3_S);
+    __syncthreads();
+    pdl_wait();  // mid from the gate/up kernel is complete and visible
+    for (int it = warp; it < ni; it += kWarps) {
+        if (it != warp) {
+            T::load(fa, tptr(it, 0), lane);
+            if (nbi > 1) T::load(fb, tptr(it, 1), lane);
+        }
+        // this warp stages (quantizes) only its own expert's mid rows
+        const XStage st = xstage_carve(stage0 + it * sb, 4, a.inter);
+        xstage_fill_warps(st, a.mid, a.inter, a.ntok, 4, a.inter, rs[it], 1, 0, 1);
+        __syncwarp();
+        const XView xv = st.view();
+        float acc[2][1] = {{0.f}, {0.f}};
+        for (int b = 0; b < nbi; b += 2) {
+            tile_dot<F, 1>(fa, xv, b, acc, lane, tbl);
+            if (b + 2 < nbi) T::load(fa, tptr(it, b + 2), lane);
+            if (b + 1 < nbi) {
+                tile_dot<F, 1>(fb, xv, b + 1, acc, lane, tbl);
+                if (b + 3 < nbi) T::load(fb, tptr(it, b + 3), lane);
+            }
+        }
+        const int g8 = lane >> 2, t = lane & 3;
+        dres[it][t][g8] = acc[0][0];
+        dres[it][t][g8 + 8] = acc[1][0];
+    }
+    __syncthreads();
+    if ((int)threadIdx.x < a.ntok * 16) {
+        const int t = threadIdx.x >> 4, r = threadIdx.x & 15;
+        float o = 0.f;
+        for (int k = 0; k < a.topk; k++) {
+            const int s = t * a.topk + k;
+            o = __fadd_rn(o, __fmul_rn(P.w[s], dres[P.slot_item[s]][t][r]));
+        }
+        a.out[(size_t)t * a.hidden + mt * 16 + r] = o;
+    }
+    (void)TK;
+}
+
 // --------------------------------------------------------------- combine --
 __global__ void k_moe_combine(const MoeArgs a) {
+    pdl_wait();
     const int t = blockIdx.y;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= a.hidden) return;
@@ -323,6 +515,63 @@ static int down_any(uint32_t q, int nq, const MoeArgs& a, int mi, cudaStream_t s
     QW6_MOE_DISPATCH(q, launch_down, 2, a, mi, st)
 }
 
+
+template <typename Kern>
+static int launch_ex(Kern k, int grid, size_t smem, bool pdl, cudaStream_t st, const MoeArgs& a) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k, a) == cudaSuccess ? 0 : QW6K_ERR_CUDA;
+}
+
+// K blocks per warp of the small-batch gate/up kernel: two (half the CTAs,
+// so the early-launched down kernel's CTAs find room) when there are >= 8.
+static int nbw_of(int nb) { return nb >= 8 ? 2 : 1; }
+
+template <int F, int NBW>
+static int launch_small_gu(const MoeArgs& a, cudaStream_t st) {
+    const size_t smem = tbl_bytes_of<F>() + xstage_bytes(4, a.hidden) + (size_t)kThreads * 4 * 4;
+    static bool cfg = false;
+    if (!cfg && cudaFuncSetAttribute(k_moe_small_gu<F, NBW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     200 * 1024) != cudaSuccess)
+        return QW6K_ERR_CUDA;
+    cfg = true;
+    const int ks = a.hidden / 256 / NBW, mgroups = (a.inter / 16) / (kWarps / ks);
+    return launch_ex(k_moe_small_gu<F, NBW>, a.ntok * a.topk * mgroups, smem, false, st, a);
+}
+
+template <int F>
+static size_t small_down_smem(const MoeArgs& a) {
+    return tbl_bytes_of<F>() + (size_t)a.ntok * a.topk * xstage_bytes(4, a.inter);
+}
+
+template <int F, int NBW>
+static int launch_small_down(const MoeArgs& a, cudaStream_t st) {
+    const size_t smem = small_down_smem<F>(a);
+    if (smem > 180 * 1024) return QW6K_ERR_ARG;
+    static bool cfg = false;
+    if (!cfg && cudaFuncSetAttribute(k_moe_small_down<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
+                    cudaSuccess)
+        return QW6K_ERR_CUDA;
+    cfg = true;
+    return launch_ex(k_moe_small_down<F>, a.hidden / 16, smem, true, st, a);
+}
+
+static int small_gu_any(uint32_t q, const MoeArgs& a, cudaStream_t st) {
+    if (nbw_of(a.hidden / 256) == 1) { QW6_MOE_DISPATCH(q, launch_small_gu, 1, a, st) }
+    QW6_MOE_DISPATCH(q, launch_small_gu, 2, a, st)
+}
+static int small_down_any(uint32_t q, const MoeArgs& a, cudaStream_t st) {
+    QW6_MOE_DISPATCH(q, launch_small_down, 1, a, st)
+}
+
 }  // namespace qw6
 
 using namespace qw6;
@@ -384,15 +633,40 @@ static int moe_args(const qw6k_moe_desc* d, MoeArgs& a) {
     return 0;
 }
 
+static bool moe_small(const qw6k_moe_desc* d) {
+    if (d->ntok > 4 || d->ntok * d->topk > 32) return false;
+    const int nbh = (int)d->hidden / 256;
+    const int ksh = nbh / nbw_of(nbh);
+    if (ksh > 8 || (d->inter / 16) % (kWarps / ksh)) return false;
+    return (size_t)d->ntok * d->topk * xstage_bytes(4, (int)d->inter) + sizeof(IQTables) <= 180 * 1024;
+}
+
 extern "C" int qw6k_moe_check(const qw6k_moe_desc* d) {
     MoeArgs a;
     return moe_args(d, a);
+}
+
+/* Number of launches of one layer and the kind of launch i
+ * (0 plan, 1 gate/up, 2 down, 3 combine). */
+extern "C" int qw6k_moe_nphases(const qw6k_moe_desc* d) { return moe_small(d) ? 2 : 4; }
+extern "C" int qw6k_moe_phase_kind(const qw6k_moe_desc* d, int phase) {
+    return moe_small(d) ? phase + 1 : phase;
 }
 
 extern "C" int qw6k_moe_phase(const qw6k_moe_desc* d, int phase, cudaStream_t st) {
     MoeArgs a;
     const int rc = moe_args(d, a);
     if (rc) return rc;
+    if (moe_small(d)) {
+        switch (phase) {
+        case 0:
+            return small_gu_any(d->gq, a, st);
+        case 1:
+            return small_down_any(d->dq, a, st);
+        default:
+            return QW6K_ERR_ARG;
+        }
+    }
     const int mi = moe_items_max(d->ntok, d->ne, d->topk, (uint32_t)a.chunk);
     const int nq = a.chunk / 4;
     switch (phase) {

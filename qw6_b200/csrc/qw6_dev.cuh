@@ -116,41 +116,57 @@ __device__ __forceinline__ void mma_k16(int (&d)[4], uint32_t a0, uint32_t a1, u
 }
 
 // ------------------------------------------------------------ tables ----
-
-// Shared-memory table block (IQ formats only): codebook + sign masks.
-//   sign8[i]  (IQ2_XXS): 4 words {mask bytes 0-3, 4-7, inc 0-3, inc 4-7} for
-//             the 8-bit pattern qw6_ksigns(i); mask byte 0xff negates.
-//   sign4[n]  (IQ2_S/IQ3_S): {mask, inc} for a 4-bit pattern n.
-// Negation of a byte g>0 is (g ^ 0xff) + 1, with no carry out of the byte.
+//
+// Codebooks are staged in shared memory as byte-SELECTOR tables for prmt:
+// every IQ2 grid byte is one of {8, 25, 43} and every IQ3_S grid byte one of
+// {1, 3, ..., 15}, so an entry is stored as one 4-bit selector per weight
+// (IQ2: 8 weights -> 32 bits; IQ3_S: 4 weights -> 16 bits) and expanded by
+// prmt against constant registers holding the value set.  Half the bytes of
+// the raw codebook per lookup means fewer shared-memory bank conflicts.
 struct IQTables {
-    uint4 sign8[128];
-    uint2 sign4[16];
-    uint8_t grid[8192];  // large enough for the IQ2_S codebook
+    uint32_t sel[1024];  // IQ2_XXS: 256 entries, IQ2_S: 1024 entries (32-bit); IQ3_S: 512 x 16-bit
 };
 
-__device__ __forceinline__ uint32_t nib_mask(uint32_t n) {
-    return ((n & 1u) ? 0xffu : 0u) | ((n & 2u) ? 0xff00u : 0u) | ((n & 4u) ? 0xff0000u : 0u) |
-           ((n & 8u) ? 0xff000000u : 0u);
+constexpr uint32_t kIQ2Vals = 0x002b1908u;               // bytes {8, 25, 43}
+constexpr uint32_t kIQ3Lo = 0x07050301u, kIQ3Hi = 0x0f0d0b09u;  // bytes {1..15 odd}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
 }
 
-// Fill the tables (all threads of the CTA participate; caller syncs).
-__device__ __forceinline__ void init_iq_tables(IQTables* tb, const uint8_t* grid_g, int grid_bytes) {
-    for (int i = threadIdx.x; i < 128; i += blockDim.x) {
-        const uint32_t s = qw6_ksigns((uint32_t)i);
-        const uint32_t m0 = nib_mask(s & 15u), m1 = nib_mask(s >> 4);
-        tb->sign8[i] = make_uint4(m0, m1, m0 & 0x01010101u, m1 & 0x01010101u);
+// Build the selector table from the raw grid bytes (all threads take part;
+// the caller synchronizes).  iq3: 4-byte entries -> 16-bit selectors.
+__device__ __forceinline__ void init_iq_tables(IQTables* tb, const uint8_t* grid_g, int grid_bytes, bool iq3) {
+    if (!iq3) {
+        for (int e = threadIdx.x; e < grid_bytes / 8; e += blockDim.x) {
+            uint32_t v = 0;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const uint32_t b = grid_g[8 * e + j];
+                v |= (b == 8u ? 0u : b == 25u ? 1u : 2u) << (4 * j);
+            }
+            tb->sel[e] = v;
+        }
+    } else {
+        uint16_t* s16 = reinterpret_cast<uint16_t*>(tb->sel);
+        for (int e = threadIdx.x; e < grid_bytes / 4; e += blockDim.x) {
+            uint32_t v = 0;
+#pragma unroll
+            for (int j = 0; j < 4; j++) v |= ((uint32_t)(grid_g[4 * e + j] >> 1)) << (4 * j);
+            s16[e] = (uint16_t)v;
+        }
     }
-    for (int i = threadIdx.x; i < 16; i += blockDim.x) {
-        const uint32_t m = nib_mask((uint32_t)i);
-        tb->sign4[i] = make_uint2(m, m & 0x01010101u);
-    }
-    const uint4* src = reinterpret_cast<const uint4*>(grid_g);
-    uint4* dst = reinterpret_cast<uint4*>(tb->grid);
-    for (int i = threadIdx.x; i < grid_bytes / 16; i += blockDim.x) dst[i] = src[i];
 }
 
-__device__ __forceinline__ uint32_t apply_sign(uint32_t g, uint32_t m, uint32_t inc) {
-    return (g ^ m) + inc;
+// Sign handling without tables: bits of a 4-bit pattern n go to the low bit
+// of the 4 bytes (multiply by 2^0+2^7+2^14+2^21, no carries), then
+// negation of those bytes is (g ^ 0xff) + 1 per byte (g > 0: no carry out).
+__device__ __forceinline__ uint32_t nib_inc(uint32_t n) { return ((n & 15u) * 0x00204081u) & 0x01010101u; }
+__device__ __forceinline__ uint32_t signed_bytes(uint32_t g, uint32_t n) {
+    const uint32_t inc = nib_inc(n);
+    return (g ^ (inc * 255u)) + inc;
 }
 
 // --------------------------------------------------- packed tile layout ---
@@ -324,21 +340,46 @@ __device__ __forceinline__ XStage xstage_carve(uint8_t* base, int ntp, int cols)
     return s;
 }
 
+__device__ __forceinline__ void xstage_fill_warps(const XStage& s, const float* __restrict__ x, int ldx, int ntok,
+                                                  int ntp, int cols, const int32_t* rowsel, int rowdiv,
+                                                  int first_warp, int nwarps);
+
 // Quantize ntok token rows of x (row stride ldx floats) into the stage;
 // tokens [ntok, ntp) are zero.  Stage row j reads x row j, or row
-// rowsel[j] / rowdiv when rowsel is given (gather through an index list).
+// rowsel[j] / rowdiv when rowsel is given (gather through an index list; a
+// negative entry stages a zero row).
 // One warp per (token, 256-block); all threads of the CTA must call it
 // (caller synchronizes afterwards).
 __device__ __forceinline__ void xstage_fill(const XStage& s, const float* __restrict__ x, int ldx,
                                             int ntok, int ntp, int cols, const int32_t* rowsel = nullptr,
                                             int rowdiv = 1) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    xstage_fill_warps(s, x, ldx, ntok, ntp, cols, rowsel, rowdiv, threadIdx.x >> 5, blockDim.x >> 5);
+}
+
+// Same, executed by warps first_warp, first_warp + nwarps, ... only (no
+// block-wide synchronization inside; a single warp may stage on its own).
+__device__ __forceinline__ void xstage_fill_warps(const XStage& s, const float* __restrict__ x, int ldx, int ntok,
+                                                  int ntp, int cols, const int32_t* rowsel, int rowdiv,
+                                                  int first_warp, int nwarps) {
+    const int warp = first_warp, lane = threadIdx.x & 31, nw = nwarps;
     const int nb = cols / 256;
     for (int item = warp; item < ntp * nb; item += nw) {
         const int tok = item / nb, b = item % nb;
         float v[8];
-        if (tok < ntok) {
-            const int srow = rowsel ? rowsel[tok] / rowdiv : tok;
+        const int sel = (tok < ntok) ? (rowsel ? rowsel[tok] : tok) : -1;
+        if (sel < 0) {  // zero row: warp-uniform fast path
+            *reinterpret_cast<uint2*>(s.q + (tok * 2 + 0) * s.stride + 256 * b + 8 * lane) = make_uint2(0u, 0u);
+            *reinterpret_cast<uint2*>(s.q + (tok * 2 + 1) * s.stride + 256 * b + 8 * lane) = make_uint2(0u, 0u);
+            if ((lane & 3) == 0) {
+                const int j = tok * s.ns + 8 * b + (lane >> 2);
+                s.xsum[j] = 0.f;
+                s.nx32[j] = make_int2(0, 0);
+            }
+            if (lane == 0) s.sx[tok * nb + b] = 0.f;
+            continue;
+        }
+        if (sel >= 0) {
+            const int srow = rowsel ? sel / rowdiv : sel;
             const float4* src = reinterpret_cast<const float4*>(x + (size_t)srow * ldx + 256 * b + 8 * lane);
             const float4 u0 = src[0], u1 = src[1];
             v[0] = u0.x; v[1] = u0.y; v[2] = u0.z; v[3] = u0.w;
@@ -384,6 +425,14 @@ __device__ __forceinline__ void xstage_fill(const XStage& s, const float* __rest
         if (lane == 0) s.sx[tok * nb + b] = amax > 0.f ? amax / 32639.f : 0.f;
     }
 }
+
+// ------------------------------------------- programmatic dependent launch -
+// A kernel launched with the programmatic-serialization attribute may start
+// while its predecessor in the stream still runs; pdl_wait() blocks until
+// the predecessor grid has completed and its writes are visible (a no-op when
+// launched normally).  pdl_trigger() lets the successor start early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // ------------------------------------------------ per-format decoders ---
 //
@@ -606,11 +655,11 @@ struct Tile<QW6F_IQ2_XXS, NQ> {
                 const uint32_t gi = byte_of(iw, j & 3);
                 const uint32_t aw = word_of(f.aux[rh][j >> 2], j & 3);
                 const uint32_t sf = (aw >> (7 * t)) & 127u;
+                const uint32_t s8 = sf | ((__popc(sf) & 1u) << 7);  // qw6_ksigns(sf)
                 scl[rh] = 2 * (int)(aw >> 28) + 1;
-                const uint2 gr = *reinterpret_cast<const uint2*>(tbl->grid + gi * 8);
-                const uint4 sm = tbl->sign8[sf];
-                lo[rh] = apply_sign(gr.x, sm.x, sm.z);
-                hi[rh] = apply_sign(gr.y, sm.y, sm.w);
+                const uint32_t sel = tbl->sel[gi];
+                lo[rh] = signed_bytes(prmt(kIQ2Vals, kIQ2Vals, sel), s8);
+                hi[rh] = signed_bytes(prmt(kIQ2Vals, kIQ2Vals, sel >> 16), s8 >> 4);
             }
 #pragma unroll
             for (int qt = 0; qt < NQ; qt++) {
@@ -666,10 +715,9 @@ struct Tile<QW6F_IQ2_S, NQ> {
                     const uint32_t ib = byte16(f.P[rh][0], 2 * j + hh);
                     const uint32_t qhb = byte_of(j < 4 ? f.sh[rh].x : f.sh[rh].y, j & 3);
                     const uint32_t gi = ib | (((qhb >> (2 * l)) & 3u) << 8);
-                    const uint32_t gw = *reinterpret_cast<const uint32_t*>(tbl->grid + gi * 8 + half4);
+                    const uint32_t gw = prmt(kIQ2Vals, kIQ2Vals, tbl->sel[gi] >> (4 * half4));
                     const uint32_t sb = byte16(f.P[rh][1], 2 * j + hh);
-                    const uint2 sm = tbl->sign4[(sb >> half4) & 15u];
-                    a[rh] = apply_sign(gw, sm.x, sm.y);
+                    a[rh] = signed_bytes(gw, sb >> half4);
                     const uint32_t scb = byte_of(j < 4 ? f.sh[rh].z : f.sh[rh].w, j & 3);
                     scl[rh] = 2 * (int)((scb >> (4 * hh)) & 15u) + 1;
                 }
@@ -727,12 +775,12 @@ struct Tile<QW6F_IQ3_S, NQ> {
                 const uint32_t qhb = byte_of(j < 4 ? f.qh[rh].x : f.qh[rh].y, j & 3);
                 const uint32_t g1 = i1 | (((qhb >> (2 * t)) & 1u) << 8);
                 const uint32_t g2 = i2 | (((qhb >> (2 * t + 1)) & 1u) << 8);
-                const uint32_t gw1 = *reinterpret_cast<const uint32_t*>(tbl->grid + g1 * 4);
-                const uint32_t gw2 = *reinterpret_cast<const uint32_t*>(tbl->grid + g2 * 4);
+                const uint16_t* s16 = reinterpret_cast<const uint16_t*>(tbl->sel);
+                const uint32_t gw1 = prmt(kIQ3Lo, kIQ3Hi, s16[g1]);
+                const uint32_t gw2 = prmt(kIQ3Lo, kIQ3Hi, s16[g2]);
                 const uint32_t sb = byte_of(rh ? (j < 4 ? f.c[2].z : f.c[2].w) : (j < 4 ? f.c[2].x : f.c[2].y), j & 3);
-                const uint2 m1 = tbl->sign4[sb & 15u], m2 = tbl->sign4[sb >> 4];
-                lo[rh] = apply_sign(gw1, m1.x, m1.y);
-                hi[rh] = apply_sign(gw2, m2.x, m2.y);
+                lo[rh] = signed_bytes(gw1, sb);
+                hi[rh] = signed_bytes(gw2, sb >> 4);
                 const uint32_t scb = byte_of(f.sc[rh], j >> 1);
                 scl[rh] = 1 + 2 * (int)((j & 1) ? (scb >> 4) : (scb & 15u));
             }

@@ -62,8 +62,9 @@ int qw6k_argmax(const float *x, uint32_t n, unsigned long long *key64, uint32_t 
 
 /* Routed MoE FFN for decode batches (ntok*top_k <= 4096, hidden and inter
  * multiples of 512, hidden <= 4096).  Expert e's packed matrices live at
- * base + e*stride.  The host runs the four phases in order on one stream:
- * 0 plan (route + group by expert), 1 gate/up + silu, 2 down, 3 combine. */
+ * base + e*stride.  The host runs qw6k_moe_nphases() launches in order on
+ * one stream: for ntok <= 4 gate/up (self-routed), down, combine; otherwise
+ * plan (route + group by expert), gate/up + silu, down, combine. */
 typedef struct {
     uint32_t gq, dq;
     const void *gate, *up, *down;
@@ -77,6 +78,8 @@ typedef struct {
 
 size_t qw6k_moe_ws_bytes(uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t ne, uint32_t topk);
 int qw6k_moe_check(const qw6k_moe_desc *d);
+int qw6k_moe_nphases(const qw6k_moe_desc *d);
+int qw6k_moe_phase_kind(const qw6k_moe_desc *d, int phase); /* 0 plan, 1 gate/up, 2 down, 3 combine */
 int qw6k_moe_phase(const qw6k_moe_desc *d, int phase, cudaStream_t st);
 
 #ifdef __cplusplus

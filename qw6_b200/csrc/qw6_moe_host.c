@@ -43,8 +43,9 @@ static int moe_desc(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu_e
 static int moe_run(qw6cu_ctx *ctx, const qw6k_moe_desc *d) {
     int rc = qw6h_rc(qw6k_moe_check(d), "moe_decode");
     static const int kid[4] = {QW6H_K_MOE_PLAN, QW6H_K_MOE_GATEUP, QW6H_K_MOE_DOWN, QW6H_K_MOE_COMBINE};
-    for (int ph = 0; ph < 4 && !rc; ph++) {
-        const int rec = qw6h_prof_a(ctx, kid[ph]);
+    const int n = rc ? 0 : qw6k_moe_nphases(d);
+    for (int ph = 0; ph < n && !rc; ph++) {
+        const int rec = qw6h_prof_a(ctx, kid[qw6k_moe_phase_kind(d, ph)]);
         rc = qw6h_rc(qw6k_moe_phase(d, ph, ctx->st), "moe_decode");
         qw6h_prof_b(ctx, rec);
     }

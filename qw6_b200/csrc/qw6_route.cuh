@@ -6,14 +6,22 @@
 
 namespace qw6 {
 
-// ---------------------------------------------------------------- route --
-// One warp per token.  Lane l holds logits l, l+32, ..., so scanning its
-// slots in order and keeping strict '>' finds its lowest-index maximum; the
-// warp merge prefers the higher value, then the lower index.  qw6's scan
-// starts from element 0 and only replaces on a strict '>', hence: a NaN at
-// index 0 wins the round; any other NaN never wins (treated as -inf); when
-// every remaining value is -inf, index 0 is chosen (possibly again).
+// Order-preserving map float -> uint32 (larger float, larger key).  NaN maps
+// to the key of -inf: in qw6's scan a NaN never replaces the running best.
+__device__ __forceinline__ uint32_t route_key(float v) {
+    if (isnan(v)) v = -INFINITY;
+    const uint32_t b = __float_as_uint(v);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
 
+// One warp per token.  Lane l holds logits l, l+32, ..., l+224.  A round
+// picks the largest value, lowest index on ties (qw6 starts from element 0 and
+// replaces only on a strict '>'), via redux.sync: max over the lanes' local
+// best keys, then min over the indices that reach it.  Special cases kept
+// from the CPU scan: a NaN at index 0 wins its round; the winner is set to
+// -inf, not removed, so when all remaining values are -inf index 0 is chosen
+// (again).  Softmax over the selected logits as qw6 does: max-subtract, expf,
+// sum in selection order, divide.
 __device__ __forceinline__ void route_token(const float* __restrict__ lg, int ne, int k, int32_t* __restrict__ idx,
                                             float* __restrict__ w, int lane) {
     float v[8];
@@ -22,33 +30,24 @@ __device__ __forceinline__ void route_token(const float* __restrict__ lg, int ne
         const int e = lane + 32 * i;
         v[i] = e < ne ? lg[e] : -INFINITY;
     }
-    float sel[32];
-    int seli[32];
+    float sel_v = 0.f;  // lane r keeps round r's value and index
+    int sel_i = 0;
     for (int r = 0; r < k; r++) {
-        float bv = -INFINITY;
+        uint32_t bk = 0;
         int bi = 0x7fffffff;
 #pragma unroll
         for (int i = 0; i < 8; i++) {
             const int e = lane + 32 * i;
-            const float c = isnan(v[i]) ? -INFINITY : v[i];
-            if (e < ne && (c > bv || bi == 0x7fffffff)) {
-                bv = c;
+            const uint32_t kk = route_key(v[i]);
+            if (e < ne && (kk > bk || bi == 0x7fffffff)) {
+                bk = kk;
                 bi = e;
             }
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ov > bv || (ov == bv && oi < bi)) {
-                bv = ov;
-                bi = oi;
-            }
-        }
-        const float v0 = __shfl_sync(0xffffffffu, v[0], 0);
-        if (isnan(v0)) bi = 0;
-        // the winner's original value (NaN stays NaN)
-        const int owner = bi & 31, slot = bi >> 5;
+        const uint32_t mk = __reduce_max_sync(0xffffffffu, bi == 0x7fffffff ? 0u : bk);
+        int win = (int)__reduce_min_sync(0xffffffffu, (bi != 0x7fffffff && bk == mk) ? (uint32_t)bi : 0xffffffffu);
+        if (__shfl_sync(0xffffffffu, isnan(v[0]) ? 1 : 0, 0)) win = 0;
+        const int owner = win & 31, slot = win >> 5;
         float mine = 0.f;
 #pragma unroll
         for (int i = 0; i < 8; i++)
@@ -59,23 +58,26 @@ __device__ __forceinline__ void route_token(const float* __restrict__ lg, int ne
             for (int i = 0; i < 8; i++)
                 if (i == slot) v[i] = -INFINITY;
         }
-        sel[r & 31] = orig;
-        seli[r & 31] = bi;
+        if (lane == (r & 31)) {
+            sel_v = orig;
+            sel_i = win;
+        }
     }
+    // softmax over the k selected values, in selection order, on lane 0
+    float vals[32];
+    for (int r = 0; r < k; r++) vals[r] = __shfl_sync(0xffffffffu, sel_v, r);
     if (lane == 0) {
-        float mx = sel[0];
+        float mx = vals[0];
         for (int r = 1; r < k; r++)
-            if (sel[r] > mx) mx = sel[r];
+            if (vals[r] > mx) mx = vals[r];
         float sum = 0.f;
         for (int r = 0; r < k; r++) {
-            sel[r] = expf(__fsub_rn(sel[r], mx));
-            sum = __fadd_rn(sum, sel[r]);
+            vals[r] = expf(__fsub_rn(vals[r], mx));
+            sum = __fadd_rn(sum, vals[r]);
         }
-        for (int r = 0; r < k; r++) {
-            idx[r] = seli[r];
-            w[r] = __fdiv_rn(sel[r], sum);
-        }
+        for (int r = 0; r < k; r++) w[r] = __fdiv_rn(vals[r], sum);
     }
+    if (lane < k) idx[lane] = sel_i;
 }
 
 }  // namespace qw6

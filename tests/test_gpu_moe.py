@@ -39,7 +39,7 @@ def test_moe_golden_small(cuda):
         assert rel_err(out[t], g["out"][t]) <= TOL
 
 
-@pytest.mark.parametrize("ntok", [1, 2, 4, 5, 8, 17])
+@pytest.mark.parametrize("ntok", [1, 2, 3, 4, 5, 8, 17])
 def test_moe_small_experts_various_batches(ntok, cuda, oracle, rng):
     E, H, I, K = 16, 2048, 512, 8
     gate, up, down = S.moe_weights(rng, E, S.Q4_K, S.Q6_K, H, I)
@@ -74,3 +74,44 @@ def test_moe_rejects_mixed_gate_up_quant(cuda):
     with pytest.raises(L.Qw6CudaError):
         cuda.moe_decode(L.ExpertPack(S.Q4_K, 16, 0), L.ExpertPack(S.Q5_K, 16, 0), L.ExpertPack(S.Q6_K, 16, 0),
                         16, 16, 16, 1, 2048, 512, 8, 8)
+
+
+@pytest.mark.parametrize("ntok", [1, 3, 6])
+def test_moe_duplicate_expert_selection(ntok, cuda, oracle, rng):
+    """All logits -inf except two: qw6's scan then re-selects expert 0 for the
+    remaining slots (the winner is set to -inf, not removed); the same expert
+    appears in several slots of one token and its output is summed per slot."""
+    E, H, I, K = 16, 2048, 512, 8
+    gate, up, down = S.moe_weights(rng, E, S.Q4_K, S.Q6_K, H, I)
+    logits = np.full((ntok, E), -np.inf, np.float32)
+    logits[:, 5] = 1.0
+    logits[:, 9] = 0.5
+    x = rng.standard_normal((ntok, H), dtype=np.float32)
+    out = run_moe(cuda, S.Q4_K, gate, up, S.Q6_K, down, logits, x, K)
+    ref, idx, _ = oracle.moe_layer(S.Q4_K, gate, up, S.Q6_K, down, logits, x, top_k=K)
+    assert list(idx[0]) == [5, 9, 0, 0, 0, 0, 0, 0]
+    for t in range(ntok):
+        assert rel_err(out[t], ref[t]) <= TOL, t
+
+
+def test_moe_hidden_4096(cuda, oracle, rng):
+    E, H, I, K, T = 8, 4096, 512, 4, 2
+    gate, up, down = S.moe_weights(rng, E, S.Q5_K, S.IQ3_S, H, I)
+    logits = rng.standard_normal((T, E), dtype=np.float32)
+    x = rng.standard_normal((T, H), dtype=np.float32)
+    out = run_moe(cuda, S.Q5_K, gate, up, S.IQ3_S, down, logits, x, K)
+    ref, _, _ = oracle.moe_layer(S.Q5_K, gate, up, S.IQ3_S, down, logits, x, top_k=K)
+    for t in range(T):
+        assert rel_err(out[t], ref[t]) <= TOL, t
+
+
+@pytest.mark.parametrize("gq,dq", [(S.IQ2_S, S.Q4_K), (S.IQ2_XXS, S.IQ2_XXS), (S.Q6_K, S.Q5_K)])
+def test_moe_format_mixes(gq, dq, cuda, oracle, rng):
+    E, H, I, K, T = 12, 2048, 512, 4, 3
+    gate, up, down = S.moe_weights(rng, E, gq, dq, H, I)
+    logits = rng.standard_normal((T, E), dtype=np.float32)
+    x = rng.standard_normal((T, H), dtype=np.float32)
+    out = run_moe(cuda, gq, gate, up, dq, down, logits, x, K)
+    ref, _, _ = oracle.moe_layer(gq, gate, up, dq, down, logits, x, top_k=K)
+    for t in range(T):
+        assert rel_err(out[t], ref[t]) <= TOL, t
