@@ -117,6 +117,28 @@ int qw6cu_moe_decode_hostio(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const
                             const qw6cu_expert_pack *down, const float *logits, const float *x, float *out,
                             uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t n_experts, uint32_t top_k);
 
+/* Allocation-free qw6cu_moe_decode, for callers that cannot allocate device
+ * memory when they run the layer: code inside a CUDA stream capture, where a
+ * cudaMalloc would invalidate the capture, or a runtime that hands out all
+ * device memory from its own pool.  It has no counterpart in the reference.
+ * Scratch is a fixed 1 MiB array in device memory that the library owns
+ * (every GPU that loads the library holds it until the process exits), so
+ * shapes whose workspace (qw6cu_moe_workspace_bytes) exceeds 1 MiB are
+ * rejected with QW6CU_ERR_ARG -- for hidden 2048, inter 512, 256 experts,
+ * top-8 that is ntok > 12.  Inputs, outputs and weights are device pointers
+ * owned by the caller; work is enqueued on `stream` (a cudaStream_t, NULL =
+ * the legacy default stream) on the calling thread's current device.  The
+ * first call on a device looks up the array's device address (no allocation);
+ * make that first call before any stream capture.  Every call shares the
+ * array and leaves its contents behind; nothing in it needs to start at zero
+ * because each call writes every scratch byte it later reads.  Calls that can
+ * overlap on the GPU (different streams, or graphs replayed concurrently)
+ * race on the array and must be serialized by the caller. */
+int qw6cu_moe_decode_noalloc(const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
+                             const qw6cu_expert_pack *down, const float *logits, const float *x, float *out,
+                             uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t n_experts, uint32_t top_k,
+                             void *stream);
+
 /* Device workspace qw6cu_moe_decode needs for these dimensions. */
 size_t qw6cu_moe_workspace_bytes(uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t n_experts,
                                  uint32_t top_k);

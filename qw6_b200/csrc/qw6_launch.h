@@ -82,6 +82,13 @@ int qw6k_moe_nphases(const qw6k_moe_desc *d);
 int qw6k_moe_phase_kind(const qw6k_moe_desc *d, int phase); /* 0 plan, 1 gate/up, 2 down, 3 combine */
 int qw6k_moe_phase(const qw6k_moe_desc *d, int phase, cudaStream_t st);
 
+/* Fixed 1 MiB device scratch (k_static.cu) of the allocation-free MoE entry
+ * point; *ptr is its device address on the current device (looked up with
+ * cudaGetSymbolAddress on the first call per device). */
+#define QW6K_STATIC_SCRATCH_BYTES (1u << 20)
+#define QW6K_MAX_DEVICES 64
+int qw6k_static_scratch(void **ptr, size_t *bytes);
+
 #ifdef __cplusplus
 }
 #endif

@@ -101,3 +101,52 @@ int qw6cu_moe_decode_hostio(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const
     }
     return rc;
 }
+
+/* Allocation-free variant: the workspace is the library's fixed 1 MiB device
+ * array (k_static.cu) instead of a context buffer, and work goes on the
+ * caller's stream on the calling thread's current device. */
+int qw6cu_moe_decode_noalloc(const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
+                             const qw6cu_expert_pack *down, const float *logits, const float *x, float *out,
+                             uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t n_experts, uint32_t top_k,
+                             void *stream) {
+    if (!gate || !up || !down || gate->quant != up->quant) {
+        qw6h_set_err("qw6cu_moe_decode_noalloc: gate and up packs must be given and share one quant type");
+        return QW6CU_ERR_ARG;
+    }
+    void *scratch = NULL;
+    size_t cap = 0;
+    if (qw6k_static_scratch(&scratch, &cap)) {
+        qw6h_set_err("qw6cu_moe_decode_noalloc: cudaGetSymbolAddress of the fixed scratch failed");
+        return QW6CU_ERR_CUDA;
+    }
+    qw6k_moe_desc d;
+    d.gq = gate->quant;
+    d.dq = down->quant;
+    d.gate = gate->base;
+    d.up = up->base;
+    d.down = down->base;
+    d.gstride = gate->stride;
+    d.ustride = up->stride;
+    d.dstride = down->stride;
+    d.logits = logits;
+    d.x = x;
+    d.out = out;
+    d.ntok = ntok;
+    d.hidden = hidden;
+    d.inter = inter;
+    d.ne = n_experts;
+    d.topk = top_k;
+    d.ws = scratch;
+    d.ws_bytes = qw6k_moe_ws_bytes(ntok, hidden, inter, n_experts, top_k);
+    if (d.ws_bytes > cap) {
+        qw6h_set_err("qw6cu_moe_decode_noalloc: this shape needs %zu bytes of scratch; the fixed scratch holds %zu "
+                     "(use fewer tokens or qw6cu_moe_decode)",
+                     d.ws_bytes, cap);
+        return QW6CU_ERR_ARG;
+    }
+    int rc = qw6h_rc(qw6k_moe_check(&d), "moe_decode_noalloc");
+    const int n = rc ? 0 : qw6k_moe_nphases(&d);
+    for (int ph = 0; ph < n && !rc; ph++)
+        rc = qw6h_rc(qw6k_moe_phase(&d, ph, (cudaStream_t)stream), "moe_decode_noalloc");
+    return rc;
+}

@@ -102,6 +102,7 @@ def load() -> C.CDLL:
     pk = C.POINTER(ExpertPack)
     lib.qw6cu_moe_decode.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32]
     lib.qw6cu_moe_decode_hostio.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32]
+    lib.qw6cu_moe_decode_noalloc.argtypes = [pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp]
     lib.qw6cu_profile_begin.argtypes = [_vp, _u32]
     lib.qw6cu_profile_end.argtypes = [_vp, C.POINTER(C.c_double), C.POINTER(C.c_uint32)]
     lib.qw6cu_kernel_name.argtypes = [C.c_int]
@@ -182,6 +183,15 @@ def moe_gather_host(expert_out, w, shared, shared_weight, dim, top_k):
                                          None if sh is None else sh.ctypes.data, float(shared_weight), out,
                                          dim, top_k), "moe_gather_host")
     return out
+
+
+def moe_decode_noalloc(gate: ExpertPack, up: ExpertPack, down: ExpertPack, logits, x, out, ntok, hidden, inter,
+                       n_experts, top_k, stream=0) -> None:
+    """qw6cu_moe_decode_noalloc: device pointers, caller's stream (0 = the
+    legacy default stream), no device allocation; scratch is the library's
+    fixed 1 MiB device array."""
+    _check(load().qw6cu_moe_decode_noalloc(C.byref(gate), C.byref(up), C.byref(down), logits, x, out, ntok, hidden,
+                                           inter, n_experts, top_k, stream or None), "qw6cu_moe_decode_noalloc")
 
 
 def selftest() -> int:
