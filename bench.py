@@ -282,9 +282,11 @@ def run_ours(args, rank, local_rank, world):
     e2e_s = float(te.item())
 
     matvec = matvec_sweep(torch, ctx, stream) if (rank == 0 and args.matvec) else None
+    lmh = lm_head_bench(torch, ctx, stream, rank, world, dist) if args.lm_head else None
     result = None
     if rank == 0:
         result = report(args, world, ms_max, prof, clk, e2e_steps, e2e_s, matvec, raw)
+        result["lm_head"] = lmh
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -342,6 +344,63 @@ def matvec_sweep(torch, ctx, stream):
             lat.append(e0.elapsed_time(e1) * 1e3)
     out["c0_q4k_512x2048_latency_us"] = round(float(np.median(lat)), 2)
     return out
+
+
+def lm_head_bench(torch, ctx, stream, rank, world, dist):
+    """Config 4's Q6_K LM head [248320 x 2048] with fused argmax, row-sharded
+    over the ranks (rank r holds rows [r*V/N, (r+1)*V/N)); the shards' 8-byte
+    (logit, index) keys are all-gathered with NCCL and reduced on every rank.
+    Returns per-token latency and tokens/s for batch 1 and batch 32."""
+    from qw6_b200 import synth as S
+    hbm, _ = peaks()
+    V, H = S.VOCAB, HIDDEN
+    r0 = (V * rank // world) // 16 * 16
+    r1 = V if rank == world - 1 else (V * (rank + 1) // world) // 16 * 16
+    rows = r1 - r0
+    pb = ctx.packed_bytes(S.Q6_K, rows, H)
+    w = torch.randint(0, 256, (pb,), dtype=torch.uint8, device="cuda")
+    # finite fp16 scales: zero the high byte of every d (rows x blocks) so no inf/NaN logits
+    res = {}
+    for ntok in (1, 32):
+        x = torch.randn((ntok, H), device="cuda")
+        keys = torch.zeros((ntok,), dtype=torch.int64, device="cuda")
+        allk = torch.zeros((world, ntok), dtype=torch.int64, device="cuda")
+        idx = torch.empty(ntok, dtype=torch.int32, device="cuda")
+        val = torch.empty(ntok, dtype=torch.float32, device="cuda")
+
+        def one():
+            ctx.lm_head_argmax(S.Q6_K, w.data_ptr(), x.data_ptr(), ntok, rows, H, r0, keys.data_ptr())
+            if world > 1:
+                with torch.cuda.stream(stream):
+                    dist.all_gather_into_tensor(allk.view(-1), keys)
+                ctx.argmax_keys_reduce(allk.data_ptr(), world, ntok, idx.data_ptr(), val.data_ptr())
+            else:
+                ctx.argmax_keys_reduce(keys.data_ptr(), 1, ntok, idx.data_ptr(), val.data_ptr())
+
+        for _ in range(3):
+            one()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        n = 20
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            one()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / n], device="cuda", dtype=torch.float64)
+        if dist:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        shard_bytes = rows * (H // 256) * 210 + ntok * H * 4
+        res[f"b{ntok}"] = {"us_per_call": round(ms * 1e3, 2), "tokens_s": round(ntok / (ms / 1e3), 1),
+                           "shard_rows": rows, "shard_gbs": round(shard_bytes / ms / 1e6, 1),
+                           "shard_frac": round(shard_bytes / ms / 1e6 / hbm, 3)}
+    res["shards"] = world
+    res["collective"] = "NCCL all_gather of 8-byte keys" if world > 1 else None
+    del w
+    return res
 
 
 def traffic_from_profiles(kernel: str):
@@ -484,6 +543,7 @@ def main():
                     help="resident layer copies (16 keeps the working set >> L2; fewer for profiling)")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--no-matvec", dest="matvec", action="store_false")
+    ap.add_argument("--no-lm-head", dest="lm_head", action="store_false")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -88,6 +88,23 @@ int qw6cu_moe_gather(qw6cu_ctx *ctx, const float *expert_out, const float *w, co
 /* argmax with qw6_cpu_argmax semantics; idx/val are device pointers. */
 int qw6cu_argmax(qw6cu_ctx *ctx, const float *x, uint32_t n, uint32_t *idx, float *val);
 
+/* ---- LM head + greedy argmax ---- */
+
+/* Fused output projection and argmax (qw6.c:2493 then qw6_cpu_argmax,
+ * qw6.c:2858-2863) over one row shard [row_offset, row_offset + rows) of the
+ * vocabulary: keys[t] (device, 8 bytes per token) receives the packed
+ * (logit, global row index) maximum of token t's logits over the shard --
+ * larger logit first, lower index on ties, NaN handled like the CPU scan.
+ * logits (nullable) also receives the rows x ntok logits (token-major).
+ * x: [ntok x cols] device fp32, ntok <= 32.  Shards of one vocabulary are
+ * combined exactly by taking the max of their keys. */
+int qw6cu_lm_head_argmax(qw6cu_ctx *ctx, uint32_t quant, const void *packed, const float *x, uint32_t ntok,
+                         uint32_t rows, uint32_t cols, uint32_t row_offset, unsigned long long *keys, float *logits);
+/* idx[t] / val[t] (val nullable; device) from the max over nshards of
+ * keys[s*ntok + t] -- e.g. after all-gathering every shard's keys. */
+int qw6cu_argmax_keys_reduce(qw6cu_ctx *ctx, const unsigned long long *keys, uint32_t nshards, uint32_t ntok,
+                             uint32_t *idx, float *val);
+
 /* ---- routed MoE FFN (decode batches) ---- */
 
 /* One GGUF expert pack in the packed tile layout: expert e's matrix starts at
@@ -149,7 +166,7 @@ size_t qw6cu_moe_workspace_bytes(uint32_t ntok, uint32_t hidden, uint32_t inter,
  * begin: allocate events for up to max_launches launches and start
  * recording; end: synchronize, then write per-kernel-id total milliseconds
  * and launch counts into arrays of QW6CU_NKERNELS entries and stop. */
-#define QW6CU_NKERNELS 9
+#define QW6CU_NKERNELS 10
 int qw6cu_profile_begin(qw6cu_ctx *ctx, uint32_t max_launches);
 int qw6cu_profile_end(qw6cu_ctx *ctx, double *ms_total, uint32_t *launches);
 const char *qw6cu_kernel_name(int kernel_id);

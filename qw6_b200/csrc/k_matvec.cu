@@ -6,6 +6,7 @@
 // qw6_vk_pipe_matvec (qw6_vk.c:2386-2430) with the matmul_*.comp shaders.
 #include <cuda_runtime.h>
 
+#include "qw6_argmax.cuh"
 #include "qw6_dev.cuh"
 #include "qw6_grids.cuh"
 #include "qw6_launch.h"
@@ -143,11 +144,13 @@ __global__ void k_pack(const uint8_t* __restrict__ raw, uint8_t* __restrict__ pa
 struct MvArgs {
     const uint8_t* w;
     const float* x;
-    float* y;
+    float* y;  // may be null when KEYS (argmax only)
     int rows, cols, ntok, ldx, ldy, ks, nb, mtiles;
+    unsigned long long* keys;  // KEYS: per-token packed (value, row_offset + row) max
+    uint32_t row_offset;
 };
 
-template <int F, int NQ>
+template <int F, int NQ, bool KEYS>
 __global__ void __launch_bounds__(kThreads) k_matvec(const MvArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     using T = Tile<F, NQ>;
@@ -178,8 +181,12 @@ __global__ void __launch_bounds__(kThreads) k_matvec(const MvArgs a) {
     const XView xv = xs.view();
 
     float acc[2][NQ];
+    unsigned long long best[NQ];
 #pragma unroll
-    for (int qt = 0; qt < NQ; qt++) acc[0][qt] = acc[1][qt] = 0.f;
+    for (int qt = 0; qt < NQ; qt++) {
+        acc[0][qt] = acc[1][qt] = 0.f;
+        best[qt] = 0ull;
+    }
 
     auto epilogue = [&](int step) {
         const int mt = item_mt(step / nbk);
@@ -211,8 +218,20 @@ __global__ void __launch_bounds__(kThreads) k_matvec(const MvArgs a) {
                 const int tok = 4 * qt + t;
                 if (tok < a.ntok) {
                     const int r0 = mt * 16 + g;
-                    if (r0 < a.rows) a.y[(size_t)tok * a.ldy + r0] = acc[0][qt];
-                    if (r0 + 8 < a.rows) a.y[(size_t)tok * a.ldy + r0 + 8] = acc[1][qt];
+                    if (!KEYS || a.y) {
+                        if (r0 < a.rows) a.y[(size_t)tok * a.ldy + r0] = acc[0][qt];
+                        if (r0 + 8 < a.rows) a.y[(size_t)tok * a.ldy + r0 + 8] = acc[1][qt];
+                    }
+                    if (KEYS) {
+                        if (r0 < a.rows) {
+                            const unsigned long long k0 = argmax_key(acc[0][qt], a.row_offset + (uint32_t)r0);
+                            best[qt] = k0 > best[qt] ? k0 : best[qt];
+                        }
+                        if (r0 + 8 < a.rows) {
+                            const unsigned long long k1 = argmax_key(acc[1][qt], a.row_offset + (uint32_t)r0 + 8);
+                            best[qt] = k1 > best[qt] ? k1 : best[qt];
+                        }
+                    }
                 }
             }
         }
@@ -228,6 +247,20 @@ __global__ void __launch_bounds__(kThreads) k_matvec(const MvArgs a) {
             if (step_ok(s + 2)) T::load(fa, tile_ptr(s + 2), lane);
             if (step_ok(s + 1)) tile_dot<F, NQ>(fb, xv, split * nbk + (s + 1) % nbk, acc, lane, tbl);
             if ((s + 1) % nbk == nbk - 1) epilogue(s + 1);
+        }
+    }
+    if (KEYS) {
+        // lanes 4g+t share token t: fold over g (lane bits 2..4), one atomic per warp and token
+#pragma unroll
+        for (int qt = 0; qt < NQ; qt++) {
+            unsigned long long k = best[qt];
+#pragma unroll
+            for (int o = 4; o < 32; o <<= 1) {
+                const unsigned long long v = __shfl_xor_sync(0xffffffffu, k, o);
+                k = v > k ? v : k;
+            }
+            const int tok = 4 * qt + (lane & 3);
+            if (lane < 4 && tok < a.ntok && k) atomicMax(a.keys + tok, k);
         }
     }
 }
@@ -251,22 +284,25 @@ static size_t mv_smem(int cols) {
     return (IsIQ<F>::value ? sizeof(IQTables) : 0) + xstage_bytes(4 * NQ, cols) + (size_t)kThreads * 2 * NQ * 4;
 }
 
-template <int F, int NQ>
+template <int F, int NQ, bool KEYS>
 static int launch_mv(const uint8_t* w, const float* x, float* y, int rows, int cols, int ntok, int ldx,
-                     int ldy, cudaStream_t st) {
+                     int ldy, cudaStream_t st, unsigned long long* keys = nullptr, uint32_t row_offset = 0) {
     const size_t smem = mv_smem<F, NQ>(cols);
+    if (smem > 200 * 1024) return QW6K_ERR_ARG;
     static int configured = 0;
     static int occ = 1;
     if (!configured) {
-        if (cudaFuncSetAttribute(k_matvec<F, NQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
+        if (cudaFuncSetAttribute(k_matvec<F, NQ, KEYS>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
             cudaSuccess)
             return QW6K_ERR_CUDA;
         configured = 1;
     }
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_matvec<F, NQ>, kThreads, smem) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_matvec<F, NQ, KEYS>, kThreads, smem) != cudaSuccess ||
         occ < 1)
         return QW6K_ERR_CUDA;
     MvArgs a;
+    a.keys = keys;
+    a.row_offset = row_offset;
     a.w = w;
     a.x = x;
     a.y = y;
@@ -284,16 +320,25 @@ static int launch_mv(const uint8_t* w, const float* x, float* y, int rows, int c
     const int wpm = kWarps / ks;
     const long long ngrp = (a.mtiles + wpm - 1) / wpm;
     const int grid = (int)(ngrp < (long long)num_sms() * occ ? ngrp : (long long)num_sms() * occ);
-    k_matvec<F, NQ><<<grid, kThreads, smem, st>>>(a);
+    k_matvec<F, NQ, KEYS><<<grid, kThreads, smem, st>>>(a);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
 }
 
 template <int F>
 static int launch_mv_nq(const uint8_t* w, const float* x, float* y, int rows, int cols, int ntok, int ldx,
                         int ldy, cudaStream_t st) {
-    if (ntok <= 4) return launch_mv<F, 1>(w, x, y, rows, cols, ntok, ldx, ldy, st);
-    if (ntok <= 8) return launch_mv<F, 2>(w, x, y, rows, cols, ntok, ldx, ldy, st);
-    if (ntok <= 32) return launch_mv<F, 8>(w, x, y, rows, cols, ntok, ldx, ldy, st);
+    if (ntok <= 4) return launch_mv<F, 1, false>(w, x, y, rows, cols, ntok, ldx, ldy, st);
+    if (ntok <= 8) return launch_mv<F, 2, false>(w, x, y, rows, cols, ntok, ldx, ldy, st);
+    if (ntok <= 32) return launch_mv<F, 8, false>(w, x, y, rows, cols, ntok, ldx, ldy, st);
+    return QW6K_ERR_ARG;
+}
+
+template <int F>
+static int launch_mv_keys(const uint8_t* w, const float* x, float* y, int rows, int cols, int ntok, int ldx,
+                          int ldy, unsigned long long* keys, uint32_t row_offset, cudaStream_t st) {
+    if (ntok <= 4) return launch_mv<F, 1, true>(w, x, y, rows, cols, ntok, ldx, ldy, st, keys, row_offset);
+    if (ntok <= 8) return launch_mv<F, 2, true>(w, x, y, rows, cols, ntok, ldx, ldy, st, keys, row_offset);
+    if (ntok <= 32) return launch_mv<F, 8, true>(w, x, y, rows, cols, ntok, ldx, ldy, st, keys, row_offset);
     return QW6K_ERR_ARG;
 }
 
@@ -363,6 +408,20 @@ extern "C" int qw6k_matvec(uint32_t quant, const void* packed, const float* x, f
     if ((reinterpret_cast<uintptr_t>(packed) & 15u) || (reinterpret_cast<uintptr_t>(x) & 15u) || (ldx & 3u))
         return QW6K_ERR_ALIGN;
 #define CALL(F) launch_mv_nq<F>((const uint8_t*)packed, x, y, (int)rows, (int)cols, (int)ntok, (int)ldx, (int)ldy, st)
+    QW6_DISPATCH_BLOCK(quant, CALL)
+#undef CALL
+}
+
+extern "C" int qw6k_matvec_argmax(uint32_t quant, const void* packed, const float* x, float* y,
+                                  unsigned long long* keys, uint32_t rows, uint32_t cols, uint32_t ntok,
+                                  uint32_t ldx, uint32_t ldy, uint32_t row_offset, cudaStream_t st) {
+    if (!packed || !x || !keys || !rows || !cols || cols % 256 || !ntok || ntok > 32 || ldx < cols ||
+        (y && ldy < rows) || rows > (1u << 30) || cols > 65536 || (uint64_t)row_offset + rows > 0xffffffffull)
+        return QW6K_ERR_ARG;
+    if ((reinterpret_cast<uintptr_t>(packed) & 15u) || (reinterpret_cast<uintptr_t>(x) & 15u) || (ldx & 3u))
+        return QW6K_ERR_ALIGN;
+    if (cudaMemsetAsync(keys, 0, (size_t)ntok * sizeof(unsigned long long), st) != cudaSuccess) return QW6K_ERR_CUDA;
+#define CALL(F) launch_mv_keys<F>((const uint8_t*)packed, x, y, (int)rows, (int)cols, (int)ntok, (int)ldx, (int)ldy, keys, row_offset, st)
     QW6_DISPATCH_BLOCK(quant, CALL)
 #undef CALL
 }

@@ -12,6 +12,7 @@
 #include <cstdint>
 
 #include "qw6_launch.h"
+#include "qw6_argmax.cuh"
 #include "qw6_route.cuh"
 
 namespace qw6 {
@@ -43,30 +44,7 @@ __global__ void k_silu_mul(const float* __restrict__ g, const float* __restrict_
 }
 
 // --------------------------------------------------------------- argmax --
-// Packed key = ordered(value) << 32 | (~index): a larger key is a larger
-// value, then a lower index.  NaN orders as -inf except at index 0, where it
-// takes the maximal key (qw6_cpu_argmax never moves past a NaN x[0]).
-__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t i) {
-    uint32_t u;
-    if (isnan(v)) {
-        if (i == 0) return ~0ull;
-        u = 0x007fffffu;  // ordered(-inf)
-    } else {
-        const uint32_t b = __float_as_uint(v);
-        u = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-    }
-    return ((unsigned long long)u << 32) | (unsigned long long)(~i);
-}
-
-__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long k) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const unsigned long long x = __shfl_xor_sync(0xffffffffu, k, o);
-        k = x > k ? x : k;
-    }
-    return k;
-}
-
+// (keys: qw6_argmax.cuh)
 __global__ void k_argmax_partial(const float* __restrict__ x, uint32_t n, unsigned long long* __restrict__ key) {
     unsigned long long best = 0;
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
@@ -90,6 +68,20 @@ __global__ void k_argmax_final(const float* __restrict__ x, uint32_t n, const un
     if (i >= n) i = 0;  // unreachable: every element contributes a non-zero key
     *out_idx = i;
     if (out_val) *out_val = x[i];
+}
+
+// keys[s*ntok + t] for s < nshards: max over shards, then (index, value).
+__global__ void k_argmax_keys_reduce(const unsigned long long* __restrict__ keys, int nshards, int ntok,
+                                     uint32_t* __restrict__ idx, float* __restrict__ val) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= ntok) return;
+    unsigned long long k = 0;
+    for (int s = 0; s < nshards; s++) {
+        const unsigned long long v = keys[(size_t)s * ntok + t];
+        k = v > k ? v : k;
+    }
+    idx[t] = argmax_key_index(k);
+    if (val) val[t] = argmax_key_value(k);
 }
 
 // ------------------------------------------------------------ f32 matvec --
@@ -155,6 +147,13 @@ extern "C" int qw6k_argmax(const float* x, uint32_t n, unsigned long long* key64
     if (blocks > 592) blocks = 592;
     k_argmax_partial<<<blocks, 256, 0, st>>>(x, n, key64);
     k_argmax_final<<<1, 1, 0, st>>>(x, n, key64, out_idx, out_val);
+    return launched();
+}
+
+extern "C" int qw6k_argmax_keys_reduce(const unsigned long long* keys, uint32_t nshards, uint32_t ntok, uint32_t* idx,
+                                       float* val, cudaStream_t st) {
+    if (!keys || !idx || !nshards || !ntok) return QW6K_ERR_ARG;
+    k_argmax_keys_reduce<<<(ntok + 127) / 128, 128, 0, st>>>(keys, (int)nshards, (int)ntok, idx, val);
     return launched();
 }
 

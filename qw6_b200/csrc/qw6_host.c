@@ -166,8 +166,8 @@ void *qw6h_buf(qw6cu_ctx *ctx, int i, size_t bytes) {
 
 /* --------------------------------------------------------- profiler --- */
 
-static const char *k_names[QW6H_K_COUNT] = {"matvec", "pack", "dequant", "route", "argmax",
-                                             "moe_plan", "moe_gateup", "moe_down", "moe_combine"};
+static const char *k_names[QW6H_K_COUNT] = {"matvec",   "pack",       "dequant",  "route",       "argmax",
+                                             "moe_plan", "moe_gateup", "moe_down", "moe_combine", "lm_head"};
 
 const char *qw6cu_kernel_name(int kid) { return kid >= 0 && kid < QW6H_K_COUNT ? k_names[kid] : "?"; }
 
@@ -310,6 +310,24 @@ int qw6cu_argmax(qw6cu_ctx *ctx, const float *x, uint32_t n, uint32_t *idx, floa
     unsigned long long *key = qw6h_buf(ctx, QW6H_BUF_KEY, 64);
     if (!key) return QW6CU_ERR_NOMEM;
     return qw6h_rc(qw6k_argmax(x, n, key, idx, val, ctx->st), "argmax");
+}
+
+int qw6cu_lm_head_argmax(qw6cu_ctx *ctx, uint32_t quant, const void *packed, const float *x, uint32_t ntok,
+                         uint32_t rows, uint32_t cols, uint32_t row_offset, unsigned long long *keys, float *logits) {
+    int rc = qw6h_use(ctx);
+    if (rc) return rc;
+    const int rec = qw6h_prof_a(ctx, QW6H_K_LM_HEAD);
+    rc = qw6h_rc(qw6k_matvec_argmax(quant, packed, x, logits, keys, rows, cols, ntok, cols, rows, row_offset, ctx->st),
+                 "lm_head_argmax");
+    qw6h_prof_b(ctx, rec);
+    return rc;
+}
+
+int qw6cu_argmax_keys_reduce(qw6cu_ctx *ctx, const unsigned long long *keys, uint32_t nshards, uint32_t ntok,
+                             uint32_t *idx, float *val) {
+    int rc = qw6h_use(ctx);
+    if (rc) return rc;
+    return qw6h_rc(qw6k_argmax_keys_reduce(keys, nshards, ntok, idx, val, ctx->st), "argmax_keys_reduce");
 }
 
 /* ------------------------------------------ per-call host entry points --- */

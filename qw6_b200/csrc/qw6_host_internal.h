@@ -35,6 +35,7 @@ enum {
     QW6H_K_MOE_GATEUP,
     QW6H_K_MOE_DOWN,
     QW6H_K_MOE_COMBINE,
+    QW6H_K_LM_HEAD,
     QW6H_K_COUNT
 };
 

@@ -40,6 +40,16 @@ int qw6k_dequant(uint32_t quant, const void *raw, float *out, uint32_t rows, uin
 int qw6k_matvec(uint32_t quant, const void *packed, const float *x, float *y, uint32_t rows,
                 uint32_t cols, uint32_t ntok, uint32_t ldx, uint32_t ldy, cudaStream_t st);
 
+/* LM head: keys[t] = max over rows r of the packed (logit, row_offset + r)
+ * key of token t (qw6_argmax.cuh); y (nullable) also receives the logits.
+ * keys are zeroed first.  Row shards combine with qw6k_argmax_keys_reduce. */
+int qw6k_matvec_argmax(uint32_t quant, const void *packed, const float *x, float *y, unsigned long long *keys,
+                       uint32_t rows, uint32_t cols, uint32_t ntok, uint32_t ldx, uint32_t ldy, uint32_t row_offset,
+                       cudaStream_t st);
+/* idx[t], val[t] (val nullable) from the max over nshards of keys[s*ntok + t]. */
+int qw6k_argmax_keys_reduce(const unsigned long long *keys, uint32_t nshards, uint32_t ntok, uint32_t *idx,
+                            float *val, cudaStream_t st);
+
 /* fp32 weights (row-major rows x cols). */
 int qw6k_matvec_f32(const float *w, const float *x, float *y, uint32_t rows, uint32_t cols,
                     cudaStream_t st);

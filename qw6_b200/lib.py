@@ -103,6 +103,8 @@ def load() -> C.CDLL:
     lib.qw6cu_moe_decode.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32]
     lib.qw6cu_moe_decode_hostio.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32]
     lib.qw6cu_moe_decode_noalloc.argtypes = [pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp]
+    lib.qw6cu_lm_head_argmax.argtypes = [_vp, _u32, _vp, _vp, _u32, _u32, _u32, _u32, _vp, _vp]
+    lib.qw6cu_argmax_keys_reduce.argtypes = [_vp, _vp, _u32, _u32, _vp, _vp]
     lib.qw6cu_profile_begin.argtypes = [_vp, _u32]
     lib.qw6cu_profile_end.argtypes = [_vp, C.POINTER(C.c_double), C.POINTER(C.c_uint32)]
     lib.qw6cu_kernel_name.argtypes = [C.c_int]
@@ -262,12 +264,19 @@ class Context:
         _check(self.lib.qw6cu_moe_decode_hostio(self.h, C.byref(gate), C.byref(up), C.byref(down), logits, x, out,
                                                 ntok, hidden, inter, n_experts, top_k), "qw6cu_moe_decode_hostio")
 
+    def lm_head_argmax(self, quant, packed, x, ntok, rows, cols, row_offset, keys, logits=None):
+        _check(self.lib.qw6cu_lm_head_argmax(self.h, quant, packed, x, ntok, rows, cols, row_offset, keys, logits),
+               "qw6cu_lm_head_argmax")
+
+    def argmax_keys_reduce(self, keys, nshards, ntok, idx, val=None):
+        _check(self.lib.qw6cu_argmax_keys_reduce(self.h, keys, nshards, ntok, idx, val), "qw6cu_argmax_keys_reduce")
+
     def profile_begin(self, max_launches: int) -> None:
         _check(self.lib.qw6cu_profile_begin(self.h, max_launches), "qw6cu_profile_begin")
 
     def profile_end(self) -> dict:
         """{kernel name: (total ms, launches)} for the kernels that ran."""
-        n = 9
+        n = 10
         ms = (C.c_double * n)()
         cnt = (C.c_uint32 * n)()
         _check(self.lib.qw6cu_profile_end(self.h, ms, cnt), "qw6cu_profile_end")
