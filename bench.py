@@ -359,7 +359,6 @@ def lm_head_bench(torch, ctx, stream, rank, world, dist):
     rows = r1 - r0
     pb = ctx.packed_bytes(S.Q6_K, rows, H)
     w = torch.randint(0, 256, (pb,), dtype=torch.uint8, device="cuda")
-    # finite fp16 scales: zero the high byte of every d (rows x blocks) so no inf/NaN logits
     res = {}
     for ntok in (1, 32):
         x = torch.randn((ntok, H), device="cuda")

@@ -88,6 +88,18 @@ int qw6cu_moe_gather(qw6cu_ctx *ctx, const float *expert_out, const float *w, co
 /* argmax with qw6_cpu_argmax semantics; idx/val are device pointers. */
 int qw6cu_argmax(qw6cu_ctx *ctx, const float *x, uint32_t n, uint32_t *idx, float *val);
 
+/* ---- dense GEMM on the tensor cores ---- */
+
+/* D[M x N] (fp32, row-major) = A[M x K] . B[N x K]^T with bf16 K-major A and
+ * B (row-major with K contiguous), on tcgen05 tensor cores with TMEM
+ * accumulators.  K % 64 == 0; A, B 16-byte aligned. */
+int qw6cu_gemm_bf16_nt(qw6cu_ctx *ctx, const void *A, const void *B, float *D, uint32_t M, uint32_t N, uint32_t K);
+
+/* Synchronize and report whether any kernel of this context gave up a
+ * bounded device-side wait since the last check (QW6CU_ERR_TIMEOUT; the
+ * affected outputs are invalid).  Waits give up after 2 s instead of hanging. */
+int qw6cu_check_device_errors(qw6cu_ctx *ctx);
+
 /* ---- LM head + greedy argmax ---- */
 
 /* Fused output projection and argmax (qw6.c:2493 then qw6_cpu_argmax,

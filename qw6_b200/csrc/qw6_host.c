@@ -161,6 +161,8 @@ void *qw6h_buf(qw6cu_ctx *ctx, int i, size_t bytes) {
         return NULL;
     }
     b->n = want;
+    /* new buffers start zeroed (the device error word relies on it) */
+    cudaMemsetAsync(b->p, 0, want, ctx->st);
     return b->p;
 }
 
@@ -328,6 +330,38 @@ int qw6cu_argmax_keys_reduce(qw6cu_ctx *ctx, const unsigned long long *keys, uin
     int rc = qw6h_use(ctx);
     if (rc) return rc;
     return qw6h_rc(qw6k_argmax_keys_reduce(keys, nshards, ntok, idx, val, ctx->st), "argmax_keys_reduce");
+}
+
+/* Device error word of the context (bounded waits record timeouts here). */
+static int *dev_err(qw6cu_ctx *ctx) {
+    uint8_t *k = qw6h_buf(ctx, QW6H_BUF_KEY, 64);
+    return k ? (int *)(k + 32) : NULL;
+}
+
+int qw6cu_gemm_bf16_nt(qw6cu_ctx *ctx, const void *A, const void *B, float *D, uint32_t M, uint32_t N, uint32_t K) {
+    int rc = qw6h_use(ctx);
+    if (rc) return rc;
+    int *err = dev_err(ctx);
+    if (!err) return QW6CU_ERR_NOMEM;
+    return qw6h_rc(qw6k_gemm_bf16_nt(A, B, D, M, N, K, err, ctx->st), "gemm_bf16_nt");
+}
+
+int qw6cu_check_device_errors(qw6cu_ctx *ctx) {
+    int rc = qw6h_use(ctx);
+    if (rc) return rc;
+    int *err = dev_err(ctx);
+    if (!err) return QW6CU_ERR_NOMEM;
+    int h = 0;
+    cudaError_t e = cudaMemcpyAsync(&h, err, sizeof h, cudaMemcpyDeviceToHost, ctx->st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->st);
+    if (e != cudaSuccess) return cuda_fail("qw6cu_check_device_errors", e);
+    if (h) {
+        cudaMemsetAsync(err, 0, sizeof h, ctx->st);
+        cudaStreamSynchronize(ctx->st);
+        qw6h_set_err("a device-side bounded wait timed out (code %d); the kernel returned without its result", h);
+        return QW6CU_ERR_TIMEOUT;
+    }
+    return 0;
 }
 
 /* ------------------------------------------ per-call host entry points --- */

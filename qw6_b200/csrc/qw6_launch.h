@@ -50,6 +50,11 @@ int qw6k_matvec_argmax(uint32_t quant, const void *packed, const float *x, float
 int qw6k_argmax_keys_reduce(const unsigned long long *keys, uint32_t nshards, uint32_t ntok, uint32_t *idx,
                             float *val, cudaStream_t st);
 
+/* D[M x N] fp32 = A[M x K] . B[N x K]^T, bf16 K-major operands, on tcgen05
+ * (K % 64 == 0).  *err (device int) is set non-zero if a bounded wait timed out. */
+int qw6k_gemm_bf16_nt(const void *A, const void *B, float *D, uint32_t M, uint32_t N, uint32_t K, int *err,
+                      cudaStream_t st);
+
 /* fp32 weights (row-major rows x cols). */
 int qw6k_matvec_f32(const float *w, const float *x, float *y, uint32_t rows, uint32_t cols,
                     cudaStream_t st);

@@ -103,6 +103,8 @@ def load() -> C.CDLL:
     lib.qw6cu_moe_decode.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32]
     lib.qw6cu_moe_decode_hostio.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32]
     lib.qw6cu_moe_decode_noalloc.argtypes = [pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp]
+    lib.qw6cu_gemm_bf16_nt.argtypes = [_vp, _vp, _vp, _vp, _u32, _u32, _u32]
+    lib.qw6cu_check_device_errors.argtypes = [_vp]
     lib.qw6cu_lm_head_argmax.argtypes = [_vp, _u32, _vp, _vp, _u32, _u32, _u32, _u32, _vp, _vp]
     lib.qw6cu_argmax_keys_reduce.argtypes = [_vp, _vp, _u32, _u32, _vp, _vp]
     lib.qw6cu_profile_begin.argtypes = [_vp, _u32]
@@ -263,6 +265,12 @@ class Context:
         """Host pointers (ints) for logits/x/out; synchronous."""
         _check(self.lib.qw6cu_moe_decode_hostio(self.h, C.byref(gate), C.byref(up), C.byref(down), logits, x, out,
                                                 ntok, hidden, inter, n_experts, top_k), "qw6cu_moe_decode_hostio")
+
+    def gemm_bf16_nt(self, A, B, D, M, N, K):
+        _check(self.lib.qw6cu_gemm_bf16_nt(self.h, A, B, D, M, N, K), "qw6cu_gemm_bf16_nt")
+
+    def check_device_errors(self):
+        _check(self.lib.qw6cu_check_device_errors(self.h), "qw6cu_check_device_errors")
 
     def lm_head_argmax(self, quant, packed, x, ntok, rows, cols, row_offset, keys, logits=None):
         _check(self.lib.qw6cu_lm_head_argmax(self.h, quant, packed, x, ntok, rows, cols, row_offset, keys, logits),
