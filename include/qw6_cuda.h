@@ -172,13 +172,30 @@ int qw6cu_moe_decode_noalloc(const qw6cu_expert_pack *gate, const qw6cu_expert_p
 size_t qw6cu_moe_workspace_bytes(uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t n_experts,
                                  uint32_t top_k);
 
+/* ---- routed MoE FFN (prefill batches, tensor cores) ---- */
+
+/* The same layer as qw6cu_moe_decode for large token batches, as grouped
+ * GEMMs on the tcgen05 tensor cores: tokens are grouped by selected expert,
+ * each expert's packed Q4_K/Q6_K rows are dequantized to bf16 tiles in shared
+ * memory and multiplied against the expert's bf16 token rows (fp32
+ * accumulation in TMEM); silu(g)*u is kept in bf16; the down projection
+ * scatter-adds w_e * D into out with fp32 atomics (summation order of the 8
+ * slots not fixed).  x_bf16: [ntok x hidden] bf16 (device); out: fp32
+ * [ntok x hidden], overwritten.  Tolerance vs the fp32 CPU composition:
+ * 2e-2.  gate/up/down quant: Q4_K or Q6_K; hidden, inter multiples of 256. */
+int qw6cu_moe_prefill(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
+                      const qw6cu_expert_pack *down, const float *logits, const void *x_bf16, float *out,
+                      uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t n_experts, uint32_t top_k);
+size_t qw6cu_moe_prefill_workspace_bytes(uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t n_experts,
+                                         uint32_t top_k);
+
 /* ---- profiling ----
  * Per-launch CUDA events around every kernel this context enqueues (the
  * counterpart of qw6's QW6_PROFILE timestamp queries, qw6_vk.c:2315-2357).
  * begin: allocate events for up to max_launches launches and start
  * recording; end: synchronize, then write per-kernel-id total milliseconds
  * and launch counts into arrays of QW6CU_NKERNELS entries and stop. */
-#define QW6CU_NKERNELS 10
+#define QW6CU_NKERNELS 13
 int qw6cu_profile_begin(qw6cu_ctx *ctx, uint32_t max_launches);
 int qw6cu_profile_end(qw6cu_ctx *ctx, double *ms_total, uint32_t *launches);
 const char *qw6cu_kernel_name(int kernel_id);

@@ -169,7 +169,8 @@ void *qw6h_buf(qw6cu_ctx *ctx, int i, size_t bytes) {
 /* --------------------------------------------------------- profiler --- */
 
 static const char *k_names[QW6H_K_COUNT] = {"matvec",   "pack",       "dequant",  "route",       "argmax",
-                                             "moe_plan", "moe_gateup", "moe_down", "moe_combine", "lm_head"};
+                                             "moe_plan", "moe_gateup", "moe_down", "moe_combine", "lm_head",
+                                             "pf_plan",  "pf_gemm1",   "pf_gemm2"};
 
 const char *qw6cu_kernel_name(int kid) { return kid >= 0 && kid < QW6H_K_COUNT ? k_names[kid] : "?"; }
 
@@ -333,7 +334,7 @@ int qw6cu_argmax_keys_reduce(qw6cu_ctx *ctx, const unsigned long long *keys, uin
 }
 
 /* Device error word of the context (bounded waits record timeouts here). */
-static int *dev_err(qw6cu_ctx *ctx) {
+int *qw6h_dev_err(qw6cu_ctx *ctx) {
     uint8_t *k = qw6h_buf(ctx, QW6H_BUF_KEY, 64);
     return k ? (int *)(k + 32) : NULL;
 }
@@ -341,7 +342,7 @@ static int *dev_err(qw6cu_ctx *ctx) {
 int qw6cu_gemm_bf16_nt(qw6cu_ctx *ctx, const void *A, const void *B, float *D, uint32_t M, uint32_t N, uint32_t K) {
     int rc = qw6h_use(ctx);
     if (rc) return rc;
-    int *err = dev_err(ctx);
+    int *err = qw6h_dev_err(ctx);
     if (!err) return QW6CU_ERR_NOMEM;
     return qw6h_rc(qw6k_gemm_bf16_nt(A, B, D, M, N, K, err, ctx->st), "gemm_bf16_nt");
 }
@@ -349,7 +350,7 @@ int qw6cu_gemm_bf16_nt(qw6cu_ctx *ctx, const void *A, const void *B, float *D, u
 int qw6cu_check_device_errors(qw6cu_ctx *ctx) {
     int rc = qw6h_use(ctx);
     if (rc) return rc;
-    int *err = dev_err(ctx);
+    int *err = qw6h_dev_err(ctx);
     if (!err) return QW6CU_ERR_NOMEM;
     int h = 0;
     cudaError_t e = cudaMemcpyAsync(&h, err, sizeof h, cudaMemcpyDeviceToHost, ctx->st);

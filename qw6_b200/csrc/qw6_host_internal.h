@@ -36,6 +36,9 @@ enum {
     QW6H_K_MOE_DOWN,
     QW6H_K_MOE_COMBINE,
     QW6H_K_LM_HEAD,
+    QW6H_K_PF_PLAN,
+    QW6H_K_PF_GEMM1,
+    QW6H_K_PF_GEMM2,
     QW6H_K_COUNT
 };
 
@@ -64,6 +67,7 @@ qw6cu_ctx *qw6h_default_locked(void);
 /* Profiler hooks around one launch: rec = qw6h_prof_a(ctx, kid); launch;
  * qw6h_prof_b(ctx, rec).  No-ops unless profiling is on. */
 int qw6h_prof_a(qw6cu_ctx *ctx, int kid);
+int *qw6h_dev_err(qw6cu_ctx *ctx);
 void qw6h_prof_b(qw6cu_ctx *ctx, int rec);
 
 #endif /* QW6_HOST_INTERNAL_H */

@@ -97,6 +97,15 @@ int qw6k_moe_nphases(const qw6k_moe_desc *d);
 int qw6k_moe_phase_kind(const qw6k_moe_desc *d, int phase); /* 0 plan, 1 gate/up, 2 down, 3 combine */
 int qw6k_moe_phase(const qw6k_moe_desc *d, int phase, cudaStream_t st);
 
+/* Routed MoE FFN for prefill batches on tcgen05 (k_prefill.cu): desc->x is
+ * bf16 [ntok x hidden]; gate/up/down Q4_K or Q6_K packed; hidden, inter
+ * multiples of 256.  Phases 0..5 in order on one stream (route, count,
+ * offsets, scatter, gate/up GEMM, down GEMM + weighted scatter-add into out,
+ * which phase 5 zeroes first).  *err records bounded-wait timeouts. */
+size_t qw6k_moe_prefill_ws_bytes(uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t ne, uint32_t topk);
+int qw6k_moe_prefill_check(const qw6k_moe_desc *d, int *err);
+int qw6k_moe_prefill_phase(const qw6k_moe_desc *d, int *err, int phase, cudaStream_t st);
+
 /* Fixed 1 MiB device scratch (k_static.cu) of the allocation-free MoE entry
  * point; *ptr is its device address on the current device (looked up with
  * cudaGetSymbolAddress on the first call per device). */

@@ -150,3 +150,50 @@ int qw6cu_moe_decode_noalloc(const qw6cu_expert_pack *gate, const qw6cu_expert_p
         rc = qw6h_rc(qw6k_moe_phase(&d, ph, (cudaStream_t)stream), "moe_decode_noalloc");
     return rc;
 }
+
+size_t qw6cu_moe_prefill_workspace_bytes(uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t n_experts,
+                                         uint32_t top_k) {
+    return qw6k_moe_prefill_ws_bytes(ntok, hidden, inter, n_experts, top_k);
+}
+
+int qw6cu_moe_prefill(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
+                      const qw6cu_expert_pack *down, const float *logits, const void *x_bf16, float *out,
+                      uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t n_experts, uint32_t top_k) {
+    int rc = qw6h_use(ctx);
+    if (rc) return rc;
+    if (!gate || !up || !down || gate->quant != up->quant) {
+        qw6h_set_err("qw6cu_moe_prefill: gate and up packs must be given and share one quant type");
+        return QW6CU_ERR_ARG;
+    }
+    int *err = qw6h_dev_err(ctx);
+    if (!err) return QW6CU_ERR_NOMEM;
+    qw6k_moe_desc d;
+    d.gq = gate->quant;
+    d.dq = down->quant;
+    d.gate = gate->base;
+    d.up = up->base;
+    d.down = down->base;
+    d.gstride = gate->stride;
+    d.ustride = up->stride;
+    d.dstride = down->stride;
+    d.logits = logits;
+    d.x = (const float *)x_bf16;
+    d.out = out;
+    d.ntok = ntok;
+    d.hidden = hidden;
+    d.inter = inter;
+    d.ne = n_experts;
+    d.topk = top_k;
+    d.ws_bytes = qw6k_moe_prefill_ws_bytes(ntok, hidden, inter, n_experts, top_k);
+    d.ws = qw6h_buf(ctx, QW6H_BUF_WS, d.ws_bytes);
+    if (!d.ws) return QW6CU_ERR_NOMEM;
+    rc = qw6h_rc(qw6k_moe_prefill_check(&d, err), "moe_prefill");
+    static const int kid[6] = {QW6H_K_PF_PLAN, QW6H_K_PF_PLAN, QW6H_K_PF_PLAN,
+                               QW6H_K_PF_PLAN, QW6H_K_PF_GEMM1, QW6H_K_PF_GEMM2};
+    for (int ph = 0; ph < 6 && !rc; ph++) {
+        const int rec = qw6h_prof_a(ctx, kid[ph]);
+        rc = qw6h_rc(qw6k_moe_prefill_phase(&d, err, ph, ctx->st), "moe_prefill");
+        qw6h_prof_b(ctx, rec);
+    }
+    return rc;
+}

@@ -103,6 +103,9 @@ def load() -> C.CDLL:
     lib.qw6cu_moe_decode.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32]
     lib.qw6cu_moe_decode_hostio.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32]
     lib.qw6cu_moe_decode_noalloc.argtypes = [pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp]
+    lib.qw6cu_moe_prefill.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32]
+    lib.qw6cu_moe_prefill_workspace_bytes.argtypes = [_u32, _u32, _u32, _u32, _u32]
+    lib.qw6cu_moe_prefill_workspace_bytes.restype = _sz
     lib.qw6cu_gemm_bf16_nt.argtypes = [_vp, _vp, _vp, _vp, _u32, _u32, _u32]
     lib.qw6cu_check_device_errors.argtypes = [_vp]
     lib.qw6cu_lm_head_argmax.argtypes = [_vp, _u32, _vp, _vp, _u32, _u32, _u32, _u32, _vp, _vp]
@@ -266,6 +269,11 @@ class Context:
         _check(self.lib.qw6cu_moe_decode_hostio(self.h, C.byref(gate), C.byref(up), C.byref(down), logits, x, out,
                                                 ntok, hidden, inter, n_experts, top_k), "qw6cu_moe_decode_hostio")
 
+    def moe_prefill(self, gate: ExpertPack, up: ExpertPack, down: ExpertPack, logits, x_bf16, out, ntok, hidden,
+                    inter, n_experts, top_k):
+        _check(self.lib.qw6cu_moe_prefill(self.h, C.byref(gate), C.byref(up), C.byref(down), logits, x_bf16, out,
+                                          ntok, hidden, inter, n_experts, top_k), "qw6cu_moe_prefill")
+
     def gemm_bf16_nt(self, A, B, D, M, N, K):
         _check(self.lib.qw6cu_gemm_bf16_nt(self.h, A, B, D, M, N, K), "qw6cu_gemm_bf16_nt")
 
@@ -284,7 +292,7 @@ class Context:
 
     def profile_end(self) -> dict:
         """{kernel name: (total ms, launches)} for the kernels that ran."""
-        n = 10
+        n = 13
         ms = (C.c_double * n)()
         cnt = (C.c_uint32 * n)()
         _check(self.lib.qw6cu_profile_end(self.h, ms, cnt), "qw6cu_profile_end")
