@@ -283,10 +283,12 @@ def run_ours(args, rank, local_rank, world):
 
     matvec = matvec_sweep(torch, ctx, stream) if (rank == 0 and args.matvec) else None
     lmh = lm_head_bench(torch, ctx, stream, rank, world, dist) if args.lm_head else None
+    pf = prefill_bench(torch, ctx, stream, L, args.prefill_steps) if (rank == 0 and args.prefill) else None
     result = None
     if rank == 0:
         result = report(args, world, ms_max, prof, clk, e2e_steps, e2e_s, matvec, raw)
         result["lm_head"] = lmh
+        result["prefill"] = pf
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -344,6 +346,57 @@ def matvec_sweep(torch, ctx, stream):
             lat.append(e0.elapsed_time(e1) * 1e3)
     out["c0_q4k_512x2048_latency_us"] = round(float(np.median(lat)), 2)
     return out
+
+
+PREFILL_FLOPS = 2 * 4096 * TOPK * (2 * INTER * HIDDEN + HIDDEN * INTER) * 2 // 2  # 2 FLOP per MAC
+
+
+def prefill_bench(torch, ctx, stream, L, steps):
+    """Config 3 on one GPU: 4096 bf16 tokens through the 256-expert layer
+    (Q4_K gate/up, Q6_K down) with the tcgen05 grouped GEMMs; tokens/s and
+    dense bf16 TFLOP/s (206.2 GFLOP per step) against the measured peak."""
+    from qw6_b200 import synth as S
+    gate, up, down, logits, xbits = S.config3()
+    packs, held = [], []
+    for q, m, r, c in ((S.Q4_K, gate, INTER, HIDDEN), (S.Q4_K, up, INTER, HIDDEN), (S.Q6_K, down, HIDDEN, INTER)):
+        pb = ctx.packed_bytes(q, r, c)
+        raw = torch.from_numpy(m.reshape(-1)).cuda()
+        pk = torch.empty(pb * NE, dtype=torch.uint8, device="cuda")
+        torch.cuda.synchronize()
+        ctx.pack(q, raw.data_ptr(), pk.data_ptr(), r, c, NE, m[0].nbytes, pb)
+        ctx.synchronize()
+        held.append(pk)
+        packs.append(L.ExpertPack(q, pk.data_ptr(), pb))
+    lg = torch.from_numpy(logits).cuda()
+    x = torch.from_numpy(xbits.view(np.int16)).cuda()
+    out = torch.empty((4096, HIDDEN), device="cuda")
+    torch.cuda.synchronize()
+
+    def one():
+        ctx.moe_prefill(packs[0], packs[1], packs[2], lg.data_ptr(), x.data_ptr(), out.data_ptr(), 4096, HIDDEN,
+                        INTER, NE, TOPK)
+
+    for _ in range(3):
+        one()
+    ctx.check_device_errors()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        one()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    ctx.profile_begin(8 * 6)
+    one()
+    prof = ctx.profile_end()
+    ctx.check_device_errors()
+    pk_bf16 = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"] if (
+        ROOT / "MEASURED_PEAKS.json").exists() else 1590.0
+    tflops = PREFILL_FLOPS / (ms / 1e3) / 1e12
+    return {"workload": "config 3: 4096 tokens, 256 experts, top-8, bias N(0,0.5), 1 GPU",
+            "steps": steps, "ms_per_step": round(ms, 4), "tokens_s": round(4096 / (ms / 1e3), 1),
+            "tflops": round(tflops, 1), "frac_bf16_peak": round(tflops / pk_bf16, 3),
+            "kernels": {k: {"avg_us": round(v[0] / v[1] * 1e3, 2), "launches": v[1]} for k, v in prof.items()}}
 
 
 def lm_head_bench(torch, ctx, stream, rank, world, dist):
@@ -543,6 +596,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--no-matvec", dest="matvec", action="store_false")
     ap.add_argument("--no-lm-head", dest="lm_head", action="store_false")
+    ap.add_argument("--no-prefill", dest="prefill", action="store_false")
+    ap.add_argument("--prefill-steps", type=int, default=20)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -189,6 +189,40 @@ int qw6cu_moe_prefill(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu
 size_t qw6cu_moe_prefill_workspace_bytes(uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t n_experts,
                                          uint32_t top_k);
 
+/* Expert-parallel building block: the same grouped GEMMs with the routing
+ * supplied per row instead of computed from logits.  Row r of x_bf16
+ * ([nrows x hidden], device) is sent through expert row_expert[r] (an index
+ * into these packs, < n_experts) and out[r] (fp32 [nrows x hidden],
+ * overwritten) = row_weight[r] * down(silu(gate x_r) * up x_r).  Used on the
+ * rank that owns the experts after an all-to-all dispatch of token rows. */
+int qw6cu_moe_prefill_rows(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
+                           const qw6cu_expert_pack *down, const void *x_bf16, const int32_t *row_expert,
+                           const float *row_weight, float *out, uint32_t nrows, uint32_t hidden, uint32_t inter,
+                           uint32_t n_experts);
+
+/* ---- expert parallelism (prefill) ----
+ * Experts are sharded contiguously over `world` ranks: rank r owns experts
+ * [r*experts_per_rank, (r+1)*experts_per_rank).  One layer on a rank:
+ *   qw6cu_moe_route -> qw6cu_ep_count -> all-to-all of dst_count ->
+ *   qw6cu_ep_pack -> all-to-all of send_x / send_expert / send_weight ->
+ *   qw6cu_moe_prefill_rows on the received rows (local packs) ->
+ *   all-to-all of the weighted outputs back in send-row order ->
+ *   qw6cu_ep_combine.  (qw6_b200/ep.py runs this with NCCL.) */
+
+/* dst_count[world] (zeroed here) = assignments bound for each rank;
+ * pos[a] = position of assignment a among those of its destination. */
+int qw6cu_ep_count(qw6cu_ctx *ctx, const int32_t *idx, uint32_t nassign, uint32_t world, uint32_t experts_per_rank,
+                   int32_t *dst_count, int32_t *pos);
+/* Send row p = (exclusive prefix of dst_count)[dst] + pos[a]: token row
+ * (bf16, hidden) of assignment a = t*top_k + k, its expert index local to the
+ * destination, its routing weight; send_pos[a] = p. */
+int qw6cu_ep_pack(qw6cu_ctx *ctx, const int32_t *idx, const float *w, const int32_t *pos, const int32_t *dst_count,
+                  uint32_t nassign, uint32_t top_k, uint32_t world, uint32_t experts_per_rank, const void *x_bf16,
+                  uint32_t hidden, void *send_x, int32_t *send_expert, float *send_weight, int32_t *send_pos);
+/* out[t] (fp32, overwritten) = sum_k ret[send_pos[t*top_k + k]] in slot order. */
+int qw6cu_ep_combine(qw6cu_ctx *ctx, const float *ret, const int32_t *send_pos, uint32_t ntok, uint32_t top_k,
+                     uint32_t hidden, float *out);
+
 /* ---- profiling ----
  * Per-launch CUDA events around every kernel this context enqueues (the
  * counterpart of qw6's QW6_PROFILE timestamp queries, qw6_vk.c:2315-2357).

@@ -45,7 +45,8 @@ struct PfArgs {
     int4* items;
     int* nitems;
     int32_t* order;
-    __nv_bfloat16* h;
+    __nv_bfloat16* h;     // [TK][inter]  silu(gate)*up per assignment
+    __nv_bfloat16* dout;  // [TK][hidden] expert output per assignment
     int* err;
 };
 
@@ -102,9 +103,11 @@ __global__ void k_pf_scatter(const PfArgs a) {
 }
 
 // ------------------------------------------------------ A-tile producers --
-// Write rows (16*mi + g, 16*mi + g + 8) of a 128 x 64 bf16 A tile (K slab ks)
-// from the packed tile-block `tb`; this lane covers K [8t, 8t+8) of both
-// 32-halves of the slab, i.e. swizzle chunks t and 4 + t.
+// A lane fills rows (16*mi + g, 16*mi + g + 8) of a 128 x 64 bf16 A tile
+// (one K slab) from the packed tile-block; it covers K [8t, 8t+8) of both
+// 32-halves of the slab, i.e. swizzle chunks t and 4 + t.  Loading (into
+// registers) and dequantizing/storing are split so that the loads of slab
+// k+1 are in flight while slab k is dequantized.
 
 __device__ __forceinline__ uint4 pack8_bf16(const float (&v)[8]) {
     uint4 r;
@@ -117,267 +120,271 @@ __device__ __forceinline__ uint4 pack8_bf16(const float (&v)[8]) {
     return r;
 }
 
-// Q4_K: slab c = ks % 4 of block ks / 4 holds sub-blocks 2c (low nibbles of
-// qs[32c..32c+32)) and 2c+1 (high nibbles).
-__device__ __forceinline__ void produce_q4k(uint8_t* sa, const uint8_t* tb, int c, int mi, int lane) {
-    const int g = lane >> 2, t = lane & 3;
-#pragma unroll
-    for (int rh = 0; rh < 2; rh++) {
-        const uint2 q = ldg64(tb + 256 + ((rh * 2 + (c >> 1)) * 32 + lane) * 16 + (c & 1) * 8);
-        const uint4 h = ldg128(tb + (g + 8 * rh) * 16);
-        const float d = f16f(h.x), dmin = f16f(h.x >> 16);
-        const uint32_t S0 = h.y, S1 = h.z, S2 = h.w;
-        const uint32_t SC0 = S0 & 0x3f3f3f3fu, MN0 = S1 & 0x3f3f3f3fu;
-        const uint32_t SC1 = (S2 & 0x0f0f0f0fu) | ((S0 >> 2) & 0x30303030u);
-        const uint32_t MN1 = ((S2 >> 4) & 0x0f0f0f0fu) | ((S1 >> 2) & 0x30303030u);
-        const int j0 = 2 * c, j1 = 2 * c + 1;
-        const float dl = d * (float)byte_of(j0 < 4 ? SC0 : SC1, j0 & 3);
-        const float ml = dmin * (float)byte_of(j0 < 4 ? MN0 : MN1, j0 & 3);
-        const float dh = d * (float)byte_of(j1 < 4 ? SC0 : SC1, j1 & 3);
-        const float mh = dmin * (float)byte_of(j1 < 4 ? MN0 : MN1, j1 & 3);
-        float lo[8], hi[8];
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const uint32_t b = byte_of(i < 4 ? q.x : q.y, i & 3);
-            lo[i] = fmaf(dl, (float)(b & 15u), -ml);
-            hi[i] = fmaf(dh, (float)(b >> 4), -mh);
-        }
-        const uint32_t row = mi * 16 + g + 8 * rh;
-        *reinterpret_cast<uint4*>(sa + sw128_off(row, t)) = pack8_bf16(lo);
-        *reinterpret_cast<uint4*>(sa + sw128_off(row, 4 + t)) = pack8_bf16(hi);
-    }
-}
-
-// Q6_K: slab c = ks % 4 covers half n = c/2, runs kk = 2(c%2) and 2(c%2)+1;
-// scale sc[8n + 2kk] (qw6's even-scale reading, qw6.c:1568-1571).
-__device__ __forceinline__ void produce_q6k(uint8_t* sa, const uint8_t* tb, int c, int mi, int lane) {
-    const int g = lane >> 2, t = lane & 3, n = c >> 1, k0 = 2 * (c & 1);
-#pragma unroll
-    for (int rh = 0; rh < 2; rh++) {
-        const uint4 L = ldg128(tb + 288 + ((rh * 3 + n) * 32 + lane) * 16);
-        const uint2 H = ldg64(tb + 288 + ((rh * 3 + 2) * 32 + lane) * 16 + n * 8);
-        const uint4 sc = ldg128(tb + (g + 8 * rh) * 16);
-        const float d = f16f(ldg16(tb + 256 + (g + 8 * rh) * 2));
-        const float d0 = d * (float)(int8_t)byte16(sc, 8 * n + 2 * k0);
-        const float d1 = d * (float)(int8_t)byte16(sc, 8 * n + 2 * (k0 + 1));
-        float v0[8], v1[8];
-#pragma unroll
-        for (int hw = 0; hw < 2; hw++) {
-            const uint32_t A = hw ? L.y : L.x, B = hw ? L.w : L.z, Hh = hw ? H.y : H.x;
-            uint32_t q0, q1;
-            if (k0 == 0) {
-                q0 = (A & 0x0f0f0f0fu) | ((Hh << 4) & 0x30303030u);
-                q1 = (B & 0x0f0f0f0fu) | ((Hh << 2) & 0x30303030u);
-            } else {
-                q0 = ((A >> 4) & 0x0f0f0f0fu) | (Hh & 0x30303030u);
-                q1 = ((B >> 4) & 0x0f0f0f0fu) | ((Hh >> 2) & 0x30303030u);
-            }
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                v0[4 * hw + i] = d0 * (float)((int)byte_of(q0, i) - 32);
-                v1[4 * hw + i] = d1 * (float)((int)byte_of(q1, i) - 32);
-            }
-        }
-        const uint32_t row = mi * 16 + g + 8 * rh;
-        *reinterpret_cast<uint4*>(sa + sw128_off(row, t)) = pack8_bf16(v0);
-        *reinterpret_cast<uint4*>(sa + sw128_off(row, 4 + t)) = pack8_bf16(v1);
-    }
-}
-
 template <int F>
-__device__ __forceinline__ void produce_a(uint8_t* sa, const uint8_t* tb, int c, int mi, int lane) {
-    if constexpr (F == QW6F_Q6_K)
-        produce_q6k(sa, tb, c, mi, lane);
-    else
-        produce_q4k(sa, tb, c, mi, lane);
+struct ASlab;
+
+// Q4_K: slab c of a super-block holds sub-blocks 2c (low nibbles of
+// qs[32c..32c+32)) and 2c+1 (high nibbles).
+template <>
+struct ASlab<QW6F_Q4_K_M> {
+    uint2 q[2];
+    uint4 h[2];
+    __device__ __forceinline__ void load(const uint8_t* tb, int c, int lane) {
+        const int g = lane >> 2;
+#pragma unroll
+        for (int rh = 0; rh < 2; rh++) {
+            q[rh] = ldg64(tb + 256 + ((rh * 2 + (c >> 1)) * 32 + lane) * 16 + (c & 1) * 8);
+            h[rh] = ldg128(tb + (g + 8 * rh) * 16);
+        }
+    }
+    __device__ __forceinline__ void store(uint8_t* sa, int c, int mi, int lane) const {
+        const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+        for (int rh = 0; rh < 2; rh++) {
+            const float d = f16f(h[rh].x), dmin = f16f(h[rh].x >> 16);
+            const uint32_t S0 = h[rh].y, S1 = h[rh].z, S2 = h[rh].w;
+            const uint32_t SC = (c < 2) ? (S0 & 0x3f3f3f3fu) : ((S2 & 0x0f0f0f0fu) | ((S0 >> 2) & 0x30303030u));
+            const uint32_t MN = (c < 2) ? (S1 & 0x3f3f3f3fu) : (((S2 >> 4) & 0x0f0f0f0fu) | ((S1 >> 2) & 0x30303030u));
+            const int j0 = (2 * c) & 3, j1 = (2 * c + 1) & 3;
+            const float dl = d * (float)byte_of(SC, j0), ml = dmin * (float)byte_of(MN, j0);
+            const float dh = d * (float)byte_of(SC, j1), mh = dmin * (float)byte_of(MN, j1);
+            float lo[8], hi[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const uint32_t b = byte_of(i < 4 ? q[rh].x : q[rh].y, i & 3);
+                lo[i] = fmaf(dl, (float)(b & 15u), -ml);
+                hi[i] = fmaf(dh, (float)(b >> 4), -mh);
+            }
+            const uint32_t row = mi * 16 + g + 8 * rh;
+            *reinterpret_cast<uint4*>(sa + sw128_off(row, t)) = pack8_bf16(lo);
+            *reinterpret_cast<uint4*>(sa + sw128_off(row, 4 + t)) = pack8_bf16(hi);
+        }
+    }
+};
+
+// Q6_K: slab c covers half n = c/2, runs kk = 2(c%2) and 2(c%2)+1; scale
+// sc[8n + 2kk] (qw6's even-scale reading, qw6.c:1568-1571).
+template <>
+struct ASlab<QW6F_Q6_K> {
+    uint4 L[2], sc[2];
+    uint2 H[2];
+    uint32_t dd[2];
+    __device__ __forceinline__ void load(const uint8_t* tb, int c, int lane) {
+        const int g = lane >> 2, n = c >> 1;
+#pragma unroll
+        for (int rh = 0; rh < 2; rh++) {
+            L[rh] = ldg128(tb + 288 + ((rh * 3 + n) * 32 + lane) * 16);
+            H[rh] = ldg64(tb + 288 + ((rh * 3 + 2) * 32 + lane) * 16 + n * 8);
+            sc[rh] = ldg128(tb + (g + 8 * rh) * 16);
+            dd[rh] = ldg16(tb + 256 + (g + 8 * rh) * 2);
+        }
+    }
+    __device__ __forceinline__ void store(uint8_t* sa, int c, int mi, int lane) const {
+        const int g = lane >> 2, t = lane & 3, n = c >> 1, k0 = 2 * (c & 1);
+#pragma unroll
+        for (int rh = 0; rh < 2; rh++) {
+            const float d = f16f(dd[rh]);
+            const float d0 = d * (float)(int8_t)byte16(sc[rh], 8 * n + 2 * k0);
+            const float d1 = d * (float)(int8_t)byte16(sc[rh], 8 * n + 2 * (k0 + 1));
+            float v0[8], v1[8];
+#pragma unroll
+            for (int hw = 0; hw < 2; hw++) {
+                const uint32_t A = hw ? L[rh].y : L[rh].x, B = hw ? L[rh].w : L[rh].z, Hh = hw ? H[rh].y : H[rh].x;
+                uint32_t q0, q1;
+                if (k0 == 0) {
+                    q0 = (A & 0x0f0f0f0fu) | ((Hh << 4) & 0x30303030u);
+                    q1 = (B & 0x0f0f0f0fu) | ((Hh << 2) & 0x30303030u);
+                } else {
+                    q0 = ((A >> 4) & 0x0f0f0f0fu) | (Hh & 0x30303030u);
+                    q1 = ((B >> 4) & 0x0f0f0f0fu) | ((Hh >> 2) & 0x30303030u);
+                }
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    v0[4 * hw + i] = d0 * (float)((int)byte_of(q0, i) - 32);
+                    v1[4 * hw + i] = d1 * (float)((int)byte_of(q1, i) - 32);
+                }
+            }
+            const uint32_t row = mi * 16 + g + 8 * rh;
+            *reinterpret_cast<uint4*>(sa + sw128_off(row, t)) = pack8_bf16(v0);
+            *reinterpret_cast<uint4*>(sa + sw128_off(row, 4 + t)) = pack8_bf16(v1);
+        }
+    }
+};
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// B rows: bf16 row j of the item from src + rowidx[j] * ld (K slab ks);
-// rows >= cnt are zero (up to npad).
-__device__ __forceinline__ void produce_b(uint8_t* sb, const __nv_bfloat16* src, int ld, const int* rowidx, int cnt,
-                                          int npad, int ks) {
+// B rows (K slab ks): bf16 row j of the item from src + rowidx[j]*ld, zero
+// for j >= cnt (up to npad), streamed with cp.async.
+__device__ __forceinline__ void issue_b(uint8_t* sb, const __nv_bfloat16* src, int ld, const int* rowidx, int cnt,
+                                        int npad, int ks) {
     for (int i = threadIdx.x; i < npad * 8; i += blockDim.x) {
         const int r = i >> 3, cc = i & 7;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (r < cnt) v = *reinterpret_cast<const uint4*>(src + (size_t)rowidx[r] * ld + ks * 64 + cc * 8);
-        *reinterpret_cast<uint4*>(sb + sw128_off(r, cc)) = v;
+        const bool live = r < cnt;
+        const __nv_bfloat16* p = src + (live ? (size_t)rowidx[r] * ld + ks * 64 + cc * 8 : 0);
+        cp_async16(sb + sw128_off(r, cc), p, live ? 16u : 0u);
     }
 }
 
 __device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
-// ----------------------------------------------------------------- gemm1 --
-template <int GQ>
-__global__ void __launch_bounds__(256, 1) k_pf_gemm1(const PfArgs a) {
+// ------------------------------------------------------------- the GEMM --
+// MODE 0 (gate/up): A0 = gate rows [128 ft, +128), A1 = up rows, K = hidden,
+//   B = X rows of the item's tokens; epilogue H = bf16(silu(D0) * D1).
+// MODE 1 (down): A0/A1 = down rows [256 ft, +128) / [256 ft + 128, +128),
+//   K = inter, B = H rows of the item's assignments; epilogue writes the
+//   per-assignment expert outputs (bf16) for the slot-order combine.
+// 8 warps: warp w dequantizes 16-row m-tiles 2(w%4), 2(w%4)+1 of A(w/4);
+// all threads stream B with cp.async; thread 0 issues the MMAs.  Three smem
+// stages; every wait is time-bounded.
+constexpr int kPfStages = 3;
+
+template <int F, int MODE>
+__global__ void __launch_bounds__(256, 1) k_pf_gemm(const PfArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     constexpr uint32_t A_BYTES = 128 * 128, B_BYTES = kPfChunk * 128, STAGE = 2 * A_BYTES + B_BYTES;
-    constexpr int TB = Fmt<GQ>::TB;
-    __shared__ uint64_t mbar[2];
+    constexpr int TB = Fmt<F>::TB, S = kPfStages;
+    __shared__ uint64_t mbar[S];
     __shared__ uint32_t tmem_base;
-    __shared__ int ncommit[2];
-    __shared__ int rowtok[kPfChunk];
-    const int ftiles = a.inter / 128;
-    const int item = blockIdx.x / ftiles, ft = blockIdx.x % ftiles;
+    __shared__ int ncommit[S];
+    __shared__ int rows[kPfChunk];
+    const int K = MODE == 0 ? a.hidden : a.inter;
+    const int nft = MODE == 0 ? a.inter / 128 : a.hidden / 256;
+    const int item = blockIdx.x / nft, ft = blockIdx.x % nft;
     if (item >= *a.nitems) return;
     const int4 it = a.items[item];
     const int e = it.x, off = it.y, cnt = it.z, npad = (cnt + 15) & ~15;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    for (int j = tid; j < cnt; j += blockDim.x) rowtok[j] = a.order[off + j] / a.topk;
+    for (int j = tid; j < cnt; j += blockDim.x) rows[j] = MODE == 0 ? a.order[off + j] / a.topk : a.order[off + j];
     if (warp == 0) tmem_alloc(&tmem_base, 512);
     if (tid == 0) {
-        mbar_init(&mbar[0], 1);
-        mbar_init(&mbar[1], 1);
+        for (int i = 0; i < S; i++) {
+            mbar_init(&mbar[i], 1);
+            ncommit[i] = 0;
+        }
         mbar_fence_init();
-        ncommit[0] = ncommit[1] = 0;
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_base;
     const uint32_t idesc = umma_idesc_bf16(128, npad);
-    const int nbh = a.hidden / 256, nk = a.hidden / 64;
-    // producer unit of this warp: matrix (gate/up) and two 16-row m-tiles
+    const int nbk = K / 256, nk = K / 64;
+    const __nv_bfloat16* bsrc = MODE == 0 ? a.x : a.h;
     const int mtx = warp >> 2, mi0 = 2 * (warp & 3);
-    const uint8_t* wbase = (mtx ? a.up + (size_t)e * a.ustride : a.gate + (size_t)e * a.gstride);
+    // first packed m-tile of this warp's A matrix
+    const uint8_t* wbase;
+    int mt0;
+    if (MODE == 0) {
+        wbase = mtx ? a.up + (size_t)e * a.ustride : a.gate + (size_t)e * a.gstride;
+        mt0 = ft * 8;
+    } else {
+        wbase = a.down + (size_t)e * a.dstride;
+        mt0 = (2 * ft + mtx) * 8;
+    }
+    auto tile = [&](int u, int ks) { return wbase + ((size_t)(mt0 + mi0 + u) * nbk + (ks >> 2)) * TB; };
+
+    ASlab<F> cur[2], nxt[2];
+    issue_b(smem + 2 * A_BYTES, bsrc, K, rows, cnt, npad, 0);
+    cp_async_commit();
+    cur[0].load(tile(0, 0), 0, lane);
+    cur[1].load(tile(1, 0), 0, lane);
     bool ok = true;
-    for (int ks = 0; ks < nk && ok; ks++) {
-        const int s = ks & 1;
-        if (ks >= 2) ok = mbar_wait(&mbar[s], ((ks - 2) >> 1) & 1, a.err, 11);
+    for (int ks = 0; ks < nk; ks++) {
+        const int s = ks % S;
+        if (ks + 1 < nk) {
+            const int s1 = (ks + 1) % S;
+            if (ks + 1 >= S) ok = ok && mbar_wait(&mbar[s1], ((ks + 1 - S) / S) & 1, a.err, 31 + MODE);
+            if (ok) issue_b(smem + s1 * STAGE + 2 * A_BYTES, bsrc, K, rows, cnt, npad, ks + 1);
+            nxt[0].load(tile(0, ks + 1), (ks + 1) & 3, lane);
+            nxt[1].load(tile(1, ks + 1), (ks + 1) & 3, lane);
+        }
+        cp_async_commit();
+        uint8_t* sa = smem + s * STAGE + mtx * A_BYTES;
+        if (ok) {
+            cur[0].store(sa, ks & 3, mi0, lane);
+            cur[1].store(sa, ks & 3, mi0 + 1, lane);
+        }
+        cp_async_wait<1>();
+        fence_async_smem();
         ok = __syncthreads_and(ok);
         if (!ok) break;
-        uint8_t* sa = smem + s * STAGE;
-        const int b = ks >> 2, c = ks & 3;
-#pragma unroll
-        for (int u = 0; u < 2; u++) {
-            const int mi = mi0 + u;
-            produce_a<GQ>(sa + mtx * A_BYTES, wbase + ((size_t)(ft * 8 + mi) * nbh + b) * TB, c, mi, lane);
-        }
-        produce_b(sa + 2 * A_BYTES, a.x, a.hidden, rowtok, cnt, npad, ks);
-        fence_async_smem();
-        __syncthreads();
         if (tid == 0) {
             tc_fence_after();
-            const uint32_t ag = smem_u32(sa), au = ag + A_BYTES, bb = ag + 2 * A_BYTES;
+            const uint32_t a0 = smem_u32(smem + s * STAGE), a1 = a0 + A_BYTES, bb = a0 + 2 * A_BYTES;
 #pragma unroll
             for (int k4 = 0; k4 < 4; k4++) {
                 const uint64_t bd = umma_desc_sw128(bb + 32 * k4);
                 const uint32_t acc = (ks > 0 || k4 > 0) ? 1u : 0u;
-                umma_bf16(tmem, umma_desc_sw128(ag + 32 * k4), bd, idesc, acc);
-                umma_bf16(tmem + 256, umma_desc_sw128(au + 32 * k4), bd, idesc, acc);
+                umma_bf16(tmem, umma_desc_sw128(a0 + 32 * k4), bd, idesc, acc);
+                umma_bf16(tmem + 256, umma_desc_sw128(a1 + 32 * k4), bd, idesc, acc);
             }
             umma_commit(&mbar[s]);
             ncommit[s]++;
         }
+        cur[0] = nxt[0];
+        cur[1] = nxt[1];
     }
-    if (ok) ok = mbar_wait(&mbar[(nk - 1) & 1], ((nk - 1) >> 1) & 1, a.err, 12);
+    cp_async_wait<0>();
+    if (ok) ok = mbar_wait(&mbar[(nk - 1) % S], ((nk - 1) / S) & 1, a.err, 33 + MODE);
     ok = __syncthreads_and(ok);
     tc_fence_after();
     if (ok) {
-        const int wq = warp & 3, wg = warp >> 2, f = ft * 128 + wq * 32 + lane;
+        const int wq = warp & 3, wg = warp >> 2;
         const uint32_t lrow = (uint32_t)(wq * 32) << 16;
         for (int c0 = wg * 16; c0 < npad; c0 += 32) {
-            float gv[16], uv[16];
-            tmem_ld16(tmem + lrow + (uint32_t)c0, gv);
-            tmem_ld16(tmem + lrow + 256u + (uint32_t)c0, uv);
+            float v0[16], v1[16];
+            tmem_ld16(tmem + lrow + (uint32_t)c0, v0);
+            tmem_ld16(tmem + lrow + 256u + (uint32_t)c0, v1);
+            if (MODE == 0) {
+                const int f = ft * 128 + wq * 32 + lane;
 #pragma unroll
-            for (int j = 0; j < 16; j++) {
-                const int r = c0 + j;
-                if (r < cnt)
-                    a.h[(size_t)a.order[off + r] * a.inter + f] = __float2bfloat16_rn(silu_fast(gv[j]) * uv[j]);
+                for (int j = 0; j < 16; j++)
+                    if (c0 + j < cnt)
+                        a.h[(size_t)a.order[off + c0 + j] * a.inter + f] = __float2bfloat16_rn(silu_fast(v0[j]) * v1[j]);
+            } else {
+                const int f = 2 * ft * 128 + wq * 32 + lane;
+#pragma unroll
+                for (int j = 0; j < 16; j++)
+                    if (c0 + j < cnt) {
+                        __nv_bfloat16* o = a.dout + (size_t)rows[c0 + j] * a.hidden + f;
+                        o[0] = __float2bfloat16_rn(v0[j]);
+                        o[128] = __float2bfloat16_rn(v1[j]);
+                    }
             }
         }
     } else {
         __syncthreads();
-        for (int s = 0; s < 2; s++)
-            if (ncommit[s] > 0) mbar_wait(&mbar[s], (ncommit[s] - 1) & 1, nullptr, 0);
+        for (int i = 0; i < S; i++)
+            if (ncommit[i] > 0) mbar_wait(&mbar[i], (ncommit[i] - 1) & 1, nullptr, 0);
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
-// ----------------------------------------------------------------- gemm2 --
-template <int DQ>
-__global__ void __launch_bounds__(256, 2) k_pf_gemm2(const PfArgs a) {
-    extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    constexpr uint32_t A_BYTES = 128 * 128, B_BYTES = kPfChunk * 128, STAGE = A_BYTES + B_BYTES;
-    constexpr int TB = Fmt<DQ>::TB;
-    __shared__ uint64_t mbar[2];
-    __shared__ uint32_t tmem_base;
-    __shared__ int ncommit[2];
-    __shared__ int rowa[kPfChunk];
-    const int ftiles = a.hidden / 128;
-    const int item = blockIdx.x / ftiles, ft = blockIdx.x % ftiles;
-    if (item >= *a.nitems) return;
-    const int4 it = a.items[item];
-    const int e = it.x, off = it.y, cnt = it.z, npad = (cnt + 15) & ~15;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    for (int j = tid; j < cnt; j += blockDim.x) rowa[j] = a.order[off + j];
-    if (warp == 0) tmem_alloc(&tmem_base, 256);
-    if (tid == 0) {
-        mbar_init(&mbar[0], 1);
-        mbar_init(&mbar[1], 1);
-        mbar_fence_init();
-        ncommit[0] = ncommit[1] = 0;
+// out[t][f] = sum_k w[t,k] * dout[t*topk + k][f], fp32 in slot order k
+// (rows mode: out[r] = w[r] * dout[r]).
+__global__ void k_pf_combine(const PfArgs a) {
+    const int t = blockIdx.y, f = (blockIdx.x * blockDim.x + threadIdx.x) * 2;
+    if (f >= a.hidden) return;
+    float o0 = 0.f, o1 = 0.f;
+    for (int k = 0; k < a.topk; k++) {
+        const size_t s = (size_t)t * a.topk + k;
+        const float w = a.w[s];
+        const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(a.dout + s * a.hidden + f);
+        o0 = fmaf(w, __bfloat162float(v.x), o0);
+        o1 = fmaf(w, __bfloat162float(v.y), o1);
     }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = tmem_base;
-    const uint32_t idesc = umma_idesc_bf16(128, npad);
-    const int nbi = a.inter / 256, nk = a.inter / 64;
-    const uint8_t* wbase = a.down + (size_t)e * a.dstride;
-    bool ok = true;
-    for (int ks = 0; ks < nk && ok; ks++) {
-        const int s = ks & 1;
-        if (ks >= 2) ok = mbar_wait(&mbar[s], ((ks - 2) >> 1) & 1, a.err, 21);
-        ok = __syncthreads_and(ok);
-        if (!ok) break;
-        uint8_t* sa = smem + s * STAGE;
-        const int b = ks >> 2, c = ks & 3, mi = warp;
-        produce_a<DQ>(sa, wbase + ((size_t)(ft * 8 + mi) * nbi + b) * TB, c, mi, lane);
-        produce_b(sa + A_BYTES, a.h, a.inter, rowa, cnt, npad, ks);
-        fence_async_smem();
-        __syncthreads();
-        if (tid == 0) {
-            tc_fence_after();
-            const uint32_t aa = smem_u32(sa), bb = aa + A_BYTES;
-#pragma unroll
-            for (int k4 = 0; k4 < 4; k4++)
-                umma_bf16(tmem, umma_desc_sw128(aa + 32 * k4), umma_desc_sw128(bb + 32 * k4), idesc,
-                          (ks > 0 || k4 > 0) ? 1u : 0u);
-            umma_commit(&mbar[s]);
-            ncommit[s]++;
-        }
-    }
-    if (ok) ok = mbar_wait(&mbar[(nk - 1) & 1], ((nk - 1) >> 1) & 1, a.err, 22);
-    ok = __syncthreads_and(ok);
-    tc_fence_after();
-    if (ok) {
-        const int wq = warp & 3, wg = warp >> 2, f = ft * 128 + wq * 32 + lane;
-        const uint32_t lrow = (uint32_t)(wq * 32) << 16;
-        for (int c0 = wg * 16; c0 < npad; c0 += 32) {
-            float v[16];
-            tmem_ld16(tmem + lrow + (uint32_t)c0, v);
-#pragma unroll
-            for (int j = 0; j < 16; j++) {
-                const int r = c0 + j;
-                if (r < cnt) {
-                    const int as = rowa[r];
-                    atomicAdd(a.out + (size_t)(as / a.topk) * a.hidden + f, a.w[as] * v[j]);
-                }
-            }
-        }
-    } else {
-        __syncthreads();
-        for (int s = 0; s < 2; s++)
-            if (ncommit[s] > 0) mbar_wait(&mbar[s], (ncommit[s] - 1) & 1, nullptr, 0);
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 0) tmem_dealloc(tmem, 256);
+    *reinterpret_cast<float2*>(a.out + (size_t)t * a.hidden + f) = make_float2(o0, o1);
 }
 
 }  // namespace qw6
@@ -390,17 +397,19 @@ static int pf_items_max(uint32_t tk, uint32_t ne) { return (int)((tk < ne ? tk :
 
 extern "C" size_t qw6k_moe_prefill_ws_bytes(uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t ne,
                                            uint32_t topk) {
-    (void)hidden;
     const size_t tk = (size_t)ntok * topk;
     return al256(tk * 4) * 4 + al256(256 * 4) * 2 + al256((size_t)pf_items_max((uint32_t)tk, ne) * 16) + 256 +
-           al256(tk * inter * 2);
+           al256(tk * inter * 2) + al256(tk * hidden * 2);
 }
 
 static int pf_args(const qw6k_moe_desc* d, int* err, PfArgs& a) {
-    if (!d || !d->gate || !d->up || !d->down || !d->logits || !d->x || !d->out || !d->ws || !err || !d->ntok ||
+    const bool rows_mode = d && !d->logits;
+    if (rows_mode && (d->topk != 1 || !d->row_expert || !d->row_weight)) return QW6K_ERR_ARG;
+    if (!d || !d->gate || !d->up || !d->down || !d->x || !d->out || !d->ws || !err || !d->ntok ||
         !d->ne || d->ne > 256 || !d->topk || d->topk > 32 || d->topk > d->ne || (size_t)d->ntok * d->topk > (1u << 22))
         return QW6K_ERR_ARG;
-    if (d->hidden % 256 || d->inter % 256 || !d->hidden || !d->inter || d->hidden > 16384 || d->inter > 16384)
+    if (d->hidden % 256 || d->inter % 128 || d->inter % 256 || !d->hidden || !d->inter || d->hidden > 16384 ||
+        d->inter > 16384)
         return QW6K_ERR_ARG;
     if (d->gq != QW6F_Q4_K_M && d->gq != QW6F_Q4_K_S && d->gq != QW6F_Q6_K) return QW6K_ERR_QUANT;
     if (d->dq != QW6F_Q4_K_M && d->dq != QW6F_Q4_K_S && d->dq != QW6F_Q6_K) return QW6K_ERR_QUANT;
@@ -434,31 +443,25 @@ static int pf_args(const qw6k_moe_desc* d, int* err, PfArgs& a) {
     a.off = (int32_t*)p; p += al256(256 * 4);
     a.items = (int4*)p; p += al256((size_t)pf_items_max((uint32_t)tk, d->ne) * 16);
     a.nitems = (int*)p; p += 256;
-    a.h = (__nv_bfloat16*)p;
+    a.h = (__nv_bfloat16*)p; p += al256(tk * d->inter * 2);
+    a.dout = (__nv_bfloat16*)p;
+    if (rows_mode) {  // caller-supplied routing
+        a.idx = const_cast<int32_t*>(d->row_expert);
+        a.w = const_cast<float*>(d->row_weight);
+    }
     return 0;
 }
 
-template <int GQ>
-static int launch_g1(const PfArgs& a, int mi, cudaStream_t st) {
-    const size_t smem = 2 * (2 * 128 * 128 + kPfChunk * 128) + 1024;
+template <int F, int MODE>
+static int launch_pf(const PfArgs& a, int mi, cudaStream_t st) {
+    const size_t smem = (size_t)kPfStages * (2 * 128 * 128 + kPfChunk * 128) + 1024;
     static bool cfg = false;
-    if (!cfg && cudaFuncSetAttribute(k_pf_gemm1<GQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+    if (!cfg && cudaFuncSetAttribute(k_pf_gemm<F, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
                     cudaSuccess)
         return QW6K_ERR_CUDA;
     cfg = true;
-    k_pf_gemm1<GQ><<<mi * (a.inter / 128), 256, smem, st>>>(a);
-    return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
-}
-
-template <int DQ>
-static int launch_g2(const PfArgs& a, int mi, cudaStream_t st) {
-    const size_t smem = 2 * (128 * 128 + kPfChunk * 128) + 1024;
-    static bool cfg = false;
-    if (!cfg && cudaFuncSetAttribute(k_pf_gemm2<DQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-                    cudaSuccess)
-        return QW6K_ERR_CUDA;
-    cfg = true;
-    k_pf_gemm2<DQ><<<mi * (a.hidden / 128), 256, smem, st>>>(a);
+    const int nft = MODE == 0 ? a.inter / 128 : a.hidden / 256;
+    k_pf_gemm<F, MODE><<<mi * nft, 256, smem, st>>>(a);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
 }
 
@@ -468,7 +471,7 @@ extern "C" int qw6k_moe_prefill_check(const qw6k_moe_desc* d, int* err) {
 }
 
 /* phases: 0 route, 1 count (after zeroing counts), 2 offsets, 3 scatter,
- * 4 gate/up GEMM (+silu), 5 down GEMM with weighted scatter-add (after zeroing out) */
+ * 4 gate/up GEMM (+silu), 5 down GEMM (per-assignment outputs), 6 combine */
 extern "C" int qw6k_moe_prefill_phase(const qw6k_moe_desc* d, int* err, int phase, cudaStream_t st) {
     PfArgs a;
     const int rc = pf_args(d, err, a);
@@ -477,6 +480,7 @@ extern "C" int qw6k_moe_prefill_phase(const qw6k_moe_desc* d, int* err, int phas
     const int mi = pf_items_max((uint32_t)tk, (uint32_t)a.ne);
     switch (phase) {
     case 0:
+        if (!d->logits) return 0;  // rows mode: routing supplied by the caller
         k_pf_route<<<(a.ntok + 7) / 8, 256, 0, st>>>(a);
         break;
     case 1:
@@ -490,10 +494,14 @@ extern "C" int qw6k_moe_prefill_phase(const qw6k_moe_desc* d, int* err, int phas
         k_pf_scatter<<<(tk + 255) / 256, 256, 0, st>>>(a);
         break;
     case 4:
-        return (d->gq == QW6F_Q6_K) ? launch_g1<QW6F_Q6_K>(a, mi, st) : launch_g1<QW6F_Q4_K_M>(a, mi, st);
+        return (d->gq == QW6F_Q6_K) ? launch_pf<QW6F_Q6_K, 0>(a, mi, st) : launch_pf<QW6F_Q4_K_M, 0>(a, mi, st);
     case 5:
-        if (cudaMemsetAsync(a.out, 0, (size_t)a.ntok * a.hidden * 4, st) != cudaSuccess) return QW6K_ERR_CUDA;
-        return (d->dq == QW6F_Q6_K) ? launch_g2<QW6F_Q6_K>(a, mi, st) : launch_g2<QW6F_Q4_K_M>(a, mi, st);
+        return (d->dq == QW6F_Q6_K) ? launch_pf<QW6F_Q6_K, 1>(a, mi, st) : launch_pf<QW6F_Q4_K_M, 1>(a, mi, st);
+    case 6: {
+        dim3 g((a.hidden / 2 + 255) / 256, a.ntok);
+        k_pf_combine<<<g, 256, 0, st>>>(a);
+        break;
+    }
     default:
         return QW6K_ERR_ARG;
     }

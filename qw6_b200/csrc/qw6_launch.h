@@ -89,6 +89,10 @@ typedef struct {
     uint32_t ntok, hidden, inter, ne, topk;
     void *ws;
     size_t ws_bytes;
+    /* prefill "rows" mode (logits == NULL, topk == 1): row r of x goes to
+     * expert row_expert[r] with weight row_weight[r]; out[r] = w * FFN(x[r]) */
+    const int32_t *row_expert;
+    const float *row_weight;
 } qw6k_moe_desc;
 
 size_t qw6k_moe_ws_bytes(uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t ne, uint32_t topk);
@@ -99,12 +103,21 @@ int qw6k_moe_phase(const qw6k_moe_desc *d, int phase, cudaStream_t st);
 
 /* Routed MoE FFN for prefill batches on tcgen05 (k_prefill.cu): desc->x is
  * bf16 [ntok x hidden]; gate/up/down Q4_K or Q6_K packed; hidden, inter
- * multiples of 256.  Phases 0..5 in order on one stream (route, count,
- * offsets, scatter, gate/up GEMM, down GEMM + weighted scatter-add into out,
- * which phase 5 zeroes first).  *err records bounded-wait timeouts. */
+ * multiples of 256.  Phases 0..6 in order on one stream (route, count,
+ * offsets, scatter, gate/up GEMM, down GEMM, slot-order combine into out).
+ * *err records bounded-wait timeouts. */
 size_t qw6k_moe_prefill_ws_bytes(uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t ne, uint32_t topk);
 int qw6k_moe_prefill_check(const qw6k_moe_desc *d, int *err);
 int qw6k_moe_prefill_phase(const qw6k_moe_desc *d, int *err, int phase, cudaStream_t st);
+
+/* Expert-parallel dispatch/combine helpers (k_ep.cu). */
+int qw6k_ep_count(const int32_t *idx, uint32_t n, uint32_t world, uint32_t epr, int32_t *cnt, int32_t *pos,
+                  cudaStream_t st);
+int qw6k_ep_pack(const int32_t *idx, const float *w, const int32_t *pos, const int32_t *cnt, uint32_t n, uint32_t topk,
+                 uint32_t world, uint32_t epr, const void *x_bf16, uint32_t hidden, void *send_x, int32_t *send_e,
+                 float *send_w, int32_t *send_pos, cudaStream_t st);
+int qw6k_ep_combine(const float *ret, const int32_t *send_pos, uint32_t ntok, uint32_t topk, uint32_t hidden,
+                    float *out, cudaStream_t st);
 
 /* Fixed 1 MiB device scratch (k_static.cu) of the allocation-free MoE entry
  * point; *ptr is its device address on the current device (looked up with

@@ -2,6 +2,7 @@
 #define _POSIX_C_SOURCE 200809L
 
 #include <stddef.h>
+#include <string.h>
 #include <stdint.h>
 
 #include <cuda_runtime_api.h>
@@ -58,6 +59,7 @@ int qw6cu_moe_decode(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu_
     int rc = qw6h_use(ctx);
     if (rc) return rc;
     qw6k_moe_desc d;
+    memset(&d, 0, sizeof d);
     if ((rc = moe_desc(ctx, gate, up, down, ntok, hidden, inter, n_experts, top_k, &d))) return rc;
     d.logits = logits;
     d.x = x;
@@ -75,6 +77,7 @@ int qw6cu_moe_decode_hostio(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const
         return QW6CU_ERR_ARG;
     }
     qw6k_moe_desc d;
+    memset(&d, 0, sizeof d);
     if ((rc = moe_desc(ctx, gate, up, down, ntok, hidden, inter, n_experts, top_k, &d))) return rc;
     const size_t lb = (size_t)ntok * n_experts * 4, xb = (size_t)ntok * hidden * 4;
     uint8_t *in = qw6h_buf(ctx, QW6H_BUF_X, ((lb + 255) & ~(size_t)255) + xb);
@@ -120,6 +123,7 @@ int qw6cu_moe_decode_noalloc(const qw6cu_expert_pack *gate, const qw6cu_expert_p
         return QW6CU_ERR_CUDA;
     }
     qw6k_moe_desc d;
+    memset(&d, 0, sizeof d);
     d.gq = gate->quant;
     d.dq = down->quant;
     d.gate = gate->base;
@@ -168,6 +172,7 @@ int qw6cu_moe_prefill(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu
     int *err = qw6h_dev_err(ctx);
     if (!err) return QW6CU_ERR_NOMEM;
     qw6k_moe_desc d;
+    memset(&d, 0, sizeof d);
     d.gq = gate->quant;
     d.dq = down->quant;
     d.gate = gate->base;
@@ -188,12 +193,81 @@ int qw6cu_moe_prefill(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu
     d.ws = qw6h_buf(ctx, QW6H_BUF_WS, d.ws_bytes);
     if (!d.ws) return QW6CU_ERR_NOMEM;
     rc = qw6h_rc(qw6k_moe_prefill_check(&d, err), "moe_prefill");
-    static const int kid[6] = {QW6H_K_PF_PLAN, QW6H_K_PF_PLAN, QW6H_K_PF_PLAN,
-                               QW6H_K_PF_PLAN, QW6H_K_PF_GEMM1, QW6H_K_PF_GEMM2};
-    for (int ph = 0; ph < 6 && !rc; ph++) {
+    static const int kid[7] = {QW6H_K_PF_PLAN,  QW6H_K_PF_PLAN,  QW6H_K_PF_PLAN, QW6H_K_PF_PLAN,
+                               QW6H_K_PF_GEMM1, QW6H_K_PF_GEMM2, QW6H_K_PF_PLAN};
+    for (int ph = 0; ph < 7 && !rc; ph++) {
         const int rec = qw6h_prof_a(ctx, kid[ph]);
         rc = qw6h_rc(qw6k_moe_prefill_phase(&d, err, ph, ctx->st), "moe_prefill");
         qw6h_prof_b(ctx, rec);
     }
     return rc;
+}
+
+int qw6cu_moe_prefill_rows(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
+                           const qw6cu_expert_pack *down, const void *x_bf16, const int32_t *row_expert,
+                           const float *row_weight, float *out, uint32_t nrows, uint32_t hidden, uint32_t inter,
+                           uint32_t n_experts) {
+    int rc = qw6h_use(ctx);
+    if (rc) return rc;
+    if (!gate || !up || !down || gate->quant != up->quant || !row_expert || !row_weight) {
+        qw6h_set_err("qw6cu_moe_prefill_rows: packs (gate/up of one quant type) and row routing are required");
+        return QW6CU_ERR_ARG;
+    }
+    int *err = qw6h_dev_err(ctx);
+    if (!err) return QW6CU_ERR_NOMEM;
+    qw6k_moe_desc d;
+    memset(&d, 0, sizeof d);
+    d.gq = gate->quant;
+    d.dq = down->quant;
+    d.gate = gate->base;
+    d.up = up->base;
+    d.down = down->base;
+    d.gstride = gate->stride;
+    d.ustride = up->stride;
+    d.dstride = down->stride;
+    d.x = (const float *)x_bf16;
+    d.out = out;
+    d.ntok = nrows;
+    d.hidden = hidden;
+    d.inter = inter;
+    d.ne = n_experts;
+    d.topk = 1;
+    d.row_expert = row_expert;
+    d.row_weight = row_weight;
+    d.ws_bytes = qw6k_moe_prefill_ws_bytes(nrows, hidden, inter, n_experts, 1);
+    d.ws = qw6h_buf(ctx, QW6H_BUF_WS, d.ws_bytes);
+    if (!d.ws) return QW6CU_ERR_NOMEM;
+    rc = qw6h_rc(qw6k_moe_prefill_check(&d, err), "moe_prefill_rows");
+    static const int kid[7] = {QW6H_K_PF_PLAN,  QW6H_K_PF_PLAN,  QW6H_K_PF_PLAN, QW6H_K_PF_PLAN,
+                               QW6H_K_PF_GEMM1, QW6H_K_PF_GEMM2, QW6H_K_PF_PLAN};
+    for (int ph = 1; ph < 7 && !rc; ph++) {
+        const int rec = qw6h_prof_a(ctx, kid[ph]);
+        rc = qw6h_rc(qw6k_moe_prefill_phase(&d, err, ph, ctx->st), "moe_prefill_rows");
+        qw6h_prof_b(ctx, rec);
+    }
+    return rc;
+}
+
+int qw6cu_ep_count(qw6cu_ctx *ctx, const int32_t *idx, uint32_t nassign, uint32_t world, uint32_t experts_per_rank,
+                   int32_t *dst_count, int32_t *pos) {
+    int rc = qw6h_use(ctx);
+    if (rc) return rc;
+    return qw6h_rc(qw6k_ep_count(idx, nassign, world, experts_per_rank, dst_count, pos, ctx->st), "ep_count");
+}
+
+int qw6cu_ep_pack(qw6cu_ctx *ctx, const int32_t *idx, const float *w, const int32_t *pos, const int32_t *dst_count,
+                  uint32_t nassign, uint32_t top_k, uint32_t world, uint32_t experts_per_rank, const void *x_bf16,
+                  uint32_t hidden, void *send_x, int32_t *send_expert, float *send_weight, int32_t *send_pos) {
+    int rc = qw6h_use(ctx);
+    if (rc) return rc;
+    return qw6h_rc(qw6k_ep_pack(idx, w, pos, dst_count, nassign, top_k, world, experts_per_rank, x_bf16, hidden, send_x,
+                                send_expert, send_weight, send_pos, ctx->st),
+                   "ep_pack");
+}
+
+int qw6cu_ep_combine(qw6cu_ctx *ctx, const float *ret, const int32_t *send_pos, uint32_t ntok, uint32_t top_k,
+                     uint32_t hidden, float *out) {
+    int rc = qw6h_use(ctx);
+    if (rc) return rc;
+    return qw6h_rc(qw6k_ep_combine(ret, send_pos, ntok, top_k, hidden, out, ctx->st), "ep_combine");
 }
