@@ -192,36 +192,47 @@ size_t qw6cu_moe_prefill_workspace_bytes(uint32_t ntok, uint32_t hidden, uint32_
 /* Expert-parallel building block: the same grouped GEMMs with the routing
  * supplied per row instead of computed from logits.  Row r of x_bf16
  * ([nrows x hidden], device) is sent through expert row_expert[r] (an index
- * into these packs, < n_experts) and out[r] (fp32 [nrows x hidden],
- * overwritten) = row_weight[r] * down(silu(gate x_r) * up x_r).  Used on the
- * rank that owns the experts after an all-to-all dispatch of token rows. */
-int qw6cu_moe_prefill_rows(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
-                           const qw6cu_expert_pack *down, const void *x_bf16, const int32_t *row_expert,
-                           const float *row_weight, float *out, uint32_t nrows, uint32_t hidden, uint32_t inter,
-                           uint32_t n_experts);
+ * into these packs, < n_experts) and out_bf16[r] (bf16 [nrows x hidden],
+ * overwritten) = down(silu(gate x_r) * up x_r), unweighted -- bit for bit the
+ * per-assignment expert output qw6cu_moe_prefill forms before its combine.
+ * Used on the rank that owns the experts after an all-to-all dispatch of
+ * token rows. */
+int qw6cu_moe_expert_rows(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
+                          const qw6cu_expert_pack *down, const void *x_bf16, const int32_t *row_expert,
+                          void *out_bf16, uint32_t nrows, uint32_t hidden, uint32_t inter, uint32_t n_experts);
 
 /* ---- expert parallelism (prefill) ----
  * Experts are sharded contiguously over `world` ranks: rank r owns experts
  * [r*experts_per_rank, (r+1)*experts_per_rank).  One layer on a rank:
- *   qw6cu_moe_route -> qw6cu_ep_count -> all-to-all of dst_count ->
- *   qw6cu_ep_pack -> all-to-all of send_x / send_expert / send_weight ->
- *   qw6cu_moe_prefill_rows on the received rows (local packs) ->
- *   all-to-all of the weighted outputs back in send-row order ->
- *   qw6cu_ep_combine.  (qw6_b200/ep.py runs this with NCCL.) */
+ *   qw6cu_moe_route -> qw6cu_ep_count -> all-to-all of expert_count (each
+ *   rank receives the counts of its own experts from every source) ->
+ *   qw6cu_ep_pack -> all-to-all of the send rows -> qw6cu_ep_expand ->
+ *   qw6cu_moe_expert_rows on the received rows (local packs) -> all-to-all
+ *   of the bf16 expert outputs back in send-row order -> qw6cu_ep_combine.
+ * The result equals qw6cu_moe_prefill on the same tokens: the same expert
+ * outputs, weighted and summed in the same slot order.  (qw6_b200/ep.py runs
+ * this with NCCL.) */
 
-/* dst_count[world] (zeroed here) = assignments bound for each rank;
- * pos[a] = position of assignment a among those of its destination. */
-int qw6cu_ep_count(qw6cu_ctx *ctx, const int32_t *idx, uint32_t nassign, uint32_t world, uint32_t experts_per_rank,
-                   int32_t *dst_count, int32_t *pos);
-/* Send row p = (exclusive prefix of dst_count)[dst] + pos[a]: token row
- * (bf16, hidden) of assignment a = t*top_k + k, its expert index local to the
- * destination, its routing weight; send_pos[a] = p. */
-int qw6cu_ep_pack(qw6cu_ctx *ctx, const int32_t *idx, const float *w, const int32_t *pos, const int32_t *dst_count,
-                  uint32_t nassign, uint32_t top_k, uint32_t world, uint32_t experts_per_rank, const void *x_bf16,
-                  uint32_t hidden, void *send_x, int32_t *send_expert, float *send_weight, int32_t *send_pos);
-/* out[t] (fp32, overwritten) = sum_k ret[send_pos[t*top_k + k]] in slot order. */
-int qw6cu_ep_combine(qw6cu_ctx *ctx, const float *ret, const int32_t *send_pos, uint32_t ntok, uint32_t top_k,
-                     uint32_t hidden, float *out);
+/* expert_count[n_experts] (zeroed here) = assignments routed to each global
+ * expert; pos[a] = position of assignment a among those of its expert. */
+int qw6cu_ep_count(qw6cu_ctx *ctx, const int32_t *idx, uint32_t nassign, uint32_t n_experts, int32_t *expert_count,
+                   int32_t *pos);
+/* Send row p = (exclusive prefix of expert_count)[idx[a]] + pos[a] gets the
+ * token row (bf16, hidden) of assignment a = t*top_k + k; send_pos[a] = p.
+ * Send rows are sorted by global expert, hence grouped by destination rank
+ * and, inside each destination's block, by its local expert. */
+int qw6cu_ep_pack(qw6cu_ctx *ctx, const int32_t *idx, const int32_t *pos, const int32_t *expert_count,
+                  uint32_t nassign, uint32_t top_k, uint32_t n_experts, const void *x_bf16, uint32_t hidden,
+                  void *send_x, int32_t *send_pos);
+/* recv_count[s*experts_per_rank + e] rows from source rank s for local
+ * expert e arrive in (s, e) order; row_expert[r] (overwritten) = e of
+ * received row r.  world * experts_per_rank <= 256. */
+int qw6cu_ep_expand(qw6cu_ctx *ctx, const int32_t *recv_count, uint32_t world, uint32_t experts_per_rank,
+                    int32_t *row_expert);
+/* out[t] (fp32, overwritten) = sum_k w[t*top_k+k] * ret_bf16[send_pos[t*top_k+k]]
+ * as fp32 fma in slot order k (the single-GPU prefill combine). */
+int qw6cu_ep_combine(qw6cu_ctx *ctx, const void *ret_bf16, const float *w, const int32_t *send_pos, uint32_t ntok,
+                     uint32_t top_k, uint32_t hidden, float *out);
 
 /* ---- profiling ----
  * Per-launch CUDA events around every kernel this context enqueues (the
@@ -229,7 +240,7 @@ int qw6cu_ep_combine(qw6cu_ctx *ctx, const float *ret, const int32_t *send_pos, 
  * begin: allocate events for up to max_launches launches and start
  * recording; end: synchronize, then write per-kernel-id total milliseconds
  * and launch counts into arrays of QW6CU_NKERNELS entries and stop. */
-#define QW6CU_NKERNELS 13
+#define QW6CU_NKERNELS 15
 int qw6cu_profile_begin(qw6cu_ctx *ctx, uint32_t max_launches);
 int qw6cu_profile_end(qw6cu_ctx *ctx, double *ms_total, uint32_t *launches);
 const char *qw6cu_kernel_name(int kernel_id);

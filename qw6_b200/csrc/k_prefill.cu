@@ -404,8 +404,8 @@ extern "C" size_t qw6k_moe_prefill_ws_bytes(uint32_t ntok, uint32_t hidden, uint
 
 static int pf_args(const qw6k_moe_desc* d, int* err, PfArgs& a) {
     const bool rows_mode = d && !d->logits;
-    if (rows_mode && (d->topk != 1 || !d->row_expert || !d->row_weight)) return QW6K_ERR_ARG;
-    if (!d || !d->gate || !d->up || !d->down || !d->x || !d->out || !d->ws || !err || !d->ntok ||
+    if (rows_mode && (d->topk != 1 || !d->row_expert || !d->dout)) return QW6K_ERR_ARG;
+    if (!d || !d->gate || !d->up || !d->down || !d->x || (!d->out && !rows_mode) || !d->ws || !err || !d->ntok ||
         !d->ne || d->ne > 256 || !d->topk || d->topk > 32 || d->topk > d->ne || (size_t)d->ntok * d->topk > (1u << 22))
         return QW6K_ERR_ARG;
     if (d->hidden % 256 || d->inter % 128 || d->inter % 256 || !d->hidden || !d->inter || d->hidden > 16384 ||
@@ -445,9 +445,10 @@ static int pf_args(const qw6k_moe_desc* d, int* err, PfArgs& a) {
     a.nitems = (int*)p; p += 256;
     a.h = (__nv_bfloat16*)p; p += al256(tk * d->inter * 2);
     a.dout = (__nv_bfloat16*)p;
-    if (rows_mode) {  // caller-supplied routing
+    if (rows_mode) {  // caller-supplied routing; expert outputs into the caller's buffer
+        if (reinterpret_cast<uintptr_t>(d->dout) & 15u) return QW6K_ERR_ALIGN;
         a.idx = const_cast<int32_t*>(d->row_expert);
-        a.w = const_cast<float*>(d->row_weight);
+        a.dout = (__nv_bfloat16*)d->dout;
     }
     return 0;
 }
@@ -498,6 +499,7 @@ extern "C" int qw6k_moe_prefill_phase(const qw6k_moe_desc* d, int* err, int phas
     case 5:
         return (d->dq == QW6F_Q6_K) ? launch_pf<QW6F_Q6_K, 1>(a, mi, st) : launch_pf<QW6F_Q4_K_M, 1>(a, mi, st);
     case 6: {
+        if (!d->logits) return 0;  // rows mode: the caller combines
         dim3 g((a.hidden / 2 + 255) / 256, a.ntok);
         k_pf_combine<<<g, 256, 0, st>>>(a);
         break;

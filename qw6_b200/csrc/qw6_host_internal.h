@@ -39,6 +39,8 @@ enum {
     QW6H_K_PF_PLAN,
     QW6H_K_PF_GEMM1,
     QW6H_K_PF_GEMM2,
+    QW6H_K_PF_COMBINE,
+    QW6H_K_EP,
     QW6H_K_COUNT
 };
 

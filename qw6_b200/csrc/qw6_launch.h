@@ -89,10 +89,11 @@ typedef struct {
     uint32_t ntok, hidden, inter, ne, topk;
     void *ws;
     size_t ws_bytes;
-    /* prefill "rows" mode (logits == NULL, topk == 1): row r of x goes to
-     * expert row_expert[r] with weight row_weight[r]; out[r] = w * FFN(x[r]) */
+    /* prefill "rows" mode (logits == NULL, topk == 1, out unused): row r of
+     * x goes to expert row_expert[r]; dout[r] (bf16, [ntok x hidden]) =
+     * FFN_e(x[r]), unweighted */
     const int32_t *row_expert;
-    const float *row_weight;
+    void *dout;
 } qw6k_moe_desc;
 
 size_t qw6k_moe_ws_bytes(uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t ne, uint32_t topk);
@@ -111,13 +112,12 @@ int qw6k_moe_prefill_check(const qw6k_moe_desc *d, int *err);
 int qw6k_moe_prefill_phase(const qw6k_moe_desc *d, int *err, int phase, cudaStream_t st);
 
 /* Expert-parallel dispatch/combine helpers (k_ep.cu). */
-int qw6k_ep_count(const int32_t *idx, uint32_t n, uint32_t world, uint32_t epr, int32_t *cnt, int32_t *pos,
-                  cudaStream_t st);
-int qw6k_ep_pack(const int32_t *idx, const float *w, const int32_t *pos, const int32_t *cnt, uint32_t n, uint32_t topk,
-                 uint32_t world, uint32_t epr, const void *x_bf16, uint32_t hidden, void *send_x, int32_t *send_e,
-                 float *send_w, int32_t *send_pos, cudaStream_t st);
-int qw6k_ep_combine(const float *ret, const int32_t *send_pos, uint32_t ntok, uint32_t topk, uint32_t hidden,
-                    float *out, cudaStream_t st);
+int qw6k_ep_count(const int32_t *idx, uint32_t n, uint32_t ne, int32_t *cnt, int32_t *pos, cudaStream_t st);
+int qw6k_ep_pack(const int32_t *idx, const int32_t *pos, const int32_t *cnt, uint32_t n, uint32_t topk, uint32_t ne,
+                 const void *x_bf16, uint32_t hidden, void *send_x, int32_t *send_pos, cudaStream_t st);
+int qw6k_ep_expand(const int32_t *recv_cnt, uint32_t world, uint32_t epr, int32_t *row_expert, cudaStream_t st);
+int qw6k_ep_combine(const void *ret_bf16, const float *w, const int32_t *send_pos, uint32_t ntok, uint32_t topk,
+                    uint32_t hidden, float *out, cudaStream_t st);
 
 /* Fixed 1 MiB device scratch (k_static.cu) of the allocation-free MoE entry
  * point; *ptr is its device address on the current device (looked up with

@@ -194,7 +194,7 @@ int qw6cu_moe_prefill(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu
     if (!d.ws) return QW6CU_ERR_NOMEM;
     rc = qw6h_rc(qw6k_moe_prefill_check(&d, err), "moe_prefill");
     static const int kid[7] = {QW6H_K_PF_PLAN,  QW6H_K_PF_PLAN,  QW6H_K_PF_PLAN, QW6H_K_PF_PLAN,
-                               QW6H_K_PF_GEMM1, QW6H_K_PF_GEMM2, QW6H_K_PF_PLAN};
+                               QW6H_K_PF_GEMM1, QW6H_K_PF_GEMM2, QW6H_K_PF_COMBINE};
     for (int ph = 0; ph < 7 && !rc; ph++) {
         const int rec = qw6h_prof_a(ctx, kid[ph]);
         rc = qw6h_rc(qw6k_moe_prefill_phase(&d, err, ph, ctx->st), "moe_prefill");
@@ -203,16 +203,16 @@ int qw6cu_moe_prefill(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu
     return rc;
 }
 
-int qw6cu_moe_prefill_rows(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
-                           const qw6cu_expert_pack *down, const void *x_bf16, const int32_t *row_expert,
-                           const float *row_weight, float *out, uint32_t nrows, uint32_t hidden, uint32_t inter,
-                           uint32_t n_experts) {
+int qw6cu_moe_expert_rows(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
+                          const qw6cu_expert_pack *down, const void *x_bf16, const int32_t *row_expert,
+                          void *out_bf16, uint32_t nrows, uint32_t hidden, uint32_t inter, uint32_t n_experts) {
     int rc = qw6h_use(ctx);
     if (rc) return rc;
-    if (!gate || !up || !down || gate->quant != up->quant || !row_expert || !row_weight) {
-        qw6h_set_err("qw6cu_moe_prefill_rows: packs (gate/up of one quant type) and row routing are required");
+    if (!gate || !up || !down || gate->quant != up->quant || !row_expert || !out_bf16) {
+        qw6h_set_err("qw6cu_moe_expert_rows: packs (gate/up of one quant type), row_expert and out are required");
         return QW6CU_ERR_ARG;
     }
+    if (!nrows) return 0;
     int *err = qw6h_dev_err(ctx);
     if (!err) return QW6CU_ERR_NOMEM;
     qw6k_moe_desc d;
@@ -226,48 +226,66 @@ int qw6cu_moe_prefill_rows(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const 
     d.ustride = up->stride;
     d.dstride = down->stride;
     d.x = (const float *)x_bf16;
-    d.out = out;
     d.ntok = nrows;
     d.hidden = hidden;
     d.inter = inter;
     d.ne = n_experts;
     d.topk = 1;
     d.row_expert = row_expert;
-    d.row_weight = row_weight;
+    d.dout = out_bf16;
     d.ws_bytes = qw6k_moe_prefill_ws_bytes(nrows, hidden, inter, n_experts, 1);
     d.ws = qw6h_buf(ctx, QW6H_BUF_WS, d.ws_bytes);
     if (!d.ws) return QW6CU_ERR_NOMEM;
-    rc = qw6h_rc(qw6k_moe_prefill_check(&d, err), "moe_prefill_rows");
-    static const int kid[7] = {QW6H_K_PF_PLAN,  QW6H_K_PF_PLAN,  QW6H_K_PF_PLAN, QW6H_K_PF_PLAN,
-                               QW6H_K_PF_GEMM1, QW6H_K_PF_GEMM2, QW6H_K_PF_PLAN};
-    for (int ph = 1; ph < 7 && !rc; ph++) {
+    rc = qw6h_rc(qw6k_moe_prefill_check(&d, err), "moe_expert_rows");
+    static const int kid[6] = {QW6H_K_PF_PLAN, QW6H_K_PF_PLAN, QW6H_K_PF_PLAN, QW6H_K_PF_PLAN, QW6H_K_PF_GEMM1,
+                               QW6H_K_PF_GEMM2};
+    for (int ph = 1; ph < 6 && !rc; ph++) {
         const int rec = qw6h_prof_a(ctx, kid[ph]);
-        rc = qw6h_rc(qw6k_moe_prefill_phase(&d, err, ph, ctx->st), "moe_prefill_rows");
+        rc = qw6h_rc(qw6k_moe_prefill_phase(&d, err, ph, ctx->st), "moe_expert_rows");
         qw6h_prof_b(ctx, rec);
     }
     return rc;
 }
 
-int qw6cu_ep_count(qw6cu_ctx *ctx, const int32_t *idx, uint32_t nassign, uint32_t world, uint32_t experts_per_rank,
-                   int32_t *dst_count, int32_t *pos) {
+int qw6cu_ep_count(qw6cu_ctx *ctx, const int32_t *idx, uint32_t nassign, uint32_t n_experts, int32_t *expert_count,
+                   int32_t *pos) {
     int rc = qw6h_use(ctx);
     if (rc) return rc;
-    return qw6h_rc(qw6k_ep_count(idx, nassign, world, experts_per_rank, dst_count, pos, ctx->st), "ep_count");
+    const int rec = qw6h_prof_a(ctx, QW6H_K_EP);
+    rc = qw6h_rc(qw6k_ep_count(idx, nassign, n_experts, expert_count, pos, ctx->st), "ep_count");
+    qw6h_prof_b(ctx, rec);
+    return rc;
 }
 
-int qw6cu_ep_pack(qw6cu_ctx *ctx, const int32_t *idx, const float *w, const int32_t *pos, const int32_t *dst_count,
-                  uint32_t nassign, uint32_t top_k, uint32_t world, uint32_t experts_per_rank, const void *x_bf16,
-                  uint32_t hidden, void *send_x, int32_t *send_expert, float *send_weight, int32_t *send_pos) {
+int qw6cu_ep_pack(qw6cu_ctx *ctx, const int32_t *idx, const int32_t *pos, const int32_t *expert_count,
+                  uint32_t nassign, uint32_t top_k, uint32_t n_experts, const void *x_bf16, uint32_t hidden,
+                  void *send_x, int32_t *send_pos) {
     int rc = qw6h_use(ctx);
     if (rc) return rc;
-    return qw6h_rc(qw6k_ep_pack(idx, w, pos, dst_count, nassign, top_k, world, experts_per_rank, x_bf16, hidden, send_x,
-                                send_expert, send_weight, send_pos, ctx->st),
-                   "ep_pack");
+    const int rec = qw6h_prof_a(ctx, QW6H_K_EP);
+    rc = qw6h_rc(qw6k_ep_pack(idx, pos, expert_count, nassign, top_k, n_experts, x_bf16, hidden, send_x, send_pos,
+                              ctx->st),
+                 "ep_pack");
+    qw6h_prof_b(ctx, rec);
+    return rc;
 }
 
-int qw6cu_ep_combine(qw6cu_ctx *ctx, const float *ret, const int32_t *send_pos, uint32_t ntok, uint32_t top_k,
-                     uint32_t hidden, float *out) {
+int qw6cu_ep_expand(qw6cu_ctx *ctx, const int32_t *recv_count, uint32_t world, uint32_t experts_per_rank,
+                    int32_t *row_expert) {
     int rc = qw6h_use(ctx);
     if (rc) return rc;
-    return qw6h_rc(qw6k_ep_combine(ret, send_pos, ntok, top_k, hidden, out, ctx->st), "ep_combine");
+    const int rec = qw6h_prof_a(ctx, QW6H_K_EP);
+    rc = qw6h_rc(qw6k_ep_expand(recv_count, world, experts_per_rank, row_expert, ctx->st), "ep_expand");
+    qw6h_prof_b(ctx, rec);
+    return rc;
+}
+
+int qw6cu_ep_combine(qw6cu_ctx *ctx, const void *ret_bf16, const float *w, const int32_t *send_pos, uint32_t ntok,
+                     uint32_t top_k, uint32_t hidden, float *out) {
+    int rc = qw6h_use(ctx);
+    if (rc) return rc;
+    const int rec = qw6h_prof_a(ctx, QW6H_K_EP);
+    rc = qw6h_rc(qw6k_ep_combine(ret_bf16, w, send_pos, ntok, top_k, hidden, out, ctx->st), "ep_combine");
+    qw6h_prof_b(ctx, rec);
+    return rc;
 }

@@ -1,0 +1,137 @@
+"""Expert-parallel routed MoE for prefill batches.
+
+The experts are sharded contiguously over the ranks of a process group
+(rank r owns experts [r*E/G, (r+1)*E/G)); each rank holds its own tokens.
+One layer (`ep_moe_prefill`):
+
+  1. route this rank's tokens (top-k of their router logits);
+  2. count the assignments of every global expert; one all-to-all gives each
+     rank the counts of its own experts from every source;
+  3. pack each assignment's bf16 token row into send rows sorted by global
+     expert (so grouped by destination, and by local expert inside each
+     destination's block);
+  4. all-to-all the rows to their owners; the owner recovers each received
+     row's expert from the exchanged counts;
+  5. the owner runs the tensor-core grouped GEMMs over the rows it received
+     (unweighted bf16 expert outputs);
+  6. all-to-all the outputs back in send-row order;
+  7. weight and sum each token's top-k outputs in slot order.
+
+Steps 5-7 are the same arithmetic in the same order as the single-GPU
+qw6cu_moe_prefill, so the result does not depend on the number of ranks.
+Compute steps are libqw6cuda kernels (`CudaBackend`); the exchanges are
+torch.distributed all-to-alls (NCCL between GPUs).  The orchestration is
+backend-agnostic so that the same code runs on CPU gloo ranks in the tests.
+Remote rows are always received into this rank's own memory before any
+kernel reads them.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import lib as L
+
+_CUDA_STREAM_LEGACY = 1  # cudaStreamLegacy: torch's default stream reports handle 0
+
+
+class CudaBackend:
+    """libqw6cuda kernels on the current rank's GPU (device tensors), issued
+    on torch's current stream so they order with the collectives."""
+
+    out_dtype = torch.bfloat16
+
+    def __init__(self, ctx: L.Context, gate: L.ExpertPack, up: L.ExpertPack, down: L.ExpertPack, hidden: int,
+                 inter: int, experts_per_rank: int):
+        self.ctx, self.gate, self.up, self.down = ctx, gate, up, down
+        self.hidden, self.inter, self.epr = hidden, inter, experts_per_rank
+        self.device = torch.device("cuda", torch.cuda.current_device())
+
+    def _bind(self):
+        self.ctx.set_stream(torch.cuda.current_stream(self.device).cuda_stream or _CUDA_STREAM_LEGACY)
+        return self.ctx
+
+    def empty(self, shape, dtype):
+        return torch.empty(shape, dtype=dtype, device=self.device)
+
+    def route(self, logits, ntok, n_experts, top_k):
+        idx = self.empty((ntok * top_k,), torch.int32)
+        w = self.empty((ntok * top_k,), torch.float32)
+        self._bind().moe_route(logits.data_ptr(), ntok, n_experts, top_k, idx.data_ptr(), w.data_ptr())
+        return idx, w
+
+    def count(self, idx, n, n_experts):
+        cnt = self.empty((n_experts,), torch.int32)
+        pos = self.empty((n,), torch.int32)
+        self._bind().ep_count(idx.data_ptr(), n, n_experts, cnt.data_ptr(), pos.data_ptr())
+        return cnt, pos
+
+    def pack(self, idx, pos, cnt, n, top_k, n_experts, x):
+        send_x = self.empty((n, self.hidden), torch.bfloat16)
+        send_pos = self.empty((n,), torch.int32)
+        self._bind().ep_pack(idx.data_ptr(), pos.data_ptr(), cnt.data_ptr(), n, top_k, n_experts, x.data_ptr(),
+                             self.hidden, send_x.data_ptr(), send_pos.data_ptr())
+        return send_x, send_pos
+
+    def expand(self, recv_cnt, world, nrecv):
+        row_e = self.empty((max(nrecv, 1),), torch.int32)
+        self._bind().ep_expand(recv_cnt.data_ptr(), world, self.epr, row_e.data_ptr())
+        return row_e
+
+    def expert_rows(self, recv_x, row_e, nrecv):
+        out = self.empty((nrecv, self.hidden), torch.bfloat16)
+        if nrecv:
+            self._bind().moe_expert_rows(self.gate, self.up, self.down, recv_x.data_ptr(), row_e.data_ptr(),
+                                         out.data_ptr(), nrecv, self.hidden, self.inter, self.epr)
+        return out
+
+    def combine(self, ret, w, send_pos, ntok, top_k):
+        out = self.empty((ntok, self.hidden), torch.float32)
+        self._bind().ep_combine(ret.data_ptr(), w.data_ptr(), send_pos.data_ptr(), ntok, top_k, self.hidden,
+                                out.data_ptr())
+        return out
+
+    def local_layer(self, logits, x, ntok, n_experts, top_k):
+        """All experts on this GPU: the single-GPU qw6cu_moe_prefill."""
+        out = self.empty((ntok, self.hidden), torch.float32)
+        self._bind().moe_prefill(self.gate, self.up, self.down, logits.data_ptr(), x.data_ptr(), out.data_ptr(), ntok,
+                                 self.hidden, self.inter, n_experts, top_k)
+        return out
+
+
+def ep_moe_prefill(backend, logits: torch.Tensor, x_bf16: torch.Tensor, top_k: int, n_experts: int,
+                   group=None, stats: dict | None = None) -> torch.Tensor:
+    """One routed-MoE layer for this rank's tokens with experts sharded over
+    `group`.  logits [T x n_experts] fp32, x_bf16 [T x hidden] bf16 (this
+    rank's tokens); returns out [T x hidden] fp32.  Without a process group
+    (or with one rank) the backend holds all experts and runs the layer
+    locally.  `stats`, when given, receives the number of rows this rank's
+    experts processed ("rows")."""
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    ntok, hidden = x_bf16.shape
+    n = ntok * top_k
+    if n_experts % world or n_experts > 256:
+        raise ValueError(f"{n_experts} experts do not shard evenly over {world} ranks")
+    if world == 1 and hasattr(backend, "local_layer"):
+        if stats is not None:
+            stats["rows"] = n
+        return backend.local_layer(logits, x_bf16, ntok, n_experts, top_k)
+    epr = n_experts // world
+    idx, w = backend.route(logits, ntok, n_experts, top_k)
+    cnt, pos = backend.count(idx, n, n_experts)
+    recv_cnt = torch.empty_like(cnt)  # [source][local expert]
+    dist.all_to_all_single(recv_cnt, cnt, group=group)
+    counts = torch.cat([cnt, recv_cnt]).cpu()  # split sizes are host-side lists
+    send_counts = counts[:n_experts].view(world, epr).sum(1).tolist()
+    recv_counts = counts[n_experts:].view(world, epr).sum(1).tolist()
+    nrecv = sum(recv_counts)
+    if stats is not None:
+        stats["rows"] = nrecv
+    send_x, send_pos = backend.pack(idx, pos, cnt, n, top_k, n_experts, x_bf16)
+    recv_x = backend.empty((nrecv, hidden), x_bf16.dtype)
+    dist.all_to_all_single(recv_x, send_x, recv_counts, send_counts, group=group)
+    row_e = backend.expand(recv_cnt, world, nrecv)
+    recv_out = backend.expert_rows(recv_x, row_e, nrecv)
+    ret = backend.empty((n, hidden), recv_out.dtype)
+    dist.all_to_all_single(ret, recv_out, send_counts, recv_counts, group=group)
+    return backend.combine(ret, w, send_pos, ntok, top_k)

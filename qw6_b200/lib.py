@@ -104,10 +104,11 @@ def load() -> C.CDLL:
     lib.qw6cu_moe_decode_hostio.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32]
     lib.qw6cu_moe_decode_noalloc.argtypes = [pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp]
     lib.qw6cu_moe_prefill.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32]
-    lib.qw6cu_moe_prefill_rows.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32]
-    lib.qw6cu_ep_count.argtypes = [_vp, _vp, _u32, _u32, _u32, _vp, _vp]
-    lib.qw6cu_ep_pack.argtypes = [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _vp, _u32, _vp, _vp, _vp, _vp]
-    lib.qw6cu_ep_combine.argtypes = [_vp, _vp, _vp, _u32, _u32, _u32, _vp]
+    lib.qw6cu_moe_expert_rows.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32]
+    lib.qw6cu_ep_count.argtypes = [_vp, _vp, _u32, _u32, _vp, _vp]
+    lib.qw6cu_ep_pack.argtypes = [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _vp, _u32, _vp, _vp]
+    lib.qw6cu_ep_expand.argtypes = [_vp, _vp, _u32, _u32, _vp]
+    lib.qw6cu_ep_combine.argtypes = [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _vp]
     lib.qw6cu_moe_prefill_workspace_bytes.argtypes = [_u32, _u32, _u32, _u32, _u32]
     lib.qw6cu_moe_prefill_workspace_bytes.restype = _sz
     lib.qw6cu_gemm_bf16_nt.argtypes = [_vp, _vp, _vp, _vp, _u32, _u32, _u32]
@@ -278,22 +279,23 @@ class Context:
         _check(self.lib.qw6cu_moe_prefill(self.h, C.byref(gate), C.byref(up), C.byref(down), logits, x_bf16, out,
                                           ntok, hidden, inter, n_experts, top_k), "qw6cu_moe_prefill")
 
-    def moe_prefill_rows(self, gate: ExpertPack, up: ExpertPack, down: ExpertPack, x_bf16, row_expert, row_weight,
-                         out, nrows, hidden, inter, n_experts):
-        _check(self.lib.qw6cu_moe_prefill_rows(self.h, C.byref(gate), C.byref(up), C.byref(down), x_bf16, row_expert,
-                                               row_weight, out, nrows, hidden, inter, n_experts),
-               "qw6cu_moe_prefill_rows")
+    def moe_expert_rows(self, gate: ExpertPack, up: ExpertPack, down: ExpertPack, x_bf16, row_expert, out_bf16,
+                        nrows, hidden, inter, n_experts):
+        _check(self.lib.qw6cu_moe_expert_rows(self.h, C.byref(gate), C.byref(up), C.byref(down), x_bf16, row_expert,
+                                              out_bf16, nrows, hidden, inter, n_experts), "qw6cu_moe_expert_rows")
 
-    def ep_count(self, idx, nassign, world, epr, dst_count, pos):
-        _check(self.lib.qw6cu_ep_count(self.h, idx, nassign, world, epr, dst_count, pos), "qw6cu_ep_count")
+    def ep_count(self, idx, nassign, n_experts, expert_count, pos):
+        _check(self.lib.qw6cu_ep_count(self.h, idx, nassign, n_experts, expert_count, pos), "qw6cu_ep_count")
 
-    def ep_pack(self, idx, w, pos, dst_count, nassign, top_k, world, epr, x_bf16, hidden, send_x, send_e, send_w,
-                send_pos):
-        _check(self.lib.qw6cu_ep_pack(self.h, idx, w, pos, dst_count, nassign, top_k, world, epr, x_bf16, hidden,
-                                      send_x, send_e, send_w, send_pos), "qw6cu_ep_pack")
+    def ep_pack(self, idx, pos, expert_count, nassign, top_k, n_experts, x_bf16, hidden, send_x, send_pos):
+        _check(self.lib.qw6cu_ep_pack(self.h, idx, pos, expert_count, nassign, top_k, n_experts, x_bf16, hidden,
+                                      send_x, send_pos), "qw6cu_ep_pack")
 
-    def ep_combine(self, ret, send_pos, ntok, top_k, hidden, out):
-        _check(self.lib.qw6cu_ep_combine(self.h, ret, send_pos, ntok, top_k, hidden, out), "qw6cu_ep_combine")
+    def ep_expand(self, recv_count, world, experts_per_rank, row_expert):
+        _check(self.lib.qw6cu_ep_expand(self.h, recv_count, world, experts_per_rank, row_expert), "qw6cu_ep_expand")
+
+    def ep_combine(self, ret_bf16, w, send_pos, ntok, top_k, hidden, out):
+        _check(self.lib.qw6cu_ep_combine(self.h, ret_bf16, w, send_pos, ntok, top_k, hidden, out), "qw6cu_ep_combine")
 
     def gemm_bf16_nt(self, A, B, D, M, N, K):
         _check(self.lib.qw6cu_gemm_bf16_nt(self.h, A, B, D, M, N, K), "qw6cu_gemm_bf16_nt")
@@ -313,7 +315,7 @@ class Context:
 
     def profile_end(self) -> dict:
         """{kernel name: (total ms, launches)} for the kernels that ran."""
-        n = 13
+        n = 15
         ms = (C.c_double * n)()
         cnt = (C.c_uint32 * n)()
         _check(self.lib.qw6cu_profile_end(self.h, ms, cnt), "qw6cu_profile_end")

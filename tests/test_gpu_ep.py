@@ -1,0 +1,125 @@
+"""GPU: expert-parallel prefill MoE over NCCL.
+
+Each of `world` ranks (one spawned process per GPU) owns E/world experts and
+T/world tokens and runs qw6_b200.ep.ep_moe_prefill with the libqw6cuda
+backend.  The gathered outputs must equal, bit for bit, the single-GPU
+qw6cu_moe_prefill on all tokens (same expert outputs, same slot-order
+combine), and match the CPU oracle's composition on a seeded sample of
+tokens within 2e-2 (the bf16 tensor-core prefill tolerance).  world=1 runs
+on any GPU box; larger worlds are skipped when the box has fewer GPUs."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from qw6_b200 import synth as S
+
+pytestmark = pytest.mark.gpu
+
+E, H, I, K, T = 32, 2048, 512, 8, 512
+
+
+def _data(case):
+    rng = np.random.Generator(np.random.PCG64(909))
+    gate, up, down = S.moe_weights(rng, E, S.Q4_K, S.Q6_K, H, I)
+    bias = (rng.standard_normal(E) * 0.5).astype(np.float32)
+    logits = (rng.standard_normal((T, E), dtype=np.float32) + bias).astype(np.float32)
+    if case == "upper_half_idle":  # no token routes to experts E/2.. (their owners receive nothing)
+        logits[:, E // 2:] = -1e4
+    xbits = S.bf16_round(rng.standard_normal((T, H), dtype=np.float32))
+    return gate, up, down, logits, xbits
+
+
+def _pack_all(ctx, torch, L, mats, lo, hi):
+    packs, held = [], []
+    for qq, m, r, c in mats:
+        mine = np.ascontiguousarray(m[lo:hi])
+        pb = ctx.packed_bytes(qq, r, c)
+        raw = torch.from_numpy(mine.reshape(-1)).cuda()
+        pk = torch.empty(pb * (hi - lo), dtype=torch.uint8, device="cuda")
+        torch.cuda.synchronize()
+        ctx.pack(qq, raw.data_ptr(), pk.data_ptr(), r, c, hi - lo, mine[0].nbytes, pb)
+        ctx.synchronize()
+        held.append(pk)
+        packs.append(L.ExpertPack(qq, pk.data_ptr(), pb))
+    return packs, held
+
+
+def _rank(rank, world, port, case, q):
+    import torch
+    import torch.distributed as dist
+
+    from qw6_b200 import lib as L
+    from qw6_b200.ep import CudaBackend, ep_moe_prefill
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        gate, up, down, logits, xbits = _data(case)
+        mats = ((S.Q4_K, gate, I, H), (S.Q4_K, up, I, H), (S.Q6_K, down, H, I))
+        epr, tpr = E // world, T // world
+        ctx = L.Context(rank)
+        packs, held = _pack_all(ctx, torch, L, mats, rank * epr, (rank + 1) * epr)
+        be = CudaBackend(ctx, packs[0], packs[1], packs[2], H, I, epr)
+        sl = slice(rank * tpr, (rank + 1) * tpr)
+        lg = torch.from_numpy(logits[sl]).cuda()
+        x = torch.from_numpy(xbits[sl].view(np.int16)).cuda().view(torch.bfloat16)
+        torch.cuda.synchronize()
+        out = ep_moe_prefill(be, lg, x, K, E)
+        torch.cuda.synchronize()
+        ctx.check_device_errors()
+        full = None
+        if rank == 0:  # single-GPU reference over all tokens and experts
+            ctx.set_stream(None)
+            fpacks, fheld = _pack_all(ctx, torch, L, mats, 0, E)
+            lga = torch.from_numpy(logits).cuda()
+            xa = torch.from_numpy(xbits.view(np.int16)).cuda()
+            fo = torch.empty((T, H), dtype=torch.float32, device="cuda")
+            torch.cuda.synchronize()
+            ctx.moe_prefill(fpacks[0], fpacks[1], fpacks[2], lga.data_ptr(), xa.data_ptr(), fo.data_ptr(), T, H, I,
+                            E, K)
+            ctx.synchronize()
+            ctx.check_device_errors()
+            full = fo.cpu().numpy()
+        q.put((rank, out.cpu().numpy(), full))
+        ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("case", ["spread", "upper_half_idle"])
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_ep_prefill_nccl(world, case, oracle):
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, world, port, case, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in procs:
+        r, o, f = q.get(timeout=600)
+        got[r] = (o, f)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    out = np.concatenate([got[r][0] for r in range(world)])
+    full = got[0][1]
+    assert np.array_equal(out.view(np.uint32), full.view(np.uint32)), float(np.max(np.abs(out - full)))
+    gate, up, down, logits, xbits = _data(case)
+    toks = np.random.Generator(np.random.PCG64(5)).choice(T, 24, replace=False)
+    ref, _, _ = oracle.moe_layer(S.Q4_K, gate, up, S.Q6_K, down, logits[toks], S.bf16_to_f32(xbits[toks]), top_k=K)
+    errs = [float(np.max(np.abs(out[t] - ref[i])) / np.max(np.abs(ref[i]))) for i, t in enumerate(toks)]
+    assert max(errs) <= 2e-2, max(errs)
