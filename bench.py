@@ -3,22 +3,24 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload: one MoE FFN layer at decode batch 1 --
-hidden 2048, 256 experts, top-8, expert intermediate 512, Q4_K gate/up,
-Q6_K down, router logits fp32[256] ~ N(0,1), x fp32[2048] ~ N(0,1).
-A step is one token through the layer: route -> 8 x (gate, up, silu*up,
-down) -> routing-weighted sum, all on the GPU through libqw6cuda's C ABI.
+Headline workload: one prefill MoE FFN layer
+over 4096 bf16 tokens -- hidden 2048, 256 experts, top-8, expert
+intermediate 512, Q4_K gate/up, Q6_K down, router logits fp32 ~ N(0,1) plus
+a per-expert bias ~ N(0,0.5).  At N GPUs the experts are sharded 256/N per
+GPU and the tokens 4096/N per GPU (strong scaling: the job is always the
+same 4096 tokens); a step is route -> NCCL all-to-all dispatch of token
+rows -> tcgen05 grouped GEMMs on each owner -> all-to-all of the expert
+outputs back -> slot-order combine (qw6_b200.ep.ep_moe_prefill).  N resident
+copies of each GPU's expert shard (~522 MB per GPU, > 4x L2) are used round
+robin, one per step.
 
-Inputs larger than L2: 16 copies of the layer (16 x 522 MB of expert
-weights) are resident and step s uses layer s % 16 with its own logits and
-x, so an expert's weights are re-touched only after >= 256 MB of other
-traffic (L2 is 126 MB).  Steps run as a CUDA graph replayed back to back.
-
-Printed JSON line (rank 0): metric "MoE-layer tokens/s", value = whole-job
-tokens/s (N replicas at N GPUs, weak scaling), the dominant kernel's HBM
-roofline, an end-to-end number through the host-buffer C entry point
-(qw6cu_moe_decode_hostio), the CPU baseline (qw6's own CPU code), clocks
-sampled during the timed region, and per-format matvec HBM throughput.
+Printed JSON line (rank 0): metric "MoE-layer tokens/s" (whole job), the
+dominant kernel's tensor-core roofline, an end-to-end number with the
+step's logits/x copied from pinned host memory and the output read back
+every step, the CPU baseline (qw6's own CPU code on a sample of the same
+tokens), clocks sampled during the timed region, and sub-results: decode
+(config 1, batch 1, CUDA graph, HBM roofline), the per-format matvec sweep
+and the row-sharded LM head (config 4).
 
 --impl reference times qw6's own CPU implementation (oracle/_ref, built from
 the reference sources) of the same layer on the host cores.
@@ -167,6 +169,25 @@ def build_layers(torch, ctx, L, n_layers):
     return (gate, up, down), packs, layers
 
 
+def timed(torch, stream, dist, fn, nsteps):
+    """Device time of nsteps calls of fn on `stream`, bracketed by barrier +
+    synchronize, max over ranks (ms)."""
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for s in range(nsteps):
+            fn(s)
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([ev0.elapsed_time(ev1)], device="cuda", dtype=torch.float64)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def run_ours(args, rank, local_rank, world):
     import torch
 
@@ -183,10 +204,146 @@ def run_ours(args, rank, local_rank, world):
     stream = torch.cuda.Stream()
     ctx = L.Context(local_rank)
     ctx.set_stream(stream.cuda_stream)
-    raw, packs, layers = build_layers(torch, ctx, L, args.layers)
-    nl = args.layers
+    head = ep_bench(args, torch, ctx, L, stream, rank, world, dist)
+    dec = decode_bench(args, torch, ctx, L, stream, rank, world, dist) if args.decode else None
+    matvec = matvec_sweep(torch, ctx, stream) if (rank == 0 and args.matvec) else None
+    lmh = lm_head_bench(torch, ctx, stream, rank, world, dist) if args.lm_head else None
+    result = None
+    if rank == 0:
+        result = report(args, world, head)
+        result["decode"] = dec
+        result["matvec"] = matvec
+        result["lm_head"] = lmh
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    ctx.close()
+    return result
+
+
+PF_FLOPS_ROW = {"pf_gemm1": 2 * 2 * INTER * HIDDEN, "pf_gemm2": 2 * HIDDEN * INTER}  # per routed row
+T3 = 4096
+
+
+def ep_bench(args, torch, ctx, L, stream, rank, world, dist):
+    """Config 3 with the experts sharded over the ranks.  N=1: the
+    single-GPU layer (qw6cu_moe_prefill); N>1: the peer-memory expert-parallel
+    layer (qw6_b200.ep.PeerMoE: dispatch/combine kernels over NVLink, no
+    host round trip).  Timed steps are replayed from CUDA graphs; one eager
+    step is profiled per kernel; the end-to-end leg copies each step's
+    inputs from pinned host memory and reads the output back."""
+    from qw6_b200 import synth as S
+    from qw6_b200.ep import PeerMoE
+    gate, up, down, logits, xbits = S.config3()
+    epr, tpr = NE // world, T3 // world
+    lo = rank * epr
+    ncopies = world  # world copies of a 256/world-expert shard: ~522 MB resident per GPU
+    copies = []
+    for q, m, r, c in ((S.Q4_K, gate, INTER, HIDDEN), (S.Q4_K, up, INTER, HIDDEN), (S.Q6_K, down, HIDDEN, INTER)):
+        mine = np.ascontiguousarray(m[lo:lo + epr])
+        pb = ctx.packed_bytes(q, r, c)
+        raw = torch.from_numpy(mine.reshape(-1)).cuda()
+        pk = torch.empty(pb * epr, dtype=torch.uint8, device="cuda")
+        torch.cuda.synchronize()
+        ctx.pack(q, raw.data_ptr(), pk.data_ptr(), r, c, epr, mine[0].nbytes, pb)
+        ctx.synchronize()
+        del raw
+        copies.append((q, pb, [pk] + [pk.clone() for _ in range(ncopies - 1)]))
+    packs = [tuple(L.ExpertPack(q, cp[i].data_ptr(), pb) for q, pb, cp in copies) for i in range(ncopies)]
+    sl = slice(rank * tpr, (rank + 1) * tpr)
+    lg = torch.from_numpy(logits[sl]).cuda()
+    x = torch.from_numpy(xbits[sl].view(np.int16)).cuda()
+    out = torch.empty((tpr, HIDDEN), dtype=torch.float32, device="cuda")
+    pm = PeerMoE(ctx, *packs[0], NE, TOPK, HIDDEN, INTER, tpr) if world > 1 else None
+    torch.cuda.synchronize()
+
+    def step(s, lgt=lg, xt=x, o=out):
+        pk = packs[s % ncopies]
+        if pm is not None:
+            pm(lgt, xt, o, packs=pk)
+        else:
+            ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+            ctx.moe_prefill(*pk, lgt.data_ptr(), xt.data_ptr(), o.data_ptr(), tpr, HIDDEN, INTER, NE, TOPK)
 
     K, W = args.steps, args.warmup
+    with torch.cuda.stream(stream):
+        for s in range(W):
+            step(s)
+    torch.cuda.synchronize()
+    ctx.check_device_errors()
+
+    G = max(1, min(K, 2 * ncopies if ncopies > 1 else 8))
+
+    def capture(n):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for s in range(n):
+                step(s)
+        return g
+
+    full = capture(G)
+    tail = capture(K % G) if K % G else None
+    with torch.cuda.stream(stream):
+        full.replay()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local_rank_of(rank)) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    reps = K // G
+    ms = timed(torch, stream, dist, lambda i: (full if i < reps else tail).replay(), reps + (1 if tail else 0))
+    clk = clocks.stop() if clocks else None
+    ctx.check_device_errors()
+    del full, tail
+
+    # one profiled eager step: per-kernel device time and launch count
+    with torch.cuda.stream(stream):
+        ctx.profile_begin(64)
+        step(0)
+        prof = ctx.profile_end()
+    rows = pm.last_rows() if pm is not None else tpr * TOPK
+
+    # end to end: this step's logits/x from pinned host memory, output read back
+    h_lg = torch.from_numpy(logits[sl]).pin_memory()
+    h_x = torch.from_numpy(xbits[sl].view(np.int16)).pin_memory()
+    h_out = torch.empty((tpr, HIDDEN), dtype=torch.float32).pin_memory()
+    d_lg, d_x, d_out = torch.empty_like(lg), torch.empty_like(x), torch.empty_like(out)
+
+    def e2e_step(s):
+        d_lg.copy_(h_lg, non_blocking=True)
+        d_x.copy_(h_x, non_blocking=True)
+        step(s, d_lg, d_x, d_out)
+        h_out.copy_(d_out, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    with torch.cuda.stream(stream):
+        for s in range(3):
+            e2e_step(s)
+    ke = max(1, min(K, 100))
+    e2e_ms = timed(torch, stream, dist, e2e_step, ke)
+    ctx.check_device_errors()
+    out_ok = bool(np.isfinite(h_out.numpy()).all())
+    if pm is not None:
+        if dist:
+            dist.barrier()
+        pm.close()
+    del packs, copies
+    torch.cuda.empty_cache()
+    return {"ms": ms, "clk": clk, "prof": prof, "rows": rows, "e2e_ms": e2e_ms, "e2e_steps": ke, "graph_steps": G,
+            "h2d": tpr * NE * 4 + tpr * HIDDEN * 2, "d2h": tpr * HIDDEN * 4, "finite": out_ok,
+            "cpu_data": (gate, up, down, logits[:16], S.bf16_to_f32(xbits[:16]))}
+
+
+def local_rank_of(rank):
+    return int(os.environ.get("LOCAL_RANK", rank))
+
+
+def decode_bench(args, torch, ctx, L, stream, rank, world, dist):
+    """Config 1 (decode batch 1) as N replicas: a CUDA graph of 256 steps
+    replayed back to back over 16 resident layer copies; HBM roofline of
+    the dominant kernel; end to end through qw6cu_moe_decode_hostio."""
+    raw, packs, layers = build_layers(torch, ctx, L, args.layers)
+    nl = args.layers
+    K = args.decode_steps
     nslots = GRAPH_STEPS
     gen = torch.Generator(device="cuda").manual_seed(1000 + rank)
     logits = torch.randn((nslots, NE), generator=gen, device="cuda", dtype=torch.float32)
@@ -200,9 +357,8 @@ def run_ours(args, rank, local_rank, world):
         ctx.moe_decode(g, u, d, logits[j].data_ptr(), xs[j].data_ptr(), outs[j].data_ptr(), 1, HIDDEN, INTER, NE,
                        TOPK)
 
-    # warm-up (eager): allocates the workspace, sets kernel attributes
     with torch.cuda.stream(stream):
-        for s in range(max(W, 1)):
+        for s in range(max(args.warmup, 1)):
             step(s)
     ctx.synchronize()
 
@@ -216,40 +372,12 @@ def run_ours(args, rank, local_rank, world):
         return g
 
     full = capture(GRAPH_STEPS, False)
-    tail_n = K % GRAPH_STEPS
-    tail = capture(tail_n, False) if tail_n else None
-    reps = K // GRAPH_STEPS
-
-    def timed_region():
-        for _ in range(reps):
-            full.replay()
-        if tail is not None:
-            tail.replay()
-
-    # warm replays, then the timed region bracketed by barrier + sync
+    reps = max(1, K // GRAPH_STEPS)
+    K = reps * GRAPH_STEPS
     with torch.cuda.stream(stream):
         full.replay()
     torch.cuda.synchronize()
-    clocks = ClockSampler(local_rank) if rank == 0 else None
-    if clocks:
-        clocks.start()
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        ev0.record(stream)
-        timed_region()
-        ev1.record(stream)
-    torch.cuda.synchronize()
-    ms = ev0.elapsed_time(ev1)
-    clk = clocks.stop() if clocks else None
-    t = torch.tensor([ms], device="cuda", dtype=torch.float64)
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
-
-    # per-kernel durations from a separately captured, profiled graph
+    ms = timed(torch, stream, dist, lambda s: full.replay(), reps)
     pg = capture(GRAPH_STEPS, True)
     with torch.cuda.stream(stream):
         pg.replay()
@@ -257,43 +385,58 @@ def run_ours(args, rank, local_rank, world):
     with torch.cuda.stream(stream):
         pg.replay()
     prof = ctx.profile_end()
-    del pg, full, tail
+    del pg, full
 
-    # end-to-end through the host-buffer entry point (pinned host memory)
     e2e_steps = min(K, 2048)
     h_logits = torch.randn((64, NE), dtype=torch.float32).pin_memory()
     h_x = torch.randn((64, HIDDEN), dtype=torch.float32).pin_memory()
     h_out = torch.empty((64, HIDDEN), dtype=torch.float32).pin_memory()
-    for s in range(8):
+
+    def hostio(s):
         g, u, d = layers[s % nl]
         ctx.moe_decode_hostio(g, u, d, h_logits[s % 64].data_ptr(), h_x[s % 64].data_ptr(),
                               h_out[s % 64].data_ptr(), 1, HIDDEN, INTER, NE, TOPK)
+
+    for s in range(8):
+        hostio(s)
     if dist:
         dist.barrier()
     t0 = time.perf_counter()
     for s in range(e2e_steps):
-        g, u, d = layers[s % nl]
-        ctx.moe_decode_hostio(g, u, d, h_logits[s % 64].data_ptr(), h_x[s % 64].data_ptr(),
-                              h_out[s % 64].data_ptr(), 1, HIDDEN, INTER, NE, TOPK)
-    e2e_s = time.perf_counter() - t0
-    te = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
+        hostio(s)
+    te = torch.tensor([time.perf_counter() - t0], device="cuda", dtype=torch.float64)
     if dist:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_s = float(te.item())
+    del layers, packs
+    torch.cuda.empty_cache()
 
-    matvec = matvec_sweep(torch, ctx, stream) if (rank == 0 and args.matvec) else None
-    lmh = lm_head_bench(torch, ctx, stream, rank, world, dist) if args.lm_head else None
-    pf = prefill_bench(torch, ctx, stream, L, args.prefill_steps) if (rank == 0 and args.prefill) else None
-    result = None
-    if rank == 0:
-        result = report(args, world, ms_max, prof, clk, e2e_steps, e2e_s, matvec, raw)
-        result["lm_head"] = lmh
-        result["prefill"] = pf
-    if dist:
-        dist.barrier()
-        dist.destroy_process_group()
-    ctx.close()
-    return result
+    hbm, peak_kind = peaks()
+    per_launch = {
+        "moe_gateup": TOPK * 2 * Q4K_BYTES_EXPERT + HIDDEN * 4 + TOPK * INTER * 4,
+        "moe_down": TOPK * Q6K_BYTES_EXPERT + TOPK * INTER * 4 + HIDDEN * 4,  # down + fused combine
+    }
+    dom = max((k for k in prof if k in per_launch), key=lambda k: prof[k][0])
+    dom_ms = prof[dom][0] / prof[dom][1]
+    achieved = per_launch[dom] / (dom_ms / 1e3) / 1e9
+    step_bytes = WEIGHT_BYTES_TOKEN + HIDDEN * 4 * 2 + NE * 4
+    tokens = K * world
+    return {
+        "workload": "config 1: MoE FFN layer, decode batch 1 (N independent replicas)",
+        "tokens_s": round(tokens / (ms / 1e3), 1), "ms_per_step": round(ms / K, 5), "steps": K,
+        "hbm_gbs_step": round(step_bytes * K / (ms / 1e3) / 1e9, 1),
+        "l2": f"inputs larger than L2: {nl} resident layer copies "
+              f"({nl * NE * (2 * Q4K_BYTES_EXPERT + Q6K_BYTES_EXPERT) / 1e9:.1f} GB), step s uses layer s % {nl}",
+        "graph": f"CUDA graph of {GRAPH_STEPS} steps replayed",
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 3), "peak_kind": peak_kind,
+                     "traffic": traffic_from_profiles(dom), "algorithmic_bytes_per_launch": per_launch[dom]},
+        "kernels": {k: {"avg_us": round(v[0] / v[1] * 1e3, 2), "launches_profiled": v[1]} for k, v in prof.items()},
+        "e2e": {"value": round(e2e_steps * world / e2e_s, 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": (NE + HIDDEN) * 4, "d2h_bytes_per_step": HIDDEN * 4,
+                "api": "qw6cu_moe_decode_hostio (pinned host logits/x/out, synchronous per step)"},
+        "gpu_launches_per_step": sum(c for _, c in prof.values()) // GRAPH_STEPS,
+    }
 
 
 def matvec_sweep(torch, ctx, stream):
@@ -346,57 +489,6 @@ def matvec_sweep(torch, ctx, stream):
             lat.append(e0.elapsed_time(e1) * 1e3)
     out["c0_q4k_512x2048_latency_us"] = round(float(np.median(lat)), 2)
     return out
-
-
-PREFILL_FLOPS = 2 * 4096 * TOPK * (2 * INTER * HIDDEN + HIDDEN * INTER) * 2 // 2  # 2 FLOP per MAC
-
-
-def prefill_bench(torch, ctx, stream, L, steps):
-    """Config 3 on one GPU: 4096 bf16 tokens through the 256-expert layer
-    (Q4_K gate/up, Q6_K down) with the tcgen05 grouped GEMMs; tokens/s and
-    dense bf16 TFLOP/s (206.2 GFLOP per step) against the measured peak."""
-    from qw6_b200 import synth as S
-    gate, up, down, logits, xbits = S.config3()
-    packs, held = [], []
-    for q, m, r, c in ((S.Q4_K, gate, INTER, HIDDEN), (S.Q4_K, up, INTER, HIDDEN), (S.Q6_K, down, HIDDEN, INTER)):
-        pb = ctx.packed_bytes(q, r, c)
-        raw = torch.from_numpy(m.reshape(-1)).cuda()
-        pk = torch.empty(pb * NE, dtype=torch.uint8, device="cuda")
-        torch.cuda.synchronize()
-        ctx.pack(q, raw.data_ptr(), pk.data_ptr(), r, c, NE, m[0].nbytes, pb)
-        ctx.synchronize()
-        held.append(pk)
-        packs.append(L.ExpertPack(q, pk.data_ptr(), pb))
-    lg = torch.from_numpy(logits).cuda()
-    x = torch.from_numpy(xbits.view(np.int16)).cuda()
-    out = torch.empty((4096, HIDDEN), device="cuda")
-    torch.cuda.synchronize()
-
-    def one():
-        ctx.moe_prefill(packs[0], packs[1], packs[2], lg.data_ptr(), x.data_ptr(), out.data_ptr(), 4096, HIDDEN,
-                        INTER, NE, TOPK)
-
-    for _ in range(3):
-        one()
-    ctx.check_device_errors()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(steps):
-        one()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / steps
-    ctx.profile_begin(8 * 6)
-    one()
-    prof = ctx.profile_end()
-    ctx.check_device_errors()
-    pk_bf16 = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"] if (
-        ROOT / "MEASURED_PEAKS.json").exists() else 1590.0
-    tflops = PREFILL_FLOPS / (ms / 1e3) / 1e12
-    return {"workload": "config 3: 4096 tokens, 256 experts, top-8, bias N(0,0.5), 1 GPU",
-            "steps": steps, "ms_per_step": round(ms, 4), "tokens_s": round(4096 / (ms / 1e3), 1),
-            "tflops": round(tflops, 1), "frac_bf16_peak": round(tflops / pk_bf16, 3),
-            "kernels": {k: {"avg_us": round(v[0] / v[1] * 1e3, 2), "launches": v[1]} for k, v in prof.items()}}
 
 
 def lm_head_bench(torch, ctx, stream, rank, world, dist):
@@ -467,61 +559,64 @@ def traffic_from_profiles(kernel: str):
     return None
 
 
-def report(args, world, ms_max, prof, clk, e2e_steps, e2e_s, matvec, raw):
-    hbm, peak_kind = peaks()
-    K = args.steps
-    tokens = K * world
-    value = tokens / (ms_max / 1e3)
-    # roofline of the dominant kernel (largest total time)
-    per_launch = {
-        "moe_gateup": TOPK * 2 * Q4K_BYTES_EXPERT + HIDDEN * 4 + TOPK * INTER * 4,
-        "moe_down": TOPK * Q6K_BYTES_EXPERT + TOPK * INTER * 4 + HIDDEN * 4,  # down + fused combine
-    }
-    dom = max((k for k in prof if k in per_launch), key=lambda k: prof[k][0])
-    dom_ms = prof[dom][0] / prof[dom][1]
-    achieved = per_launch[dom] / (dom_ms / 1e3) / 1e9
-    traffic = traffic_from_profiles(dom)
-    step_bytes = WEIGHT_BYTES_TOKEN + HIDDEN * 4 * 2 + NE * 4
-    launches = sum(c for _, c in prof.values()) // GRAPH_STEPS * K
-    kernels = {k: {"avg_us": round(v[0] / v[1] * 1e3, 2), "launches_profiled": v[1]} for k, v in prof.items()}
+def bf16_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["bf16_tflops"]), "measured (burst)"
+    return 1590.0, "fallback (burst)"
 
+
+def report(args, world, head):
+    hbm, hbm_kind = peaks()
+    tflops_peak, tf_kind = bf16_peak()
+    K = args.steps
+    ms = head["ms"]
+    value = T3 * K / (ms / 1e3)
+    prof, rows = head["prof"], head["rows"]
+    dom = max((k for k in prof if k in PF_FLOPS_ROW), key=lambda k: prof[k][0])
+    dom_ms = prof[dom][0] / prof[dom][1]
+    flops = rows * PF_FLOPS_ROW[dom]
+    achieved = flops / (dom_ms / 1e3) / 1e12
+    launches = sum(c for _, c in prof.values())
+    shard_weight_bytes = NE // world * (2 * Q4K_BYTES_EXPERT + Q6K_BYTES_EXPERT)
     cpu = None
-    if args.cpu_baseline:
-        gate, up, down = raw
-        from qw6_b200 import synth as S
-        _, _, _, lg, x = S.config1()
-        rng = np.random.Generator(np.random.PCG64(77))
-        lgs = np.concatenate([lg, rng.standard_normal((15, NE), dtype=np.float32)])
-        xs = np.concatenate([x, rng.standard_normal((15, HIDDEN), dtype=np.float32)])
-        rate, units, dt = cpu_reference_rate(gate, up, down, lgs, xs, budget_s=12.0, threads=1)
+    if args.cpu_baseline and world == 1:
+        gate, up, down, lg, x = head["cpu_data"]
+        rate, units, dt = cpu_reference_rate(gate, up, down, lg, x, budget_s=12.0, threads=1)
         cpu = {"value": round(rate, 3), "unit": "tokens/s", "cores": 1, "kind": "reference",
-               "sample": f"{units} (token, expert) units = {units / TOPK:.1f} tokens of config 1 through qw6's own "
+               "sample": f"{units} (token, expert) units = {units / TOPK:.1f} of config 3's tokens through qw6's own "
                          f"qw6_cpu_moe_route / qw6_tensor_matvec / qw6_silu (oracle/_ref), 1 thread, {dt:.1f} s"}
-    line = {
+    return {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": K,
-        "warmup": args.warmup, "ms_per_step": round(ms_max / K, 5), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "s8 mma (int32 acc) + f32", "data": "synthetic (seeded GGUF blocks, config 1)",
-        "config": {"workload": "config 1: MoE FFN layer, decode batch 1", "hidden": HIDDEN, "experts": NE,
-                   "top_k": TOPK, "inter": INTER, "gate_up": "Q4_K", "down": "Q6_K",
-                   "parallelism": "replicas" if world > 1 else "1 GPU",
-                   "l2": f"inputs larger than L2: {args.layers} resident layer copies "
-                         f"({args.layers * NE * (2 * Q4K_BYTES_EXPERT + Q6K_BYTES_EXPERT) / 1e9:.1f} GB), "
-                         f"step s uses layer s % {args.layers}",
-                   "graph": f"CUDA graph of {GRAPH_STEPS} steps replayed"},
-        "hbm_gbs_step": round(step_bytes * tokens / (ms_max / 1e3) / 1e9 / world, 1),
-        "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(achieved / hbm, 3), "peak_kind": peak_kind, "traffic": traffic,
-                     "algorithmic_bytes_per_launch": per_launch[dom]},
-        "kernels": kernels,
-        "e2e": {"value": round(e2e_steps * world / e2e_s, 1), "unit": "tokens/s",
-                "h2d_bytes_per_step": (NE + HIDDEN) * 4, "d2h_bytes_per_step": HIDDEN * 4,
-                "api": "qw6cu_moe_decode_hostio (pinned host logits/x/out, synchronous per step)"},
-        "gpu_launches": int(launches),
-        "clocks": clk,
+        "warmup": args.warmup, "ms_per_step": round(ms / K, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16 (tcgen05 kind::f16, f32 accumulate; Q4_K/Q6_K weights)",
+        "data": "synthetic (seeded GGUF blocks, config 3)",
+        "config": {"workload": "config 3: prefill MoE FFN layer, 4096 tokens", "tokens": T3, "hidden": HIDDEN,
+                   "experts": NE, "top_k": TOPK, "inter": INTER, "gate_up": "Q4_K", "down": "Q6_K",
+                   "router_bias": "N(0,0.5) per expert",
+                   "parallelism": f"ep{world}: {NE // world} experts and {T3 // world} tokens per GPU"
+                                  + (", dispatch/combine by this library's kernels over NVLink peer memory"
+                                     if world > 1 else ""),
+                   "graph": f"CUDA graphs of {head['graph_steps']} steps replayed",
+                   "l2": f"inputs larger than L2: {world} resident copies of each GPU's expert shard "
+                         f"({world * shard_weight_bytes / 1e6:.0f} MB per GPU), step s uses copy s % {world}"},
+        "roofline": {"bound": "tensor", "kernel": dom, "achieved": round(achieved, 1), "peak": tflops_peak,
+                     "unit": "TFLOP/s", "frac": round(achieved / tflops_peak, 3), "peak_kind": tf_kind,
+                     "traffic": traffic_from_profiles(dom) if world == 1 else None,
+                     "algorithmic_flops_per_launch": flops, "rows_rank0": rows},
+        "hbm": {"weight_bytes_per_step": shard_weight_bytes, "gbs": round(shard_weight_bytes * K / (ms / 1e3) / 1e9, 1),
+                "frac": round(shard_weight_bytes * K / (ms / 1e3) / 1e9 / hbm, 4), "peak": hbm, "peak_kind": hbm_kind},
+        "kernels": {k: {"avg_us": round(v[0] / v[1] * 1e3, 2), "launches_per_step": v[1]} for k, v in prof.items()},
+        "e2e": {"value": round(T3 * head["e2e_steps"] / (head["e2e_ms"] / 1e3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": head["h2d"], "d2h_bytes_per_step": head["d2h"],
+                "api": ("qw6_b200.ep.PeerMoE" if world > 1 else "qw6cu_moe_prefill")
+                       + " with this rank's logits/x copied from pinned host memory and the fp32 output copied "
+                         "back and synchronized every step (per-rank bytes)",
+                "output_finite": head["finite"]},
+        "gpu_launches": int(launches * K),
+        "clocks": head["clk"],
         "cpu_baseline": cpu,
-        "matvec": matvec,
     }
-    return line
 
 
 # --------------------------------------------------------- reference arm --
@@ -530,10 +625,8 @@ def run_reference(args, rank, world):
     if rank != 0:
         return None
     from qw6_b200 import synth as S
-    gate, up, down, lg, x = S.config1()
-    rng = np.random.Generator(np.random.PCG64(77))
-    lgs = np.concatenate([lg, rng.standard_normal((63, NE), dtype=np.float32)])
-    xs = np.concatenate([x, rng.standard_normal((63, HIDDEN), dtype=np.float32)])
+    gate, up, down, lg, xb = S.config3()
+    lgs, xs = lg[:256], S.bf16_to_f32(xb[:256])
     from oracle.oracle import Reference, cpu_count
     threads = cpu_count()
     # each step: `threads` (token, expert) units in parallel; bound the run to a few minutes
@@ -571,15 +664,18 @@ def run_reference(args, rank, world):
     value = K * per_step / TOPK / dt
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "tokens/s", "n_gpus": world, "steps": K,
-        "warmup": W, "ms_per_step": round(dt / K * 1e3, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded GGUF blocks, config 1)",
-        "config": {"workload": "config 1: MoE FFN layer, decode batch 1", "hidden": HIDDEN, "experts": NE,
-                   "top_k": TOPK, "inter": INTER, "gate_up": "Q4_K", "down": "Q6_K"},
+        "warmup": W, "ms_per_step": round(dt / K * 1e3, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded GGUF blocks, config 3)",
+        "config": {"workload": "config 3: prefill MoE FFN layer, 4096 tokens", "tokens": T3, "hidden": HIDDEN,
+                   "experts": NE, "top_k": TOPK, "inter": INTER, "gate_up": "Q4_K", "down": "Q6_K",
+                   "router_bias": "N(0,0.5) per expert"},
         "impl": "reference",
         "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads, "kind": "reference",
-                         "sample": f"{per_step} (token, expert) units per step on {threads} threads through "
-                                   "qw6's own CPU code (oracle/_ref: qw6_cpu_moe_route, qw6_tensor_matvec, "
-                                   "qw6_silu); the reference's Vulkan path is unavailable on this box"},
+                         "sample": f"{per_step} (token, expert) units per step of config 3's first 256 tokens on "
+                                   f"{threads} threads through qw6's own CPU code (oracle/_ref: qw6_cpu_moe_route, "
+                                   "qw6_tensor_matvec, qw6_silu; the reference has no batched path, so tokens are "
+                                   "looped as qw6_prefill does); the reference's Vulkan path is unavailable on "
+                                   "this box"},
         "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     return line
@@ -588,16 +684,16 @@ def run_reference(args, rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=8192)
-    ap.add_argument("--warmup", type=int, default=16)
+    ap.add_argument("--steps", type=int, default=500)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="resident layer copies (16 keeps the working set >> L2; fewer for profiling)")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--no-matvec", dest="matvec", action="store_false")
     ap.add_argument("--no-lm-head", dest="lm_head", action="store_false")
-    ap.add_argument("--no-prefill", dest="prefill", action="store_false")
-    ap.add_argument("--prefill-steps", type=int, default=20)
+    ap.add_argument("--no-decode", dest="decode", action="store_false")
+    ap.add_argument("--decode-steps", type=int, default=8192)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -234,6 +234,41 @@ int qw6cu_ep_expand(qw6cu_ctx *ctx, const int32_t *recv_count, uint32_t world, u
 int qw6cu_ep_combine(qw6cu_ctx *ctx, const void *ret_bf16, const float *w, const int32_t *send_pos, uint32_t ntok,
                      uint32_t top_k, uint32_t hidden, float *out);
 
+/* ---- expert parallelism over peer memory (prefill) ----
+ * The same layer with no host round trip: one qw6cu_ep per rank (one
+ * process per GPU) owns a symmetric device region that the other ranks map
+ * through CUDA IPC.  Counts, token rows and expert outputs move through
+ * peer memory (NVLink), ordered by epoch-stamped signal words; every wait
+ * gives up after 2 s, records a timeout in the context's error word
+ * (qw6cu_check_device_errors) and turns the rest of the layer into no-ops.
+ * Setup: qw6cu_ep_create on every rank -> qw6cu_ep_handle -> all-gather the
+ * handles in rank order -> qw6cu_ep_connect.  Then every rank calls
+ * qw6cu_ep_layer once per layer step, in the same order; the call enqueues
+ * all its kernels on the context's stream without synchronising, so a step
+ * can be captured in a CUDA graph.  The result equals qw6cu_moe_prefill on
+ * the union of the ranks' tokens, bit for bit. */
+typedef struct qw6cu_ep qw6cu_ep;
+/* bytes of one rank's handle (a cudaIpcMemHandle_t) */
+size_t qw6cu_ep_handle_bytes(void);
+/* Experts are sharded contiguously (n_experts / world per rank); up to
+ * max_tokens tokens per rank and call.  Allocates the symmetric region
+ * (2 * world * max_tokens * top_k * hidden * 2 bytes plus signals/counts)
+ * and the private buffers. */
+int qw6cu_ep_create(qw6cu_ctx *ctx, uint32_t rank, uint32_t world, uint32_t n_experts, uint32_t top_k,
+                    uint32_t hidden, uint32_t inter, uint32_t max_tokens, qw6cu_ep **out);
+int qw6cu_ep_handle(qw6cu_ep *ep, void *handle);
+/* handles: world x qw6cu_ep_handle_bytes(), in rank order (own entry ignored) */
+int qw6cu_ep_connect(qw6cu_ep *ep, const void *handles);
+/* gate/up/down: this rank's experts (local index 0 .. n_experts/world - 1);
+ * logits fp32 [ntok x n_experts], x bf16 [ntok x hidden], out fp32 [ntok x
+ * hidden] -- this rank's tokens, device memory; ntok <= max_tokens. */
+int qw6cu_ep_layer(qw6cu_ep *ep, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
+                   const qw6cu_expert_pack *down, const float *logits, const void *x_bf16, float *out,
+                   uint32_t ntok);
+/* rows this rank's experts processed in the last layer (synchronises) */
+int qw6cu_ep_last_rows(qw6cu_ep *ep, uint32_t *rows);
+void qw6cu_ep_destroy(qw6cu_ep *ep);
+
 /* ---- profiling ----
  * Per-launch CUDA events around every kernel this context enqueues (the
  * counterpart of qw6's QW6_PROFILE timestamp queries, qw6_vk.c:2315-2357).

@@ -94,6 +94,176 @@ __global__ void k_ep_combine(const __nv_bfloat16* __restrict__ ret, const float*
     *reinterpret_cast<float2*>(out + (size_t)t * hidden + f) = make_float2(o0, o1);
 }
 
+// ------------------------------------------------ peer-memory EP layer --
+// One layer of expert parallelism without host round trips: the count
+// exchange, the dispatch of token rows into the owners' receive buffers and
+// the combine's reads of the owners' expert outputs all go through peer
+// memory (NVLink), ordered by epoch-stamped signal words.  Receive rows are
+// laid out by (local expert, source rank), so each owner's rows for an
+// expert are contiguous and the grouped GEMM runs in sorted mode.  Buffers
+// are reused across steps without extra barriers: a source writes step i+1
+// data into an owner only after its own step-i combine, which waited for
+// that owner's step-i outputs, so the owner is done with them.
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint64_t ep_now_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+constexpr uint64_t kEpWaitLimitNs = 2000000000ull;  // 2 s
+
+// wait until *f has reached epoch ep (wrap-safe); false after the time limit
+__device__ bool ep_wait_flag(const uint32_t* f, uint32_t ep) {
+    if ((int)(ld_acquire_sys(f) - ep) >= 0) return true;
+    const uint64_t t0 = ep_now_ns();
+    while ((int)(ld_acquire_sys(f) - ep) < 0)
+        if (ep_now_ns() - t0 > kEpWaitLimitNs) return false;
+    return true;
+}
+
+__device__ __forceinline__ uint32_t* ep_sig(const qw6k_ep_desc& d, uint32_t p, int kind, uint32_t src) {
+    return reinterpret_cast<uint32_t*>(d.peers[p] + d.o_sig) + kind * QW6K_EP_MAX_WORLD + src;
+}
+
+// wait (threads 0..world-1) for signal `kind` from every source; sets abort
+__device__ bool ep_wait_all(const qw6k_ep_desc& d, int kind, uint32_t ep) {
+    bool ok = true;
+    if (threadIdx.x < d.world) {
+        ok = ep_wait_flag(ep_sig(d, d.rank, kind, threadIdx.x), ep);
+        if (!ok) {
+            atomicExch(d.err, 41 + kind);
+            atomicExch(d.abort, 1);
+        }
+    }
+    return __syncthreads_and(ok);
+}
+
+// phase 0 (1 CTA x 256): stamp the step, publish this rank's per-expert
+// counts into every rank's matrix, wait for all sources, then plan:
+//   colsum[g]  = rows of global expert g over all sources,
+//   base[g]    = exclusive prefix of colsum inside g's owner block,
+//   sendoff[g] = base[g] + rows for g from sources < this rank,
+//   local_cnt  = colsum over this rank's own experts.
+__global__ void __launch_bounds__(256) k_ep_publish(const qw6k_ep_desc d) {
+    __shared__ uint32_t s_ep;
+    __shared__ int colsum[256];
+    const int tid = threadIdx.x, ne = (int)d.ne, epr = ne / (int)d.world;
+    if (tid == 0) {
+        s_ep = *d.epoch + 1;
+        *d.epoch = s_ep;
+    }
+    __syncthreads();
+    const uint32_t ep = s_ep, par = ep & 1u;
+    if (*d.abort) {
+        if (tid < epr) d.local_cnt[tid] = 0;
+        return;
+    }
+    for (uint32_t p = 0; p < d.world; p++) {
+        int32_t* m = reinterpret_cast<int32_t*>(d.peers[p] + d.o_cnt) + ((size_t)par * d.world + d.rank) * ne;
+        for (int g = tid; g < ne; g += blockDim.x) m[g] = d.cnt_self[g];
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (tid < (int)d.world) st_release_sys(ep_sig(d, tid, QW6K_EP_SIG_COUNTS, d.rank), ep);
+    if (!ep_wait_all(d, QW6K_EP_SIG_COUNTS, ep)) {
+        if (tid < epr) d.local_cnt[tid] = 0;
+        return;
+    }
+    const int32_t* mine = reinterpret_cast<const int32_t*>(d.peers[d.rank] + d.o_cnt) + (size_t)par * d.world * ne;
+    int cs = 0, before = 0;
+    if (tid < ne) {
+        for (uint32_t s = 0; s < d.world; s++) {
+            const int v = __ldcg(mine + (size_t)s * ne + tid);
+            cs += v;
+            if (s < d.rank) before += v;
+        }
+        colsum[tid] = cs;
+    }
+    __syncthreads();
+    if (tid < ne) {
+        int base = 0;
+        for (int g = (tid / epr) * epr; g < tid; g++) base += colsum[g];
+        d.sendoff[tid] = base + before;
+        // an owner block can never hold more rows than the receive capacity
+        int tot = 0;
+        for (int g = (tid / epr) * epr; g < (tid / epr + 1) * epr; g++) tot += colsum[g];
+        if (tot > (int)d.cap) {
+            atomicExch(d.err, 44);
+            atomicExch(d.abort, 1);
+        }
+    }
+    __syncthreads();
+    if (tid < epr) d.local_cnt[tid] = *d.abort ? 0 : colsum[d.rank * epr + tid];
+}
+
+// phase 1: warp per assignment copies the token row into its owner's rx at
+// sendoff[g] + pos[a]; the last CTA to finish signals every owner.
+__global__ void __launch_bounds__(256) k_ep_dispatch(const qw6k_ep_desc d) {
+    __shared__ bool last;
+    const int n = (int)(d.ntok * d.topk), epr = (int)(d.ne / d.world);
+    const bool go = !*d.abort;
+    const int a = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (go && a < n) {
+        const int g = d.idx[a], owner = g / epr, row = d.sendoff[g] + d.pos[a];
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(d.x) +
+                                                          (size_t)(a / (int)d.topk) * d.hidden);
+        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(d.peers[owner] + d.o_rx) +
+                                              (size_t)row * d.hidden);
+        for (int i = lane; i < (int)d.hidden / 8; i += 32) dst[i] = src[i];
+        if (lane == 0) d.send_row[a] = row;
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(d.done_ctas, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (last) {
+        __threadfence_system();
+        if (threadIdx.x == 0) *d.done_ctas = 0;
+        if (go && threadIdx.x < d.world) st_release_sys(ep_sig(d, threadIdx.x, QW6K_EP_SIG_ROWS, d.rank), *d.epoch);
+    }
+}
+
+// phases 2 and 4: wait for a signal from every rank
+__global__ void k_ep_wait(const qw6k_ep_desc d, int kind) {
+    if (*d.abort) return;
+    ep_wait_all(d, kind, *d.epoch);
+}
+
+// phase 3: this rank's expert outputs are complete
+__global__ void k_ep_signal_done(const qw6k_ep_desc d) {
+    if (*d.abort) return;
+    __threadfence_system();
+    if (threadIdx.x < d.world) st_release_sys(ep_sig(d, threadIdx.x, QW6K_EP_SIG_DONE, d.rank), *d.epoch);
+}
+
+// phase 5: out[t] = sum_k w * dout_owner[send_row] (fp32 fma, slot order),
+// reading the owners' outputs over peer memory
+__global__ void k_ep_combine_p2p(const qw6k_ep_desc d) {
+    const int t = blockIdx.y, f = (blockIdx.x * blockDim.x + threadIdx.x) * 2;
+    if (f >= (int)d.hidden || *d.abort) return;
+    const int topk = (int)d.topk, epr = (int)(d.ne / d.world);
+    float o0 = 0.f, o1 = 0.f;
+    for (int k = 0; k < topk; k++) {
+        const size_t a = (size_t)t * topk + k;
+        const int owner = d.idx[a] / epr;
+        const __nv_bfloat16* src =
+            reinterpret_cast<const __nv_bfloat16*>(d.peers[owner] + d.o_dout) + (size_t)d.send_row[a] * d.hidden + f;
+        const unsigned int bits = __ldcg(reinterpret_cast<const unsigned int*>(src));
+        const float wk = d.w[a];
+        o0 = fmaf(wk, __uint_as_float(bits << 16), o0);
+        o1 = fmaf(wk, __uint_as_float(bits & 0xffff0000u), o1);
+    }
+    *reinterpret_cast<float2*>(d.out + (size_t)t * d.hidden + f) = make_float2(o0, o1);
+}
+
 }  // namespace qw6
 
 using namespace qw6;
@@ -131,5 +301,38 @@ extern "C" int qw6k_ep_combine(const void* ret_bf16, const float* w, const int32
     if ((reinterpret_cast<uintptr_t>(ret_bf16) & 3u) || (reinterpret_cast<uintptr_t>(out) & 7u)) return QW6K_ERR_ALIGN;
     dim3 g((hidden / 2 + 255) / 256, ntok);
     k_ep_combine<<<g, 256, 0, st>>>((const __nv_bfloat16*)ret_bf16, w, send_pos, (int)topk, (int)hidden, out);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
+}
+
+extern "C" int qw6k_ep_p2p_phase(const qw6k_ep_desc* d, int phase, cudaStream_t st) {
+    if (!d || !d->peers || !d->world || d->world > QW6K_EP_MAX_WORLD || d->rank >= d->world || !d->ne ||
+        d->ne > 256 || d->ne % d->world || !d->topk || !d->ntok || !d->hidden || d->hidden % 8 || !d->epoch ||
+        !d->abort || !d->done_ctas || !d->err || !d->idx || !d->w || !d->cnt_self || !d->pos || !d->sendoff ||
+        !d->local_cnt || !d->send_row || !d->x || !d->out || !d->cap)
+        return QW6K_ERR_ARG;
+    switch (phase) {
+    case 0:
+        k_ep_publish<<<1, 256, 0, st>>>(*d);
+        break;
+    case 1:
+        k_ep_dispatch<<<(d->ntok * d->topk + 7) / 8, 256, 0, st>>>(*d);
+        break;
+    case 2:
+        k_ep_wait<<<1, 64, 0, st>>>(*d, QW6K_EP_SIG_ROWS);
+        break;
+    case 3:
+        k_ep_signal_done<<<1, 64, 0, st>>>(*d);
+        break;
+    case 4:
+        k_ep_wait<<<1, 64, 0, st>>>(*d, QW6K_EP_SIG_DONE);
+        break;
+    case 5: {
+        dim3 g((d->hidden / 2 + 255) / 256, d->ntok);
+        k_ep_combine_p2p<<<g, 256, 0, st>>>(*d);
+        break;
+    }
+    default:
+        return QW6K_ERR_ARG;
+    }
     return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
 }

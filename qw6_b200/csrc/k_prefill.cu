@@ -106,19 +106,26 @@ __global__ void k_pf_scatter(const PfArgs a) {
 // A lane fills rows (16*mi + g, 16*mi + g + 8) of a 128 x 64 bf16 A tile
 // (one K slab) from the packed tile-block; it covers K [8t, 8t+8) of both
 // 32-halves of the slab, i.e. swizzle chunks t and 4 + t.  Loading (into
-// registers) and dequantizing/storing are split so that the loads of slab
-// k+1 are in flight while slab k is dequantized.
+// registers) and dequantizing/storing are split so that the loads of later
+// slabs are in flight while slab k is dequantized.
+//
+// Dequantization works on bf16 pairs: two quant bytes are spread into the
+// two halves of a word (prmt), the 4- or 6-bit values are or-ed into the
+// mantissa of bf16 128.0 (0x4300 | q == 128 + q exactly for q < 128), the
+// bias is removed exactly with one bf16x2 add, and one bf16x2 fma/mul
+// applies the sub-block scale (rounded to bf16) and min:
+//   Q4_K  w = fma(q, bf16(d*sc), -bf16(dmin*m))
+//   Q6_K  w = (q - 32) * bf16(d*sc)
+// a single rounding of each product to bf16 after the scale's own rounding
+// (relative error <= 2^-8 of the weight), well inside the bf16 prefill
+// tolerance.
 
-__device__ __forceinline__ uint4 pack8_bf16(const float (&v)[8]) {
-    uint4 r;
-    __nv_bfloat162 p0 = __floats2bfloat162_rn(v[0], v[1]), p1 = __floats2bfloat162_rn(v[2], v[3]);
-    __nv_bfloat162 p2 = __floats2bfloat162_rn(v[4], v[5]), p3 = __floats2bfloat162_rn(v[6], v[7]);
-    r.x = *reinterpret_cast<uint32_t*>(&p0);
-    r.y = *reinterpret_cast<uint32_t*>(&p1);
-    r.z = *reinterpret_cast<uint32_t*>(&p2);
-    r.w = *reinterpret_cast<uint32_t*>(&p3);
-    return r;
-}
+__device__ __forceinline__ uint32_t bf2_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
+__device__ __forceinline__ __nv_bfloat162 bf2_of(uint32_t u) { return *reinterpret_cast<__nv_bfloat162*>(&u); }
+// bytes 2p, 2p+1 of w (p = 0, 1) into the low byte of each 16-bit half
+__device__ __forceinline__ uint32_t spread_pair(uint32_t w, int p) { return prmt(w, 0u, p ? 0x4342u : 0x4140u); }
+// (hi:lo) small unsigned ints (< 128, one per half) -> bf16x2 of 128 + q
+__device__ __forceinline__ uint32_t bf16_magic(uint32_t halves) { return halves | 0x43004300u; }
 
 template <int F>
 struct ASlab;
@@ -139,6 +146,7 @@ struct ASlab<QW6F_Q4_K_M> {
     }
     __device__ __forceinline__ void store(uint8_t* sa, int c, int mi, int lane) const {
         const int g = lane >> 2, t = lane & 3;
+        const __nv_bfloat162 m128 = __floats2bfloat162_rn(-128.f, -128.f);
 #pragma unroll
         for (int rh = 0; rh < 2; rh++) {
             const float d = f16f(h[rh].x), dmin = f16f(h[rh].x >> 16);
@@ -146,47 +154,54 @@ struct ASlab<QW6F_Q4_K_M> {
             const uint32_t SC = (c < 2) ? (S0 & 0x3f3f3f3fu) : ((S2 & 0x0f0f0f0fu) | ((S0 >> 2) & 0x30303030u));
             const uint32_t MN = (c < 2) ? (S1 & 0x3f3f3f3fu) : (((S2 >> 4) & 0x0f0f0f0fu) | ((S1 >> 2) & 0x30303030u));
             const int j0 = (2 * c) & 3, j1 = (2 * c + 1) & 3;
-            const float dl = d * (float)byte_of(SC, j0), ml = dmin * (float)byte_of(MN, j0);
-            const float dh = d * (float)byte_of(SC, j1), mh = dmin * (float)byte_of(MN, j1);
-            float lo[8], hi[8];
+            const __nv_bfloat162 dl = __float2bfloat162_rn(d * (float)byte_of(SC, j0));
+            const __nv_bfloat162 ml = __float2bfloat162_rn(-(dmin * (float)byte_of(MN, j0)));
+            const __nv_bfloat162 dh = __float2bfloat162_rn(d * (float)byte_of(SC, j1));
+            const __nv_bfloat162 mh = __float2bfloat162_rn(-(dmin * (float)byte_of(MN, j1)));
+            uint32_t lo[4], hi[4];
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
-                const uint32_t b = byte_of(i < 4 ? q[rh].x : q[rh].y, i & 3);
-                lo[i] = fmaf(dl, (float)(b & 15u), -ml);
-                hi[i] = fmaf(dh, (float)(b >> 4), -mh);
+            for (int pr = 0; pr < 4; pr++) {
+                const uint32_t sp = spread_pair(pr < 2 ? q[rh].x : q[rh].y, pr & 1);
+                const __nv_bfloat162 ql = __hadd2(bf2_of(bf16_magic(sp & 0x000f000fu)), m128);
+                const __nv_bfloat162 qh = __hadd2(bf2_of(bf16_magic((sp >> 4) & 0x000f000fu)), m128);
+                lo[pr] = bf2_bits(__hfma2(ql, dl, ml));
+                hi[pr] = bf2_bits(__hfma2(qh, dh, mh));
             }
             const uint32_t row = mi * 16 + g + 8 * rh;
-            *reinterpret_cast<uint4*>(sa + sw128_off(row, t)) = pack8_bf16(lo);
-            *reinterpret_cast<uint4*>(sa + sw128_off(row, 4 + t)) = pack8_bf16(hi);
+            *reinterpret_cast<uint4*>(sa + sw128_off(row, t)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            *reinterpret_cast<uint4*>(sa + sw128_off(row, 4 + t)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
         }
     }
 };
 
 // Q6_K: slab c covers half n = c/2, runs kk = 2(c%2) and 2(c%2)+1; scale
 // sc[8n + 2kk] (qw6's even-scale reading, qw6.c:1568-1571).
+// The two scales of slab c are bytes 8n + 2k0 and 8n + 2k0 + 2 of the row's
+// 16 scales, i.e. bytes 0 and 2 of scale word c.
 template <>
 struct ASlab<QW6F_Q6_K> {
-    uint4 L[2], sc[2];
+    uint4 L[2];
     uint2 H[2];
-    uint32_t dd[2];
+    uint32_t sc[2], dd[2];
     __device__ __forceinline__ void load(const uint8_t* tb, int c, int lane) {
         const int g = lane >> 2, n = c >> 1;
 #pragma unroll
         for (int rh = 0; rh < 2; rh++) {
             L[rh] = ldg128(tb + 288 + ((rh * 3 + n) * 32 + lane) * 16);
             H[rh] = ldg64(tb + 288 + ((rh * 3 + 2) * 32 + lane) * 16 + n * 8);
-            sc[rh] = ldg128(tb + (g + 8 * rh) * 16);
+            sc[rh] = ldg32(tb + (g + 8 * rh) * 16 + 4 * c);
             dd[rh] = ldg16(tb + 256 + (g + 8 * rh) * 2);
         }
     }
     __device__ __forceinline__ void store(uint8_t* sa, int c, int mi, int lane) const {
-        const int g = lane >> 2, t = lane & 3, n = c >> 1, k0 = 2 * (c & 1);
+        const int g = lane >> 2, t = lane & 3, k0 = 2 * (c & 1);
+        const __nv_bfloat162 m160 = __floats2bfloat162_rn(-160.f, -160.f);  // -(128 + 32)
 #pragma unroll
         for (int rh = 0; rh < 2; rh++) {
             const float d = f16f(dd[rh]);
-            const float d0 = d * (float)(int8_t)byte16(sc[rh], 8 * n + 2 * k0);
-            const float d1 = d * (float)(int8_t)byte16(sc[rh], 8 * n + 2 * (k0 + 1));
-            float v0[8], v1[8];
+            const __nv_bfloat162 d0 = __float2bfloat162_rn(d * (float)(int8_t)byte_of(sc[rh], 0));
+            const __nv_bfloat162 d1 = __float2bfloat162_rn(d * (float)(int8_t)byte_of(sc[rh], 2));
+            uint32_t v0[4], v1[4];
 #pragma unroll
             for (int hw = 0; hw < 2; hw++) {
                 const uint32_t A = hw ? L[rh].y : L[rh].x, B = hw ? L[rh].w : L[rh].z, Hh = hw ? H[rh].y : H[rh].x;
@@ -199,14 +214,16 @@ struct ASlab<QW6F_Q6_K> {
                     q1 = ((B >> 4) & 0x0f0f0f0fu) | ((Hh >> 2) & 0x30303030u);
                 }
 #pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    v0[4 * hw + i] = d0 * (float)((int)byte_of(q0, i) - 32);
-                    v1[4 * hw + i] = d1 * (float)((int)byte_of(q1, i) - 32);
+                for (int p = 0; p < 2; p++) {
+                    const __nv_bfloat162 a = __hadd2(bf2_of(bf16_magic(spread_pair(q0, p))), m160);
+                    const __nv_bfloat162 b = __hadd2(bf2_of(bf16_magic(spread_pair(q1, p))), m160);
+                    v0[2 * hw + p] = bf2_bits(__hmul2(a, d0));
+                    v1[2 * hw + p] = bf2_bits(__hmul2(b, d1));
                 }
             }
             const uint32_t row = mi * 16 + g + 8 * rh;
-            *reinterpret_cast<uint4*>(sa + sw128_off(row, t)) = pack8_bf16(v0);
-            *reinterpret_cast<uint4*>(sa + sw128_off(row, 4 + t)) = pack8_bf16(v1);
+            *reinterpret_cast<uint4*>(sa + sw128_off(row, t)) = make_uint4(v0[0], v0[1], v0[2], v0[3]);
+            *reinterpret_cast<uint4*>(sa + sw128_off(row, 4 + t)) = make_uint4(v1[0], v1[1], v1[2], v1[3]);
         }
     }
 };
@@ -215,23 +232,43 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t 
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
                  : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
 
-// B rows (K slab ks): bf16 row j of the item from src + rowidx[j]*ld, zero
-// for j >= cnt (up to npad), streamed with cp.async.
-__device__ __forceinline__ void issue_b(uint8_t* sb, const __nv_bfloat16* src, int ld, const int* rowidx, int cnt,
-                                        int npad, int ks) {
-    for (int i = threadIdx.x; i < npad * 8; i += blockDim.x) {
-        const int r = i >> 3, cc = i & 7;
-        const bool live = r < cnt;
-        const __nv_bfloat16* p = src + (live ? (size_t)rowidx[r] * ld + ks * 64 + cc * 8 : 0);
-        cp_async16(sb + sw128_off(r, cc), p, live ? 16u : 0u);
+// B rows: producer thread p always copies 16-byte chunk p % 8 of rows
+// p / 8 + 32k (k < 8) of each slab; the source row pointers and swizzled
+// destination offsets are computed once per tile.  Rows j >= cnt (up to
+// npad) are zero-filled.
+struct BRows {
+    const __nv_bfloat16* src[8];
+    uint32_t dst[8];
+    uint32_t bytes[8];
+    int n;
+    __device__ __forceinline__ void init(const __nv_bfloat16* base, int ld, const int* rowidx, int cnt, int npad,
+                                         int ptid) {
+        const int cc = ptid & 7;
+        n = 0;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int r = (ptid >> 3) + 32 * k;
+            const bool live = r < cnt;
+            src[k] = base + (live ? (size_t)rowidx[r] * ld + cc * 8 : 0);
+            dst[k] = sw128_off(r, cc);
+            bytes[k] = live ? 16u : 0u;
+            if (r < npad) n = k + 1;
+        }
     }
+    __device__ __forceinline__ void issue(uint8_t* sb, int ks) const {
+#pragma unroll
+        for (int k = 0; k < 8; k++)
+            if (k < n) cp_async16(sb + dst[k], src[k] + (bytes[k] ? ks * 64 : 0), bytes[k]);
+    }
+};
+
+// arrive on *b once every cp.async this thread issued so far has landed
+// (the barrier's expected count includes this arrival)
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* b) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(b)) : "memory");
 }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 __device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
@@ -241,20 +278,28 @@ __device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f 
 // MODE 1 (down): A0/A1 = down rows [256 ft, +128) / [256 ft + 128, +128),
 //   K = inter, B = H rows of the item's assignments; epilogue writes the
 //   per-assignment expert outputs (bf16) for the slot-order combine.
-// 8 warps: warp w dequantizes 16-row m-tiles 2(w%4), 2(w%4)+1 of A(w/4);
-// all threads stream B with cp.async; thread 0 issues the MMAs.  Three smem
-// stages; every wait is time-bounded.
+// Warp-specialized, kPfStages shared-memory stages, one 64-wide K slab each:
+//   warps 0-7 (producers): wait stage empty; stream the slab's B rows with
+//     cp.async (arriving on the stage's full barrier when they land);
+//     dequantize A (warp w: 16-row m-tiles 2(w%4), 2(w%4)+1 of A(w/4)) from
+//     registers loaded two slabs earlier into the swizzled stage; arrive on
+//     full; load the A fragments of slab ks+2;
+//   warp 8 (lane 0): wait full; 8 MMAs (two accumulators x 4 K-steps);
+//     commit to the stage's empty barrier; at the end commit to `done`.
+// Every wait is time-bounded; on a timeout the error word is set, in-flight
+// copies and MMAs are drained and the CTA exits without an epilogue.
 constexpr int kPfStages = 3;
+constexpr int kPfProducers = 256;
+constexpr int kPfThreads = kPfProducers + 32;
 
 template <int F, int MODE>
-__global__ void __launch_bounds__(256, 1) k_pf_gemm(const PfArgs a) {
+__global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     constexpr uint32_t A_BYTES = 128 * 128, B_BYTES = kPfChunk * 128, STAGE = 2 * A_BYTES + B_BYTES;
     constexpr int TB = Fmt<F>::TB, S = kPfStages;
-    __shared__ uint64_t mbar[S];
+    __shared__ uint64_t full[S], empty[S], done;
     __shared__ uint32_t tmem_base;
-    __shared__ int ncommit[S];
     __shared__ int rows[kPfChunk];
     const int K = MODE == 0 ? a.hidden : a.inter;
     const int nft = MODE == 0 ? a.inter / 128 : a.hidden / 256;
@@ -263,61 +308,79 @@ __global__ void __launch_bounds__(256, 1) k_pf_gemm(const PfArgs a) {
     const int4 it = a.items[item];
     const int e = it.x, off = it.y, cnt = it.z, npad = (cnt + 15) & ~15;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    for (int j = tid; j < cnt; j += blockDim.x) rows[j] = MODE == 0 ? a.order[off + j] / a.topk : a.order[off + j];
-    if (warp == 0) tmem_alloc(&tmem_base, 512);
+    const int32_t* ord = a.order;  // null: the rows are already grouped by expert (sorted mode)
+    for (int j = tid; j < cnt; j += blockDim.x)
+        rows[j] = ord ? (MODE == 0 ? ord[off + j] / a.topk : ord[off + j]) : off + j;
+    if (warp == 8) tmem_alloc(&tmem_base, 512);
     if (tid == 0) {
         for (int i = 0; i < S; i++) {
-            mbar_init(&mbar[i], 1);
-            ncommit[i] = 0;
+            mbar_init(&full[i], 2 * kPfProducers);  // one plain + one cp.async arrival per producer
+            mbar_init(&empty[i], 1);
         }
+        mbar_init(&done, 1);
         mbar_fence_init();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_base;
-    const uint32_t idesc = umma_idesc_bf16(128, npad);
     const int nbk = K / 256, nk = K / 64;
-    const __nv_bfloat16* bsrc = MODE == 0 ? a.x : a.h;
-    const int mtx = warp >> 2, mi0 = 2 * (warp & 3);
-    // first packed m-tile of this warp's A matrix
-    const uint8_t* wbase;
-    int mt0;
-    if (MODE == 0) {
-        wbase = mtx ? a.up + (size_t)e * a.ustride : a.gate + (size_t)e * a.gstride;
-        mt0 = ft * 8;
-    } else {
-        wbase = a.down + (size_t)e * a.dstride;
-        mt0 = (2 * ft + mtx) * 8;
-    }
-    auto tile = [&](int u, int ks) { return wbase + ((size_t)(mt0 + mi0 + u) * nbk + (ks >> 2)) * TB; };
-
-    ASlab<F> cur[2], nxt[2];
-    issue_b(smem + 2 * A_BYTES, bsrc, K, rows, cnt, npad, 0);
-    cp_async_commit();
-    cur[0].load(tile(0, 0), 0, lane);
-    cur[1].load(tile(1, 0), 0, lane);
     bool ok = true;
-    for (int ks = 0; ks < nk; ks++) {
-        const int s = ks % S;
-        if (ks + 1 < nk) {
-            const int s1 = (ks + 1) % S;
-            if (ks + 1 >= S) ok = ok && mbar_wait(&mbar[s1], ((ks + 1 - S) / S) & 1, a.err, 31 + MODE);
-            if (ok) issue_b(smem + s1 * STAGE + 2 * A_BYTES, bsrc, K, rows, cnt, npad, ks + 1);
-            nxt[0].load(tile(0, ks + 1), (ks + 1) & 3, lane);
-            nxt[1].load(tile(1, ks + 1), (ks + 1) & 3, lane);
+
+    if (warp < 8) {
+        // ---------------------------------------------------- producers --
+        const __nv_bfloat16* bsrc = MODE == 0 ? a.x : a.h;
+        const int mtx = warp >> 2, mi0 = 2 * (warp & 3);
+        const uint8_t* wbase;
+        int mt0;
+        if (MODE == 0) {
+            wbase = mtx ? a.up + (size_t)e * a.ustride : a.gate + (size_t)e * a.gstride;
+            mt0 = ft * 8;
+        } else {
+            wbase = a.down + (size_t)e * a.dstride;
+            mt0 = (2 * ft + mtx) * 8;
         }
-        cp_async_commit();
-        uint8_t* sa = smem + s * STAGE + mtx * A_BYTES;
-        if (ok) {
-            cur[0].store(sa, ks & 3, mi0, lane);
-            cur[1].store(sa, ks & 3, mi0 + 1, lane);
+        auto tile = [&](int u, int ks) { return wbase + ((size_t)(mt0 + mi0 + u) * nbk + (ks >> 2)) * TB; };
+        BRows br;
+        br.init(bsrc, K, rows, cnt, npad, tid);
+        ASlab<F> r0[2], r1[2];  // A fragments of slabs ks and ks+1
+        r0[0].load(tile(0, 0), 0, lane);
+        r0[1].load(tile(1, 0), 0, lane);
+        if (nk > 1) {
+            r1[0].load(tile(0, 1), 1, lane);
+            r1[1].load(tile(1, 1), 1, lane);
         }
-        cp_async_wait<1>();
-        fence_async_smem();
-        ok = __syncthreads_and(ok);
-        if (!ok) break;
-        if (tid == 0) {
+        for (int ks = 0; ks < nk; ks++) {
+            const int s = ks % S;
+            if (ks >= S && !mbar_wait(&empty[s], ((ks / S) - 1) & 1, a.err, 31 + MODE)) {
+                ok = false;
+                break;
+            }
+            uint8_t* st = smem + s * STAGE;
+            br.issue(st + 2 * A_BYTES, ks);
+            cp_async_arrive_noinc(&full[s]);
+            uint8_t* sa = st + mtx * A_BYTES;
+            r0[0].store(sa, ks & 3, mi0, lane);
+            r0[1].store(sa, ks & 3, mi0 + 1, lane);
+            fence_async_smem();
+            mbar_arrive(&full[s]);
+            r0[0] = r1[0];
+            r0[1] = r1[1];
+            if (ks + 2 < nk) {
+                r1[0].load(tile(0, ks + 2), (ks + 2) & 3, lane);
+                r1[1].load(tile(1, ks + 2), (ks + 2) & 3, lane);
+            }
+        }
+        cp_async_wait_all();
+    } else if (lane == 0) {
+        // ------------------------------------------------- MMA issuer ----
+        const uint32_t idesc = umma_idesc_bf16(128, npad);
+        for (int ks = 0; ks < nk; ks++) {
+            const int s = ks % S;
+            if (!mbar_wait(&full[s], (ks / S) & 1, a.err, 35 + MODE)) {
+                ok = false;
+                break;
+            }
             tc_fence_after();
             const uint32_t a0 = smem_u32(smem + s * STAGE), a1 = a0 + A_BYTES, bb = a0 + 2 * A_BYTES;
 #pragma unroll
@@ -327,17 +390,15 @@ __global__ void __launch_bounds__(256, 1) k_pf_gemm(const PfArgs a) {
                 umma_bf16(tmem, umma_desc_sw128(a0 + 32 * k4), bd, idesc, acc);
                 umma_bf16(tmem + 256, umma_desc_sw128(a1 + 32 * k4), bd, idesc, acc);
             }
-            umma_commit(&mbar[s]);
-            ncommit[s]++;
+            umma_commit(&empty[s]);
         }
-        cur[0] = nxt[0];
-        cur[1] = nxt[1];
+        umma_commit(&done);  // arrives once every MMA issued above has completed
     }
-    cp_async_wait<0>();
-    if (ok) ok = mbar_wait(&mbar[(nk - 1) % S], ((nk - 1) / S) & 1, a.err, 33 + MODE);
+    // all MMAs drained before TMEM is read or released
+    if (warp < 8 || lane == 0) ok = mbar_wait(&done, 0, a.err, 37 + MODE) && ok;
     ok = __syncthreads_and(ok);
     tc_fence_after();
-    if (ok) {
+    if (ok && warp < 8) {
         const int wq = warp & 3, wg = warp >> 2;
         const uint32_t lrow = (uint32_t)(wq * 32) << 16;
         for (int c0 = wg * 16; c0 < npad; c0 += 32) {
@@ -349,7 +410,8 @@ __global__ void __launch_bounds__(256, 1) k_pf_gemm(const PfArgs a) {
 #pragma unroll
                 for (int j = 0; j < 16; j++)
                     if (c0 + j < cnt)
-                        a.h[(size_t)a.order[off + c0 + j] * a.inter + f] = __float2bfloat16_rn(silu_fast(v0[j]) * v1[j]);
+                        a.h[(size_t)(ord ? ord[off + c0 + j] : off + c0 + j) * a.inter + f] =
+                            __float2bfloat16_rn(silu_fast(v0[j]) * v1[j]);
             } else {
                 const int f = 2 * ft * 128 + wq * 32 + lane;
 #pragma unroll
@@ -361,14 +423,10 @@ __global__ void __launch_bounds__(256, 1) k_pf_gemm(const PfArgs a) {
                     }
             }
         }
-    } else {
-        __syncthreads();
-        for (int i = 0; i < S; i++)
-            if (ncommit[i] > 0) mbar_wait(&mbar[i], (ncommit[i] - 1) & 1, nullptr, 0);
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(tmem, 512);
+    if (warp == 8) tmem_dealloc(tmem, 512);
 }
 
 // out[t][f] = sum_k w[t,k] * dout[t*topk + k][f], fp32 in slot order k
@@ -404,7 +462,8 @@ extern "C" size_t qw6k_moe_prefill_ws_bytes(uint32_t ntok, uint32_t hidden, uint
 
 static int pf_args(const qw6k_moe_desc* d, int* err, PfArgs& a) {
     const bool rows_mode = d && !d->logits;
-    if (rows_mode && (d->topk != 1 || !d->row_expert || !d->dout)) return QW6K_ERR_ARG;
+    const bool sorted = rows_mode && d->expert_counts;
+    if (rows_mode && (d->topk != 1 || (!d->row_expert && !sorted) || !d->dout)) return QW6K_ERR_ARG;
     if (!d || !d->gate || !d->up || !d->down || !d->x || (!d->out && !rows_mode) || !d->ws || !err || !d->ntok ||
         !d->ne || d->ne > 256 || !d->topk || d->topk > 32 || d->topk > d->ne || (size_t)d->ntok * d->topk > (1u << 22))
         return QW6K_ERR_ARG;
@@ -450,6 +509,10 @@ static int pf_args(const qw6k_moe_desc* d, int* err, PfArgs& a) {
         a.idx = const_cast<int32_t*>(d->row_expert);
         a.dout = (__nv_bfloat16*)d->dout;
     }
+    if (sorted) {  // rows grouped by expert in expert order, expert_counts[e] rows each
+        a.cnt = const_cast<int32_t*>(d->expert_counts);
+        a.order = nullptr;
+    }
     return 0;
 }
 
@@ -462,7 +525,7 @@ static int launch_pf(const PfArgs& a, int mi, cudaStream_t st) {
         return QW6K_ERR_CUDA;
     cfg = true;
     const int nft = MODE == 0 ? a.inter / 128 : a.hidden / 256;
-    k_pf_gemm<F, MODE><<<mi * nft, 256, smem, st>>>(a);
+    k_pf_gemm<F, MODE><<<mi * nft, kPfThreads, smem, st>>>(a);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
 }
 
@@ -485,6 +548,7 @@ extern "C" int qw6k_moe_prefill_phase(const qw6k_moe_desc* d, int* err, int phas
         k_pf_route<<<(a.ntok + 7) / 8, 256, 0, st>>>(a);
         break;
     case 1:
+        if (!a.order) return 0;  // sorted mode: counts supplied
         if (cudaMemsetAsync(a.cnt, 0, 256 * 4, st) != cudaSuccess) return QW6K_ERR_CUDA;
         k_pf_count<<<(tk + 255) / 256, 256, 0, st>>>(a);
         break;
@@ -492,6 +556,7 @@ extern "C" int qw6k_moe_prefill_phase(const qw6k_moe_desc* d, int* err, int phas
         k_pf_offsets<<<1, 256, 0, st>>>(a);
         break;
     case 3:
+        if (!a.order) return 0;  // sorted mode: already in expert order
         k_pf_scatter<<<(tk + 255) / 256, 256, 0, st>>>(a);
         break;
     case 4:

@@ -94,6 +94,9 @@ typedef struct {
      * FFN_e(x[r]), unweighted */
     const int32_t *row_expert;
     void *dout;
+    /* sorted rows mode (rows mode with row_expert == NULL): the rows of x are
+     * grouped by expert in expert order, expert_counts[e] (device) rows each */
+    const int32_t *expert_counts;
 } qw6k_moe_desc;
 
 size_t qw6k_moe_ws_bytes(uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t ne, uint32_t topk);
@@ -118,6 +121,36 @@ int qw6k_ep_pack(const int32_t *idx, const int32_t *pos, const int32_t *cnt, uin
 int qw6k_ep_expand(const int32_t *recv_cnt, uint32_t world, uint32_t epr, int32_t *row_expert, cudaStream_t st);
 int qw6k_ep_combine(const void *ret_bf16, const float *w, const int32_t *send_pos, uint32_t ntok, uint32_t topk,
                     uint32_t hidden, float *out, cudaStream_t st);
+
+/* Expert parallelism over peer memory (k_ep.cu, phases of one layer).
+ * Every rank holds one symmetric region with the same layout: signal words
+ * (3 kinds x 64 sources, u32 epochs), a double-buffered count matrix
+ * [2][world][ne] (i32), received token rows rx [cap][hidden] (bf16) and
+ * expert outputs dout [cap][hidden] (bf16); peers[p] is rank p's region as
+ * mapped in this process. */
+#define QW6K_EP_MAX_WORLD 64
+enum { QW6K_EP_SIG_COUNTS = 0, QW6K_EP_SIG_ROWS = 1, QW6K_EP_SIG_DONE = 2 };
+typedef struct {
+    uint8_t *const *peers; /* device array [world] */
+    size_t o_sig, o_cnt, o_rx, o_dout;
+    uint32_t rank, world, ne, topk, hidden, ntok, cap;
+    uint32_t *epoch;     /* private: step counter (phase 0 increments it) */
+    int *abort;          /* private: set once any wait gives up; later phases do nothing */
+    uint32_t *done_ctas; /* private: dispatch completion counter */
+    int *err;            /* error word: 41 + phase kind of a wait that timed out */
+    const int32_t *idx;  /* [ntok*topk] routing of this rank's tokens */
+    const float *w;
+    const int32_t *cnt_self, *pos; /* per global expert counts / positions (qw6k_ep_count) */
+    int32_t *sendoff;    /* [ne] first row of this rank's block for each expert at its owner */
+    int32_t *local_cnt;  /* [ne/world] rows per local expert this step */
+    int32_t *send_row;   /* [ntok*topk] row of each assignment at its owner */
+    const void *x;       /* bf16 [ntok][hidden] */
+    float *out;          /* fp32 [ntok][hidden] */
+} qw6k_ep_desc;
+/* phases: 0 publish counts + wait + plan, 1 dispatch rows + signal,
+ * 2 wait for all rows, 3 signal outputs ready, 4 wait for all outputs,
+ * 5 combine (peer reads) */
+int qw6k_ep_p2p_phase(const qw6k_ep_desc *d, int phase, cudaStream_t st);
 
 /* Fixed 1 MiB device scratch (k_static.cu) of the allocation-free MoE entry
  * point; *ptr is its device address on the current device (looked up with

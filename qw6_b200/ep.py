@@ -135,3 +135,48 @@ def ep_moe_prefill(backend, logits: torch.Tensor, x_bf16: torch.Tensor, top_k: i
     ret = backend.empty((n, hidden), recv_out.dtype)
     dist.all_to_all_single(ret, recv_out, send_counts, recv_counts, group=group)
     return backend.combine(ret, w, send_pos, ntok, top_k)
+
+
+class PeerMoE:
+    """The peer-memory expert-parallel layer (libqw6cuda qw6cu_ep_*): token
+    rows and expert outputs move over NVLink by loads/stores in this
+    library's own kernels, with no host synchronisation inside a layer, so a
+    step can be captured in a CUDA graph.  Construction is collective over
+    `group`: every rank allocates its symmetric region and the CUDA IPC
+    handles are all-gathered.  Results are bit-identical to
+    `ep_moe_prefill` and to the single-GPU layer."""
+
+    def __init__(self, ctx: L.Context, gate: L.ExpertPack, up: L.ExpertPack, down: L.ExpertPack, n_experts: int,
+                 top_k: int, hidden: int, inter: int, max_tokens: int, group=None):
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.ctx, self.packs, self.hidden, self.max_tokens = ctx, (gate, up, down), hidden, max_tokens
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        self.ep = L.PeerEP(ctx, rank, world, n_experts, top_k, hidden, inter, max_tokens)
+        mine = self.ep.handle()
+        if world > 1:
+            allh = [None] * world
+            dist.all_gather_object(allh, mine, group=group)
+        else:
+            allh = [mine]
+        self.ep.connect(allh)
+        if world > 1:
+            dist.barrier(group=group)
+
+    def __call__(self, logits: torch.Tensor, x_bf16: torch.Tensor, out: torch.Tensor | None = None,
+                 packs: tuple | None = None) -> torch.Tensor:
+        """One layer step on torch's current stream (`packs` overrides the
+        expert packs given at construction, e.g. another layer's)."""
+        ntok = x_bf16.shape[0]
+        if out is None:
+            out = torch.empty((ntok, self.hidden), dtype=torch.float32, device=self.device)
+        self.ctx.set_stream(torch.cuda.current_stream(self.device).cuda_stream or _CUDA_STREAM_LEGACY)
+        self.ep.layer(*(packs or self.packs), logits.data_ptr(), x_bf16.data_ptr(), out.data_ptr(), ntok)
+        return out
+
+    def last_rows(self) -> int:
+        return self.ep.last_rows()
+
+    def close(self):
+        self.ep.close()
+

@@ -109,6 +109,15 @@ def load() -> C.CDLL:
     lib.qw6cu_ep_pack.argtypes = [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _vp, _u32, _vp, _vp]
     lib.qw6cu_ep_expand.argtypes = [_vp, _vp, _u32, _u32, _vp]
     lib.qw6cu_ep_combine.argtypes = [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _vp]
+    lib.qw6cu_ep_handle_bytes.restype = _sz
+    lib.qw6cu_ep_handle_bytes.argtypes = []
+    lib.qw6cu_ep_create.argtypes = [_vp, _u32, _u32, _u32, _u32, _u32, _u32, _u32, C.POINTER(_vp)]
+    lib.qw6cu_ep_handle.argtypes = [_vp, _vp]
+    lib.qw6cu_ep_connect.argtypes = [_vp, _vp]
+    lib.qw6cu_ep_layer.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32]
+    lib.qw6cu_ep_last_rows.argtypes = [_vp, C.POINTER(_u32)]
+    lib.qw6cu_ep_destroy.argtypes = [_vp]
+    lib.qw6cu_ep_destroy.restype = None
     lib.qw6cu_moe_prefill_workspace_bytes.argtypes = [_u32, _u32, _u32, _u32, _u32]
     lib.qw6cu_moe_prefill_workspace_bytes.restype = _sz
     lib.qw6cu_gemm_bf16_nt.argtypes = [_vp, _vp, _vp, _vp, _u32, _u32, _u32]
@@ -324,3 +333,50 @@ class Context:
     @staticmethod
     def moe_workspace_bytes(ntok, hidden, inter, n_experts, top_k) -> int:
         return int(load().qw6cu_moe_workspace_bytes(ntok, hidden, inter, n_experts, top_k))
+
+
+class PeerEP:
+    """A qw6cu_ep: this rank's endpoint of the peer-memory expert-parallel
+    MoE layer (experts sharded contiguously over `world` ranks)."""
+
+    def __init__(self, ctx: Context, rank: int, world: int, n_experts: int, top_k: int, hidden: int, inter: int,
+                 max_tokens: int) -> None:
+        self.ctx, self.lib = ctx, ctx.lib
+        h = _vp()
+        _check(self.lib.qw6cu_ep_create(ctx.h, rank, world, n_experts, top_k, hidden, inter, max_tokens, C.byref(h)),
+               "qw6cu_ep_create")
+        self.h = h
+
+    @staticmethod
+    def handle_bytes() -> int:
+        return int(load().qw6cu_ep_handle_bytes())
+
+    def handle(self) -> bytes:
+        buf = C.create_string_buffer(self.handle_bytes())
+        _check(self.lib.qw6cu_ep_handle(self.h, buf), "qw6cu_ep_handle")
+        return buf.raw
+
+    def connect(self, handles: list[bytes]) -> None:
+        blob = b"".join(handles)
+        _check(self.lib.qw6cu_ep_connect(self.h, C.c_char_p(blob)), "qw6cu_ep_connect")
+
+    def layer(self, gate: ExpertPack, up: ExpertPack, down: ExpertPack, logits, x_bf16, out, ntok) -> None:
+        _check(self.lib.qw6cu_ep_layer(self.h, C.byref(gate), C.byref(up), C.byref(down), logits, x_bf16, out, ntok),
+               "qw6cu_ep_layer")
+
+    def last_rows(self) -> int:
+        r = _u32()
+        _check(self.lib.qw6cu_ep_last_rows(self.h, C.byref(r)), "qw6cu_ep_last_rows")
+        return int(r.value)
+
+    def close(self) -> None:
+        if self.h:
+            self.lib.qw6cu_ep_destroy(self.h)
+            self.h = _vp()
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass
+

@@ -1,8 +1,10 @@
-"""GPU: expert-parallel prefill MoE over NCCL.
+"""GPU: expert-parallel prefill MoE, NCCL and peer-memory variants.
 
 Each of `world` ranks (one spawned process per GPU) owns E/world experts and
-T/world tokens and runs qw6_b200.ep.ep_moe_prefill with the libqw6cuda
-backend.  The gathered outputs must equal, bit for bit, the single-GPU
+T/world tokens and runs (a) qw6_b200.ep.ep_moe_prefill over NCCL
+all-to-alls and (b) qw6_b200.ep.PeerMoE (libqw6cuda's own dispatch/combine
+kernels over peer memory) three times in a row and once more as a replayed
+CUDA graph.  Every gathered output must equal, bit for bit, the single-GPU
 qw6cu_moe_prefill on all tokens (same expert outputs, same slot-order
 combine), and match the CPU oracle's composition on a seeded sample of
 tokens within 2e-2 (the bf16 tensor-core prefill tolerance).  world=1 runs
@@ -51,7 +53,7 @@ def _rank(rank, world, port, case, q):
     import torch.distributed as dist
 
     from qw6_b200 import lib as L
-    from qw6_b200.ep import CudaBackend, ep_moe_prefill
+    from qw6_b200.ep import CudaBackend, PeerMoE, ep_moe_prefill
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -70,6 +72,25 @@ def _rank(rank, world, port, case, q):
         out = ep_moe_prefill(be, lg, x, K, E)
         torch.cuda.synchronize()
         ctx.check_device_errors()
+        # peer-memory layer: repeated steps reuse the buffers (epochs 1..3) ...
+        pm = PeerMoE(ctx, packs[0], packs[1], packs[2], E, K, H, I, tpr)
+        peer = [pm(lg, x).cpu().numpy() for _ in range(3)]
+        ctx.check_device_errors()
+        # ... and a captured step replays with fresh epochs
+        s = torch.cuda.Stream()
+        gout = torch.empty((tpr, H), dtype=torch.float32, device="cuda")
+        gout.fill_(float("nan"))
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            pm(lg, x, gout)
+        for _ in range(2):
+            g.replay()
+        torch.cuda.synchronize()
+        ctx.check_device_errors()
+        peer.append(gout.cpu().numpy())
+        del g
+        pm.close()
         full = None
         if rank == 0:  # single-GPU reference over all tokens and experts
             ctx.set_stream(None)
@@ -83,7 +104,7 @@ def _rank(rank, world, port, case, q):
             ctx.synchronize()
             ctx.check_device_errors()
             full = fo.cpu().numpy()
-        q.put((rank, out.cpu().numpy(), full))
+        q.put((rank, out.cpu().numpy(), peer, full))
         ctx.close()
     finally:
         dist.destroy_process_group()
@@ -110,14 +131,17 @@ def test_ep_prefill_nccl(world, case, oracle):
         p.start()
     got = {}
     for _ in procs:
-        r, o, f = q.get(timeout=600)
-        got[r] = (o, f)
+        r, o, pr, f = q.get(timeout=600)
+        got[r] = (o, pr, f)
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
     out = np.concatenate([got[r][0] for r in range(world)])
-    full = got[0][1]
+    full = got[0][2]
     assert np.array_equal(out.view(np.uint32), full.view(np.uint32)), float(np.max(np.abs(out - full)))
+    for i in range(4):  # three eager peer steps, then the graph replay
+        peer = np.concatenate([got[r][1][i] for r in range(world)])
+        assert np.array_equal(peer.view(np.uint32), full.view(np.uint32)), (i, float(np.nanmax(np.abs(peer - full))))
     gate, up, down, logits, xbits = _data(case)
     toks = np.random.Generator(np.random.PCG64(5)).choice(T, 24, replace=False)
     ref, _, _ = oracle.moe_layer(S.Q4_K, gate, up, S.Q6_K, down, logits[toks], S.bf16_to_f32(xbits[toks]), top_k=K)
