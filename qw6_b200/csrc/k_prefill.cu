@@ -234,21 +234,23 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t 
 }
 
 // B rows: producer thread p always copies 16-byte chunk p % 8 of rows
-// p / 8 + 32k (k < 8) of each slab; the source row pointers and swizzled
-// destination offsets are computed once per tile.  Rows j >= cnt (up to
-// npad) are zero-filled.
+// p / 8 + (NP / 8) k of each slab (NP producers); the source row pointers
+// and swizzled destination offsets are computed once per tile.  Rows
+// j >= cnt (up to npad) are zero-filled.
+template <int NP>
 struct BRows {
-    const __nv_bfloat16* src[8];
-    uint32_t dst[8];
-    uint32_t bytes[8];
+    static constexpr int R = kPfChunk * 8 / NP;  // rows per thread at npad = kPfChunk
+    const __nv_bfloat16* src[R];
+    uint32_t dst[R];
+    uint32_t bytes[R];
     int n;
     __device__ __forceinline__ void init(const __nv_bfloat16* base, int ld, const int* rowidx, int cnt, int npad,
                                          int ptid) {
         const int cc = ptid & 7;
         n = 0;
 #pragma unroll
-        for (int k = 0; k < 8; k++) {
-            const int r = (ptid >> 3) + 32 * k;
+        for (int k = 0; k < R; k++) {
+            const int r = (ptid >> 3) + (NP / 8) * k;
             const bool live = r < cnt;
             src[k] = base + (live ? (size_t)rowidx[r] * ld + cc * 8 : 0);
             dst[k] = sw128_off(r, cc);
@@ -258,7 +260,7 @@ struct BRows {
     }
     __device__ __forceinline__ void issue(uint8_t* sb, int ks) const {
 #pragma unroll
-        for (int k = 0; k < 8; k++)
+        for (int k = 0; k < R; k++)
             if (k < n) cp_async16(sb + dst[k], src[k] + (bytes[k] ? ks * 64 : 0), bytes[k]);
     }
 };
@@ -279,18 +281,19 @@ __device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f 
 //   K = inter, B = H rows of the item's assignments; epilogue writes the
 //   per-assignment expert outputs (bf16) for the slot-order combine.
 // Warp-specialized, kPfStages shared-memory stages, one 64-wide K slab each:
-//   warps 0-7 (producers): wait stage empty; stream the slab's B rows with
+//   warps 0-15 (producers): wait stage empty; stream the slab's B rows with
 //     cp.async (arriving on the stage's full barrier when they land);
-//     dequantize A (warp w: 16-row m-tiles 2(w%4), 2(w%4)+1 of A(w/4)) from
-//     registers loaded two slabs earlier into the swizzled stage; arrive on
-//     full; load the A fragments of slab ks+2;
-//   warp 8 (lane 0): wait full; 8 MMAs (two accumulators x 4 K-steps);
+//     dequantize A (warp w: 16-row m-tile w%8 of A(w/8)) from registers
+//     loaded two slabs earlier into the swizzled stage; arrive on full; load
+//     the A fragments of slab ks+2;
+//   warp 16 (lane 0): wait full; 8 MMAs (two accumulators x 4 K-steps);
 //     commit to the stage's empty barrier; at the end commit to `done`.
 // Every wait is time-bounded; on a timeout the error word is set, in-flight
 // copies and MMAs are drained and the CTA exits without an epilogue.
 constexpr int kPfStages = 3;
-constexpr int kPfProducers = 256;
+constexpr int kPfProducers = 512;
 constexpr int kPfThreads = kPfProducers + 32;
+constexpr int kPfMmaWarp = kPfProducers / 32;
 
 template <int F, int MODE>
 __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfArgs a) {
@@ -311,7 +314,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfArgs a) {
     const int32_t* ord = a.order;  // null: the rows are already grouped by expert (sorted mode)
     for (int j = tid; j < cnt; j += blockDim.x)
         rows[j] = ord ? (MODE == 0 ? ord[off + j] / a.topk : ord[off + j]) : off + j;
-    if (warp == 8) tmem_alloc(&tmem_base, 512);
+    if (warp == kPfMmaWarp) tmem_alloc(&tmem_base, 512);
     if (tid == 0) {
         for (int i = 0; i < S; i++) {
             mbar_init(&full[i], 2 * kPfProducers);  // one plain + one cp.async arrival per producer
@@ -327,10 +330,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfArgs a) {
     const int nbk = K / 256, nk = K / 64;
     bool ok = true;
 
-    if (warp < 8) {
+    if (warp < kPfMmaWarp) {
         // ---------------------------------------------------- producers --
         const __nv_bfloat16* bsrc = MODE == 0 ? a.x : a.h;
-        const int mtx = warp >> 2, mi0 = 2 * (warp & 3);
+        const int mtx = warp >> 3, mi = warp & 7;
         const uint8_t* wbase;
         int mt0;
         if (MODE == 0) {
@@ -340,16 +343,12 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfArgs a) {
             wbase = a.down + (size_t)e * a.dstride;
             mt0 = (2 * ft + mtx) * 8;
         }
-        auto tile = [&](int u, int ks) { return wbase + ((size_t)(mt0 + mi0 + u) * nbk + (ks >> 2)) * TB; };
-        BRows br;
+        auto tile = [&](int ks) { return wbase + ((size_t)(mt0 + mi) * nbk + (ks >> 2)) * TB; };
+        BRows<kPfProducers> br;
         br.init(bsrc, K, rows, cnt, npad, tid);
-        ASlab<F> r0[2], r1[2];  // A fragments of slabs ks and ks+1
-        r0[0].load(tile(0, 0), 0, lane);
-        r0[1].load(tile(1, 0), 0, lane);
-        if (nk > 1) {
-            r1[0].load(tile(0, 1), 1, lane);
-            r1[1].load(tile(1, 1), 1, lane);
-        }
+        ASlab<F> r0, r1;  // A fragments of slabs ks and ks+1
+        r0.load(tile(0), 0, lane);
+        if (nk > 1) r1.load(tile(1), 1, lane);
         for (int ks = 0; ks < nk; ks++) {
             const int s = ks % S;
             if (ks >= S && !mbar_wait(&empty[s], ((ks / S) - 1) & 1, a.err, 31 + MODE)) {
@@ -359,17 +358,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfArgs a) {
             uint8_t* st = smem + s * STAGE;
             br.issue(st + 2 * A_BYTES, ks);
             cp_async_arrive_noinc(&full[s]);
-            uint8_t* sa = st + mtx * A_BYTES;
-            r0[0].store(sa, ks & 3, mi0, lane);
-            r0[1].store(sa, ks & 3, mi0 + 1, lane);
+            r0.store(st + mtx * A_BYTES, ks & 3, mi, lane);
             fence_async_smem();
             mbar_arrive(&full[s]);
-            r0[0] = r1[0];
-            r0[1] = r1[1];
-            if (ks + 2 < nk) {
-                r1[0].load(tile(0, ks + 2), (ks + 2) & 3, lane);
-                r1[1].load(tile(1, ks + 2), (ks + 2) & 3, lane);
-            }
+            r0 = r1;
+            if (ks + 2 < nk) r1.load(tile(ks + 2), (ks + 2) & 3, lane);
         }
         cp_async_wait_all();
     } else if (lane == 0) {
@@ -395,13 +388,15 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfArgs a) {
         umma_commit(&done);  // arrives once every MMA issued above has completed
     }
     // all MMAs drained before TMEM is read or released
-    if (warp < 8 || lane == 0) ok = mbar_wait(&done, 0, a.err, 37 + MODE) && ok;
+    if (warp < kPfMmaWarp || lane == 0) ok = mbar_wait(&done, 0, a.err, 37 + MODE) && ok;
     ok = __syncthreads_and(ok);
     tc_fence_after();
-    if (ok && warp < 8) {
+    if (ok && warp < kPfMmaWarp) {
+        // warp w reads TMEM lanes 32 (w % 4) .. +31 and every (kPfMmaWarp/4)-th 16-column group
+        constexpr int NG = kPfMmaWarp / 4;
         const int wq = warp & 3, wg = warp >> 2;
         const uint32_t lrow = (uint32_t)(wq * 32) << 16;
-        for (int c0 = wg * 16; c0 < npad; c0 += 32) {
+        for (int c0 = wg * 16; c0 < npad; c0 += 16 * NG) {
             float v0[16], v1[16];
             tmem_ld16(tmem + lrow + (uint32_t)c0, v0);
             tmem_ld16(tmem + lrow + 256u + (uint32_t)c0, v1);
@@ -426,7 +421,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfArgs a) {
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 8) tmem_dealloc(tmem, 512);
+    if (warp == kPfMmaWarp) tmem_dealloc(tmem, 512);
 }
 
 // out[t][f] = sum_k w[t,k] * dout[t*topk + k][f], fp32 in slot order k
