@@ -128,32 +128,39 @@ __device__ __forceinline__ uint32_t spread_pair(uint32_t w, int p) { return prmt
 __device__ __forceinline__ uint32_t bf16_magic(uint32_t halves) { return halves | 0x43004300u; }
 
 template <int F>
-struct ASlab;
+struct ASlab;  // one lane's quant bytes of one K slab (both row halves)
+template <int F>
+struct AHdr;   // one lane's per-row header of one super-block (both row halves)
 
 // Q4_K: slab c of a super-block holds sub-blocks 2c (low nibbles of
 // qs[32c..32c+32)) and 2c+1 (high nibbles).
 template <>
+struct AHdr<QW6F_Q4_K_M> {
+    uint4 h[2];  // d | dmin << 16, scales/mins words S0, S1, S2
+    __device__ __forceinline__ void load(const uint8_t* tb, int lane) {
+#pragma unroll
+        for (int rh = 0; rh < 2; rh++) h[rh] = ldg128(tb + ((lane >> 2) + 8 * rh) * 16);
+    }
+};
+template <>
 struct ASlab<QW6F_Q4_K_M> {
     uint2 q[2];
-    uint4 h[2];
-    __device__ __forceinline__ void load(const uint8_t* tb, int c, int lane) {
-        const int g = lane >> 2;
+    template <int C>
+    __device__ __forceinline__ void load(const uint8_t* tb, int lane) {
 #pragma unroll
-        for (int rh = 0; rh < 2; rh++) {
-            q[rh] = ldg64(tb + 256 + ((rh * 2 + (c >> 1)) * 32 + lane) * 16 + (c & 1) * 8);
-            h[rh] = ldg128(tb + (g + 8 * rh) * 16);
-        }
+        for (int rh = 0; rh < 2; rh++) q[rh] = ldg64(tb + 256 + ((rh * 2 + (C >> 1)) * 32 + lane) * 16 + (C & 1) * 8);
     }
-    __device__ __forceinline__ void store(uint8_t* sa, int c, int mi, int lane) const {
+    template <int C>
+    __device__ __forceinline__ void store(uint8_t* sa, const AHdr<QW6F_Q4_K_M>& hd, int mi, int lane) const {
         const int g = lane >> 2, t = lane & 3;
         const __nv_bfloat162 m128 = __floats2bfloat162_rn(-128.f, -128.f);
+        constexpr int j0 = (2 * C) & 3, j1 = (2 * C + 1) & 3;
 #pragma unroll
         for (int rh = 0; rh < 2; rh++) {
-            const float d = f16f(h[rh].x), dmin = f16f(h[rh].x >> 16);
-            const uint32_t S0 = h[rh].y, S1 = h[rh].z, S2 = h[rh].w;
-            const uint32_t SC = (c < 2) ? (S0 & 0x3f3f3f3fu) : ((S2 & 0x0f0f0f0fu) | ((S0 >> 2) & 0x30303030u));
-            const uint32_t MN = (c < 2) ? (S1 & 0x3f3f3f3fu) : (((S2 >> 4) & 0x0f0f0f0fu) | ((S1 >> 2) & 0x30303030u));
-            const int j0 = (2 * c) & 3, j1 = (2 * c + 1) & 3;
+            const float d = f16f(hd.h[rh].x), dmin = f16f(hd.h[rh].x >> 16);
+            const uint32_t S0 = hd.h[rh].y, S1 = hd.h[rh].z, S2 = hd.h[rh].w;
+            const uint32_t SC = (C < 2) ? (S0 & 0x3f3f3f3fu) : ((S2 & 0x0f0f0f0fu) | ((S0 >> 2) & 0x30303030u));
+            const uint32_t MN = (C < 2) ? (S1 & 0x3f3f3f3fu) : (((S2 >> 4) & 0x0f0f0f0fu) | ((S1 >> 2) & 0x30303030u));
             const __nv_bfloat162 dl = __float2bfloat162_rn(d * (float)byte_of(SC, j0));
             const __nv_bfloat162 ml = __float2bfloat162_rn(-(dmin * (float)byte_of(MN, j0)));
             const __nv_bfloat162 dh = __float2bfloat162_rn(d * (float)byte_of(SC, j1));
@@ -175,32 +182,46 @@ struct ASlab<QW6F_Q4_K_M> {
 };
 
 // Q6_K: slab c covers half n = c/2, runs kk = 2(c%2) and 2(c%2)+1; scale
-// sc[8n + 2kk] (qw6's even-scale reading, qw6.c:1568-1571).
-// The two scales of slab c are bytes 8n + 2k0 and 8n + 2k0 + 2 of the row's
-// 16 scales, i.e. bytes 0 and 2 of scale word c.
+// sc[8n + 2kk] (qw6's even-scale reading, qw6.c:1568-1571).  The two scales
+// of slab c are bytes 8n + 2k0 and 8n + 2k0 + 2 of the row's 16 scales,
+// i.e. bytes 0 and 2 of scale word c.
+template <>
+struct AHdr<QW6F_Q6_K> {
+    uint4 sc[2];
+    uint32_t dd[2];
+    __device__ __forceinline__ void load(const uint8_t* tb, int lane) {
+        const int g = lane >> 2;
+#pragma unroll
+        for (int rh = 0; rh < 2; rh++) {
+            sc[rh] = ldg128(tb + (g + 8 * rh) * 16);
+            dd[rh] = ldg16(tb + 256 + (g + 8 * rh) * 2);
+        }
+    }
+};
 template <>
 struct ASlab<QW6F_Q6_K> {
     uint4 L[2];
     uint2 H[2];
-    uint32_t sc[2], dd[2];
-    __device__ __forceinline__ void load(const uint8_t* tb, int c, int lane) {
-        const int g = lane >> 2, n = c >> 1;
+    template <int C>
+    __device__ __forceinline__ void load(const uint8_t* tb, int lane) {
+        constexpr int n = C >> 1;
 #pragma unroll
         for (int rh = 0; rh < 2; rh++) {
             L[rh] = ldg128(tb + 288 + ((rh * 3 + n) * 32 + lane) * 16);
             H[rh] = ldg64(tb + 288 + ((rh * 3 + 2) * 32 + lane) * 16 + n * 8);
-            sc[rh] = ldg32(tb + (g + 8 * rh) * 16 + 4 * c);
-            dd[rh] = ldg16(tb + 256 + (g + 8 * rh) * 2);
         }
     }
-    __device__ __forceinline__ void store(uint8_t* sa, int c, int mi, int lane) const {
-        const int g = lane >> 2, t = lane & 3, k0 = 2 * (c & 1);
+    template <int C>
+    __device__ __forceinline__ void store(uint8_t* sa, const AHdr<QW6F_Q6_K>& hd, int mi, int lane) const {
+        const int g = lane >> 2, t = lane & 3;
+        constexpr int k0 = 2 * (C & 1);
         const __nv_bfloat162 m160 = __floats2bfloat162_rn(-160.f, -160.f);  // -(128 + 32)
 #pragma unroll
         for (int rh = 0; rh < 2; rh++) {
-            const float d = f16f(dd[rh]);
-            const __nv_bfloat162 d0 = __float2bfloat162_rn(d * (float)(int8_t)byte_of(sc[rh], 0));
-            const __nv_bfloat162 d1 = __float2bfloat162_rn(d * (float)(int8_t)byte_of(sc[rh], 2));
+            const float d = f16f(hd.dd[rh]);
+            const uint32_t scw = word_of(hd.sc[rh], C);
+            const __nv_bfloat162 d0 = __float2bfloat162_rn(d * (float)(int8_t)byte_of(scw, 0));
+            const __nv_bfloat162 d1 = __float2bfloat162_rn(d * (float)(int8_t)byte_of(scw, 2));
             uint32_t v0[4], v1[4];
 #pragma unroll
             for (int hw = 0; hw < 2; hw++) {
@@ -252,16 +273,23 @@ struct BRows {
         for (int k = 0; k < R; k++) {
             const int r = (ptid >> 3) + (NP / 8) * k;
             const bool live = r < cnt;
-            src[k] = base + (live ? (size_t)rowidx[r] * ld + cc * 8 : 0);
+            // dead rows read nothing (src-size 0) from a valid address of row 0
+            src[k] = base + (live ? (size_t)rowidx[r] * ld : 0) + cc * 8;
             dst[k] = sw128_off(r, cc);
             bytes[k] = live ? 16u : 0u;
             if (r < npad) n = k + 1;
         }
     }
-    __device__ __forceinline__ void issue(uint8_t* sb, int ks) const {
+    // slab C (0..3) of the current 256-wide K block
+    template <int C>
+    __device__ __forceinline__ void issue(uint8_t* sb) const {
 #pragma unroll
         for (int k = 0; k < R; k++)
-            if (k < n) cp_async16(sb + dst[k], src[k] + (bytes[k] ? ks * 64 : 0), bytes[k]);
+            if (k < n) cp_async16(sb + dst[k], src[k] + C * 64, bytes[k]);
+    }
+    __device__ __forceinline__ void next_block() {
+#pragma unroll
+        for (int k = 0; k < R; k++) src[k] += 256;
     }
 };
 
@@ -343,26 +371,73 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfArgs a) {
             wbase = a.down + (size_t)e * a.dstride;
             mt0 = (2 * ft + mtx) * 8;
         }
-        auto tile = [&](int ks) { return wbase + ((size_t)(mt0 + mi) * nbk + (ks >> 2)) * TB; };
+        const uint8_t* tb = wbase + (size_t)(mt0 + mi) * nbk * TB;  // this warp's m-tile, K block 0
         BRows<kPfProducers> br;
         br.init(bsrc, K, rows, cnt, npad, tid);
-        ASlab<F> r0, r1;  // A fragments of slabs ks and ks+1
-        r0.load(tile(0), 0, lane);
-        if (nk > 1) r1.load(tile(1), 1, lane);
-        for (int ks = 0; ks < nk; ks++) {
-            const int s = ks % S;
-            if (ks >= S && !mbar_wait(&empty[s], ((ks / S) - 1) & 1, a.err, 31 + MODE)) {
-                ok = false;
-                break;
+        // A fragments of slabs ks (even: ra, odd: rb) two slabs ahead; headers one K block ahead
+        ASlab<F> ra, rb;
+        AHdr<F> hc, hn;
+        hc.load(tb, lane);
+        hn = hc;
+        ra.template load<0>(tb, lane);
+        rb.template load<1>(tb, lane);
+        for (int kb = 0; kb < nbk && ok; kb++) {
+            const uint8_t* tbn = tb + TB;
+            const bool more = kb + 1 < nbk;
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const int ks = kb * 4 + c, s = ks % S;
+                if (ks >= S && !mbar_wait(&empty[s], ((ks / S) - 1) & 1, a.err, 31 + MODE)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* st = smem + s * STAGE;
+                uint8_t* sa = st + mtx * A_BYTES;
+                switch (c) {  // c is a compile-time constant after unrolling
+                case 0:
+                    br.template issue<0>(st + 2 * A_BYTES);
+                    cp_async_arrive_noinc(&full[s]);
+                    ra.template store<0>(sa, hc, mi, lane);
+                    break;
+                case 1:
+                    br.template issue<1>(st + 2 * A_BYTES);
+                    cp_async_arrive_noinc(&full[s]);
+                    rb.template store<1>(sa, hc, mi, lane);
+                    break;
+                case 2:
+                    br.template issue<2>(st + 2 * A_BYTES);
+                    cp_async_arrive_noinc(&full[s]);
+                    ra.template store<2>(sa, hc, mi, lane);
+                    break;
+                default:
+                    br.template issue<3>(st + 2 * A_BYTES);
+                    cp_async_arrive_noinc(&full[s]);
+                    rb.template store<3>(sa, hc, mi, lane);
+                    break;
+                }
+                fence_async_smem();
+                mbar_arrive(&full[s]);
+                switch (c) {  // refill the buffer just consumed with slab ks + 2
+                case 0:
+                    ra.template load<2>(tb, lane);
+                    break;
+                case 1:
+                    rb.template load<3>(tb, lane);
+                    break;
+                case 2:
+                    if (more) {
+                        hn.load(tbn, lane);
+                        ra.template load<0>(tbn, lane);
+                    }
+                    break;
+                default:
+                    if (more) rb.template load<1>(tbn, lane);
+                    break;
+                }
             }
-            uint8_t* st = smem + s * STAGE;
-            br.issue(st + 2 * A_BYTES, ks);
-            cp_async_arrive_noinc(&full[s]);
-            r0.store(st + mtx * A_BYTES, ks & 3, mi, lane);
-            fence_async_smem();
-            mbar_arrive(&full[s]);
-            r0 = r1;
-            if (ks + 2 < nk) r1.load(tile(ks + 2), (ks + 2) & 3, lane);
+            hc = hn;
+            tb = tbn;
+            br.next_block();
         }
         cp_async_wait_all();
     } else if (lane == 0) {

@@ -94,12 +94,15 @@ __device__ __forceinline__ void mbar_fence_init() { asm volatile("fence.mbarrier
 __device__ __forceinline__ void mbar_arrive(uint64_t* b) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
 }
+// Test phase `parity`; if it is not complete yet the thread is suspended
+// (without issuing) until the phase completes or kSuspendHintNs pass.
+constexpr uint32_t kSuspendHintNs = 20000;
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
     uint32_t ok;
     asm volatile(
-        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\nselp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
-        : "r"(smem_u32(b)), "r"(parity)
+        : "r"(smem_u32(b)), "r"(parity), "r"(kSuspendHintNs)
         : "memory");
     return ok != 0;
 }
@@ -113,16 +116,17 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // timeout the error word gets `code` and false is returned (no hang).
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
+// The clock is read once per 64 suspended polls (each up to kSuspendHintNs).
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, int* err, int code) {
     if (mbar_try_wait(b, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
-    while (!mbar_try_wait(b, parity)) {
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    for (uint32_t n = 1;; n++) {
+        if (mbar_try_wait(b, parity)) return true;
+        if ((n & 63) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
             if (err) atomicExch(err, code);
             return false;
         }
     }
-    return true;
 }
 
 }  // namespace qw6
