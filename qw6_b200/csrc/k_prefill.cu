@@ -109,23 +109,26 @@ __global__ void k_pf_scatter(const PfArgs a) {
 // registers) and dequantizing/storing are split so that the loads of later
 // slabs are in flight while slab k is dequantized.
 //
-// Dequantization works on bf16 pairs: two quant bytes are spread into the
-// two halves of a word (prmt), the 4- or 6-bit values are or-ed into the
-// mantissa of bf16 128.0 (0x4300 | q == 128 + q exactly for q < 128), the
-// bias is removed exactly with one bf16x2 add, and one bf16x2 fma/mul
-// applies the sub-block scale (rounded to bf16) and min:
-//   Q4_K  w = fma(q, bf16(d*sc), -bf16(dmin*m))
-//   Q6_K  w = (q - 32) * bf16(d*sc)
-// a single rounding of each product to bf16 after the scale's own rounding
-// (relative error <= 2^-8 of the weight), well inside the bf16 prefill
-// tolerance.
+// Dequantization works on bf16 pairs.  Two small unsigned values (< 128) are
+// placed in the low bytes of the two 16-bit halves of a word with one prmt
+// whose second source supplies 0x43 high bytes: 0x43vv is bf16 128 + v
+// exactly.  The bias is then removed exactly inside a bf16x2 add or fma:
+//   Q4_K scale  bf16(d*sc)   = fma(128 + sc, d_b, -128 d_b)   (one rounding)
+//        min    bf16(-dm*m)  = fma(128 + m, -dm_b, 128 dm_b)
+//        weight fma(128 + q - 128, scale, min)                 (one rounding)
+//   Q6_K weight (128 + q - 160) * bf16(d*sc)                   (one rounding)
+// with d_b, dm_b the super-block's fp16 d, dmin rounded to bf16.  A weight
+// carries at most three bf16 roundings (relative error < 2^-7.4), inside
+// the bf16 prefill tolerance.
 
+constexpr uint32_t kBf16Hi = 0x43434343u;  // prmt source of the 0x43 high bytes
+// bytes p0, p1 of w -> halves (0x43 p0, 0x43 p1): bf16 (128 + w.b[p0], 128 + w.b[p1])
+template <int P0, int P1>
+__device__ __forceinline__ uint32_t bf16_pair(uint32_t w) {
+    return prmt(w, kBf16Hi, (uint32_t)(P0 | (4 << 4) | (P1 << 8) | (4 << 12)));
+}
 __device__ __forceinline__ uint32_t bf2_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
 __device__ __forceinline__ __nv_bfloat162 bf2_of(uint32_t u) { return *reinterpret_cast<__nv_bfloat162*>(&u); }
-// bytes 2p, 2p+1 of w (p = 0, 1) into the low byte of each 16-bit half
-__device__ __forceinline__ uint32_t spread_pair(uint32_t w, int p) { return prmt(w, 0u, p ? 0x4342u : 0x4140u); }
-// (hi:lo) small unsigned ints (< 128, one per half) -> bf16x2 of 128 + q
-__device__ __forceinline__ uint32_t bf16_magic(uint32_t halves) { return halves | 0x43004300u; }
 
 template <int F>
 struct ASlab;  // one lane's quant bytes of one K slab (both row halves)
@@ -133,17 +136,37 @@ template <int F>
 struct AHdr;   // one lane's per-row header of one super-block (both row halves)
 
 // Q4_K: slab c of a super-block holds sub-blocks 2c (low nibbles of
-// qs[32c..32c+32)) and 2c+1 (high nibbles).
+// qs[32c..32c+32)) and 2c+1 (high nibbles).  The header is unpacked once per
+// super-block: 6-bit scales/mins of sub-blocks 0-3 and 4-7 as byte words
+// (qw6_get_scale_min_k4, qw6.c:1480-1490) and the bf16 constants.
 template <>
 struct AHdr<QW6F_Q4_K_M> {
-    uint4 h[2];  // d | dmin << 16, scales/mins words S0, S1, S2
+    uint4 h[2];  // raw: d | dmin << 16, words S0, S1, S2
+    uint32_t sc_lo[2], sc_hi[2], mn_lo[2], mn_hi[2];
+    __nv_bfloat162 d2[2], nd128[2], ndm2[2], dm128[2];
     __device__ __forceinline__ void load(const uint8_t* tb, int lane) {
 #pragma unroll
         for (int rh = 0; rh < 2; rh++) h[rh] = ldg128(tb + ((lane >> 2) + 8 * rh) * 16);
     }
+    __device__ __forceinline__ void unpack() {
+#pragma unroll
+        for (int rh = 0; rh < 2; rh++) {
+            const uint32_t S0 = h[rh].y, S1 = h[rh].z, S2 = h[rh].w;
+            sc_lo[rh] = S0 & 0x3f3f3f3fu;
+            mn_lo[rh] = S1 & 0x3f3f3f3fu;
+            sc_hi[rh] = (S2 & 0x0f0f0f0fu) | ((S0 >> 2) & 0x30303030u);
+            mn_hi[rh] = ((S2 >> 4) & 0x0f0f0f0fu) | ((S1 >> 2) & 0x30303030u);
+            const float d = f16f(h[rh].x), dmin = f16f(h[rh].x >> 16);
+            d2[rh] = __float2bfloat162_rn(d);
+            nd128[rh] = __float2bfloat162_rn(-128.f * d);
+            ndm2[rh] = __float2bfloat162_rn(-dmin);
+            dm128[rh] = __float2bfloat162_rn(128.f * dmin);
+        }
+    }
 };
 template <>
 struct ASlab<QW6F_Q4_K_M> {
+    static constexpr bool kPairShared = false;  // every slab has its own bytes
     uint2 q[2];
     template <int C>
     __device__ __forceinline__ void load(const uint8_t* tb, int lane) {
@@ -157,22 +180,20 @@ struct ASlab<QW6F_Q4_K_M> {
         constexpr int j0 = (2 * C) & 3, j1 = (2 * C + 1) & 3;
 #pragma unroll
         for (int rh = 0; rh < 2; rh++) {
-            const float d = f16f(hd.h[rh].x), dmin = f16f(hd.h[rh].x >> 16);
-            const uint32_t S0 = hd.h[rh].y, S1 = hd.h[rh].z, S2 = hd.h[rh].w;
-            const uint32_t SC = (C < 2) ? (S0 & 0x3f3f3f3fu) : ((S2 & 0x0f0f0f0fu) | ((S0 >> 2) & 0x30303030u));
-            const uint32_t MN = (C < 2) ? (S1 & 0x3f3f3f3fu) : (((S2 >> 4) & 0x0f0f0f0fu) | ((S1 >> 2) & 0x30303030u));
-            const __nv_bfloat162 dl = __float2bfloat162_rn(d * (float)byte_of(SC, j0));
-            const __nv_bfloat162 ml = __float2bfloat162_rn(-(dmin * (float)byte_of(MN, j0)));
-            const __nv_bfloat162 dh = __float2bfloat162_rn(d * (float)byte_of(SC, j1));
-            const __nv_bfloat162 mh = __float2bfloat162_rn(-(dmin * (float)byte_of(MN, j1)));
+            const uint32_t SC = C < 2 ? hd.sc_lo[rh] : hd.sc_hi[rh], MN = C < 2 ? hd.mn_lo[rh] : hd.mn_hi[rh];
+            const __nv_bfloat162 dl = __hfma2(bf2_of(bf16_pair<j0, j0>(SC)), hd.d2[rh], hd.nd128[rh]);
+            const __nv_bfloat162 dh = __hfma2(bf2_of(bf16_pair<j1, j1>(SC)), hd.d2[rh], hd.nd128[rh]);
+            const __nv_bfloat162 ml = __hfma2(bf2_of(bf16_pair<j0, j0>(MN)), hd.ndm2[rh], hd.dm128[rh]);
+            const __nv_bfloat162 mh = __hfma2(bf2_of(bf16_pair<j1, j1>(MN)), hd.ndm2[rh], hd.dm128[rh]);
             uint32_t lo[4], hi[4];
 #pragma unroll
-            for (int pr = 0; pr < 4; pr++) {
-                const uint32_t sp = spread_pair(pr < 2 ? q[rh].x : q[rh].y, pr & 1);
-                const __nv_bfloat162 ql = __hadd2(bf2_of(bf16_magic(sp & 0x000f000fu)), m128);
-                const __nv_bfloat162 qh = __hadd2(bf2_of(bf16_magic((sp >> 4) & 0x000f000fu)), m128);
-                lo[pr] = bf2_bits(__hfma2(ql, dl, ml));
-                hi[pr] = bf2_bits(__hfma2(qh, dh, mh));
+            for (int w = 0; w < 2; w++) {
+                const uint32_t W = w ? q[rh].y : q[rh].x;
+                const uint32_t L = W & 0x0f0f0f0fu, H = (W >> 4) & 0x0f0f0f0fu;
+                lo[2 * w] = bf2_bits(__hfma2(__hadd2(bf2_of(bf16_pair<0, 1>(L)), m128), dl, ml));
+                lo[2 * w + 1] = bf2_bits(__hfma2(__hadd2(bf2_of(bf16_pair<2, 3>(L)), m128), dl, ml));
+                hi[2 * w] = bf2_bits(__hfma2(__hadd2(bf2_of(bf16_pair<0, 1>(H)), m128), dh, mh));
+                hi[2 * w + 1] = bf2_bits(__hfma2(__hadd2(bf2_of(bf16_pair<2, 3>(H)), m128), dh, mh));
             }
             const uint32_t row = mi * 16 + g + 8 * rh;
             *reinterpret_cast<uint4*>(sa + sw128_off(row, t)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
@@ -184,11 +205,13 @@ struct ASlab<QW6F_Q4_K_M> {
 // Q6_K: slab c covers half n = c/2, runs kk = 2(c%2) and 2(c%2)+1; scale
 // sc[8n + 2kk] (qw6's even-scale reading, qw6.c:1568-1571).  The two scales
 // of slab c are bytes 8n + 2k0 and 8n + 2k0 + 2 of the row's 16 scales,
-// i.e. bytes 0 and 2 of scale word c.
+// i.e. bytes 0 and 2 of scale word c.  Scales are signed int8, converted
+// exactly through fp32.
 template <>
 struct AHdr<QW6F_Q6_K> {
     uint4 sc[2];
     uint32_t dd[2];
+    float d[2];
     __device__ __forceinline__ void load(const uint8_t* tb, int lane) {
         const int g = lane >> 2;
 #pragma unroll
@@ -197,9 +220,14 @@ struct AHdr<QW6F_Q6_K> {
             dd[rh] = ldg16(tb + 256 + (g + 8 * rh) * 2);
         }
     }
+    __device__ __forceinline__ void unpack() {
+#pragma unroll
+        for (int rh = 0; rh < 2; rh++) d[rh] = f16f(dd[rh]);
+    }
 };
 template <>
 struct ASlab<QW6F_Q6_K> {
+    static constexpr bool kPairShared = true;  // slabs 2m and 2m+1 read the same bytes (low/high nibbles)
     uint4 L[2];
     uint2 H[2];
     template <int C>
@@ -218,10 +246,12 @@ struct ASlab<QW6F_Q6_K> {
         const __nv_bfloat162 m160 = __floats2bfloat162_rn(-160.f, -160.f);  // -(128 + 32)
 #pragma unroll
         for (int rh = 0; rh < 2; rh++) {
-            const float d = f16f(hd.dd[rh]);
             const uint32_t scw = word_of(hd.sc[rh], C);
-            const __nv_bfloat162 d0 = __float2bfloat162_rn(d * (float)(int8_t)byte_of(scw, 0));
-            const __nv_bfloat162 d1 = __float2bfloat162_rn(d * (float)(int8_t)byte_of(scw, 2));
+            // signed bytes 0 and 2 -> fp32 exactly: (2^23 + 128 + s) - (2^23 + 128)
+            const float s0 = __uint_as_float(0x4b000000u | ((scw ^ 0x80u) & 0xffu)) - 8388736.f;
+            const float s1 = __uint_as_float(0x4b000000u | (((scw >> 16) ^ 0x80u) & 0xffu)) - 8388736.f;
+            const __nv_bfloat162 d0 = __float2bfloat162_rn(hd.d[rh] * s0);
+            const __nv_bfloat162 d1 = __float2bfloat162_rn(hd.d[rh] * s1);
             uint32_t v0[4], v1[4];
 #pragma unroll
             for (int hw = 0; hw < 2; hw++) {
@@ -234,13 +264,10 @@ struct ASlab<QW6F_Q6_K> {
                     q0 = ((A >> 4) & 0x0f0f0f0fu) | (Hh & 0x30303030u);
                     q1 = ((B >> 4) & 0x0f0f0f0fu) | ((Hh >> 2) & 0x30303030u);
                 }
-#pragma unroll
-                for (int p = 0; p < 2; p++) {
-                    const __nv_bfloat162 a = __hadd2(bf2_of(bf16_magic(spread_pair(q0, p))), m160);
-                    const __nv_bfloat162 b = __hadd2(bf2_of(bf16_magic(spread_pair(q1, p))), m160);
-                    v0[2 * hw + p] = bf2_bits(__hmul2(a, d0));
-                    v1[2 * hw + p] = bf2_bits(__hmul2(b, d1));
-                }
+                v0[2 * hw] = bf2_bits(__hmul2(__hadd2(bf2_of(bf16_pair<0, 1>(q0)), m160), d0));
+                v0[2 * hw + 1] = bf2_bits(__hmul2(__hadd2(bf2_of(bf16_pair<2, 3>(q0)), m160), d0));
+                v1[2 * hw] = bf2_bits(__hmul2(__hadd2(bf2_of(bf16_pair<0, 1>(q1)), m160), d1));
+                v1[2 * hw + 1] = bf2_bits(__hmul2(__hadd2(bf2_of(bf16_pair<2, 3>(q1)), m160), d1));
             }
             const uint32_t row = mi * 16 + g + 8 * rh;
             *reinterpret_cast<uint4*>(sa + sw128_off(row, t)) = make_uint4(v0[0], v0[1], v0[2], v0[3]);
@@ -287,6 +314,14 @@ struct BRows {
         for (int k = 0; k < R; k++)
             if (k < n) cp_async16(sb + dst[k], src[k] + C * 64, bytes[k]);
     }
+    __device__ __forceinline__ void issue_c(uint8_t* sb, int c) const {
+        switch (c) {
+        case 0: issue<0>(sb); break;
+        case 1: issue<1>(sb); break;
+        case 2: issue<2>(sb); break;
+        default: issue<3>(sb); break;
+        }
+    }
     __device__ __forceinline__ void next_block() {
 #pragma unroll
         for (int k = 0; k < R; k++) src[k] += 256;
@@ -308,7 +343,10 @@ __device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f 
 // MODE 1 (down): A0/A1 = down rows [256 ft, +128) / [256 ft + 128, +128),
 //   K = inter, B = H rows of the item's assignments; epilogue writes the
 //   per-assignment expert outputs (bf16) for the slot-order combine.
-// Warp-specialized, kPfStages shared-memory stages, one 64-wide K slab each:
+// Warp-specialized over a ring of shared-memory stages, one 64-wide K slab
+// each (two 128 x 64 A tiles + npad x 64 B rows).  The ring fills a fixed
+// shared-memory budget, so tiles with few tokens get more stages in flight
+// (3 at npad 256 ... 5 at npad <= 64):
 //   warps 0-15 (producers): wait stage empty; stream the slab's B rows with
 //     cp.async (arriving on the stage's full barrier when they land);
 //     dequantize A (warp w: 16-row m-tile w%8 of A(w/8)) from registers
@@ -318,7 +356,8 @@ __device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f 
 //     commit to the stage's empty barrier; at the end commit to `done`.
 // Every wait is time-bounded; on a timeout the error word is set, in-flight
 // copies and MMAs are drained and the CTA exits without an epilogue.
-constexpr int kPfStages = 3;
+constexpr int kPfMaxStages = 6;
+constexpr uint32_t kPfStageBudget = 200 * 1024;  // bytes of stages per CTA
 constexpr int kPfProducers = 512;
 constexpr int kPfThreads = kPfProducers + 32;
 constexpr int kPfMmaWarp = kPfProducers / 32;
@@ -327,9 +366,9 @@ template <int F, int MODE>
 __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    constexpr uint32_t A_BYTES = 128 * 128, B_BYTES = kPfChunk * 128, STAGE = 2 * A_BYTES + B_BYTES;
-    constexpr int TB = Fmt<F>::TB, S = kPfStages;
-    __shared__ uint64_t full[S], empty[S], done;
+    constexpr uint32_t A_BYTES = 128 * 128;
+    constexpr int TB = Fmt<F>::TB;
+    __shared__ uint64_t full[kPfMaxStages], empty[kPfMaxStages], done;
     __shared__ uint32_t tmem_base;
     __shared__ int rows[kPfChunk];
     const int K = MODE == 0 ? a.hidden : a.inter;
@@ -338,13 +377,15 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfArgs a) {
     if (item >= *a.nitems) return;
     const int4 it = a.items[item];
     const int e = it.x, off = it.y, cnt = it.z, npad = (cnt + 15) & ~15;
+    const uint32_t STAGE = 2 * A_BYTES + (uint32_t)npad * 128;  // multiple of 2 KB: atoms stay 1 KB aligned
+    const int S = min(kPfMaxStages, (int)(kPfStageBudget / STAGE));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int32_t* ord = a.order;  // null: the rows are already grouped by expert (sorted mode)
     for (int j = tid; j < cnt; j += blockDim.x)
         rows[j] = ord ? (MODE == 0 ? ord[off + j] / a.topk : ord[off + j]) : off + j;
     if (warp == kPfMmaWarp) tmem_alloc(&tmem_base, 512);
     if (tid == 0) {
-        for (int i = 0; i < S; i++) {
+        for (int i = 0; i < kPfMaxStages; i++) {
             mbar_init(&full[i], 2 * kPfProducers);  // one plain + one cp.async arrival per producer
             mbar_init(&empty[i], 1);
         }
@@ -374,78 +415,81 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfArgs a) {
         const uint8_t* tb = wbase + (size_t)(mt0 + mi) * nbk * TB;  // this warp's m-tile, K block 0
         BRows<kPfProducers> br;
         br.init(bsrc, K, rows, cnt, npad, tid);
-        // A fragments of slabs ks (even: ra, odd: rb) two slabs ahead; headers one K block ahead
-        ASlab<F> ra, rb;
+        // A fragments and headers one K block (four slabs) ahead: buffer c
+        // holds slab c of the block being stored, then slab c of the next one
+        ASlab<F> rq[4];
         AHdr<F> hc, hn;
         hc.load(tb, lane);
+        hc.unpack();
         hn = hc;
-        ra.template load<0>(tb, lane);
-        rb.template load<1>(tb, lane);
+        rq[0].template load<0>(tb, lane);
+        rq[2].template load<2>(tb, lane);
+        if (!ASlab<F>::kPairShared) {
+            rq[1].template load<1>(tb, lane);
+            rq[3].template load<3>(tb, lane);
+        }
+        int s = 0;          // stage of slab ks
+        uint32_t rnd = 0;   // how many times the ring has wrapped before slab ks
         for (int kb = 0; kb < nbk && ok; kb++) {
             const uint8_t* tbn = tb + TB;
             const bool more = kb + 1 < nbk;
+            if (more) hn.load(tbn, lane);
 #pragma unroll
             for (int c = 0; c < 4; c++) {
-                const int ks = kb * 4 + c, s = ks % S;
-                if (ks >= S && !mbar_wait(&empty[s], ((ks / S) - 1) & 1, a.err, 31 + MODE)) {
+                if (c > 0 && ++s == S) {
+                    s = 0;
+                    rnd++;
+                }
+                // stage reuse: wait for the MMAs of this stage's previous round
+                if (rnd > 0 && !mbar_wait(&empty[s], (rnd - 1) & 1, a.err, 31 + MODE)) {
                     ok = false;
                     break;
                 }
                 uint8_t* st = smem + s * STAGE;
                 uint8_t* sa = st + mtx * A_BYTES;
-                switch (c) {  // c is a compile-time constant after unrolling
+                br.template issue_c(st + 2 * A_BYTES, c);
+                cp_async_arrive_noinc(&full[s]);
+                constexpr bool share = ASlab<F>::kPairShared;
+                // c is a compile-time constant after unrolling; with shared pairs
+                // slab c reads buffer c & ~1, refilled after its second slab
+                switch (c) {
                 case 0:
-                    br.template issue<0>(st + 2 * A_BYTES);
-                    cp_async_arrive_noinc(&full[s]);
-                    ra.template store<0>(sa, hc, mi, lane);
+                    rq[0].template store<0>(sa, hc, mi, lane);
+                    if (!share && more) rq[0].template load<0>(tbn, lane);
                     break;
                 case 1:
-                    br.template issue<1>(st + 2 * A_BYTES);
-                    cp_async_arrive_noinc(&full[s]);
-                    rb.template store<1>(sa, hc, mi, lane);
+                    rq[share ? 0 : 1].template store<1>(sa, hc, mi, lane);
+                    if (more) rq[share ? 0 : 1].template load<(share ? 0 : 1)>(tbn, lane);
                     break;
                 case 2:
-                    br.template issue<2>(st + 2 * A_BYTES);
-                    cp_async_arrive_noinc(&full[s]);
-                    ra.template store<2>(sa, hc, mi, lane);
+                    rq[2].template store<2>(sa, hc, mi, lane);
+                    if (!share && more) rq[2].template load<2>(tbn, lane);
                     break;
                 default:
-                    br.template issue<3>(st + 2 * A_BYTES);
-                    cp_async_arrive_noinc(&full[s]);
-                    rb.template store<3>(sa, hc, mi, lane);
+                    rq[share ? 2 : 3].template store<3>(sa, hc, mi, lane);
+                    if (more) rq[share ? 2 : 3].template load<(share ? 2 : 3)>(tbn, lane);
                     break;
                 }
                 fence_async_smem();
                 mbar_arrive(&full[s]);
-                switch (c) {  // refill the buffer just consumed with slab ks + 2
-                case 0:
-                    ra.template load<2>(tb, lane);
-                    break;
-                case 1:
-                    rb.template load<3>(tb, lane);
-                    break;
-                case 2:
-                    if (more) {
-                        hn.load(tbn, lane);
-                        ra.template load<0>(tbn, lane);
-                    }
-                    break;
-                default:
-                    if (more) rb.template load<1>(tbn, lane);
-                    break;
-                }
             }
             hc = hn;
+            hc.unpack();
             tb = tbn;
             br.next_block();
+            if (++s == S) {  // advance to the stage of the next block's slab 0
+                s = 0;
+                rnd++;
+            }
         }
         cp_async_wait_all();
     } else if (lane == 0) {
         // ------------------------------------------------- MMA issuer ----
         const uint32_t idesc = umma_idesc_bf16(128, npad);
-        for (int ks = 0; ks < nk; ks++) {
-            const int s = ks % S;
-            if (!mbar_wait(&full[s], (ks / S) & 1, a.err, 35 + MODE)) {
+        int s = 0;
+        uint32_t rnd = 0;
+        for (int ks = 0; ks < nk; ks++, s = (s + 1 == S) ? 0 : s + 1, rnd += (s == 0)) {
+            if (!mbar_wait(&full[s], rnd & 1, a.err, 35 + MODE)) {
                 ok = false;
                 break;
             }
@@ -588,7 +632,7 @@ static int pf_args(const qw6k_moe_desc* d, int* err, PfArgs& a) {
 
 template <int F, int MODE>
 static int launch_pf(const PfArgs& a, int mi, cudaStream_t st) {
-    const size_t smem = (size_t)kPfStages * (2 * 128 * 128 + kPfChunk * 128) + 1024;
+    const size_t smem = (size_t)kPfStageBudget + 1024;
     static bool cfg = false;
     if (!cfg && cudaFuncSetAttribute(k_pf_gemm<F, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
                     cudaSuccess)
