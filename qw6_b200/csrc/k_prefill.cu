@@ -447,7 +447,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfArgs a) {
                 }
                 uint8_t* st = smem + s * STAGE;
                 uint8_t* sa = st + mtx * A_BYTES;
-                br.template issue_c(st + 2 * A_BYTES, c);
+                br.issue_c(st + 2 * A_BYTES, c);
                 cp_async_arrive_noinc(&full[s]);
                 constexpr bool share = ASlab<F>::kPairShared;
                 // c is a compile-time constant after unrolling; with shared pairs
