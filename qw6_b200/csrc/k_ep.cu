@@ -97,8 +97,9 @@ __global__ void k_ep_combine(const __nv_bfloat16* __restrict__ ret, const float*
 // ------------------------------------------------ peer-memory EP layer --
 // One layer of expert parallelism without host round trips: the count
 // exchange, the dispatch of token rows into the owners' receive buffers and
-// the combine's reads of the owners' expert outputs all go through peer
-// memory (NVLink), ordered by epoch-stamped signal words.  Receive rows are
+// the owners' down GEMM writing each output row back into its source's
+// memory all go through peer memory (NVLink), ordered by epoch-stamped
+// signal words; the combine then reads only local memory.  Receive rows are
 // laid out by (local expert, source rank), so each owner's rows for an
 // expert are contiguous and the grouped GEMM runs in sorted mode.  Buffers
 // are reused across steps without extra barriers: a source writes step i+1
@@ -218,7 +219,11 @@ __global__ void __launch_bounds__(256) k_ep_dispatch(const qw6k_ep_desc d) {
         uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(d.peers[owner] + d.o_rx) +
                                               (size_t)row * d.hidden);
         for (int i = lane; i < (int)d.hidden / 8; i += 32) dst[i] = src[i];
-        if (lane == 0) d.send_row[a] = row;
+        if (lane == 0) {
+            d.send_row[a] = row;
+            // where the owner's down GEMM must deliver this row's output
+            reinterpret_cast<int32_t*>(d.peers[owner] + d.o_sdst)[row] = (int)(d.rank * d.nmax) + a;
+        }
     }
     __threadfence_system();
     __syncthreads();
@@ -244,19 +249,17 @@ __global__ void k_ep_signal_done(const qw6k_ep_desc d) {
     if (threadIdx.x < d.world) st_release_sys(ep_sig(d, threadIdx.x, QW6K_EP_SIG_DONE, d.rank), *d.epoch);
 }
 
-// phase 5: out[t] = sum_k w * dout_owner[send_row] (fp32 fma, slot order),
-// reading the owners' outputs over peer memory
-__global__ void k_ep_combine_p2p(const qw6k_ep_desc d) {
+// phase 5: out[t] = sum_k w[a] * ret[a] (fp32 fma, slot order); the owners
+// have written each assignment's bf16 output into this rank's ret
+__global__ void k_ep_combine_ret(const qw6k_ep_desc d) {
     const int t = blockIdx.y, f = (blockIdx.x * blockDim.x + threadIdx.x) * 2;
     if (f >= (int)d.hidden || *d.abort) return;
-    const int topk = (int)d.topk, epr = (int)(d.ne / d.world);
+    const int topk = (int)d.topk;
+    const __nv_bfloat16* ret = reinterpret_cast<const __nv_bfloat16*>(d.peers[d.rank] + d.o_ret);
     float o0 = 0.f, o1 = 0.f;
     for (int k = 0; k < topk; k++) {
         const size_t a = (size_t)t * topk + k;
-        const int owner = d.idx[a] / epr;
-        const __nv_bfloat16* src =
-            reinterpret_cast<const __nv_bfloat16*>(d.peers[owner] + d.o_dout) + (size_t)d.send_row[a] * d.hidden + f;
-        const unsigned int bits = __ldcg(reinterpret_cast<const unsigned int*>(src));
+        const unsigned int bits = __ldcg(reinterpret_cast<const unsigned int*>(ret + a * d.hidden + f));
         const float wk = d.w[a];
         o0 = fmaf(wk, __uint_as_float(bits << 16), o0);
         o1 = fmaf(wk, __uint_as_float(bits & 0xffff0000u), o1);
@@ -308,7 +311,7 @@ extern "C" int qw6k_ep_p2p_phase(const qw6k_ep_desc* d, int phase, cudaStream_t 
     if (!d || !d->peers || !d->world || d->world > QW6K_EP_MAX_WORLD || d->rank >= d->world || !d->ne ||
         d->ne > 256 || d->ne % d->world || !d->topk || !d->ntok || !d->hidden || d->hidden % 8 || !d->epoch ||
         !d->abort || !d->done_ctas || !d->err || !d->idx || !d->w || !d->cnt_self || !d->pos || !d->sendoff ||
-        !d->local_cnt || !d->send_row || !d->x || !d->out || !d->cap)
+        !d->local_cnt || !d->send_row || !d->x || !d->out || !d->cap || !d->nmax || d->ntok * d->topk > d->nmax)
         return QW6K_ERR_ARG;
     switch (phase) {
     case 0:
@@ -328,7 +331,7 @@ extern "C" int qw6k_ep_p2p_phase(const qw6k_ep_desc* d, int phase, cudaStream_t 
         break;
     case 5: {
         dim3 g((d->hidden / 2 + 255) / 256, d->ntok);
-        k_ep_combine_p2p<<<g, 256, 0, st>>>(*d);
+        k_ep_combine_ret<<<g, 256, 0, st>>>(*d);
         break;
     }
     default:

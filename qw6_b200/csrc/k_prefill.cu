@@ -47,6 +47,10 @@ struct PfArgs {
     int32_t* order;
     __nv_bfloat16* h;     // [TK][inter]  silu(gate)*up per assignment
     __nv_bfloat16* dout;  // [TK][hidden] expert output per assignment
+    uint8_t* const* out_peers;  // push mode: outputs go to other GPUs (see qw6k_moe_desc)
+    size_t out_off;
+    const int32_t* slot_dst;
+    int out_rows;
     int* err;
 };
 
@@ -371,6 +375,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfArgs a) {
     __shared__ uint64_t full[kPfMaxStages], empty[kPfMaxStages], done;
     __shared__ uint32_t tmem_base;
     __shared__ int rows[kPfChunk];
+    __shared__ __nv_bfloat16* drow[MODE == 1 ? kPfChunk : 1];  // push mode: output row pointers
     const int K = MODE == 0 ? a.hidden : a.inter;
     const int nft = MODE == 0 ? a.inter / 128 : a.hidden / 256;
     const int item = blockIdx.x / nft, ft = blockIdx.x % nft;
@@ -381,8 +386,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfArgs a) {
     const int S = min(kPfMaxStages, (int)(kPfStageBudget / STAGE));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int32_t* ord = a.order;  // null: the rows are already grouped by expert (sorted mode)
-    for (int j = tid; j < cnt; j += blockDim.x)
+    for (int j = tid; j < cnt; j += blockDim.x) {
         rows[j] = ord ? (MODE == 0 ? ord[off + j] / a.topk : ord[off + j]) : off + j;
+        if (MODE == 1 && a.out_peers) {
+            const int sd = a.slot_dst[off + j], src = sd / a.out_rows;
+            drow[MODE == 1 ? j : 0] = reinterpret_cast<__nv_bfloat16*>(a.out_peers[src] + a.out_off) +
+                                      (size_t)(sd - src * a.out_rows) * a.hidden;
+        }
+    }
     if (warp == kPfMmaWarp) tmem_alloc(&tmem_base, 512);
     if (tid == 0) {
         for (int i = 0; i < kPfMaxStages; i++) {
@@ -531,13 +542,15 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfArgs a) {
 #pragma unroll
                 for (int j = 0; j < 16; j++)
                     if (c0 + j < cnt) {
-                        __nv_bfloat16* o = a.dout + (size_t)rows[c0 + j] * a.hidden + f;
+                        __nv_bfloat16* o =
+                            (a.out_peers ? drow[MODE == 1 ? c0 + j : 0] : a.dout + (size_t)rows[c0 + j] * a.hidden) + f;
                         o[0] = __float2bfloat16_rn(v0[j]);
                         o[128] = __float2bfloat16_rn(v1[j]);
                     }
             }
         }
     }
+    if (MODE == 1 && a.out_peers) __threadfence_system();  // pushed rows visible before the layer signals
     tc_fence_before();
     __syncthreads();
     if (warp == kPfMmaWarp) tmem_dealloc(tmem, 512);
@@ -577,7 +590,9 @@ extern "C" size_t qw6k_moe_prefill_ws_bytes(uint32_t ntok, uint32_t hidden, uint
 static int pf_args(const qw6k_moe_desc* d, int* err, PfArgs& a) {
     const bool rows_mode = d && !d->logits;
     const bool sorted = rows_mode && d->expert_counts;
-    if (rows_mode && (d->topk != 1 || (!d->row_expert && !sorted) || !d->dout)) return QW6K_ERR_ARG;
+    const bool push = sorted && d->out_peers;
+    if (rows_mode && (d->topk != 1 || (!d->row_expert && !sorted) || (!d->dout && !push))) return QW6K_ERR_ARG;
+    if (push && (!d->slot_dst || !d->out_rows)) return QW6K_ERR_ARG;
     if (!d || !d->gate || !d->up || !d->down || !d->x || (!d->out && !rows_mode) || !d->ws || !err || !d->ntok ||
         !d->ne || d->ne > 256 || !d->topk || d->topk > 32 || d->topk > d->ne || (size_t)d->ntok * d->topk > (1u << 22))
         return QW6K_ERR_ARG;
@@ -618,10 +633,21 @@ static int pf_args(const qw6k_moe_desc* d, int* err, PfArgs& a) {
     a.nitems = (int*)p; p += 256;
     a.h = (__nv_bfloat16*)p; p += al256(tk * d->inter * 2);
     a.dout = (__nv_bfloat16*)p;
+    a.out_peers = nullptr;
+    a.out_off = 0;
+    a.slot_dst = nullptr;
+    a.out_rows = 0;
     if (rows_mode) {  // caller-supplied routing; expert outputs into the caller's buffer
         if (reinterpret_cast<uintptr_t>(d->dout) & 15u) return QW6K_ERR_ALIGN;
         a.idx = const_cast<int32_t*>(d->row_expert);
         a.dout = (__nv_bfloat16*)d->dout;
+    }
+    if (push) {
+        if (d->out_off & 15u) return QW6K_ERR_ALIGN;
+        a.out_peers = d->out_peers;
+        a.out_off = d->out_off;
+        a.slot_dst = d->slot_dst;
+        a.out_rows = (int)d->out_rows;
     }
     if (sorted) {  // rows grouped by expert in expert order, expert_counts[e] rows each
         a.cnt = const_cast<int32_t*>(d->expert_counts);

@@ -3,8 +3,10 @@
  * One qw6cu_ep per rank (one process per GPU).  It owns:
  *   - a symmetric region (one cudaMalloc, identical layout on every rank):
  *     signal words, the double-buffered [2][world][ne] count matrix, the
- *     receive rows rx [cap][hidden] bf16 and the expert outputs dout
- *     [cap][hidden] bf16, cap = world * max_tokens * top_k;
+ *     receive rows rx [cap][hidden] bf16 with the destination of each
+ *     row's output, and ret [max_tokens * top_k][hidden] bf16, where the
+ *     owners' down GEMM writes this rank's expert outputs;
+ *     cap = world * max_tokens * top_k;
  *   - private buffers: step epoch, abort and dispatch-counter words, routing,
  *     per-expert counts/positions, send offsets and rows, and the grouped
  *     GEMM workspace.
@@ -13,8 +15,9 @@
  * qw6cu_ep_layer then enqueues the whole layer on the context's stream with
  * no host synchronisation (so it can be captured in a CUDA graph):
  *   route -> count -> publish counts / plan -> dispatch rows -> wait rows ->
- *   grouped GEMMs over the received rows (sorted mode) -> signal outputs ->
- *   wait outputs -> combine with peer reads.
+ *   grouped GEMMs over the received rows (sorted mode; the down GEMM writes
+ *   every output row straight into its source's ret) -> signal outputs ->
+ *   wait outputs -> local combine.
  */
 #include <stdint.h>
 #include <stdlib.h>
@@ -30,7 +33,7 @@ struct qw6cu_ep {
     qw6cu_ctx *ctx;
     uint32_t rank, world, ne, epr, topk, hidden, inter, max_tok, cap;
     uint8_t *region;
-    size_t region_bytes, o_sig, o_cnt, o_rx, o_dout;
+    size_t region_bytes, o_sig, o_cnt, o_rx, o_sdst, o_ret;
     uint8_t *peer_host[QW6K_EP_MAX_WORLD];
     int opened[QW6K_EP_MAX_WORLD];
     int connected;
@@ -80,8 +83,9 @@ int qw6cu_ep_create(qw6cu_ctx *ctx, uint32_t rank, uint32_t world, uint32_t n_ex
     ep->o_sig = 0;
     ep->o_cnt = al256(3 * QW6K_EP_MAX_WORLD * sizeof(uint32_t));
     ep->o_rx = ep->o_cnt + al256((size_t)2 * world * n_experts * sizeof(int32_t));
-    ep->o_dout = ep->o_rx + al256((size_t)ep->cap * hidden * 2);
-    ep->region_bytes = ep->o_dout + al256((size_t)ep->cap * hidden * 2);
+    ep->o_sdst = ep->o_rx + al256((size_t)ep->cap * hidden * 2);
+    ep->o_ret = ep->o_sdst + al256((size_t)ep->cap * 4);
+    ep->region_bytes = ep->o_ret + al256(n * hidden * 2);
     cudaError_t e = cudaMalloc((void **)&ep->region, ep->region_bytes);
     if (e != cudaSuccess) {
         free(ep);
@@ -207,7 +211,9 @@ int qw6cu_ep_layer(qw6cu_ep *ep, const qw6cu_expert_pack *gate, const qw6cu_expe
     d.o_sig = ep->o_sig;
     d.o_cnt = ep->o_cnt;
     d.o_rx = ep->o_rx;
-    d.o_dout = ep->o_dout;
+    d.o_sdst = ep->o_sdst;
+    d.o_ret = ep->o_ret;
+    d.nmax = (uint32_t)(ep->max_tok * ep->topk);
     d.rank = ep->rank;
     d.world = ep->world;
     d.ne = ep->ne;
@@ -245,7 +251,10 @@ int qw6cu_ep_layer(qw6cu_ep *ep, const qw6cu_expert_pack *gate, const qw6cu_expe
     m.inter = ep->inter;
     m.ne = ep->epr;
     m.topk = 1;
-    m.dout = ep->region + ep->o_dout;
+    m.out_peers = (uint8_t *const *)ep->peers_dev;
+    m.out_off = ep->o_ret;
+    m.slot_dst = (const int32_t *)(ep->region + ep->o_sdst);
+    m.out_rows = ep->max_tok * ep->topk;
     m.expert_counts = ep->local_cnt;
     m.ws = ep->ws;
     m.ws_bytes = ep->ws_bytes;

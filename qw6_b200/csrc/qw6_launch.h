@@ -97,6 +97,13 @@ typedef struct {
     /* sorted rows mode (rows mode with row_expert == NULL): the rows of x are
      * grouped by expert in expert order, expert_counts[e] (device) rows each */
     const int32_t *expert_counts;
+    /* push mode (sorted rows, dout == NULL): the expert output of row r goes
+     * to out_peers[s] + out_off + q * hidden * 2 bytes (bf16 row), where
+     * slot_dst[r] = s * out_rows + q -- another GPU's memory over NVLink */
+    uint8_t *const *out_peers;
+    size_t out_off;
+    const int32_t *slot_dst;
+    uint32_t out_rows;
 } qw6k_moe_desc;
 
 size_t qw6k_moe_ws_bytes(uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t ne, uint32_t topk);
@@ -125,15 +132,17 @@ int qw6k_ep_combine(const void *ret_bf16, const float *w, const int32_t *send_po
 /* Expert parallelism over peer memory (k_ep.cu, phases of one layer).
  * Every rank holds one symmetric region with the same layout: signal words
  * (3 kinds x 64 sources, u32 epochs), a double-buffered count matrix
- * [2][world][ne] (i32), received token rows rx [cap][hidden] (bf16) and
- * expert outputs dout [cap][hidden] (bf16); peers[p] is rank p's region as
- * mapped in this process. */
+ * [2][world][ne] (i32), received token rows rx [cap][hidden] (bf16), the
+ * destination of each received row's output sdst [cap] (i32: source rank *
+ * nmax + source assignment) and the returned expert outputs of this rank's
+ * own assignments ret [nmax][hidden] (bf16, written by the owners' down
+ * GEMM); peers[p] is rank p's region as mapped in this process. */
 #define QW6K_EP_MAX_WORLD 64
 enum { QW6K_EP_SIG_COUNTS = 0, QW6K_EP_SIG_ROWS = 1, QW6K_EP_SIG_DONE = 2 };
 typedef struct {
     uint8_t *const *peers; /* device array [world] */
-    size_t o_sig, o_cnt, o_rx, o_dout;
-    uint32_t rank, world, ne, topk, hidden, ntok, cap;
+    size_t o_sig, o_cnt, o_rx, o_sdst, o_ret;
+    uint32_t rank, world, ne, topk, hidden, ntok, cap, nmax;
     uint32_t *epoch;     /* private: step counter (phase 0 increments it) */
     int *abort;          /* private: set once any wait gives up; later phases do nothing */
     uint32_t *done_ctas; /* private: dispatch completion counter */
@@ -148,8 +157,8 @@ typedef struct {
     float *out;          /* fp32 [ntok][hidden] */
 } qw6k_ep_desc;
 /* phases: 0 publish counts + wait + plan, 1 dispatch rows + signal,
- * 2 wait for all rows, 3 signal outputs ready, 4 wait for all outputs,
- * 5 combine (peer reads) */
+ * 2 wait for all rows, 3 signal outputs delivered, 4 wait for all outputs,
+ * 5 combine (local reads of ret) */
 int qw6k_ep_p2p_phase(const qw6k_ep_desc *d, int phase, cudaStream_t st);
 
 /* Fixed 1 MiB device scratch (k_static.cu) of the allocation-free MoE entry
