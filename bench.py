@@ -295,11 +295,16 @@ def ep_bench(args, torch, ctx, L, stream, rank, world, dist):
     ctx.check_device_errors()
     del full, tail
 
-    # one profiled eager step: per-kernel device time and launch count
-    with torch.cuda.stream(stream):
-        ctx.profile_begin(64)
-        step(0)
-        prof = ctx.profile_end()
+    # per-kernel device time from a separately captured graph of G steps
+    # (event nodes around every launch), replayed twice; per-step averages
+    ctx.profile_begin(32 * G + 8)
+    pg = capture(G)
+    for _ in range(2):
+        with torch.cuda.stream(stream):
+            pg.replay()
+        torch.cuda.synchronize()
+    prof = {k: (ms_ / G, n // G) for k, (ms_, n) in ctx.profile_end().items()}
+    del pg
     rows = pm.last_rows() if pm is not None else tpr * TOPK
 
     # end to end: this step's logits/x from pinned host memory, output read back

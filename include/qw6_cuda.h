@@ -275,7 +275,7 @@ void qw6cu_ep_destroy(qw6cu_ep *ep);
  * begin: allocate events for up to max_launches launches and start
  * recording; end: synchronize, then write per-kernel-id total milliseconds
  * and launch counts into arrays of QW6CU_NKERNELS entries and stop. */
-#define QW6CU_NKERNELS 15
+#define QW6CU_NKERNELS 19
 int qw6cu_profile_begin(qw6cu_ctx *ctx, uint32_t max_launches);
 int qw6cu_profile_end(qw6cu_ctx *ctx, double *ms_total, uint32_t *launches);
 const char *qw6cu_kernel_name(int kernel_id);

@@ -147,11 +147,35 @@ __device__ bool ep_wait_all(const qw6k_ep_desc& d, int kind, uint32_t ep) {
     return __syncthreads_and(ok);
 }
 
-// phase 0 (1 CTA x 256): stamp the step, publish this rank's per-expert
-// counts into every rank's matrix, wait for all sources, then plan:
-//   colsum[g]  = rows of global expert g over all sources,
+// phase 6 (runs first; counters zeroed by the launcher), thread per token:
+// per global expert counts and positions, and per owner the unique token
+// rows -- a token whose experts share an owner sends its row there once
+// (upos >= 0 on its first such slot, -1 - position on the later ones).
+__global__ void k_ep_count_u(const qw6k_ep_desc d) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= (int)d.ntok) return;
+    const int topk = (int)d.topk, epr = (int)(d.ne / d.world);
+    const int32_t* ix = d.idx + (size_t)t * topk;
+    for (int k = 0; k < topk; k++) {
+        const int a = t * topk + k, g = ix[k], own = g / epr;
+        d.pos[a] = atomicAdd(&d.cnt_self[g], 1);
+        int first = k;
+        for (int j = 0; j < k; j++)
+            if (ix[j] / epr == own) {
+                first = j;
+                break;
+            }
+        d.upos[a] = first == k ? atomicAdd(&d.ucnt[own], 1) : -1 - d.upos[t * topk + first];
+    }
+}
+
+// phase 0 (1 CTA x 256): stamp the step, publish this rank's per-expert and
+// per-owner unique-row counts into every rank's matrix, wait for all
+// sources, then plan:
+//   colsum[g]  = slots of global expert g over all sources,
 //   base[g]    = exclusive prefix of colsum inside g's owner block,
-//   sendoff[g] = base[g] + rows for g from sources < this rank,
+//   sendoff[g] = base[g] + slots for g from sources < this rank,
+//   ubase[o]   = unique rows sent to owner o by sources < this rank,
 //   local_cnt  = colsum over this rank's own experts.
 __global__ void __launch_bounds__(256) k_ep_publish(const qw6k_ep_desc d) {
     __shared__ uint32_t s_ep;
@@ -167,9 +191,10 @@ __global__ void __launch_bounds__(256) k_ep_publish(const qw6k_ep_desc d) {
         if (tid < epr) d.local_cnt[tid] = 0;
         return;
     }
+    const int L = ne + (int)d.world;  // matrix row: per-expert counts, then per-owner unique rows
     for (uint32_t p = 0; p < d.world; p++) {
-        int32_t* m = reinterpret_cast<int32_t*>(d.peers[p] + d.o_cnt) + ((size_t)par * d.world + d.rank) * ne;
-        for (int g = tid; g < ne; g += blockDim.x) m[g] = d.cnt_self[g];
+        int32_t* m = reinterpret_cast<int32_t*>(d.peers[p] + d.o_cnt) + ((size_t)par * d.world + d.rank) * L;
+        for (int g = tid; g < L; g += blockDim.x) m[g] = g < ne ? d.cnt_self[g] : d.ucnt[g - ne];
     }
     __threadfence_system();
     __syncthreads();
@@ -178,15 +203,28 @@ __global__ void __launch_bounds__(256) k_ep_publish(const qw6k_ep_desc d) {
         if (tid < epr) d.local_cnt[tid] = 0;
         return;
     }
-    const int32_t* mine = reinterpret_cast<const int32_t*>(d.peers[d.rank] + d.o_cnt) + (size_t)par * d.world * ne;
+    const int32_t* mine = reinterpret_cast<const int32_t*>(d.peers[d.rank] + d.o_cnt) + (size_t)par * d.world * L;
     int cs = 0, before = 0;
     if (tid < ne) {
         for (uint32_t s = 0; s < d.world; s++) {
-            const int v = __ldcg(mine + (size_t)s * ne + tid);
+            const int v = __ldcg(mine + (size_t)s * L + tid);
             cs += v;
             if (s < d.rank) before += v;
         }
         colsum[tid] = cs;
+    }
+    if (tid < (int)d.world) {  // unique rows: this rank's base at owner tid, and owner tid's total
+        int ub = 0, tot = 0;
+        for (uint32_t s = 0; s < d.world; s++) {
+            const int v = __ldcg(mine + (size_t)s * L + ne + tid);
+            if (s < d.rank) ub += v;
+            tot += v;
+        }
+        d.ubase[tid] = ub;
+        if (tot > (int)d.cap) {  // no owner may receive more rows than its buffer holds
+            atomicExch(d.err, 44);
+            atomicExch(d.abort, 1);
+        }
     }
     __syncthreads();
     if (tid < ne) {
@@ -213,16 +251,20 @@ __global__ void __launch_bounds__(256) k_ep_dispatch(const qw6k_ep_desc d) {
     const bool go = !*d.abort;
     const int a = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (go && a < n) {
-        const int g = d.idx[a], owner = g / epr, row = d.sendoff[g] + d.pos[a];
-        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(d.x) +
-                                                          (size_t)(a / (int)d.topk) * d.hidden);
-        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(d.peers[owner] + d.o_rx) +
-                                              (size_t)row * d.hidden);
-        for (int i = lane; i < (int)d.hidden / 8; i += 32) dst[i] = src[i];
+        const int g = d.idx[a], owner = g / epr, slot = d.sendoff[g] + d.pos[a], up = d.upos[a];
+        const int urow = d.ubase[owner] + (up >= 0 ? up : -1 - up);
+        if (up >= 0) {  // first slot of this token at this owner: send the row
+            const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(d.x) +
+                                                              (size_t)(a / (int)d.topk) * d.hidden);
+            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(d.peers[owner] + d.o_rx) +
+                                                  (size_t)urow * d.hidden);
+            for (int i = lane; i < (int)d.hidden / 8; i += 32) dst[i] = src[i];
+        }
         if (lane == 0) {
-            d.send_row[a] = row;
-            // where the owner's down GEMM must deliver this row's output
-            reinterpret_cast<int32_t*>(d.peers[owner] + d.o_sdst)[row] = (int)(d.rank * d.nmax) + a;
+            d.send_row[a] = slot;
+            // the slot's token row at the owner, and where its output goes
+            reinterpret_cast<int32_t*>(d.peers[owner] + d.o_sbrow)[slot] = urow;
+            reinterpret_cast<int32_t*>(d.peers[owner] + d.o_sdst)[slot] = (int)(d.rank * d.nmax) + a;
         }
     }
     __threadfence_system();
@@ -311,9 +353,16 @@ extern "C" int qw6k_ep_p2p_phase(const qw6k_ep_desc* d, int phase, cudaStream_t 
     if (!d || !d->peers || !d->world || d->world > QW6K_EP_MAX_WORLD || d->rank >= d->world || !d->ne ||
         d->ne > 256 || d->ne % d->world || !d->topk || !d->ntok || !d->hidden || d->hidden % 8 || !d->epoch ||
         !d->abort || !d->done_ctas || !d->err || !d->idx || !d->w || !d->cnt_self || !d->pos || !d->sendoff ||
-        !d->local_cnt || !d->send_row || !d->x || !d->out || !d->cap || !d->nmax || d->ntok * d->topk > d->nmax)
+        !d->local_cnt || !d->send_row || !d->x || !d->out || !d->cap || !d->nmax || d->ntok * d->topk > d->nmax ||
+        !d->ucnt || !d->upos || !d->ubase)
         return QW6K_ERR_ARG;
     switch (phase) {
+    case 6:
+        if (cudaMemsetAsync(d->cnt_self, 0, d->ne * sizeof(int32_t), st) != cudaSuccess ||
+            cudaMemsetAsync(d->ucnt, 0, d->world * sizeof(int32_t), st) != cudaSuccess)
+            return QW6K_ERR_CUDA;
+        k_ep_count_u<<<(d->ntok + 127) / 128, 128, 0, st>>>(*d);
+        break;
     case 0:
         k_ep_publish<<<1, 256, 0, st>>>(*d);
         break;

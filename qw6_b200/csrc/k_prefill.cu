@@ -47,6 +47,7 @@ struct PfArgs {
     int32_t* order;
     __nv_bfloat16* h;     // [TK][inter]  silu(gate)*up per assignment
     __nv_bfloat16* dout;  // [TK][hidden] expert output per assignment
+    const int32_t* slot_row;    // sorted mode: x row of each slot (null: identity)
     uint8_t* const* out_peers;  // push mode: outputs go to other GPUs (see qw6k_moe_desc)
     size_t out_off;
     const int32_t* slot_dst;
@@ -387,7 +388,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfArgs a) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int32_t* ord = a.order;  // null: the rows are already grouped by expert (sorted mode)
     for (int j = tid; j < cnt; j += blockDim.x) {
-        rows[j] = ord ? (MODE == 0 ? ord[off + j] / a.topk : ord[off + j]) : off + j;
+        rows[j] = ord ? (MODE == 0 ? ord[off + j] / a.topk : ord[off + j])
+                      : (MODE == 0 && a.slot_row ? a.slot_row[off + j] : off + j);
         if (MODE == 1 && a.out_peers) {
             const int sd = a.slot_dst[off + j], src = sd / a.out_rows;
             drow[MODE == 1 ? j : 0] = reinterpret_cast<__nv_bfloat16*>(a.out_peers[src] + a.out_off) +
@@ -522,35 +524,59 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfArgs a) {
     ok = __syncthreads_and(ok);
     tc_fence_after();
     if (ok && warp < kPfMmaWarp) {
-        // warp w reads TMEM lanes 32 (w % 4) .. +31 and every (kPfMmaWarp/4)-th 16-column group
+        // Warp w reads TMEM lanes 32 (w % 4) .. +31 (its 32 features of each
+        // accumulator) for every (kPfMmaWarp/4)-th group of 16 token columns,
+        // stages them token-major in its own 2 KB of the (now idle) stage
+        // memory and writes 16-byte pieces of the output rows.
         constexpr int NG = kPfMmaWarp / 4;
         const int wq = warp & 3, wg = warp >> 2;
         const uint32_t lrow = (uint32_t)(wq * 32) << 16;
+        __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(smem + warp * 2048);  // [16 tokens][64]
         for (int c0 = wg * 16; c0 < npad; c0 += 16 * NG) {
             float v0[16], v1[16];
             tmem_ld16(tmem + lrow + (uint32_t)c0, v0);
             tmem_ld16(tmem + lrow + 256u + (uint32_t)c0, v1);
             if (MODE == 0) {
-                const int f = ft * 128 + wq * 32 + lane;
 #pragma unroll
-                for (int j = 0; j < 16; j++)
-                    if (c0 + j < cnt)
-                        a.h[(size_t)(ord ? ord[off + c0 + j] : off + c0 + j) * a.inter + f] =
-                            __float2bfloat16_rn(silu_fast(v0[j]) * v1[j]);
-            } else {
-                const int f = 2 * ft * 128 + wq * 32 + lane;
+                for (int j = 0; j < 16; j++) stg[j * 64 + lane] = __float2bfloat16_rn(silu_fast(v0[j]) * v1[j]);
+                __syncwarp();
+                // 16 tokens x 64 B: lane writes pieces (token idx/4, quarter idx%4) for idx = lane, lane + 32
 #pragma unroll
-                for (int j = 0; j < 16; j++)
+                for (int it = 0; it < 2; it++) {
+                    const int idx = it * 32 + lane, j = idx >> 2, q = idx & 3;
                     if (c0 + j < cnt) {
-                        __nv_bfloat16* o =
-                            (a.out_peers ? drow[MODE == 1 ? c0 + j : 0] : a.dout + (size_t)rows[c0 + j] * a.hidden) + f;
-                        o[0] = __float2bfloat16_rn(v0[j]);
-                        o[128] = __float2bfloat16_rn(v1[j]);
+                        const uint4 v = *reinterpret_cast<const uint4*>(stg + j * 64 + q * 8);
+                        __nv_bfloat16* o = a.h + (size_t)(ord ? ord[off + c0 + j] : off + c0 + j) * a.inter +
+                                           ft * 128 + wq * 32 + q * 8;
+                        *reinterpret_cast<uint4*>(o) = v;
                     }
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    stg[j * 64 + lane] = __float2bfloat16_rn(v0[j]);
+                    stg[j * 64 + 32 + lane] = __float2bfloat16_rn(v1[j]);
+                }
+                __syncwarp();
+                // 16 tokens x 2 halves x 64 B: piece (token, half, quarter) per idx
+#pragma unroll
+                for (int it = 0; it < 4; it++) {
+                    const int idx = it * 32 + lane, j = idx >> 3, h = (idx >> 2) & 1, q = idx & 3;
+                    if (c0 + j < cnt) {
+                        const uint4 v = *reinterpret_cast<const uint4*>(stg + j * 64 + h * 32 + q * 8);
+                        __nv_bfloat16* o = (a.out_peers ? drow[MODE == 1 ? c0 + j : 0]
+                                                        : a.dout + (size_t)rows[c0 + j] * a.hidden) +
+                                           2 * ft * 128 + h * 128 + wq * 32 + q * 8;
+                        *reinterpret_cast<uint4*>(o) = v;
+                    }
+                }
             }
+            __syncwarp();
         }
     }
-    if (MODE == 1 && a.out_peers) __threadfence_system();  // pushed rows visible before the layer signals
+    // Pushed rows need no fence here: kernel completion flushes this grid's
+    // writes at system scope, and the next kernel on the stream publishes the
+    // layer's signal with a system-scope fence + release store.
     tc_fence_before();
     __syncthreads();
     if (warp == kPfMmaWarp) tmem_dealloc(tmem, 512);
@@ -633,6 +659,7 @@ static int pf_args(const qw6k_moe_desc* d, int* err, PfArgs& a) {
     a.nitems = (int*)p; p += 256;
     a.h = (__nv_bfloat16*)p; p += al256(tk * d->inter * 2);
     a.dout = (__nv_bfloat16*)p;
+    a.slot_row = sorted ? d->slot_row : nullptr;
     a.out_peers = nullptr;
     a.out_off = 0;
     a.slot_dst = nullptr;

@@ -33,7 +33,7 @@ struct qw6cu_ep {
     qw6cu_ctx *ctx;
     uint32_t rank, world, ne, epr, topk, hidden, inter, max_tok, cap;
     uint8_t *region;
-    size_t region_bytes, o_sig, o_cnt, o_rx, o_sdst, o_ret;
+    size_t region_bytes, o_sig, o_cnt, o_rx, o_sbrow, o_sdst, o_ret;
     uint8_t *peer_host[QW6K_EP_MAX_WORLD];
     int opened[QW6K_EP_MAX_WORLD];
     int connected;
@@ -41,7 +41,7 @@ struct qw6cu_ep {
     uint8_t **peers_dev;
     uint32_t *epoch, *done_ctas;
     int *abort;
-    int32_t *idx, *cnt_self, *pos, *sendoff, *local_cnt, *send_row;
+    int32_t *idx, *cnt_self, *pos, *sendoff, *local_cnt, *send_row, *ucnt, *upos, *ubase;
     float *w;
     void *ws;
     size_t ws_bytes;
@@ -82,8 +82,9 @@ int qw6cu_ep_create(qw6cu_ctx *ctx, uint32_t rank, uint32_t world, uint32_t n_ex
     const size_t n = (size_t)max_tokens * top_k;
     ep->o_sig = 0;
     ep->o_cnt = al256(3 * QW6K_EP_MAX_WORLD * sizeof(uint32_t));
-    ep->o_rx = ep->o_cnt + al256((size_t)2 * world * n_experts * sizeof(int32_t));
-    ep->o_sdst = ep->o_rx + al256((size_t)ep->cap * hidden * 2);
+    ep->o_rx = ep->o_cnt + al256((size_t)2 * world * (n_experts + world) * sizeof(int32_t));
+    ep->o_sbrow = ep->o_rx + al256((size_t)ep->cap * hidden * 2);
+    ep->o_sdst = ep->o_sbrow + al256((size_t)ep->cap * 4);
     ep->o_ret = ep->o_sdst + al256((size_t)ep->cap * 4);
     ep->region_bytes = ep->o_ret + al256(n * hidden * 2);
     cudaError_t e = cudaMalloc((void **)&ep->region, ep->region_bytes);
@@ -93,7 +94,8 @@ int qw6cu_ep_create(qw6cu_ctx *ctx, uint32_t rank, uint32_t world, uint32_t n_ex
     }
     /* the sorted-mode grouped GEMM over up to cap received rows of epr experts */
     ep->ws_bytes = qw6k_moe_prefill_ws_bytes(ep->cap, hidden, inter, ep->epr, 1);
-    size_t off = 0, o_peers, o_epoch, o_idx, o_w, o_cnt, o_pos, o_send, o_local, o_row, o_ws;
+    size_t off = 0, o_peers, o_epoch, o_idx, o_w, o_cnt, o_pos, o_send, o_local, o_row, o_ucnt, o_upos, o_ubase,
+           o_ws;
     o_peers = off; off += al256(QW6K_EP_MAX_WORLD * sizeof(void *));
     o_epoch = off; off += 256; /* epoch, abort, done_ctas */
     o_idx = off; off += al256(n * 4);
@@ -103,6 +105,9 @@ int qw6cu_ep_create(qw6cu_ctx *ctx, uint32_t rank, uint32_t world, uint32_t n_ex
     o_send = off; off += al256(256 * 4);
     o_local = off; off += al256(256 * 4);
     o_row = off; off += al256(n * 4);
+    o_ucnt = off; off += al256(QW6K_EP_MAX_WORLD * 4);
+    o_upos = off; off += al256(n * 4);
+    o_ubase = off; off += al256(QW6K_EP_MAX_WORLD * 4);
     o_ws = off; off += al256(ep->ws_bytes);
     e = cudaMalloc((void **)&ep->priv, off);
     if (e != cudaSuccess) {
@@ -121,6 +126,9 @@ int qw6cu_ep_create(qw6cu_ctx *ctx, uint32_t rank, uint32_t world, uint32_t n_ex
     ep->sendoff = (int32_t *)(ep->priv + o_send);
     ep->local_cnt = (int32_t *)(ep->priv + o_local);
     ep->send_row = (int32_t *)(ep->priv + o_row);
+    ep->ucnt = (int32_t *)(ep->priv + o_ucnt);
+    ep->upos = (int32_t *)(ep->priv + o_upos);
+    ep->ubase = (int32_t *)(ep->priv + o_ubase);
     ep->ws = ep->priv + o_ws;
     /* signals and counts start at zero (epoch 0 = nothing published) */
     if ((e = cudaMemset(ep->region, 0, ep->o_rx)) != cudaSuccess ||
@@ -195,13 +203,8 @@ int qw6cu_ep_layer(qw6cu_ep *ep, const qw6cu_expert_pack *gate, const qw6cu_expe
     if (rc) return rc;
     int *err = qw6h_dev_err(ctx);
     if (!err) return QW6CU_ERR_NOMEM;
-    const uint32_t n = ntok * ep->topk;
     int r = qw6h_prof_a(ctx, QW6H_K_ROUTE);
     rc = qw6h_rc(qw6k_moe_route(logits, ntok, ep->ne, ep->topk, ep->idx, ep->w, ctx->st), "ep route");
-    qw6h_prof_b(ctx, r);
-    if (rc) return rc;
-    r = qw6h_prof_a(ctx, QW6H_K_EP);
-    rc = qw6h_rc(qw6k_ep_count(ep->idx, n, ep->ne, ep->cnt_self, ep->pos, ctx->st), "ep count");
     qw6h_prof_b(ctx, r);
     if (rc) return rc;
 
@@ -211,6 +214,7 @@ int qw6cu_ep_layer(qw6cu_ep *ep, const qw6cu_expert_pack *gate, const qw6cu_expe
     d.o_sig = ep->o_sig;
     d.o_cnt = ep->o_cnt;
     d.o_rx = ep->o_rx;
+    d.o_sbrow = ep->o_sbrow;
     d.o_sdst = ep->o_sdst;
     d.o_ret = ep->o_ret;
     d.nmax = (uint32_t)(ep->max_tok * ep->topk);
@@ -229,6 +233,9 @@ int qw6cu_ep_layer(qw6cu_ep *ep, const qw6cu_expert_pack *gate, const qw6cu_expe
     d.w = ep->w;
     d.cnt_self = ep->cnt_self;
     d.pos = ep->pos;
+    d.ucnt = ep->ucnt;
+    d.upos = ep->upos;
+    d.ubase = ep->ubase;
     d.sendoff = ep->sendoff;
     d.local_cnt = ep->local_cnt;
     d.send_row = ep->send_row;
@@ -256,14 +263,20 @@ int qw6cu_ep_layer(qw6cu_ep *ep, const qw6cu_expert_pack *gate, const qw6cu_expe
     m.slot_dst = (const int32_t *)(ep->region + ep->o_sdst);
     m.out_rows = ep->max_tok * ep->topk;
     m.expert_counts = ep->local_cnt;
+    m.slot_row = (const int32_t *)(ep->region + ep->o_sbrow);
     m.ws = ep->ws;
     m.ws_bytes = ep->ws_bytes;
     rc = qw6h_rc(qw6k_moe_prefill_check(&m, err), "ep grouped GEMM");
     if (rc) return rc;
 
     /* publish/plan, dispatch, wait rows | GEMMs | signal, wait outputs, combine */
+    static const int ep_kid[6] = {QW6H_K_EP_PUBLISH, QW6H_K_EP_DISPATCH, QW6H_K_EP_WAIT,
+                                  QW6H_K_EP,         QW6H_K_EP_WAIT,     QW6H_K_EP_COMBINE};
+    r = qw6h_prof_a(ctx, QW6H_K_EP);
+    rc = qw6h_rc(qw6k_ep_p2p_phase(&d, 6, ctx->st), "ep count");
+    qw6h_prof_b(ctx, r);
     for (int ph = 0; ph < 3 && !rc; ph++) {
-        r = qw6h_prof_a(ctx, QW6H_K_EP);
+        r = qw6h_prof_a(ctx, ep_kid[ph]);
         rc = qw6h_rc(qw6k_ep_p2p_phase(&d, ph, ctx->st), "ep phase");
         qw6h_prof_b(ctx, r);
     }
@@ -275,7 +288,7 @@ int qw6cu_ep_layer(qw6cu_ep *ep, const qw6cu_expert_pack *gate, const qw6cu_expe
         qw6h_prof_b(ctx, r);
     }
     for (int ph = 3; ph < 6 && !rc; ph++) {
-        r = qw6h_prof_a(ctx, QW6H_K_EP);
+        r = qw6h_prof_a(ctx, ep_kid[ph]);
         rc = qw6h_rc(qw6k_ep_p2p_phase(&d, ph, ctx->st), "ep phase");
         qw6h_prof_b(ctx, r);
     }

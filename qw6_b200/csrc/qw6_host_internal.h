@@ -41,6 +41,10 @@ enum {
     QW6H_K_PF_GEMM2,
     QW6H_K_PF_COMBINE,
     QW6H_K_EP,
+    QW6H_K_EP_PUBLISH,
+    QW6H_K_EP_DISPATCH,
+    QW6H_K_EP_WAIT,
+    QW6H_K_EP_COMBINE,
     QW6H_K_COUNT
 };
 

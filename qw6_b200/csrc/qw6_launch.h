@@ -97,6 +97,9 @@ typedef struct {
     /* sorted rows mode (rows mode with row_expert == NULL): the rows of x are
      * grouped by expert in expert order, expert_counts[e] (device) rows each */
     const int32_t *expert_counts;
+    /* sorted rows mode: x row of slot r is slot_row[r] (NULL: row r) --
+     * received token rows are shared by the slots of one token's experts */
+    const int32_t *slot_row;
     /* push mode (sorted rows, dout == NULL): the expert output of row r goes
      * to out_peers[s] + out_off + q * hidden * 2 bytes (bf16 row), where
      * slot_dst[r] = s * out_rows + q -- another GPU's memory over NVLink */
@@ -132,16 +135,18 @@ int qw6k_ep_combine(const void *ret_bf16, const float *w, const int32_t *send_po
 /* Expert parallelism over peer memory (k_ep.cu, phases of one layer).
  * Every rank holds one symmetric region with the same layout: signal words
  * (3 kinds x 64 sources, u32 epochs), a double-buffered count matrix
- * [2][world][ne] (i32), received token rows rx [cap][hidden] (bf16), the
- * destination of each received row's output sdst [cap] (i32: source rank *
- * nmax + source assignment) and the returned expert outputs of this rank's
- * own assignments ret [nmax][hidden] (bf16, written by the owners' down
- * GEMM); peers[p] is rank p's region as mapped in this process. */
+ * [2][world][ne + world] (i32: rows per expert, then unique token rows per
+ * owner), received token rows rx [cap][hidden] (bf16, one per (source,
+ * token) pair), and per received slot (expert-major) its row in rx sbrow
+ * [cap] and the destination of its output sdst [cap] (source rank * nmax +
+ * source assignment), and the returned expert outputs of this rank's own
+ * assignments ret [nmax][hidden] (bf16, written by the owners' down GEMM);
+ * peers[p] is rank p's region as mapped in this process. */
 #define QW6K_EP_MAX_WORLD 64
 enum { QW6K_EP_SIG_COUNTS = 0, QW6K_EP_SIG_ROWS = 1, QW6K_EP_SIG_DONE = 2 };
 typedef struct {
     uint8_t *const *peers; /* device array [world] */
-    size_t o_sig, o_cnt, o_rx, o_sdst, o_ret;
+    size_t o_sig, o_cnt, o_rx, o_sbrow, o_sdst, o_ret;
     uint32_t rank, world, ne, topk, hidden, ntok, cap, nmax;
     uint32_t *epoch;     /* private: step counter (phase 0 increments it) */
     int *abort;          /* private: set once any wait gives up; later phases do nothing */
@@ -149,8 +154,12 @@ typedef struct {
     int *err;            /* error word: 41 + phase kind of a wait that timed out */
     const int32_t *idx;  /* [ntok*topk] routing of this rank's tokens */
     const float *w;
-    const int32_t *cnt_self, *pos; /* per global expert counts / positions (qw6k_ep_count) */
-    int32_t *sendoff;    /* [ne] first row of this rank's block for each expert at its owner */
+    int32_t *cnt_self, *pos;  /* [ne] rows per global expert, [ntok*topk] position among its expert's */
+    int32_t *ucnt, *upos;     /* [world] unique token rows per owner, [ntok*topk] position of the
+                                 assignment's token row among them (-1 - position: a later slot of a
+                                 token already sent to that owner) */
+    int32_t *sendoff;    /* [ne] first slot of this rank's block for each expert at its owner */
+    int32_t *ubase;      /* [world] first rx row of this rank's unique rows at each owner */
     int32_t *local_cnt;  /* [ne/world] rows per local expert this step */
     int32_t *send_row;   /* [ntok*topk] row of each assignment at its owner */
     const void *x;       /* bf16 [ntok][hidden] */
@@ -158,7 +167,8 @@ typedef struct {
 } qw6k_ep_desc;
 /* phases: 0 publish counts + wait + plan, 1 dispatch rows + signal,
  * 2 wait for all rows, 3 signal outputs delivered, 4 wait for all outputs,
- * 5 combine (local reads of ret) */
+ * 5 combine (local reads of ret), 6 count (per expert and per owner; runs
+ * first) */
 int qw6k_ep_p2p_phase(const qw6k_ep_desc *d, int phase, cudaStream_t st);
 
 /* Fixed 1 MiB device scratch (k_static.cu) of the allocation-free MoE entry

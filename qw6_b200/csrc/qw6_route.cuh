@@ -25,28 +25,31 @@ __device__ __forceinline__ uint32_t route_key(float v) {
 __device__ __forceinline__ void route_token(const float* __restrict__ lg, int ne, int k, int32_t* __restrict__ idx,
                                             float* __restrict__ w, int lane) {
     float v[8];
+    uint32_t key[8];
 #pragma unroll
     for (int i = 0; i < 8; i++) {
         const int e = lane + 32 * i;
         v[i] = e < ne ? lg[e] : -INFINITY;
+        key[i] = route_key(v[i]);
     }
+    const uint32_t kNegInf = 0x007fffffu;  // route_key(-inf)
     float sel_v = 0.f;  // lane r keeps round r's value and index
     int sel_i = 0;
+    bool nan0 = __shfl_sync(0xffffffffu, isnan(v[0]) ? 1 : 0, 0) != 0;  // logit 0 is NaN (until selected)
     for (int r = 0; r < k; r++) {
         uint32_t bk = 0;
         int bi = 0x7fffffff;
 #pragma unroll
         for (int i = 0; i < 8; i++) {
             const int e = lane + 32 * i;
-            const uint32_t kk = route_key(v[i]);
-            if (e < ne && (kk > bk || bi == 0x7fffffff)) {
-                bk = kk;
+            if (e < ne && (key[i] > bk || bi == 0x7fffffff)) {
+                bk = key[i];
                 bi = e;
             }
         }
         const uint32_t mk = __reduce_max_sync(0xffffffffu, bi == 0x7fffffff ? 0u : bk);
         int win = (int)__reduce_min_sync(0xffffffffu, (bi != 0x7fffffff && bk == mk) ? (uint32_t)bi : 0xffffffffu);
-        if (__shfl_sync(0xffffffffu, isnan(v[0]) ? 1 : 0, 0)) win = 0;
+        if (nan0) win = 0;
         const int owner = win & 31, slot = win >> 5;
         float mine = 0.f;
 #pragma unroll
@@ -56,28 +59,32 @@ __device__ __forceinline__ void route_token(const float* __restrict__ lg, int ne
         if (lane == owner) {
 #pragma unroll
             for (int i = 0; i < 8; i++)
-                if (i == slot) v[i] = -INFINITY;
+                if (i == slot) {
+                    v[i] = -INFINITY;
+                    key[i] = kNegInf;
+                }
         }
+        if (win == 0) nan0 = false;
         if (lane == (r & 31)) {
             sel_v = orig;
             sel_i = win;
         }
     }
-    // softmax over the k selected values, in selection order, on lane 0
-    float vals[32];
-    for (int r = 0; r < k; r++) vals[r] = __shfl_sync(0xffffffffu, sel_v, r);
-    if (lane == 0) {
-        float mx = vals[0];
-        for (int r = 1; r < k; r++)
-            if (vals[r] > mx) mx = vals[r];
-        float sum = 0.f;
-        for (int r = 0; r < k; r++) {
-            vals[r] = expf(__fsub_rn(vals[r], mx));
-            sum = __fadd_rn(sum, vals[r]);
-        }
-        for (int r = 0; r < k; r++) w[r] = __fdiv_rn(vals[r], sum);
+    // softmax over the k selected values as qw6 computes it: the max by a
+    // strict '>' scan in selection order, expf(v - max), the sum in selection
+    // order, then each weight divided by the sum
+    float mx = __shfl_sync(0xffffffffu, sel_v, 0);
+    for (int r = 1; r < k; r++) {
+        const float t = __shfl_sync(0xffffffffu, sel_v, r);
+        if (t > mx) mx = t;
     }
-    if (lane < k) idx[lane] = sel_i;
+    const float ex = expf(__fsub_rn(sel_v, mx));
+    float sum = 0.f;
+    for (int r = 0; r < k; r++) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, ex, r));
+    if (lane < k) {
+        idx[lane] = sel_i;
+        w[lane] = __fdiv_rn(ex, sum);
+    }
 }
 
 }  // namespace qw6

@@ -324,7 +324,7 @@ class Context:
 
     def profile_end(self) -> dict:
         """{kernel name: (total ms, launches)} for the kernels that ran."""
-        n = 15
+        n = 19
         ms = (C.c_double * n)()
         cnt = (C.c_uint32 * n)()
         _check(self.lib.qw6cu_profile_end(self.h, ms, cnt), "qw6cu_profile_end")
