@@ -24,6 +24,7 @@
 #include <cstdint>
 
 #include "qw6_launch.h"
+#include "qw6_pdl.cuh"
 
 namespace qw6 {
 
@@ -152,6 +153,7 @@ __device__ bool ep_wait_all(const qw6k_ep_desc& d, int kind, uint32_t ep) {
 // rows -- a token whose experts share an owner sends its row there once
 // (upos >= 0 on its first such slot, -1 - position on the later ones).
 __global__ void k_ep_count_u(const qw6k_ep_desc d) {
+    pdl_grid_wait();
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= (int)d.ntok) return;
     const int topk = (int)d.topk, epr = (int)(d.ne / d.world);
@@ -180,6 +182,7 @@ __global__ void k_ep_count_u(const qw6k_ep_desc d) {
 __global__ void __launch_bounds__(256) k_ep_publish(const qw6k_ep_desc d) {
     __shared__ uint32_t s_ep;
     __shared__ int colsum[256];
+    pdl_grid_wait();
     const int tid = threadIdx.x, ne = (int)d.ne, epr = ne / (int)d.world;
     if (tid == 0) {
         s_ep = *d.epoch + 1;
@@ -189,6 +192,8 @@ __global__ void __launch_bounds__(256) k_ep_publish(const qw6k_ep_desc d) {
     const uint32_t ep = s_ep, par = ep & 1u;
     if (*d.abort) {
         if (tid < epr) d.local_cnt[tid] = 0;
+        for (int g = tid; g < ne; g += blockDim.x) d.cnt_self[g] = 0;
+        if (tid < (int)d.world) d.ucnt[tid] = 0;
         return;
     }
     const int L = ne + (int)d.world;  // matrix row: per-expert counts, then per-owner unique rows
@@ -198,6 +203,9 @@ __global__ void __launch_bounds__(256) k_ep_publish(const qw6k_ep_desc d) {
     }
     __threadfence_system();
     __syncthreads();
+    // the counters are consumed: zero them for the next step's count kernel
+    for (int g = tid; g < ne; g += blockDim.x) d.cnt_self[g] = 0;
+    if (tid < (int)d.world) d.ucnt[tid] = 0;
     if (tid < (int)d.world) st_release_sys(ep_sig(d, tid, QW6K_EP_SIG_COUNTS, d.rank), ep);
     if (!ep_wait_all(d, QW6K_EP_SIG_COUNTS, ep)) {
         if (tid < epr) d.local_cnt[tid] = 0;
@@ -247,6 +255,7 @@ __global__ void __launch_bounds__(256) k_ep_publish(const qw6k_ep_desc d) {
 // sendoff[g] + pos[a]; the last CTA to finish signals every owner.
 __global__ void __launch_bounds__(256) k_ep_dispatch(const qw6k_ep_desc d) {
     __shared__ bool last;
+    pdl_grid_wait();
     const int n = (int)(d.ntok * d.topk), epr = (int)(d.ne / d.world);
     const bool go = !*d.abort;
     const int a = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
@@ -262,14 +271,17 @@ __global__ void __launch_bounds__(256) k_ep_dispatch(const qw6k_ep_desc d) {
         }
         if (lane == 0) {
             d.send_row[a] = slot;
-            // the slot's token row at the owner, and where its output goes
-            reinterpret_cast<int32_t*>(d.peers[owner] + d.o_sbrow)[slot] = urow;
-            reinterpret_cast<int32_t*>(d.peers[owner] + d.o_sdst)[slot] = (int)(d.rank * d.nmax) + a;
+            // the slot's token row at the owner and where its output goes, one 8-byte store
+            reinterpret_cast<int2*>(d.peers[owner] + d.o_smeta)[slot] = make_int2(urow, (int)(d.rank * d.nmax) + a);
         }
     }
-    __threadfence_system();
+    // the barrier orders every thread's stores before thread 0's system-scope
+    // fence, which orders them before the completion count and the signal
     __syncthreads();
-    if (threadIdx.x == 0) last = atomicAdd(d.done_ctas, 1u) == gridDim.x - 1;
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        last = atomicAdd(d.done_ctas, 1u) == gridDim.x - 1;
+    }
     __syncthreads();
     if (last) {
         __threadfence_system();
@@ -280,12 +292,14 @@ __global__ void __launch_bounds__(256) k_ep_dispatch(const qw6k_ep_desc d) {
 
 // phases 2 and 4: wait for a signal from every rank
 __global__ void k_ep_wait(const qw6k_ep_desc d, int kind) {
+    pdl_grid_wait();
     if (*d.abort) return;
     ep_wait_all(d, kind, *d.epoch);
 }
 
 // phase 3: this rank's expert outputs are complete
 __global__ void k_ep_signal_done(const qw6k_ep_desc d) {
+    pdl_grid_wait();
     if (*d.abort) return;
     __threadfence_system();
     if (threadIdx.x < d.world) st_release_sys(ep_sig(d, threadIdx.x, QW6K_EP_SIG_DONE, d.rank), *d.epoch);
@@ -294,6 +308,7 @@ __global__ void k_ep_signal_done(const qw6k_ep_desc d) {
 // phase 5: out[t] = sum_k w[a] * ret[a] (fp32 fma, slot order); the owners
 // have written each assignment's bf16 output into this rank's ret
 __global__ void k_ep_combine_ret(const qw6k_ep_desc d) {
+    pdl_grid_wait();
     const int t = blockIdx.y, f = (blockIdx.x * blockDim.x + threadIdx.x) * 2;
     if (f >= (int)d.hidden || *d.abort) return;
     const int topk = (int)d.topk;
@@ -356,35 +371,35 @@ extern "C" int qw6k_ep_p2p_phase(const qw6k_ep_desc* d, int phase, cudaStream_t 
         !d->local_cnt || !d->send_row || !d->x || !d->out || !d->cap || !d->nmax || d->ntok * d->topk > d->nmax ||
         !d->ucnt || !d->upos || !d->ubase)
         return QW6K_ERR_ARG;
+    // every phase is launched as a programmatic dependent of the previous
+    // kernel on the stream; the counters of phase 6 are zeroed at create and
+    // re-zeroed by phase 0 once consumed
+    cudaError_t e;
     switch (phase) {
     case 6:
-        if (cudaMemsetAsync(d->cnt_self, 0, d->ne * sizeof(int32_t), st) != cudaSuccess ||
-            cudaMemsetAsync(d->ucnt, 0, d->world * sizeof(int32_t), st) != cudaSuccess)
-            return QW6K_ERR_CUDA;
-        k_ep_count_u<<<(d->ntok + 127) / 128, 128, 0, st>>>(*d);
+        e = launch_pdl(k_ep_count_u, dim3((d->ntok + 127) / 128), dim3(128), 0, st, *d);
         break;
     case 0:
-        k_ep_publish<<<1, 256, 0, st>>>(*d);
+        e = launch_pdl(k_ep_publish, dim3(1), dim3(256), 0, st, *d);
         break;
     case 1:
-        k_ep_dispatch<<<(d->ntok * d->topk + 7) / 8, 256, 0, st>>>(*d);
+        e = launch_pdl(k_ep_dispatch, dim3((d->ntok * d->topk + 7) / 8), dim3(256), 0, st, *d);
         break;
     case 2:
-        k_ep_wait<<<1, 64, 0, st>>>(*d, QW6K_EP_SIG_ROWS);
+        e = launch_pdl(k_ep_wait, dim3(1), dim3(64), 0, st, *d, (int)QW6K_EP_SIG_ROWS);
         break;
     case 3:
-        k_ep_signal_done<<<1, 64, 0, st>>>(*d);
+        e = launch_pdl(k_ep_signal_done, dim3(1), dim3(64), 0, st, *d);
         break;
     case 4:
-        k_ep_wait<<<1, 64, 0, st>>>(*d, QW6K_EP_SIG_DONE);
+        e = launch_pdl(k_ep_wait, dim3(1), dim3(64), 0, st, *d, (int)QW6K_EP_SIG_DONE);
         break;
-    case 5: {
-        dim3 g((d->hidden / 2 + 255) / 256, d->ntok);
-        k_ep_combine_ret<<<g, 256, 0, st>>>(*d);
+    case 5:
+        e = launch_pdl(k_ep_combine_ret, dim3((d->hidden / 2 + 255) / 256, d->ntok), dim3(256), 0, st, *d);
         break;
-    }
     default:
         return QW6K_ERR_ARG;
     }
+    if (e != cudaSuccess) return QW6K_ERR_CUDA;
     return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
 }

@@ -12,6 +12,7 @@
 #include <cstdint>
 
 #include "qw6_launch.h"
+#include "qw6_pdl.cuh"
 #include "qw6_argmax.cuh"
 #include "qw6_route.cuh"
 
@@ -19,6 +20,7 @@ namespace qw6 {
 
 __global__ void k_route(const float* __restrict__ logits, int ntok, int ne, int k, int32_t* __restrict__ idx,
                         float* __restrict__ w) {
+    pdl_grid_wait();
     const int tok = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (tok >= ntok) return;
     route_token(logits + (size_t)tok * ne, ne, k, idx + (size_t)tok * k, w + (size_t)tok * k, threadIdx.x & 31);
@@ -122,7 +124,9 @@ extern "C" int qw6k_moe_route(const float* logits, uint32_t ntok, uint32_t n_exp
         top_k > n_experts)
         return QW6K_ERR_ARG;
     const int wpb = 4;
-    k_route<<<(ntok + wpb - 1) / wpb, 32 * wpb, 0, st>>>(logits, (int)ntok, (int)n_experts, (int)top_k, idx, w);
+    if (launch_pdl(k_route, dim3((ntok + wpb - 1) / wpb), dim3(32 * wpb), 0, st, logits, (int)ntok, (int)n_experts,
+                   (int)top_k, idx, w) != cudaSuccess)
+        return QW6K_ERR_CUDA;
     return launched();
 }
 

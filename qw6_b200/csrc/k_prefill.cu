@@ -21,6 +21,7 @@
 
 #include "qw6_dev.cuh"
 #include "qw6_launch.h"
+#include "qw6_pdl.cuh"
 #include "qw6_route.cuh"
 #include "qw6_tc.cuh"
 
@@ -48,6 +49,7 @@ struct PfArgs {
     __nv_bfloat16* h;     // [TK][inter]  silu(gate)*up per assignment
     __nv_bfloat16* dout;  // [TK][hidden] expert output per assignment
     const int32_t* slot_row;    // sorted mode: x row of each slot (null: identity)
+    int slot_stride;            // element stride of slot_row / slot_dst
     uint8_t* const* out_peers;  // push mode: outputs go to other GPUs (see qw6k_moe_desc)
     size_t out_off;
     const int32_t* slot_dst;
@@ -58,6 +60,7 @@ struct PfArgs {
 // ------------------------------------------------------------------ plan --
 
 __global__ void k_pf_route(const PfArgs a) {
+    pdl_grid_wait();
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (t >= a.ntok) return;
     route_token(a.logits + (size_t)t * a.ne, a.ne, a.topk, a.idx + (size_t)t * a.topk, a.w + (size_t)t * a.topk,
@@ -65,6 +68,7 @@ __global__ void k_pf_route(const PfArgs a) {
 }
 
 __global__ void k_pf_count(const PfArgs a) {
+    pdl_grid_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < a.ntok * a.topk) a.pos[i] = atomicAdd(&a.cnt[a.idx[i]], 1);
 }
@@ -72,6 +76,7 @@ __global__ void k_pf_count(const PfArgs a) {
 // exclusive scans of counts and of 256-token chunks; the work-item list
 __global__ void __launch_bounds__(256) k_pf_offsets(const PfArgs a) {
     __shared__ int wsum[2][8];
+    pdl_grid_wait();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int own = tid < a.ne ? a.cnt[tid] : 0;
     int v = own, ch = (own + kPfChunk - 1) / kPfChunk;
@@ -103,6 +108,7 @@ __global__ void __launch_bounds__(256) k_pf_offsets(const PfArgs a) {
 }
 
 __global__ void k_pf_scatter(const PfArgs a) {
+    pdl_grid_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < a.ntok * a.topk) a.order[a.off[a.idx[i]] + a.pos[i]] = i;
 }
@@ -377,6 +383,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfArgs a) {
     __shared__ uint32_t tmem_base;
     __shared__ int rows[kPfChunk];
     __shared__ __nv_bfloat16* drow[MODE == 1 ? kPfChunk : 1];  // push mode: output row pointers
+    pdl_grid_wait();
     const int K = MODE == 0 ? a.hidden : a.inter;
     const int nft = MODE == 0 ? a.inter / 128 : a.hidden / 256;
     const int item = blockIdx.x / nft, ft = blockIdx.x % nft;
@@ -389,9 +396,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfArgs a) {
     const int32_t* ord = a.order;  // null: the rows are already grouped by expert (sorted mode)
     for (int j = tid; j < cnt; j += blockDim.x) {
         rows[j] = ord ? (MODE == 0 ? ord[off + j] / a.topk : ord[off + j])
-                      : (MODE == 0 && a.slot_row ? a.slot_row[off + j] : off + j);
+                      : (MODE == 0 && a.slot_row ? a.slot_row[(size_t)(off + j) * a.slot_stride] : off + j);
         if (MODE == 1 && a.out_peers) {
-            const int sd = a.slot_dst[off + j], src = sd / a.out_rows;
+            const int sd = a.slot_dst[(size_t)(off + j) * a.slot_stride], src = sd / a.out_rows;
             drow[MODE == 1 ? j : 0] = reinterpret_cast<__nv_bfloat16*>(a.out_peers[src] + a.out_off) +
                                       (size_t)(sd - src * a.out_rows) * a.hidden;
         }
@@ -585,6 +592,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfArgs a) {
 // out[t][f] = sum_k w[t,k] * dout[t*topk + k][f], fp32 in slot order k
 // (rows mode: out[r] = w[r] * dout[r]).
 __global__ void k_pf_combine(const PfArgs a) {
+    pdl_grid_wait();
     const int t = blockIdx.y, f = (blockIdx.x * blockDim.x + threadIdx.x) * 2;
     if (f >= a.hidden) return;
     float o0 = 0.f, o1 = 0.f;
@@ -660,6 +668,7 @@ static int pf_args(const qw6k_moe_desc* d, int* err, PfArgs& a) {
     a.h = (__nv_bfloat16*)p; p += al256(tk * d->inter * 2);
     a.dout = (__nv_bfloat16*)p;
     a.slot_row = sorted ? d->slot_row : nullptr;
+    a.slot_stride = d->slot_stride > 1 ? (int)d->slot_stride : 1;
     a.out_peers = nullptr;
     a.out_off = 0;
     a.slot_dst = nullptr;
@@ -692,8 +701,8 @@ static int launch_pf(const PfArgs& a, int mi, cudaStream_t st) {
         return QW6K_ERR_CUDA;
     cfg = true;
     const int nft = MODE == 0 ? a.inter / 128 : a.hidden / 256;
-    k_pf_gemm<F, MODE><<<mi * nft, kPfThreads, smem, st>>>(a);
-    return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
+    return launch_pdl(k_pf_gemm<F, MODE>, dim3(mi * nft), dim3(kPfThreads), smem, st, a) == cudaSuccess ? 0
+                                                                                             : QW6K_ERR_CUDA;
 }
 
 extern "C" int qw6k_moe_prefill_check(const qw6k_moe_desc* d, int* err) {
@@ -712,19 +721,19 @@ extern "C" int qw6k_moe_prefill_phase(const qw6k_moe_desc* d, int* err, int phas
     switch (phase) {
     case 0:
         if (!d->logits) return 0;  // rows mode: routing supplied by the caller
-        k_pf_route<<<(a.ntok + 7) / 8, 256, 0, st>>>(a);
+        if (launch_pdl(k_pf_route, dim3((a.ntok + 7) / 8), dim3(256), 0, st, a) != cudaSuccess) return QW6K_ERR_CUDA;
         break;
     case 1:
         if (!a.order) return 0;  // sorted mode: counts supplied
         if (cudaMemsetAsync(a.cnt, 0, 256 * 4, st) != cudaSuccess) return QW6K_ERR_CUDA;
-        k_pf_count<<<(tk + 255) / 256, 256, 0, st>>>(a);
+        if (launch_pdl(k_pf_count, dim3((tk + 255) / 256), dim3(256), 0, st, a) != cudaSuccess) return QW6K_ERR_CUDA;
         break;
     case 2:
-        k_pf_offsets<<<1, 256, 0, st>>>(a);
+        if (launch_pdl(k_pf_offsets, dim3(1), dim3(256), 0, st, a) != cudaSuccess) return QW6K_ERR_CUDA;
         break;
     case 3:
         if (!a.order) return 0;  // sorted mode: already in expert order
-        k_pf_scatter<<<(tk + 255) / 256, 256, 0, st>>>(a);
+        if (launch_pdl(k_pf_scatter, dim3((tk + 255) / 256), dim3(256), 0, st, a) != cudaSuccess) return QW6K_ERR_CUDA;
         break;
     case 4:
         return (d->gq == QW6F_Q6_K) ? launch_pf<QW6F_Q6_K, 0>(a, mi, st) : launch_pf<QW6F_Q4_K_M, 0>(a, mi, st);
@@ -733,7 +742,7 @@ extern "C" int qw6k_moe_prefill_phase(const qw6k_moe_desc* d, int* err, int phas
     case 6: {
         if (!d->logits) return 0;  // rows mode: the caller combines
         dim3 g((a.hidden / 2 + 255) / 256, a.ntok);
-        k_pf_combine<<<g, 256, 0, st>>>(a);
+        if (launch_pdl(k_pf_combine, g, dim3(256), 0, st, a) != cudaSuccess) return QW6K_ERR_CUDA;
         break;
     }
     default:

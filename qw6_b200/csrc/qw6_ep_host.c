@@ -33,7 +33,7 @@ struct qw6cu_ep {
     qw6cu_ctx *ctx;
     uint32_t rank, world, ne, epr, topk, hidden, inter, max_tok, cap;
     uint8_t *region;
-    size_t region_bytes, o_sig, o_cnt, o_rx, o_sbrow, o_sdst, o_ret;
+    size_t region_bytes, o_sig, o_cnt, o_rx, o_smeta, o_ret;
     uint8_t *peer_host[QW6K_EP_MAX_WORLD];
     int opened[QW6K_EP_MAX_WORLD];
     int connected;
@@ -83,9 +83,8 @@ int qw6cu_ep_create(qw6cu_ctx *ctx, uint32_t rank, uint32_t world, uint32_t n_ex
     ep->o_sig = 0;
     ep->o_cnt = al256(3 * QW6K_EP_MAX_WORLD * sizeof(uint32_t));
     ep->o_rx = ep->o_cnt + al256((size_t)2 * world * (n_experts + world) * sizeof(int32_t));
-    ep->o_sbrow = ep->o_rx + al256((size_t)ep->cap * hidden * 2);
-    ep->o_sdst = ep->o_sbrow + al256((size_t)ep->cap * 4);
-    ep->o_ret = ep->o_sdst + al256((size_t)ep->cap * 4);
+    ep->o_smeta = ep->o_rx + al256((size_t)ep->cap * hidden * 2);
+    ep->o_ret = ep->o_smeta + al256((size_t)ep->cap * 8);
     ep->region_bytes = ep->o_ret + al256(n * hidden * 2);
     cudaError_t e = cudaMalloc((void **)&ep->region, ep->region_bytes);
     if (e != cudaSuccess) {
@@ -132,7 +131,7 @@ int qw6cu_ep_create(qw6cu_ctx *ctx, uint32_t rank, uint32_t world, uint32_t n_ex
     ep->ws = ep->priv + o_ws;
     /* signals and counts start at zero (epoch 0 = nothing published) */
     if ((e = cudaMemset(ep->region, 0, ep->o_rx)) != cudaSuccess ||
-        (e = cudaMemset(ep->priv, 0, o_idx)) != cudaSuccess || (e = cudaDeviceSynchronize()) != cudaSuccess) {
+        (e = cudaMemset(ep->priv, 0, o_ws)) != cudaSuccess || (e = cudaDeviceSynchronize()) != cudaSuccess) {
         qw6cu_ep_destroy(ep);
         return ep_fail("qw6cu_ep_create: cudaMemset", e);
     }
@@ -214,8 +213,7 @@ int qw6cu_ep_layer(qw6cu_ep *ep, const qw6cu_expert_pack *gate, const qw6cu_expe
     d.o_sig = ep->o_sig;
     d.o_cnt = ep->o_cnt;
     d.o_rx = ep->o_rx;
-    d.o_sbrow = ep->o_sbrow;
-    d.o_sdst = ep->o_sdst;
+    d.o_smeta = ep->o_smeta;
     d.o_ret = ep->o_ret;
     d.nmax = (uint32_t)(ep->max_tok * ep->topk);
     d.rank = ep->rank;
@@ -260,10 +258,11 @@ int qw6cu_ep_layer(qw6cu_ep *ep, const qw6cu_expert_pack *gate, const qw6cu_expe
     m.topk = 1;
     m.out_peers = (uint8_t *const *)ep->peers_dev;
     m.out_off = ep->o_ret;
-    m.slot_dst = (const int32_t *)(ep->region + ep->o_sdst);
+    m.slot_dst = (const int32_t *)(ep->region + ep->o_smeta) + 1;
     m.out_rows = ep->max_tok * ep->topk;
     m.expert_counts = ep->local_cnt;
-    m.slot_row = (const int32_t *)(ep->region + ep->o_sbrow);
+    m.slot_row = (const int32_t *)(ep->region + ep->o_smeta);
+    m.slot_stride = 2;
     m.ws = ep->ws;
     m.ws_bytes = ep->ws_bytes;
     rc = qw6h_rc(qw6k_moe_prefill_check(&m, err), "ep grouped GEMM");

@@ -102,11 +102,13 @@ typedef struct {
     const int32_t *slot_row;
     /* push mode (sorted rows, dout == NULL): the expert output of row r goes
      * to out_peers[s] + out_off + q * hidden * 2 bytes (bf16 row), where
-     * slot_dst[r] = s * out_rows + q -- another GPU's memory over NVLink */
+     * slot_dst[r * slot_stride] = s * out_rows + q -- another GPU's memory
+     * over NVLink; slot_row is read with the same stride */
     uint8_t *const *out_peers;
     size_t out_off;
     const int32_t *slot_dst;
     uint32_t out_rows;
+    uint32_t slot_stride; /* 0 or 1: dense; 2: interleaved (row, dst) pairs */
 } qw6k_moe_desc;
 
 size_t qw6k_moe_ws_bytes(uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t ne, uint32_t topk);
@@ -137,8 +139,8 @@ int qw6k_ep_combine(const void *ret_bf16, const float *w, const int32_t *send_po
  * (3 kinds x 64 sources, u32 epochs), a double-buffered count matrix
  * [2][world][ne + world] (i32: rows per expert, then unique token rows per
  * owner), received token rows rx [cap][hidden] (bf16, one per (source,
- * token) pair), and per received slot (expert-major) its row in rx sbrow
- * [cap] and the destination of its output sdst [cap] (source rank * nmax +
+ * token) pair), per received slot (expert-major) smeta [cap] (i32 pairs:
+ * its row in rx, and the destination of its output as source rank * nmax +
  * source assignment), and the returned expert outputs of this rank's own
  * assignments ret [nmax][hidden] (bf16, written by the owners' down GEMM);
  * peers[p] is rank p's region as mapped in this process. */
@@ -146,7 +148,7 @@ int qw6k_ep_combine(const void *ret_bf16, const float *w, const int32_t *send_po
 enum { QW6K_EP_SIG_COUNTS = 0, QW6K_EP_SIG_ROWS = 1, QW6K_EP_SIG_DONE = 2 };
 typedef struct {
     uint8_t *const *peers; /* device array [world] */
-    size_t o_sig, o_cnt, o_rx, o_sbrow, o_sdst, o_ret;
+    size_t o_sig, o_cnt, o_rx, o_smeta, o_ret;
     uint32_t rank, world, ne, topk, hidden, ntok, cap, nmax;
     uint32_t *epoch;     /* private: step counter (phase 0 increments it) */
     int *abort;          /* private: set once any wait gives up; later phases do nothing */

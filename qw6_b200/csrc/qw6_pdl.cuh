@@ -1,0 +1,32 @@
+// qw6_pdl.cuh -- programmatic dependent launch for chains of kernels on one
+// stream (also inside CUDA graphs): a kernel launched with launch_pdl may be
+// scheduled while its predecessor still runs, and must call pdl_wait()
+// before it touches anything the predecessor writes (pdl_wait returns at
+// once when the kernel was launched normally).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <utility>
+
+namespace qw6 {
+
+__device__ __forceinline__ void pdl_grid_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+}  // namespace qw6
