@@ -154,9 +154,30 @@ __device__ bool ep_wait_all(const qw6k_ep_desc& d, int kind, uint32_t ep) {
 // (upos >= 0 on its first such slot, -1 - position on the later ones).
 __global__ void k_ep_count_u(const qw6k_ep_desc d) {
     pdl_grid_wait();
+    const int topk = (int)d.topk, epr = (int)(d.ne / d.world);
+    if (topk <= 8) {  // 8 lanes per token, one slot each
+        const int lane = threadIdx.x & 31, sub = lane & 7;
+        const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 3;
+        const bool act = t < (int)d.ntok && sub < topk;
+        const int a = t * topk + sub;
+        const int g = act ? d.idx[a] : -1, own = act ? g / epr : -1;
+        // first slot of this token with the same owner (lanes of one token share an 8-lane group)
+        int first = sub;
+        for (int j = 0; j < 8; j++) {
+            const int oj = __shfl_sync(0xffffffffu, own, (lane & ~7) | j);
+            if (j < sub && oj == own && first == sub) first = j;
+        }
+        int up = 0;
+        if (act) {
+            d.pos[a] = atomicAdd(&d.cnt_self[g], 1);
+            if (first == sub) up = atomicAdd(&d.ucnt[own], 1);
+        }
+        const int upf = __shfl_sync(0xffffffffu, up, (lane & ~7) | first);
+        if (act) d.upos[a] = first == sub ? up : -1 - upf;
+        return;
+    }
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= (int)d.ntok) return;
-    const int topk = (int)d.topk, epr = (int)(d.ne / d.world);
     const int32_t* ix = d.idx + (size_t)t * topk;
     for (int k = 0; k < topk; k++) {
         const int a = t * topk + k, g = ix[k], own = g / epr;
@@ -182,6 +203,7 @@ __global__ void k_ep_count_u(const qw6k_ep_desc d) {
 __global__ void __launch_bounds__(256) k_ep_publish(const qw6k_ep_desc d) {
     __shared__ uint32_t s_ep;
     __shared__ int colsum[256];
+    __shared__ int pre[257];
     pdl_grid_wait();
     const int tid = threadIdx.x, ne = (int)d.ne, epr = ne / (int)d.world;
     if (tid == 0) {
@@ -219,8 +241,8 @@ __global__ void __launch_bounds__(256) k_ep_publish(const qw6k_ep_desc d) {
             cs += v;
             if (s < d.rank) before += v;
         }
-        colsum[tid] = cs;
     }
+    colsum[tid] = cs;
     if (tid < (int)d.world) {  // unique rows: this rank's base at owner tid, and owner tid's total
         int ub = 0, tot = 0;
         for (uint32_t s = 0; s < d.world; s++) {
@@ -235,31 +257,51 @@ __global__ void __launch_bounds__(256) k_ep_publish(const qw6k_ep_desc d) {
         }
     }
     __syncthreads();
-    if (tid < ne) {
-        int base = 0;
-        for (int g = (tid / epr) * epr; g < tid; g++) base += colsum[g];
-        d.sendoff[tid] = base + before;
-        // an owner block can never hold more rows than the receive capacity
-        int tot = 0;
-        for (int g = (tid / epr) * epr; g < (tid / epr + 1) * epr; g++) tot += colsum[g];
-        if (tot > (int)d.cap) {
-            atomicExch(d.err, 44);
-            atomicExch(d.abort, 1);
+    // exclusive prefix of colsum over all experts (warp scans + warp totals);
+    // pre[ne] is the total, so an owner block [b0, b1) holds pre[b1] - pre[b0]
+    // slots and the prefix inside it is pre[g] - pre[b0]
+    {
+        __shared__ int wsum[8];
+        const int lane = tid & 31, wid = tid >> 5;
+        const int v = colsum[tid];  // 0 for tid >= ne
+        int x = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        if (lane == 31) wsum[wid] = x;
+        __syncthreads();
+        int wb = 0;
+        for (int w = 0; w < wid; w++) wb += wsum[w];
+        pre[tid] = wb + x - v;
+        if (tid == 255) pre[256] = wb + x;
+        __syncthreads();
+        if (tid < ne) {
+            const int b0 = (tid / epr) * epr;
+            d.sendoff[tid] = pre[tid] - pre[b0] + before;
+            // an owner block can never hold more slots than the receive capacity
+            if (tid == b0 && pre[b0 + epr] - pre[b0] > (int)d.cap) {
+                atomicExch(d.err, 44);
+                atomicExch(d.abort, 1);
+            }
         }
     }
     __syncthreads();
     if (tid < epr) d.local_cnt[tid] = *d.abort ? 0 : colsum[d.rank * epr + tid];
 }
 
-// phase 1: warp per assignment copies the token row into its owner's rx at
-// sendoff[g] + pos[a]; the last CTA to finish signals every owner.
+// phase 1: warps loop over the assignments (grid-stride): the token row goes
+// to its owner's rx at its unique row (first slot of the token at that owner
+// only), the slot's metadata as one 8-byte store; the last CTA to finish
+// signals every owner.
 __global__ void __launch_bounds__(256) k_ep_dispatch(const qw6k_ep_desc d) {
     __shared__ bool last;
     pdl_grid_wait();
     const int n = (int)(d.ntok * d.topk), epr = (int)(d.ne / d.world);
     const bool go = !*d.abort;
-    const int a = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (go && a < n) {
+    const int lane = threadIdx.x & 31, nw = gridDim.x * (blockDim.x >> 5);
+    for (int a = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); go && a < n; a += nw) {
         const int g = d.idx[a], owner = g / epr, slot = d.sendoff[g] + d.pos[a], up = d.upos[a];
         const int urow = d.ubase[owner] + (up >= 0 ? up : -1 - up);
         if (up >= 0) {  // first slot of this token at this owner: send the row
@@ -267,7 +309,17 @@ __global__ void __launch_bounds__(256) k_ep_dispatch(const qw6k_ep_desc d) {
                                                               (size_t)(a / (int)d.topk) * d.hidden);
             uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(d.peers[owner] + d.o_rx) +
                                                   (size_t)urow * d.hidden);
-            for (int i = lane; i < (int)d.hidden / 8; i += 32) dst[i] = src[i];
+            // 4 KB rows per pass: all loads in flight before the stores
+            const int nv = (int)d.hidden / 8;
+            for (int i0 = 0; i0 < nv; i0 += 256) {
+                uint4 v[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++)
+                    if (i0 + u * 32 + lane < nv) v[u] = __ldg(src + i0 + u * 32 + lane);
+#pragma unroll
+                for (int u = 0; u < 8; u++)
+                    if (i0 + u * 32 + lane < nv) dst[i0 + u * 32 + lane] = v[u];
+            }
         }
         if (lane == 0) {
             d.send_row[a] = slot;
@@ -377,14 +429,17 @@ extern "C" int qw6k_ep_p2p_phase(const qw6k_ep_desc* d, int phase, cudaStream_t 
     cudaError_t e;
     switch (phase) {
     case 6:
-        e = launch_pdl(k_ep_count_u, dim3((d->ntok + 127) / 128), dim3(128), 0, st, *d);
+        e = d->topk <= 8 ? launch_pdl(k_ep_count_u, dim3((d->ntok * 8 + 255) / 256), dim3(256), 0, st, *d)
+                         : launch_pdl(k_ep_count_u, dim3((d->ntok + 127) / 128), dim3(128), 0, st, *d);
         break;
     case 0:
         e = launch_pdl(k_ep_publish, dim3(1), dim3(256), 0, st, *d);
         break;
-    case 1:
-        e = launch_pdl(k_ep_dispatch, dim3((d->ntok * d->topk + 7) / 8), dim3(256), 0, st, *d);
+    case 1: {
+        const uint32_t n = d->ntok * d->topk, ctas = (n + 7) / 8;
+        e = launch_pdl(k_ep_dispatch, dim3(ctas < 296u ? ctas : 296u), dim3(256), 0, st, *d);
         break;
+    }
     case 2:
         e = launch_pdl(k_ep_wait, dim3(1), dim3(64), 0, st, *d, (int)QW6K_EP_SIG_ROWS);
         break;
