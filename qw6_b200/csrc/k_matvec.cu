@@ -175,7 +175,7 @@ __global__ void __launch_bounds__(kThreads) k_matvec(const MvArgs a) {
 
     typename T::Frag fa, fb;
     if (step_ok(0)) T::load(fa, tile_ptr(0), lane);
-    if constexpr (IsIQ<F>::value) init_iq_tables(tbl, grid_ptr<F>(), GridBytes<F>::value, F == QW6F_IQ3_S);
+    if constexpr (IsIQ<F>::value) init_iq_tables(tbl, grid_ptr<F>(), GridBytes<F>::value, F == QW6F_IQ3_S, F == QW6F_IQ2_XXS);
     xstage_fill(xs, a.x, a.ldx, a.ntok, 4 * NQ, a.cols);
     __syncthreads();
     const XView xv = xs.view();

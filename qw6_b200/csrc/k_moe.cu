@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(kThreads) k_moe_gateup(const MoeArgs a) {
     IQTables* tbl = reinterpret_cast<IQTables*>(smem);
     XStage xs = xstage_carve(smem + tbl_bytes_of<F>(), 4 * NQ, a.hidden);
     float* red = reinterpret_cast<float*>(smem + tbl_bytes_of<F>() + xstage_bytes(4 * NQ, a.hidden));
-    if constexpr (IsIQ<F>::value) init_iq_tables(tbl, grid_ptr<F>(), GridBytes<F>::value, F == QW6F_IQ3_S);
+    if constexpr (IsIQ<F>::value) init_iq_tables(tbl, grid_ptr<F>(), GridBytes<F>::value, F == QW6F_IQ3_S, F == QW6F_IQ2_XXS);
     xstage_fill(xs, a.x, a.hidden, cnt, 4 * NQ, a.hidden, sel, a.topk);
     __syncthreads();
     const XView xv = xs.view();
@@ -208,7 +208,7 @@ __global__ void __launch_bounds__(kThreads) k_moe_down(const MoeArgs a) {
     IQTables* tbl = reinterpret_cast<IQTables*>(smem);
     XStage xs = xstage_carve(smem + tbl_bytes_of<F>(), 4 * NQ, a.inter);
     float* red = reinterpret_cast<float*>(smem + tbl_bytes_of<F>() + xstage_bytes(4 * NQ, a.inter));
-    if constexpr (IsIQ<F>::value) init_iq_tables(tbl, grid_ptr<F>(), GridBytes<F>::value, F == QW6F_IQ3_S);
+    if constexpr (IsIQ<F>::value) init_iq_tables(tbl, grid_ptr<F>(), GridBytes<F>::value, F == QW6F_IQ3_S, F == QW6F_IQ2_XXS);
     xstage_fill(xs, a.mid, a.inter, cnt, 4 * NQ, a.inter, sel, 1);
     __syncthreads();
     const XView xv = xs.view();
@@ -325,7 +325,7 @@ __global__ void __launch_bounds__(kThreads) k_moe_small_gu(const MoeArgs a) {
     IQTables* tbl = reinterpret_cast<IQTables*>(smem);
     XStage xs = xstage_carve(smem + tbl_bytes_of<F>(), 4, a.hidden);
     float* red = reinterpret_cast<float*>(smem + tbl_bytes_of<F>() + xstage_bytes(4, a.hidden));
-    if constexpr (IsIQ<F>::value) init_iq_tables(tbl, grid_ptr<F>(), GridBytes<F>::value, F == QW6F_IQ3_S);
+    if constexpr (IsIQ<F>::value) init_iq_tables(tbl, grid_ptr<F>(), GridBytes<F>::value, F == QW6F_IQ3_S, F == QW6F_IQ2_XXS);
     xstage_fill(xs, a.x, a.hidden, a.ntok, 4, a.hidden);
     __syncthreads();
     const XView xv = xs.view();
@@ -406,7 +406,7 @@ __global__ void __launch_bounds__(kThreads) k_moe_small_down(const MoeArgs a) {
     IQTables* tbl = reinterpret_cast<IQTables*>(smem);
     uint8_t* stage0 = smem + tbl_bytes_of<F>();
     const size_t sb = xstage_bytes(4, a.inter);
-    if constexpr (IsIQ<F>::value) init_iq_tables(tbl, grid_ptr<F>(), GridBytes<F>::value, F == QW6F_IQ3_S);
+    if constexpr (IsIQ<F>::value) init_iq_tables(tbl, grid_ptr<F>(), GridBytes<F>::value, F == QW6F_IQ3_S, F == QW6F_IQ2_XXS);
     __syncthreads();
     pdl_wait();  // mid from the gate/up kernel is complete and visible
     for (int it = warp; it < ni; it += kWarps) {

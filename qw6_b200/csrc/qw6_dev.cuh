@@ -123,11 +123,22 @@ __device__ __forceinline__ void mma_k16(int (&d)[4], uint32_t a0, uint32_t a1, u
 // (IQ2: 8 weights -> 32 bits; IQ3_S: 4 weights -> 16 bits) and expanded by
 // prmt against constant registers holding the value set.  Half the bytes of
 // the raw codebook per lookup means fewer shared-memory bank conflicts.
+//
+// Signs.  IQ2 selectors use values 0..2 per nibble; with the second prmt
+// source holding the negated values, bit 2 of a nibble selects the negative
+// byte, so a sign pattern becomes an OR of a mask with bit 4j+2 set for every
+// negative weight j: sgn[] maps the 7 stored sign bits of IQ2_XXS (the 8th is
+// their parity) or the 8 sign bits of IQ2_S to that mask.  IQ3_S's eight
+// values fill both prmt sources; its sgn[] maps 4 sign bits to the pair
+// (xor mask 0xff, increment 0x01 per negative byte) of two's-complement
+// negation.
 struct IQTables {
     uint32_t sel[1024];  // IQ2_XXS: 256 entries, IQ2_S: 1024 entries (32-bit); IQ3_S: 512 x 16-bit
+    uint32_t sgn[256];   // IQ2_XXS: 128 masks; IQ2_S: 256 masks; IQ3_S: 16 (xor, inc) pairs
 };
 
 constexpr uint32_t kIQ2Vals = 0x002b1908u;               // bytes {8, 25, 43}
+constexpr uint32_t kIQ2Neg = 0x00d5e7f8u;                // bytes {-8, -25, -43}
 constexpr uint32_t kIQ3Lo = 0x07050301u, kIQ3Hi = 0x0f0d0b09u;  // bytes {1..15 odd}
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
@@ -138,7 +149,30 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
 
 // Build the selector table from the raw grid bytes (all threads take part;
 // the caller synchronizes).  iq3: 4-byte entries -> 16-bit selectors.
-__device__ __forceinline__ void init_iq_tables(IQTables* tb, const uint8_t* grid_g, int grid_bytes, bool iq3) {
+__device__ __forceinline__ uint32_t nibble_bit2_mask(uint32_t s8) {
+    uint32_t m = 0;
+#pragma unroll
+    for (int j = 0; j < 8; j++) m |= ((s8 >> j) & 1u) << (4 * j + 2);
+    return m;
+}
+__device__ __forceinline__ void init_iq_tables(IQTables* tb, const uint8_t* grid_g, int grid_bytes, bool iq3,
+                                               bool xxs = false) {
+    if (!iq3) {
+        for (int i = threadIdx.x; i < 256; i += blockDim.x)
+            tb->sgn[i] = nibble_bit2_mask(xxs ? (i & 127) | ((__popc(i & 127) & 1u) << 7) : i);
+    } else {
+        for (int n = threadIdx.x; n < 16; n += blockDim.x) {
+            uint32_t m = 0, inc = 0;
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                if ((n >> j) & 1) {
+                    m |= 0xffu << (8 * j);
+                    inc |= 1u << (8 * j);
+                }
+            tb->sgn[2 * n] = m;
+            tb->sgn[2 * n + 1] = inc;
+        }
+    }
     if (!iq3) {
         for (int e = threadIdx.x; e < grid_bytes / 8; e += blockDim.x) {
             uint32_t v = 0;
@@ -654,12 +688,11 @@ struct Tile<QW6F_IQ2_XXS, NQ> {
                 const uint32_t iw = rh ? (j < 4 ? f.idx.z : f.idx.w) : (j < 4 ? f.idx.x : f.idx.y);
                 const uint32_t gi = byte_of(iw, j & 3);
                 const uint32_t aw = word_of(f.aux[rh][j >> 2], j & 3);
-                const uint32_t sf = (aw >> (7 * t)) & 127u;
-                const uint32_t s8 = sf | ((__popc(sf) & 1u) << 7);  // qw6_ksigns(sf)
+                const uint32_t sf = (aw >> (7 * t)) & 127u;  // signs of qw6_ksigns(sf) via sgn[]
                 scl[rh] = 2 * (int)(aw >> 28) + 1;
-                const uint32_t sel = tbl->sel[gi];
-                lo[rh] = signed_bytes(prmt(kIQ2Vals, kIQ2Vals, sel), s8);
-                hi[rh] = signed_bytes(prmt(kIQ2Vals, kIQ2Vals, sel >> 16), s8 >> 4);
+                const uint32_t ss = tbl->sel[gi] | tbl->sgn[sf];
+                lo[rh] = prmt(kIQ2Vals, kIQ2Neg, ss);
+                hi[rh] = prmt(kIQ2Vals, kIQ2Neg, ss >> 16);
             }
 #pragma unroll
             for (int qt = 0; qt < NQ; qt++) {
@@ -715,9 +748,8 @@ struct Tile<QW6F_IQ2_S, NQ> {
                     const uint32_t ib = byte16(f.P[rh][0], 2 * j + hh);
                     const uint32_t qhb = byte_of(j < 4 ? f.sh[rh].x : f.sh[rh].y, j & 3);
                     const uint32_t gi = ib | (((qhb >> (2 * l)) & 3u) << 8);
-                    const uint32_t gw = prmt(kIQ2Vals, kIQ2Vals, tbl->sel[gi] >> (4 * half4));
                     const uint32_t sb = byte16(f.P[rh][1], 2 * j + hh);
-                    a[rh] = signed_bytes(gw, sb >> half4);
+                    a[rh] = prmt(kIQ2Vals, kIQ2Neg, (tbl->sel[gi] | tbl->sgn[sb]) >> (4 * half4));
                     const uint32_t scb = byte_of(j < 4 ? f.sh[rh].z : f.sh[rh].w, j & 3);
                     scl[rh] = 2 * (int)((scb >> (4 * hh)) & 15u) + 1;
                 }
@@ -779,8 +811,10 @@ struct Tile<QW6F_IQ3_S, NQ> {
                 const uint32_t gw1 = prmt(kIQ3Lo, kIQ3Hi, s16[g1]);
                 const uint32_t gw2 = prmt(kIQ3Lo, kIQ3Hi, s16[g2]);
                 const uint32_t sb = byte_of(rh ? (j < 4 ? f.c[2].z : f.c[2].w) : (j < 4 ? f.c[2].x : f.c[2].y), j & 3);
-                lo[rh] = signed_bytes(gw1, sb);
-                hi[rh] = signed_bytes(gw2, sb >> 4);
+                const uint2 ml = *reinterpret_cast<const uint2*>(&tbl->sgn[2 * (sb & 15u)]);
+                const uint2 mh = *reinterpret_cast<const uint2*>(&tbl->sgn[2 * (sb >> 4)]);
+                lo[rh] = (gw1 ^ ml.x) + ml.y;
+                hi[rh] = (gw2 ^ mh.x) + mh.y;
                 const uint32_t scb = byte_of(f.sc[rh], j >> 1);
                 scl[rh] = 1 + 2 * (int)((j & 1) ? (scb >> 4) : (scb & 15u));
             }
