@@ -150,8 +150,17 @@ struct MvArgs {
     uint32_t row_offset;
 };
 
+// Batch-1 kernels run 2 CTAs per SM; those of the smaller tile formats keep
+// two tile-blocks in flight per warp (three register buffers), the rest
+// double-buffer.
+template <int F, int NQ>
+struct MvTriple {
+    static constexpr bool value = NQ == 1 && F != QW6F_Q6_K;
+};
+
 template <int F, int NQ, bool KEYS>
-__global__ void __launch_bounds__(kThreads) k_matvec(const MvArgs a) {
+__global__ void __launch_bounds__(kThreads, NQ == 1 ? 2 : 1) k_matvec(const MvArgs a) {
+    constexpr bool kTriple = MvTriple<F, NQ>::value;
     extern __shared__ __align__(16) uint8_t smem[];
     using T = Tile<F, NQ>;
     constexpr int TB = T::TB;
@@ -173,7 +182,7 @@ __global__ void __launch_bounds__(kThreads) k_matvec(const MvArgs a) {
     };
     auto step_ok = [&](int step) { return step < nsteps && item_mt(step / nbk) < a.mtiles; };
 
-    typename T::Frag fa, fb;
+    typename T::Frag fa, fb, fc;
     if (step_ok(0)) T::load(fa, tile_ptr(0), lane);
     if constexpr (IsIQ<F>::value) init_iq_tables(tbl, grid_ptr<F>(), GridBytes<F>::value, F == QW6F_IQ3_S, F == QW6F_IQ2_XXS);
     xstage_fill(xs, a.x, a.ldx, a.ntok, 4 * NQ, a.cols);
@@ -239,15 +248,34 @@ __global__ void __launch_bounds__(kThreads) k_matvec(const MvArgs a) {
         for (int qt = 0; qt < NQ; qt++) acc[0][qt] = acc[1][qt] = 0.f;
     };
 
-    for (int s = 0; s < nsteps; s += 2) {
-        if (step_ok(s + 1)) T::load(fb, tile_ptr(s + 1), lane);
+    if constexpr (!kTriple) {
+        for (int s = 0; s < nsteps; s += 2) {
+            if (step_ok(s + 1)) T::load(fb, tile_ptr(s + 1), lane);
+            if (step_ok(s)) tile_dot<F, NQ>(fa, xv, split * nbk + s % nbk, acc, lane, tbl);
+            if (s % nbk == nbk - 1) epilogue(s);
+            if (s + 1 < nsteps) {
+                if (step_ok(s + 2)) T::load(fa, tile_ptr(s + 2), lane);
+                if (step_ok(s + 1)) tile_dot<F, NQ>(fb, xv, split * nbk + (s + 1) % nbk, acc, lane, tbl);
+                if ((s + 1) % nbk == nbk - 1) epilogue(s + 1);
+            }
+        }
+    } else {
+    // three fragment buffers: the loads of steps s+1 and s+2 are in flight
+    // while step s is consumed
+    if (step_ok(1)) T::load(fb, tile_ptr(1), lane);
+    for (int s = 0; s < nsteps; s += 3) {
+        if (step_ok(s + 2)) T::load(fc, tile_ptr(s + 2), lane);
         if (step_ok(s)) tile_dot<F, NQ>(fa, xv, split * nbk + s % nbk, acc, lane, tbl);
         if (s % nbk == nbk - 1) epilogue(s);
-        if (s + 1 < nsteps) {
-            if (step_ok(s + 2)) T::load(fa, tile_ptr(s + 2), lane);
-            if (step_ok(s + 1)) tile_dot<F, NQ>(fb, xv, split * nbk + (s + 1) % nbk, acc, lane, tbl);
-            if ((s + 1) % nbk == nbk - 1) epilogue(s + 1);
-        }
+        if (s + 1 >= nsteps) break;
+        if (step_ok(s + 3)) T::load(fa, tile_ptr(s + 3), lane);
+        if (step_ok(s + 1)) tile_dot<F, NQ>(fb, xv, split * nbk + (s + 1) % nbk, acc, lane, tbl);
+        if ((s + 1) % nbk == nbk - 1) epilogue(s + 1);
+        if (s + 2 >= nsteps) break;
+        if (step_ok(s + 4)) T::load(fb, tile_ptr(s + 4), lane);
+        if (step_ok(s + 2)) tile_dot<F, NQ>(fc, xv, split * nbk + (s + 2) % nbk, acc, lane, tbl);
+        if ((s + 2) % nbk == nbk - 1) epilogue(s + 2);
+    }
     }
     if (KEYS) {
         // lanes 4g+t share token t: fold over g (lane bits 2..4), one atomic per warp and token
