@@ -233,14 +233,19 @@ def ep_bench(args, torch, ctx, L, stream, rank, world, dist):
     step is profiled per kernel; the end-to-end leg copies each step's
     inputs from pinned host memory and reads the output back."""
     from qw6_b200 import synth as S
-    from qw6_b200.ep import PeerMoE
-    gate, up, down, logits, xbits = S.config3()
+    from qw6_b200.ep import PeerMoE, balance_experts
+    gate, up, down, logits, xbits, bias = S.config3(with_bias=True)
     epr, tpr = NE // world, T3 // world
-    lo = rank * epr
+    placement = None
+    if world > 1:  # balance the ranks' rows on routing statistics of an independent calibration batch
+        cal = S.router_sample(bias, T3, seed=1003)
+        cnt = np.bincount(np.argsort(-cal, axis=1, kind="stable")[:, :TOPK].ravel(), minlength=NE)
+        placement = balance_experts(cnt, world)
+    mine_ids = placement[rank] if placement is not None else np.arange(rank * epr, (rank + 1) * epr)
     ncopies = world  # world copies of a 256/world-expert shard: ~522 MB resident per GPU
     copies = []
     for q, m, r, c in ((S.Q4_K, gate, INTER, HIDDEN), (S.Q4_K, up, INTER, HIDDEN), (S.Q6_K, down, HIDDEN, INTER)):
-        mine = np.ascontiguousarray(m[lo:lo + epr])
+        mine = np.ascontiguousarray(m[mine_ids])
         pb = ctx.packed_bytes(q, r, c)
         raw = torch.from_numpy(mine.reshape(-1)).cuda()
         pk = torch.empty(pb * epr, dtype=torch.uint8, device="cuda")
@@ -254,7 +259,7 @@ def ep_bench(args, torch, ctx, L, stream, rank, world, dist):
     lg = torch.from_numpy(logits[sl]).cuda()
     x = torch.from_numpy(xbits[sl].view(np.int16)).cuda()
     out = torch.empty((tpr, HIDDEN), dtype=torch.float32, device="cuda")
-    pm = PeerMoE(ctx, *packs[0], NE, TOPK, HIDDEN, INTER, tpr) if world > 1 else None
+    pm = PeerMoE(ctx, *packs[0], NE, TOPK, HIDDEN, INTER, tpr, placement=placement) if world > 1 else None
     torch.cuda.synchronize()
 
     def step(s, lgt=lg, xt=x, o=out):
@@ -600,7 +605,9 @@ def report(args, world, head):
                    "experts": NE, "top_k": TOPK, "inter": INTER, "gate_up": "Q4_K", "down": "Q6_K",
                    "router_bias": "N(0,0.5) per expert",
                    "parallelism": f"ep{world}: {NE // world} experts and {T3 // world} tokens per GPU"
-                                  + (", dispatch/combine by this library's kernels over NVLink peer memory"
+                                  + (", dispatch/combine by this library's kernels over NVLink peer memory, "
+                                     "experts placed by balance_experts on the routing counts of an independent "
+                                     "calibration batch (same router bias, fresh token noise)"
                                      if world > 1 else ""),
                    "graph": f"CUDA graphs of {head['graph_steps']} steps replayed",
                    "l2": f"inputs larger than L2: {world} resident copies of each GPU's expert shard "

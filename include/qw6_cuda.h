@@ -250,8 +250,9 @@ int qw6cu_ep_combine(qw6cu_ctx *ctx, const void *ret_bf16, const float *w, const
 typedef struct qw6cu_ep qw6cu_ep;
 /* bytes of one rank's handle (a cudaIpcMemHandle_t) */
 size_t qw6cu_ep_handle_bytes(void);
-/* Experts are sharded contiguously (n_experts / world per rank); up to
- * max_tokens tokens per rank and call.  Allocates the symmetric region
+/* Experts are sharded contiguously (n_experts / world per rank) unless
+ * qw6cu_ep_set_placement says otherwise; up to max_tokens tokens per rank
+ * and call.  Allocates the symmetric region
  * (2 * world * max_tokens * top_k * hidden * 2 bytes plus signals/counts)
  * and the private buffers. */
 int qw6cu_ep_create(qw6cu_ctx *ctx, uint32_t rank, uint32_t world, uint32_t n_experts, uint32_t top_k,
@@ -259,6 +260,14 @@ int qw6cu_ep_create(qw6cu_ctx *ctx, uint32_t rank, uint32_t world, uint32_t n_ex
 int qw6cu_ep_handle(qw6cu_ep *ep, void *handle);
 /* handles: world x qw6cu_ep_handle_bytes(), in rank order (own entry ignored) */
 int qw6cu_ep_connect(qw6cu_ep *ep, const void *handles);
+/* Expert placement (the same on every rank): experts[r * epr + j] is the
+ * routed expert id that rank r holds as its local expert j, epr =
+ * n_experts / world; a permutation of 0 .. n_experts-1.  Balancing the
+ * ranks' rows by placing experts from routing statistics evens out the
+ * grouped GEMMs without changing any output bit.  Synchronises the
+ * context's stream; call between steps, with each rank's packs reordered
+ * to match. */
+int qw6cu_ep_set_placement(qw6cu_ep *ep, const uint32_t *experts);
 /* gate/up/down: this rank's experts (local index 0 .. n_experts/world - 1);
  * logits fp32 [ntok x n_experts], x bf16 [ntok x hidden], out fp32 [ntok x
  * hidden] -- this rank's tokens, device memory; ntok <= max_tokens. */

@@ -149,7 +149,7 @@ __device__ bool ep_wait_all(const qw6k_ep_desc& d, int kind, uint32_t ep) {
 }
 
 // phase 6 (runs first; counters zeroed by the launcher), thread per token:
-// per global expert counts and positions, and per owner the unique token
+// per placed expert counts and positions, and per owner the unique token
 // rows -- a token whose experts share an owner sends its row there once
 // (upos >= 0 on its first such slot, -1 - position on the later ones).
 __global__ void k_ep_count_u(const qw6k_ep_desc d) {
@@ -160,7 +160,7 @@ __global__ void k_ep_count_u(const qw6k_ep_desc d) {
         const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 3;
         const bool act = t < (int)d.ntok && sub < topk;
         const int a = t * topk + sub;
-        const int g = act ? d.idx[a] : -1, own = act ? g / epr : -1;
+        const int g = act ? d.eslot[d.idx[a]] : -1, own = act ? g / epr : -1;
         // first slot of this token with the same owner (lanes of one token share an 8-lane group)
         int first = sub;
         for (int j = 0; j < 8; j++) {
@@ -180,11 +180,11 @@ __global__ void k_ep_count_u(const qw6k_ep_desc d) {
     if (t >= (int)d.ntok) return;
     const int32_t* ix = d.idx + (size_t)t * topk;
     for (int k = 0; k < topk; k++) {
-        const int a = t * topk + k, g = ix[k], own = g / epr;
+        const int a = t * topk + k, g = d.eslot[ix[k]], own = g / epr;
         d.pos[a] = atomicAdd(&d.cnt_self[g], 1);
         int first = k;
         for (int j = 0; j < k; j++)
-            if (ix[j] / epr == own) {
+            if (d.eslot[ix[j]] / epr == own) {
                 first = j;
                 break;
             }
@@ -192,78 +192,126 @@ __global__ void k_ep_count_u(const qw6k_ep_desc d) {
     }
 }
 
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // phase 0 (1 CTA x 256): stamp the step, publish this rank's per-expert and
 // per-owner unique-row counts into every rank's matrix, wait for all
-// sources, then plan:
-//   colsum[g]  = slots of global expert g over all sources,
+// sources, then plan (placed expert ids):
+//   colsum[g]  = slots of expert g over all sources,
 //   base[g]    = exclusive prefix of colsum inside g's owner block,
 //   sendoff[g] = base[g] + slots for g from sources < this rank,
 //   ubase[o]   = unique rows sent to owner o by sources < this rank,
 //   local_cnt  = colsum over this rank's own experts.
+// Every matrix entry carries the low 8 bits of the step's epoch above its
+// count (counts < 2^24): a 32-bit store arrives whole, so a receiver that
+// reads this step's tag in an entry has its count -- no fence and no
+// separate signal.  Tags of the same matrix buffer (parity) two steps apart
+// differ, and no rank runs two steps ahead of another.  Loops over ranks
+// issue their peer pointers and loads eight at a time before using them.
 __global__ void __launch_bounds__(256) k_ep_publish(const qw6k_ep_desc d) {
     __shared__ uint32_t s_ep;
+    __shared__ int s_bad;
     __shared__ int colsum[256];
     __shared__ int pre[257];
+    __shared__ int wsum[8];
     pdl_grid_wait();
-    const int tid = threadIdx.x, ne = (int)d.ne, epr = ne / (int)d.world;
+    const int tid = threadIdx.x, ne = (int)d.ne, world = (int)d.world, epr = ne / world;
     if (tid == 0) {
         s_ep = *d.epoch + 1;
         *d.epoch = s_ep;
+        s_bad = 0;
     }
     __syncthreads();
-    const uint32_t ep = s_ep, par = ep & 1u;
+    const uint32_t ep = s_ep, par = ep & 1u, tag = (ep & 0xffu) << 24;
     if (*d.abort) {
         if (tid < epr) d.local_cnt[tid] = 0;
         for (int g = tid; g < ne; g += blockDim.x) d.cnt_self[g] = 0;
-        if (tid < (int)d.world) d.ucnt[tid] = 0;
+        if (tid < world) d.ucnt[tid] = 0;
         return;
     }
-    const int L = ne + (int)d.world;  // matrix row: per-expert counts, then per-owner unique rows
-    for (uint32_t p = 0; p < d.world; p++) {
-        int32_t* m = reinterpret_cast<int32_t*>(d.peers[p] + d.o_cnt) + ((size_t)par * d.world + d.rank) * L;
-        for (int g = tid; g < L; g += blockDim.x) m[g] = g < ne ? d.cnt_self[g] : d.ucnt[g - ne];
+    // matrix row: per-expert counts, then per-owner unique rows; ne <= 256,
+    // so entry tid + 256 (if any) is a unique-row count
+    const int L = ne + world, g1 = tid + 256;
+    const uint32_t v0 = tag | (uint32_t)(tid < ne ? d.cnt_self[tid] : tid < L ? d.ucnt[tid - ne] : 0);
+    const uint32_t v1 = tag | (uint32_t)(g1 < L ? d.ucnt[g1 - ne] : 0);
+    const size_t row = ((size_t)par * world + d.rank) * L;
+    for (int p0 = 0; p0 < world; p0 += 8) {
+        uint8_t* pp[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) pp[j] = p0 + j < world ? d.peers[p0 + j] : nullptr;
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            if (p0 + j < world) {
+                uint32_t* m = reinterpret_cast<uint32_t*>(pp[j] + d.o_cnt) + row;
+                if (tid < L) st_relaxed_sys(m + tid, v0);
+                if (g1 < L) st_relaxed_sys(m + g1, v1);
+            }
     }
-    __threadfence_system();
     __syncthreads();
     // the counters are consumed: zero them for the next step's count kernel
-    for (int g = tid; g < ne; g += blockDim.x) d.cnt_self[g] = 0;
-    if (tid < (int)d.world) d.ucnt[tid] = 0;
-    if (tid < (int)d.world) st_release_sys(ep_sig(d, tid, QW6K_EP_SIG_COUNTS, d.rank), ep);
-    if (!ep_wait_all(d, QW6K_EP_SIG_COUNTS, ep)) {
+    if (tid < ne) d.cnt_self[tid] = 0;
+    if (tid < world) d.ucnt[tid] = 0;
+    // column tid over the sources: expert tid's slots, or (tid < world) the
+    // unique rows for owner tid; poll until every entry carries this step's tag
+    const uint32_t* mine = reinterpret_cast<const uint32_t*>(d.peers[d.rank] + d.o_cnt) + (size_t)par * world * L;
+    int cs = 0, before = 0, ub = 0, tot = 0;
+    bool ok = true;
+    const uint64_t t0 = ep_now_ns();
+    for (int s0 = 0; s0 < world && ok; s0 += 8) {
+        uint32_t v[8], u[8];
+        for (;;) {
+            bool ready = true;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const bool in = s0 + j < world;
+                v[j] = in && tid < ne ? ld_relaxed_sys(mine + (size_t)(s0 + j) * L + tid) : tag;
+                u[j] = in && tid < world ? ld_relaxed_sys(mine + (size_t)(s0 + j) * L + ne + tid) : tag;
+                ready = ready && (v[j] & 0xff000000u) == tag && (u[j] & 0xff000000u) == tag;
+            }
+            if (ready) break;
+            if (ep_now_ns() - t0 > kEpWaitLimitNs) {
+                ok = false;
+                break;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int vc = (int)(v[j] & 0xffffffu), uc = (int)(u[j] & 0xffffffu);
+            cs += vc;
+            tot += uc;
+            if (s0 + j < (int)d.rank) {
+                before += vc;
+                ub += uc;
+            }
+        }
+    }
+    if (!ok) {
+        atomicExch(d.err, 41 + QW6K_EP_SIG_COUNTS);
+        atomicExch(d.abort, 1);
+    }
+    if (!__syncthreads_and(ok)) {
         if (tid < epr) d.local_cnt[tid] = 0;
         return;
     }
-    const int32_t* mine = reinterpret_cast<const int32_t*>(d.peers[d.rank] + d.o_cnt) + (size_t)par * d.world * L;
-    int cs = 0, before = 0;
-    if (tid < ne) {
-        for (uint32_t s = 0; s < d.world; s++) {
-            const int v = __ldcg(mine + (size_t)s * L + tid);
-            cs += v;
-            if (s < d.rank) before += v;
-        }
-    }
-    colsum[tid] = cs;
-    if (tid < (int)d.world) {  // unique rows: this rank's base at owner tid, and owner tid's total
-        int ub = 0, tot = 0;
-        for (uint32_t s = 0; s < d.world; s++) {
-            const int v = __ldcg(mine + (size_t)s * L + ne + tid);
-            if (s < d.rank) ub += v;
-            tot += v;
-        }
+    colsum[tid] = tid < ne ? cs : 0;
+    if (tid < world) {  // this rank's base at owner tid; no owner may receive more rows than its buffer holds
         d.ubase[tid] = ub;
-        if (tot > (int)d.cap) {  // no owner may receive more rows than its buffer holds
-            atomicExch(d.err, 44);
-            atomicExch(d.abort, 1);
-        }
+        if (tot > (int)d.cap) s_bad = 1;
     }
     __syncthreads();
     // exclusive prefix of colsum over all experts (warp scans + warp totals);
     // pre[ne] is the total, so an owner block [b0, b1) holds pre[b1] - pre[b0]
     // slots and the prefix inside it is pre[g] - pre[b0]
     {
-        __shared__ int wsum[8];
         const int lane = tid & 31, wid = tid >> 5;
-        const int v = colsum[tid];  // 0 for tid >= ne
+        const int v = colsum[tid];
         int x = v;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -273,7 +321,8 @@ __global__ void __launch_bounds__(256) k_ep_publish(const qw6k_ep_desc d) {
         if (lane == 31) wsum[wid] = x;
         __syncthreads();
         int wb = 0;
-        for (int w = 0; w < wid; w++) wb += wsum[w];
+#pragma unroll
+        for (int w = 0; w < 8; w++) wb += w < wid ? wsum[w] : 0;
         pre[tid] = wb + x - v;
         if (tid == 255) pre[256] = wb + x;
         __syncthreads();
@@ -281,14 +330,19 @@ __global__ void __launch_bounds__(256) k_ep_publish(const qw6k_ep_desc d) {
             const int b0 = (tid / epr) * epr;
             d.sendoff[tid] = pre[tid] - pre[b0] + before;
             // an owner block can never hold more slots than the receive capacity
-            if (tid == b0 && pre[b0 + epr] - pre[b0] > (int)d.cap) {
-                atomicExch(d.err, 44);
-                atomicExch(d.abort, 1);
-            }
+            if (tid == b0 && pre[b0 + epr] - pre[b0] > (int)d.cap) s_bad = 1;
         }
     }
     __syncthreads();
-    if (tid < epr) d.local_cnt[tid] = *d.abort ? 0 : colsum[d.rank * epr + tid];
+    if (s_bad) {
+        if (tid == 0) {
+            atomicExch(d.err, 44);
+            atomicExch(d.abort, 1);
+        }
+        if (tid < epr) d.local_cnt[tid] = 0;
+        return;
+    }
+    if (tid < epr) d.local_cnt[tid] = colsum[d.rank * epr + tid];
 }
 
 // phase 1: warps loop over the assignments (grid-stride): the token row goes
@@ -302,7 +356,7 @@ __global__ void __launch_bounds__(256) k_ep_dispatch(const qw6k_ep_desc d) {
     const bool go = !*d.abort;
     const int lane = threadIdx.x & 31, nw = gridDim.x * (blockDim.x >> 5);
     for (int a = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); go && a < n; a += nw) {
-        const int g = d.idx[a], owner = g / epr, slot = d.sendoff[g] + d.pos[a], up = d.upos[a];
+        const int g = d.eslot[d.idx[a]], owner = g / epr, slot = d.sendoff[g] + d.pos[a], up = d.upos[a];
         const int urow = d.ubase[owner] + (up >= 0 ? up : -1 - up);
         if (up >= 0) {  // first slot of this token at this owner: send the row
             const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(d.x) +
@@ -421,7 +475,7 @@ extern "C" int qw6k_ep_p2p_phase(const qw6k_ep_desc* d, int phase, cudaStream_t 
         d->ne > 256 || d->ne % d->world || !d->topk || !d->ntok || !d->hidden || d->hidden % 8 || !d->epoch ||
         !d->abort || !d->done_ctas || !d->err || !d->idx || !d->w || !d->cnt_self || !d->pos || !d->sendoff ||
         !d->local_cnt || !d->send_row || !d->x || !d->out || !d->cap || !d->nmax || d->ntok * d->topk > d->nmax ||
-        !d->ucnt || !d->upos || !d->ubase)
+        !d->ucnt || !d->upos || !d->ubase || !d->eslot)
         return QW6K_ERR_ARG;
     // every phase is launched as a programmatic dependent of the previous
     // kernel on the stream; the counters of phase 6 are zeroed at create and

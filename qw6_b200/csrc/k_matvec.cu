@@ -164,8 +164,8 @@ __global__ void __launch_bounds__(kThreads, NQ == 1 ? 2 : 1) k_matvec(const MvAr
     extern __shared__ __align__(16) uint8_t smem[];
     using T = Tile<F, NQ>;
     constexpr int TB = T::TB;
-    constexpr size_t tbl_bytes = IsIQ<F>::value ? sizeof(IQTables) : 0;
-    IQTables* tbl = reinterpret_cast<IQTables*>(smem);
+    constexpr size_t tbl_bytes = IQLut<F>::bytes;
+    uint32_t* tbl = reinterpret_cast<uint32_t*>(smem);
     XStage xs = xstage_carve(smem + tbl_bytes, 4 * NQ, a.cols);
     float* red = reinterpret_cast<float*>(smem + tbl_bytes + xstage_bytes(4 * NQ, a.cols));
 
@@ -184,7 +184,7 @@ __global__ void __launch_bounds__(kThreads, NQ == 1 ? 2 : 1) k_matvec(const MvAr
 
     typename T::Frag fa, fb, fc;
     if (step_ok(0)) T::load(fa, tile_ptr(0), lane);
-    if constexpr (IsIQ<F>::value) init_iq_tables(tbl, grid_ptr<F>(), GridBytes<F>::value, F == QW6F_IQ3_S, F == QW6F_IQ2_XXS);
+    if constexpr (IsIQ<F>::value) IQLut<F>::init(tbl, grid_ptr<F>());
     xstage_fill(xs, a.x, a.ldx, a.ntok, 4 * NQ, a.cols);
     __syncthreads();
     const XView xv = xs.view();
@@ -309,7 +309,7 @@ static int num_sms() {
 
 template <int F, int NQ>
 static size_t mv_smem(int cols) {
-    return (IsIQ<F>::value ? sizeof(IQTables) : 0) + xstage_bytes(4 * NQ, cols) + (size_t)kThreads * 2 * NQ * 4;
+    return IQLut<F>::bytes + xstage_bytes(4 * NQ, cols) + (size_t)kThreads * 2 * NQ * 4;
 }
 
 template <int F, int NQ, bool KEYS>

@@ -99,7 +99,7 @@ __device__ __forceinline__ float silu_exact(float v) { return __fdiv_rn(v, __fad
 
 template <int F>
 __host__ __device__ constexpr size_t tbl_bytes_of() {
-    return IsIQ<F>::value ? sizeof(IQTables) : 0;
+    return IQLut<F>::bytes;
 }
 
 // ---------------------------------------------------------------- gateup --
@@ -126,10 +126,10 @@ __global__ void __launch_bounds__(kThreads) k_moe_gateup(const MoeArgs a) {
     T::load(u0, ub, lane);
     T::load(u1, ub + TB, lane);
 
-    IQTables* tbl = reinterpret_cast<IQTables*>(smem);
+    uint32_t* tbl = reinterpret_cast<uint32_t*>(smem);
     XStage xs = xstage_carve(smem + tbl_bytes_of<F>(), 4 * NQ, a.hidden);
     float* red = reinterpret_cast<float*>(smem + tbl_bytes_of<F>() + xstage_bytes(4 * NQ, a.hidden));
-    if constexpr (IsIQ<F>::value) init_iq_tables(tbl, grid_ptr<F>(), GridBytes<F>::value, F == QW6F_IQ3_S, F == QW6F_IQ2_XXS);
+    if constexpr (IsIQ<F>::value) IQLut<F>::init(tbl, grid_ptr<F>());
     xstage_fill(xs, a.x, a.hidden, cnt, 4 * NQ, a.hidden, sel, a.topk);
     __syncthreads();
     const XView xv = xs.view();
@@ -205,10 +205,10 @@ __global__ void __launch_bounds__(kThreads) k_moe_down(const MoeArgs a) {
     T::load(d0, db, lane);
     T::load(d1, db + TB, lane);
 
-    IQTables* tbl = reinterpret_cast<IQTables*>(smem);
+    uint32_t* tbl = reinterpret_cast<uint32_t*>(smem);
     XStage xs = xstage_carve(smem + tbl_bytes_of<F>(), 4 * NQ, a.inter);
     float* red = reinterpret_cast<float*>(smem + tbl_bytes_of<F>() + xstage_bytes(4 * NQ, a.inter));
-    if constexpr (IsIQ<F>::value) init_iq_tables(tbl, grid_ptr<F>(), GridBytes<F>::value, F == QW6F_IQ3_S, F == QW6F_IQ2_XXS);
+    if constexpr (IsIQ<F>::value) IQLut<F>::init(tbl, grid_ptr<F>());
     xstage_fill(xs, a.mid, a.inter, cnt, 4 * NQ, a.inter, sel, 1);
     __syncthreads();
     const XView xv = xs.view();
@@ -322,10 +322,10 @@ __global__ void __launch_bounds__(kThreads) k_moe_small_gu(const MoeArgs a) {
         a.idx[threadIdx.x] = P.idx[threadIdx.x];
         a.w[threadIdx.x] = P.w[threadIdx.x];
     }
-    IQTables* tbl = reinterpret_cast<IQTables*>(smem);
+    uint32_t* tbl = reinterpret_cast<uint32_t*>(smem);
     XStage xs = xstage_carve(smem + tbl_bytes_of<F>(), 4, a.hidden);
     float* red = reinterpret_cast<float*>(smem + tbl_bytes_of<F>() + xstage_bytes(4, a.hidden));
-    if constexpr (IsIQ<F>::value) init_iq_tables(tbl, grid_ptr<F>(), GridBytes<F>::value, F == QW6F_IQ3_S, F == QW6F_IQ2_XXS);
+    if constexpr (IsIQ<F>::value) IQLut<F>::init(tbl, grid_ptr<F>());
     xstage_fill(xs, a.x, a.hidden, a.ntok, 4, a.hidden);
     __syncthreads();
     const XView xv = xs.view();
@@ -403,10 +403,10 @@ __global__ void __launch_bounds__(kThreads) k_moe_small_down(const MoeArgs a) {
                 if (P.idx[t * a.topk + k] == P.items[it]) r = t * a.topk + k;
         rs[it][t] = r;
     }
-    IQTables* tbl = reinterpret_cast<IQTables*>(smem);
+    uint32_t* tbl = reinterpret_cast<uint32_t*>(smem);
     uint8_t* stage0 = smem + tbl_bytes_of<F>();
     const size_t sb = xstage_bytes(4, a.inter);
-    if constexpr (IsIQ<F>::value) init_iq_tables(tbl, grid_ptr<F>(), GridBytes<F>::value, F == QW6F_IQ3_S, F == QW6F_IQ2_XXS);
+    if constexpr (IsIQ<F>::value) IQLut<F>::init(tbl, grid_ptr<F>());
     __syncthreads();
     pdl_wait();  // mid from the gate/up kernel is complete and visible
     for (int it = warp; it < ni; it += kWarps) {
@@ -638,7 +638,10 @@ static bool moe_small(const qw6k_moe_desc* d) {
     const int nbh = (int)d->hidden / 256;
     const int ksh = nbh / nbw_of(nbh);
     if (ksh > 8 || (d->inter / 16) % (kWarps / ksh)) return false;
-    return (size_t)d->ntok * d->topk * xstage_bytes(4, (int)d->inter) + sizeof(IQTables) <= 180 * 1024;
+    const size_t lut = d->dq == QW6F_IQ2_XXS ? IQLut<QW6F_IQ2_XXS>::bytes
+                       : d->dq == QW6F_IQ2_S ? IQLut<QW6F_IQ2_S>::bytes
+                       : d->dq == QW6F_IQ3_S ? IQLut<QW6F_IQ3_S>::bytes : 0;
+    return (size_t)d->ntok * d->topk * xstage_bytes(4, (int)d->inter) + lut <= 180 * 1024;
 }
 
 extern "C" int qw6k_moe_check(const qw6k_moe_desc* d) {

@@ -435,25 +435,31 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfArgs a) {
         const uint8_t* tb = wbase + (size_t)(mt0 + mi) * nbk * TB;  // this warp's m-tile, K block 0
         BRows<kPfProducers> br;
         br.init(bsrc, K, rows, cnt, npad, tid);
+        // The lane takes the packed data (and rows) of lane 4 g' + t with
+        // g' = (g >> 1) | 4 (g & 1): the 8 lanes of each phase of a 16-byte
+        // shared store then write rows r and r + 4, whose chunks t ^ (r & 7)
+        // never coincide under the 128-byte swizzle (adjacent rows would
+        // collide pairwise); the loads stay coalesced.
+        const int plane = 4 * (((lane >> 3) & 3) | ((lane & 4) ? 4 : 0)) + (lane & 3);
         // A fragments and headers one K block (four slabs) ahead: buffer c
         // holds slab c of the block being stored, then slab c of the next one
         ASlab<F> rq[4];
         AHdr<F> hc, hn;
-        hc.load(tb, lane);
+        hc.load(tb, plane);
         hc.unpack();
         hn = hc;
-        rq[0].template load<0>(tb, lane);
-        rq[2].template load<2>(tb, lane);
+        rq[0].template load<0>(tb, plane);
+        rq[2].template load<2>(tb, plane);
         if (!ASlab<F>::kPairShared) {
-            rq[1].template load<1>(tb, lane);
-            rq[3].template load<3>(tb, lane);
+            rq[1].template load<1>(tb, plane);
+            rq[3].template load<3>(tb, plane);
         }
         int s = 0;          // stage of slab ks
         uint32_t rnd = 0;   // how many times the ring has wrapped before slab ks
         for (int kb = 0; kb < nbk && ok; kb++) {
             const uint8_t* tbn = tb + TB;
             const bool more = kb + 1 < nbk;
-            if (more) hn.load(tbn, lane);
+            if (more) hn.load(tbn, plane);
 #pragma unroll
             for (int c = 0; c < 4; c++) {
                 if (c > 0 && ++s == S) {
@@ -474,20 +480,20 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfArgs a) {
                 // slab c reads buffer c & ~1, refilled after its second slab
                 switch (c) {
                 case 0:
-                    rq[0].template store<0>(sa, hc, mi, lane);
-                    if (!share && more) rq[0].template load<0>(tbn, lane);
+                    rq[0].template store<0>(sa, hc, mi, plane);
+                    if (!share && more) rq[0].template load<0>(tbn, plane);
                     break;
                 case 1:
-                    rq[share ? 0 : 1].template store<1>(sa, hc, mi, lane);
-                    if (more) rq[share ? 0 : 1].template load<(share ? 0 : 1)>(tbn, lane);
+                    rq[share ? 0 : 1].template store<1>(sa, hc, mi, plane);
+                    if (more) rq[share ? 0 : 1].template load<(share ? 0 : 1)>(tbn, plane);
                     break;
                 case 2:
-                    rq[2].template store<2>(sa, hc, mi, lane);
-                    if (!share && more) rq[2].template load<2>(tbn, lane);
+                    rq[2].template store<2>(sa, hc, mi, plane);
+                    if (!share && more) rq[2].template load<2>(tbn, plane);
                     break;
                 default:
-                    rq[share ? 2 : 3].template store<3>(sa, hc, mi, lane);
-                    if (more) rq[share ? 2 : 3].template load<(share ? 2 : 3)>(tbn, lane);
+                    rq[share ? 2 : 3].template store<3>(sa, hc, mi, plane);
+                    if (more) rq[share ? 2 : 3].template load<(share ? 2 : 3)>(tbn, plane);
                     break;
                 }
                 fence_async_smem();

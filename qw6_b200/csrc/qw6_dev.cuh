@@ -132,11 +132,6 @@ __device__ __forceinline__ void mma_k16(int (&d)[4], uint32_t a0, uint32_t a1, u
 // values fill both prmt sources; its sgn[] maps 4 sign bits to the pair
 // (xor mask 0xff, increment 0x01 per negative byte) of two's-complement
 // negation.
-struct IQTables {
-    uint32_t sel[1024];  // IQ2_XXS: 256 entries, IQ2_S: 1024 entries (32-bit); IQ3_S: 512 x 16-bit
-    uint32_t sgn[256];   // IQ2_XXS: 128 masks; IQ2_S: 256 masks; IQ3_S: 16 (xor, inc) pairs
-};
-
 constexpr uint32_t kIQ2Vals = 0x002b1908u;               // bytes {8, 25, 43}
 constexpr uint32_t kIQ2Neg = 0x00d5e7f8u;                // bytes {-8, -25, -43}
 constexpr uint32_t kIQ3Lo = 0x07050301u, kIQ3Hi = 0x0f0d0b09u;  // bytes {1..15 odd}
@@ -147,61 +142,72 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     return r;
 }
 
-// Build the selector table from the raw grid bytes (all threads take part;
-// the caller synchronizes).  iq3: 4-byte entries -> 16-bit selectors.
 __device__ __forceinline__ uint32_t nibble_bit2_mask(uint32_t s8) {
     uint32_t m = 0;
 #pragma unroll
     for (int j = 0; j < 8; j++) m |= ((s8 >> j) & 1u) << (4 * j + 2);
     return m;
 }
-__device__ __forceinline__ void init_iq_tables(IQTables* tb, const uint8_t* grid_g, int grid_bytes, bool iq3,
-                                               bool xxs = false) {
-    if (!iq3) {
-        for (int i = threadIdx.x; i < 256; i += blockDim.x)
-            tb->sgn[i] = nibble_bit2_mask(xxs ? (i & 127) | ((__popc(i & 127) & 1u) << 7) : i);
-    } else {
-        for (int n = threadIdx.x; n < 16; n += blockDim.x) {
-            uint32_t m = 0, inc = 0;
-#pragma unroll
-            for (int j = 0; j < 4; j++)
-                if ((n >> j) & 1) {
-                    m |= 0xffu << (8 * j);
-                    inc |= 1u << (8 * j);
-                }
-            tb->sgn[2 * n] = m;
-            tb->sgn[2 * n + 1] = inc;
-        }
-    }
-    if (!iq3) {
-        for (int e = threadIdx.x; e < grid_bytes / 8; e += blockDim.x) {
-            uint32_t v = 0;
-#pragma unroll
-            for (int j = 0; j < 8; j++) {
-                const uint32_t b = grid_g[8 * e + j];
-                v |= (b == 8u ? 0u : b == 25u ? 1u : 2u) << (4 * j);
-            }
-            tb->sel[e] = v;
-        }
-    } else {
-        uint16_t* s16 = reinterpret_cast<uint16_t*>(tb->sel);
-        for (int e = threadIdx.x; e < grid_bytes / 4; e += blockDim.x) {
-            uint32_t v = 0;
-#pragma unroll
-            for (int j = 0; j < 4; j++) v |= ((uint32_t)(grid_g[4 * e + j] >> 1)) << (4 * j);
-            s16[e] = (uint16_t)v;
-        }
-    }
-}
 
-// Sign handling without tables: bits of a 4-bit pattern n go to the low bit
-// of the 4 bytes (multiply by 2^0+2^7+2^14+2^21, no carries), then
-// negation of those bytes is (g ^ 0xff) + 1 per byte (g > 0: no carry out).
-__device__ __forceinline__ uint32_t nib_inc(uint32_t n) { return ((n & 15u) * 0x00204081u) & 0x01010101u; }
-__device__ __forceinline__ uint32_t signed_bytes(uint32_t g, uint32_t n) {
-    const uint32_t inc = nib_inc(n);
-    return (g ^ (inc * 255u)) + inc;
-}
+template <int F>
+struct IsIQ {
+    static constexpr bool value = F == QW6F_IQ2_XXS || F == QW6F_IQ2_S || F == QW6F_IQ3_S;
+};
+
+// Layout in shared memory (32-bit words): the selector table, then the sign
+// table.
+//   IQ2_XXS: sel 256 entries; sgn 128 masks, indexed by the 7 stored sign bits
+//   IQ2_S:   sel 1024 entries; sgn 256 masks
+//   IQ3_S:   sel 512 16-bit selectors, one per word; sgn 16 (xor, inc) pairs
+// (Per-lane copies of the tables, which make a warp's 32 random lookups one
+// shared-memory wavefront, measured no faster on B200: the IQ kernels wait
+// on instruction latency, not on bank conflicts.)
+template <int F>
+struct IQLut {
+    static constexpr int kSel = F == QW6F_IQ2_S ? 1024 : F == QW6F_IQ3_S ? 512 : 256;
+    static constexpr int kSgn = F == QW6F_IQ2_S ? 256 : F == QW6F_IQ3_S ? 32 : 128;  // words
+    static constexpr size_t bytes = IsIQ<F>::value ? 4 * ((size_t)kSel + kSgn) : 0;
+
+    __device__ __forceinline__ static uint32_t sel(const uint32_t* t, uint32_t e) { return t[e]; }
+    __device__ __forceinline__ static uint32_t sgn(const uint32_t* t, uint32_t e) { return t[kSel + e]; }
+    __device__ __forceinline__ static uint2 sgn2(const uint32_t* t, uint32_t p) {
+        return reinterpret_cast<const uint2*>(t + kSel)[p];
+    }
+
+    // Build the tables from the raw grid bytes (all threads take part; the
+    // caller synchronizes).
+    __device__ static void init(uint32_t* t, const uint8_t* grid_g) {
+        for (int e = threadIdx.x; e < kSel; e += blockDim.x) {
+            uint32_t v = 0;
+            if constexpr (F == QW6F_IQ3_S) {
+#pragma unroll
+                for (int j = 0; j < 4; j++) v |= ((uint32_t)(grid_g[4 * e + j] >> 1)) << (4 * j);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const uint32_t b = grid_g[8 * e + j];
+                    v |= (b == 8u ? 0u : b == 25u ? 1u : 2u) << (4 * j);
+                }
+            }
+            t[e] = v;
+        }
+        if constexpr (F == QW6F_IQ3_S) {
+            for (int n = threadIdx.x; n < 16; n += blockDim.x) {
+                uint32_t m = 0, inc = 0;
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    if ((n >> j) & 1) {
+                        m |= 0xffu << (8 * j);
+                        inc |= 1u << (8 * j);
+                    }
+                reinterpret_cast<uint2*>(t + kSel)[n] = make_uint2(m, inc);
+            }
+        } else {
+            for (int i = threadIdx.x; i < kSgn; i += blockDim.x)
+                t[kSel + i] = nibble_bit2_mask(F == QW6F_IQ2_XXS ? i | ((__popc(i) & 1u) << 7) : i);
+        }
+    }
+};
 
 // --------------------------------------------------- packed tile layout ---
 //
@@ -673,7 +679,7 @@ struct Tile<QW6F_IQ2_XXS, NQ> {
         }
     }
     __device__ __forceinline__ static void dot(const Frag& f, const XView& xv, int b, float (&acc)[2][NQ],
-                                               int lane, const IQTables* tbl) {
+                                               int lane, const uint32_t* tbl) {
         const int t = lane & 3;
         float dfac[2] = {f16f(f.d[0]) * 0.125f, f16f(f.d[1]) * 0.125f};
         int iH[2][NQ], iL[2][NQ];
@@ -690,7 +696,7 @@ struct Tile<QW6F_IQ2_XXS, NQ> {
                 const uint32_t aw = word_of(f.aux[rh][j >> 2], j & 3);
                 const uint32_t sf = (aw >> (7 * t)) & 127u;  // signs of qw6_ksigns(sf) via sgn[]
                 scl[rh] = 2 * (int)(aw >> 28) + 1;
-                const uint32_t ss = tbl->sel[gi] | tbl->sgn[sf];
+                const uint32_t ss = IQLut<QW6F_IQ2_XXS>::sel(tbl, gi) | IQLut<QW6F_IQ2_XXS>::sgn(tbl, sf);
                 lo[rh] = prmt(kIQ2Vals, kIQ2Neg, ss);
                 hi[rh] = prmt(kIQ2Vals, kIQ2Neg, ss >> 16);
             }
@@ -730,7 +736,7 @@ struct Tile<QW6F_IQ2_S, NQ> {
         }
     }
     __device__ __forceinline__ static void dot(const Frag& f, const XView& xv, int b, float (&acc)[2][NQ],
-                                               int lane, const IQTables* tbl) {
+                                               int lane, const uint32_t* tbl) {
         const int t = lane & 3, pr = t >> 1, half4 = 4 * (t & 1);
         float dfac[2] = {f16f(f.d[0]) * 0.125f, f16f(f.d[1]) * 0.125f};
         int iH[2][NQ], iL[2][NQ];
@@ -749,7 +755,9 @@ struct Tile<QW6F_IQ2_S, NQ> {
                     const uint32_t qhb = byte_of(j < 4 ? f.sh[rh].x : f.sh[rh].y, j & 3);
                     const uint32_t gi = ib | (((qhb >> (2 * l)) & 3u) << 8);
                     const uint32_t sb = byte16(f.P[rh][1], 2 * j + hh);
-                    a[rh] = prmt(kIQ2Vals, kIQ2Neg, (tbl->sel[gi] | tbl->sgn[sb]) >> (4 * half4));
+                    a[rh] = prmt(kIQ2Vals, kIQ2Neg,
+                                 (IQLut<QW6F_IQ2_S>::sel(tbl, gi) | IQLut<QW6F_IQ2_S>::sgn(tbl, sb)) >>
+                                     (4 * half4));
                     const uint32_t scb = byte_of(j < 4 ? f.sh[rh].z : f.sh[rh].w, j & 3);
                     scl[rh] = 2 * (int)((scb >> (4 * hh)) & 15u) + 1;
                 }
@@ -791,7 +799,7 @@ struct Tile<QW6F_IQ3_S, NQ> {
         }
     }
     __device__ __forceinline__ static void dot(const Frag& f, const XView& xv, int b, float (&acc)[2][NQ],
-                                               int lane, const IQTables* tbl) {
+                                               int lane, const uint32_t* tbl) {
         const int t = lane & 3;
         float dfac[2] = {f16f(f.d[0]), f16f(f.d[1])};
         int iH[2][NQ], iL[2][NQ];
@@ -807,12 +815,12 @@ struct Tile<QW6F_IQ3_S, NQ> {
                 const uint32_t qhb = byte_of(j < 4 ? f.qh[rh].x : f.qh[rh].y, j & 3);
                 const uint32_t g1 = i1 | (((qhb >> (2 * t)) & 1u) << 8);
                 const uint32_t g2 = i2 | (((qhb >> (2 * t + 1)) & 1u) << 8);
-                const uint16_t* s16 = reinterpret_cast<const uint16_t*>(tbl->sel);
-                const uint32_t gw1 = prmt(kIQ3Lo, kIQ3Hi, s16[g1]);
-                const uint32_t gw2 = prmt(kIQ3Lo, kIQ3Hi, s16[g2]);
+                using Lut = IQLut<QW6F_IQ3_S>;
+                const uint32_t gw1 = prmt(kIQ3Lo, kIQ3Hi, Lut::sel(tbl, g1));
+                const uint32_t gw2 = prmt(kIQ3Lo, kIQ3Hi, Lut::sel(tbl, g2));
                 const uint32_t sb = byte_of(rh ? (j < 4 ? f.c[2].z : f.c[2].w) : (j < 4 ? f.c[2].x : f.c[2].y), j & 3);
-                const uint2 ml = *reinterpret_cast<const uint2*>(&tbl->sgn[2 * (sb & 15u)]);
-                const uint2 mh = *reinterpret_cast<const uint2*>(&tbl->sgn[2 * (sb >> 4)]);
+                const uint2 ml = Lut::sgn2(tbl, sb & 15u);
+                const uint2 mh = Lut::sgn2(tbl, sb >> 4);
                 lo[rh] = (gw1 ^ ml.x) + ml.y;
                 hi[rh] = (gw2 ^ mh.x) + mh.y;
                 const uint32_t scb = byte_of(f.sc[rh], j >> 1);
@@ -834,18 +842,10 @@ struct Tile<QW6F_IQ3_S, NQ> {
 };
 
 // Uniform call shape for the kernels (K formats ignore the tables).
-template <int F>
-struct IsIQ {
-    static constexpr bool value = F == QW6F_IQ2_XXS || F == QW6F_IQ2_S || F == QW6F_IQ3_S;
-};
-template <int F>
-struct GridBytes {
-    static constexpr int value = F == QW6F_IQ2_S ? 8192 : (F == QW6F_IQ2_XXS || F == QW6F_IQ3_S) ? 2048 : 0;
-};
 
 template <int F, int NQ>
 __device__ __forceinline__ void tile_dot(const typename Tile<F, NQ>::Frag& f, const XView& xv, int b,
-                                         float (&acc)[2][NQ], int lane, const IQTables* tbl) {
+                                         float (&acc)[2][NQ], int lane, const uint32_t* tbl) {
     if constexpr (IsIQ<F>::value)
         Tile<F, NQ>::dot(f, xv, b, acc, lane, tbl);
     else

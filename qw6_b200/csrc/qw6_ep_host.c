@@ -41,7 +41,7 @@ struct qw6cu_ep {
     uint8_t **peers_dev;
     uint32_t *epoch, *done_ctas;
     int *abort;
-    int32_t *idx, *cnt_self, *pos, *sendoff, *local_cnt, *send_row, *ucnt, *upos, *ubase;
+    int32_t *idx, *cnt_self, *pos, *sendoff, *local_cnt, *send_row, *ucnt, *upos, *ubase, *eslot;
     float *w;
     void *ws;
     size_t ws_bytes;
@@ -94,7 +94,7 @@ int qw6cu_ep_create(qw6cu_ctx *ctx, uint32_t rank, uint32_t world, uint32_t n_ex
     /* the sorted-mode grouped GEMM over up to cap received rows of epr experts */
     ep->ws_bytes = qw6k_moe_prefill_ws_bytes(ep->cap, hidden, inter, ep->epr, 1);
     size_t off = 0, o_peers, o_epoch, o_idx, o_w, o_cnt, o_pos, o_send, o_local, o_row, o_ucnt, o_upos, o_ubase,
-           o_ws;
+           o_eslot, o_ws;
     o_peers = off; off += al256(QW6K_EP_MAX_WORLD * sizeof(void *));
     o_epoch = off; off += 256; /* epoch, abort, done_ctas */
     o_idx = off; off += al256(n * 4);
@@ -107,6 +107,7 @@ int qw6cu_ep_create(qw6cu_ctx *ctx, uint32_t rank, uint32_t world, uint32_t n_ex
     o_ucnt = off; off += al256(QW6K_EP_MAX_WORLD * 4);
     o_upos = off; off += al256(n * 4);
     o_ubase = off; off += al256(QW6K_EP_MAX_WORLD * 4);
+    o_eslot = off; off += al256(256 * 4);
     o_ws = off; off += al256(ep->ws_bytes);
     e = cudaMalloc((void **)&ep->priv, off);
     if (e != cudaSuccess) {
@@ -128,10 +129,16 @@ int qw6cu_ep_create(qw6cu_ctx *ctx, uint32_t rank, uint32_t world, uint32_t n_ex
     ep->ucnt = (int32_t *)(ep->priv + o_ucnt);
     ep->upos = (int32_t *)(ep->priv + o_upos);
     ep->ubase = (int32_t *)(ep->priv + o_ubase);
+    ep->eslot = (int32_t *)(ep->priv + o_eslot);
     ep->ws = ep->priv + o_ws;
-    /* signals and counts start at zero (epoch 0 = nothing published) */
+    /* signals and counts start at zero (epoch 0 = nothing published); rank r
+     * owns experts [r*epr, (r+1)*epr) until qw6cu_ep_set_placement */
+    int32_t ident[256];
+    for (uint32_t g = 0; g < n_experts; g++) ident[g] = (int32_t)g;
     if ((e = cudaMemset(ep->region, 0, ep->o_rx)) != cudaSuccess ||
-        (e = cudaMemset(ep->priv, 0, o_ws)) != cudaSuccess || (e = cudaDeviceSynchronize()) != cudaSuccess) {
+        (e = cudaMemset(ep->priv, 0, o_ws)) != cudaSuccess ||
+        (e = cudaMemcpy(ep->eslot, ident, n_experts * sizeof(int32_t), cudaMemcpyHostToDevice)) != cudaSuccess ||
+        (e = cudaDeviceSynchronize()) != cudaSuccess) {
         qw6cu_ep_destroy(ep);
         return ep_fail("qw6cu_ep_create: cudaMemset", e);
     }
@@ -177,6 +184,28 @@ int qw6cu_ep_connect(qw6cu_ep *ep, const void *handles) {
     if (e != cudaSuccess) return ep_fail("qw6cu_ep_connect: cudaMemcpy", e);
     ep->connected = 1;
     return 0;
+}
+
+int qw6cu_ep_set_placement(qw6cu_ep *ep, const uint32_t *experts) {
+    if (!ep || !experts) {
+        qw6h_set_err("qw6cu_ep_set_placement: null argument");
+        return QW6CU_ERR_ARG;
+    }
+    int32_t slot[256];
+    for (uint32_t g = 0; g < ep->ne; g++) slot[g] = -1;
+    for (uint32_t i = 0; i < ep->ne; i++) {
+        if (experts[i] >= ep->ne || slot[experts[i]] >= 0) {
+            qw6h_set_err("qw6cu_ep_set_placement: experts is not a permutation of 0..n_experts-1 (entry %u)", i);
+            return QW6CU_ERR_ARG;
+        }
+        slot[experts[i]] = (int32_t)i;
+    }
+    int rc = qw6h_use(ep->ctx);
+    if (rc) return rc;
+    /* ordered on the layer's stream: steps enqueued before keep the old placement */
+    cudaError_t e = cudaMemcpyAsync(ep->eslot, slot, ep->ne * sizeof(int32_t), cudaMemcpyHostToDevice, ep->ctx->st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ep->ctx->st);
+    return e == cudaSuccess ? 0 : ep_fail("qw6cu_ep_set_placement", e);
 }
 
 void qw6cu_ep_destroy(qw6cu_ep *ep) {
@@ -229,6 +258,7 @@ int qw6cu_ep_layer(qw6cu_ep *ep, const qw6cu_expert_pack *gate, const qw6cu_expe
     d.err = err;
     d.idx = ep->idx;
     d.w = ep->w;
+    d.eslot = ep->eslot;
     d.cnt_self = ep->cnt_self;
     d.pos = ep->pos;
     d.ucnt = ep->ucnt;

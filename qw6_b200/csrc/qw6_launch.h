@@ -137,14 +137,16 @@ int qw6k_ep_combine(const void *ret_bf16, const float *w, const int32_t *send_po
 /* Expert parallelism over peer memory (k_ep.cu, phases of one layer).
  * Every rank holds one symmetric region with the same layout: signal words
  * (3 kinds x 64 sources, u32 epochs), a double-buffered count matrix
- * [2][world][ne + world] (i32: rows per expert, then unique token rows per
- * owner), received token rows rx [cap][hidden] (bf16, one per (source,
- * token) pair), per received slot (expert-major) smeta [cap] (i32 pairs:
+ * [2][world][ne + world] (u32: rows per expert, then unique token rows per
+ * owner, each below 2^24 and tagged with the step's epoch in its top 8
+ * bits, so that an entry is its own arrival signal), received token rows
+ * rx [cap][hidden] (bf16, one per (source, token) pair), per received slot (expert-major) smeta [cap] (i32 pairs:
  * its row in rx, and the destination of its output as source rank * nmax +
  * source assignment), and the returned expert outputs of this rank's own
  * assignments ret [nmax][hidden] (bf16, written by the owners' down GEMM);
  * peers[p] is rank p's region as mapped in this process. */
 #define QW6K_EP_MAX_WORLD 64
+/* wait kinds (41 + kind is the timeout error); counts need no signal word */
 enum { QW6K_EP_SIG_COUNTS = 0, QW6K_EP_SIG_ROWS = 1, QW6K_EP_SIG_DONE = 2 };
 typedef struct {
     uint8_t *const *peers; /* device array [world] */
@@ -156,7 +158,9 @@ typedef struct {
     int *err;            /* error word: 41 + phase kind of a wait that timed out */
     const int32_t *idx;  /* [ntok*topk] routing of this rank's tokens */
     const float *w;
-    int32_t *cnt_self, *pos;  /* [ne] rows per global expert, [ntok*topk] position among its expert's */
+    const int32_t *eslot; /* [ne] placed index of each routed expert id: rank eslot / (ne/world) owns it,
+                             as its local expert eslot % (ne/world); everything below is in placed ids */
+    int32_t *cnt_self, *pos;  /* [ne] rows per placed expert, [ntok*topk] position among its expert's */
     int32_t *ucnt, *upos;     /* [world] unique token rows per owner, [ntok*topk] position of the
                                  assignment's token row among them (-1 - position: a later slot of a
                                  token already sent to that owner) */

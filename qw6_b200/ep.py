@@ -27,6 +27,7 @@ kernel reads them.
 """
 from __future__ import annotations
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -137,6 +138,52 @@ def ep_moe_prefill(backend, logits: torch.Tensor, x_bf16: torch.Tensor, top_k: i
     return backend.combine(ret, w, send_pos, ntok, top_k)
 
 
+def balance_experts(counts, world: int) -> "np.ndarray":
+    """Expert placement for `world` ranks from per-expert routing counts
+    (rows per expert over a calibration sample), the same idea as an
+    expert-parallel load balancer: every rank holds n_experts/world experts
+    and the ranks' row totals are evened out -- experts in decreasing count
+    go to the least-loaded rank with room left, then pairs are swapped
+    between the heaviest rank and a lighter one while that lowers the
+    heavier total.  Returns int32 [world, n_experts/world] (rank r's experts,
+    ascending); flattened it is the `experts` array of qw6cu_ep_set_placement.
+    Placement never changes a result bit: each expert's rows go through the
+    same GEMM arithmetic on whichever rank holds it."""
+    counts = np.asarray(counts, dtype=np.int64)
+    ne = counts.shape[0]
+    if world < 1 or ne % world:
+        raise ValueError("n_experts must be a multiple of world")
+    epr = ne // world
+    members = [[] for _ in range(world)]
+    load = np.zeros(world, np.int64)
+    for g in np.argsort(-counts, kind="stable"):
+        r = min((r for r in range(world) if len(members[r]) < epr), key=lambda r: (load[r], r))
+        members[r].append(int(g))
+        load[r] += counts[g]
+    while True:  # every swap lowers the sum of squared loads, so this ends
+        hi = int(np.argmax(load))
+        done = True
+        for lo in np.argsort(load, kind="stable"):
+            gap = load[hi] - load[lo]
+            if lo == hi or gap <= 1:
+                continue
+            ca = counts[members[hi]][:, None]
+            cb = counts[members[lo]][None, :]
+            d = ca - cb
+            score = np.where((d > 0) & (d < gap), np.abs(gap - 2 * d), np.iinfo(np.int64).max)
+            i, j = np.unravel_index(int(np.argmin(score)), score.shape)
+            if score[i, j] == np.iinfo(np.int64).max:
+                continue
+            a, b = members[hi][i], members[lo][j]
+            members[hi][i], members[lo][j] = b, a
+            load[hi] -= counts[a] - counts[b]
+            load[lo] += counts[a] - counts[b]
+            done = False
+            break
+        if done:
+            return np.array([sorted(m) for m in members], dtype=np.int32)
+
+
 class PeerMoE:
     """The peer-memory expert-parallel layer (libqw6cuda qw6cu_ep_*): token
     rows and expert outputs move over NVLink by loads/stores in this
@@ -147,7 +194,10 @@ class PeerMoE:
     `ep_moe_prefill` and to the single-GPU layer."""
 
     def __init__(self, ctx: L.Context, gate: L.ExpertPack, up: L.ExpertPack, down: L.ExpertPack, n_experts: int,
-                 top_k: int, hidden: int, inter: int, max_tokens: int, group=None):
+                 top_k: int, hidden: int, inter: int, max_tokens: int, group=None, placement=None):
+        """placement: None (rank r holds experts [r*epr, (r+1)*epr)) or an
+        int array [world, epr] as from `balance_experts`, the same on every
+        rank; the packs then hold this rank's row of it, in that order."""
         world = dist.get_world_size(group) if dist.is_initialized() else 1
         rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.ctx, self.packs, self.hidden, self.max_tokens = ctx, (gate, up, down), hidden, max_tokens
@@ -160,6 +210,11 @@ class PeerMoE:
         else:
             allh = [mine]
         self.ep.connect(allh)
+        if placement is not None:
+            pl = np.asarray(placement, dtype=np.int64)
+            if pl.shape != (world, n_experts // world):
+                raise ValueError(f"placement must have shape ({world}, {n_experts // world})")
+            self.ep.set_placement(pl.reshape(-1))
         if world > 1:
             dist.barrier(group=group)
 

@@ -115,6 +115,7 @@ def load() -> C.CDLL:
     lib.qw6cu_ep_handle.argtypes = [_vp, _vp]
     lib.qw6cu_ep_connect.argtypes = [_vp, _vp]
     lib.qw6cu_ep_layer.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32]
+    lib.qw6cu_ep_set_placement.argtypes = [_vp, _vp]
     lib.qw6cu_ep_last_rows.argtypes = [_vp, C.POINTER(_u32)]
     lib.qw6cu_ep_destroy.argtypes = [_vp]
     lib.qw6cu_ep_destroy.restype = None
@@ -337,7 +338,8 @@ class Context:
 
 class PeerEP:
     """A qw6cu_ep: this rank's endpoint of the peer-memory expert-parallel
-    MoE layer (experts sharded contiguously over `world` ranks)."""
+    MoE layer (experts sharded over `world` ranks: contiguously, or as
+    `set_placement` says)."""
 
     def __init__(self, ctx: Context, rank: int, world: int, n_experts: int, top_k: int, hidden: int, inter: int,
                  max_tokens: int) -> None:
@@ -363,6 +365,12 @@ class PeerEP:
     def layer(self, gate: ExpertPack, up: ExpertPack, down: ExpertPack, logits, x_bf16, out, ntok) -> None:
         _check(self.lib.qw6cu_ep_layer(self.h, C.byref(gate), C.byref(up), C.byref(down), logits, x_bf16, out, ntok),
                "qw6cu_ep_layer")
+
+    def set_placement(self, experts) -> None:
+        """experts: n_experts routed expert ids, rank r's local experts at
+        [r*epr, (r+1)*epr) (the same on every rank)."""
+        arr = (_u32 * len(experts))(*[int(e) for e in experts])
+        _check(self.lib.qw6cu_ep_set_placement(self.h, arr), "qw6cu_ep_set_placement")
 
     def last_rows(self) -> int:
         r = _u32()

@@ -119,14 +119,25 @@ def bf16_to_f32(h: np.ndarray) -> np.ndarray:
     return (h.astype(np.uint32) << 16).view(np.float32)
 
 
-def config3(seed: int = 3, ntok: int = 4096, n_experts: int = N_EXPERTS):
-    """Prefill MoE: logits N(0,1) + per-expert bias N(0,0.5); X bf16."""
+def config3(seed: int = 3, ntok: int = 4096, n_experts: int = N_EXPERTS, with_bias: bool = False):
+    """Prefill MoE: logits N(0,1) + per-expert bias N(0,0.5); X bf16.
+    with_bias: also return the router bias (the model's share of the
+    logits), from which `router_sample` draws independent token batches."""
     rng = np.random.Generator(np.random.PCG64(seed))
     gate, up, down = moe_weights(rng, n_experts)
     bias = (rng.standard_normal(n_experts) * 0.5).astype(np.float32)
     logits = rng.standard_normal((ntok, n_experts), dtype=np.float32) + bias[None, :]
     x = bf16_round(rng.standard_normal((ntok, HIDDEN), dtype=np.float32))
+    if with_bias:
+        return gate, up, down, logits.astype(np.float32), x, bias
     return gate, up, down, logits.astype(np.float32), x
+
+
+def router_sample(bias: np.ndarray, ntok: int, seed: int) -> np.ndarray:
+    """Router logits of another batch of the same model as config3: fresh
+    N(0,1) token noise plus the given per-expert bias."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    return (rng.standard_normal((ntok, bias.shape[0]), dtype=np.float32) + bias[None, :]).astype(np.float32)
 
 
 def config4(seed: int = 4, batch: int = 1, vocab: int = VOCAB):

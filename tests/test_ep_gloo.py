@@ -123,3 +123,36 @@ def test_ep_prefill_two_gloo_ranks(oracle):
     out = np.concatenate([got[0], got[1]])
     err = float(np.max(np.abs(out - ref)) / np.max(np.abs(ref)))
     assert err <= 1e-5, err
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_balance_experts(world):
+    """Placement: a permutation with n_experts/world experts per rank, no
+    heavier than contiguous sharding, within one expert's count of the mean
+    on config 3's skewed routing, and the same on every call."""
+    from qw6_b200.ep import balance_experts
+    _, _, _, logits, _, bias = S.config3(ntok=1024, with_bias=True)
+    cnt = np.bincount(np.argsort(-logits, axis=1, kind="stable")[:, :8].ravel(), minlength=logits.shape[1])
+    pl = balance_experts(cnt, world)
+    ne = cnt.shape[0]
+    assert pl.shape == (world, ne // world)
+    assert np.array_equal(np.sort(pl.reshape(-1)), np.arange(ne))
+    load = cnt[pl].sum(axis=1)
+    contiguous = cnt.reshape(world, -1).sum(axis=1)
+    assert load.max() <= contiguous.max()
+    assert load.max() - cnt.sum() / world <= cnt.max(), (load, cnt.max())
+    assert np.array_equal(pl, balance_experts(cnt, world))
+    # an independent batch of the same router balances the measured one almost as well
+    cal = S.router_sample(bias, 1024, seed=11)
+    ccnt = np.bincount(np.argsort(-cal, axis=1, kind="stable")[:, :8].ravel(), minlength=ne)
+    if world > 1:
+        assert cnt[balance_experts(ccnt, world)].sum(axis=1).max() < contiguous.max()
+
+
+def test_balance_experts_edges():
+    from qw6_b200.ep import balance_experts
+    assert np.array_equal(balance_experts(np.zeros(8, np.int64), 2), [[0, 1, 2, 3], [4, 5, 6, 7]])  # ties: contiguous
+    pl = balance_experts([100, 0, 0, 0], 4)
+    assert sorted(pl.reshape(-1).tolist()) == [0, 1, 2, 3]
+    with pytest.raises(ValueError):
+        balance_experts(np.ones(6), 4)

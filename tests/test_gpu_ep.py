@@ -3,8 +3,9 @@
 Each of `world` ranks (one spawned process per GPU) owns E/world experts and
 T/world tokens and runs (a) qw6_b200.ep.ep_moe_prefill over NCCL
 all-to-alls and (b) qw6_b200.ep.PeerMoE (libqw6cuda's own dispatch/combine
-kernels over peer memory) three times in a row and once more as a replayed
-CUDA graph.  Every gathered output must equal, bit for bit, the single-GPU
+kernels over peer memory) three times in a row, once more as a replayed
+CUDA graph and once with the experts placed by a permutation.  Every
+gathered output must equal, bit for bit, the single-GPU
 qw6cu_moe_prefill on all tokens (same expert outputs, same slot-order
 combine), and match the CPU oracle's composition on a seeded sample of
 tokens within 2e-2 (the bf16 tensor-core prefill tolerance).  world=1 runs
@@ -33,15 +34,16 @@ def _data(case):
     return gate, up, down, logits, xbits
 
 
-def _pack_all(ctx, torch, L, mats, lo, hi):
+def _pack_all(ctx, torch, L, mats, lo, hi, ids=None):
     packs, held = [], []
+    ids = np.arange(lo, hi) if ids is None else np.asarray(ids)
     for qq, m, r, c in mats:
-        mine = np.ascontiguousarray(m[lo:hi])
+        mine = np.ascontiguousarray(m[ids])
         pb = ctx.packed_bytes(qq, r, c)
         raw = torch.from_numpy(mine.reshape(-1)).cuda()
-        pk = torch.empty(pb * (hi - lo), dtype=torch.uint8, device="cuda")
+        pk = torch.empty(pb * len(ids), dtype=torch.uint8, device="cuda")
         torch.cuda.synchronize()
-        ctx.pack(qq, raw.data_ptr(), pk.data_ptr(), r, c, hi - lo, mine[0].nbytes, pb)
+        ctx.pack(qq, raw.data_ptr(), pk.data_ptr(), r, c, len(ids), mine[0].nbytes, pb)
         ctx.synchronize()
         held.append(pk)
         packs.append(L.ExpertPack(qq, pk.data_ptr(), pb))
@@ -91,6 +93,14 @@ def _rank(rank, world, port, case, q):
         peer.append(gout.cpu().numpy())
         del g
         pm.close()
+        # experts placed by a (seeded) permutation instead of contiguous blocks
+        pl = np.random.Generator(np.random.PCG64(77)).permutation(E).reshape(world, epr).astype(np.int32)
+        ppacks, pheld = _pack_all(ctx, torch, L, mats, 0, 0, pl[rank])
+        pm = PeerMoE(ctx, ppacks[0], ppacks[1], ppacks[2], E, K, H, I, tpr, placement=pl)
+        peer.append(pm(lg, x).cpu().numpy())
+        ctx.check_device_errors()
+        pm.close()
+        del pheld
         full = None
         if rank == 0:  # single-GPU reference over all tokens and experts
             ctx.set_stream(None)
@@ -139,7 +149,7 @@ def test_ep_prefill_nccl(world, case, oracle):
     out = np.concatenate([got[r][0] for r in range(world)])
     full = got[0][2]
     assert np.array_equal(out.view(np.uint32), full.view(np.uint32)), float(np.max(np.abs(out - full)))
-    for i in range(4):  # three eager peer steps, then the graph replay
+    for i in range(5):  # three eager peer steps, the graph replay, the permuted placement
         peer = np.concatenate([got[r][1][i] for r in range(world)])
         assert np.array_equal(peer.view(np.uint32), full.view(np.uint32)), (i, float(np.nanmax(np.abs(peer - full))))
     gate, up, down, logits, xbits = _data(case)
