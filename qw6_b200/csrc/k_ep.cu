@@ -490,8 +490,12 @@ extern "C" int qw6k_ep_p2p_phase(const qw6k_ep_desc* d, int phase, cudaStream_t 
         e = launch_pdl(k_ep_publish, dim3(1), dim3(256), 0, st, *d);
         break;
     case 1: {
-        const uint32_t n = d->ntok * d->topk, ctas = (n + 7) / 8;
-        e = launch_pdl(k_ep_dispatch, dim3(ctas < 296u ? ctas : 296u), dim3(256), 0, st, *d);
+        // a warp per assignment up to a grid that stays resident (4 CTAs of
+        // 256 threads per SM at the kernel's register count): each warp's
+        // loop is a chain of dependent loads, so fewer rounds per warp is
+        // what shortens the dispatch
+        const uint32_t n = d->ntok * d->topk, ctas = (n + 7) / 8, cap = 4u * 148u;
+        e = launch_pdl(k_ep_dispatch, dim3(ctas < cap ? ctas : cap), dim3(256), 0, st, *d);
         break;
     }
     case 2:
