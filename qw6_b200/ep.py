@@ -61,6 +61,10 @@ class CudaBackend:
         self._bind().moe_route(logits.data_ptr(), ntok, n_experts, top_k, idx.data_ptr(), w.data_ptr())
         return idx, w
 
+    def place(self, idx, eslot):
+        """Routed expert ids -> placed ids (eslot: int32 numpy [n_experts])."""
+        return torch.as_tensor(eslot, device=self.device).index_select(0, idx.long()).to(torch.int32)
+
     def count(self, idx, n, n_experts):
         cnt = self.empty((n_experts,), torch.int32)
         pos = self.empty((n,), torch.int32)
@@ -100,28 +104,56 @@ class CudaBackend:
         return out
 
 
+def placement_slots(placement, world: int, n_experts: int):
+    """Validate an expert placement ([world, n_experts/world] routed ids, as
+    from `balance_experts`) and return (eslot, identity): eslot[routed id] =
+    placed id (rank * epr + local index) as int32."""
+    pl = np.asarray(placement, dtype=np.int64)
+    if pl.shape != (world, n_experts // world):
+        raise ValueError(f"placement must have shape ({world}, {n_experts // world})")
+    flat = pl.reshape(-1)
+    if not np.array_equal(np.sort(flat), np.arange(n_experts)):
+        raise ValueError("placement is not a permutation of the experts")
+    eslot = np.empty(n_experts, np.int32)
+    eslot[flat] = np.arange(n_experts, dtype=np.int32)
+    return eslot, bool(np.array_equal(flat, np.arange(n_experts)))
+
+
+def _all_to_all(out, inp, out_splits=None, in_splits=None, group=None):
+    if not dist.is_initialized() or dist.get_world_size(group) == 1:
+        out.copy_(inp)
+    else:
+        dist.all_to_all_single(out, inp, out_splits, in_splits, group=group)
+
+
 def ep_moe_prefill(backend, logits: torch.Tensor, x_bf16: torch.Tensor, top_k: int, n_experts: int,
-                   group=None, stats: dict | None = None) -> torch.Tensor:
+                   group=None, stats: dict | None = None, placement=None) -> torch.Tensor:
     """One routed-MoE layer for this rank's tokens with experts sharded over
     `group`.  logits [T x n_experts] fp32, x_bf16 [T x hidden] bf16 (this
     rank's tokens); returns out [T x hidden] fp32.  Without a process group
     (or with one rank) the backend holds all experts and runs the layer
-    locally.  `stats`, when given, receives the number of rows this rank's
-    experts processed ("rows")."""
+    locally.  `placement` (None: rank r holds experts [r*epr, (r+1)*epr)) is
+    an int array [world, epr] as from `balance_experts`, the same on every
+    rank; the backend's local expert j is then placement[rank][j].  Results
+    do not depend on it.  `stats`, when given, receives the number of rows
+    this rank's experts processed ("rows")."""
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     ntok, hidden = x_bf16.shape
     n = ntok * top_k
     if n_experts % world or n_experts > 256:
         raise ValueError(f"{n_experts} experts do not shard evenly over {world} ranks")
-    if world == 1 and hasattr(backend, "local_layer"):
+    eslot, identity = placement_slots(placement, world, n_experts) if placement is not None else (None, True)
+    if world == 1 and identity and hasattr(backend, "local_layer"):
         if stats is not None:
             stats["rows"] = n
         return backend.local_layer(logits, x_bf16, ntok, n_experts, top_k)
     epr = n_experts // world
     idx, w = backend.route(logits, ntok, n_experts, top_k)
+    if not identity:  # every later step works in placed ids: owner = id // epr
+        idx = backend.place(idx, eslot)
     cnt, pos = backend.count(idx, n, n_experts)
     recv_cnt = torch.empty_like(cnt)  # [source][local expert]
-    dist.all_to_all_single(recv_cnt, cnt, group=group)
+    _all_to_all(recv_cnt, cnt, group=group)
     counts = torch.cat([cnt, recv_cnt]).cpu()  # split sizes are host-side lists
     send_counts = counts[:n_experts].view(world, epr).sum(1).tolist()
     recv_counts = counts[n_experts:].view(world, epr).sum(1).tolist()
@@ -130,11 +162,11 @@ def ep_moe_prefill(backend, logits: torch.Tensor, x_bf16: torch.Tensor, top_k: i
         stats["rows"] = nrecv
     send_x, send_pos = backend.pack(idx, pos, cnt, n, top_k, n_experts, x_bf16)
     recv_x = backend.empty((nrecv, hidden), x_bf16.dtype)
-    dist.all_to_all_single(recv_x, send_x, recv_counts, send_counts, group=group)
+    _all_to_all(recv_x, send_x, recv_counts, send_counts, group=group)
     row_e = backend.expand(recv_cnt, world, nrecv)
     recv_out = backend.expert_rows(recv_x, row_e, nrecv)
     ret = backend.empty((n, hidden), recv_out.dtype)
-    dist.all_to_all_single(ret, recv_out, send_counts, recv_counts, group=group)
+    _all_to_all(ret, recv_out, send_counts, recv_counts, group=group)
     return backend.combine(ret, w, send_pos, ntok, top_k)
 
 
@@ -211,10 +243,8 @@ class PeerMoE:
             allh = [mine]
         self.ep.connect(allh)
         if placement is not None:
-            pl = np.asarray(placement, dtype=np.int64)
-            if pl.shape != (world, n_experts // world):
-                raise ValueError(f"placement must have shape ({world}, {n_experts // world})")
-            self.ep.set_placement(pl.reshape(-1))
+            placement_slots(placement, world, n_experts)  # shape and permutation checks
+            self.ep.set_placement(np.asarray(placement, dtype=np.int64).reshape(-1))
         if world > 1:
             dist.barrier(group=group)
 

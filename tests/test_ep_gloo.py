@@ -25,10 +25,15 @@ class OracleBackend:
 
     out_dtype = torch.float32
 
-    def __init__(self, gate, up, down, epr, rank):
+    def __init__(self, gate, up, down, epr, rank, experts=None):
         from oracle.oracle import Oracle
         self.o = Oracle()
         self.gate, self.up, self.down, self.epr, self.rank = gate, up, down, epr, rank
+        # routed id of local expert j (contiguous sharding unless placed)
+        self.experts = list(range(rank * epr, (rank + 1) * epr)) if experts is None else [int(e) for e in experts]
+
+    def place(self, idx, eslot):
+        return torch.from_numpy(np.asarray(eslot)[idx.numpy()].astype(np.int32))
 
     def empty(self, shape, dtype):
         return torch.empty(shape, dtype=dtype)
@@ -62,7 +67,7 @@ class OracleBackend:
         out = np.zeros((nrecv, H), np.float32)
         xs = recv_x.float().numpy()
         for r in range(nrecv):
-            e = self.rank * self.epr + int(row_e[r])
+            e = self.experts[int(row_e[r])]
             g = self.o.matvec(S.Q4_K, self.gate[e], xs[r], I, H)
             u = self.o.matvec(S.Q4_K, self.up[e], xs[r], I, H)
             out[r] = self.o.matvec(S.Q6_K, self.down[e], self.o.silu_mul(g, u), H, I)
@@ -96,7 +101,12 @@ def _rank(rank, world, port, q):
         x = torch.from_numpy(S.bf16_to_f32(xbits[sl])).to(torch.bfloat16)
         be = OracleBackend(gate, up, down, E // world, rank)
         out = ep_moe_prefill(be, torch.from_numpy(logits[sl]), x, K, E)
-        q.put((rank, out.numpy()))
+        # the same layer with the experts placed by a permutation
+        pl = np.random.Generator(np.random.PCG64(41)).permutation(E).reshape(world, E // world)
+        bp = OracleBackend(gate, up, down, E // world, rank, experts=pl[rank])
+        stats = {}
+        outp = ep_moe_prefill(bp, torch.from_numpy(logits[sl]), x, K, E, stats=stats, placement=pl)
+        q.put((rank, (out.numpy(), outp.numpy(), stats["rows"])))
     finally:
         dist.destroy_process_group()
 
@@ -120,9 +130,24 @@ def test_ep_prefill_two_gloo_ranks(oracle):
         assert p.exitcode == 0
     gate, up, down, logits, xbits = _data()
     ref, _, _ = oracle.moe_layer(S.Q4_K, gate, up, S.Q6_K, down, logits, S.bf16_to_f32(xbits), top_k=K)
-    out = np.concatenate([got[0], got[1]])
+    out = np.concatenate([got[0][0], got[1][0]])
     err = float(np.max(np.abs(out - ref)) / np.max(np.abs(ref)))
     assert err <= 1e-5, err
+    # placement changes which rank computes an expert, never a result bit
+    outp = np.concatenate([got[0][1], got[1][1]])
+    assert np.array_equal(outp.view(np.uint32), out.view(np.uint32))
+    assert got[0][2] + got[1][2] == 2 * T_PER_RANK * K
+
+
+def test_placement_slots():
+    from qw6_b200.ep import placement_slots
+    eslot, ident = placement_slots([[2, 0], [3, 1]], 2, 4)
+    assert eslot.tolist() == [1, 3, 0, 2] and not ident
+    assert placement_slots(np.arange(4).reshape(2, 2), 2, 4)[1]
+    with pytest.raises(ValueError):
+        placement_slots([[0, 0], [1, 2]], 2, 4)  # not a permutation
+    with pytest.raises(ValueError):
+        placement_slots([[0, 1, 2, 3]], 2, 4)  # wrong shape
 
 
 @pytest.mark.parametrize("world", [1, 2, 4, 8])

@@ -3,8 +3,8 @@
 Each of `world` ranks (one spawned process per GPU) owns E/world experts and
 T/world tokens and runs (a) qw6_b200.ep.ep_moe_prefill over NCCL
 all-to-alls and (b) qw6_b200.ep.PeerMoE (libqw6cuda's own dispatch/combine
-kernels over peer memory) three times in a row, once more as a replayed
-CUDA graph and once with the experts placed by a permutation.  Every
+kernels over peer memory) three times in a row and once more as a replayed
+CUDA graph; then both with the experts placed by a permutation.  Every
 gathered output must equal, bit for bit, the single-GPU
 qw6cu_moe_prefill on all tokens (same expert outputs, same slot-order
 combine), and match the CPU oracle's composition on a seeded sample of
@@ -100,6 +100,12 @@ def _rank(rank, world, port, case, q):
         peer.append(pm(lg, x).cpu().numpy())
         ctx.check_device_errors()
         pm.close()
+        # ... and the NCCL form with the same placement
+        ctx.set_stream(None)
+        bp = CudaBackend(ctx, ppacks[0], ppacks[1], ppacks[2], H, I, epr)
+        torch.cuda.synchronize()
+        peer.append(ep_moe_prefill(bp, lg, x, K, E, placement=pl).cpu().numpy())
+        ctx.check_device_errors()
         del pheld
         full = None
         if rank == 0:  # single-GPU reference over all tokens and experts
@@ -149,7 +155,7 @@ def test_ep_prefill_nccl(world, case, oracle):
     out = np.concatenate([got[r][0] for r in range(world)])
     full = got[0][2]
     assert np.array_equal(out.view(np.uint32), full.view(np.uint32)), float(np.max(np.abs(out - full)))
-    for i in range(5):  # three eager peer steps, the graph replay, the permuted placement
+    for i in range(6):  # three eager peer steps, the graph replay, the permuted placement (peer, NCCL)
         peer = np.concatenate([got[r][1][i] for r in range(world)])
         assert np.array_equal(peer.view(np.uint32), full.view(np.uint32)), (i, float(np.nanmax(np.abs(peer - full))))
     gate, up, down, logits, xbits = _data(case)
