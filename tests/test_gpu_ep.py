@@ -160,6 +160,9 @@ def test_ep_prefill_nccl(world, case, oracle):
         assert np.array_equal(peer.view(np.uint32), full.view(np.uint32)), (i, float(np.nanmax(np.abs(peer - full))))
     gate, up, down, logits, xbits = _data(case)
     toks = np.random.Generator(np.random.PCG64(5)).choice(T, 24, replace=False)
-    ref, _, _ = oracle.moe_layer(S.Q4_K, gate, up, S.Q6_K, down, logits[toks], S.bf16_to_f32(xbits[toks]), top_k=K)
-    errs = [float(np.max(np.abs(out[t] - ref[i])) / np.max(np.abs(ref[i]))) for i, t in enumerate(toks)]
-    assert max(errs) <= 2e-2, max(errs)
+    x32 = S.bf16_to_f32(xbits[toks])
+    ref, _, _ = oracle.moe_layer(S.Q4_K, gate, up, S.Q6_K, down, logits[toks], x32, top_k=K)
+    ref64 = oracle.moe_layer(S.Q4_K, gate, up, S.Q6_K, down, logits[toks], x32, top_k=K, f64=True)
+    for r in (ref, ref64):  # the fp32 oracle and its float64 recomputation
+        errs = [float(np.max(np.abs(out[t] - r[i])) / np.max(np.abs(r[i]))) for i, t in enumerate(toks)]
+        assert max(errs) <= 2e-2, max(errs)

@@ -31,10 +31,16 @@ def run_prefill(cuda, gq, gate, up, dq, down, logits, x_bf16_bits, top_k):
 
 
 def check_tokens(oracle, gq, gate, up, dq, down, logits, xbits, out, tokens, top_k):
+    """Max relative error of the sampled tokens against the fp32 oracle and
+    against its float64 recomputation (which shows the fp32 oracle's own
+    accumulation-order noise); both within the bf16 prefill tolerance."""
     x32 = S.bf16_to_f32(xbits)
     ref, _, _ = oracle.moe_layer(gq, gate, up, dq, down, logits[tokens], x32[tokens], top_k=top_k)
+    ref64 = oracle.moe_layer(gq, gate, up, dq, down, logits[tokens], x32[tokens], top_k=top_k, f64=True)
     errs = [rel_err(out[t], ref[i]) for i, t in enumerate(tokens)]
+    errs64 = [rel_err(out[t], ref64[i]) for i, t in enumerate(tokens)]
     assert max(errs) <= TOL, max(errs)
+    assert max(errs64) <= TOL, max(errs64)
     return max(errs)
 
 
