@@ -45,6 +45,10 @@ class _ExpertPack(C.Structure):
     _fields_ = [("quant", C.c_uint32), ("base", C.c_void_p), ("stride", C.c_size_t)]
 
 
+class _Matrix(C.Structure):
+    _fields_ = [("quant", C.c_uint32), ("w", C.c_void_p)]
+
+
 class Oracle:
     """C restatement (qw6_oracle.c)."""
 
@@ -69,6 +73,11 @@ class Oracle:
                                      C.c_uint32, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p]
         lib.qo_moe_layer_f64.argtypes = [pk, pk, pk, _f32p, _f32p, _f64p, C.c_uint32, C.c_uint32,
                                          C.c_uint32, C.c_uint32, C.c_uint32]
+        lib.qo_rmsnorm.argtypes = [_f32p, _f32p, _f32p, C.c_uint32]
+        lib.qo_rmsnorm.restype = None
+        mp = C.POINTER(_Matrix)
+        lib.qo_moe_block.argtypes = [_f32p, _f32p, mp, pk, pk, pk, mp, mp, mp, mp, _f32p, C.c_uint32, C.c_uint32,
+                                     C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32]
         self.lib = lib
 
     def fp16_to_f32(self, h: int) -> float:
@@ -132,6 +141,47 @@ class Oracle:
         arr = _u8(arr)
         return _ExpertPack(quant, arr.ctypes.data, arr[0].nbytes), arr
 
+    def rmsnorm(self, x, w):
+        """qw6_cpu_rmsnorm (qw6.c:2502-2512)."""
+        x = np.ascontiguousarray(x, np.float32)
+        w = np.ascontiguousarray(w, np.float32)
+        out = np.empty_like(x)
+        self.lib.qo_rmsnorm(x, w, out, x.size)
+        return out
+
+    def moe_block(self, x, norm_w, router, experts, shared=None, top_k=8):
+        """The MoE FFN block around qw6_apply_layer_moe (qw6.c:2474-2484,
+        2226-2290) for every token row of x: rmsnorm, router matvec, routed
+        experts, the optional shared expert with its sigmoid gate, residual
+        add.  router: (quant, matrix [n_experts rows]); experts: (gq, gate,
+        up, dq, down) as for moe_layer; shared: None or ((quant, gate),
+        (quant, up), (quant, down), (quant, router) or None)."""
+        gq, gate, up, dq, down = experts
+        x = np.ascontiguousarray(x, np.float32)
+        ntok, hidden = x.shape
+        norm_w = np.ascontiguousarray(norm_w, np.float32)
+        keep = []
+
+        def mat(qm):
+            if qm is None:
+                return None
+            arr = _u8(qm[1])
+            keep.append(arr)
+            return C.byref(_Matrix(qm[0], arr.ctypes.data))
+
+        pg, _a = self._pack(gq, gate)
+        pu, _b = self._pack(gq, up)
+        pd, _c = self._pack(dq, down)
+        sg, su, sd, sr = shared if shared is not None else (None, None, None, None)
+        shared_inter = np.asarray(sg[1]).shape[0] if sg is not None else 0
+        out = np.empty_like(x)
+        rc = self.lib.qo_moe_block(x, norm_w, mat(router), C.byref(pg), C.byref(pu), C.byref(pd), mat(sg),
+                                   mat(su), mat(sd), mat(sr), out, ntok, hidden, gate.shape[1], shared_inter,
+                                   gate.shape[0], top_k)
+        if rc:
+            raise ValueError("moe_block failed")
+        return out
+
     def moe_layer(self, gq, gate, up, dq, down, logits, x, top_k=8, f64=False):
         """Routed MoE FFN (qw6.c:2246-2264) for every token row of x."""
         logits = np.ascontiguousarray(logits, np.float32)
@@ -178,6 +228,9 @@ class Reference:
         lib.ref_argmax.argtypes = [_f32p, C.c_int]
         lib.ref_silu.argtypes = [C.c_float]
         lib.ref_silu.restype = C.c_float
+        lib.ref_sigmoid.argtypes = [C.c_float]
+        lib.ref_sigmoid.restype = C.c_float
+        lib.ref_rmsnorm.argtypes = [_f32p, _f32p, _f32p, C.c_int]
         self.lib = lib
 
     def dequantize(self, quant, w, rows, cols):
@@ -217,6 +270,44 @@ class Reference:
 
     def silu(self, v: float) -> float:
         return self.lib.ref_silu(v)
+
+    def sigmoid(self, v: float) -> float:
+        return self.lib.ref_sigmoid(v)
+
+    def rmsnorm(self, x, w):
+        x = np.ascontiguousarray(x, np.float32)
+        w = np.ascontiguousarray(w, np.float32)
+        out = np.empty_like(x)
+        if self.lib.ref_rmsnorm(x, w, out, x.size):
+            raise ValueError("ref rmsnorm failed")
+        return out
+
+    def moe_block(self, x, norm_w, router, experts, shared=None, top_k=8):
+        """qw6.c:2474-2484 around qw6_apply_layer_moe (qw6.c:2226-2290),
+        composed from qw6's own functions in its order (same arguments as
+        Oracle.moe_block)."""
+        gq, gate, up, dq, down = experts
+        x = np.ascontiguousarray(x, np.float32)
+        ntok, hidden = x.shape
+        ne = gate.shape[0]
+        out = np.empty_like(x)
+        for t in range(ntok):
+            normed = self.rmsnorm(x[t], norm_w)
+            logits = self.matvec(router[0], router[1], normed, ne, hidden)
+            ffn = self.moe_layer(gq, gate, up, dq, down, logits[None, :], normed[None, :], top_k)[0][0]
+            if shared is not None:
+                (sgq, sgw), (suq, suw), (sdq, sdw), sr = shared
+                s = np.float32(1.0)
+                if sr is not None:
+                    s = np.float32(self.sigmoid(float(np.atleast_1d(self.matvec(sr[0], sr[1], normed, 1, hidden))[0])))
+                si = np.asarray(sgw).shape[0]
+                g = self.matvec(sgq, sgw, normed, si, hidden)
+                u = self.matvec(suq, suw, normed, si, hidden)
+                mid = np.array([self.silu(float(v)) for v in g], np.float32) * u
+                d = self.matvec(sdq, sdw, mid.astype(np.float32), hidden, si)
+                ffn = (ffn + s * d).astype(np.float32)
+            out[t] = (x[t] + ffn).astype(np.float32)
+        return out
 
     def moe_layer(self, gq, gate, up, dq, down, logits, x, top_k=8):
         """qw6.c:2246-2264 composed from qw6's own public functions."""

@@ -377,3 +377,60 @@ int qo_moe_layer_f64(const qo_expert_pack *gate, const qo_expert_pack *up,
     free(g); free(u); free(tmp); free(row); free(mid);
     return rc;
 }
+
+/* qw6.c:2502-2512 */
+void qo_rmsnorm(const float *x, const float *weight, float *out, uint32_t dim) {
+    float ss = 0.0f;
+    for (uint32_t i = 0; i < dim; i++) ss += x[i] * x[i];
+    ss = 1.0f / sqrtf(ss / (float)dim + 1e-6f);
+    for (uint32_t i = 0; i < dim; i++) out[i] = x[i] * ss * weight[i];
+}
+
+/* qw6_sigmoid, qw6.h:295-297 */
+static float sigmoid(float v) { return 1.0f / (1.0f + expf(-v)); }
+
+/* qw6.c:2474-2484 around qw6.c:2226-2290 */
+int qo_moe_block(const float *x, const float *norm_w, const qo_matrix *router,
+                 const qo_expert_pack *gate, const qo_expert_pack *up,
+                 const qo_expert_pack *down, const qo_matrix *sgate,
+                 const qo_matrix *sup, const qo_matrix *sdown,
+                 const qo_matrix *srouter, float *out, uint32_t ntok,
+                 uint32_t hidden, uint32_t inter, uint32_t shared_inter,
+                 uint32_t n_experts, uint32_t top_k) {
+    if (!x || !norm_w || !router || !gate || !up || !down || !out || !hidden || !n_experts ||
+        n_experts > 256 || !top_k || top_k > n_experts)
+        return -1;
+    const int shared = sgate && sup && sdown;
+    if ((sgate || sup || sdown) && !shared) return -1;
+    if (shared && !shared_inter) return -1;
+    const uint32_t si = shared ? shared_inter : 1;
+    float *normed = malloc(hidden * sizeof(float)), *ffn = malloc(hidden * sizeof(float));
+    float *tmp = malloc(hidden * sizeof(float)), *logits = malloc(n_experts * sizeof(float));
+    float *sg = malloc(si * sizeof(float)), *su = malloc(si * sizeof(float)), *smid = malloc(si * sizeof(float));
+    int rc = (normed && ffn && tmp && logits && sg && su && smid) ? 0 : -1;
+    for (uint32_t t = 0; t < ntok && rc == 0; t++) {
+        const float *xt = x + (size_t)t * hidden;
+        qo_rmsnorm(xt, norm_w, normed, hidden);
+        rc = qo_matvec(router->quant, router->w, normed, logits, n_experts, hidden);
+        if (!rc) rc = qo_moe_layer(gate, up, down, logits, normed, ffn, 1, hidden, inter, n_experts, top_k, NULL, NULL);
+        if (!rc && shared) {
+            float s = 1.0f;
+            if (srouter) {
+                rc = qo_matvec(srouter->quant, srouter->w, normed, &s, 1, hidden);
+                s = sigmoid(s);
+            }
+            if (!rc) rc = qo_matvec(sgate->quant, sgate->w, normed, sg, shared_inter, hidden);
+            if (!rc) rc = qo_matvec(sup->quant, sup->w, normed, su, shared_inter, hidden);
+            if (!rc) {
+                for (uint32_t i = 0; i < shared_inter; i++) smid[i] = silu(sg[i]) * su[i];
+                rc = qo_matvec(sdown->quant, sdown->w, smid, tmp, hidden, shared_inter);
+            }
+            if (!rc)
+                for (uint32_t i = 0; i < hidden; i++) ffn[i] += s * tmp[i];
+        }
+        if (!rc)
+            for (uint32_t i = 0; i < hidden; i++) out[(size_t)t * hidden + i] = xt[i] + ffn[i];
+    }
+    free(normed); free(ffn); free(tmp); free(logits); free(sg); free(su); free(smid);
+    return rc;
+}

@@ -92,6 +92,37 @@ int qo_moe_layer_f64(const qo_expert_pack *gate, const qo_expert_pack *up,
                      uint32_t hidden, uint32_t inter, uint32_t n_experts,
                      uint32_t top_k);
 
+/* qw6_cpu_rmsnorm, qw6.c:2502-2512: ss = sum x[i]^2 (one fp32
+ * accumulator), scale = 1 / sqrtf(ss / dim + 1e-6f) (QW6_RMS_EPS,
+ * qw6.h:67), out[i] = x[i] * scale * weight[i] evaluated left to right. */
+void qo_rmsnorm(const float *x, const float *weight, float *out, uint32_t dim);
+
+/* One dense matrix of a block (FP32/FP16/BF16 or a GGUF block format),
+ * rows x cols as its use implies. */
+typedef struct {
+    uint32_t quant;
+    const void *w;
+} qo_matrix;
+
+/* The MoE FFN block as qw6's forward pass runs it around
+ * qw6_apply_layer_moe (qw6.c:2474-2484, 2226-2290), per token t:
+ *   normed = rmsnorm(x[t], norm_w)
+ *   logits = router . normed                (router: [n_experts x hidden])
+ *   ffn    = routed experts on normed       (as qo_moe_layer)
+ *   with a shared expert (sgate, sup: [shared_inter x hidden], sdown:
+ *   [hidden x shared_inter]): s = sigmoid(srouter . normed), or 1 without
+ *   srouter ([1 x hidden]); ffn[i] += s * (sdown . (silu(sgate . normed) *
+ *   (sup . normed)))[i]
+ *   out[t][i] = x[t][i] + ffn[i]            (the residual add)
+ * sgate/sup/sdown: all or none (NULL). */
+int qo_moe_block(const float *x, const float *norm_w, const qo_matrix *router,
+                 const qo_expert_pack *gate, const qo_expert_pack *up,
+                 const qo_expert_pack *down, const qo_matrix *sgate,
+                 const qo_matrix *sup, const qo_matrix *sdown,
+                 const qo_matrix *srouter, float *out, uint32_t ntok,
+                 uint32_t hidden, uint32_t inter, uint32_t shared_inter,
+                 uint32_t n_experts, uint32_t top_k);
+
 #ifdef __cplusplus
 }
 #endif

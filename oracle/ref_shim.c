@@ -5,7 +5,9 @@
  * oracle/_ref/libqw6ref.so by oracle/Makefile, so that tests and the
  * CPU-baseline leg of bench.py can call qw6's real implementation:
  *   qw6_tensor_dequantize_row (qw6.c:1674), qw6_tensor_matvec (qw6.c:1769),
- *   qw6_cpu_moe_route (qw6.c:2796), qw6_cpu_argmax (qw6.c:2858).
+ *   qw6_cpu_moe_route (qw6.c:2796), qw6_cpu_argmax (qw6.c:2858),
+ *   qw6_cpu_rmsnorm (qw6.c:2502), and the qw6_silu / qw6_sigmoid inlines
+ *   (qw6.h:292-297).
  * The shim only wraps raw block bytes in a qw6_tensor_t and validates
  * arguments first, because the reference asserts (exit(1)) on bad input.
  */
@@ -69,3 +71,11 @@ int ref_argmax(const float *x, int n) {
 }
 
 float ref_silu(float v) { return qw6_silu(v); }
+
+float ref_sigmoid(float v) { return qw6_sigmoid(v); }
+
+int ref_rmsnorm(const float *x, const float *w, float *out, int dim) {
+    if (!x || !w || !out || dim <= 0) return -1;
+    qw6_cpu_rmsnorm(out, x, w, dim);
+    return 0;
+}

@@ -168,3 +168,49 @@ def test_kat_route_sin_cos(oracle, reference):
     i2, w2 = reference.moe_route(lg, 8)
     assert i1[0] == 7 and i1[1] == 149
     assert np.array_equal(i1, i2) and np.max(np.abs(w1 - w2)) <= 2e-5
+
+
+def _block_data(rng, E=16, H=512, I=256, SI=256, ntok=3):
+    gate, up, down = S.moe_weights(rng, E, S.Q4_K, S.Q6_K, H, I)
+    router = (S.FP32, (rng.standard_normal((E, H), dtype=np.float32) * np.float32(0.05)).astype(np.float32))
+    shared = ((S.Q4_K, S.make_matrix(S.Q4_K, SI, H, rng)), (S.Q4_K, S.make_matrix(S.Q4_K, SI, H, rng)),
+              (S.Q6_K, S.make_matrix(S.Q6_K, H, SI, rng)),
+              (S.FP32, (rng.standard_normal((1, H), dtype=np.float32) * np.float32(0.05)).astype(np.float32)))
+    norm_w = (1.0 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+    x = rng.standard_normal((ntok, H), dtype=np.float32)
+    return x, norm_w, router, (S.Q4_K, gate, up, S.Q6_K, down), shared
+
+
+@pytest.mark.parametrize("variant", ["shared_gated", "shared_ungated", "routed_only"])
+def test_moe_block_matches_reference_bitexact(variant, oracle, reference, rng):
+    """The full MoE FFN block (rmsnorm, router matvec, routed experts,
+    shared expert with its sigmoid gate, residual add) restated in C equals
+    qw6's own functions composed in qw6's order, bit for bit."""
+    x, norm_w, router, experts, shared = _block_data(rng)
+    if variant == "shared_ungated":
+        shared = shared[:3] + (None,)
+    elif variant == "routed_only":
+        shared = None
+    got = oracle.moe_block(x, norm_w, router, experts, shared, top_k=4)
+    want = reference.moe_block(x, norm_w, router, experts, shared, top_k=4)
+    assert same_bits(got, want)
+    assert np.all(np.isfinite(got))
+
+
+def test_rmsnorm_matches_reference_bitexact(oracle, reference, rng):
+    for dim in (1, 7, 512, 2048):
+        x = (rng.standard_normal(dim) * 10.0 ** rng.uniform(-3, 3)).astype(np.float32)
+        w = rng.standard_normal(dim).astype(np.float32)
+        assert same_bits(oracle.rmsnorm(x, w), reference.rmsnorm(x, w))
+
+
+def test_moe_block_shared_expert_contributes(oracle, rng):
+    x, norm_w, router, experts, shared = _block_data(rng, ntok=2)
+    routed = oracle.moe_block(x, norm_w, router, experts, None, top_k=4)
+    gated = oracle.moe_block(x, norm_w, router, experts, shared, top_k=4)
+    ungated = oracle.moe_block(x, norm_w, router, experts, shared[:3] + (None,), top_k=4)
+    assert not np.array_equal(routed, gated) and not np.array_equal(gated, ungated)
+    # the residual: with zero routed and shared weights the block returns x unchanged
+    zero = tuple(np.zeros_like(m) for m in experts[1:3]) + (np.zeros_like(experts[4]),)
+    z = oracle.moe_block(x, norm_w, router, (experts[0], zero[0], zero[1], experts[3], zero[2]), None, top_k=4)
+    assert same_bits(z, x)
