@@ -14,6 +14,11 @@ and the CUDA library on machines without the reference tree:
   moe_small.npz     qw6_apply_layer_moe composition (qw6.c:2246-2264) for a
                     4-expert layer whose weights are regenerated from the seed
                     (their sha256 is stored to detect generator drift)
+  moe_block.npz     the full MoE FFN block (qw6.c:2474-2484 around
+                    qw6.c:2226-2290: RMSNorm, fp32 router, routed experts,
+                    shared expert with its sigmoid gate, residual add), weights
+                    regenerated from the seed by block_inputs() and checked by
+                    sha256
 
 Usage: python tests/golden/gen_golden.py
 """
@@ -108,6 +113,36 @@ def moe_case(ref):
                 logits=logits, x=x, out=out, idx=idx, w=w)
 
 
+def block_inputs(seed):
+    """Inputs of the moe_block fixture, all drawn from one seeded generator:
+    x [T x H], norm_w [H], the fp32 router [E x H], the routed experts
+    (Q4_K gate/up [I x H], Q6_K down [H x I]) and the shared expert (Q4_K
+    gate/up [SI x H], Q6_K down [H x SI], fp32 router [1 x H])."""
+    E, H, I, SI, K, T = 4, 512, 256, 256, 2, 3
+    rng = np.random.Generator(np.random.PCG64(seed))
+    gate, up, down = S.moe_weights(rng, E, S.Q4_K, S.Q6_K, H, I)
+    router = (rng.standard_normal((E, H), dtype=np.float32) * np.float32(0.05)).astype(np.float32)
+    sg, su = S.make_matrix(S.Q4_K, SI, H, rng), S.make_matrix(S.Q4_K, SI, H, rng)
+    sd = S.make_matrix(S.Q6_K, H, SI, rng)
+    sr = (rng.standard_normal((1, H), dtype=np.float32) * np.float32(0.05)).astype(np.float32)
+    norm_w = (1.0 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+    x = rng.standard_normal((T, H), dtype=np.float32)
+    experts = (S.Q4_K, gate, up, S.Q6_K, down)
+    shared = ((S.Q4_K, sg), (S.Q4_K, su), (S.Q6_K, sd), (S.FP32, sr))
+    sha = hashlib.sha256(b"".join(a.tobytes() for a in (gate, up, down, router, sg, su, sd, sr, norm_w, x)))
+    return dict(dims=(E, H, I, SI, K, T), x=x, norm_w=norm_w, router=(S.FP32, router), experts=experts,
+                shared=shared, sha=sha.hexdigest())
+
+
+def block_case(ref):
+    seed = 22
+    b = block_inputs(seed)
+    K = b["dims"][4]
+    out = ref.moe_block(b["x"], b["norm_w"], b["router"], b["experts"], b["shared"], top_k=K)
+    routed = ref.moe_block(b["x"], b["norm_w"], b["router"], b["experts"], None, top_k=K)
+    return dict(seed=np.int32(seed), sha=np.array(b["sha"]), out=out, out_routed=routed)
+
+
 def main():
     ref = Reference()
     for i, q in enumerate(S.BLOCK_QUANTS):
@@ -115,6 +150,7 @@ def main():
     np.savez_compressed(HERE / "route.npz", **route_case(ref))
     np.savez_compressed(HERE / "argmax.npz", **argmax_case(ref))
     np.savez_compressed(HERE / "moe_small.npz", **moe_case(ref))
+    np.savez_compressed(HERE / "moe_block.npz", **block_case(ref))
     print("golden fixtures written to", HERE)
 
 

@@ -50,3 +50,17 @@ def test_golden_moe(oracle):
     out, idx, w = oracle.moe_layer(S.Q4_K, gate, up, S.Q6_K, down, g["logits"], g["x"], top_k=K)
     assert np.array_equal(idx, g["idx"]) and same_bits(w, g["w"])
     assert same_bits(out, g["out"])
+
+
+def test_golden_moe_block(oracle):
+    """The full MoE FFN block against qw6's own composition (with and
+    without the shared expert); inputs regenerated from the fixture's seed."""
+    from tests.golden.gen_golden import block_inputs
+    g = np.load(GOLDEN / "moe_block.npz")
+    b = block_inputs(int(g["seed"]))
+    assert b["sha"] == str(g["sha"]), "synthetic generator drifted from the fixture"
+    K = b["dims"][4]
+    out = oracle.moe_block(b["x"], b["norm_w"], b["router"], b["experts"], b["shared"], top_k=K)
+    assert same_bits(out, g["out"])
+    routed = oracle.moe_block(b["x"], b["norm_w"], b["router"], b["experts"], None, top_k=K)
+    assert same_bits(routed, g["out_routed"])
