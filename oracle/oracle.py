@@ -78,6 +78,8 @@ class Oracle:
         mp = C.POINTER(_Matrix)
         lib.qo_moe_block.argtypes = [_f32p, _f32p, mp, pk, pk, pk, mp, mp, mp, mp, _f32p, C.c_uint32, C.c_uint32,
                                      C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32]
+        lib.qo_moe_block_f64.argtypes = [_f32p, _f32p, mp, pk, pk, pk, mp, mp, mp, mp, _f64p, C.c_uint32,
+                                         C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32]
         self.lib = lib
 
     def fp16_to_f32(self, h: int) -> float:
@@ -149,13 +151,14 @@ class Oracle:
         self.lib.qo_rmsnorm(x, w, out, x.size)
         return out
 
-    def moe_block(self, x, norm_w, router, experts, shared=None, top_k=8):
+    def moe_block(self, x, norm_w, router, experts, shared=None, top_k=8, f64=False):
         """The MoE FFN block around qw6_apply_layer_moe (qw6.c:2474-2484,
         2226-2290) for every token row of x: rmsnorm, router matvec, routed
         experts, the optional shared expert with its sigmoid gate, residual
         add.  router: (quant, matrix [n_experts rows]); experts: (gq, gate,
         up, dq, down) as for moe_layer; shared: None or ((quant, gate),
-        (quant, up), (quant, down), (quant, router) or None)."""
+        (quant, up), (quant, down), (quant, router) or None).  f64: the
+        double-precision error reference (same routing)."""
         gq, gate, up, dq, down = experts
         x = np.ascontiguousarray(x, np.float32)
         ntok, hidden = x.shape
@@ -174,10 +177,10 @@ class Oracle:
         pd, _c = self._pack(dq, down)
         sg, su, sd, sr = shared if shared is not None else (None, None, None, None)
         shared_inter = np.asarray(sg[1]).shape[0] if sg is not None else 0
-        out = np.empty_like(x)
-        rc = self.lib.qo_moe_block(x, norm_w, mat(router), C.byref(pg), C.byref(pu), C.byref(pd), mat(sg),
-                                   mat(su), mat(sd), mat(sr), out, ntok, hidden, gate.shape[1], shared_inter,
-                                   gate.shape[0], top_k)
+        out = np.empty(x.shape, np.float64 if f64 else np.float32)
+        fn = self.lib.qo_moe_block_f64 if f64 else self.lib.qo_moe_block
+        rc = fn(x, norm_w, mat(router), C.byref(pg), C.byref(pu), C.byref(pd), mat(sg), mat(su), mat(sd), mat(sr),
+                out, ntok, hidden, gate.shape[1], shared_inter, gate.shape[0], top_k)
         if rc:
             raise ValueError("moe_block failed")
         return out

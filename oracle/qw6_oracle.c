@@ -434,3 +434,75 @@ int qo_moe_block(const float *x, const float *norm_w, const qo_matrix *router,
     free(normed); free(ffn); free(tmp); free(logits); free(sg); free(su); free(smid);
     return rc;
 }
+
+/* y[r] = sum_c W[r][c] * x[c] in double over the dequantized rows of W
+ * ([rows x cols]); row is scratch of cols floats */
+static int matvec_d(uint32_t quant, const void *w, const double *x, double *y, uint32_t rows, uint32_t cols,
+                    float *row) {
+    for (uint32_t r = 0; r < rows; r++) {
+        if (qo_dequantize_row(quant, w, cols, r, row)) return -1;
+        double a = 0.0;
+        for (uint32_t c = 0; c < cols; c++) a += (double)row[c] * x[c];
+        y[r] = a;
+    }
+    return 0;
+}
+
+int qo_moe_block_f64(const float *x, const float *norm_w, const qo_matrix *router,
+                     const qo_expert_pack *gate, const qo_expert_pack *up,
+                     const qo_expert_pack *down, const qo_matrix *sgate,
+                     const qo_matrix *sup, const qo_matrix *sdown,
+                     const qo_matrix *srouter, double *out, uint32_t ntok,
+                     uint32_t hidden, uint32_t inter, uint32_t shared_inter,
+                     uint32_t n_experts, uint32_t top_k) {
+    if (!x || !norm_w || !router || !gate || !up || !down || !out || !hidden || !n_experts ||
+        n_experts > 256 || !top_k || top_k > n_experts)
+        return -1;
+    const int shared = sgate && sup && sdown;
+    if ((sgate || sup || sdown) && !shared) return -1;
+    if (shared && !shared_inter) return -1;
+    const uint32_t mi = inter > shared_inter ? inter : shared_inter, wide = hidden > mi ? hidden : mi;
+    float *n32 = malloc(hidden * sizeof(float)), *logits = malloc(n_experts * sizeof(float));
+    float *row = malloc(wide * sizeof(float));
+    double *nd = malloc(hidden * sizeof(double)), *ffn = malloc(hidden * sizeof(double));
+    double *tmp = malloc(hidden * sizeof(double)), *g = malloc(mi * sizeof(double));
+    double *u = malloc(mi * sizeof(double)), *mid = malloc(mi * sizeof(double));
+    int rc = (n32 && logits && row && nd && ffn && tmp && g && u && mid) ? 0 : -1;
+    int32_t idx[256];
+    float w[256];
+    for (uint32_t t = 0; t < ntok && rc == 0; t++) {
+        const float *xt = x + (size_t)t * hidden;
+        /* routing exactly as the fp32 block */
+        qo_rmsnorm(xt, norm_w, n32, hidden);
+        rc = qo_matvec(router->quant, router->w, n32, logits, n_experts, hidden);
+        if (!rc) rc = qo_moe_route(logits, n_experts, top_k, idx, w);
+        /* the arithmetic in double */
+        double ss = 0.0;
+        for (uint32_t i = 0; i < hidden; i++) ss += (double)xt[i] * xt[i];
+        const double scale = 1.0 / sqrt(ss / hidden + 1e-6);
+        for (uint32_t i = 0; i < hidden; i++) nd[i] = (double)xt[i] * scale * norm_w[i];
+        for (uint32_t i = 0; i < hidden; i++) ffn[i] = 0.0;
+        for (uint32_t k = 0; k < top_k && rc == 0; k++) {
+            rc = matvec_d(gate->quant, expert_ptr(gate, idx[k]), nd, g, inter, hidden, row);
+            if (!rc) rc = matvec_d(up->quant, expert_ptr(up, idx[k]), nd, u, inter, hidden, row);
+            for (uint32_t i = 0; i < inter && !rc; i++) mid[i] = g[i] / (1.0 + exp(-g[i])) * u[i];
+            if (!rc) rc = matvec_d(down->quant, expert_ptr(down, idx[k]), mid, tmp, hidden, inter, row);
+            for (uint32_t i = 0; i < hidden && !rc; i++) ffn[i] += (double)w[k] * tmp[i];
+        }
+        if (!rc && shared) {
+            double s = 1.0;
+            if (srouter) {
+                rc = matvec_d(srouter->quant, srouter->w, nd, &s, 1, hidden, row);
+                s = 1.0 / (1.0 + exp(-s));
+            }
+            if (!rc) rc = matvec_d(sgate->quant, sgate->w, nd, g, shared_inter, hidden, row);
+            if (!rc) rc = matvec_d(sup->quant, sup->w, nd, u, shared_inter, hidden, row);
+            for (uint32_t i = 0; i < shared_inter && !rc; i++) mid[i] = g[i] / (1.0 + exp(-g[i])) * u[i];
+            if (!rc) rc = matvec_d(sdown->quant, sdown->w, mid, tmp, hidden, shared_inter, row);
+            for (uint32_t i = 0; i < hidden && !rc; i++) ffn[i] += s * tmp[i];
+        }
+        for (uint32_t i = 0; i < hidden && !rc; i++) out[(size_t)t * hidden + i] = (double)xt[i] + ffn[i];
+    }
+    free(n32); free(logits); free(row); free(nd); free(ffn); free(tmp); free(g); free(u); free(mid);
+    return rc;
+}

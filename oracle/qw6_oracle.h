@@ -123,6 +123,19 @@ int qo_moe_block(const float *x, const float *norm_w, const qo_matrix *router,
                  uint32_t hidden, uint32_t inter, uint32_t shared_inter,
                  uint32_t n_experts, uint32_t top_k);
 
+/* The same block in double precision on the bit-exact weights (error
+ * reference): RMSNorm, the expert and shared-expert contractions, the
+ * sigmoid gate and the residual in double; the experts and their weights
+ * are chosen by the fp32 rule on the fp32 router logits (qo_rmsnorm +
+ * qo_matvec), so both forms route identically. */
+int qo_moe_block_f64(const float *x, const float *norm_w, const qo_matrix *router,
+                     const qo_expert_pack *gate, const qo_expert_pack *up,
+                     const qo_expert_pack *down, const qo_matrix *sgate,
+                     const qo_matrix *sup, const qo_matrix *sdown,
+                     const qo_matrix *srouter, double *out, uint32_t ntok,
+                     uint32_t hidden, uint32_t inter, uint32_t shared_inter,
+                     uint32_t n_experts, uint32_t top_k);
+
 #ifdef __cplusplus
 }
 #endif

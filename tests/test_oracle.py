@@ -214,3 +214,16 @@ def test_moe_block_shared_expert_contributes(oracle, rng):
     zero = tuple(np.zeros_like(m) for m in experts[1:3]) + (np.zeros_like(experts[4]),)
     z = oracle.moe_block(x, norm_w, router, (experts[0], zero[0], zero[1], experts[3], zero[2]), None, top_k=4)
     assert same_bits(z, x)
+
+
+@pytest.mark.parametrize("shared_on", [True, False])
+def test_moe_block_f64_error_reference(shared_on, oracle, rng):
+    """The double-precision block routes like the fp32 one and differs from
+    it only by fp32 accumulation noise."""
+    x, norm_w, router, experts, shared = _block_data(rng)
+    sh = shared if shared_on else None
+    out32 = oracle.moe_block(x, norm_w, router, experts, sh, top_k=4)
+    out64 = oracle.moe_block(x, norm_w, router, experts, sh, top_k=4, f64=True)
+    assert out64.dtype == np.float64
+    err = float(np.max(np.abs(out32 - out64)) / np.max(np.abs(out64)))
+    assert 0 < err <= 1e-5, err
