@@ -7,12 +7,15 @@ Headline workload: one prefill MoE FFN layer
 over 4096 bf16 tokens -- hidden 2048, 256 experts, top-8, expert
 intermediate 512, Q4_K gate/up, Q6_K down, router logits fp32 ~ N(0,1) plus
 a per-expert bias ~ N(0,0.5).  At N GPUs the experts are sharded 256/N per
-GPU and the tokens 4096/N per GPU (strong scaling: the job is always the
-same 4096 tokens); a step is route -> NCCL all-to-all dispatch of token
-rows -> tcgen05 grouped GEMMs on each owner -> all-to-all of the expert
-outputs back -> slot-order combine (qw6_b200.ep.ep_moe_prefill).  N resident
-copies of each GPU's expert shard (~522 MB per GPU, > 4x L2) are used round
-robin, one per step.
+GPU (placed by qw6_b200.ep.balance_experts on the routing counts of an
+independent calibration batch) and the tokens 4096/N per GPU (strong
+scaling: the job is always the same 4096 tokens); a step is route -> count
+-> count exchange and plan -> dispatch of token rows into the owners'
+memory over NVLink -> tcgen05 grouped GEMMs on each owner, whose down GEMM
+writes each output row back into its source's memory -> slot-order combine
+(qw6_b200.ep.PeerMoE, this library's own kernels, no host round trip).  N
+resident copies of each GPU's expert shard (~522 MB per GPU, > 4x L2) are
+used round robin, one per step.
 
 Printed JSON line (rank 0): metric "MoE-layer tokens/s" (whole job), the
 dominant kernel's tensor-core roofline, an end-to-end number with the
@@ -33,7 +36,6 @@ import os
 import subprocess
 import sys
 import tempfile
-import threading
 import time
 from pathlib import Path
 

@@ -1,7 +1,6 @@
 """GPU parity of the routed MoE FFN (qw6cu_moe_decode) against the oracle's
 composition of qw6_apply_layer_moe (qw6.c:2246-2264) and the golden fixture.
 Routing indices must match exactly; outputs within 1e-3 max relative error."""
-from pathlib import Path
 
 import numpy as np
 import pytest
