@@ -75,6 +75,8 @@ class Oracle:
                                          C.c_uint32, C.c_uint32, C.c_uint32]
         lib.qo_rmsnorm.argtypes = [_f32p, _f32p, _f32p, C.c_uint32]
         lib.qo_rmsnorm.restype = None
+        lib.qo_sample.argtypes = [_f32p, C.c_uint32, C.c_float, C.c_float, C.c_int, C.c_float]
+        lib.qo_sample.restype = C.c_int32
         mp = C.POINTER(_Matrix)
         lib.qo_moe_block.argtypes = [_f32p, _f32p, mp, pk, pk, pk, mp, mp, mp, mp, _f32p, C.c_uint32, C.c_uint32,
                                      C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32]
@@ -142,6 +144,11 @@ class Oracle:
     def _pack(quant, arr):
         arr = _u8(arr)
         return _ExpertPack(quant, arr.ctypes.data, arr[0].nbytes), arr
+
+    def sample(self, logits, temp, top_p, top_k, u):
+        """qw6_sample (qw6.c:2921-2982) with its uniform draw u given."""
+        logits = np.ascontiguousarray(logits, np.float32)
+        return int(self.lib.qo_sample(logits, logits.size, temp, top_p, top_k, u))
 
     def rmsnorm(self, x, w):
         """qw6_cpu_rmsnorm (qw6.c:2502-2512)."""
@@ -234,7 +241,11 @@ class Reference:
         lib.ref_sigmoid.argtypes = [C.c_float]
         lib.ref_sigmoid.restype = C.c_float
         lib.ref_rmsnorm.argtypes = [_f32p, _f32p, _f32p, C.c_int]
+        lib.ref_sample.argtypes = [_f32p, C.c_float, C.c_float, C.c_int, C.c_uint]
+        lib.ref_rand_unit.argtypes = [C.c_uint]
+        lib.ref_rand_unit.restype = C.c_float
         self.lib = lib
+        self.vocab = int(lib.ref_vocab_size())
 
     def dequantize(self, quant, w, rows, cols):
         w = _u8(w)
@@ -276,6 +287,17 @@ class Reference:
 
     def sigmoid(self, v: float) -> float:
         return self.lib.ref_sigmoid(v)
+
+    def sample(self, logits, temp, top_p, top_k, seed):
+        """qw6_sample over qw6's full vocabulary row, libc rand() seeded with seed."""
+        logits = np.ascontiguousarray(logits, np.float32)
+        if logits.size != self.vocab:
+            raise ValueError(f"qw6_sample reads {self.vocab} logits")
+        return int(self.lib.ref_sample(logits, temp, top_p, top_k, seed))
+
+    def rand_unit(self, seed) -> float:
+        """The uniform draw qw6_sample makes after srand(seed)."""
+        return float(self.lib.ref_rand_unit(seed))
 
     def rmsnorm(self, x, w):
         x = np.ascontiguousarray(x, np.float32)

@@ -506,3 +506,68 @@ int qo_moe_block_f64(const float *x, const float *norm_w, const qo_matrix *route
     free(n32); free(logits); free(row); free(nd); free(ffn); free(tmp); free(g); free(u); free(mid);
     return rc;
 }
+
+typedef struct {
+    int idx;
+    float score;
+} qo_sample_item;
+
+/* qw6.c:2909-2915: descending score, then ascending index */
+static int sample_item_cmp(const void *a, const void *b) {
+    const qo_sample_item *ia = (const qo_sample_item *)a, *ib = (const qo_sample_item *)b;
+    if (ia->score < ib->score) return 1;
+    if (ia->score > ib->score) return -1;
+    return ia->idx - ib->idx;
+}
+
+/* qw6.c:2921-2982 */
+int32_t qo_sample(const float *logits, uint32_t n, float temp, float top_p, int top_k, float u) {
+    if (!logits || !n) return -1;
+    if (temp <= 0.0f) return qo_argmax(logits, n);
+    if (top_k < 0) top_k = 0;
+    if (top_p <= 0.0f || top_p > 1.0f) top_p = 1.0f;
+    qo_sample_item *items = malloc((size_t)n * sizeof(*items));
+    if (!items) return -1;
+    float max_score = -INFINITY;
+    for (uint32_t i = 0; i < n; i++) {
+        const float score = logits[i] / temp;
+        items[i].idx = (int)i;
+        items[i].score = score;
+        if (score > max_score) max_score = score;
+    }
+    qsort(items, n, sizeof(*items), sample_item_cmp);
+    int limit = (int)n;
+    if (top_k > 0 && top_k < limit) limit = top_k;
+    double sum = 0.0;
+    for (int i = 0; i < limit; i++) sum += exp((double)items[i].score - (double)max_score);
+    if (sum <= 0.0) {
+        const int32_t tok = items[0].idx;
+        free(items);
+        return tok;
+    }
+    int nucleus = limit;
+    if (top_p < 1.0f) {
+        double cum = 0.0;
+        nucleus = 0;
+        for (int i = 0; i < limit; i++) {
+            cum += exp((double)items[i].score - (double)max_score) / sum;
+            nucleus = i + 1;
+            if (cum >= (double)top_p) break;
+        }
+        if (nucleus < 1) nucleus = 1;
+    }
+    double keep_sum = 0.0;
+    for (int i = 0; i < nucleus; i++) keep_sum += exp((double)items[i].score - (double)max_score);
+    const double target = u * keep_sum;
+    double acc = 0.0;
+    int32_t tok = items[nucleus - 1].idx;
+    for (int i = 0; i < nucleus; i++) {
+        acc += exp((double)items[i].score - (double)max_score);
+        if (target <= acc) {
+            tok = items[i].idx;
+            break;
+        }
+    }
+    free(items);
+    return tok;
+}

@@ -136,6 +136,15 @@ int qo_moe_block_f64(const float *x, const float *norm_w, const qo_matrix *route
                      uint32_t hidden, uint32_t inter, uint32_t shared_inter,
                      uint32_t n_experts, uint32_t top_k);
 
+/* qw6_sample, qw6.c:2904-2982, with its one uniform draw u in [0, 1) given
+ * (qw6 takes it from libc: (float)rand() / ((float)RAND_MAX + 1.0f)):
+ * temp <= 0 -> argmax; else scores logits/temp (fp32) sorted descending
+ * (ties: lower index first), top_k (<= 0: all) limits them, top_p
+ * (outside (0, 1]: 1) takes the shortest prefix whose double-precision
+ * probabilities reach it, and the token is the first whose cumulative
+ * exp(score - max) reaches u * (sum over the kept prefix). */
+int32_t qo_sample(const float *logits, uint32_t n, float temp, float top_p, int top_k, float u);
+
 #ifdef __cplusplus
 }
 #endif

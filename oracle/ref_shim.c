@@ -6,11 +6,13 @@
  * CPU-baseline leg of bench.py can call qw6's real implementation:
  *   qw6_tensor_dequantize_row (qw6.c:1674), qw6_tensor_matvec (qw6.c:1769),
  *   qw6_cpu_moe_route (qw6.c:2796), qw6_cpu_argmax (qw6.c:2858),
- *   qw6_cpu_rmsnorm (qw6.c:2502), and the qw6_silu / qw6_sigmoid inlines
- *   (qw6.h:292-297).
+ *   qw6_cpu_rmsnorm (qw6.c:2502), qw6_sample (qw6.c:2921, over qw6's full
+ *   QW6_VOCAB_SIZE logits, with libc's rand() seeded first), and the
+ *   qw6_silu / qw6_sigmoid inlines (qw6.h:292-297).
  * The shim only wraps raw block bytes in a qw6_tensor_t and validates
  * arguments first, because the reference asserts (exit(1)) on bad input.
  */
+#include <stdlib.h>
 #include <string.h>
 
 #include "qw6.h"
@@ -78,4 +80,22 @@ int ref_rmsnorm(const float *x, const float *w, float *out, int dim) {
     if (!x || !w || !out || dim <= 0) return -1;
     qw6_cpu_rmsnorm(out, x, w, dim);
     return 0;
+}
+
+int ref_vocab_size(void) { return QW6_VOCAB_SIZE; }
+
+/* logits: QW6_VOCAB_SIZE floats (qw6_sample reads the session's whole row) */
+int ref_sample(const float *logits, float temp, float top_p, int top_k, unsigned seed) {
+    if (!logits) return -1;
+    qw6_session_t s;
+    memset(&s, 0, sizeof(s));
+    s.logits = (float *)logits;
+    srand(seed);
+    return (int)qw6_sample(&s, temp, top_p, top_k);
+}
+
+/* the uniform draw qw6_sample makes after srand(seed) (qw6.c:2917-2919) */
+float ref_rand_unit(unsigned seed) {
+    srand(seed);
+    return (float)rand() / ((float)RAND_MAX + 1.0f);
 }

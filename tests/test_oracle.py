@@ -227,3 +227,28 @@ def test_moe_block_f64_error_reference(shared_on, oracle, rng):
     assert out64.dtype == np.float64
     err = float(np.max(np.abs(out32 - out64)) / np.max(np.abs(out64)))
     assert 0 < err <= 1e-5, err
+
+
+def test_sample_cpu_kat(oracle):
+    """qw6's own sampling self-test (qw6.c:3369-3384)."""
+    v = np.zeros(248320, np.float32)
+    v[:3] = [1.0, 2.0, 3.0]
+    assert oracle.sample(v, 0.0, 1.0, 0, 0.5) == 2
+    assert oracle.sample(v, 1.0, 1.0, 1, 0.99) == 2
+    v[:] = -100.0
+    v[:3] = [10.0, 0.0, 0.0]
+    assert oracle.sample(v, 1.0, 0.5, 0, 0.99) == 0
+
+
+@pytest.mark.parametrize("temp,top_p,top_k", [(0.0, 1.0, 0), (1.0, 1.0, 0), (0.7, 0.9, 40), (1.3, 0.5, 0),
+                                              (1.0, 1.0, 1), (0.8, 1.0, 50), (1.0, 0.95, 0), (2.0, 1.5, -3)])
+def test_sample_matches_reference(temp, top_p, top_k, oracle, reference):
+    """The sampler restated with its uniform draw given equals qw6_sample
+    with libc rand() seeded to produce that draw (the full vocabulary row,
+    with a few tied logits)."""
+    rng = np.random.Generator(np.random.PCG64(int(temp * 10) + top_k + 100))
+    logits = (rng.standard_normal(reference.vocab) * 3.0).astype(np.float32)
+    logits[rng.integers(0, reference.vocab, 8)] = logits.max()
+    for seed in (1, 7, 12345):
+        u = reference.rand_unit(seed)
+        assert oracle.sample(logits, temp, top_p, top_k, u) == reference.sample(logits, temp, top_p, top_k, seed)
