@@ -19,6 +19,9 @@ and the CUDA library on machines without the reference tree:
                     shared expert with its sigmoid gate, residual add), weights
                     regenerated from the seed by block_inputs() and checked by
                     sha256
+  sample.npz        qw6_sample on full-vocabulary logit rows regenerated from a
+                    seed by sample_logits(), for several (temp, top_p, top_k)
+                    and libc rand() seeds, with the uniform draw each made
 
 Usage: python tests/golden/gen_golden.py
 """
@@ -143,6 +146,30 @@ def block_case(ref):
     return dict(seed=np.int32(seed), sha=np.array(b["sha"]), out=out, out_routed=routed)
 
 
+SAMPLE_PARAMS = [(0.0, 1.0, 0), (1.0, 1.0, 0), (0.7, 0.9, 40), (1.3, 0.5, 0), (1.0, 1.0, 1), (0.8, 1.0, 50),
+                 (1.0, 0.95, 0)]
+
+
+def sample_logits(seed, vocab):
+    """One logit row of the sample fixture: N(0, 3) with 8 tied maxima."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    logits = (rng.standard_normal(vocab) * 3.0).astype(np.float32)
+    logits[rng.integers(0, vocab, 8)] = logits.max()
+    return logits
+
+
+def sample_case(ref):
+    rows = []
+    for i, (temp, top_p, top_k) in enumerate(SAMPLE_PARAMS):
+        logits = sample_logits(300 + i, ref.vocab)
+        for rseed in (1, 7, 12345):
+            rows.append((300 + i, temp, top_p, top_k, rseed, ref.rand_unit(rseed),
+                         ref.sample(logits, temp, top_p, top_k, rseed)))
+    a = np.array(rows, dtype=np.float64)
+    sha = hashlib.sha256(sample_logits(300, ref.vocab).tobytes()).hexdigest()
+    return dict(vocab=np.int32(ref.vocab), cases=a, sha=np.array(sha))
+
+
 def main():
     ref = Reference()
     for i, q in enumerate(S.BLOCK_QUANTS):
@@ -151,6 +178,7 @@ def main():
     np.savez_compressed(HERE / "argmax.npz", **argmax_case(ref))
     np.savez_compressed(HERE / "moe_small.npz", **moe_case(ref))
     np.savez_compressed(HERE / "moe_block.npz", **block_case(ref))
+    np.savez_compressed(HERE / "sample.npz", **sample_case(ref))
     print("golden fixtures written to", HERE)
 
 

@@ -64,3 +64,19 @@ def test_golden_moe_block(oracle):
     assert same_bits(out, g["out"])
     routed = oracle.moe_block(b["x"], b["norm_w"], b["router"], b["experts"], None, top_k=K)
     assert same_bits(routed, g["out_routed"])
+
+
+def test_golden_sample(oracle):
+    """qw6_sample's picks (with the uniform draw each made) on logit rows
+    regenerated from the fixture's seeds."""
+    from tests.golden.gen_golden import sample_logits
+    g = np.load(GOLDEN / "sample.npz")
+    vocab = int(g["vocab"])
+    assert hashlib.sha256(sample_logits(300, vocab).tobytes()).hexdigest() == str(g["sha"])
+    rows = {}
+    for seed, temp, top_p, top_k, _rseed, u, tok in g["cases"]:
+        seed = int(seed)
+        if seed not in rows:
+            rows[seed] = sample_logits(seed, vocab)
+        assert oracle.sample(rows[seed], float(temp), float(top_p), int(top_k), float(u)) == int(tok)
+    assert len({int(t) for t in g["cases"][:, 6]}) > 3  # the picks are not all the same token
