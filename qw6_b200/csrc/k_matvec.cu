@@ -8,6 +8,7 @@
 
 #include "qw6_argmax.cuh"
 #include "qw6_dev.cuh"
+#include "qw6_devcfg.cuh"
 #include "qw6_grids.cuh"
 #include "qw6_launch.h"
 
@@ -295,17 +296,7 @@ __global__ void __launch_bounds__(kThreads, NQ == 1 ? 2 : 1) k_matvec(const MvAr
 
 // ---------------------------------------------------------- launchers ----
 
-static int g_num_sms = 0;
-
-static int num_sms() {
-    if (!g_num_sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-        if (g_num_sms <= 0) g_num_sms = 148;
-    }
-    return g_num_sms;
-}
+static int num_sms() { return device_sms(); }
 
 template <int F, int NQ>
 static size_t mv_smem(int cols) {
@@ -317,14 +308,9 @@ static int launch_mv(const uint8_t* w, const float* x, float* y, int rows, int c
                      int ldy, cudaStream_t st, unsigned long long* keys = nullptr, uint32_t row_offset = 0) {
     const size_t smem = mv_smem<F, NQ>(cols);
     if (smem > 200 * 1024) return QW6K_ERR_ARG;
-    static int configured = 0;
-    static int occ = 1;
-    if (!configured) {
-        if (cudaFuncSetAttribute(k_matvec<F, NQ, KEYS>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
-            cudaSuccess)
-            return QW6K_ERR_CUDA;
-        configured = 1;
-    }
+    static DevFlags configured;
+    int occ = 1;
+    if (smem_optin(configured, k_matvec<F, NQ, KEYS>, 200 * 1024)) return QW6K_ERR_CUDA;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_matvec<F, NQ, KEYS>, kThreads, smem) != cudaSuccess ||
         occ < 1)
         return QW6K_ERR_CUDA;

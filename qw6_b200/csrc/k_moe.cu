@@ -19,6 +19,7 @@
 #include <cuda_runtime.h>
 
 #include "qw6_dev.cuh"
+#include "qw6_devcfg.cuh"
 #include "qw6_grids.cuh"
 #include "qw6_launch.h"
 #include "qw6_route.cuh"
@@ -470,11 +471,8 @@ template <int F, int NQ>
 static int launch_gateup(const MoeArgs& a, int max_items, cudaStream_t st) {
     const size_t smem = gu_smem<F, NQ>(a.hidden);
     if (smem > 200 * 1024) return QW6K_ERR_ARG;
-    static bool cfg = false;
-    if (!cfg && cudaFuncSetAttribute(k_moe_gateup<F, NQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
-                    cudaSuccess)
-        return QW6K_ERR_CUDA;
-    cfg = true;
+    static DevFlags cfg;
+    if (smem_optin(cfg, k_moe_gateup<F, NQ>, 200 * 1024)) return QW6K_ERR_CUDA;
     const int mgroups = (a.inter / 16) / (kWarps / a.ks_gu);
     k_moe_gateup<F, NQ><<<max_items * mgroups, kThreads, smem, st>>>(a);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
@@ -484,11 +482,8 @@ template <int F, int NQ>
 static int launch_down(const MoeArgs& a, int max_items, cudaStream_t st) {
     const size_t smem = gu_smem<F, NQ>(a.inter);
     if (smem > 200 * 1024) return QW6K_ERR_ARG;
-    static bool cfg = false;
-    if (!cfg && cudaFuncSetAttribute(k_moe_down<F, NQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
-                    cudaSuccess)
-        return QW6K_ERR_CUDA;
-    cfg = true;
+    static DevFlags cfg;
+    if (smem_optin(cfg, k_moe_down<F, NQ>, 200 * 1024)) return QW6K_ERR_CUDA;
     const int mgroups = (a.hidden / 16) / (kWarps / a.ks_dn);
     k_moe_down<F, NQ><<<max_items * mgroups, kThreads, smem, st>>>(a);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
@@ -538,11 +533,8 @@ static int nbw_of(int nb) { return nb >= 8 ? 2 : 1; }
 template <int F, int NBW>
 static int launch_small_gu(const MoeArgs& a, cudaStream_t st) {
     const size_t smem = tbl_bytes_of<F>() + xstage_bytes(4, a.hidden) + (size_t)kThreads * 4 * 4;
-    static bool cfg = false;
-    if (!cfg && cudaFuncSetAttribute(k_moe_small_gu<F, NBW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     200 * 1024) != cudaSuccess)
-        return QW6K_ERR_CUDA;
-    cfg = true;
+    static DevFlags cfg;
+    if (smem_optin(cfg, k_moe_small_gu<F, NBW>, 200 * 1024)) return QW6K_ERR_CUDA;
     const int ks = a.hidden / 256 / NBW, mgroups = (a.inter / 16) / (kWarps / ks);
     return launch_ex(k_moe_small_gu<F, NBW>, a.ntok * a.topk * mgroups, smem, false, st, a);
 }
@@ -556,11 +548,8 @@ template <int F, int NBW>
 static int launch_small_down(const MoeArgs& a, cudaStream_t st) {
     const size_t smem = small_down_smem<F>(a);
     if (smem > 180 * 1024) return QW6K_ERR_ARG;
-    static bool cfg = false;
-    if (!cfg && cudaFuncSetAttribute(k_moe_small_down<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
-                    cudaSuccess)
-        return QW6K_ERR_CUDA;
-    cfg = true;
+    static DevFlags cfg;
+    if (smem_optin(cfg, k_moe_small_down<F>, 200 * 1024)) return QW6K_ERR_CUDA;
     return launch_ex(k_moe_small_down<F>, a.hidden / 16, smem, true, st, a);
 }
 

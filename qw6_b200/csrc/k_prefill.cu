@@ -20,6 +20,7 @@
 #include <cuda_runtime.h>
 
 #include "qw6_dev.cuh"
+#include "qw6_devcfg.cuh"
 #include "qw6_launch.h"
 #include "qw6_pdl.cuh"
 #include "qw6_route.cuh"
@@ -701,11 +702,8 @@ static int pf_args(const qw6k_moe_desc* d, int* err, PfArgs& a) {
 template <int F, int MODE>
 static int launch_pf(const PfArgs& a, int mi, cudaStream_t st) {
     const size_t smem = (size_t)kPfStageBudget + 1024;
-    static bool cfg = false;
-    if (!cfg && cudaFuncSetAttribute(k_pf_gemm<F, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-                    cudaSuccess)
-        return QW6K_ERR_CUDA;
-    cfg = true;
+    static DevFlags cfg;
+    if (smem_optin(cfg, k_pf_gemm<F, MODE>, (int)smem)) return QW6K_ERR_CUDA;
     const int nft = MODE == 0 ? a.inter / 128 : a.hidden / 256;
     return launch_pdl(k_pf_gemm<F, MODE>, dim3(mi * nft), dim3(kPfThreads), smem, st, a) == cudaSuccess ? 0
                                                                                              : QW6K_ERR_CUDA;

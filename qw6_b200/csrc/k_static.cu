@@ -7,24 +7,29 @@
 // host-side stand-in, never a device address, so the address handed to the
 // kernels comes from cudaGetSymbolAddress, looked up once per device with
 // that device current.
+#include <atomic>
+
 #include <cuda_runtime.h>
 
 #include "qw6_launch.h"
 
 static __device__ __align__(256) unsigned char g_qw6_static_scratch[QW6K_STATIC_SCRATCH_BYTES];
 
+// One slot per device ordinal.  The address is published with release order
+// after cudaGetSymbolAddress returned it and read with acquire order, so a
+// thread that sees a non-null slot also sees the address itself; two threads
+// racing on a device's first call both look it up and store the same value.
+static std::atomic<void*> g_scratch_addr[QW6K_MAX_DEVICES];
+
 extern "C" int qw6k_static_scratch(void** ptr, size_t* bytes) {
-    static void* addr[QW6K_MAX_DEVICES];
-    static int ready[QW6K_MAX_DEVICES];
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= QW6K_MAX_DEVICES) return QW6K_ERR_CUDA;
-    if (!ready[dev]) {
-        void* p = nullptr;
+    void* p = g_scratch_addr[dev].load(std::memory_order_acquire);
+    if (!p) {
         if (cudaGetSymbolAddress(&p, g_qw6_static_scratch) != cudaSuccess || !p) return QW6K_ERR_CUDA;
-        addr[dev] = p;
-        ready[dev] = 1;
+        g_scratch_addr[dev].store(p, std::memory_order_release);
     }
-    *ptr = addr[dev];
+    *ptr = p;
     *bytes = QW6K_STATIC_SCRATCH_BYTES;
     return 0;
 }

@@ -11,6 +11,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include "qw6_devcfg.cuh"
 #include "qw6_launch.h"
 #include "qw6_tc.cuh"
 
@@ -104,11 +105,8 @@ __global__ void __launch_bounds__(128) k_gemm_bf16_nt(const __nv_bfloat16* __res
 template <int BN>
 static int launch_gemm(const void* A, const void* B, float* D, int M, int N, int K, int* err, cudaStream_t st) {
     const size_t smem = 2 * (128 * 128 + BN * 128) + 1024;
-    static bool cfg = false;
-    if (!cfg && cudaFuncSetAttribute(k_gemm_bf16_nt<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-                    cudaSuccess)
-        return QW6K_ERR_CUDA;
-    cfg = true;
+    static DevFlags cfg;
+    if (smem_optin(cfg, k_gemm_bf16_nt<BN>, (int)smem)) return QW6K_ERR_CUDA;
     dim3 grid((M + 127) / 128, (N + BN - 1) / BN);
     k_gemm_bf16_nt<BN><<<grid, 128, smem, st>>>((const __nv_bfloat16*)A, (const __nv_bfloat16*)B, D, M, N, K, err);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
