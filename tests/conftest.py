@@ -8,7 +8,23 @@ import pytest
 ROOT = Path(__file__).resolve().parents[1]
 sys.path.insert(0, str(ROOT))
 
-REF_DIR = Path(os.environ.get("QW6_REF", "/root/reference"))
+
+
+def _reference_dir():
+    """qw6's source tree, for the tests that read or compile it: $QW6_REF, else
+    BASELINE.json's `reference_path`.  None when neither names an existing
+    tree (those tests then skip)."""
+    p = os.environ.get("QW6_REF")
+    if not p:
+        try:
+            import json
+            p = json.loads((ROOT / "BASELINE.json").read_text()).get("reference_path")
+        except (OSError, ValueError):
+            p = None
+    return Path(p) if p and Path(p).is_dir() else None
+
+
+REF_DIR = _reference_dir() or ROOT / "_no_reference_tree"
 
 
 def pytest_configure(config):
