@@ -112,6 +112,41 @@ class Oracle:
             raise ValueError("matvec_f64 failed")
         return y
 
+    def moe_layer_grouped_f64(self, gq, gate, up, dq, down, logits, x, top_k=8):
+        """Float64 recomputation of the routed-MoE layer (qw6.c:2246-2264) for a
+        whole token batch, grouped by expert: the routing (indices and fp32
+        softmax weights) is the oracle's bit-exact qw6_cpu_moe_route, every
+        expert's weights are the oracle's bit-exact dequantization widened to
+        float64, and each expert's rows are one float64 matmul per projection,
+        so a batch of thousands of tokens takes seconds.  Returns (out [ntok,
+        hidden] float64, idx, w)."""
+        logits = np.ascontiguousarray(logits, np.float32)
+        x = np.ascontiguousarray(x, np.float32).astype(np.float64)
+        ntok, hidden = x.shape
+        inter = gate.shape[1]
+        idx = np.empty((ntok, top_k), np.int32)
+        w = np.empty((ntok, top_k), np.float32)
+        for t in range(ntok):
+            idx[t], w[t] = self.moe_route(logits[t], top_k)
+        out = np.zeros((ntok, hidden), np.float64)
+        flat = idx.reshape(-1)
+        order = np.argsort(flat, kind="stable")
+        bounds = np.searchsorted(flat[order], np.arange(gate.shape[0] + 1))
+        for e in range(gate.shape[0]):
+            sel = order[bounds[e]:bounds[e + 1]]
+            if sel.size == 0:
+                continue
+            tok = sel // top_k
+            wg = self.dequantize(gq, gate[e], inter, hidden).astype(np.float64)
+            wu = self.dequantize(gq, up[e], inter, hidden).astype(np.float64)
+            wd = self.dequantize(dq, down[e], hidden, inter).astype(np.float64)
+            xe = x[tok]
+            g, u = xe @ wg.T, xe @ wu.T
+            with np.errstate(over="ignore"):  # exp(-g) = inf for very negative g: silu -> 0, as intended
+                mid = g / (1.0 + np.exp(-g)) * u
+            np.add.at(out, tok, (mid @ wd.T) * w.reshape(-1)[sel].astype(np.float64)[:, None])
+        return out, idx, w
+
     def moe_route(self, logits: np.ndarray, top_k: int):
         logits = np.ascontiguousarray(logits, np.float32)
         idx = np.empty(top_k, np.int32)
@@ -244,6 +279,9 @@ class Reference:
         lib.ref_sample.argtypes = [_f32p, C.c_float, C.c_float, C.c_int, C.c_uint]
         lib.ref_rand_unit.argtypes = [C.c_uint]
         lib.ref_rand_unit.restype = C.c_float
+        lib.ref_moe_tokens.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_size_t, C.c_int, C.c_void_p, C.c_size_t,
+                                       C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32,
+                                       C.c_uint32, C.c_int, C.c_int]
         self.lib = lib
         self.vocab = int(lib.ref_vocab_size())
 
@@ -269,6 +307,23 @@ class Reference:
     def matvec_rows(self, quant, w_rows, x, rows, cols):
         """matvec over a contiguous slice of rows (bounded CPU samples)."""
         return self.matvec(quant, w_rows, x, rows, cols)
+
+    def moe_tokens(self, gq, gate, up, dq, down, logits, x, t0, t1, top_k=8):
+        """Tokens [t0, t1) of the routed-MoE layer through qw6's own expert loop
+        (qw6.c:2246-2264) run entirely in C; gate/up/down are expert packs
+        [n_experts, rows, row_bytes], logits [ntok, n_experts], x [ntok, hidden].
+        Returns out rows [t1 - t0, hidden]."""
+        gate, up, down = (np.ascontiguousarray(a).view(np.uint8) for a in (gate, up, down))
+        logits = np.ascontiguousarray(logits[t0:t1], np.float32)
+        x = np.ascontiguousarray(x[t0:t1], np.float32)
+        ne, hidden, inter = logits.shape[1], x.shape[1], up.shape[1]
+        out = np.zeros_like(x)
+        rc = self.lib.ref_moe_tokens(gq, gate.ctypes.data, up.ctypes.data, gate[0].nbytes, dq, down.ctypes.data,
+                                     down[0].nbytes, logits.ctypes.data, x.ctypes.data, out.ctypes.data, 0,
+                                     t1 - t0, hidden, inter, ne, top_k)
+        if rc:
+            raise ValueError("ref moe_tokens failed")
+        return out
 
     def moe_route(self, logits, top_k):
         logits = np.ascontiguousarray(logits, np.float32)

@@ -7,8 +7,9 @@
  *   qw6_tensor_dequantize_row (qw6.c:1674), qw6_tensor_matvec (qw6.c:1769),
  *   qw6_cpu_moe_route (qw6.c:2796), qw6_cpu_argmax (qw6.c:2858),
  *   qw6_cpu_rmsnorm (qw6.c:2502), qw6_sample (qw6.c:2921, over qw6's full
- *   QW6_VOCAB_SIZE logits, with libc's rand() seeded first), and the
- *   qw6_silu / qw6_sigmoid inlines (qw6.h:292-297).
+ *   QW6_VOCAB_SIZE logits, with libc's rand() seeded first), the
+ *   qw6_silu / qw6_sigmoid inlines (qw6.h:292-297), and the routed-expert
+ *   loop of qw6_apply_layer_moe (qw6.c:2246-2264) over a range of tokens.
  * The shim only wraps raw block bytes in a qw6_tensor_t and validates
  * arguments first, because the reference asserts (exit(1)) on bad input.
  */
@@ -98,4 +99,53 @@ int ref_sample(const float *logits, float temp, float top_p, int top_k, unsigned
 float ref_rand_unit(unsigned seed) {
     srand(seed);
     return (float)rand() / ((float)RAND_MAX + 1.0f);
+}
+
+/* Tokens [t0, t1) of a routed-MoE layer exactly as qw6_apply_layer_moe's
+ * expert loop runs them (qw6.c:2246-2264): per token, qw6_cpu_moe_route of
+ * its logits row, then for each selected expert in selection order
+ * g = Wg[e].x, u = Wu[e].x, mid = silu(g)*u, t = Wd[e].mid, out += w_e*t.
+ * Expert e's matrices are at base + e*stride (bind_expert_pack, qw6.c:542-597);
+ * x and out are [ntok][hidden] rows, logits [ntok][n_experts].  No shared
+ * expert (the benchmark configurations have none).  The whole loop runs in C,
+ * so a caller can time qw6's CPU path without interpreter work per element. */
+int ref_moe_tokens(int gq, const void *gate, const void *up, size_t gstride, int dq,
+                   const void *down, size_t dstride, const float *logits, const float *x,
+                   float *out, uint32_t t0, uint32_t t1, uint32_t hidden, uint32_t inter,
+                   int n_experts, int top_k) {
+    if (!gate || !up || !down || !logits || !x || !out || t1 < t0 || !block_ok(gq, hidden) ||
+        !block_ok(dq, inter) || n_experts <= 0 || n_experts > 256 || top_k <= 0 || top_k > n_experts ||
+        top_k > 32)
+        return -1;
+    float *g = malloc(sizeof(float) * inter), *u = malloc(sizeof(float) * inter);
+    float *mid = malloc(sizeof(float) * inter), *tmp = malloc(sizeof(float) * hidden);
+    int rc = (g && u && mid && tmp) ? 0 : -1;
+    for (uint32_t t = t0; t < t1 && rc == 0; t++) {
+        int idx[32];
+        float w[32];
+        const float *xt = x + (size_t)t * hidden;
+        float *ot = out + (size_t)t * hidden;
+        memset(ot, 0, sizeof(float) * hidden);
+        qw6_cpu_moe_route(idx, w, logits + (size_t)t * n_experts, n_experts, top_k);
+        for (int k = 0; k < top_k && rc == 0; k++) {
+            const size_t e = (size_t)idx[k];
+            qw6_tensor_t tg, tu, td;
+            wrap(&tg, gq, (const uint8_t *)gate + e * gstride, inter, hidden);
+            wrap(&tu, gq, (const uint8_t *)up + e * gstride, inter, hidden);
+            wrap(&td, dq, (const uint8_t *)down + e * dstride, hidden, inter);
+            rc = qw6_tensor_matvec(g, &tg, xt, 0);
+            if (rc == 0) rc = qw6_tensor_matvec(u, &tu, xt, 0);
+            if (rc == 0) {
+                for (uint32_t i = 0; i < inter; i++) mid[i] = qw6_silu(g[i]) * u[i];
+                rc = qw6_tensor_matvec(tmp, &td, mid, 0);
+            }
+            if (rc == 0)
+                for (uint32_t i = 0; i < hidden; i++) ot[i] += w[k] * tmp[i];
+        }
+    }
+    free(g);
+    free(u);
+    free(mid);
+    free(tmp);
+    return rc;
 }

@@ -124,6 +124,25 @@ def test_moe_layer_matches_reference_composition(oracle, reference, rng):
     o2, i2, w2 = reference.moe_layer(S.Q4_K, gate, up, S.Q6_K, down, logits, x, top_k=4)
     assert np.array_equal(i1, i2) and same_bits(w1, w2)
     assert same_bits(o1, o2)
+    # the all-C token loop the CPU baseline times gives the same bits
+    o3 = reference.moe_tokens(S.Q4_K, gate, up, S.Q6_K, down, logits, x, 0, 2, top_k=4)
+    assert same_bits(o3, o2)
+    assert same_bits(reference.moe_tokens(S.Q4_K, gate, up, S.Q6_K, down, logits, x, 1, 2, top_k=4), o2[1:])
+
+
+def test_moe_layer_grouped_f64_matches_per_token_f64(oracle, rng):
+    """The expert-grouped float64 recomputation used for whole-batch GPU
+    checks agrees with the oracle's per-token float64 layer (same routing,
+    same bit-exact weights) to float64 rounding."""
+    E, H, I, T = 12, 512, 256, 9
+    gate, up, down = S.moe_weights(rng, E, S.Q4_K, S.Q6_K, H, I)
+    logits = rng.standard_normal((T, E), dtype=np.float32)
+    x = rng.standard_normal((T, H), dtype=np.float32)
+    g64, idx, w = oracle.moe_layer_grouped_f64(S.Q4_K, gate, up, S.Q6_K, down, logits, x, top_k=4)
+    p64 = oracle.moe_layer(S.Q4_K, gate, up, S.Q6_K, down, logits, x, top_k=4, f64=True)
+    _, i32, w32 = oracle.moe_layer(S.Q4_K, gate, up, S.Q6_K, down, logits, x, top_k=4)
+    assert np.array_equal(idx, i32) and same_bits(w, w32)
+    assert np.max(np.abs(g64 - p64)) <= 1e-12 * np.max(np.abs(p64))
 
 
 # ---- known-answer tests of qw6's Vulkan self-test, against the oracle ----
