@@ -116,60 +116,115 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------ CPU legs ----
+#
+# qw6's own CPU implementation of the layer (oracle/_ref, compiled from the
+# reference sources): qw6_cpu_moe_route + the expert loop of
+# qw6_apply_layer_moe (qw6.c:2246-2264), run entirely in C per token
+# (ref_moe_tokens).  qw6 is single-threaded; the harness slices tokens over a
+# fork pool of one process per host core.  The pool is forked before this
+# process touches CUDA (a pool forked after CUDA initialisation can hang).
 
-def cpu_reference_rate(gate, up, down, logits, x, budget_s: float, threads: int):
-    """qw6's own CPU code (oracle/_ref): tokens/s of the MoE layer over a
-    bounded sample.  Units of work are (token, selected expert) pairs run on
-    `threads` host threads (ctypes drops the GIL inside qw6's C)."""
-    from concurrent.futures import ThreadPoolExecutor
+_POOL = {}  # set in the parent before forking; the workers inherit it
 
-    from oracle.oracle import Reference
-    ref = Reference()
-    ntok = logits.shape[0]
-    routes = [ref.moe_route(logits[t], TOPK) for t in range(ntok)]
 
-    def unit(u):
-        t, k = divmod(u, TOPK)
-        t %= ntok
-        e = int(routes[t][0][k])
-        g = ref.matvec(4, gate[e], x[t], INTER, HIDDEN)
-        uu = ref.matvec(4, up[e], x[t], INTER, HIDDEN)
-        mid = np.array([ref.silu(float(v)) for v in g], np.float32) * uu
-        return np.float32(routes[t][1][k]) * ref.matvec(7, down[e], mid.astype(np.float32), HIDDEN, INTER)
+def host_info() -> dict:
+    model = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    from oracle.oracle import cpu_count
+    return {"nproc": os.cpu_count(), "usable_cores": cpu_count(), "cpu_model": model}
 
-    done = 0
-    t0 = time.perf_counter()
-    with ThreadPoolExecutor(max_workers=threads) as ex:
-        while time.perf_counter() - t0 < budget_s:
-            list(ex.map(unit, range(done, done + threads)))
-            done += threads
-    dt = time.perf_counter() - t0
-    return done / TOPK / dt, done, dt
+
+def _pool_tokens(span):
+    t0, t1 = span
+    ref = _POOL.get("ref")
+    if ref is None:
+        from oracle.oracle import Reference
+        ref = _POOL["ref"] = Reference()
+    gate, up, down, logits, x = _POOL["data"]
+    ref.moe_tokens(4, gate, up, 7, down, logits, x, t0, t1, top_k=TOPK)
+    return t1 - t0
+
+
+class CpuMoE:
+    """qw6's CPU MoE layer over a token sample, 1 thread or a fork pool."""
+
+    def __init__(self, gate, up, down, logits, x, workers: int):
+        _POOL["data"] = (gate, up, down, logits, x)
+        self.ntok = logits.shape[0]
+        self.workers = workers
+        self.next = 0
+        self.pool = None
+        if workers > 1:
+            import multiprocessing as mp
+            self.pool = mp.get_context("fork").Pool(workers)
+
+    def spans(self, ntok, per):
+        out = []
+        while ntok > 0:
+            n = min(per, ntok, self.ntok - self.next)
+            out.append((self.next, self.next + n))
+            self.next = (self.next + n) % self.ntok
+            ntok -= n
+        return out
+
+    def run(self, ntok, per=1) -> float:
+        """Seconds to run ntok tokens of the sample (continuing round robin)."""
+        sp = self.spans(ntok, per)
+        t0 = time.perf_counter()
+        if self.pool is None:
+            for s in sp:
+                _pool_tokens(s)
+        else:
+            self.pool.map(_pool_tokens, sp, chunksize=1)
+        return time.perf_counter() - t0
+
+    def close(self):
+        if self.pool is not None:
+            self.pool.close()
+            self.pool.join()
+            self.pool = None
+
+
+def cpu_baseline_c3(gate, up, down, logits, x, seconds_1=4.0, seconds_n=10.0) -> dict:
+    """qw6's CPU path on config 3's tokens: ~seconds_1 on one thread and
+    ~seconds_n over all usable cores (token-sliced fork pool)."""
+    from oracle.oracle import cpu_count
+    info = host_info()
+    one = CpuMoE(gate, up, down, logits, x, 1)
+    one.run(1)  # warm (loads the library, touches the first experts)
+    n1, dt1 = 0, 0.0
+    while dt1 < seconds_1:
+        dt1 += one.run(2)
+        n1 += 2
+    rate1 = n1 / dt1
+    workers = cpu_count()
+    pool = CpuMoE(gate, up, down, logits, x, workers)
+    pool.run(workers)
+    per_round = workers * max(1, int(rate1 * 2.0))  # ~2 s rounds
+    nn, dtn = 0, 0.0
+    while dtn < seconds_n:
+        dtn += pool.run(per_round)
+        nn += per_round
+    pool.close()
+    raten = nn / dtn
+    return {"value": round(raten, 2), "unit": "tokens/s", "cores": workers, "kind": "reference",
+            "value_1core": round(rate1, 2),
+            "sample": f"{nn} of config 3's tokens in {dtn:.1f} s over a fork pool of {workers} processes (token "
+                      f"slices; 'harness parallelised', qw6 itself is single-threaded) and {n1} tokens in "
+                      f"{dt1:.1f} s on 1 thread, each token through qw6's own qw6_cpu_moe_route and expert loop "
+                      "(qw6_tensor_matvec, qw6_silu; qw6.c:2246-2264) compiled from the reference sources "
+                      "(oracle/_ref); the reference's Vulkan path is unavailable on this box",
+            "host": info}
 
 
 # ------------------------------------------------------------- our arm ----
-
-def build_layers(torch, ctx, L, n_layers):
-    """Config-1 expert packs (seeded numpy generator), packed on the GPU,
-    replicated into n_layers resident copies."""
-    from qw6_b200 import synth as S
-    gate, up, down, _, _ = S.config1()
-    packs = []
-    for q, m, r, c in ((S.Q4_K, gate, INTER, HIDDEN), (S.Q4_K, up, INTER, HIDDEN), (S.Q6_K, down, HIDDEN, INTER)):
-        pb = ctx.packed_bytes(q, r, c)
-        raw = torch.from_numpy(m.reshape(-1)).cuda()
-        pk = torch.empty(pb * NE, dtype=torch.uint8, device="cuda")
-        torch.cuda.synchronize()
-        ctx.pack(q, raw.data_ptr(), pk.data_ptr(), r, c, NE, m[0].nbytes, pb)
-        ctx.synchronize()
-        del raw
-        copies = [pk] + [pk.clone() for _ in range(n_layers - 1)]
-        packs.append((q, pb, copies))
-    layers = []
-    for li in range(n_layers):
-        layers.append(tuple(L.ExpertPack(q, copies[li].data_ptr(), pb) for q, pb, copies in packs))
-    return (gate, up, down), packs, layers
-
 
 def timed(torch, stream, dist, fn, nsteps):
     """Device time of nsteps calls of fn on `stream`, bracketed by barrier +
@@ -193,8 +248,15 @@ def timed(torch, stream, dist, fn, nsteps):
 def run_ours(args, rank, local_rank, world):
     import torch
 
-    from qw6_b200 import lib as L
+    from qw6_b200 import synth as S
+    c3 = S.config3(with_bias=True)
+    cpu = None
+    if args.cpu_baseline and world == 1 and rank == 0:
+        # before this process initialises CUDA: the pool is forked
+        gate, up, down, logits, xbits, _ = c3
+        cpu = cpu_baseline_c3(gate, up, down, logits, S.bf16_to_f32(xbits))
 
+    from qw6_b200 import lib as L
     torch.cuda.set_device(local_rank)
     dist = None
     if world > 1:
@@ -206,14 +268,20 @@ def run_ours(args, rank, local_rank, world):
     stream = torch.cuda.Stream()
     ctx = L.Context(local_rank)
     ctx.set_stream(stream.cuda_stream)
-    head = ep_bench(args, torch, ctx, L, stream, rank, world, dist)
-    dec = decode_bench(args, torch, ctx, L, stream, rank, world, dist) if args.decode else None
-    matvec = matvec_sweep(torch, ctx, stream) if (rank == 0 and args.matvec) else None
+    head = ep_bench(args, torch, ctx, L, stream, rank, world, dist, c3)
+    del c3
+    dec = {}
+    if args.decode:
+        for c in (1, 2):
+            dec[f"config{c}"] = moe_decode_bench(args, torch, ctx, L, stream, rank, world, dist, c)
+    matvec = None
+    if rank == 0 and args.matvec:
+        matvec = {"configs": matvec_configs(torch, ctx, stream), "tall_sweep": matvec_sweep(torch, ctx, stream)}
     lmh = lm_head_bench(torch, ctx, stream, rank, world, dist) if args.lm_head else None
     result = None
     if rank == 0:
-        result = report(args, world, head)
-        result["decode"] = dec
+        result = report(args, world, head, cpu)
+        result["decode"] = dec or None
         result["matvec"] = matvec
         result["lm_head"] = lmh
     if dist:
@@ -227,7 +295,7 @@ PF_FLOPS_ROW = {"pf_gemm1": 2 * 2 * INTER * HIDDEN, "pf_gemm2": 2 * HIDDEN * INT
 T3 = 4096
 
 
-def ep_bench(args, torch, ctx, L, stream, rank, world, dist):
+def ep_bench(args, torch, ctx, L, stream, rank, world, dist, c3):
     """Config 3 with the experts sharded over the ranks.  N=1: the
     single-GPU layer (qw6cu_moe_prefill); N>1: the peer-memory expert-parallel
     layer (qw6_b200.ep.PeerMoE: dispatch/combine kernels over NVLink, no
@@ -236,7 +304,7 @@ def ep_bench(args, torch, ctx, L, stream, rank, world, dist):
     inputs from pinned host memory and reads the output back."""
     from qw6_b200 import synth as S
     from qw6_b200.ep import PeerMoE, balance_experts
-    gate, up, down, logits, xbits, bias = S.config3(with_bias=True)
+    gate, up, down, logits, xbits, bias = c3
     epr, tpr = NE // world, T3 // world
     placement = None
     if world > 1:  # balance the ranks' rows on routing statistics of an independent calibration batch
@@ -341,73 +409,109 @@ def ep_bench(args, torch, ctx, L, stream, rank, world, dist):
     del packs, copies
     torch.cuda.empty_cache()
     return {"ms": ms, "clk": clk, "prof": prof, "rows": rows, "e2e_ms": e2e_ms, "e2e_steps": ke, "graph_steps": G,
-            "h2d": tpr * NE * 4 + tpr * HIDDEN * 2, "d2h": tpr * HIDDEN * 4, "finite": out_ok,
-            "cpu_data": (gate, up, down, logits[:16], S.bf16_to_f32(xbits[:16]))}
+            "h2d": tpr * NE * 4 + tpr * HIDDEN * 2, "d2h": tpr * HIDDEN * 4, "finite": out_ok}
 
 
 def local_rank_of(rank):
     return int(os.environ.get("LOCAL_RANK", rank))
 
 
-def decode_bench(args, torch, ctx, L, stream, rank, world, dist):
-    """Config 1 (decode batch 1) as N replicas: a CUDA graph of 256 steps
-    replayed back to back over 16 resident layer copies; HBM roofline of
-    the dominant kernel; end to end through qw6cu_moe_decode_hostio."""
-    raw, packs, layers = build_layers(torch, ctx, L, args.layers)
-    nl = args.layers
-    K = args.decode_steps
-    nslots = GRAPH_STEPS
-    gen = torch.Generator(device="cuda").manual_seed(1000 + rank)
-    logits = torch.randn((nslots, NE), generator=gen, device="cuda", dtype=torch.float32)
-    xs = torch.randn((nslots, HIDDEN), generator=gen, device="cuda", dtype=torch.float32)
-    outs = torch.empty((nslots, HIDDEN), device="cuda", dtype=torch.float32)
+IQ2XXS_BYTES_EXPERT = 512 * 8 * 66                            # one IQ2_XXS expert matrix (gate, up or down)
+DECODE = {  # config: (tokens, gate/up quant, down quant, gate/up bytes per expert, down bytes per expert, graph steps)
+    1: (1, 4, 7, Q4K_BYTES_EXPERT, Q6K_BYTES_EXPERT, 256),
+    2: (64, 13, 13, IQ2XXS_BYTES_EXPERT, IQ2XXS_BYTES_EXPERT, 32),
+}
+
+
+def distinct_experts(logits: np.ndarray) -> int:
+    """Experts a batch of router logits selects (top-8, lower index on ties,
+    as qw6_cpu_moe_route)."""
+    return int(np.unique(np.argsort(-logits, axis=1, kind="stable")[:, :TOPK]).size)
+
+
+def moe_decode_bench(args, torch, ctx, L, stream, rank, world, dist, config):
+    """Configs 1 and 2 (decode batch 1 / batched decode of 64 tokens with
+    IQ2_XXS experts) as N replicas: a CUDA graph of steps replayed back to
+    back over `args.layers` resident layer copies (step s uses copy s % layers
+    and router/activation slot s % 16); HBM roofline of the step and of its
+    dominant kernel over the distinct experts' bytes; end to end through
+    qw6cu_moe_decode_hostio."""
+    from qw6_b200 import synth as S
+    ntok, gq, dq, gub, dnb, gsteps = DECODE[config]
+    nl, nslots = args.layers, 16
+    rng = np.random.Generator(np.random.PCG64(config))
+    gate, up, down = S.moe_weights(rng, NE, gq, dq)
+    copies = []
+    for q, m, r, c in ((gq, gate, INTER, HIDDEN), (gq, up, INTER, HIDDEN), (dq, down, HIDDEN, INTER)):
+        pb = ctx.packed_bytes(q, r, c)
+        raw = torch.from_numpy(m.reshape(-1)).cuda()
+        pk = torch.empty(pb * NE, dtype=torch.uint8, device="cuda")
+        torch.cuda.synchronize()
+        ctx.pack(q, raw.data_ptr(), pk.data_ptr(), r, c, NE, m[0].nbytes, pb)
+        ctx.synchronize()
+        del raw
+        copies.append((q, pb, [pk] + [pk.clone() for _ in range(nl - 1)]))
+    del gate, up, down
+    layers = [tuple(L.ExpertPack(q, cp[i].data_ptr(), pb) for q, pb, cp in copies) for i in range(nl)]
+    # router logits and activations of 16 token batches (seeded, N(0,1))
+    lg_np = [np.random.Generator(np.random.PCG64(1000 * config + 17 * rank + j)).standard_normal(
+        (ntok, NE), dtype=np.float32) for j in range(nslots)]
+    eact = [distinct_experts(v) for v in lg_np]
+    logits = torch.from_numpy(np.stack(lg_np)).cuda()
+    xs = torch.from_numpy(np.random.Generator(np.random.PCG64(2000 * config + rank)).standard_normal(
+        (nslots, ntok, HIDDEN), dtype=np.float32)).cuda()
+    outs = torch.empty((nslots, ntok, HIDDEN), device="cuda", dtype=torch.float32)
     torch.cuda.synchronize()
 
     def step(s):
         g, u, d = layers[s % nl]
         j = s % nslots
-        ctx.moe_decode(g, u, d, logits[j].data_ptr(), xs[j].data_ptr(), outs[j].data_ptr(), 1, HIDDEN, INTER, NE,
-                       TOPK)
+        ctx.moe_decode(g, u, d, logits[j].data_ptr(), xs[j].data_ptr(), outs[j].data_ptr(), ntok, HIDDEN, INTER,
+                       NE, TOPK)
 
     with torch.cuda.stream(stream):
-        for s in range(max(args.warmup, 1)):
+        for s in range(max(args.warmup, 3)):
             step(s)
     ctx.synchronize()
+    ctx.check_device_errors()
 
     def capture(nsteps, profile):
         g = torch.cuda.CUDAGraph()
         if profile:
-            ctx.profile_begin(4 * nsteps + 8)
+            ctx.profile_begin(8 * nsteps + 8)
         with torch.cuda.graph(g, stream=stream, capture_error_mode="thread_local"):
             for s in range(nsteps):
                 step(s)
         return g
 
-    full = capture(GRAPH_STEPS, False)
-    reps = max(1, K // GRAPH_STEPS)
-    K = reps * GRAPH_STEPS
+    K = args.decode_steps if config == 1 else max(gsteps, args.decode_steps // 8)
+    full = capture(gsteps, False)
+    reps = max(1, K // gsteps)
+    K = reps * gsteps
     with torch.cuda.stream(stream):
         full.replay()
     torch.cuda.synchronize()
     ms = timed(torch, stream, dist, lambda s: full.replay(), reps)
-    pg = capture(GRAPH_STEPS, True)
-    with torch.cuda.stream(stream):
-        pg.replay()
-    torch.cuda.synchronize()
-    with torch.cuda.stream(stream):
-        pg.replay()
+    pg = capture(gsteps, True)
+    for _ in range(2):
+        with torch.cuda.stream(stream):
+            pg.replay()
+        torch.cuda.synchronize()
     prof = ctx.profile_end()
     del pg, full
+    ctx.check_device_errors()
 
-    e2e_steps = min(K, 2048)
-    h_logits = torch.randn((64, NE), dtype=torch.float32).pin_memory()
-    h_x = torch.randn((64, HIDDEN), dtype=torch.float32).pin_memory()
-    h_out = torch.empty((64, HIDDEN), dtype=torch.float32).pin_memory()
+    # end to end: host logits/x in, host out, synchronous per step
+    e2e_steps = min(K, 2048 if config == 1 else 256)
+    h_logits = torch.from_numpy(np.stack(lg_np)).pin_memory()
+    h_x = xs.cpu().pin_memory()
+    h_out = torch.empty((nslots, ntok, HIDDEN), dtype=torch.float32).pin_memory()
 
     def hostio(s):
         g, u, d = layers[s % nl]
-        ctx.moe_decode_hostio(g, u, d, h_logits[s % 64].data_ptr(), h_x[s % 64].data_ptr(),
-                              h_out[s % 64].data_ptr(), 1, HIDDEN, INTER, NE, TOPK)
+        j = s % nslots
+        ctx.moe_decode_hostio(g, u, d, h_logits[j].data_ptr(), h_x[j].data_ptr(), h_out[j].data_ptr(), ntok,
+                              HIDDEN, INTER, NE, TOPK)
 
     for s in range(8):
         hostio(s)
@@ -420,41 +524,133 @@ def decode_bench(args, torch, ctx, L, stream, rank, world, dist):
     if dist:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_s = float(te.item())
-    del layers, packs
+    del layers, copies
     torch.cuda.empty_cache()
 
     hbm, peak_kind = peaks()
-    per_launch = {
-        "moe_gateup": TOPK * 2 * Q4K_BYTES_EXPERT + HIDDEN * 4 + TOPK * INTER * 4,
-        "moe_down": TOPK * Q6K_BYTES_EXPERT + TOPK * INTER * 4 + HIDDEN * 4,  # down + fused combine
-    }
+    ea = float(np.mean([eact[s % nslots] for s in range(K)]))
+    xb, ob, lb = ntok * HIDDEN * 4, ntok * HIDDEN * 4, ntok * NE * 4
+    mid = ntok * TOPK * INTER * 4
+    per_launch = {"moe_gateup": ea * 2 * gub + xb + mid, "moe_down": ea * dnb + mid + ob}
+    if config == 1:  # down + fused combine; gate/up routes itself
+        per_launch["moe_gateup"] += lb
+    else:
+        per_launch["moe_down"] = ea * dnb + mid + ntok * TOPK * HIDDEN * 4
+    step_bytes = ea * (2 * gub + dnb) + xb + ob + lb
     dom = max((k for k in prof if k in per_launch), key=lambda k: prof[k][0])
     dom_ms = prof[dom][0] / prof[dom][1]
     achieved = per_launch[dom] / (dom_ms / 1e3) / 1e9
-    step_bytes = WEIGHT_BYTES_TOKEN + HIDDEN * 4 * 2 + NE * 4
-    tokens = K * world
+    step_gbs = step_bytes * K / (ms / 1e3) / 1e9
+    tokens = K * ntok * world
     return {
-        "workload": "config 1: MoE FFN layer, decode batch 1 (N independent replicas)",
+        "workload": {1: "config 1: MoE FFN layer, decode batch 1, Q4_K gate/up + Q6_K down",
+                     2: "config 2: batched-decode MoE layer, 64 tokens, IQ2_XXS gate/up/down"}[config]
+                    + " (N independent replicas)",
         "tokens_s": round(tokens / (ms / 1e3), 1), "ms_per_step": round(ms / K, 5), "steps": K,
-        "hbm_gbs_step": round(step_bytes * K / (ms / 1e3) / 1e9, 1),
+        "distinct_experts_per_step": round(ea, 2),
+        "algorithmic_bytes_per_step": int(step_bytes),
+        "hbm_gbs_step": round(step_gbs, 1), "hbm_frac_step": round(step_gbs / hbm, 3),
         "l2": f"inputs larger than L2: {nl} resident layer copies "
-              f"({nl * NE * (2 * Q4K_BYTES_EXPERT + Q6K_BYTES_EXPERT) / 1e9:.1f} GB), step s uses layer s % {nl}",
-        "graph": f"CUDA graph of {GRAPH_STEPS} steps replayed",
+              f"({nl * NE * (2 * gub + dnb) / 1e9:.1f} GB), step s uses layer s % {nl}",
+        "graph": f"CUDA graph of {gsteps} steps replayed",
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 3), "peak_kind": peak_kind,
-                     "traffic": traffic_from_profiles(dom), "algorithmic_bytes_per_launch": per_launch[dom]},
+                     "traffic": traffic_from_profiles(f"decode_c{config}_{dom}"),
+                     "algorithmic_bytes_per_launch": int(per_launch[dom])},
         "kernels": {k: {"avg_us": round(v[0] / v[1] * 1e3, 2), "launches_profiled": v[1]} for k, v in prof.items()},
-        "e2e": {"value": round(e2e_steps * world / e2e_s, 1), "unit": "tokens/s",
-                "h2d_bytes_per_step": (NE + HIDDEN) * 4, "d2h_bytes_per_step": HIDDEN * 4,
+        "e2e": {"value": round(e2e_steps * ntok * world / e2e_s, 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": lb + xb, "d2h_bytes_per_step": ob,
                 "api": "qw6cu_moe_decode_hostio (pinned host logits/x/out, synchronous per step)"},
-        "gpu_launches_per_step": sum(c for _, c in prof.values()) // GRAPH_STEPS,
+        "gpu_launches_per_step": sum(c for _, c in prof.values()) // gsteps,
     }
 
 
+MATVEC_CONFIGS = (  # (name, quant, rows, cols): config 0 and config 4's projections
+    ("c0_q4k_512x2048", 4, 512, 2048),
+    ("c4_q5k_4096x2048", 6, 4096, 2048),
+    ("c4_iq2s_2048x4096", 11, 2048, 4096),
+    ("c4_iq3s_2048x2048", 9, 2048, 2048),
+)
+
+
+def matvec_configs(torch, ctx, stream):
+    """Configs 0 and 4 (projections) at their own shapes, batch 1 and 32, by
+    the rotation protocol: K distinct copies of the packed matrix (K x bytes
+    >= 512 MB, 4x L2) launched back to back inside one CUDA graph, median of
+    >= 20 replays; plus the single-call latency with L2 flushed."""
+    from qw6_b200 import synth as S
+    hbm, kind = peaks()
+    rng = np.random.Generator(np.random.PCG64(4))
+    res = {"protocol": "K copies (K x weight bytes >= 512 MB) rotated in one CUDA graph; median of 25 replays",
+           "peak": hbm, "peak_kind": kind}
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    for name, q, rows, cols in MATVEC_CONFIGS:
+        raw = S.make_matrix(q, rows, cols, rng) if q != 4 else S.config0()[0]
+        pb = ctx.packed_bytes(q, rows, cols)
+        stride = (pb + 255) // 256 * 256
+        ncopy = max(1, -(-(512 << 20) // pb))
+        w = torch.empty(stride * ncopy, dtype=torch.uint8, device="cuda")
+        rd = torch.from_numpy(raw.reshape(-1)).cuda()
+        torch.cuda.synchronize()
+        ctx.pack(q, rd.data_ptr(), w.data_ptr(), rows, cols)
+        ctx.synchronize()
+        w.view(ncopy, stride)[1:] = w.view(ncopy, stride)[0]
+        del rd
+        wbytes = rows * (cols // 256) * S.BLOCK_BYTES[q]
+        entry = {"shape": [rows, cols], "weight_bytes": wbytes, "copies": ncopy}
+        for ntok in (1, 32):
+            x = torch.randn(ntok, cols, device="cuda")
+            y = torch.empty(ntok, rows, device="cuda")
+            torch.cuda.synchronize()
+            for _ in range(3):
+                ctx.matvec(q, w.data_ptr(), x.data_ptr(), y.data_ptr(), rows, cols, ntok)
+            ctx.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream, capture_error_mode="thread_local"):
+                for i in range(ncopy):
+                    ctx.matvec(q, w.data_ptr() + i * stride, x.data_ptr(), y.data_ptr(), rows, cols, ntok)
+            with torch.cuda.stream(stream):
+                g.replay()
+            torch.cuda.synchronize()
+            times = []
+            for _ in range(25):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                with torch.cuda.stream(stream):
+                    g.replay()
+                e1.record(stream)
+                torch.cuda.synchronize()
+                times.append(e0.elapsed_time(e1) / ncopy)
+            ms = float(np.median(times))
+            del g
+            # single call with L2 flushed
+            lat = []
+            for i in range(12):
+                with torch.cuda.stream(stream):
+                    flush.fill_(i & 255)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                ctx.matvec(q, w.data_ptr(), x.data_ptr(), y.data_ptr(), rows, cols, ntok)
+                e1.record(stream)
+                torch.cuda.synchronize()
+                if i >= 2:
+                    lat.append(e0.elapsed_time(e1) * 1e3)
+            b = wbytes + ntok * cols * 4 + ntok * rows * 4
+            entry[f"b{ntok}"] = {"us_per_call": round(ms * 1e3, 3), "gbs": round(b / ms / 1e6, 1),
+                                 "frac": round(b / ms / 1e6 / hbm, 3),
+                                 "single_call_l2_flushed_us": round(float(np.median(lat)), 2)}
+            del x, y
+        res[name] = entry
+        del w
+        torch.cuda.empty_cache()
+    del flush
+    return res
+
+
 def matvec_sweep(torch, ctx, stream):
-    """HBM throughput of the fused dequant-matvec per format on a matrix of
-    >= 512 MB (4x L2) in the packed layout, plus single-call latency of
-    config 0's 512 x 2048 Q4_K matvec with L2 flushed."""
+    """Streaming HBM throughput of the fused dequant-matvec per format, batch
+    1, on one tall matrix of >= 512 MB (4x L2) in the packed layout, 20
+    launches back to back."""
     from qw6_b200 import synth as S
     hbm, _ = peaks()
     out = {}
@@ -482,24 +678,6 @@ def matvec_sweep(torch, ctx, stream):
         out[S.QUANT_NAMES[q]] = {"shape": [rows, cols], "bytes": bytes_, "us": round(ms * 1e3, 2),
                                  "gbs": round(bytes_ / ms / 1e6, 1), "frac": round(bytes_ / ms / 1e6 / hbm, 3)}
         del w, x, y
-    # config 0 single call, L2 flushed between calls
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
-    w0 = torch.randint(0, 256, (ctx.packed_bytes(S.Q4_K, 512, 2048),), dtype=torch.uint8, device="cuda")
-    x0 = torch.randn(2048, device="cuda")
-    y0 = torch.empty(512, device="cuda")
-    lat = []
-    torch.cuda.synchronize()
-    for i in range(25):
-        with torch.cuda.stream(stream):
-            flush.fill_(i & 255)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        ctx.matvec(S.Q4_K, w0.data_ptr(), x0.data_ptr(), y0.data_ptr(), 512, 2048)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        if i >= 5:
-            lat.append(e0.elapsed_time(e1) * 1e3)
-    out["c0_q4k_512x2048_latency_us"] = round(float(np.median(lat)), 2)
     return out
 
 
@@ -578,9 +756,16 @@ def bf16_peak():
     return 1590.0, "fallback (burst)"
 
 
-def report(args, world, head):
-    hbm, hbm_kind = peaks()
+def c3_config():
+    """config of the headline line (identical in both arms)."""
+    return {"workload": "config 3: prefill MoE FFN layer, 4096 tokens", "tokens": T3, "hidden": HIDDEN,
+            "experts": NE, "top_k": TOPK, "inter": INTER, "gate_up": "Q4_K", "down": "Q6_K",
+            "router_bias": "N(0,0.5) per expert"}
+
+
+def report(args, world, head, cpu):
     tflops_peak, tf_kind = bf16_peak()
+    hbm, hbm_kind = peaks()
     K = args.steps
     ms = head["ms"]
     value = T3 * K / (ms / 1e3)
@@ -591,22 +776,13 @@ def report(args, world, head):
     achieved = flops / (dom_ms / 1e3) / 1e12
     launches = sum(c for _, c in prof.values())
     shard_weight_bytes = NE // world * (2 * Q4K_BYTES_EXPERT + Q6K_BYTES_EXPERT)
-    cpu = None
-    if args.cpu_baseline and world == 1:
-        gate, up, down, lg, x = head["cpu_data"]
-        rate, units, dt = cpu_reference_rate(gate, up, down, lg, x, budget_s=12.0, threads=1)
-        cpu = {"value": round(rate, 3), "unit": "tokens/s", "cores": 1, "kind": "reference",
-               "sample": f"{units} (token, expert) units = {units / TOPK:.1f} of config 3's tokens through qw6's own "
-                         f"qw6_cpu_moe_route / qw6_tensor_matvec / qw6_silu (oracle/_ref), 1 thread, {dt:.1f} s"}
     return {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": K,
         "warmup": args.warmup, "ms_per_step": round(ms / K, 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16 (tcgen05 kind::f16, f32 accumulate; Q4_K/Q6_K weights)",
         "data": "synthetic (seeded GGUF blocks, config 3)",
-        "config": {"workload": "config 3: prefill MoE FFN layer, 4096 tokens", "tokens": T3, "hidden": HIDDEN,
-                   "experts": NE, "top_k": TOPK, "inter": INTER, "gate_up": "Q4_K", "down": "Q6_K",
-                   "router_bias": "N(0,0.5) per expert",
-                   "parallelism": f"ep{world}: {NE // world} experts and {T3 // world} tokens per GPU"
+        "config": c3_config(),
+        "method": {"parallelism": f"ep{world}: {NE // world} experts and {T3 // world} tokens per GPU"
                                   + (", dispatch/combine by this library's kernels over NVLink peer memory, "
                                      "experts placed by balance_experts on the routing counts of an independent "
                                      "calibration batch (same router bias, fresh token noise)"
@@ -636,63 +812,47 @@ def report(args, world, head):
 # --------------------------------------------------------- reference arm --
 
 def run_reference(args, rank, world):
+    """qw6's own CPU implementation of config 3's layer (oracle/_ref) on all
+    usable host cores: each step runs a bounded sample of the 4096 tokens,
+    sliced one token per task over a fork pool (qw6 is single-threaded).  The
+    whole --steps/--warmup run is sized to end within a few minutes."""
     if rank != 0:
         return None
+    from oracle.oracle import cpu_count
     from qw6_b200 import synth as S
     gate, up, down, lg, xb = S.config3()
-    lgs, xs = lg[:256], S.bf16_to_f32(xb[:256])
-    from oracle.oracle import Reference, cpu_count
-    threads = cpu_count()
-    # each step: `threads` (token, expert) units in parallel; bound the run to a few minutes
-    from concurrent.futures import ThreadPoolExecutor
-    ref = Reference()
-    routes = [ref.moe_route(lgs[t], TOPK) for t in range(lgs.shape[0])]
-
-    def unit(u):
-        t, k = divmod(u, TOPK)
-        t %= lgs.shape[0]
-        e = int(routes[t][0][k])
-        g = ref.matvec(4, gate[e], xs[t], INTER, HIDDEN)
-        uu = ref.matvec(4, up[e], xs[t], INTER, HIDDEN)
-        mid = np.array([ref.silu(float(v)) for v in g], np.float32) * uu
-        return np.float32(routes[t][1][k]) * ref.matvec(7, down[e], mid.astype(np.float32), HIDDEN, INTER)
-
+    x = S.bf16_to_f32(xb)
+    workers = cpu_count()
+    one = CpuMoE(gate, up, down, lg, x, 1)
+    one.run(1)
+    t1 = one.run(2) / 2  # seconds per token on one core
     K, W = args.steps, args.warmup
-    with ThreadPoolExecutor(max_workers=threads) as ex:
-        t_unit0 = time.perf_counter()
-        list(ex.map(unit, range(threads)))
-        t_unit = time.perf_counter() - t_unit0
-        per_step = threads
-        budget = 180.0
-        if (K + W) * t_unit > budget:  # shrink the per-step sample to stay within a few minutes
-            per_step = max(1, int(threads * budget / ((K + W) * t_unit)))
-        done = 0
-        for _ in range(W):
-            list(ex.map(unit, range(done, done + per_step)))
-            done += per_step
-        t0 = time.perf_counter()
-        for _ in range(K):
-            list(ex.map(unit, range(done, done + per_step)))
-            done += per_step
-        dt = time.perf_counter() - t0
-    value = K * per_step / TOPK / dt
-    line = {
+    per_step_s = min(6.0, 150.0 / (K + W))
+    per_step = workers * max(1, int(per_step_s / t1))
+    pool = CpuMoE(gate, up, down, lg, x, workers)
+    for _ in range(W):
+        pool.run(per_step)
+    dt = 0.0
+    for _ in range(K):
+        dt += pool.run(per_step)
+    pool.close()
+    value = K * per_step / dt
+    return {
         "metric": METRIC, "value": round(value, 3), "unit": "tokens/s", "n_gpus": world, "steps": K,
         "warmup": W, "ms_per_step": round(dt / K * 1e3, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded GGUF blocks, config 3)",
-        "config": {"workload": "config 3: prefill MoE FFN layer, 4096 tokens", "tokens": T3, "hidden": HIDDEN,
-                   "experts": NE, "top_k": TOPK, "inter": INTER, "gate_up": "Q4_K", "down": "Q6_K",
-                   "router_bias": "N(0,0.5) per expert"},
+        "config": c3_config(),
         "impl": "reference",
-        "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads, "kind": "reference",
-                         "sample": f"{per_step} (token, expert) units per step of config 3's first 256 tokens on "
-                                   f"{threads} threads through qw6's own CPU code (oracle/_ref: qw6_cpu_moe_route, "
-                                   "qw6_tensor_matvec, qw6_silu; the reference has no batched path, so tokens are "
-                                   "looped as qw6_prefill does); the reference's Vulkan path is unavailable on "
-                                   "this box"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": workers, "kind": "reference",
+                         "sample": f"{per_step} of config 3's tokens per step (round robin over the 4096) on a fork "
+                                   f"pool of {workers} processes, one token per task, each token through qw6's own "
+                                   "qw6_cpu_moe_route and expert loop (qw6_tensor_matvec, qw6_silu; "
+                                   "qw6.c:2246-2264) compiled from the reference sources (oracle/_ref); the "
+                                   "reference has no batched path and is single-threaded, so the pool is the "
+                                   "harness's; its Vulkan path is unavailable on this box",
+                         "host": host_info()},
         "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    return line
 
 
 def main():
