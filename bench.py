@@ -683,33 +683,25 @@ def matvec_sweep(torch, ctx, stream):
 
 def lm_head_bench(torch, ctx, stream, rank, world, dist):
     """Config 4's Q6_K LM head [248320 x 2048] with fused argmax, row-sharded
-    over the ranks (rank r holds rows [r*V/N, (r+1)*V/N)); the shards' 8-byte
-    (logit, index) keys are all-gathered with NCCL and reduced on every rank.
-    Returns per-token latency and tokens/s for batch 1 and batch 32."""
+    over the ranks (qw6_b200.lm_head: rank r holds shard_rows(V, N, r)); the
+    shards' 8-byte (logit, index) keys are all-gathered with NCCL and reduced
+    on every rank.  Returns per-token latency and tokens/s for batch 1 and 32."""
     from qw6_b200 import synth as S
+    from qw6_b200.lm_head import CudaLMHeadShard, shard_rows, sharded_argmax
     hbm, _ = peaks()
     V, H = S.VOCAB, HIDDEN
-    r0 = (V * rank // world) // 16 * 16
-    r1 = V if rank == world - 1 else (V * (rank + 1) // world) // 16 * 16
+    r0, r1 = shard_rows(V, world, rank)
     rows = r1 - r0
     pb = ctx.packed_bytes(S.Q6_K, rows, H)
     w = torch.randint(0, 256, (pb,), dtype=torch.uint8, device="cuda")
+    shard = CudaLMHeadShard(ctx, S.Q6_K, w.data_ptr(), rows, H, r0)
     res = {}
     for ntok in (1, 32):
         x = torch.randn((ntok, H), device="cuda")
-        keys = torch.zeros((ntok,), dtype=torch.int64, device="cuda")
-        allk = torch.zeros((world, ntok), dtype=torch.int64, device="cuda")
-        idx = torch.empty(ntok, dtype=torch.int32, device="cuda")
-        val = torch.empty(ntok, dtype=torch.float32, device="cuda")
 
         def one():
-            ctx.lm_head_argmax(S.Q6_K, w.data_ptr(), x.data_ptr(), ntok, rows, H, r0, keys.data_ptr())
-            if world > 1:
-                with torch.cuda.stream(stream):
-                    dist.all_gather_into_tensor(allk.view(-1), keys)
-                ctx.argmax_keys_reduce(allk.data_ptr(), world, ntok, idx.data_ptr(), val.data_ptr())
-            else:
-                ctx.argmax_keys_reduce(keys.data_ptr(), 1, ntok, idx.data_ptr(), val.data_ptr())
+            with torch.cuda.stream(stream):
+                sharded_argmax(shard, x, world)
 
         for _ in range(3):
             one()
@@ -731,6 +723,7 @@ def lm_head_bench(torch, ctx, stream, rank, world, dist):
         res[f"b{ntok}"] = {"us_per_call": round(ms * 1e3, 2), "tokens_s": round(ntok / (ms / 1e3), 1),
                            "shard_rows": rows, "shard_gbs": round(shard_bytes / ms / 1e6, 1),
                            "shard_frac": round(shard_bytes / ms / 1e6 / hbm, 3)}
+    ctx.set_stream(stream.cuda_stream)
     res["shards"] = world
     res["collective"] = "NCCL all_gather of 8-byte keys" if world > 1 else None
     del w
