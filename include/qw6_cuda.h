@@ -133,7 +133,7 @@ typedef struct {
  * up_e x_t), composed as qw6_apply_layer_moe (qw6.c:2246-2264) without the
  * shared expert.  gate/up are [inter x hidden], down [hidden x inter];
  * gate and up must share one quant type.  ntok * top_k <= 4096; hidden and
- * inter multiples of 512, hidden <= 4096; n_experts <= 256.  Routing,
+ * inter multiples of 256 (512 when ntok > 4), hidden <= 4096; n_experts <= 256.  Routing,
  * grouping and the expert matvecs all run on the device (no host sync).
  * Uses the context workspace (grown on first use, which synchronizes). */
 int qw6cu_moe_decode(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
@@ -147,26 +147,62 @@ int qw6cu_moe_decode_hostio(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const
                             uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t n_experts, uint32_t top_k);
 
 /* Allocation-free qw6cu_moe_decode, for callers that cannot allocate device
- * memory when they run the layer: code inside a CUDA stream capture, where a
- * cudaMalloc would invalidate the capture, or a runtime that hands out all
- * device memory from its own pool.  It has no counterpart in the reference.
- * Scratch is a fixed 1 MiB array in device memory that the library owns
- * (every GPU that loads the library holds it until the process exits), so
- * shapes whose workspace (qw6cu_moe_workspace_bytes) exceeds 1 MiB are
- * rejected with QW6CU_ERR_ARG -- for hidden 2048, inter 512, 256 experts,
- * top-8 that is ntok > 12.  Inputs, outputs and weights are device pointers
- * owned by the caller; work is enqueued on `stream` (a cudaStream_t, NULL =
- * the legacy default stream) on the calling thread's current device.  The
- * first call on a device looks up the array's device address (no allocation);
- * make that first call before any stream capture.  Every call shares the
- * array and leaves its contents behind; nothing in it needs to start at zero
- * because each call writes every scratch byte it later reads.  Calls that can
- * overlap on the GPU (different streams, or graphs replayed concurrently)
- * race on the array and must be serialized by the caller. */
+ * memory at the point where they run the layer: a runtime or serving process
+ * that hands out all device memory from its own pool, or one whose
+ * device-memory footprint must stay fixed after start-up (an allocation there
+ * can fail, or stall on device-wide synchronisation, at a point where neither
+ * is acceptable).  It has no counterpart in the reference.  Scratch is a fixed
+ * 1 MiB array in device memory that the library owns (every GPU that loads
+ * the library holds it until the process exits), so shapes whose workspace
+ * (qw6cu_moe_workspace_bytes) exceeds 1 MiB are rejected with QW6CU_ERR_ARG
+ * -- for hidden 2048, inter 512, 256 experts, top-8 that is ntok > 12.
+ * Inputs, outputs and weights are device pointers owned by the caller; work is
+ * enqueued on `stream` (a cudaStream_t, NULL = the legacy default stream) on
+ * the calling thread's current device.  The first call on a device does a
+ * one-time set-up there: it looks up the array's device address
+ * (cudaGetSymbolAddress) and configures and loads every kernel this entry
+ * point can launch; make that first call before any stream capture.  Every
+ * call shares the array and leaves its contents behind; nothing in it needs
+ * to start at zero because each call writes every scratch byte it later
+ * reads.  Calls that can overlap on the GPU (different streams, or graphs
+ * replayed concurrently) race on the array and must be serialized by the
+ * caller. */
 int qw6cu_moe_decode_noalloc(const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
                              const qw6cu_expert_pack *down, const float *logits, const float *x, float *out,
                              uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t n_experts, uint32_t top_k,
                              void *stream);
+
+/* ---- the MoE FFN block (decode batches) ---- */
+
+/* The shared expert of a MoE layer: gate/up [inter x hidden] and down
+ * [hidden x inter], each in the packed tile layout of its quant type
+ * (qw6cu_pack) or FP16/BF16 row-major; router: fp32 [hidden] (its sigmoid
+ * weighs the shared expert) or NULL (weight 1), as qw6.c:2266-2285. */
+typedef struct {
+    uint32_t gate_quant, up_quant, down_quant;
+    const void *gate, *up, *down;
+    uint32_t inter;
+    const float *router;
+} qw6cu_shared_expert;
+
+/* One MoE FFN block for ntok token rows, as qw6's forward pass applies it
+ * to every layer (qw6.c:2474-2484 around qw6_apply_layer_moe,
+ * qw6.c:2226-2290):
+ *   normed = rmsnorm(x) * norm_w (eps 1e-6), logits = router . normed,
+ *   ffn = routed experts (qw6cu_moe_decode on normed and logits)
+ *         + s * shared_down(silu(shared_gate normed) * shared_up normed),
+ *   out = x + ffn.
+ * router: fp32 [n_experts x hidden] row-major, 16-byte aligned; norm_w fp32
+ * [hidden]; shared: NULL for none.  x, out: fp32 [ntok x hidden]; all device
+ * pointers, enqueued on the context's stream with no host synchronization
+ * (the context workspace is grown on first use, which synchronizes).  The
+ * router logits are computed in fp32 like qw6's, but with a different
+ * summation order, so a token whose k-th and (k+1)-th logits differ by
+ * rounding only may select a different expert than the CPU. */
+int qw6cu_moe_block(qw6cu_ctx *ctx, const float *x, const float *norm_w, const float *router,
+                    const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up, const qw6cu_expert_pack *down,
+                    const qw6cu_shared_expert *shared, float *out, uint32_t ntok, uint32_t hidden, uint32_t inter,
+                    uint32_t n_experts, uint32_t top_k);
 
 /* Device workspace qw6cu_moe_decode needs for these dimensions. */
 size_t qw6cu_moe_workspace_bytes(uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t n_experts,
@@ -284,7 +320,7 @@ void qw6cu_ep_destroy(qw6cu_ep *ep);
  * begin: allocate events for up to max_launches launches and start
  * recording; end: synchronize, then write per-kernel-id total milliseconds
  * and launch counts into arrays of QW6CU_NKERNELS entries and stop. */
-#define QW6CU_NKERNELS 19
+#define QW6CU_NKERNELS 20
 int qw6cu_profile_begin(qw6cu_ctx *ctx, uint32_t max_launches);
 int qw6cu_profile_end(qw6cu_ctx *ctx, double *ms_total, uint32_t *launches);
 const char *qw6cu_kernel_name(int kernel_id);

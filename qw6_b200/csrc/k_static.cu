@@ -16,17 +16,22 @@
 static __device__ __align__(256) unsigned char g_qw6_static_scratch[QW6K_STATIC_SCRATCH_BYTES];
 
 // One slot per device ordinal.  The address is published with release order
-// after cudaGetSymbolAddress returned it and read with acquire order, so a
-// thread that sees a non-null slot also sees the address itself; two threads
-// racing on a device's first call both look it up and store the same value.
+// after the device's set-up succeeded and read with acquire order, so a
+// thread that sees a non-null slot also sees a finished set-up; two threads
+// racing on a device's first call both do the set-up (it is idempotent) and
+// store the same value.
 static std::atomic<void*> g_scratch_addr[QW6K_MAX_DEVICES];
 
+// First call on a device: the array's device address, and every decode
+// kernel configured and loaded (qw6k_moe_decode_setup), so that later calls
+// only enqueue launches.
 extern "C" int qw6k_static_scratch(void** ptr, size_t* bytes) {
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= QW6K_MAX_DEVICES) return QW6K_ERR_CUDA;
     void* p = g_scratch_addr[dev].load(std::memory_order_acquire);
     if (!p) {
         if (cudaGetSymbolAddress(&p, g_qw6_static_scratch) != cudaSuccess || !p) return QW6K_ERR_CUDA;
+        if (qw6k_moe_decode_setup() != 0) return QW6K_ERR_CUDA;
         g_scratch_addr[dev].store(p, std::memory_order_release);
     }
     *ptr = p;

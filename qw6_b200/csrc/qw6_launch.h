@@ -116,6 +116,17 @@ int qw6k_moe_check(const qw6k_moe_desc *d);
 int qw6k_moe_nphases(const qw6k_moe_desc *d);
 int qw6k_moe_phase_kind(const qw6k_moe_desc *d, int phase); /* 0 plan, 1 gate/up, 2 down, 3 combine */
 int qw6k_moe_phase(const qw6k_moe_desc *d, int phase, cudaStream_t st);
+/* Configure and load every decode kernel on the current device. */
+int qw6k_moe_decode_setup(void);
+
+/* MoE FFN block (k_block.cu).  pre: normed = rmsnorm(x) * norm_w, logits =
+ * router . normed (fp32 router [ne x hidden]), sgate[t] = sigmoid(srouter .
+ * normed) or 1 when srouter is NULL.  post: out = x + (ffn + sgate * shared)
+ * (shared nullable). */
+int qw6k_block_pre(const float *x, const float *norm_w, const float *router, const float *srouter, float *normed,
+                   float *logits, float *sgate, uint32_t ntok, uint32_t hidden, uint32_t ne, cudaStream_t st);
+int qw6k_block_post(const float *x, const float *ffn, const float *shared, const float *sgate, float *out,
+                    uint32_t ntok, uint32_t hidden, cudaStream_t st);
 
 /* Routed MoE FFN for prefill batches on tcgen05 (k_prefill.cu): desc->x is
  * bf16 [ntok x hidden]; gate/up/down Q4_K or Q6_K packed; hidden, inter
@@ -179,7 +190,8 @@ int qw6k_ep_p2p_phase(const qw6k_ep_desc *d, int phase, cudaStream_t st);
 
 /* Fixed 1 MiB device scratch (k_static.cu) of the allocation-free MoE entry
  * point; *ptr is its device address on the current device (looked up with
- * cudaGetSymbolAddress on the first call per device). */
+ * cudaGetSymbolAddress on the first call per device, which also configures
+ * every decode kernel there). */
 #define QW6K_STATIC_SCRATCH_BYTES (1u << 20)
 #define QW6K_MAX_DEVICES 64
 int qw6k_static_scratch(void **ptr, size_t *bytes);

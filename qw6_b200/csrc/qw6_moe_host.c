@@ -119,7 +119,8 @@ int qw6cu_moe_decode_noalloc(const qw6cu_expert_pack *gate, const qw6cu_expert_p
     void *scratch = NULL;
     size_t cap = 0;
     if (qw6k_static_scratch(&scratch, &cap)) {
-        qw6h_set_err("qw6cu_moe_decode_noalloc: cudaGetSymbolAddress of the fixed scratch failed");
+        qw6h_set_err("qw6cu_moe_decode_noalloc: first-call set-up on this device failed (cudaGetSymbolAddress of "
+                     "the fixed scratch, or configuring the decode kernels)");
         return QW6CU_ERR_CUDA;
     }
     qw6k_moe_desc d;
@@ -287,5 +288,72 @@ int qw6cu_ep_combine(qw6cu_ctx *ctx, const void *ret_bf16, const float *w, const
     const int rec = qw6h_prof_a(ctx, QW6H_K_EP);
     rc = qw6h_rc(qw6k_ep_combine(ret_bf16, w, send_pos, ntok, top_k, hidden, out, ctx->st), "ep_combine");
     qw6h_prof_b(ctx, rec);
+    return rc;
+}
+
+/* ------------------------------------------------------ MoE FFN block -- */
+
+static size_t al256h(size_t n) { return (n + 255) & ~(size_t)255; }
+
+/* y[t] = W . x[t] for ntok tokens in chunks of the matvec's 32 */
+static int block_matvec(qw6cu_ctx *ctx, uint32_t quant, const void *w, const float *x, float *y, uint32_t rows,
+                        uint32_t cols, uint32_t ntok) {
+    int rc = 0;
+    for (uint32_t t0 = 0; t0 < ntok && !rc; t0 += 32) {
+        const uint32_t n = ntok - t0 < 32 ? ntok - t0 : 32;
+        const int rec = qw6h_prof_a(ctx, QW6H_K_MATVEC);
+        rc = qw6h_rc(qw6k_matvec(quant, w, x + (size_t)t0 * cols, y + (size_t)t0 * rows, rows, cols, n, cols, rows,
+                                 ctx->st),
+                     "moe_block shared expert");
+        qw6h_prof_b(ctx, rec);
+    }
+    return rc;
+}
+
+int qw6cu_moe_block(qw6cu_ctx *ctx, const float *x, const float *norm_w, const float *router,
+                    const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up, const qw6cu_expert_pack *down,
+                    const qw6cu_shared_expert *shared, float *out, uint32_t ntok, uint32_t hidden, uint32_t inter,
+                    uint32_t n_experts, uint32_t top_k) {
+    int rc = qw6h_use(ctx);
+    if (rc) return rc;
+    if (!x || !norm_w || !router || !out || !ntok || !hidden || !n_experts || n_experts > 256 ||
+        (shared && (!shared->gate || !shared->up || !shared->down || !shared->inter))) {
+        qw6h_set_err("qw6cu_moe_block: invalid arguments");
+        return QW6CU_ERR_ARG;
+    }
+    const uint32_t si = shared ? shared->inter : 0;
+    const size_t o_norm = 0, o_log = o_norm + al256h((size_t)ntok * hidden * 4),
+                 o_sg = o_log + al256h((size_t)ntok * n_experts * 4), o_ffn = o_sg + al256h((size_t)ntok * 4),
+                 o_g = o_ffn + al256h((size_t)ntok * hidden * 4), o_u = o_g + al256h((size_t)ntok * si * 4),
+                 o_m = o_u + al256h((size_t)ntok * si * 4), o_sh = o_m + al256h((size_t)ntok * si * 4),
+                 total = o_sh + (shared ? al256h((size_t)ntok * hidden * 4) : 0);
+    uint8_t *b = qw6h_buf(ctx, QW6H_BUF_BLOCK, total);
+    if (!b) return QW6CU_ERR_NOMEM;
+    float *normed = (float *)(b + o_norm), *logits = (float *)(b + o_log), *sg = (float *)(b + o_sg);
+    float *ffn = (float *)(b + o_ffn), *g = (float *)(b + o_g), *u = (float *)(b + o_u), *m = (float *)(b + o_m);
+    float *sh = shared ? (float *)(b + o_sh) : NULL;
+    qw6k_moe_desc d;
+    memset(&d, 0, sizeof d);
+    if ((rc = moe_desc(ctx, gate, up, down, ntok, hidden, inter, n_experts, top_k, &d))) return rc;
+    d.logits = logits;
+    d.x = normed;
+    d.out = ffn;
+    int rec = qw6h_prof_a(ctx, QW6H_K_MOE_BLOCK);
+    rc = qw6h_rc(qw6k_block_pre(x, norm_w, router, shared ? shared->router : NULL, normed, logits, sg, ntok, hidden,
+                                n_experts, ctx->st),
+                 "moe_block");
+    qw6h_prof_b(ctx, rec);
+    if (!rc) rc = moe_run(ctx, &d);
+    if (!rc && shared) {
+        rc = block_matvec(ctx, shared->gate_quant, shared->gate, normed, g, si, hidden, ntok);
+        if (!rc) rc = block_matvec(ctx, shared->up_quant, shared->up, normed, u, si, hidden, ntok);
+        if (!rc) rc = qw6h_rc(qw6k_silu_mul(g, u, m, ntok * si, ctx->st), "moe_block shared expert");
+        if (!rc) rc = block_matvec(ctx, shared->down_quant, shared->down, m, sh, hidden, si, ntok);
+    }
+    if (!rc) {
+        rec = qw6h_prof_a(ctx, QW6H_K_MOE_BLOCK);
+        rc = qw6h_rc(qw6k_block_post(x, ffn, sh, sg, out, ntok, hidden, ctx->st), "moe_block");
+        qw6h_prof_b(ctx, rec);
+    }
     return rc;
 }

@@ -1,11 +1,12 @@
 """GPU: the allocation-free MoE entry point (qw6cu_moe_decode_noalloc).
 
-Some callers cannot call cudaMalloc at the point where they run the MoE layer
-(for example a runtime that owns all device memory through its own pool, or
-code running while a CUDA graph is being captured, where an allocation would
-break the capture). For them the library keeps a fixed 1 MiB scratch array in
-device memory and this entry point works only out of that array, plus the
-caller's own inputs and outputs.
+Some callers cannot call cudaMalloc at the point where they run the MoE layer:
+a runtime or serving process that hands out all device memory from its own
+pool, or one whose device-memory footprint must stay fixed after start-up (an
+allocation there can fail, or stall on device-wide synchronisation, at a
+point where neither is acceptable). For them the library keeps a fixed 1 MiB
+scratch array in device memory and this entry point works only out of that
+array, plus the caller's own inputs and outputs.
 
 The test checks it through the C ABI against qw6cu_moe_decode (the entry point
 that uses the context's workspace) on two calls in a row, which also covers
@@ -34,11 +35,15 @@ def _packs(cuda, rng, E, H, I):
                   L.ExpertPack(S.Q6_K, pd.data_ptr(), sd))
 
 
-@pytest.mark.parametrize("ntok", [1, 4, 8])
-def test_noalloc_matches_workspace_entry_point(ntok):
+@pytest.mark.parametrize("ntok,E", [(1, 32), (4, 32), (8, 32), (12, 256)])
+def test_noalloc_matches_workspace_entry_point(ntok, E):
+    """ntok 1 and 4 take the two-kernel small-batch path, 8 and 12 the planned
+    path; 12 tokens over 256 experts is the largest batch whose workspace
+    fits the fixed scratch."""
     torch = pytest.importorskip("torch")
     rng = np.random.Generator(np.random.PCG64(99 + ntok))
-    E, H, I, K = 32, 2048, 512, 8
+    H, I, K = 2048, 512, 8
+    assert L.Context.moe_workspace_bytes(ntok, H, I, E, K) <= 1 << 20
     ctx = L.Context(0)
     keep, (g, u, d) = _packs(ctx, rng, E, H, I)
     logits = dev(rng.standard_normal((ntok, E), dtype=np.float32))
