@@ -4,24 +4,27 @@
 //   route -> for each selected expert e (selection order):
 //   g = Wg[e].x, u = Wu[e].x, mid = silu(g)*u, t = Wd[e].mid, out += w_e*t.
 // The Vulkan pipeline runs this as a host readback of the routing plus 5
-// synchronous dispatches per expert (qw6_vk.c:3357-3407).  Here it is four
-// kernels with no host round trip:
-//   plan    route every token, group the (token, slot) assignments by
-//           expert (deterministic counting sort) and cut each expert's list
-//           into work items of <= 4*NQ tokens;
-//   gateup  per (work item, 16-row tile): gate and up tiles of the expert,
-//           int8 tensor-core matvec over the item's tokens, silu(g)*u;
-//   down    per (work item, 16-row tile of hidden): Wd[e] . mid;
-//   combine out[t] = sum_k w[t,k] * down[t,k] in slot order (fp32, rounded
-//           like the CPU loop).
-// Each expert's weights are read once per work item, i.e. once per layer
-// when an expert has <= 4*NQ tokens.
+// synchronous dispatches per expert (qw6_vk.c:3357-3407).  Here there is no
+// host round trip and every expert's weights are read once per layer (once
+// per work item of <= 4*NQ tokens when an expert has more):
+//   ntok <= 4   two launches: self-routed gate/up + silu (k_moe_small_gu),
+//               then down with the slot-order combine (k_moe_small_down,
+//               programmatic dependent launch: it routes and prefetches its
+//               weights while gate/up runs);
+//   ntok > 4    four launches: plan (route every token, group the (token,
+//               slot) assignments by expert with a stable counting sort, cut
+//               each expert's list into work items), gate/up per item,
+//               down per item, slot-order combine (k_moe_plan, k_moe_gateup,
+//               k_moe_down, k_moe_combine).
+// Weight tile-blocks go straight from HBM into registers (16-byte coalesced
+// loads of the packed layout, qw6_dev.cuh) and are multiplied with int8 MMAs.
 #include <cuda_runtime.h>
 
 #include "qw6_dev.cuh"
 #include "qw6_devcfg.cuh"
 #include "qw6_grids.cuh"
 #include "qw6_launch.h"
+#include "qw6_pdl.cuh"
 #include "qw6_route.cuh"
 
 namespace qw6 {
@@ -35,7 +38,6 @@ struct MoeArgs {
     const float* x;
     float* out;
     int ntok, hidden, inter, ne, topk, chunk;
-    int ks_gu, ks_dn;  // k-splits of the gate/up (K = hidden) and down (K = inter) tiles
     // workspace
     int32_t* idx;
     float* w;
@@ -49,6 +51,9 @@ struct MoeArgs {
 // ------------------------------------------------------------------ plan --
 __global__ void __launch_bounds__(512) k_moe_plan(const MoeArgs a) {
     __shared__ int cnt[256], off[257], ich[257];
+    __shared__ int sidx[4096];  // the routed expert of every assignment (ntok * topk <= 4096)
+    pdl_wait();  // logits and the workspace are free to use
+    pdl_trigger();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
     const int TK = a.ntok * a.topk;
     for (int t = warp; t < a.ntok; t += nw)
@@ -56,7 +61,11 @@ __global__ void __launch_bounds__(512) k_moe_plan(const MoeArgs a) {
                     lane);
     for (int e = tid; e < 256; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
-    for (int i = tid; i < TK; i += blockDim.x) atomicAdd(&cnt[a.idx[i]], 1);
+    for (int i = tid; i < TK; i += blockDim.x) {
+        const int e = a.idx[i];
+        sidx[i] = e;
+        atomicAdd(&cnt[e], 1);
+    }
     __syncthreads();
     // exclusive scans of the per-expert counts and chunk counts: each of the
     // first 8 warps scans 32 experts with shuffles, then the warp totals
@@ -84,9 +93,9 @@ __global__ void __launch_bounds__(512) k_moe_plan(const MoeArgs a) {
     __syncthreads();
     // stable counting sort: rank = earlier assignments with the same expert
     for (int i = tid; i < TK; i += blockDim.x) {
-        const int e = a.idx[i];
+        const int e = sidx[i];
         int r = 0;
-        for (int j = 0; j < i; j++) r += a.idx[j] == e;
+        for (int j = 0; j < i; j++) r += sidx[j] == e;
         a.order[off[e] + r] = i;
     }
     for (int e = tid; e < a.ne; e += blockDim.x) {
@@ -102,159 +111,6 @@ template <int F>
 __host__ __device__ constexpr size_t tbl_bytes_of() {
     return IQLut<F>::bytes;
 }
-
-// ---------------------------------------------------------------- gateup --
-template <int F, int NQ>
-__global__ void __launch_bounds__(kThreads) k_moe_gateup(const MoeArgs a) {
-    extern __shared__ __align__(16) uint8_t smem[];
-    using T = Tile<F, NQ>;
-    constexpr int TB = T::TB;
-    const int ks = a.ks_gu, mpc = kWarps / ks;
-    const int mgroups = (a.inter / 16) / mpc;
-    const int item = blockIdx.x / mgroups, mg = blockIdx.x % mgroups;
-    if (item >= *a.nitems) return;
-    const int4 it = a.items[item];
-    const int e = it.x, cnt = it.z;
-    const int32_t* sel = a.order + it.y;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int ms = warp / ks, split = warp % ks, mt = mg * mpc + ms, nbh = a.hidden / 256, b0 = split * 2;
-
-    const uint8_t* gb = a.gate + (size_t)e * a.gstride + ((size_t)mt * nbh + b0) * TB;
-    const uint8_t* ub = a.up + (size_t)e * a.ustride + ((size_t)mt * nbh + b0) * TB;
-    typename T::Frag g0, g1, u0, u1;
-    T::load(g0, gb, lane);
-    T::load(g1, gb + TB, lane);
-    T::load(u0, ub, lane);
-    T::load(u1, ub + TB, lane);
-
-    uint32_t* tbl = reinterpret_cast<uint32_t*>(smem);
-    XStage xs = xstage_carve(smem + tbl_bytes_of<F>(), 4 * NQ, a.hidden);
-    float* red = reinterpret_cast<float*>(smem + tbl_bytes_of<F>() + xstage_bytes(4 * NQ, a.hidden));
-    if constexpr (IsIQ<F>::value) IQLut<F>::init(tbl, grid_ptr<F>());
-    xstage_fill(xs, a.x, a.hidden, cnt, 4 * NQ, a.hidden, sel, a.topk);
-    __syncthreads();
-    const XView xv = xs.view();
-
-    float ag[2][NQ], au[2][NQ];
-#pragma unroll
-    for (int q = 0; q < NQ; q++) ag[0][q] = ag[1][q] = au[0][q] = au[1][q] = 0.f;
-    tile_dot<F, NQ>(g0, xv, b0, ag, lane, tbl);
-    tile_dot<F, NQ>(g1, xv, b0 + 1, ag, lane, tbl);
-    tile_dot<F, NQ>(u0, xv, b0, au, lane, tbl);
-    tile_dot<F, NQ>(u1, xv, b0 + 1, au, lane, tbl);
-
-    if (ks > 1) {
-        float* r = red + (warp * 32 + lane) * 4 * NQ;
-#pragma unroll
-        for (int q = 0; q < NQ; q++) {
-            r[4 * q + 0] = ag[0][q];
-            r[4 * q + 1] = ag[1][q];
-            r[4 * q + 2] = au[0][q];
-            r[4 * q + 3] = au[1][q];
-        }
-        __syncthreads();
-        if (split == 0) {
-#pragma unroll
-            for (int q = 0; q < NQ; q++) {
-                float s[4] = {0.f, 0.f, 0.f, 0.f};
-                for (int p = 0; p < ks; p++) {
-                    const float* rp = red + ((warp + p) * 32 + lane) * 4 * NQ + 4 * q;
-                    s[0] += rp[0];
-                    s[1] += rp[1];
-                    s[2] += rp[2];
-                    s[3] += rp[3];
-                }
-                ag[0][q] = s[0];
-                ag[1][q] = s[1];
-                au[0][q] = s[2];
-                au[1][q] = s[3];
-            }
-        }
-    }
-    if (split == 0) {
-        const int g = lane >> 2, t = lane & 3;
-#pragma unroll
-        for (int q = 0; q < NQ; q++) {
-            const int j = 4 * q + t;
-            if (j < cnt) {
-                float* m = a.mid + (size_t)sel[j] * a.inter + mt * 16 + g;
-                m[0] = __fmul_rn(silu_exact(ag[0][q]), au[0][q]);
-                m[8] = __fmul_rn(silu_exact(ag[1][q]), au[1][q]);
-            }
-        }
-    }
-}
-
-// ------------------------------------------------------------------ down --
-template <int F, int NQ>
-__global__ void __launch_bounds__(kThreads) k_moe_down(const MoeArgs a) {
-    extern __shared__ __align__(16) uint8_t smem[];
-    using T = Tile<F, NQ>;
-    constexpr int TB = T::TB;
-    const int ks = a.ks_dn, mpc = kWarps / ks;
-    const int mgroups = (a.hidden / 16) / mpc;
-    const int item = blockIdx.x / mgroups, mg = blockIdx.x % mgroups;
-    if (item >= *a.nitems) return;
-    const int4 it = a.items[item];
-    const int e = it.x, cnt = it.z;
-    const int32_t* sel = a.order + it.y;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int ms = warp / ks, split = warp % ks, mt = mg * mpc + ms, nbi = a.inter / 256, b0 = split * 2;
-
-    const uint8_t* db = a.down + (size_t)e * a.dstride + ((size_t)mt * nbi + b0) * TB;
-    typename T::Frag d0, d1;
-    T::load(d0, db, lane);
-    T::load(d1, db + TB, lane);
-
-    uint32_t* tbl = reinterpret_cast<uint32_t*>(smem);
-    XStage xs = xstage_carve(smem + tbl_bytes_of<F>(), 4 * NQ, a.inter);
-    float* red = reinterpret_cast<float*>(smem + tbl_bytes_of<F>() + xstage_bytes(4 * NQ, a.inter));
-    if constexpr (IsIQ<F>::value) IQLut<F>::init(tbl, grid_ptr<F>());
-    xstage_fill(xs, a.mid, a.inter, cnt, 4 * NQ, a.inter, sel, 1);
-    __syncthreads();
-    const XView xv = xs.view();
-
-    float acc[2][NQ];
-#pragma unroll
-    for (int q = 0; q < NQ; q++) acc[0][q] = acc[1][q] = 0.f;
-    tile_dot<F, NQ>(d0, xv, b0, acc, lane, tbl);
-    tile_dot<F, NQ>(d1, xv, b0 + 1, acc, lane, tbl);
-
-    if (ks > 1) {
-        float* r = red + (warp * 32 + lane) * 2 * NQ;
-#pragma unroll
-        for (int q = 0; q < NQ; q++) {
-            r[2 * q] = acc[0][q];
-            r[2 * q + 1] = acc[1][q];
-        }
-        __syncthreads();
-        if (split == 0) {
-#pragma unroll
-            for (int q = 0; q < NQ; q++) {
-                float s0 = 0.f, s1 = 0.f;
-                for (int p = 0; p < ks; p++) {
-                    s0 += red[((warp + p) * 32 + lane) * 2 * NQ + 2 * q];
-                    s1 += red[((warp + p) * 32 + lane) * 2 * NQ + 2 * q + 1];
-                }
-                acc[0][q] = s0;
-                acc[1][q] = s1;
-            }
-        }
-    }
-    if (split == 0) {
-        const int g = lane >> 2, t = lane & 3;
-#pragma unroll
-        for (int q = 0; q < NQ; q++) {
-            const int j = 4 * q + t;
-            if (j < cnt) {
-                float* o = a.dout + (size_t)sel[j] * a.hidden + mt * 16 + g;
-                o[0] = acc[0][q];
-                o[8] = acc[1][q];
-            }
-        }
-    }
-}
-
 
 // ====================================================== small batches ====
 // ntok <= 4: every CTA routes the token(s) itself (no planner launch), lists
@@ -446,6 +302,166 @@ __global__ void __launch_bounds__(kThreads) k_moe_small_down(const MoeArgs a) {
     (void)TK;
 }
 
+// ==================================================== planned batches ====
+// ntok > 4: the planner grouped the assignments by expert into work items
+// (expert, <= 4*NQ of its assignments); gate/up runs per (item, 16-row tile)
+// with one warp per K block (gate and up tile-blocks loaded straight into
+// registers), down per (item, 8/ks 16-row tiles of hidden) with ks warps per
+// tile (two K blocks each), and k_moe_combine sums the slots in order.
+template <int F, int NQ, int NBW>
+__global__ void __launch_bounds__(kThreads) k_moe_gateup(const MoeArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    using T = Tile<F, NQ>;
+    constexpr int TB = T::TB;
+    const int ks = a.hidden / 256 / NBW, mpc = kWarps / ks;
+    const int mgroups = (a.inter / 16) / mpc;
+    const int item = blockIdx.x / mgroups, mg = blockIdx.x % mgroups;
+    if (item >= *a.nitems) return;
+    const int4 it = a.items[item];
+    const int e = it.x, cnt = it.z;
+    const int32_t* sel = a.order + it.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ms = warp / ks, split = warp % ks, mt = mg * mpc + ms, nbh = a.hidden / 256, b0 = split * NBW;
+
+    const uint8_t* gb = a.gate + (size_t)e * a.gstride + ((size_t)mt * nbh + b0) * TB;
+    const uint8_t* ub = a.up + (size_t)e * a.ustride + ((size_t)mt * nbh + b0) * TB;
+    typename T::Frag g[NBW], u[NBW];
+#pragma unroll
+    for (int i = 0; i < NBW; i++) {
+        T::load(g[i], gb + i * TB, lane);
+        T::load(u[i], ub + i * TB, lane);
+    }
+
+    uint32_t* tbl = reinterpret_cast<uint32_t*>(smem);
+    XStage xs = xstage_carve(smem + tbl_bytes_of<F>(), 4 * NQ, a.hidden);
+    float* red = reinterpret_cast<float*>(smem + tbl_bytes_of<F>() + xstage_bytes(4 * NQ, a.hidden));
+    if constexpr (IsIQ<F>::value) IQLut<F>::init(tbl, grid_ptr<F>());
+    xstage_fill(xs, a.x, a.hidden, cnt, 4 * NQ, a.hidden, sel, a.topk);
+    __syncthreads();
+    const XView xv = xs.view();
+
+    float ag[2][NQ], au[2][NQ];
+#pragma unroll
+    for (int q = 0; q < NQ; q++) ag[0][q] = ag[1][q] = au[0][q] = au[1][q] = 0.f;
+#pragma unroll
+    for (int i = 0; i < NBW; i++) {
+        tile_dot<F, NQ>(g[i], xv, b0 + i, ag, lane, tbl);
+        tile_dot<F, NQ>(u[i], xv, b0 + i, au, lane, tbl);
+    }
+
+    if (ks > 1) {
+        float* r = red + (warp * 32 + lane) * 4 * NQ;
+#pragma unroll
+        for (int q = 0; q < NQ; q++) {
+            r[4 * q + 0] = ag[0][q];
+            r[4 * q + 1] = ag[1][q];
+            r[4 * q + 2] = au[0][q];
+            r[4 * q + 3] = au[1][q];
+        }
+        __syncthreads();
+        if (split == 0) {
+#pragma unroll
+            for (int q = 0; q < NQ; q++) {
+                float s[4] = {0.f, 0.f, 0.f, 0.f};
+                for (int p = 0; p < ks; p++) {
+                    const float* rp = red + ((warp + p) * 32 + lane) * 4 * NQ + 4 * q;
+                    s[0] += rp[0];
+                    s[1] += rp[1];
+                    s[2] += rp[2];
+                    s[3] += rp[3];
+                }
+                ag[0][q] = s[0];
+                ag[1][q] = s[1];
+                au[0][q] = s[2];
+                au[1][q] = s[3];
+            }
+        }
+    }
+    if (split == 0) {
+        const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+        for (int q = 0; q < NQ; q++) {
+            const int j = 4 * q + t;
+            if (j < cnt) {
+                float* m = a.mid + (size_t)sel[j] * a.inter + mt * 16 + g;
+                m[0] = __fmul_rn(silu_exact(ag[0][q]), au[0][q]);
+                m[8] = __fmul_rn(silu_exact(ag[1][q]), au[1][q]);
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------ down --
+template <int F, int NQ>
+__global__ void __launch_bounds__(kThreads) k_moe_down(const MoeArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    using T = Tile<F, NQ>;
+    constexpr int TB = T::TB;
+    const int ks = a.inter / 512, mpc = kWarps / ks;
+    const int mgroups = (a.hidden / 16) / mpc;
+    const int item = blockIdx.x / mgroups, mg = blockIdx.x % mgroups;
+    if (item >= *a.nitems) return;
+    const int4 it = a.items[item];
+    const int e = it.x, cnt = it.z;
+    const int32_t* sel = a.order + it.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ms = warp / ks, split = warp % ks, mt = mg * mpc + ms, nbi = a.inter / 256, b0 = split * 2;
+
+    const uint8_t* db = a.down + (size_t)e * a.dstride + ((size_t)mt * nbi + b0) * TB;
+    typename T::Frag d0, d1;
+    T::load(d0, db, lane);
+    T::load(d1, db + TB, lane);
+
+    uint32_t* tbl = reinterpret_cast<uint32_t*>(smem);
+    XStage xs = xstage_carve(smem + tbl_bytes_of<F>(), 4 * NQ, a.inter);
+    float* red = reinterpret_cast<float*>(smem + tbl_bytes_of<F>() + xstage_bytes(4 * NQ, a.inter));
+    if constexpr (IsIQ<F>::value) IQLut<F>::init(tbl, grid_ptr<F>());
+    xstage_fill(xs, a.mid, a.inter, cnt, 4 * NQ, a.inter, sel, 1);
+    __syncthreads();
+    const XView xv = xs.view();
+
+    float acc[2][NQ];
+#pragma unroll
+    for (int q = 0; q < NQ; q++) acc[0][q] = acc[1][q] = 0.f;
+    tile_dot<F, NQ>(d0, xv, b0, acc, lane, tbl);
+    tile_dot<F, NQ>(d1, xv, b0 + 1, acc, lane, tbl);
+
+    if (ks > 1) {
+        float* r = red + (warp * 32 + lane) * 2 * NQ;
+#pragma unroll
+        for (int q = 0; q < NQ; q++) {
+            r[2 * q] = acc[0][q];
+            r[2 * q + 1] = acc[1][q];
+        }
+        __syncthreads();
+        if (split == 0) {
+#pragma unroll
+            for (int q = 0; q < NQ; q++) {
+                float s0 = 0.f, s1 = 0.f;
+                for (int p = 0; p < ks; p++) {
+                    s0 += red[((warp + p) * 32 + lane) * 2 * NQ + 2 * q];
+                    s1 += red[((warp + p) * 32 + lane) * 2 * NQ + 2 * q + 1];
+                }
+                acc[0][q] = s0;
+                acc[1][q] = s1;
+            }
+        }
+    }
+    if (split == 0) {
+        const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+        for (int q = 0; q < NQ; q++) {
+            const int j = 4 * q + t;
+            if (j < cnt) {
+                float* o = a.dout + (size_t)sel[j] * a.hidden + mt * 16 + g;
+                o[0] = acc[0][q];
+                o[8] = acc[1][q];
+            }
+        }
+    }
+}
+
+
 // --------------------------------------------------------------- combine --
 __global__ void k_moe_combine(const MoeArgs a) {
     pdl_wait();
@@ -462,33 +478,6 @@ __global__ void k_moe_combine(const MoeArgs a) {
 
 // -------------------------------------------------------------- launcher --
 
-template <int F, int NQ>
-static size_t gu_smem(int hidden) {
-    return tbl_bytes_of<F>() + xstage_bytes(4 * NQ, hidden) + (size_t)kThreads * 4 * NQ * 4;
-}
-
-template <int F, int NQ>
-static int launch_gateup(const MoeArgs& a, int max_items, cudaStream_t st) {
-    const size_t smem = gu_smem<F, NQ>(a.hidden);
-    if (smem > 200 * 1024) return QW6K_ERR_ARG;
-    static DevFlags cfg;
-    if (smem_optin(cfg, k_moe_gateup<F, NQ>, 200 * 1024)) return QW6K_ERR_CUDA;
-    const int mgroups = (a.inter / 16) / (kWarps / a.ks_gu);
-    k_moe_gateup<F, NQ><<<max_items * mgroups, kThreads, smem, st>>>(a);
-    return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
-}
-
-template <int F, int NQ>
-static int launch_down(const MoeArgs& a, int max_items, cudaStream_t st) {
-    const size_t smem = gu_smem<F, NQ>(a.inter);
-    if (smem > 200 * 1024) return QW6K_ERR_ARG;
-    static DevFlags cfg;
-    if (smem_optin(cfg, k_moe_down<F, NQ>, 200 * 1024)) return QW6K_ERR_CUDA;
-    const int mgroups = (a.hidden / 16) / (kWarps / a.ks_dn);
-    k_moe_down<F, NQ><<<max_items * mgroups, kThreads, smem, st>>>(a);
-    return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
-}
-
 #define QW6_MOE_DISPATCH(quant, FN, NQ, ...)                  \
     switch (quant) {                                          \
     case QW6F_Q4_K_M:                                         \
@@ -501,21 +490,11 @@ static int launch_down(const MoeArgs& a, int max_items, cudaStream_t st) {
     default: return QW6K_ERR_QUANT;                           \
     }
 
-static int gateup_any(uint32_t q, int nq, const MoeArgs& a, int mi, cudaStream_t st) {
-    if (nq == 1) { QW6_MOE_DISPATCH(q, launch_gateup, 1, a, mi, st) }
-    QW6_MOE_DISPATCH(q, launch_gateup, 2, a, mi, st)
-}
-static int down_any(uint32_t q, int nq, const MoeArgs& a, int mi, cudaStream_t st) {
-    if (nq == 1) { QW6_MOE_DISPATCH(q, launch_down, 1, a, mi, st) }
-    QW6_MOE_DISPATCH(q, launch_down, 2, a, mi, st)
-}
-
-
 template <typename Kern>
-static int launch_ex(Kern k, int grid, size_t smem, bool pdl, cudaStream_t st, const MoeArgs& a) {
+static int launch_ex(Kern k, int grid, int block, size_t smem, bool pdl, cudaStream_t st, const MoeArgs& a) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3((unsigned)block);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute at[1];
@@ -536,7 +515,7 @@ static int launch_small_gu(const MoeArgs& a, cudaStream_t st) {
     static DevFlags cfg;
     if (smem_optin(cfg, k_moe_small_gu<F, NBW>, 200 * 1024)) return QW6K_ERR_CUDA;
     const int ks = a.hidden / 256 / NBW, mgroups = (a.inter / 16) / (kWarps / ks);
-    return launch_ex(k_moe_small_gu<F, NBW>, a.ntok * a.topk * mgroups, smem, false, st, a);
+    return launch_ex(k_moe_small_gu<F, NBW>, a.ntok * a.topk * mgroups, kThreads, smem, false, st, a);
 }
 
 template <int F>
@@ -550,7 +529,47 @@ static int launch_small_down(const MoeArgs& a, cudaStream_t st) {
     if (smem > 180 * 1024) return QW6K_ERR_ARG;
     static DevFlags cfg;
     if (smem_optin(cfg, k_moe_small_down<F>, 200 * 1024)) return QW6K_ERR_CUDA;
-    return launch_ex(k_moe_small_down<F>, a.hidden / 16, smem, true, st, a);
+    return launch_ex(k_moe_small_down<F>, a.hidden / 16, kThreads, smem, true, st, a);
+}
+
+template <int F, int NQ>
+static size_t gu_smem(int hidden) {
+    return tbl_bytes_of<F>() + xstage_bytes(4 * NQ, hidden) + (size_t)kThreads * 4 * NQ * 4;
+}
+
+template <int F, int NQ>
+static int launch_gateup(const MoeArgs& a, int max_items, cudaStream_t st) {
+    const size_t smem = gu_smem<F, NQ>(a.hidden);
+    if (smem > 200 * 1024) return QW6K_ERR_ARG;
+    // one K block of gate and up per warp (two when hidden has more than 8)
+    const int nbh = a.hidden / 256, nbw = nbh > kWarps ? 2 : 1;
+    static DevFlags cfg1, cfg2;
+    if (smem_optin(nbw == 1 ? cfg1 : cfg2, nbw == 1 ? k_moe_gateup<F, NQ, 1> : k_moe_gateup<F, NQ, 2>, 200 * 1024))
+        return QW6K_ERR_CUDA;
+    const int mgroups = (a.inter / 16) / (kWarps / (nbh / nbw));
+    if (nbw == 1) k_moe_gateup<F, NQ, 1><<<max_items * mgroups, kThreads, smem, st>>>(a);
+    else k_moe_gateup<F, NQ, 2><<<max_items * mgroups, kThreads, smem, st>>>(a);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
+}
+
+template <int F, int NQ>
+static int launch_down(const MoeArgs& a, int max_items, cudaStream_t st) {
+    const size_t smem = gu_smem<F, NQ>(a.inter);
+    if (smem > 200 * 1024) return QW6K_ERR_ARG;
+    static DevFlags cfg;
+    if (smem_optin(cfg, k_moe_down<F, NQ>, 200 * 1024)) return QW6K_ERR_CUDA;
+    const int mgroups = (a.hidden / 16) / (kWarps / (a.inter / 512));
+    k_moe_down<F, NQ><<<max_items * mgroups, kThreads, smem, st>>>(a);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
+}
+
+static int gateup_any(uint32_t q, int nq, const MoeArgs& a, int mi, cudaStream_t st) {
+    if (nq == 1) { QW6_MOE_DISPATCH(q, launch_gateup, 1, a, mi, st) }
+    QW6_MOE_DISPATCH(q, launch_gateup, 2, a, mi, st)
+}
+static int down_any(uint32_t q, int nq, const MoeArgs& a, int mi, cudaStream_t st) {
+    if (nq == 1) { QW6_MOE_DISPATCH(q, launch_down, 1, a, mi, st) }
+    QW6_MOE_DISPATCH(q, launch_down, 2, a, mi, st)
 }
 
 static int small_gu_any(uint32_t q, const MoeArgs& a, cudaStream_t st) {
@@ -559,6 +578,28 @@ static int small_gu_any(uint32_t q, const MoeArgs& a, cudaStream_t st) {
 }
 static int small_down_any(uint32_t q, const MoeArgs& a, cudaStream_t st) {
     QW6_MOE_DISPATCH(q, launch_small_down, 1, a, st)
+}
+
+// Set up every kernel of the decode paths on the current device (function
+// attributes, which also loads them), so that later calls only launch.
+template <int F>
+static int dec_setup_one() {
+    static DevFlags c1, c2, c3, c4, c5, c6;
+    int rc = smem_optin(c1, k_moe_small_gu<F, 1>, 200 * 1024);
+    rc |= smem_optin(c2, k_moe_small_down<F>, 200 * 1024);
+    static DevFlags c9;
+    rc |= smem_optin(c9, k_moe_small_gu<F, 2>, 200 * 1024);
+    static DevFlags c7, c8;
+    rc |= smem_optin(c3, k_moe_gateup<F, 1, 1>, 200 * 1024);
+    rc |= smem_optin(c4, k_moe_gateup<F, 2, 1>, 200 * 1024);
+    rc |= smem_optin(c7, k_moe_gateup<F, 1, 2>, 200 * 1024);
+    rc |= smem_optin(c8, k_moe_gateup<F, 2, 2>, 200 * 1024);
+    rc |= smem_optin(c5, k_moe_down<F, 1>, 200 * 1024);
+    rc |= smem_optin(c6, k_moe_down<F, 2>, 200 * 1024);
+    cudaFuncAttributes fa;
+    rc |= cudaFuncGetAttributes(&fa, k_moe_plan) == cudaSuccess ? 0 : QW6K_ERR_CUDA;
+    rc |= cudaFuncGetAttributes(&fa, k_moe_combine) == cudaSuccess ? 0 : QW6K_ERR_CUDA;
+    return rc ? QW6K_ERR_CUDA : 0;
 }
 
 }  // namespace qw6
@@ -580,12 +621,25 @@ extern "C" size_t qw6k_moe_ws_bytes(uint32_t ntok, uint32_t hidden, uint32_t int
     return al256(tk * 4) * 3 + al256((size_t)mi * 16) + 256 + al256(tk * inter * 4) + al256(tk * hidden * 4);
 }
 
+static bool moe_small(const qw6k_moe_desc* d) {
+    if (d->ntok > 4 || d->ntok * d->topk > 32) return false;
+    const int nbh = (int)d->hidden / 256;
+    const int ksh = nbh / nbw_of(nbh);
+    if (ksh > 8 || (d->inter / 16) % (kWarps / ksh)) return false;
+    const size_t lut = d->dq == QW6F_IQ2_XXS ? IQLut<QW6F_IQ2_XXS>::bytes
+                       : d->dq == QW6F_IQ2_S ? IQLut<QW6F_IQ2_S>::bytes
+                       : d->dq == QW6F_IQ3_S ? IQLut<QW6F_IQ3_S>::bytes : 0;
+    return (size_t)d->ntok * d->topk * xstage_bytes(4, (int)d->inter) + lut <= 180 * 1024;
+}
+
 static int moe_args(const qw6k_moe_desc* d, MoeArgs& a) {
     if (!d || !d->gate || !d->up || !d->down || !d->logits || !d->x || !d->out || !d->ws || !d->ntok || !d->ne ||
         d->ne > 256 || !d->topk || d->topk > 32 || d->topk > d->ne || (size_t)d->ntok * d->topk > 4096)
         return QW6K_ERR_ARG;
     const uint32_t nbh = d->hidden / 256, nbi = d->inter / 256;
-    if (d->hidden % 512 || d->inter % 512 || nbh > 16 || nbi > 16 || d->hidden > 4096) return QW6K_ERR_ARG;
+    if (!nbh || !nbi || d->hidden % 256 || d->inter % 256 || nbh > 16 || nbi > 16 || d->hidden > 4096)
+        return QW6K_ERR_ARG;
+    if (!moe_small(d) && (d->hidden % 512 || d->inter % 512)) return QW6K_ERR_ARG;  // the planned kernels' K split
     if (d->ws_bytes < qw6k_moe_ws_bytes(d->ntok, d->hidden, d->inter, d->ne, d->topk)) return QW6K_ERR_ARG;
     if ((reinterpret_cast<uintptr_t>(d->x) | reinterpret_cast<uintptr_t>(d->gate) |
          reinterpret_cast<uintptr_t>(d->up) | reinterpret_cast<uintptr_t>(d->down) | d->gstride | d->ustride |
@@ -606,9 +660,6 @@ static int moe_args(const qw6k_moe_desc* d, MoeArgs& a) {
     a.ne = (int)d->ne;
     a.topk = (int)d->topk;
     a.chunk = (int)moe_chunk(d->ntok);
-    a.ks_gu = (int)nbh / 2;
-    a.ks_dn = (int)nbi / 2;
-    if ((a.inter / 16) % (kWarps / a.ks_gu) || (a.hidden / 16) % (kWarps / a.ks_dn)) return QW6K_ERR_ARG;
     const size_t tk = (size_t)d->ntok * d->topk;
     const int mi = moe_items_max(d->ntok, d->ne, d->topk, (uint32_t)a.chunk);
     uint8_t* p = (uint8_t*)d->ws;
@@ -622,15 +673,17 @@ static int moe_args(const qw6k_moe_desc* d, MoeArgs& a) {
     return 0;
 }
 
-static bool moe_small(const qw6k_moe_desc* d) {
-    if (d->ntok > 4 || d->ntok * d->topk > 32) return false;
-    const int nbh = (int)d->hidden / 256;
-    const int ksh = nbh / nbw_of(nbh);
-    if (ksh > 8 || (d->inter / 16) % (kWarps / ksh)) return false;
-    const size_t lut = d->dq == QW6F_IQ2_XXS ? IQLut<QW6F_IQ2_XXS>::bytes
-                       : d->dq == QW6F_IQ2_S ? IQLut<QW6F_IQ2_S>::bytes
-                       : d->dq == QW6F_IQ3_S ? IQLut<QW6F_IQ3_S>::bytes : 0;
-    return (size_t)d->ntok * d->topk * xstage_bytes(4, (int)d->inter) + lut <= 180 * 1024;
+
+/* Configure (and load) every decode kernel of every format on the current
+ * device. */
+extern "C" int qw6k_moe_decode_setup(void) {
+    int rc = dec_setup_one<QW6F_Q4_K_M>();
+    rc |= dec_setup_one<QW6F_Q5_K>();
+    rc |= dec_setup_one<QW6F_Q6_K>();
+    rc |= dec_setup_one<QW6F_IQ2_XXS>();
+    rc |= dec_setup_one<QW6F_IQ2_S>();
+    rc |= dec_setup_one<QW6F_IQ3_S>();
+    return rc ? QW6K_ERR_CUDA : 0;
 }
 
 extern "C" int qw6k_moe_check(const qw6k_moe_desc* d) {
@@ -663,17 +716,15 @@ extern "C" int qw6k_moe_phase(const qw6k_moe_desc* d, int phase, cudaStream_t st
     const int nq = a.chunk / 4;
     switch (phase) {
     case 0:
-        k_moe_plan<<<1, 512, 0, st>>>(a);
-        break;
+        return launch_pdl(k_moe_plan, dim3(1), dim3(512), 0, st, a) == cudaSuccess ? 0 : QW6K_ERR_CUDA;
     case 1:
         return gateup_any(d->gq, nq, a, mi, st);
     case 2:
         return down_any(d->dq, nq, a, mi, st);
-    case 3: {
-        dim3 cg((d->hidden + 255) / 256, d->ntok);
-        k_moe_combine<<<cg, 256, 0, st>>>(a);
-        break;
-    }
+    case 3:
+        return launch_pdl(k_moe_combine, dim3((d->hidden + 255) / 256, d->ntok), dim3(256), 0, st, a) == cudaSuccess
+                   ? 0
+                   : QW6K_ERR_CUDA;
     default:
         return QW6K_ERR_ARG;
     }

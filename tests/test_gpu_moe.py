@@ -60,6 +60,35 @@ def test_moe_config1_decode(cuda, oracle):
     assert rel_err(out[0], ref64[0]) <= TOL
 
 
+def test_moe_decode_ring_recycles(cuda, oracle, rng):
+    """4 tokens over 256 experts: up to 32 distinct experts, so every
+    gate/up CTA streams several (expert, row-tile) units through its
+    shared-memory ring and reuses its slots."""
+    E, H, I, K, T = 256, 2048, 512, 8, 4
+    gate, up, down = S.moe_weights(rng, E, S.Q4_K, S.Q6_K, H, I)
+    logits = rng.standard_normal((T, E), dtype=np.float32)
+    x = rng.standard_normal((T, H), dtype=np.float32)
+    out = run_moe(cuda, S.Q4_K, gate, up, S.Q6_K, down, logits, x, K)
+    ref, idx, _ = oracle.moe_layer(S.Q4_K, gate, up, S.Q6_K, down, logits, x, top_k=K)
+    assert len(np.unique(idx)) > 24
+    for t in range(T):
+        assert rel_err(out[t], ref[t]) <= TOL, t
+
+
+@pytest.mark.parametrize("H,I", [(1024, 2048), (2048, 1024)])
+def test_moe_decode_other_shapes(H, I, cuda, oracle, rng):
+    """inter 2048: the down kernel stages mid rows two experts at a time;
+    hidden 1024 / inter 1024: other K-split and tile counts."""
+    E, K, T = 16, 8, 2
+    gate, up, down = S.moe_weights(rng, E, S.Q4_K, S.Q6_K, H, I)
+    logits = rng.standard_normal((T, E), dtype=np.float32)
+    x = rng.standard_normal((T, H), dtype=np.float32)
+    out = run_moe(cuda, S.Q4_K, gate, up, S.Q6_K, down, logits, x, K)
+    ref, _, _ = oracle.moe_layer(S.Q4_K, gate, up, S.Q6_K, down, logits, x, top_k=K)
+    for t in range(T):
+        assert rel_err(out[t], ref[t]) <= TOL, t
+
+
 def test_moe_config2_batched_iq2xxs(cuda, oracle):
     """Config 2: 64 tokens, IQ2_XXS experts."""
     gate, up, down, logits, x = S.config2()
