@@ -294,9 +294,94 @@ __global__ void __launch_bounds__(kThreads, NQ == 1 ? 2 : 1) k_matvec(const MvAr
     }
 }
 
+// ===================================================== 16-bit weights ====
+// FP16 / BF16 weight rows (qw6_tensor_dequantize_row, qw6.c:1686-1692): no
+// blocks and no repacking -- the matrix stays row-major.  Dequantization is
+// the exact widening (qw6_fp16_to_f32 with subnormals, Inf, NaN; bf16 << 16).
+// The matvec is one warp per row: 16-byte loads of 8 weights, fp32 fma with
+// each token's x (read through L1, shared by all rows of the CTA), a warp
+// reduction; HBM-bound (weight bytes + x + y per launch).
+
+template <bool BF>
+__device__ __forceinline__ float w16(uint32_t h) {
+    if constexpr (BF) return __uint_as_float(h << 16);
+    else return f16_bits_exact(h);
+}
+
+template <bool BF>
+__global__ void k_dequant16(const uint16_t* __restrict__ w, float* __restrict__ out, long long n) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        out[i] = w16<BF>(w[i]);
+}
+
+template <bool BF, int NT>
+__global__ void __launch_bounds__(256) k_matvec16(const uint16_t* __restrict__ w, const float* __restrict__ x,
+                                                  float* __restrict__ y, int rows, int cols, int ntok, int ldx,
+                                                  int ldy) {
+    const int lane = threadIdx.x & 31;
+    const int nw = gridDim.x * (blockDim.x >> 5);
+    for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += nw) {
+        const uint16_t* wr = w + (size_t)r * cols;
+        float acc[NT];
+#pragma unroll
+        for (int t = 0; t < NT; t++) acc[t] = 0.f;
+        for (int c = 8 * lane; c < cols; c += 256) {
+            const uint4 v = ldg128(wr + c);
+            float wv[8];
+            const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                wv[2 * i] = w16<BF>(u[i] & 0xffffu);
+                wv[2 * i + 1] = w16<BF>(u[i] >> 16);
+            }
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+                if (t < ntok) {
+                    const float4 x0 = __ldg(reinterpret_cast<const float4*>(x + (size_t)t * ldx + c));
+                    const float4 x1 = __ldg(reinterpret_cast<const float4*>(x + (size_t)t * ldx + c + 4));
+                    float a = acc[t];
+                    a = fmaf(wv[0], x0.x, a);
+                    a = fmaf(wv[1], x0.y, a);
+                    a = fmaf(wv[2], x0.z, a);
+                    a = fmaf(wv[3], x0.w, a);
+                    a = fmaf(wv[4], x1.x, a);
+                    a = fmaf(wv[5], x1.y, a);
+                    a = fmaf(wv[6], x1.z, a);
+                    a = fmaf(wv[7], x1.w, a);
+                    acc[t] = a;
+                }
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            float a = acc[t];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+            if (lane == 0 && t < ntok) y[(size_t)t * ldy + r] = a;
+        }
+    }
+}
+
+template <bool BF>
+static int launch_matvec16(const void* w, const float* x, float* y, int rows, int cols, int ntok, int ldx, int ldy,
+                           cudaStream_t st) {
+    const long long want = ((long long)rows + 7) / 8;
+    const int grid = (int)(want < (long long)device_sms() * 8 ? want : (long long)device_sms() * 8);
+    const uint16_t* wp = static_cast<const uint16_t*>(w);
+    if (ntok == 1) k_matvec16<BF, 1><<<grid, 256, 0, st>>>(wp, x, y, rows, cols, ntok, ldx, ldy);
+    else if (ntok <= 4) k_matvec16<BF, 4><<<grid, 256, 0, st>>>(wp, x, y, rows, cols, ntok, ldx, ldy);
+    else if (ntok <= 8) k_matvec16<BF, 8><<<grid, 256, 0, st>>>(wp, x, y, rows, cols, ntok, ldx, ldy);
+    else k_matvec16<BF, 32><<<grid, 256, 0, st>>>(wp, x, y, rows, cols, ntok, ldx, ldy);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
+}
+
+static bool is16(uint32_t q) { return q == QW6F_FP16 || q == QW6F_BF16; }
+
 // ---------------------------------------------------------- launchers ----
 
 static int num_sms() { return device_sms(); }
+
+constexpr size_t kMvSmemMax = 200 * 1024;  // dynamic shared memory a matvec launch may use
 
 template <int F, int NQ>
 static size_t mv_smem(int cols) {
@@ -307,7 +392,7 @@ template <int F, int NQ, bool KEYS>
 static int launch_mv(const uint8_t* w, const float* x, float* y, int rows, int cols, int ntok, int ldx,
                      int ldy, cudaStream_t st, unsigned long long* keys = nullptr, uint32_t row_offset = 0) {
     const size_t smem = mv_smem<F, NQ>(cols);
-    if (smem > 200 * 1024) return QW6K_ERR_ARG;
+    if (smem > kMvSmemMax) return QW6K_ERR_ARG;
     static DevFlags configured;
     int occ = 1;
     if (smem_optin(configured, k_matvec<F, NQ, KEYS>, 200 * 1024)) return QW6K_ERR_CUDA;
@@ -338,22 +423,37 @@ static int launch_mv(const uint8_t* w, const float* x, float* y, int rows, int c
     return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
 }
 
+// Token batches: 1-4 and 5-8 tokens in one launch; 9-32 tokens in one launch
+// when the activation stage of 32 tokens fits in shared memory, else in
+// chunks of 16 tokens (each chunk streams the weights again; only very wide
+// matrices, e.g. 4096 columns, need that).
+template <int F, bool KEYS>
+static int launch_mv_batch(const uint8_t* w, const float* x, float* y, int rows, int cols, int ntok, int ldx,
+                           int ldy, cudaStream_t st, unsigned long long* keys, uint32_t row_offset) {
+    if (ntok <= 4) return launch_mv<F, 1, KEYS>(w, x, y, rows, cols, ntok, ldx, ldy, st, keys, row_offset);
+    if (ntok <= 8) return launch_mv<F, 2, KEYS>(w, x, y, rows, cols, ntok, ldx, ldy, st, keys, row_offset);
+    if (ntok > 32) return QW6K_ERR_ARG;
+    if (mv_smem<F, 8>(cols) <= kMvSmemMax)
+        return launch_mv<F, 8, KEYS>(w, x, y, rows, cols, ntok, ldx, ldy, st, keys, row_offset);
+    for (int t0 = 0; t0 < ntok; t0 += 16) {
+        const int n = ntok - t0 < 16 ? ntok - t0 : 16;
+        const int rc = launch_mv<F, 4, KEYS>(w, x + (size_t)t0 * ldx, y ? y + (size_t)t0 * ldy : nullptr, rows, cols,
+                                             n, ldx, ldy, st, keys ? keys + t0 : nullptr, row_offset);
+        if (rc) return rc;
+    }
+    return 0;
+}
+
 template <int F>
 static int launch_mv_nq(const uint8_t* w, const float* x, float* y, int rows, int cols, int ntok, int ldx,
                         int ldy, cudaStream_t st) {
-    if (ntok <= 4) return launch_mv<F, 1, false>(w, x, y, rows, cols, ntok, ldx, ldy, st);
-    if (ntok <= 8) return launch_mv<F, 2, false>(w, x, y, rows, cols, ntok, ldx, ldy, st);
-    if (ntok <= 32) return launch_mv<F, 8, false>(w, x, y, rows, cols, ntok, ldx, ldy, st);
-    return QW6K_ERR_ARG;
+    return launch_mv_batch<F, false>(w, x, y, rows, cols, ntok, ldx, ldy, st, nullptr, 0);
 }
 
 template <int F>
 static int launch_mv_keys(const uint8_t* w, const float* x, float* y, int rows, int cols, int ntok, int ldx,
                           int ldy, unsigned long long* keys, uint32_t row_offset, cudaStream_t st) {
-    if (ntok <= 4) return launch_mv<F, 1, true>(w, x, y, rows, cols, ntok, ldx, ldy, st, keys, row_offset);
-    if (ntok <= 8) return launch_mv<F, 2, true>(w, x, y, rows, cols, ntok, ldx, ldy, st, keys, row_offset);
-    if (ntok <= 32) return launch_mv<F, 8, true>(w, x, y, rows, cols, ntok, ldx, ldy, st, keys, row_offset);
-    return QW6K_ERR_ARG;
+    return launch_mv_batch<F, true>(w, x, y, rows, cols, ntok, ldx, ldy, st, keys, row_offset);
 }
 
 template <int F>
@@ -394,12 +494,21 @@ using namespace qw6;
 extern "C" size_t qw6k_tile_bytes(uint32_t quant) { return (size_t)16 * qw6_block_bytes(quant); }
 
 extern "C" size_t qw6k_packed_bytes(uint32_t quant, uint32_t rows, uint32_t cols) {
+    if (is16(quant)) return (rows && cols && cols % 8 == 0) ? (size_t)rows * cols * 2 : 0;  // row-major as stored
     if (!qw6_block_bytes(quant) || cols == 0 || cols % 256 || rows == 0) return 0;
     return (size_t)((rows + 15) / 16) * (cols / 256) * qw6k_tile_bytes(quant);
 }
 
 extern "C" int qw6k_pack(uint32_t quant, const void* raw, void* packed, uint32_t rows, uint32_t cols,
                          uint32_t nmat, size_t raw_stride, size_t packed_stride, cudaStream_t st) {
+    if (is16(quant)) {  // no repacking: copy the rows of each matrix
+        if (!raw || !packed || !rows || !cols || cols % 8 || !nmat) return QW6K_ERR_ARG;
+        const size_t bytes = (size_t)rows * cols * 2;
+        return cudaMemcpy2DAsync(packed, nmat > 1 ? packed_stride : bytes, raw, nmat > 1 ? raw_stride : bytes, bytes,
+                                 nmat, cudaMemcpyDeviceToDevice, st) == cudaSuccess
+                   ? 0
+                   : QW6K_ERR_CUDA;
+    }
     if (!raw || !packed || !rows || !cols || cols % 256 || !nmat || nmat > 65535) return QW6K_ERR_ARG;
 #define CALL(F) launch_pack<F>(raw, packed, (int)rows, (int)cols, (int)nmat, raw_stride, packed_stride, st)
     QW6_DISPATCH_BLOCK(quant, CALL)
@@ -408,6 +517,14 @@ extern "C" int qw6k_pack(uint32_t quant, const void* raw, void* packed, uint32_t
 
 extern "C" int qw6k_dequant(uint32_t quant, const void* raw, float* out, uint32_t rows, uint32_t cols,
                             cudaStream_t st) {
+    if (is16(quant)) {
+        if (!raw || !out || !rows || !cols) return QW6K_ERR_ARG;
+        const long long n = (long long)rows * cols;
+        const int grid = (int)((n + 255) / 256 < 65535 ? (n + 255) / 256 : 65535);
+        if (quant == QW6F_FP16) k_dequant16<false><<<grid, 256, 0, st>>>((const uint16_t*)raw, out, n);
+        else k_dequant16<true><<<grid, 256, 0, st>>>((const uint16_t*)raw, out, n);
+        return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
+    }
     if (!raw || !out || !rows || !cols || cols % 256) return QW6K_ERR_ARG;
 #define CALL(F) launch_dequant<F>(raw, out, (int)rows, (int)cols, st)
     QW6_DISPATCH_BLOCK(quant, CALL)
@@ -416,6 +533,17 @@ extern "C" int qw6k_dequant(uint32_t quant, const void* raw, float* out, uint32_
 
 extern "C" int qw6k_matvec(uint32_t quant, const void* packed, const float* x, float* y, uint32_t rows,
                            uint32_t cols, uint32_t ntok, uint32_t ldx, uint32_t ldy, cudaStream_t st) {
+    if (is16(quant)) {
+        if (!packed || !x || !y || !rows || !cols || cols % 8 || !ntok || ntok > 32 || ldx < cols || ldy < rows ||
+            rows > (1u << 30))
+            return QW6K_ERR_ARG;
+        if ((reinterpret_cast<uintptr_t>(packed) & 15u) || (reinterpret_cast<uintptr_t>(x) & 15u) || (ldx & 3u))
+            return QW6K_ERR_ALIGN;
+        return quant == QW6F_FP16 ? launch_matvec16<false>(packed, x, y, (int)rows, (int)cols, (int)ntok, (int)ldx,
+                                                           (int)ldy, st)
+                                  : launch_matvec16<true>(packed, x, y, (int)rows, (int)cols, (int)ntok, (int)ldx,
+                                                          (int)ldy, st);
+    }
     if (!packed || !x || !y || !rows || !cols || cols % 256 || !ntok || ntok > 32 || ldx < cols || ldy < rows ||
         rows > (1u << 30) || cols > 65536)
         return QW6K_ERR_ARG;

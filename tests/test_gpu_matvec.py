@@ -76,6 +76,58 @@ def test_matvec_multi_token(q, ntok, cuda, oracle, rng):
         assert rel_err(y[t], ref[t]) <= TOL, t
 
 
+@pytest.mark.parametrize("ntok", [20, 32])
+def test_matvec_wide_batch(ntok, cuda, oracle, rng):
+    """Config 4's IQ2_S shape [2048 x 4096] at batch 32: the 32-token
+    activation stage of 4096 columns exceeds shared memory, so the launch is
+    split into 16-token chunks."""
+    q, rows, cols = S.IQ2_S, 2048, 4096
+    w = S.make_matrix(q, rows, cols, rng)
+    x = rng.standard_normal((ntok, cols), dtype=np.float32)
+    y = gpu_matvec(cuda, q, w, x, rows, cols)
+    ref = oracle.matvec(q, w, x, rows, cols).reshape(ntok, rows)
+    for t in range(ntok):
+        assert rel_err(y[t], ref[t]) <= TOL, t
+
+
+def _halves(rng, q, rows, cols):
+    """FP16 / BF16 weight rows with special values mixed in: +-0, subnormals,
+    +-inf, NaN (for FP16 the exact widening of qw6_fp16_to_f32 is checked)."""
+    if q == S.FP16:
+        h = rng.standard_normal((rows, cols)).astype(np.float16).view(np.uint16)
+        special = np.array([0x0000, 0x8000, 0x0001, 0x03FF, 0x8001, 0x7C00, 0xFC00, 0x7E00, 0x7BFF], np.uint16)
+    else:
+        h = S.bf16_round(rng.standard_normal((rows, cols)).astype(np.float32))
+        special = np.array([0x0000, 0x8000, 0x0001, 0x007F, 0x7F80, 0xFF80, 0x7FC0, 0x7F7F], np.uint16)
+    h.reshape(-1)[: special.size] = special
+    return h.view(np.uint8).reshape(rows, cols * 2)
+
+
+@pytest.mark.parametrize("q", [S.FP16, S.BF16])
+def test_dequant16_bitexact(q, cuda, oracle, rng):
+    """FP16 / BF16 rows (qw6.c:1686-1692): the exact widening, bit for bit
+    (NaN positions only for NaN)."""
+    rows, cols = 9, 1000
+    w = _halves(rng, q, rows, cols)
+    assert same_bits(gpu_dequant(cuda, q, w, rows, cols), oracle.dequantize(q, w, rows, cols))
+
+
+@pytest.mark.parametrize("q", [S.FP16, S.BF16])
+@pytest.mark.parametrize("ntok", [1, 3, 8, 32])
+def test_matvec16_vs_oracle(q, ntok, cuda, oracle, rng):
+    """16-bit weight matvec (row-major, no repacking), 1-32 tokens, against the
+    oracle's dequant-then-dot (qw6_tensor_matvec order) and its float64 form."""
+    rows, cols = 333, 1000
+    w = _halves(rng, q, rows, cols)
+    w.view(np.uint16).reshape(-1)[:16] = 0  # keep the specials out of the dot
+    x = rng.standard_normal((ntok, cols), dtype=np.float32)
+    y = gpu_matvec(cuda, q, w, x, rows, cols)
+    ref = oracle.matvec(q, w, x, rows, cols).reshape(ntok, rows)
+    for t in range(ntok):
+        assert rel_err(y[t], ref[t]) <= TOL, t
+        assert rel_err(y[t], oracle.matvec_f64(q, w, x[t], rows, cols)) <= TOL, t
+
+
 def test_matvec_heavy_tailed_activations(cuda, oracle, rng):
     """Per-256-block activation scaling copes with outliers (like silu*up)."""
     q, rows, cols = S.Q6_K, 256, 512

@@ -50,6 +50,16 @@ def test_matvec_matches_reference_bitexact(q, oracle, reference, rng):
         assert same_bits(oracle.matvec(q, w, x, rows, cols), reference.matvec(q, w, x, rows, cols))
 
 
+@pytest.mark.parametrize("q", [S.FP16, S.BF16])
+def test_dequant16_matches_reference_bitexact(q, oracle, reference, rng):
+    """FP16 / BF16 rows, including every class of special value, widen to the
+    same bits as qw6_tensor_dequantize_row (qw6.c:1686-1692)."""
+    rows, cols = 6, 512
+    h = rng.integers(0, 1 << 16, size=(rows, cols), dtype=np.uint16)
+    w = h.view(np.uint8).reshape(rows, cols * 2)
+    assert same_bits(oracle.dequantize(q, w, rows, cols), reference.dequantize(q, w, rows, cols))
+
+
 def test_fp16_exhaustive(oracle):
     h = np.arange(65536, dtype=np.uint32).astype(np.uint16)
     ref = h.view(np.float16).astype(np.float32)
