@@ -1,0 +1,127 @@
+// k_block.cu -- the MoE FFN block around the routed experts, as qw6's
+// forward pass applies it to every layer (qw6.c:2474-2484 around
+// qw6_apply_layer_moe, qw6.c:2226-2290):
+//   normed = rmsnorm(x) * norm_w                   (qw6_cpu_rmsnorm, qw6.c:2502-2512)
+//   logits = router . normed                       (fp32 router, qw6.c:2247)
+//   ffn    = routed experts (k_moe.cu)             (qw6.c:2249-2264)
+//   s      = sigmoid(shared_router . normed) or 1  (qw6.c:2268-2273)
+//   ffn   += s * shared_down(silu(shared_gate normed) * shared_up normed)
+//   out    = x + ffn                               (qw6.c:2482-2483)
+// This file holds the prologue (RMSNorm + router logits + shared gate, one
+// pass over x per token) and the epilogue (shared-expert weighting and the
+// residual); the routed experts and the shared expert's matvecs are the
+// library's existing kernels, so the whole block is device-resident.
+#include <cuda_runtime.h>
+
+#include "qw6_dev.cuh"
+#include "qw6_devcfg.cuh"
+#include "qw6_launch.h"
+
+namespace qw6 {
+
+constexpr int kBlkThreads = 256;
+constexpr float kRmsEps = 1e-6f;  // QW6_RMS_EPS (qw6.h:67)
+
+// 1 / sqrt(sum(x^2)/dim + eps) for token row x (every thread gets it).
+// The sum is a block reduction (qw6 sums sequentially; the difference is fp32
+// rounding of the sum), the rest is qw6's expression with IEEE operations.
+__device__ float rms_inv(const float* __restrict__ x, int dim, float* red) {
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float t = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); w++) t += red[w];
+    __syncthreads();
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)dim), kRmsEps)));
+}
+
+// grid (ceil(ne / 8), ntok): CTA (b, t) computes router rows [8b, 8b+8) of
+// token t (warp per row), CTA (0, t) also writes normed[t], and the last CTA
+// of the token the shared-expert gate sigmoid(shared_router . normed).
+// normed[i] = (x[i] * inv) * w[i] as qw6 evaluates it.
+__global__ void __launch_bounds__(kBlkThreads) k_block_pre(const float* __restrict__ x,
+                                                           const float* __restrict__ norm_w,
+                                                           const float* __restrict__ router,
+                                                           const float* __restrict__ srouter, float* __restrict__ normed,
+                                                           float* __restrict__ logits, float* __restrict__ sgate,
+                                                           int hidden, int ne) {
+    extern __shared__ __align__(16) float nrm[];  // [hidden]
+    __shared__ float red[kBlkThreads / 32];
+    const int t = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float* xt = x + (size_t)t * hidden;
+    const float inv = rms_inv(xt, hidden, red);
+    for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+        const float v = __fmul_rn(__fmul_rn(xt[i], inv), norm_w[i]);
+        nrm[i] = v;
+        if (blockIdx.x == 0) normed[(size_t)t * hidden + i] = v;
+    }
+    __syncthreads();
+    const int r = blockIdx.x * (kBlkThreads / 32) + warp;
+    if (r < ne) {
+        const float* wr = router + (size_t)r * hidden;
+        float acc = 0.f;
+        for (int c = 4 * lane; c < hidden; c += 128) {
+            const float4 w4 = __ldg(reinterpret_cast<const float4*>(wr + c));
+            acc = fmaf(w4.x, nrm[c], acc);
+            acc = fmaf(w4.y, nrm[c + 1], acc);
+            acc = fmaf(w4.z, nrm[c + 2], acc);
+            acc = fmaf(w4.w, nrm[c + 3], acc);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) logits[(size_t)t * ne + r] = acc;
+    }
+    if (blockIdx.x == gridDim.x - 1 && warp == (kBlkThreads / 32) - 1) {
+        float s = 1.0f;  // no shared router: weight 1 (qw6.c:2268)
+        if (srouter) {
+            float acc = 0.f;
+            for (int c = lane; c < hidden; c += 32) acc = fmaf(srouter[c], nrm[c], acc);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            s = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-acc)));  // qw6_sigmoid (qw6.h:295-297)
+        }
+        if (lane == 0) sgate[t] = s;
+    }
+}
+
+// out[t][i] = x[t][i] + (ffn[t][i] + s[t] * sh[t][i])  (sh may be null: no
+// shared expert), each operation rounded once as qw6's loops do.
+__global__ void k_block_post(const float* __restrict__ x, const float* __restrict__ ffn, const float* __restrict__ sh,
+                             const float* __restrict__ sgate, float* __restrict__ out, int hidden, long long n) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        float f = ffn[i];
+        if (sh) f = __fadd_rn(f, __fmul_rn(sgate[i / hidden], sh[i]));
+        out[i] = __fadd_rn(x[i], f);
+    }
+}
+
+}  // namespace qw6
+
+using namespace qw6;
+
+extern "C" int qw6k_block_pre(const float* x, const float* norm_w, const float* router, const float* srouter,
+                              float* normed, float* logits, float* sgate, uint32_t ntok, uint32_t hidden, uint32_t ne,
+                              cudaStream_t st) {
+    if (!x || !norm_w || !router || !normed || !logits || !sgate || !ntok || ntok > 65535 || !hidden ||
+        hidden % 4 || hidden > 16384 || !ne || ne > 256)
+        return QW6K_ERR_ARG;
+    if ((reinterpret_cast<uintptr_t>(router) | reinterpret_cast<uintptr_t>(x)) & 15u) return QW6K_ERR_ALIGN;
+    static DevFlags cfg;
+    if (hidden * 4 > 48 * 1024 && smem_optin(cfg, k_block_pre, (int)hidden * 4)) return QW6K_ERR_CUDA;
+    const dim3 grid((ne + kBlkThreads / 32 - 1) / (kBlkThreads / 32), ntok);
+    k_block_pre<<<grid, kBlkThreads, (size_t)hidden * 4, st>>>(x, norm_w, router, srouter, normed, logits, sgate,
+                                                               (int)hidden, (int)ne);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
+}
+
+extern "C" int qw6k_block_post(const float* x, const float* ffn, const float* shared, const float* sgate, float* out,
+                               uint32_t ntok, uint32_t hidden, cudaStream_t st) {
+    if (!x || !ffn || !out || !ntok || !hidden || (shared && !sgate)) return QW6K_ERR_ARG;
+    const long long n = (long long)ntok * hidden;
+    const int grid = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+    k_block_post<<<grid, 256, 0, st>>>(x, ffn, shared, sgate, out, (int)hidden, n);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
+}

@@ -171,7 +171,7 @@ void *qw6h_buf(qw6cu_ctx *ctx, int i, size_t bytes) {
 static const char *k_names[QW6H_K_COUNT] = {"matvec",   "pack",       "dequant",  "route",       "argmax",
                                              "moe_plan", "moe_gateup", "moe_down", "moe_combine", "lm_head",
                                              "pf_plan",  "pf_gemm1",   "pf_gemm2", "pf_combine",  "ep",
-                                             "ep_publish", "ep_dispatch", "ep_wait", "ep_combine"};
+                                             "ep_publish", "ep_dispatch", "ep_wait", "ep_combine", "moe_block"};
 
 _Static_assert(QW6H_K_COUNT == QW6CU_NKERNELS, "kernel-id table and public QW6CU_NKERNELS disagree");
 

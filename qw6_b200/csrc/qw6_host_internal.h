@@ -16,6 +16,7 @@ enum {
     QW6H_BUF_Y,       /* outputs */
     QW6H_BUF_KEY,     /* small scratch (argmax key, routing weights) */
     QW6H_BUF_WS,      /* workspace of the fused MoE / LM-head calls */
+    QW6H_BUF_BLOCK,   /* intermediates of the MoE FFN block */
     QW6H_NBUF
 };
 
@@ -45,6 +46,7 @@ enum {
     QW6H_K_EP_DISPATCH,
     QW6H_K_EP_WAIT,
     QW6H_K_EP_COMBINE,
+    QW6H_K_MOE_BLOCK,
     QW6H_K_COUNT
 };
 

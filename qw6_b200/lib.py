@@ -63,6 +63,15 @@ class ExpertPack(C.Structure):
     _fields_ = [("quant", C.c_uint32), ("base", C.c_void_p), ("stride", C.c_size_t)]
 
 
+class SharedExpert(C.Structure):
+    """qw6cu_shared_expert: gate/up/down device pointers (packed or FP16/BF16
+    row-major), their quant codes, the shared intermediate size and an
+    optional fp32 [hidden] router (None: weight 1)."""
+    _fields_ = [("gate_quant", C.c_uint32), ("up_quant", C.c_uint32), ("down_quant", C.c_uint32),
+                ("gate", C.c_void_p), ("up", C.c_void_p), ("down", C.c_void_p), ("inter", C.c_uint32),
+                ("router", C.c_void_p)]
+
+
 def load() -> C.CDLL:
     """Load the in-tree library (raises if it has not been built)."""
     global _lib
@@ -104,6 +113,8 @@ def load() -> C.CDLL:
     lib.qw6cu_moe_decode_hostio.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32]
     lib.qw6cu_moe_decode_noalloc.argtypes = [pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp]
     lib.qw6cu_moe_prefill.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32]
+    lib.qw6cu_moe_block.argtypes = [_vp, _vp, _vp, _vp, pk, pk, pk, C.POINTER(SharedExpert), _vp, _u32, _u32, _u32,
+                                    _u32, _u32]
     lib.qw6cu_moe_expert_rows.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32]
     lib.qw6cu_ep_count.argtypes = [_vp, _vp, _u32, _u32, _vp, _vp]
     lib.qw6cu_ep_pack.argtypes = [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _vp, _u32, _vp, _vp]
@@ -284,6 +295,14 @@ class Context:
         _check(self.lib.qw6cu_moe_decode_hostio(self.h, C.byref(gate), C.byref(up), C.byref(down), logits, x, out,
                                                 ntok, hidden, inter, n_experts, top_k), "qw6cu_moe_decode_hostio")
 
+    def moe_block(self, x, norm_w, router, gate: ExpertPack, up: ExpertPack, down: ExpertPack,
+                  shared: "SharedExpert | None", out, ntok, hidden, inter, n_experts, top_k):
+        """qw6cu_moe_block: rmsnorm, fp32 router, routed experts, optional
+        shared expert, residual (device pointers)."""
+        _check(self.lib.qw6cu_moe_block(self.h, x, norm_w, router, C.byref(gate), C.byref(up), C.byref(down),
+                                        C.byref(shared) if shared is not None else None, out, ntok, hidden, inter,
+                                        n_experts, top_k), "qw6cu_moe_block")
+
     def moe_prefill(self, gate: ExpertPack, up: ExpertPack, down: ExpertPack, logits, x_bf16, out, ntok, hidden,
                     inter, n_experts, top_k):
         _check(self.lib.qw6cu_moe_prefill(self.h, C.byref(gate), C.byref(up), C.byref(down), logits, x_bf16, out,
@@ -325,7 +344,7 @@ class Context:
 
     def profile_end(self) -> dict:
         """{kernel name: (total ms, launches)} for the kernels that ran."""
-        n = 19
+        n = 20  # QW6CU_NKERNELS
         ms = (C.c_double * n)()
         cnt = (C.c_uint32 * n)()
         _check(self.lib.qw6cu_profile_end(self.h, ms, cnt), "qw6cu_profile_end")
