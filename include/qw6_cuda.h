@@ -117,6 +117,21 @@ int qw6cu_lm_head_argmax(qw6cu_ctx *ctx, uint32_t quant, const void *packed, con
 int qw6cu_argmax_keys_reduce(qw6cu_ctx *ctx, const unsigned long long *keys, uint32_t nshards, uint32_t ntok,
                              uint32_t *idx, float *val);
 
+/* ---- sampling ---- */
+
+/* token[r] (device) = qw6_sample's pick (qw6.c:2904-2982) over logits row r
+ * (device fp32, nrows rows of n, no NaN) with the uniform draw u[r] (device
+ * fp32 in [0, 1); qw6 takes it from libc rand()): temp <= 0 is greedy
+ * (qw6_cpu_argmax); otherwise scores logits/temp in descending order (lower
+ * index first on ties), keep the first top_k (<= 0: all), then the shortest
+ * prefix whose probabilities reach top_p (outside (0, 1]: 1), and pick the
+ * first item whose running exp(score - max) reaches u * the kept sum -- with
+ * no sort and no copy of the logits to the host.  The sums are double, in a
+ * different order than qw6's loop: a pick can differ only when u * sum lies
+ * within rounding of a cumulative boundary. */
+int qw6cu_sample(qw6cu_ctx *ctx, const float *logits, uint32_t n, uint32_t nrows, float temp, float top_p, int top_k,
+                 const float *u, uint32_t *token);
+
 /* ---- routed MoE FFN (decode batches) ---- */
 
 /* One GGUF expert pack in the packed tile layout: expert e's matrix starts at
@@ -310,9 +325,64 @@ int qw6cu_ep_set_placement(qw6cu_ep *ep, const uint32_t *experts);
 int qw6cu_ep_layer(qw6cu_ep *ep, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
                    const qw6cu_expert_pack *down, const float *logits, const void *x_bf16, float *out,
                    uint32_t ntok);
+/* Limit of every cross-GPU wait of this endpoint's later layers, in ms
+ * (default 2000): a rank whose peer stops taking part gives up after it,
+ * records the wait kind in the context's error word (41 counts, 42 rows,
+ * 43 outputs; qw6cu_check_device_errors returns QW6CU_ERR_TIMEOUT) and skips
+ * the rest of the layer. */
+int qw6cu_ep_set_wait_limit(qw6cu_ep *ep, uint32_t ms);
 /* rows this rank's experts processed in the last layer (synchronises) */
 int qw6cu_ep_last_rows(qw6cu_ep *ep, uint32_t *rows);
 void qw6cu_ep_destroy(qw6cu_ep *ep);
+
+/* ---- GGUF files ----
+ * qw6 keeps its model in one GGUF (v3) file (qw6.c:871-1240).  These calls
+ * read its tensor table from a memory mapping of the file and upload tensors
+ * to the GPU in the layout the kernels read; they synchronize the context's
+ * stream. */
+typedef struct qw6cu_gguf qw6cu_gguf;
+typedef struct {
+    const char *name;      /* owned by the qw6cu_gguf */
+    uint32_t n_dims;
+    uint64_t dims[4];      /* dims[0] = columns (contiguous), dims[1] = rows, dims[2] = experts */
+    uint32_t ggml_type;
+    int quant;             /* qw6_quant_t of the ggml type (qw6.c:1079-1094), -1 if qw6 has none */
+    uint64_t file_offset;  /* absolute, aligned */
+    uint64_t bytes;        /* data bytes (0 for an unknown type) */
+    const void *data;      /* inside the mapping */
+} qw6cu_gguf_tensor;
+/* Parse header, metadata (general.alignment) and tensor table; every tensor
+ * of a known type must fit in the file. */
+int qw6cu_gguf_open(const char *path, qw6cu_gguf **out);
+void qw6cu_gguf_close(qw6cu_gguf *g);
+uint32_t qw6cu_gguf_tensor_count(const qw6cu_gguf *g);
+int qw6cu_gguf_tensor_info(const qw6cu_gguf *g, uint32_t i, qw6cu_gguf_tensor *info);
+/* index of the tensor called name, or -1 */
+int qw6cu_gguf_find(const qw6cu_gguf *g, const char *name);
+/* Device bytes tensor i takes uploaded (0: not uploadable): block formats in
+ * the packed tile layout, FP16/BF16 and FP32 rows as stored; a 3-D tensor
+ * [cols, rows, n] holds n matrices at a 256-byte aligned stride. */
+size_t qw6cu_gguf_upload_bytes(const qw6cu_gguf *g, uint32_t i);
+/* Upload tensor i to dst (device, 256-byte aligned, >= upload_bytes); *out
+ * receives its quant, base and per-matrix stride -- for an expert pack the
+ * qw6cu_expert_pack the MoE calls take (qw6's bind_expert_pack addressing,
+ * qw6.c:542-597, with the packed stride). */
+int qw6cu_gguf_upload(qw6cu_ctx *ctx, const qw6cu_gguf *g, uint32_t i, void *dst, size_t dst_bytes,
+                      qw6cu_expert_pack *out);
+/* The routed-expert tensors of layers 0 .. n_layers-1 (blk.L.ffn_gate_exps,
+ * ffn_up_exps, ffn_down_exps) in one device allocation, and the table of
+ * their packs: packs[3 * L + k] for k = gate, up, down, on the host and as
+ * a device array of qw6cu_expert_pack for kernels that pick a layer's packs
+ * on the GPU. */
+typedef struct {
+    uint32_t n_layers;
+    qw6cu_expert_pack *packs;  /* host [n_layers * 3] */
+    void *packs_dev;           /* device copy of packs */
+    void *weights;             /* device allocation holding every pack */
+    size_t bytes;
+} qw6cu_moe_table;
+int qw6cu_gguf_upload_moe(qw6cu_ctx *ctx, const qw6cu_gguf *g, uint32_t n_layers, qw6cu_moe_table *tab);
+void qw6cu_moe_table_free(qw6cu_moe_table *tab);
 
 /* ---- profiling ----
  * Per-launch CUDA events around every kernel this context enqueues (the
@@ -320,7 +390,7 @@ void qw6cu_ep_destroy(qw6cu_ep *ep);
  * begin: allocate events for up to max_launches launches and start
  * recording; end: synchronize, then write per-kernel-id total milliseconds
  * and launch counts into arrays of QW6CU_NKERNELS entries and stop. */
-#define QW6CU_NKERNELS 20
+#define QW6CU_NKERNELS 21
 int qw6cu_profile_begin(qw6cu_ctx *ctx, uint32_t max_launches);
 int qw6cu_profile_end(qw6cu_ctx *ctx, double *ms_total, uint32_t *launches);
 const char *qw6cu_kernel_name(int kernel_id);

@@ -44,6 +44,16 @@ class Qw6CudaError(RuntimeError):
     pass
 
 
+class GgufTensor(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("n_dims", C.c_uint32), ("dims", C.c_uint64 * 4), ("ggml_type", C.c_uint32),
+                ("quant", C.c_int), ("file_offset", C.c_uint64), ("bytes", C.c_uint64), ("data", C.c_void_p)]
+
+
+class MoeTable(C.Structure):
+    _fields_ = [("n_layers", C.c_uint32), ("packs", C.c_void_p), ("packs_dev", C.c_void_p), ("weights", C.c_void_p),
+                ("bytes", C.c_size_t)]
+
+
 def build(jobs: int = 8) -> None:
     """Compile libqw6cuda.so in-tree (sm_100a)."""
     subprocess.run(["make", "-s", f"-j{jobs}", "-C", str(CSRC)], check=True)
@@ -113,6 +123,20 @@ def load() -> C.CDLL:
     lib.qw6cu_moe_decode_hostio.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32]
     lib.qw6cu_moe_decode_noalloc.argtypes = [pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp]
     lib.qw6cu_moe_prefill.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32]
+    lib.qw6cu_gguf_open.argtypes = [C.c_char_p, C.POINTER(_vp)]
+    lib.qw6cu_gguf_close.argtypes = [_vp]
+    lib.qw6cu_gguf_close.restype = None
+    lib.qw6cu_gguf_tensor_count.argtypes = [_vp]
+    lib.qw6cu_gguf_tensor_count.restype = C.c_uint32
+    lib.qw6cu_gguf_tensor_info.argtypes = [_vp, C.c_uint32, C.POINTER(GgufTensor)]
+    lib.qw6cu_gguf_find.argtypes = [_vp, C.c_char_p]
+    lib.qw6cu_gguf_upload_bytes.argtypes = [_vp, C.c_uint32]
+    lib.qw6cu_gguf_upload_bytes.restype = _sz
+    lib.qw6cu_gguf_upload.argtypes = [_vp, _vp, C.c_uint32, _vp, _sz, C.POINTER(ExpertPack)]
+    lib.qw6cu_gguf_upload_moe.argtypes = [_vp, _vp, C.c_uint32, C.POINTER(MoeTable)]
+    lib.qw6cu_moe_table_free.argtypes = [C.POINTER(MoeTable)]
+    lib.qw6cu_moe_table_free.restype = None
+    lib.qw6cu_sample.argtypes = [_vp, _vp, _u32, _u32, C.c_float, C.c_float, C.c_int, _vp, _vp]
     lib.qw6cu_moe_block.argtypes = [_vp, _vp, _vp, _vp, pk, pk, pk, C.POINTER(SharedExpert), _vp, _u32, _u32, _u32,
                                     _u32, _u32]
     lib.qw6cu_moe_expert_rows.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32]
@@ -128,6 +152,7 @@ def load() -> C.CDLL:
     lib.qw6cu_ep_layer.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32]
     lib.qw6cu_ep_set_placement.argtypes = [_vp, _vp]
     lib.qw6cu_ep_last_rows.argtypes = [_vp, C.POINTER(_u32)]
+    lib.qw6cu_ep_set_wait_limit.argtypes = [_vp, _u32]
     lib.qw6cu_ep_destroy.argtypes = [_vp]
     lib.qw6cu_ep_destroy.restype = None
     lib.qw6cu_moe_prefill_workspace_bytes.argtypes = [_u32, _u32, _u32, _u32, _u32]
@@ -295,6 +320,11 @@ class Context:
         _check(self.lib.qw6cu_moe_decode_hostio(self.h, C.byref(gate), C.byref(up), C.byref(down), logits, x, out,
                                                 ntok, hidden, inter, n_experts, top_k), "qw6cu_moe_decode_hostio")
 
+    def sample(self, logits, n, nrows, temp, top_p, top_k, u, token):
+        """qw6cu_sample: device logits [nrows x n], device u [nrows] -> device
+        token [nrows] (uint32)."""
+        _check(self.lib.qw6cu_sample(self.h, logits, n, nrows, temp, top_p, top_k, u, token), "qw6cu_sample")
+
     def moe_block(self, x, norm_w, router, gate: ExpertPack, up: ExpertPack, down: ExpertPack,
                   shared: "SharedExpert | None", out, ntok, hidden, inter, n_experts, top_k):
         """qw6cu_moe_block: rmsnorm, fp32 router, routed experts, optional
@@ -344,7 +374,7 @@ class Context:
 
     def profile_end(self) -> dict:
         """{kernel name: (total ms, launches)} for the kernels that ran."""
-        n = 20  # QW6CU_NKERNELS
+        n = 21  # QW6CU_NKERNELS
         ms = (C.c_double * n)()
         cnt = (C.c_uint32 * n)()
         _check(self.lib.qw6cu_profile_end(self.h, ms, cnt), "qw6cu_profile_end")
@@ -391,6 +421,10 @@ class PeerEP:
         arr = (_u32 * len(experts))(*[int(e) for e in experts])
         _check(self.lib.qw6cu_ep_set_placement(self.h, arr), "qw6cu_ep_set_placement")
 
+    def set_wait_limit(self, ms: int) -> None:
+        """Give up every cross-GPU wait of later layers after `ms` ms."""
+        _check(self.lib.qw6cu_ep_set_wait_limit(self.h, ms), "qw6cu_ep_set_wait_limit")
+
     def last_rows(self) -> int:
         r = _u32()
         _check(self.lib.qw6cu_ep_last_rows(self.h, C.byref(r)), "qw6cu_ep_last_rows")
@@ -407,3 +441,59 @@ class PeerEP:
         except Exception:
             pass
 
+
+
+class Gguf:
+    """A GGUF file opened by the library (qw6cu_gguf_*): its tensor table,
+    and uploads of tensors into device memory in the kernels' layout."""
+
+    def __init__(self, path) -> None:
+        self.lib = load()
+        h = _vp()
+        _check(self.lib.qw6cu_gguf_open(str(path).encode(), C.byref(h)), "qw6cu_gguf_open")
+        self.h = h
+
+    def close(self) -> None:
+        if self.h:
+            self.lib.qw6cu_gguf_close(self.h)
+            self.h = _vp()
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __len__(self) -> int:
+        return int(self.lib.qw6cu_gguf_tensor_count(self.h))
+
+    def info(self, i: int) -> dict:
+        t = GgufTensor()
+        _check(self.lib.qw6cu_gguf_tensor_info(self.h, i, C.byref(t)), "qw6cu_gguf_tensor_info")
+        return {"name": t.name.decode(), "dims": [int(t.dims[d]) for d in range(t.n_dims)],
+                "ggml_type": int(t.ggml_type), "quant": int(t.quant), "file_offset": int(t.file_offset),
+                "bytes": int(t.bytes)}
+
+    def find(self, name: str) -> int:
+        return int(self.lib.qw6cu_gguf_find(self.h, name.encode()))
+
+    def upload_bytes(self, i: int) -> int:
+        return int(self.lib.qw6cu_gguf_upload_bytes(self.h, i))
+
+    def upload(self, ctx: "Context", i: int, dst: int, dst_bytes: int) -> ExpertPack:
+        p = ExpertPack()
+        _check(self.lib.qw6cu_gguf_upload(ctx.h, self.h, i, dst, dst_bytes, C.byref(p)), "qw6cu_gguf_upload")
+        return p
+
+    def upload_moe(self, ctx: "Context", n_layers: int) -> MoeTable:
+        t = MoeTable()
+        _check(self.lib.qw6cu_gguf_upload_moe(ctx.h, self.h, n_layers, C.byref(t)), "qw6cu_gguf_upload_moe")
+        return t
+
+    def layer_packs(self, table: MoeTable, layer: int) -> tuple:
+        arr = C.cast(table.packs, C.POINTER(ExpertPack))
+        return tuple(ExpertPack(arr[3 * layer + k].quant, arr[3 * layer + k].base, arr[3 * layer + k].stride)
+                     for k in range(3))
+
+    def free_table(self, table: MoeTable) -> None:
+        self.lib.qw6cu_moe_table_free(C.byref(table))
