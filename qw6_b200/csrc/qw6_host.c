@@ -171,7 +171,7 @@ void *qw6h_buf(qw6cu_ctx *ctx, int i, size_t bytes) {
 static const char *k_names[QW6H_K_COUNT] = {"matvec",   "pack",       "dequant",  "route",       "argmax",
                                              "moe_plan", "moe_gateup", "moe_down", "moe_combine", "lm_head",
                                              "pf_plan",  "pf_gemm1",   "pf_gemm2", "pf_combine",  "ep",
-                                             "ep_publish", "ep_dispatch", "ep_wait", "ep_combine", "moe_block"};
+                                             "ep_publish", "ep_dispatch", "ep_wait", "ep_combine", "moe_block", "sample"};
 
 _Static_assert(QW6H_K_COUNT == QW6CU_NKERNELS, "kernel-id table and public QW6CU_NKERNELS disagree");
 
@@ -325,6 +325,23 @@ int qw6cu_lm_head_argmax(qw6cu_ctx *ctx, uint32_t quant, const void *packed, con
     const int rec = qw6h_prof_a(ctx, QW6H_K_LM_HEAD);
     rc = qw6h_rc(qw6k_matvec_argmax(quant, packed, x, logits, keys, rows, cols, ntok, cols, rows, row_offset, ctx->st),
                  "lm_head_argmax");
+    qw6h_prof_b(ctx, rec);
+    return rc;
+}
+
+int qw6cu_sample(qw6cu_ctx *ctx, const float *logits, uint32_t n, uint32_t nrows, float temp, float top_p, int top_k,
+                 const float *u, uint32_t *token) {
+    int rc = qw6h_use(ctx);
+    if (rc) return rc;
+    if (!logits || !u || !token || !n || !nrows) {
+        qw6h_set_err("qw6cu_sample: invalid arguments");
+        return QW6CU_ERR_ARG;
+    }
+    const size_t wb = qw6k_sample_ws_bytes(nrows);
+    void *ws = qw6h_buf(ctx, QW6H_BUF_SAMPLE, wb);
+    if (!ws) return QW6CU_ERR_NOMEM;
+    const int rec = qw6h_prof_a(ctx, QW6H_K_SAMPLE);
+    rc = qw6h_rc(qw6k_sample(logits, n, n, nrows, temp, top_p, top_k, u, token, ws, wb, ctx->st), "sample");
     qw6h_prof_b(ctx, rec);
     return rc;
 }

@@ -17,6 +17,7 @@ enum {
     QW6H_BUF_KEY,     /* small scratch (argmax key, routing weights) */
     QW6H_BUF_WS,      /* workspace of the fused MoE / LM-head calls */
     QW6H_BUF_BLOCK,   /* intermediates of the MoE FFN block */
+    QW6H_BUF_SAMPLE,  /* per-row histograms of the sampler */
     QW6H_NBUF
 };
 
@@ -47,6 +48,7 @@ enum {
     QW6H_K_EP_WAIT,
     QW6H_K_EP_COMBINE,
     QW6H_K_MOE_BLOCK,
+    QW6H_K_SAMPLE,
     QW6H_K_COUNT
 };
 

@@ -128,6 +128,13 @@ int qw6k_block_pre(const float *x, const float *norm_w, const float *router, con
 int qw6k_block_post(const float *x, const float *ffn, const float *shared, const float *sgate, float *out,
                     uint32_t ntok, uint32_t hidden, cudaStream_t st);
 
+/* Sampling (k_sample.cu): out[r] = qw6_sample's pick (qw6.c:2904-2982) over
+ * logits row r (n floats, rows ld apart) with uniform draw u[r]; ws: device
+ * scratch of qw6k_sample_ws_bytes(nrows) bytes (zeroed here). */
+size_t qw6k_sample_ws_bytes(uint32_t nrows);
+int qw6k_sample(const float *logits, uint32_t n, uint32_t ld, uint32_t nrows, float temp, float top_p, int top_k,
+                const float *u, uint32_t *out, void *ws, size_t ws_bytes, cudaStream_t st);
+
 /* Routed MoE FFN for prefill batches on tcgen05 (k_prefill.cu): desc->x is
  * bf16 [ntok x hidden]; gate/up/down Q4_K or Q6_K packed; hidden, inter
  * multiples of 256.  Phases 0..6 in order on one stream (route, count,
@@ -181,6 +188,7 @@ typedef struct {
     int32_t *send_row;   /* [ntok*topk] row of each assignment at its owner */
     const void *x;       /* bf16 [ntok][hidden] */
     float *out;          /* fp32 [ntok][hidden] */
+    uint64_t wait_ns;    /* limit of every cross-GPU wait (0: 2 s) */
 } qw6k_ep_desc;
 /* phases: 0 publish counts + wait + plan, 1 dispatch rows + signal,
  * 2 wait for all rows, 3 signal outputs delivered, 4 wait for all outputs,
