@@ -120,14 +120,16 @@ __device__ __forceinline__ uint64_t ep_now_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
-constexpr uint64_t kEpWaitLimitNs = 2000000000ull;  // 2 s
+constexpr uint64_t kEpWaitLimitNs = 2000000000ull;  // 2 s unless the endpoint sets another limit
+
+__device__ __forceinline__ uint64_t ep_limit(const qw6k_ep_desc& d) { return d.wait_ns ? d.wait_ns : kEpWaitLimitNs; }
 
 // wait until *f has reached epoch ep (wrap-safe); false after the time limit
-__device__ bool ep_wait_flag(const uint32_t* f, uint32_t ep) {
+__device__ bool ep_wait_flag(const uint32_t* f, uint32_t ep, uint64_t limit) {
     if ((int)(ld_acquire_sys(f) - ep) >= 0) return true;
     const uint64_t t0 = ep_now_ns();
     while ((int)(ld_acquire_sys(f) - ep) < 0)
-        if (ep_now_ns() - t0 > kEpWaitLimitNs) return false;
+        if (ep_now_ns() - t0 > limit) return false;
     return true;
 }
 
@@ -139,7 +141,7 @@ __device__ __forceinline__ uint32_t* ep_sig(const qw6k_ep_desc& d, uint32_t p, i
 __device__ bool ep_wait_all(const qw6k_ep_desc& d, int kind, uint32_t ep) {
     bool ok = true;
     if (threadIdx.x < d.world) {
-        ok = ep_wait_flag(ep_sig(d, d.rank, kind, threadIdx.x), ep);
+        ok = ep_wait_flag(ep_sig(d, d.rank, kind, threadIdx.x), ep, ep_limit(d));
         if (!ok) {
             atomicExch(d.err, 41 + kind);
             atomicExch(d.abort, 1);
@@ -276,7 +278,7 @@ __global__ void __launch_bounds__(256) k_ep_publish(const qw6k_ep_desc d) {
                 ready = ready && (v[j] & 0xff000000u) == tag && (u[j] & 0xff000000u) == tag;
             }
             if (ready) break;
-            if (ep_now_ns() - t0 > kEpWaitLimitNs) {
+            if (ep_now_ns() - t0 > ep_limit(d)) {
                 ok = false;
                 break;
             }

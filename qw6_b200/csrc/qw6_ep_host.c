@@ -31,6 +31,7 @@
 
 struct qw6cu_ep {
     qw6cu_ctx *ctx;
+    uint64_t wait_ns; /* limit of the cross-GPU waits (0: the 2 s default) */
     uint32_t rank, world, ne, epr, topk, hidden, inter, max_tok, cap;
     uint8_t *region;
     size_t region_bytes, o_sig, o_cnt, o_rx, o_smeta, o_ret;
@@ -218,6 +219,15 @@ void qw6cu_ep_destroy(qw6cu_ep *ep) {
     free(ep);
 }
 
+int qw6cu_ep_set_wait_limit(qw6cu_ep *ep, uint32_t ms) {
+    if (!ep || !ms) {
+        qw6h_set_err("qw6cu_ep_set_wait_limit: invalid arguments");
+        return QW6CU_ERR_ARG;
+    }
+    ep->wait_ns = (uint64_t)ms * 1000000ull;
+    return 0;
+}
+
 int qw6cu_ep_layer(qw6cu_ep *ep, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
                    const qw6cu_expert_pack *down, const float *logits, const void *x_bf16, float *out,
                    uint32_t ntok) {
@@ -256,6 +266,7 @@ int qw6cu_ep_layer(qw6cu_ep *ep, const qw6cu_expert_pack *gate, const qw6cu_expe
     d.abort = ep->abort;
     d.done_ctas = ep->done_ctas;
     d.err = err;
+    d.wait_ns = ep->wait_ns;
     d.idx = ep->idx;
     d.w = ep->w;
     d.eslot = ep->eslot;

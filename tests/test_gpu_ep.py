@@ -170,3 +170,84 @@ def test_ep_prefill_nccl(world, case, oracle):
     ref, _, _ = oracle.moe_layer(S.Q4_K, gate, up, S.Q6_K, down, logits[toks], S.bf16_to_f32(xbits[toks]), top_k=K)
     errs = [float(np.max(np.abs(out[t] - ref[i])) / np.max(np.abs(ref[i]))) for i, t in enumerate(toks)]
     assert max(errs) <= 2e-2, max(errs)
+
+
+def _rank_skip(rank, world, port, q):
+    """Rank 1 takes part in one step, then skips the next; rank 0 runs it
+    with a 300 ms limit on its cross-GPU waits."""
+    import datetime
+    import re
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    from qw6_b200 import lib as L
+    from qw6_b200.ep import PeerMoE
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        gate, up, down, logits, xbits = _data("spread")
+        mats = ((S.Q4_K, gate, I, H), (S.Q4_K, up, I, H), (S.Q6_K, down, H, I))
+        epr, tpr = E // world, T // world
+        ctx = L.Context(rank)
+        packs, held = _pack_all(ctx, torch, L, mats, rank * epr, (rank + 1) * epr)
+        sl = slice(rank * tpr, (rank + 1) * tpr)
+        lg = torch.from_numpy(logits[sl]).cuda()
+        x = torch.from_numpy(xbits[sl].view(np.int16)).cuda().view(torch.bfloat16)
+        pm = PeerMoE(ctx, packs[0], packs[1], packs[2], E, K, H, I, tpr)
+        pm(lg, x)  # a complete step on both ranks
+        torch.cuda.synchronize()
+        ctx.check_device_errors()
+        pm.ep.set_wait_limit(300)
+        dist.barrier()
+        code, dt = 0, 0.0
+        if rank == 0:  # rank 1 launches nothing for this step
+            t0 = time.perf_counter()
+            pm(lg, x)
+            torch.cuda.synchronize()
+            dt = time.perf_counter() - t0
+            try:
+                ctx.check_device_errors()
+            except L.Qw6CudaError as e:
+                m = re.search(r"code (\d+)", str(e))
+                code = int(m.group(1)) if m else -1
+        dist.barrier()
+        pm.close()
+        del held
+        q.put((rank, code, dt))
+        ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_peer_rank_skips_a_step():
+    """Failure detection without a GPU fault: when a peer stops taking part
+    between steps, the other rank's bounded waits give up after the
+    endpoint's limit, the context reports a timeout with the wait's kind
+    (error word 41-44), the layer's later phases do nothing, and both
+    processes exit normally."""
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_skip, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in procs:
+        r, code, dt = q.get(timeout=300)
+        got[r] = (code, dt)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    code, dt = got[0]
+    assert 41 <= code <= 44, code
+    assert dt < 5.0, dt
+    assert got[1][0] == 0
