@@ -70,3 +70,35 @@ def test_noalloc_rejects_shapes_beyond_its_scratch():
     with pytest.raises(L.Qw6CudaError, match="fixed scratch"):
         L.moe_decode_noalloc(L.ExpertPack(S.Q4_K, 256, 0), L.ExpertPack(S.Q4_K, 256, 0),
                              L.ExpertPack(S.Q6_K, 256, 0), 256, 256, 256, 64, 2048, 512, 256, 8, stream=0)
+
+
+def test_noalloc_on_two_devices():
+    """Each device has its own copy of the fixed scratch: the entry point runs
+    on whichever device is current, and its kernels' per-device set-up is done
+    on first use there.  Skipped with fewer than two GPUs."""
+    torch = pytest.importorskip("torch")
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ntok, E, H, I, K = 8, 32, 2048, 512, 8
+    for d in (0, 1):
+        with torch.cuda.device(d):
+            rng = np.random.Generator(np.random.PCG64(7))
+            ctx = L.Context(d)
+            keep, (g, u, dn) = _packs(ctx, rng, E, H, I)
+            logits = dev(rng.standard_normal((ntok, E), dtype=np.float32))
+            x = dev(rng.standard_normal((ntok, H), dtype=np.float32))
+            ref = empty_f32(ntok, H)
+            sync(ctx)
+            ctx.moe_decode(g, u, dn, logits.data_ptr(), x.data_ptr(), ref.data_ptr(), ntok, H, I, E, K)
+            ctx.synchronize()
+            want = host(ref)
+            out = empty_f32(ntok, H)
+            out.fill_(float("nan"))
+            torch.cuda.synchronize()
+            L.moe_decode_noalloc(g, u, dn, logits.data_ptr(), x.data_ptr(), out.data_ptr(), ntok, H, I, E, K,
+                                 stream=0)
+            got = host(out)
+            for t in range(ntok):
+                assert rel_err(got[t], want[t]) <= TOL, (d, t)
+            del keep
+            ctx.close()
