@@ -230,8 +230,9 @@ size_t qw6cu_moe_workspace_bytes(uint32_t ntok, uint32_t hidden, uint32_t inter,
  * each expert's packed Q4_K/Q6_K rows are dequantized to bf16 tiles in shared
  * memory and multiplied against the expert's bf16 token rows (fp32
  * accumulation in TMEM); silu(g)*u is kept in bf16; the down projection
- * scatter-adds w_e * D into out with fp32 atomics (summation order of the 8
- * slots not fixed).  x_bf16: [ntok x hidden] bf16 (device); out: fp32
+ * writes every assignment's bf16 expert output and a combine sums
+ * w_e * output in slot order with fp32 fma, so results do not depend on
+ * scheduling.  x_bf16: [ntok x hidden] bf16 (device); out: fp32
  * [ntok x hidden], overwritten.  Tolerance vs the fp32 CPU composition:
  * 2e-2.  gate/up/down quant: Q4_K or Q6_K; hidden, inter multiples of 256. */
 int qw6cu_moe_prefill(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
