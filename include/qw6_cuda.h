@@ -385,6 +385,75 @@ typedef struct {
 int qw6cu_gguf_upload_moe(qw6cu_ctx *ctx, const qw6cu_gguf *g, uint32_t n_layers, qw6cu_moe_table *tab);
 void qw6cu_moe_table_free(qw6cu_moe_table *tab);
 
+/* ---- decode-step executor ----
+ * qw6's per-token forward pass (qw6_forward_token, qw6.c:2426-2500; the
+ * reference's GPU pipeline is qw6_vk_pipe_forward, qw6_vk.c:3041-3462) with
+ * every weight resident on the device and one CUDA graph per step: the
+ * embedding row, 40 (n_layers) decoder layers -- Gated DeltaNet token mixing
+ * on layers l % 4 != 3, gated GQA attention with RoPE and a KV cache on
+ * l % 4 == 3, then the MoE FFN block -- the final norm, the LM head and the
+ * greedy argmax.  Dimensions are qw6's (qw6.h:24-55): hidden 2048, 256
+ * experts (top 8, inter 512), shared expert inter 512.
+ *
+ * The model is given as a list of host tensors, raw GGUF rows as qw6's
+ * qw6_tensor_t holds them (field = the tensor's role, the fields of
+ * qw6_model_t's layers, qw6.h:126-170; layer -1 for the model-level ones).
+ * Expert packs give the first expert and the byte stride between experts
+ * (bind_expert_pack, qw6.c:542-597).  Tensors sharing one host pointer are
+ * uploaded once. */
+enum {
+    QW6CU_F_NORM = 0, QW6CU_F_POST_NORM, QW6CU_F_ATTN_Q, QW6CU_F_ATTN_K, QW6CU_F_ATTN_V, QW6CU_F_ATTN_O,
+    QW6CU_F_ATTN_Q_NORM, QW6CU_F_ATTN_K_NORM, QW6CU_F_ATTN_GATE, QW6CU_F_CONV1D, QW6CU_F_DN_OUT, QW6CU_F_DN_NORM,
+    QW6CU_F_DN_ALPHA, QW6CU_F_DN_BETA, QW6CU_F_DN_DT, QW6CU_F_DN_A, QW6CU_F_MOE_ROUTER, QW6CU_F_SHARED_ROUTER,
+    QW6CU_F_SHARED_GATE, QW6CU_F_SHARED_UP, QW6CU_F_SHARED_DOWN, QW6CU_F_EXPERT_GATE, QW6CU_F_EXPERT_UP,
+    QW6CU_F_EXPERT_DOWN,
+    QW6CU_F_TOK_EMBD = 100, QW6CU_F_OUTPUT, QW6CU_F_OUTPUT_NORM
+};
+typedef struct {
+    uint32_t field;
+    int32_t layer;         /* -1 for QW6CU_F_TOK_EMBD / OUTPUT / OUTPUT_NORM */
+    uint32_t quant;        /* qw6_quant_t */
+    uint32_t rows, cols;   /* of one matrix; vectors are one row */
+    const void *data;      /* host memory */
+    size_t stride;         /* expert packs: bytes from one expert to the next */
+} qw6cu_model_tensor;
+/* Shapes (rows x cols) it checks: norm, post_norm, output_norm 1 x 2048;
+ * DeltaNet layers: attn_q (qkv) 8192 x 2048, attn_gate (z) 4096 x 2048,
+ * dn_beta, dn_alpha 32 x 2048, dn_out 2048 x 4096, conv1d 8192 x 4 FP32,
+ * dn_dt, dn_a 1 x 32, dn_norm 1 x 128; attention layers: attn_q 8192 x 2048
+ * (q and gate per head), attn_k, attn_v 512 x 2048, attn_o 2048 x 4096,
+ * attn_q_norm, attn_k_norm 1 x 256; every layer: moe_router 256 x 2048,
+ * experts 512 x 2048 (gate, up) and 2048 x 512 (down), optional shared
+ * expert 512 x 2048, 512 x 2048, 2048 x 512 and shared_router 1 x 2048;
+ * tok_embd V' x 2048, output V x 2048 (V <= 248320 logits per step).
+ * Weight matrices: the six block formats, FP16, BF16 (FP32 for the small
+ * projections); vectors and the router: any format qw6 dequantizes. */
+typedef struct qw6cu_decoder qw6cu_decoder;
+/* Upload the model, allocate the recurrent state for positions < max_ctx,
+ * run one step to set everything up, capture the step graph and clear the
+ * state.  Synchronizes the context's stream. */
+int qw6cu_decoder_create(qw6cu_ctx *ctx, const qw6cu_model_tensor *tensors, uint32_t n_tensors, uint32_t n_layers,
+                         uint32_t max_ctx, qw6cu_decoder **out);
+/* One step: token at position pos (0 .. max_ctx-1; the DeltaNet state moves
+ * on by one token per call, as qw6's does).  logits (host, output rows
+ * floats) and greedy (host: the argmax, lowest index on ties, as
+ * qw6_cpu_argmax) are optional.  Synchronous; QW6CU_ERR_CUDA with
+ * "non-finite" in qw6cu_last_error() when the hidden state or the logits
+ * hold a NaN/Inf, as qw6's forward returns -1 (qw6.c:2457-2498). */
+int qw6cu_decoder_forward(qw6cu_decoder *dec, uint32_t token, uint32_t pos, float *logits, uint32_t *greedy);
+/* n greedy steps from token at pos with no host round trip between them
+ * (each step's argmax is the next step's token, on the device); tokens
+ * (host, n) receives the picked ids. */
+int qw6cu_decoder_generate(qw6cu_decoder *dec, uint32_t token, uint32_t pos, uint32_t n, uint32_t *tokens);
+/* Device logits of the last step (fp32, *rows of them), e.g. for
+ * qw6cu_sample. */
+const float *qw6cu_decoder_logits(qw6cu_decoder *dec, uint32_t *rows);
+/* Clear the DeltaNet states, conv windows and KV caches (a new sequence). */
+int qw6cu_decoder_reset(qw6cu_decoder *dec);
+/* Device bytes the decoder holds (weights + state + scratch). */
+size_t qw6cu_decoder_device_bytes(const qw6cu_decoder *dec);
+void qw6cu_decoder_destroy(qw6cu_decoder *dec);
+
 /* ---- profiling ----
  * Per-launch CUDA events around every kernel this context enqueues (the
  * counterpart of qw6's QW6_PROFILE timestamp queries, qw6_vk.c:2315-2357).

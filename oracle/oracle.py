@@ -23,6 +23,7 @@ REF_SO = HERE / "_ref" / "libqw6ref.so"
 _f32p = np.ctypeslib.ndpointer(np.float32, flags="C")
 _f64p = np.ctypeslib.ndpointer(np.float64, flags="C")
 _i32p = np.ctypeslib.ndpointer(np.int32, flags="C")
+_u32p = np.ctypeslib.ndpointer(np.uint32, flags="C")
 
 
 def build() -> None:
@@ -76,6 +77,9 @@ class Oracle:
         lib.qo_rmsnorm.argtypes = [_f32p, _f32p, _f32p, C.c_uint32]
         lib.qo_rmsnorm.restype = None
         lib.qo_sample.argtypes = [_f32p, C.c_uint32, C.c_float, C.c_float, C.c_int, C.c_float]
+        lib.qo_fwd_state_floats.argtypes = [C.c_uint32, C.c_uint32]
+        lib.qo_fwd_state_floats.restype = C.c_size_t
+        lib.qo_forward.argtypes = [C.c_void_p, _f32p, C.c_uint32, C.c_uint32, C.c_uint32, _f32p]
         lib.qo_sample.restype = C.c_int32
         mp = C.POINTER(_Matrix)
         lib.qo_moe_block.argtypes = [_f32p, _f32p, mp, pk, pk, pk, mp, mp, mp, mp, _f32p, C.c_uint32, C.c_uint32,
@@ -180,6 +184,11 @@ class Oracle:
         arr = _u8(arr)
         return _ExpertPack(quant, arr.ctypes.data, arr[0].nbytes), arr
 
+    def forward(self, model, tokens, max_ctx=None):
+        """qo_forward (qw6_forward_token, qw6.c:2426-2500) over tokens at
+        positions 0.. from a cleared state: [n, model.vocab] logits."""
+        return _forward_oracle(self.lib, model, tokens, max_ctx or len(tokens))
+
     def sample(self, logits, temp, top_p, top_k, u):
         """qw6_sample (qw6.c:2921-2982) with its uniform draw u given."""
         logits = np.ascontiguousarray(logits, np.float32)
@@ -254,6 +263,77 @@ class Oracle:
         return out, idx, w
 
 
+class _Tensor(C.Structure):
+    _fields_ = [("quant", C.c_uint32), ("rows", C.c_uint32), ("cols", C.c_uint32), ("data", C.c_void_p),
+                ("stride", C.c_size_t)]
+
+
+class _Model(C.Structure):
+    _fields_ = [("n_layers", C.c_uint32), ("tok_embd", _Tensor), ("output", _Tensor), ("output_norm", _Tensor),
+                ("layers", C.c_void_p)]
+
+
+N_FIELDS = 24  # per-layer roles (QO_F_* / QW6CU_F_*)
+
+
+def _forward_oracle(lib, model, tokens, max_ctx):
+    """qo_forward over tokens at positions 0.. (fresh state): [n, vocab] logits."""
+    layers = (_Tensor * (model.n_layers * N_FIELDS))()
+    glob = {}
+    for f, l, q, r, c, arr, stride in model.tensors:
+        t = _Tensor(q, r, c, arr.ctypes.data, stride)
+        if l < 0:
+            glob[f] = t
+        else:
+            layers[l * N_FIELDS + f] = t
+    m = _Model(model.n_layers, glob[100], glob[101], glob[102], C.cast(layers, C.c_void_p))
+    state = np.zeros(lib.qo_fwd_state_floats(model.n_layers, max_ctx), np.float32)
+    out = np.zeros((len(tokens), model.vocab), np.float32)
+    for pos, tok in enumerate(tokens):
+        if lib.qo_forward(C.byref(m), state, max_ctx, int(tok), pos, out[pos]):
+            raise ValueError(f"qo_forward failed at position {pos}")
+    return out
+
+
+class _RefModel:
+    """A qw6_model_t built by the shim of a reference library from a model's
+    tensors (which must outlive it)."""
+
+    def __init__(self, lib, model):
+        self.lib, self.model = lib, model
+        self.h = lib.ref_model_new()
+        for f, l, q, r, c, arr, stride in model.tensors:
+            if lib.ref_model_set(self.h, l, f, q, r, c, arr.ctypes.data, stride):
+                raise ValueError(f"ref_model_set rejected field {f} layer {l}")
+
+    def close(self):
+        if self.h:
+            self.lib.ref_model_free(self.h)
+            self.h = None
+
+
+def _bind_model_shim(lib):
+    lib.ref_model_new.restype = C.c_void_p
+    lib.ref_model_set.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_uint32, C.c_uint32, C.c_void_p,
+                                  C.c_size_t]
+    lib.ref_model_free.argtypes = [C.c_void_p]
+    lib.ref_forward.argtypes = [C.c_void_p, _u32p, C.c_uint32, _f32p, C.c_uint32, C.c_int]
+
+
+def _ref_forward(lib, model, tokens, use_pipe=False):
+    """qw6_prefill one token at a time through qw6's session (qw6.c:2867-2882)."""
+    tok = np.ascontiguousarray(tokens, np.uint32)
+    out = np.zeros((tok.size, model.vocab), np.float32)
+    rm = _RefModel(lib, model)
+    try:
+        rc = lib.ref_forward(rm.h, tok, tok.size, out, model.vocab, int(use_pipe))
+    finally:
+        rm.close()
+    if rc:
+        raise ValueError("qw6's forward pass returned an error")
+    return out
+
+
 class Reference:
     """qw6's own CPU functions, compiled from its sources (oracle/_ref)."""
 
@@ -282,8 +362,16 @@ class Reference:
         lib.ref_moe_tokens.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_size_t, C.c_int, C.c_void_p, C.c_size_t,
                                        C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32,
                                        C.c_uint32, C.c_int, C.c_int]
+        _bind_model_shim(lib)
         self.lib = lib
         self.vocab = int(lib.ref_vocab_size())
+
+    def forward(self, model, tokens):
+        """qw6's CPU forward pass (qw6_forward_token, qw6.c:2426-2500) over
+        tokens at positions 0..: [n, model.vocab] logits.  qw6 runs its 40
+        layers, so the model must have 40."""
+        assert model.n_layers == 40
+        return _ref_forward(self.lib, model, tokens)
 
     def dequantize(self, quant, w, rows, cols):
         w = _u8(w)
@@ -418,3 +506,42 @@ def cpu_count() -> int:
         return len(os.sched_getaffinity(0))
     except AttributeError:  # pragma: no cover
         return os.cpu_count() or 1
+
+
+VK_SO = HERE / "_ref" / "libqw6vk.so"
+
+
+class VkReference:
+    """qw6.c built with QW6_VULKAN against include/qw6_vk.h and linked with
+    libqw6cuda.so (oracle/_ref/libqw6vk.so): qw6's own session and forward
+    pass, on its CPU path or through the qw6_vk_pipe_* entry points that this
+    library provides (qw6_forward_token's pipeline branch, qw6.c:2429-2445)."""
+
+    @staticmethod
+    def available() -> bool:
+        return VK_SO.exists()
+
+    def __init__(self) -> None:
+        lib = C.CDLL(str(VK_SO))
+        _bind_model_shim(lib)
+        lib.ref_pipe_greedy.argtypes = [C.c_void_p, _u32p, C.c_uint32, _u32p, C.c_void_p, C.c_uint32]
+        self.lib = lib
+
+    def forward(self, model, tokens, use_pipe: bool):
+        assert model.n_layers == 40
+        return _ref_forward(self.lib, model, tokens, use_pipe)
+
+    def pipe_greedy(self, model, tokens, with_logits=True):
+        """qw6_vk_pipe_forward_greedy per token: (picked ids, logits or None)."""
+        tok = np.ascontiguousarray(tokens, np.uint32)
+        picked = np.zeros(tok.size, np.uint32)
+        out = np.zeros((tok.size, model.vocab), np.float32) if with_logits else None
+        rm = _RefModel(self.lib, model)
+        try:
+            rc = self.lib.ref_pipe_greedy(rm.h, tok, tok.size, picked, out.ctypes.data if with_logits else None,
+                                          model.vocab)
+        finally:
+            rm.close()
+        if rc:
+            raise ValueError("qw6_vk_pipe_forward_greedy failed")
+        return picked, out

@@ -145,6 +145,44 @@ int qo_moe_block_f64(const float *x, const float *norm_w, const qo_matrix *route
  * exp(score - max) reaches u * (sum over the kept prefix). */
 int32_t qo_sample(const float *logits, uint32_t n, float temp, float top_p, int top_k, float u);
 
+/* ---- the per-token forward pass (qw6_forward_token, qw6.c:2426-2500) ----
+ * One tensor of qw6's model as qw6_tensor_t carries it: raw GGUF rows of
+ * `cols` values (quant = qw6_quant_t), `rows` of them; for the expert packs
+ * expert e's matrix starts at data + e * stride (bind_expert_pack,
+ * qw6.c:542-597).  Vectors (norm weights, dt bias, a) are one row. */
+typedef struct {
+    uint32_t quant, rows, cols;
+    const void *data;
+    size_t stride;
+} qo_tensor;
+
+/* Per-layer tensors, in the roles of qw6_model_t's layer fields (qw6.h:126-170);
+ * the linear-attention layers keep their qkv projection in ATTN_Q and the
+ * output gate z in ATTN_GATE, as qw6's GGUF binding does (qw6.c:599-680). */
+enum {
+    QO_F_NORM = 0, QO_F_POST_NORM, QO_F_ATTN_Q, QO_F_ATTN_K, QO_F_ATTN_V, QO_F_ATTN_O, QO_F_ATTN_Q_NORM,
+    QO_F_ATTN_K_NORM, QO_F_ATTN_GATE, QO_F_CONV1D, QO_F_DN_OUT, QO_F_DN_NORM, QO_F_DN_ALPHA, QO_F_DN_BETA,
+    QO_F_DN_DT, QO_F_DN_A, QO_F_MOE_ROUTER, QO_F_SHARED_ROUTER, QO_F_SHARED_GATE, QO_F_SHARED_UP,
+    QO_F_SHARED_DOWN, QO_F_EXPERT_GATE, QO_F_EXPERT_UP, QO_F_EXPERT_DOWN, QO_NF
+};
+#define QO_FWD_HIDDEN 2048
+
+typedef struct {
+    uint32_t n_layers;       /* qw6 runs 40; layer l is full attention when l % 4 == 3 */
+    qo_tensor tok_embd, output, output_norm;
+    const qo_tensor *layers; /* [n_layers][QO_NF] */
+} qo_model;
+
+int qo_fwd_is_full(uint32_t layer);
+/* floats of the recurrent state of n_layers layers: per DeltaNet layer its
+ * [32][128][128] state and [4][8192] conv window, per attention layer its
+ * key and value caches of max_ctx positions ([max_ctx][2][256] each);
+ * zero it before position 0 */
+size_t qo_fwd_state_floats(uint32_t n_layers, uint32_t max_ctx);
+/* logits[output.rows] of token at position pos; -1 on bad input or, as qw6,
+ * on a NaN/Inf in the hidden state or the logits */
+int qo_forward(const qo_model *m, float *state, uint32_t max_ctx, uint32_t token, uint32_t pos, float *logits);
+
 #ifdef __cplusplus
 }
 #endif

@@ -13,10 +13,14 @@
  * The shim only wraps raw block bytes in a qw6_tensor_t and validates
  * arguments first, because the reference asserts (exit(1)) on bad input.
  */
+#include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 
 #include "qw6.h"
+#ifdef QW6_VULKAN
+#include "qw6_vk.h"
+#endif
 
 static int block_ok(int quant, uint32_t cols) {
     switch (quant) {
@@ -149,3 +153,136 @@ int ref_moe_tokens(int gq, const void *gate, const void *up, size_t gstride, int
     free(tmp);
     return rc;
 }
+
+/* ---- a qw6_model_t for qw6's own forward pass ----
+ * ref_model_set fills one tensor of a calloc'd qw6_model_t from raw GGUF
+ * bytes (field ids: the per-layer roles of oracle/qw6_oracle.h's QO_F_*,
+ * then 100/101/102 for token_embd/output/output_norm; the expert packs set
+ * all QW6_NUM_EXPERTS tensors at data + e * stride, as bind_expert_pack
+ * does, qw6.c:542-597).  ref_forward runs qw6_prefill (qw6.c:2867-2882)
+ * one token at a time on a fresh session -- qw6's CPU forward pass, or, in
+ * the library built with QW6_VULKAN, qw6_forward_token's pipeline branch
+ * (qw6.c:2429-2445) after qw6_vk_pipe_init -- and copies out_rows logits
+ * after every token. */
+static qw6_tensor_t *model_field(qw6_model_t *m, int layer, int field) {
+    if (field == 100) return &m->tok_embeddings;
+    if (field == 101) return &m->output;
+    if (field == 102) return &m->output_norm;
+    if (layer < 0 || layer >= QW6_NUM_LAYERS) return NULL;
+    switch (field) {
+    case 0: return &m->layers[layer].norm;
+    case 1: return &m->layers[layer].post_norm;
+    case 2: return &m->layers[layer].attn_q;
+    case 3: return &m->layers[layer].attn_k;
+    case 4: return &m->layers[layer].attn_v;
+    case 5: return &m->layers[layer].attn_o;
+    case 6: return &m->layers[layer].attn_q_norm;
+    case 7: return &m->layers[layer].attn_k_norm;
+    case 8: return &m->layers[layer].attn_gate;
+    case 9: return &m->layers[layer].conv1d;
+    case 10: return &m->layers[layer].dn_out;
+    case 11: return &m->layers[layer].dn_norm;
+    case 12: return &m->layers[layer].dn_alpha;
+    case 13: return &m->layers[layer].dn_beta;
+    case 14: return &m->layers[layer].dn_dt;
+    case 15: return &m->layers[layer].dn_a;
+    case 16: return &m->layers[layer].moe_router;
+    case 17: return &m->layers[layer].shared_router;
+    case 18: return &m->layers[layer].shared_gate;
+    case 19: return &m->layers[layer].shared_up;
+    case 20: return &m->layers[layer].shared_down;
+    case 21: return m->layers[layer].expert_gate;
+    case 22: return m->layers[layer].expert_up;
+    case 23: return m->layers[layer].expert_down;
+    default: return NULL;
+    }
+}
+
+void *ref_model_new(void) {
+    qw6_model_t *m = calloc(1, sizeof(qw6_model_t));
+    if (m) {
+        m->weight_fd = -1;
+        m->max_context = QW6_DEFAULT_CTX;
+    }
+    return m;
+}
+
+int ref_model_set(void *model, int layer, int field, int quant, uint32_t rows, uint32_t cols, const void *data,
+                  size_t stride) {
+    qw6_model_t *m = model;
+    qw6_tensor_t *t = m ? model_field(m, layer, field) : NULL;
+    if (!t || !data || !rows || !block_ok(quant, cols)) return -1;
+    const int n = (field >= 21 && field <= 23) ? QW6_NUM_EXPERTS : 1;
+    for (int e = 0; e < n; e++) {
+        wrap(&t[e], quant, (const uint8_t *)data + (size_t)e * stride, rows, cols);
+        t[e].ne[0] = cols;
+        t[e].ne[1] = rows;
+        t[e].n_dims = rows > 1 ? 2 : 1;
+        snprintf(t[e].name, sizeof t[e].name, "f%d.l%d.e%d", field, layer, e);
+#ifdef QW6_VULKAN
+        t[e].vk_offset = (size_t)-1;
+#endif
+    }
+    return 0;
+}
+
+static void model_states_free(qw6_model_t *m) {
+    for (int l = 0; l < QW6_NUM_LAYERS; l++) {
+        free(m->deltanet_state[l]);
+        free(m->k_cache[l]);
+        free(m->v_cache[l]);
+        m->deltanet_state[l] = m->k_cache[l] = m->v_cache[l] = NULL;
+    }
+}
+
+void ref_model_free(void *model) {
+    if (!model) return;
+    model_states_free(model);
+    free(model);
+}
+
+int ref_forward(void *model, const uint32_t *tokens, uint32_t n, float *logits, uint32_t out_rows, int use_pipe) {
+    qw6_model_t *m = model;
+    if (!m || !tokens || !n || !logits || out_rows > QW6_VOCAB_SIZE) return -1;
+#ifndef QW6_VULKAN
+    if (use_pipe) return -1;
+#endif
+    qw6_session_t s;
+    if (qw6_session_init(&s, m, n, use_pipe != 0) != 0) return -1;
+    int rc = 0;
+#ifdef QW6_VULKAN
+    if (use_pipe) rc = qw6_vk_pipe_init((qw6_vk_pipe_t **)&s.vk_pipe, m, true);
+#endif
+    for (uint32_t i = 0; i < n && rc == 0; i++) {
+        rc = qw6_prefill(&s, tokens + i, 1);
+        if (rc == 0) memcpy(logits + (size_t)i * out_rows, s.logits, (size_t)out_rows * sizeof(float));
+    }
+#ifdef QW6_VULKAN
+    if (s.vk_pipe) qw6_vk_pipe_free(s.vk_pipe);
+    s.vk_pipe = NULL;
+#endif
+    qw6_session_free(&s);
+    model_states_free(m);
+    return rc;
+}
+
+#ifdef QW6_VULKAN
+/* qw6_vk_pipe_forward_greedy over the tokens: the picked id after each and,
+ * when logits is given, the logits the call returns with it */
+int ref_pipe_greedy(void *model, const uint32_t *tokens, uint32_t n, uint32_t *picked, float *logits,
+                    uint32_t out_rows) {
+    qw6_model_t *m = model;
+    if (!m || !tokens || !n || !picked || out_rows > QW6_VOCAB_SIZE) return -1;
+    qw6_vk_pipe_t *p = NULL;
+    if (qw6_vk_pipe_init(&p, m, true) != 0) return -1;
+    float *buf = logits ? calloc(QW6_VOCAB_SIZE, sizeof(float)) : NULL;
+    int rc = (logits && !buf) ? -1 : 0;
+    for (uint32_t i = 0; i < n && rc == 0; i++) {
+        rc = qw6_vk_pipe_forward_greedy(p, m, tokens[i], i, &picked[i], buf);
+        if (rc == 0 && logits) memcpy(logits + (size_t)i * out_rows, buf, (size_t)out_rows * sizeof(float));
+    }
+    free(buf);
+    qw6_vk_pipe_free(p);
+    return rc;
+}
+#endif

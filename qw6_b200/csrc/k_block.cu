@@ -16,33 +16,20 @@
 #include "qw6_dev.cuh"
 #include "qw6_devcfg.cuh"
 #include "qw6_launch.h"
+#include "qw6_norm.cuh"
 
 namespace qw6 {
 
 constexpr int kBlkThreads = 256;
-constexpr float kRmsEps = 1e-6f;  // QW6_RMS_EPS (qw6.h:67)
-
-// 1 / sqrt(sum(x^2)/dim + eps) for token row x (every thread gets it).
-// The sum is a block reduction (qw6 sums sequentially; the difference is fp32
-// rounding of the sum), the rest is qw6's expression with IEEE operations.
-__device__ float rms_inv(const float* __restrict__ x, int dim, float* red) {
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < dim; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-    __syncthreads();
-    float t = 0.f;
-    for (int w = 0; w < (int)(blockDim.x >> 5); w++) t += red[w];
-    __syncthreads();
-    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)dim), kRmsEps)));
-}
 
 // grid (ceil(ne / 8), ntok): CTA (b, t) computes router rows [8b, 8b+8) of
 // token t (warp per row), CTA (0, t) also writes normed[t], and the last CTA
 // of the token the shared-expert gate sigmoid(shared_router . normed).
-// normed[i] = (x[i] * inv) * w[i] as qw6 evaluates it.
-__global__ void __launch_bounds__(kBlkThreads) k_block_pre(const float* __restrict__ x,
+// normed[i] = (x[i] * inv) * w[i] as qw6 evaluates it.  With `add` the block
+// input is x + add (the residual add before the FFN, qw6.c:2469-2470), which
+// CTA (0, t) stores to xsum and checks for NaN/Inf (sets *bad, qw6.c:2472).
+__global__ void __launch_bounds__(kBlkThreads) k_block_pre(const float* __restrict__ x, const float* __restrict__ add,
+                                                           float* __restrict__ xsum, int* __restrict__ bad,
                                                            const float* __restrict__ norm_w,
                                                            const float* __restrict__ router,
                                                            const float* __restrict__ srouter, float* __restrict__ normed,
@@ -52,10 +39,23 @@ __global__ void __launch_bounds__(kBlkThreads) k_block_pre(const float* __restri
     __shared__ float red[kBlkThreads / 32];
     const int t = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float* xt = x + (size_t)t * hidden;
+    if (add) {  // x + add into shared memory first, then the norm of the sum
+        const float* at = add + (size_t)t * hidden;
+        bool finite = true;
+        for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+            const float v = __fadd_rn(xt[i], at[i]);
+            nrm[i] = v;
+            finite = finite && isfinite(v);
+            if (blockIdx.x == 0) xsum[(size_t)t * hidden + i] = v;
+        }
+        if (!finite && blockIdx.x == 0 && bad) atomicOr(bad, 1);
+        __syncthreads();
+        xt = nrm;
+    }
     const float inv = rms_inv(xt, hidden, red);
     for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
         const float v = __fmul_rn(__fmul_rn(xt[i], inv), norm_w[i]);
-        nrm[i] = v;
+        nrm[i] = v;  // each thread rewrites only the entries it read
         if (blockIdx.x == 0) normed[(size_t)t * hidden + i] = v;
     }
     __syncthreads();
@@ -88,40 +88,46 @@ __global__ void __launch_bounds__(kBlkThreads) k_block_pre(const float* __restri
 }
 
 // out[t][i] = x[t][i] + (ffn[t][i] + s[t] * sh[t][i])  (sh may be null: no
-// shared expert), each operation rounded once as qw6's loops do.
+// shared expert), each operation rounded once as qw6's loops do; a NaN/Inf
+// in out sets *bad (qw6.c:2485-2487).
 __global__ void k_block_post(const float* __restrict__ x, const float* __restrict__ ffn, const float* __restrict__ sh,
-                             const float* __restrict__ sgate, float* __restrict__ out, int hidden, long long n) {
+                             const float* __restrict__ sgate, float* __restrict__ out, int* __restrict__ bad,
+                             int hidden, long long n) {
+    bool finite = true;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
         float f = ffn[i];
         if (sh) f = __fadd_rn(f, __fmul_rn(sgate[i / hidden], sh[i]));
-        out[i] = __fadd_rn(x[i], f);
+        const float o = __fadd_rn(x[i], f);
+        out[i] = o;
+        finite = finite && isfinite(o);
     }
+    if (!finite && bad) atomicOr(bad, 1);
 }
 
 }  // namespace qw6
 
 using namespace qw6;
 
-extern "C" int qw6k_block_pre(const float* x, const float* norm_w, const float* router, const float* srouter,
-                              float* normed, float* logits, float* sgate, uint32_t ntok, uint32_t hidden, uint32_t ne,
-                              cudaStream_t st) {
+extern "C" int qw6k_block_pre(const float* x, const float* add, float* xsum, int* bad, const float* norm_w,
+                              const float* router, const float* srouter, float* normed, float* logits, float* sgate,
+                              uint32_t ntok, uint32_t hidden, uint32_t ne, cudaStream_t st) {
     if (!x || !norm_w || !router || !normed || !logits || !sgate || !ntok || ntok > 65535 || !hidden ||
-        hidden % 4 || hidden > 16384 || !ne || ne > 256)
+        hidden % 4 || hidden > 16384 || !ne || ne > 256 || (add && !xsum))
         return QW6K_ERR_ARG;
     if ((reinterpret_cast<uintptr_t>(router) | reinterpret_cast<uintptr_t>(x)) & 15u) return QW6K_ERR_ALIGN;
     static DevFlags cfg;
     if (hidden * 4 > 48 * 1024 && smem_optin(cfg, k_block_pre, (int)hidden * 4)) return QW6K_ERR_CUDA;
     const dim3 grid((ne + kBlkThreads / 32 - 1) / (kBlkThreads / 32), ntok);
-    k_block_pre<<<grid, kBlkThreads, (size_t)hidden * 4, st>>>(x, norm_w, router, srouter, normed, logits, sgate,
-                                                               (int)hidden, (int)ne);
+    k_block_pre<<<grid, kBlkThreads, (size_t)hidden * 4, st>>>(x, add, xsum, bad, norm_w, router, srouter, normed,
+                                                               logits, sgate, (int)hidden, (int)ne);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
 }
 
 extern "C" int qw6k_block_post(const float* x, const float* ffn, const float* shared, const float* sgate, float* out,
-                               uint32_t ntok, uint32_t hidden, cudaStream_t st) {
+                               int* bad, uint32_t ntok, uint32_t hidden, cudaStream_t st) {
     if (!x || !ffn || !out || !ntok || !hidden || (shared && !sgate)) return QW6K_ERR_ARG;
     const long long n = (long long)ntok * hidden;
     const int grid = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
-    k_block_post<<<grid, 256, 0, st>>>(x, ffn, shared, sgate, out, (int)hidden, n);
+    k_block_post<<<grid, 256, 0, st>>>(x, ffn, shared, sgate, out, bad, (int)hidden, n);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
 }

@@ -1,0 +1,355 @@
+// k_fwd.cu -- the token-mixing halves of qw6's decoder layers on the GPU, for
+// the decode-step executor (qw6_decoder.c).  One token per step; the step's
+// token id and position are read from device memory (qw6k_step), so a whole
+// step is position-independent and is captured once in a CUDA graph.
+//
+// Gated DeltaNet layer (qw6_apply_linear_attn, qw6.c:2292-2360), after the
+// projections [qkv 8192 | z 4096 | beta 32 | alpha 32] of the normalised row:
+//   k_dn_conv  slide the 4-tap conv window, conv + silu per channel,
+//              l2-normalise the 16 query and 16 key heads (qw6.c:2055-2063),
+//              beta = sigmoid(beta), g = softplus(alpha + dt) * a;
+//   k_dn_step  per value head vh (key head vh % 16, qw6.c:2084): for every
+//              state row j: row *= exp(g); pred = row . k;
+//              row += (v[j] - pred) * beta * k; o[j] = (row . q) / sqrt(128)
+//              (qw6_gated_delta_net_single, qw6.c:2079-2108), then
+//              rmsnorm(o) * silu(z) (qw6.c:2349-2355).
+// Gated attention layer (qw6_apply_full_attn, qw6.c:2368-2424), after the
+// projections [q|gate per head: 16 x 512 | k 512 | v 512]:
+//   k_fa_prep     rmsnorm per head with q_norm / k_norm, RoPE on the first 64
+//                 dimensions of each head (adjacent pairs, qw6_cpu_mrope,
+//                 qw6.c:2711-2745), k and v into the caches at pos;
+//   k_fa_attn     split-sequence attention of each query head over the pos+1
+//                 cached positions of its key/value head (8 query heads per
+//                 kv head): per chunk the max score, the sum of exp and the
+//                 exp-weighted sum of values;
+//   k_fa_combine  merge the chunks (qw6_cpu_attention_gqa's softmax,
+//                 qw6.c:2750-2793) and gate with sigmoid(gate) (qw6.c:2419).
+// Element-wise steps use qw6's operations in its order with IEEE rounding
+// (__fmul_rn, __fadd_rn, ...: no contraction); dot products and sums are
+// reductions in another order than qw6's sequential loops.
+#include <cuda_runtime.h>
+
+#include "qw6_launch.h"
+#include "qw6_norm.cuh"
+
+namespace qw6 {
+
+constexpr int kQH = 16, kKVH = 2, kHD = 256;     // attention heads (qw6.h:29-31)
+constexpr int kKH = 16, kKD = 128;               // DeltaNet key heads (qw6.h:34-35)
+constexpr int kVH = 32, kVD = 128;               // DeltaNet value heads (qw6.h:36-37)
+constexpr int kQKV = kKH * kKD * 2 + kVH * kVD;  // 8192
+constexpr int kVDim = kVH * kVD;                 // 4096
+constexpr int kRot = 64;                         // (int)(256 * 0.25f) rotary dims
+constexpr int kFaSplit = QW6K_FA_SPLIT;          // sequence chunks per kv head
+
+__device__ __forceinline__ float silu_f(float v) { return __fdiv_rn(v, __fadd_rn(1.0f, expf(-v))); }
+__device__ __forceinline__ float sigmoid_f(float v) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v))); }
+__device__ __forceinline__ float softplus_f(float v) {  // qw6_softplus, qw6.h:298-302
+    if (v > 20.0f) return v;
+    if (v < -20.0f) return expf(v);
+    return log1pf(expf(v));
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// out = rmsnorm(x) * w as qw6_cpu_rmsnorm evaluates it; one CTA.
+__global__ void __launch_bounds__(256) k_rmsnorm(const float* __restrict__ x, const float* __restrict__ w,
+                                                 float* __restrict__ out, int dim) {
+    __shared__ float red[8];
+    const float inv = rms_inv(x, dim, red);
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(x[i], inv), w[i]);
+}
+
+// grid 64 x 128 threads: CTA b owns channels [128 b, 128 b + 128) of the conv
+// (b < 16: query head b, b < 32: key head b - 16, else values).
+__global__ void __launch_bounds__(128) k_dn_conv(const float* __restrict__ proj, float* __restrict__ cs,
+                                                 const float* __restrict__ cw, const float* __restrict__ dt,
+                                                 const float* __restrict__ a, float* __restrict__ conv,
+                                                 float* __restrict__ gb) {
+    __shared__ float red[4];
+    const int c = blockIdx.x * 128 + threadIdx.x;
+    // the window holds the 4 latest qkv rows, oldest first (qw6.c:2327-2331)
+    const float s0 = cs[1 * kQKV + c], s1 = cs[2 * kQKV + c], s2 = cs[3 * kQKV + c], s3 = proj[c];
+    cs[c] = s0;
+    cs[1 * kQKV + c] = s1;
+    cs[2 * kQKV + c] = s2;
+    cs[3 * kQKV + c] = s3;
+    const float4 w = reinterpret_cast<const float4*>(cw)[c];
+    float sum = __fmul_rn(s0, w.x);
+    sum = __fadd_rn(sum, __fmul_rn(s1, w.y));
+    sum = __fadd_rn(sum, __fmul_rn(s2, w.z));
+    sum = __fadd_rn(sum, __fmul_rn(s3, w.w));
+    float v = silu_f(sum);
+    if (blockIdx.x < 2 * kKH) {  // l2 norm of a query or key head
+        const float ss = block_sum(v * v, red);
+        v = __fmul_rn(v, __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss, kRmsEps))));
+    }
+    conv[c] = v;
+    if (blockIdx.x == 0 && threadIdx.x < kVH) {
+        const int h = threadIdx.x;
+        gb[h] = sigmoid_f(proj[kQKV + kVDim + h]);
+        gb[kVH + h] = __fmul_rn(softplus_f(__fadd_rn(proj[kQKV + kVDim + kVH + h], dt[h])), a[h]);
+    }
+}
+
+// grid 32 (value heads) x 512 threads; warp w updates state rows [8w, 8w + 8).
+__global__ void __launch_bounds__(512) k_dn_step(const float* __restrict__ conv, const float* __restrict__ gb,
+                                                 const float* __restrict__ z, const float* __restrict__ nw,
+                                                 float* __restrict__ state, float* __restrict__ gated) {
+    __shared__ float o[kVD];
+    __shared__ float red[16];
+    const int vh = blockIdx.x, kh = vh % kKH, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float4 k4 = reinterpret_cast<const float4*>(conv + kKH * kKD + kh * kKD)[lane];
+    const float4 q4 = reinterpret_cast<const float4*>(conv + kh * kKD)[lane];
+    const float* v = conv + 2 * kKH * kKD + vh * kVD;
+    const float b = gb[vh], decay = expf(gb[kVH + vh]);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)kVD));
+    float4* s = reinterpret_cast<float4*>(state + (size_t)vh * kVD * kVD);
+    float4 row[8];
+#pragma unroll
+    for (int r = 0; r < 8; r++) row[r] = s[(warp * 8 + r) * (kVD / 4) + lane];
+#pragma unroll
+    for (int r = 0; r < 8; r++) {
+        const int j = warp * 8 + r;
+        float4 x = row[r];
+        x.x = __fmul_rn(x.x, decay);
+        x.y = __fmul_rn(x.y, decay);
+        x.z = __fmul_rn(x.z, decay);
+        x.w = __fmul_rn(x.w, decay);
+        const float pred = warp_sum(fmaf(x.w, k4.w, fmaf(x.z, k4.z, fmaf(x.y, k4.y, x.x * k4.x))));
+        const float delta = __fmul_rn(__fsub_rn(v[j], pred), b);
+        x.x = __fadd_rn(x.x, __fmul_rn(delta, k4.x));
+        x.y = __fadd_rn(x.y, __fmul_rn(delta, k4.y));
+        x.z = __fadd_rn(x.z, __fmul_rn(delta, k4.z));
+        x.w = __fadd_rn(x.w, __fmul_rn(delta, k4.w));
+        s[j * (kVD / 4) + lane] = x;
+        const float sum = warp_sum(fmaf(x.w, q4.w, fmaf(x.z, q4.z, fmaf(x.y, q4.y, x.x * q4.x))));
+        if (lane == 0) o[j] = __fmul_rn(sum, scale);
+    }
+    __syncthreads();
+    const int i = threadIdx.x;
+    const float oi = i < kVD ? o[i] : 0.f;
+    const float ss = block_sum(oi * oi, red);
+    if (i < kVD) {
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)kVD), kRmsEps)));
+        const float y = __fmul_rn(__fmul_rn(oi, inv), nw[i]);
+        gated[vh * kVD + i] = __fmul_rn(y, silu_f(z[vh * kVD + i]));
+    }
+}
+
+// grid 18 x 256: CTAs 0-15 the query heads, 16-17 the key/value heads.
+// freq[i/2] = powf(1e7, i / 64) for even i < 64, computed by the host's libm
+// as qw6 computes it, so that theta = pos / freq is qw6's value.
+__global__ void __launch_bounds__(256) k_fa_prep(const float* __restrict__ proj, const float* __restrict__ qn,
+                                                 const float* __restrict__ kn, const float* __restrict__ freq,
+                                                 const qw6k_step* __restrict__ step, float* __restrict__ kc,
+                                                 float* __restrict__ vc, float* __restrict__ qr) {
+    __shared__ float y[kHD];
+    __shared__ float red[8];
+    const int h = blockIdx.x, d = threadIdx.x;
+    const uint32_t pos = step->pos;
+    const bool isq = h < kQH;
+    const int kvh = h - kQH;
+    const float x = isq ? proj[h * 2 * kHD + d] : proj[kQH * 2 * kHD + kvh * kHD + d];
+    const float ss = block_sum(x * x, red);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)kHD), kRmsEps)));
+    float val = __fmul_rn(__fmul_rn(x, inv), isq ? qn[d] : kn[d]);
+    y[d] = val;
+    __syncthreads();
+    if (d < kRot) {
+        const int i = d & ~1;
+        const float theta = __fdiv_rn((float)pos, freq[i >> 1]);
+        const float c = cosf(theta), sn = sinf(theta), av = y[i], bv = y[i + 1];
+        val = (d & 1) ? __fadd_rn(__fmul_rn(av, sn), __fmul_rn(bv, c)) : __fsub_rn(__fmul_rn(av, c), __fmul_rn(bv, sn));
+    }
+    if (isq) {
+        qr[h * kHD + d] = val;
+    } else {
+        const size_t slot = ((size_t)pos * kKVH + kvh) * kHD + d;
+        kc[slot] = val;
+        vc[slot] = proj[kQH * 2 * kHD + kKVH * kHD + kvh * kHD + d];
+    }
+}
+
+// positions [c0, c1) of chunk blockIdx.x for the current sequence length
+__device__ __forceinline__ void fa_chunk(uint32_t seq, int c, uint32_t& c0, uint32_t& c1) {
+    const uint32_t per = 32u * ((seq + 32u * kFaSplit - 1) / (32u * kFaSplit));
+    c0 = (uint32_t)c * per;
+    c1 = c0 + per < seq ? c0 + per : seq;
+}
+
+// grid (kFaSplit, 2 kv heads) x 256: warp w is query head 8 g + w; lane owns
+// dimensions [8 lane, 8 lane + 8).  part: m, l per (head, chunk), then the
+// [head][chunk][256] value sums.
+__global__ void __launch_bounds__(256) k_fa_attn(const float* __restrict__ qr, const float* __restrict__ kc,
+                                                 const float* __restrict__ vc, const qw6k_step* __restrict__ step,
+                                                 float* __restrict__ part) {
+    const uint32_t seq = step->pos + 1;
+    uint32_t c0, c1;
+    fa_chunk(seq, blockIdx.x, c0, c1);
+    if (c0 >= seq) return;
+    const int g = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, h = g * (kQH / kKVH) + warp;
+    const float4* q = reinterpret_cast<const float4*>(qr + h * kHD) + 2 * lane;
+    const float4 qa = q[0], qb = q[1];
+    float m = -INFINITY, l = 0.f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (uint32_t t0 = c0; t0 < c1; t0 += 32) {
+        const int n = (int)(c1 - t0 < 32 ? c1 - t0 : 32);
+        float mine = -INFINITY;
+        for (int t = 0; t < n; t += 4) {
+            float p[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                p[u] = 0.f;
+                if (t + u < n) {
+                    const float4* kr = reinterpret_cast<const float4*>(kc + ((size_t)(t0 + t + u) * kKVH + g) * kHD) +
+                                       2 * lane;
+                    const float4 ka = kr[0], kb = kr[1];
+                    p[u] = fmaf(qa.x, ka.x, fmaf(qa.y, ka.y, fmaf(qa.z, ka.z, fmaf(qa.w, ka.w,
+                           fmaf(qb.x, kb.x, fmaf(qb.y, kb.y, fmaf(qb.z, kb.z, qb.w * kb.w)))))));
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const float sc = __fmul_rn(warp_sum(p[u]), 0.0625f);  // dot / sqrtf(256), exact
+                if (lane == t + u) mine = sc;
+            }
+        }
+        const float mn = fmaxf(m, warp_max(mine));
+        const float alpha = expf(m - mn);  // 0 for the first sub-chunk
+        const float e = lane < n ? expf(mine - mn) : 0.f;
+        l = fmaf(l, alpha, warp_sum(e));
+#pragma unroll
+        for (int i = 0; i < 8; i++) acc[i] *= alpha;
+        for (int t = 0; t < n; t++) {
+            const float et = __shfl_sync(0xffffffffu, e, t);
+            const float4* vr = reinterpret_cast<const float4*>(vc + ((size_t)(t0 + t) * kKVH + g) * kHD) + 2 * lane;
+            const float4 va = vr[0], vb = vr[1];
+            acc[0] = fmaf(et, va.x, acc[0]);
+            acc[1] = fmaf(et, va.y, acc[1]);
+            acc[2] = fmaf(et, va.z, acc[2]);
+            acc[3] = fmaf(et, va.w, acc[3]);
+            acc[4] = fmaf(et, vb.x, acc[4]);
+            acc[5] = fmaf(et, vb.y, acc[5]);
+            acc[6] = fmaf(et, vb.z, acc[6]);
+            acc[7] = fmaf(et, vb.w, acc[7]);
+        }
+        m = mn;
+    }
+    const int slot = h * kFaSplit + blockIdx.x;
+    if (lane == 0) {
+        part[2 * slot] = m;
+        part[2 * slot + 1] = l;
+    }
+    float4* o = reinterpret_cast<float4*>(part + 2 * kQH * kFaSplit + (size_t)slot * kHD) + 2 * lane;
+    o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+}
+
+// grid 16 (query heads) x 256 (dimensions)
+__global__ void __launch_bounds__(256) k_fa_combine(const float* __restrict__ part, const float* __restrict__ proj,
+                                                    const qw6k_step* __restrict__ step, float* __restrict__ attn) {
+    const uint32_t seq = step->pos + 1;
+    const int h = blockIdx.x, d = threadIdx.x;
+    int nc = 0;
+    for (; nc < kFaSplit; nc++) {
+        uint32_t c0, c1;
+        fa_chunk(seq, nc, c0, c1);
+        if (c0 >= seq) break;
+    }
+    float mx = -INFINITY;
+    for (int c = 0; c < nc; c++) mx = fmaxf(mx, part[2 * (h * kFaSplit + c)]);
+    float l = 0.f, o = 0.f;
+    for (int c = 0; c < nc; c++) {
+        const int slot = h * kFaSplit + c;
+        const float f = expf(part[2 * slot] - mx);
+        l = fmaf(part[2 * slot + 1], f, l);
+        o = fmaf(part[2 * kQH * kFaSplit + (size_t)slot * kHD + d], f, o);
+    }
+    const float gate = proj[h * 2 * kHD + kHD + d];
+    attn[h * kHD + d] = __fmul_rn(__fdiv_rn(o, l), sigmoid_f(gate));
+}
+
+__global__ void k_check_finite(const float* __restrict__ x, uint32_t n, int* __restrict__ bad) {
+    bool finite = true;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        finite = finite && isfinite(x[i]);
+    if (!finite) atomicOr(bad, 1);
+}
+
+// the step's greedy token (largest packed argmax key: largest logit, lowest
+// index on ties) becomes the next step's input at the next position
+__global__ void k_step_next(qw6k_step* __restrict__ step, const unsigned long long* __restrict__ key) {
+    step->token = ~(uint32_t)(*key & 0xffffffffull);
+    step->pos += 1;
+}
+
+}  // namespace qw6
+
+using namespace qw6;
+
+static int launched() { return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA; }
+
+extern "C" size_t qw6k_fa_part_floats(void) { return (size_t)kQH * kFaSplit * (2 + kHD); }
+
+extern "C" int qw6k_rmsnorm(const float* x, const float* w, float* out, uint32_t dim, cudaStream_t st) {
+    if (!x || !w || !out || !dim) return QW6K_ERR_ARG;
+    k_rmsnorm<<<1, 256, 0, st>>>(x, w, out, (int)dim);
+    return launched();
+}
+
+extern "C" int qw6k_dn_conv(const float* proj, float* conv_state, const float* conv_w, const float* dt, const float* a,
+                            float* conv, float* gb, cudaStream_t st) {
+    if (!proj || !conv_state || !conv_w || !dt || !a || !conv || !gb) return QW6K_ERR_ARG;
+    if (reinterpret_cast<uintptr_t>(conv_w) & 15u) return QW6K_ERR_ALIGN;
+    k_dn_conv<<<kQKV / 128, 128, 0, st>>>(proj, conv_state, conv_w, dt, a, conv, gb);
+    return launched();
+}
+
+extern "C" int qw6k_dn_step(const float* conv, const float* gb, const float* z, const float* dn_norm, float* state,
+                            float* gated, cudaStream_t st) {
+    if (!conv || !gb || !z || !dn_norm || !state || !gated) return QW6K_ERR_ARG;
+    if ((reinterpret_cast<uintptr_t>(conv) | reinterpret_cast<uintptr_t>(state)) & 15u) return QW6K_ERR_ALIGN;
+    k_dn_step<<<kVH, 512, 0, st>>>(conv, gb, z, dn_norm, state, gated);
+    return launched();
+}
+
+extern "C" int qw6k_fa_prep(const float* proj, const float* q_norm, const float* k_norm, const float* freq,
+                            const qw6k_step* step, float* k_cache, float* v_cache, float* q_rot, cudaStream_t st) {
+    if (!proj || !q_norm || !k_norm || !freq || !step || !k_cache || !v_cache || !q_rot) return QW6K_ERR_ARG;
+    k_fa_prep<<<kQH + kKVH, kHD, 0, st>>>(proj, q_norm, k_norm, freq, step, k_cache, v_cache, q_rot);
+    return launched();
+}
+
+extern "C" int qw6k_fa_attn(const float* q_rot, const float* k_cache, const float* v_cache, const qw6k_step* step,
+                            float* part, const float* proj, float* attn, cudaStream_t st) {
+    if (!q_rot || !k_cache || !v_cache || !step || !part || !proj || !attn) return QW6K_ERR_ARG;
+    if ((reinterpret_cast<uintptr_t>(q_rot) | reinterpret_cast<uintptr_t>(k_cache) |
+         reinterpret_cast<uintptr_t>(v_cache) | reinterpret_cast<uintptr_t>(part)) & 15u)
+        return QW6K_ERR_ALIGN;
+    k_fa_attn<<<dim3(kFaSplit, kKVH), 256, 0, st>>>(q_rot, k_cache, v_cache, step, part);
+    const int rc = launched();
+    if (rc) return rc;
+    k_fa_combine<<<kQH, kHD, 0, st>>>(part, proj, step, attn);
+    return launched();
+}
+
+extern "C" int qw6k_check_finite(const float* x, uint32_t n, int* bad, cudaStream_t st) {
+    if (!x || !n || !bad) return QW6K_ERR_ARG;
+    const uint32_t grid = (n + 1023) / 1024 < 148 ? (n + 1023) / 1024 : 148;
+    k_check_finite<<<grid, 256, 0, st>>>(x, n, bad);
+    return launched();
+}
+
+extern "C" int qw6k_step_next(qw6k_step* step, const unsigned long long* key, cudaStream_t st) {
+    if (!step || !key) return QW6K_ERR_ARG;
+    k_step_next<<<1, 1, 0, st>>>(step, key);
+    return launched();
+}

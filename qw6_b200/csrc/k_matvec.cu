@@ -531,6 +531,73 @@ extern "C" int qw6k_dequant(uint32_t quant, const void* raw, float* out, uint32_
 #undef CALL
 }
 
+// One row of a raw matrix, the row index read from device memory (the token
+// id of an embedding lookup, qw6.c:2456): out[cols] = the exact dequantized
+// row (qw6_tensor_dequantize_row, qw6.c:1674-1724).  An index past the
+// matrix, or a NaN/Inf in the row (qw6.c:2457), sets *bad; the row is then
+// zero-filled or written as is.
+template <int F>
+__global__ void k_dequant_row(const uint8_t* __restrict__ w, const uint32_t* __restrict__ row, float* __restrict__ out,
+                              int* __restrict__ bad, uint32_t rows, int cols) {
+    const uint32_t r = *row;
+    const int nb = cols / 256;
+    bool finite = true;
+    for (int item = threadIdx.x; item < nb * 8; item += blockDim.x) {
+        float* o = out + 32 * item;
+        if (r >= rows) {
+            for (int i = 0; i < 32; i++) o[i] = 0.f;
+            continue;
+        }
+        dequant_group<F>(w + ((size_t)r * nb + (item >> 3)) * (size_t)Fmt<F>::BB, item & 7, o);
+        for (int i = 0; i < 32; i++) finite = finite && isfinite(o[i]);
+    }
+    if ((r >= rows || !finite) && bad) atomicOr(bad, 1);
+}
+
+template <int BYTES>  // 4: fp32, 2: fp16 (BF = false) / bf16 (BF = true)
+__global__ void k_dequant_row_plain(const uint8_t* __restrict__ w, const uint32_t* __restrict__ row,
+                                    float* __restrict__ out, int* __restrict__ bad, uint32_t rows, int cols, bool bf) {
+    const uint32_t r = *row;
+    bool finite = true;
+    for (int i = threadIdx.x; i < cols; i += blockDim.x) {
+        float v = 0.f;
+        if (r < rows) {
+            if constexpr (BYTES == 4) v = reinterpret_cast<const float*>(w)[(size_t)r * cols + i];
+            else {
+                const uint32_t h = reinterpret_cast<const uint16_t*>(w)[(size_t)r * cols + i];
+                v = bf ? w16<true>(h) : w16<false>(h);
+            }
+        }
+        out[i] = v;
+        finite = finite && isfinite(v);
+    }
+    if ((r >= rows || !finite) && bad) atomicOr(bad, 1);
+}
+
+template <int F>
+static int launch_dequant_row(const void* raw, uint32_t rows, uint32_t cols, const uint32_t* row, float* out, int* bad,
+                              cudaStream_t st) {
+    k_dequant_row<F><<<1, 256, 0, st>>>((const uint8_t*)raw, row, out, bad, rows, (int)cols);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
+}
+
+extern "C" int qw6k_dequant_row(uint32_t quant, const void* raw, uint32_t rows, uint32_t cols, const uint32_t* row,
+                                float* out, int* bad, cudaStream_t st) {
+    if (!raw || !row || !out || !rows || !cols) return QW6K_ERR_ARG;
+    if (quant == QW6F_FP32 || is16(quant)) {
+        if (quant == QW6F_FP32)
+            k_dequant_row_plain<4><<<1, 256, 0, st>>>((const uint8_t*)raw, row, out, bad, rows, (int)cols, false);
+        else
+            k_dequant_row_plain<2><<<1, 256, 0, st>>>((const uint8_t*)raw, row, out, bad, rows, (int)cols,
+                                                      quant == QW6F_BF16);
+        return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
+    }
+    if (cols % 256) return QW6K_ERR_ARG;
+#define CALL(F) launch_dequant_row<F>(raw, rows, cols, row, out, bad, st)
+    QW6_DISPATCH_BLOCK(quant, CALL)
+#undef CALL
+}
+
 extern "C" int qw6k_matvec(uint32_t quant, const void* packed, const float* x, float* y, uint32_t rows,
                            uint32_t cols, uint32_t ntok, uint32_t ldx, uint32_t ldy, cudaStream_t st) {
     if (is16(quant)) {

@@ -429,14 +429,19 @@ __device__ __forceinline__ void xstage_fill_warps(const XStage& s, const float* 
             for (int i = 0; i < 8; i++) v[i] = 0.f;
         }
         float amax = 0.f, sum = 0.f;
+        bool finite = true;
 #pragma unroll
         for (int i = 0; i < 8; i++) {
             amax = fmaxf(amax, fabsf(v[i]));
             sum += v[i];
+            finite = finite && isfinite(v[i]);
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        const float inv = amax > 0.f ? 32639.f / amax : 0.f;
+        // a NaN or Inf in the block makes the block's scale NaN, so that it
+        // reaches the outputs as in qw6's fp32 dot products
+        if (!__all_sync(0xffffffffu, finite)) amax = __int_as_float(0x7fc00000);
+        const float inv = amax > 0.f ? 32639.f / amax : 0.f;  // 0 for a NaN scale
         uint32_t hw[2] = {0, 0}, lw[2] = {0, 0};
         int sh = 0, sl = 0;
 #pragma unroll
@@ -462,7 +467,7 @@ __device__ __forceinline__ void xstage_fill_warps(const XStage& s, const float* 
             s.xsum[j] = sum;
             s.nx32[j] = make_int2(-32 * sh, -32 * sl);
         }
-        if (lane == 0) s.sx[tok * nb + b] = amax > 0.f ? amax / 32639.f : 0.f;
+        if (lane == 0) s.sx[tok * nb + b] = (amax > 0.f || amax != amax) ? amax / 32639.f : 0.f;
     }
 }
 

@@ -181,8 +181,10 @@ int qw6cu_ep_connect(qw6cu_ep *ep, const void *handles) {
         ep->peer_host[p] = (uint8_t *)ptr;
         ep->opened[p] = 1;
     }
-    cudaError_t e = cudaMemcpy(ep->peers_dev, ep->peer_host, ep->world * sizeof(void *), cudaMemcpyHostToDevice);
-    if (e != cudaSuccess) return ep_fail("qw6cu_ep_connect: cudaMemcpy", e);
+    cudaError_t e =
+        cudaMemcpyAsync(ep->peers_dev, ep->peer_host, ep->world * sizeof(void *), cudaMemcpyHostToDevice, ep->ctx->st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ep->ctx->st);
+    if (e != cudaSuccess) return ep_fail("qw6cu_ep_connect: cudaMemcpyAsync", e);
     ep->connected = 1;
     return 0;
 }

@@ -373,7 +373,9 @@ int qw6cu_gguf_upload_moe(qw6cu_ctx *ctx, const qw6cu_gguf *g, uint32_t n_layers
     for (uint32_t j = 0; j < n_layers * 3 && !rc; j++)
         rc = qw6cu_gguf_upload(ctx, g, idx[j], (uint8_t *)dev + off[j], total - off[j], &packs[j]);
     if (!rc && cudaMalloc(&tdev, sizeof *packs * n_layers * 3) != cudaSuccess) rc = QW6CU_ERR_NOMEM;
-    if (!rc && cudaMemcpy(tdev, packs, sizeof *packs * n_layers * 3, cudaMemcpyHostToDevice) != cudaSuccess)
+    if (!rc && (cudaMemcpyAsync(tdev, packs, sizeof *packs * n_layers * 3, cudaMemcpyHostToDevice, ctx->st) !=
+                    cudaSuccess ||
+                cudaStreamSynchronize(ctx->st) != cudaSuccess))
         rc = QW6CU_ERR_CUDA;
     if (rc) {
         cudaFree(dev);

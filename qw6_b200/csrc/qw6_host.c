@@ -647,20 +647,3 @@ int qw6_vk_mtp_draft_host(const float *w, const float *h, float *l, uint32_t v, 
     return not_provided("qw6_vk_mtp_draft_host");
 }
 
-/* Pipeline API (qw6_vk.h:57-83): declared with qw6_model_t in the public
- * header; defined here with plain pointers, which is ABI-identical. */
-int qw6_vk_pipe_init(void **p, void *m, bool strict) {
-    (void)m; (void)strict;
-    if (p) *p = NULL;
-    return not_provided("qw6_vk_pipe_init");
-}
-int qw6_vk_pipe_forward(void *p, void *m, uint32_t token, uint32_t pos, float *logits_out) {
-    (void)p; (void)m; (void)token; (void)pos; (void)logits_out;
-    return not_provided("qw6_vk_pipe_forward");
-}
-int qw6_vk_pipe_forward_greedy(void *p, void *m, uint32_t token, uint32_t pos, uint32_t *out_token,
-                               float *dump_logits_buf) {
-    (void)p; (void)m; (void)token; (void)pos; (void)out_token; (void)dump_logits_buf;
-    return not_provided("qw6_vk_pipe_forward_greedy");
-}
-void qw6_vk_pipe_free(void *p) { (void)p; }

@@ -119,13 +119,15 @@ int qw6k_moe_phase(const qw6k_moe_desc *d, int phase, cudaStream_t st);
 /* Configure and load every decode kernel on the current device. */
 int qw6k_moe_decode_setup(void);
 
-/* MoE FFN block (k_block.cu).  pre: normed = rmsnorm(x) * norm_w, logits =
- * router . normed (fp32 router [ne x hidden]), sgate[t] = sigmoid(srouter .
- * normed) or 1 when srouter is NULL.  post: out = x + (ffn + sgate * shared)
- * (shared nullable). */
-int qw6k_block_pre(const float *x, const float *norm_w, const float *router, const float *srouter, float *normed,
-                   float *logits, float *sgate, uint32_t ntok, uint32_t hidden, uint32_t ne, cudaStream_t st);
-int qw6k_block_post(const float *x, const float *ffn, const float *shared, const float *sgate, float *out,
+/* MoE FFN block (k_block.cu).  pre: normed = rmsnorm(x') * norm_w with x' =
+ * x, or x + add written to xsum when add is given; logits = router . normed
+ * (fp32 router [ne x hidden]), sgate[t] = sigmoid(srouter . normed) or 1
+ * when srouter is NULL.  post: out = x + (ffn + sgate * shared) (shared
+ * nullable).  bad (nullable): set to 1 when x + add or out holds a NaN/Inf. */
+int qw6k_block_pre(const float *x, const float *add, float *xsum, int *bad, const float *norm_w, const float *router,
+                   const float *srouter, float *normed, float *logits, float *sgate, uint32_t ntok, uint32_t hidden,
+                   uint32_t ne, cudaStream_t st);
+int qw6k_block_post(const float *x, const float *ffn, const float *shared, const float *sgate, float *out, int *bad,
                     uint32_t ntok, uint32_t hidden, cudaStream_t st);
 
 /* Sampling (k_sample.cu): out[r] = qw6_sample's pick (qw6.c:2904-2982) over
@@ -200,6 +202,40 @@ int qw6k_ep_p2p_phase(const qw6k_ep_desc *d, int phase, cudaStream_t st);
  * point; *ptr is its device address on the current device (looked up with
  * cudaGetSymbolAddress on the first call per device, which also configures
  * every decode kernel there). */
+/* ---- decode-step executor (k_fwd.cu, k_matvec.cu) ----
+ * The token id and position of the step being computed, in device memory;
+ * bad is set by the kernels that check for NaN/Inf as qw6 does
+ * (qw6_check_nan_inf at qw6.c:2457, 2472, 2487). */
+typedef struct {
+    uint32_t token, pos;
+    int bad;
+    uint32_t reserved;
+} qw6k_step;
+#define QW6K_FA_SPLIT 128 /* sequence chunks per kv head of the attention kernel */
+/* out[cols] = row *row_idx of a raw matrix (exact dequant); bad on an index
+ * past rows or a NaN/Inf */
+int qw6k_dequant_row(uint32_t quant, const void *raw, uint32_t rows, uint32_t cols, const uint32_t *row_idx,
+                     float *out, int *bad, cudaStream_t st);
+int qw6k_rmsnorm(const float *x, const float *w, float *out, uint32_t dim, cudaStream_t st);
+/* Gated DeltaNet token step: proj = [qkv 8192 | z 4096 | beta 32 | alpha 32];
+ * conv_state [4][8192] (oldest first), conv_w [8192][4], dt/a [32]; conv
+ * [8192] and gb [64] (sigmoid(beta), softplus(alpha + dt) * a) are scratch */
+int qw6k_dn_conv(const float *proj, float *conv_state, const float *conv_w, const float *dt, const float *a,
+                 float *conv, float *gb, cudaStream_t st);
+/* state [32][128][128] updated in place; gated [4096] = rmsnorm(o) * silu(z) */
+int qw6k_dn_step(const float *conv, const float *gb, const float *z, const float *dn_norm, float *state,
+                 float *gated, cudaStream_t st);
+/* gated attention: proj = [16 x (q 256 | gate 256) | k 512 | v 512]; caches
+ * [max_ctx][2][256]; freq[32] = powf(1e7, i / 64) for even i < 64 */
+int qw6k_fa_prep(const float *proj, const float *q_norm, const float *k_norm, const float *freq,
+                 const qw6k_step *step, float *k_cache, float *v_cache, float *q_rot, cudaStream_t st);
+size_t qw6k_fa_part_floats(void);
+int qw6k_fa_attn(const float *q_rot, const float *k_cache, const float *v_cache, const qw6k_step *step, float *part,
+                 const float *proj, float *attn, cudaStream_t st);
+int qw6k_check_finite(const float *x, uint32_t n, int *bad, cudaStream_t st);
+/* step->token = the argmax of *key, step->pos += 1 */
+int qw6k_step_next(qw6k_step *step, const unsigned long long *key, cudaStream_t st);
+
 #define QW6K_STATIC_SCRATCH_BYTES (1u << 20)
 #define QW6K_MAX_DEVICES 64
 int qw6k_static_scratch(void **ptr, size_t *bytes);

@@ -339,8 +339,8 @@ int qw6cu_moe_block(qw6cu_ctx *ctx, const float *x, const float *norm_w, const f
     d.x = normed;
     d.out = ffn;
     int rec = qw6h_prof_a(ctx, QW6H_K_MOE_BLOCK);
-    rc = qw6h_rc(qw6k_block_pre(x, norm_w, router, shared ? shared->router : NULL, normed, logits, sg, ntok, hidden,
-                                n_experts, ctx->st),
+    rc = qw6h_rc(qw6k_block_pre(x, NULL, NULL, NULL, norm_w, router, shared ? shared->router : NULL, normed, logits,
+                                sg, ntok, hidden, n_experts, ctx->st),
                  "moe_block");
     qw6h_prof_b(ctx, rec);
     if (!rc) rc = moe_run(ctx, &d);
@@ -352,7 +352,7 @@ int qw6cu_moe_block(qw6cu_ctx *ctx, const float *x, const float *norm_w, const f
     }
     if (!rc) {
         rec = qw6h_prof_a(ctx, QW6H_K_MOE_BLOCK);
-        rc = qw6h_rc(qw6k_block_post(x, ffn, sh, sg, out, ntok, hidden, ctx->st), "moe_block");
+        rc = qw6h_rc(qw6k_block_post(x, ffn, sh, sg, out, NULL, ntok, hidden, ctx->st), "moe_block");
         qw6h_prof_b(ctx, rec);
     }
     return rc;

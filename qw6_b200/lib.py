@@ -69,6 +69,12 @@ _u32 = C.c_uint32
 _sz = C.c_size_t
 
 
+class ModelTensor(C.Structure):
+    """qw6cu_model_tensor: one host tensor of a model for the decoder."""
+    _fields_ = [("field", C.c_uint32), ("layer", C.c_int32), ("quant", C.c_uint32), ("rows", C.c_uint32),
+                ("cols", C.c_uint32), ("data", C.c_void_p), ("stride", C.c_size_t)]
+
+
 class ExpertPack(C.Structure):
     _fields_ = [("quant", C.c_uint32), ("base", C.c_void_p), ("stride", C.c_size_t)]
 
@@ -137,6 +143,16 @@ def load() -> C.CDLL:
     lib.qw6cu_moe_table_free.argtypes = [C.POINTER(MoeTable)]
     lib.qw6cu_moe_table_free.restype = None
     lib.qw6cu_sample.argtypes = [_vp, _vp, _u32, _u32, C.c_float, C.c_float, C.c_int, _vp, _vp]
+    lib.qw6cu_decoder_create.argtypes = [_vp, C.POINTER(ModelTensor), _u32, _u32, _u32, C.POINTER(_vp)]
+    lib.qw6cu_decoder_forward.argtypes = [_vp, _u32, _u32, _vp, _vp]
+    lib.qw6cu_decoder_generate.argtypes = [_vp, _u32, _u32, _u32, _u32p]
+    lib.qw6cu_decoder_logits.argtypes = [_vp, C.POINTER(C.c_uint32)]
+    lib.qw6cu_decoder_logits.restype = _vp
+    lib.qw6cu_decoder_reset.argtypes = [_vp]
+    lib.qw6cu_decoder_device_bytes.argtypes = [_vp]
+    lib.qw6cu_decoder_device_bytes.restype = _sz
+    lib.qw6cu_decoder_destroy.argtypes = [_vp]
+    lib.qw6cu_decoder_destroy.restype = None
     lib.qw6cu_moe_block.argtypes = [_vp, _vp, _vp, _vp, pk, pk, pk, C.POINTER(SharedExpert), _vp, _u32, _u32, _u32,
                                     _u32, _u32]
     lib.qw6cu_moe_expert_rows.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32]
@@ -497,3 +513,58 @@ class Gguf:
 
     def free_table(self, table: MoeTable) -> None:
         self.lib.qw6cu_moe_table_free(C.byref(table))
+
+
+class Decoder:
+    """qw6cu_decoder: qw6's per-token forward pass on the device, replayed
+    as one CUDA graph per step.  `model` is a qw6_b200.synth.FwdModel-like
+    object: n_layers and .tensors of (field, layer, quant, rows, cols, host
+    array, stride); its arrays must stay alive until create() returns (the
+    decoder keeps device copies)."""
+
+    def __init__(self, ctx: "Context", model, max_ctx: int) -> None:
+        self.lib = ctx.lib
+        self.ctx = ctx
+        ts = (ModelTensor * len(model.tensors))()
+        for i, (f, l, q, r, c, arr, stride) in enumerate(model.tensors):
+            ts[i] = ModelTensor(f, l, q, r, c, arr.ctypes.data, stride)
+        h = _vp()
+        _check(self.lib.qw6cu_decoder_create(ctx.h, ts, len(model.tensors), model.n_layers, max_ctx, C.byref(h)),
+               "qw6cu_decoder_create")
+        self.h = h
+        n = C.c_uint32()
+        self.lib.qw6cu_decoder_logits(self.h, C.byref(n))
+        self.vocab = int(n.value)
+
+    def close(self) -> None:
+        if self.h:
+            self.lib.qw6cu_decoder_destroy(self.h)
+            self.h = _vp()
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def forward(self, token: int, pos: int, logits: bool = True):
+        """One step: (logits [vocab] or None, greedy token id)."""
+        out = np.empty(self.vocab, np.float32) if logits else None
+        g = C.c_uint32()
+        _check(self.lib.qw6cu_decoder_forward(self.h, token, pos, out.ctypes.data if logits else None, C.byref(g)),
+               "qw6cu_decoder_forward")
+        return out, int(g.value)
+
+    def generate(self, token: int, pos: int, n: int) -> np.ndarray:
+        out = np.empty(n, np.uint32)
+        _check(self.lib.qw6cu_decoder_generate(self.h, token, pos, n, out), "qw6cu_decoder_generate")
+        return out
+
+    def logits_ptr(self) -> int:
+        return int(self.lib.qw6cu_decoder_logits(self.h, None) or 0)
+
+    def reset(self) -> None:
+        _check(self.lib.qw6cu_decoder_reset(self.h), "qw6cu_decoder_reset")
+
+    def device_bytes(self) -> int:
+        return int(self.lib.qw6cu_decoder_device_bytes(self.h))

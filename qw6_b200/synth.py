@@ -152,3 +152,116 @@ def config4(seed: int = 4, batch: int = 1, vocab: int = VOCAB):
     xs = {k: rng.standard_normal((batch, c), dtype=np.float32) for k, (_, _, _, c) in mats.items()}
     h = rng.standard_normal((batch, 2048), dtype=np.float32)
     return mats, xs, head, h
+
+
+# ---- a whole qw6 model for the decode-step executor ----
+# Roles of the tensors (qw6_model_t's fields, qw6.h:126-170; the values of
+# include/qw6_cuda.h's QW6CU_F_*).
+(F_NORM, F_POST_NORM, F_ATTN_Q, F_ATTN_K, F_ATTN_V, F_ATTN_O, F_ATTN_Q_NORM, F_ATTN_K_NORM, F_ATTN_GATE,
+ F_CONV1D, F_DN_OUT, F_DN_NORM, F_DN_ALPHA, F_DN_BETA, F_DN_DT, F_DN_A, F_MOE_ROUTER, F_SHARED_ROUTER,
+ F_SHARED_GATE, F_SHARED_UP, F_SHARED_DOWN, F_EXPERT_GATE, F_EXPERT_UP, F_EXPERT_DOWN) = range(24)
+F_TOK_EMBD, F_OUTPUT, F_OUTPUT_NORM = 100, 101, 102
+N_LAYERS = 40
+
+
+def is_full_attn(layer: int) -> bool:
+    """qw6_layer_type (qw6.h:320-324): every 4th layer is full attention."""
+    return layer % 4 == 3
+
+
+class FwdModel:
+    """Tensors of a qw6 model: (field, layer, quant, rows, cols, array, stride)
+    with raw GGUF rows in `array` (uint8, or float32 for FP32 tensors); the
+    expert packs hold all 256 experts, `stride` bytes apart."""
+
+    def __init__(self, n_layers: int, vocab: int, embd_rows: int):
+        self.n_layers, self.vocab, self.embd_rows = n_layers, vocab, embd_rows
+        self.tensors: list[tuple[int, int, int, int, int, np.ndarray, int]] = []
+
+    def add(self, field, layer, quant, rows, cols, arr, stride=0):
+        self.tensors.append((field, layer, quant, rows, cols, np.ascontiguousarray(arr), stride))
+
+    def nbytes(self) -> int:
+        seen, n = set(), 0
+        for t in self.tensors:
+            if id(t[5]) not in seen:
+                seen.add(id(t[5]))
+                n += t[5].nbytes
+        return n
+
+
+def fwd_model(seed: int = 5, n_layers: int = N_LAYERS, vocab: int = 8192, embd_rows: int = 4096,
+              attn_period: int = 8, expert_period: int = 2, expert_quant: int = IQ2_XXS,
+              weight_quant: int = Q6_K, shared: bool = True, out_scale: float = 0.1) -> FwdModel:
+    """A seeded qw6 model with qw6's dimensions (qw6.h:24-55) and the quant mix
+    of its model card's primary plan: IQ2 experts, Q6_K attention, shared
+    expert, embeddings and LM head, FP32 norms, router and conv weights.
+    Scales keep activations O(1); the matrices that write into the residual
+    stream (attention / DeltaNet output, expert and shared-expert down) are
+    scaled by out_scale, so that every layer adds a small update to it as in
+    a trained model: a random model with O(1) updates amplifies rounding
+    differences about 100x over 40 layers.  Layer l reuses the
+    weights of layer l % attn_period (attention, norms, router, shared
+    expert) and l % expert_period (experts), so that 40 layers stay small
+    on the host; both periods must be multiples of 4 or >= n_layers for the
+    attention kind to match (experts: any)."""
+    assert attn_period % 4 == 0 or attn_period >= n_layers
+    rng = np.random.Generator(np.random.PCG64(seed))
+    m = FwdModel(n_layers, vocab, embd_rows)
+    ws = 1e-4 if weight_quant in (Q4_K, Q5_K, Q6_K) else 5e-4
+    es = 5e-4 if expert_quant in (IQ2_XXS, IQ2_S, IQ3_S) else 1e-4
+
+    def mat(q, rows, cols, s):
+        if q == FP32:
+            return (rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(s * 200)).astype(np.float32)
+        if q in (FP16, BF16):
+            v = rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(s * 200)
+            return (v.astype(np.float16).view(np.uint16) if q == FP16 else bf16_round(v)).view(np.uint8)
+        return make_matrix(q, rows, cols, rng, s)
+
+    def vec(n, base=1.0, s=0.1):
+        return (base + s * rng.standard_normal((1, n))).astype(np.float32)
+
+    sets: dict[int, list] = {}
+    esets: dict[int, tuple] = {}
+    for l in range(n_layers):
+        a = l % attn_period if attn_period < n_layers else l
+        if a not in sets:
+            t = [(F_NORM, FP32, 1, HIDDEN, vec(HIDDEN)), (F_POST_NORM, FP32, 1, HIDDEN, vec(HIDDEN))]
+            if is_full_attn(l):
+                t += [(F_ATTN_Q, weight_quant, 8192, HIDDEN, mat(weight_quant, 8192, HIDDEN, ws)),
+                      (F_ATTN_K, weight_quant, 512, HIDDEN, mat(weight_quant, 512, HIDDEN, ws)),
+                      (F_ATTN_V, weight_quant, 512, HIDDEN, mat(weight_quant, 512, HIDDEN, ws)),
+                      (F_ATTN_O, weight_quant, HIDDEN, 4096, mat(weight_quant, HIDDEN, 4096, ws * out_scale)),
+                      (F_ATTN_Q_NORM, FP32, 1, 256, vec(256)), (F_ATTN_K_NORM, FP32, 1, 256, vec(256))]
+            else:
+                t += [(F_ATTN_Q, weight_quant, 8192, HIDDEN, mat(weight_quant, 8192, HIDDEN, ws)),
+                      (F_ATTN_GATE, weight_quant, 4096, HIDDEN, mat(weight_quant, 4096, HIDDEN, ws)),
+                      (F_DN_BETA, weight_quant, 32, HIDDEN, mat(weight_quant, 32, HIDDEN, ws)),
+                      (F_DN_ALPHA, weight_quant, 32, HIDDEN, mat(weight_quant, 32, HIDDEN, ws)),
+                      (F_DN_OUT, weight_quant, HIDDEN, 4096, mat(weight_quant, HIDDEN, 4096, ws * out_scale)),
+                      (F_CONV1D, FP32, 8192, 4, (rng.standard_normal((8192, 4)) * 0.5).astype(np.float32)),
+                      (F_DN_DT, FP32, 1, 32, rng.standard_normal((1, 32)).astype(np.float32)),
+                      (F_DN_A, FP32, 1, 32, -np.exp(0.5 * rng.standard_normal((1, 32))).astype(np.float32)),
+                      (F_DN_NORM, FP32, 1, 128, vec(128))]
+            t += [(F_MOE_ROUTER, FP32, N_EXPERTS, HIDDEN,
+                   (rng.standard_normal((N_EXPERTS, HIDDEN)) * 0.02).astype(np.float32))]
+            if shared:
+                t += [(F_SHARED_GATE, weight_quant, INTER, HIDDEN, mat(weight_quant, INTER, HIDDEN, ws)),
+                      (F_SHARED_UP, weight_quant, INTER, HIDDEN, mat(weight_quant, INTER, HIDDEN, ws)),
+                      (F_SHARED_DOWN, weight_quant, HIDDEN, INTER, mat(weight_quant, HIDDEN, INTER, ws * out_scale)),
+                      (F_SHARED_ROUTER, FP32, 1, HIDDEN, (rng.standard_normal((1, HIDDEN)) * 0.02).astype(np.float32))]
+            sets[a] = t
+        for (f, q, r, c, arr) in sets[a]:
+            m.add(f, l, q, r, c, arr)
+        e = l % expert_period
+        if e not in esets:
+            esets[e] = tuple(make_matrix(expert_quant, N_EXPERTS * r, c, rng, es * sc)
+                             for r, c, sc in ((INTER, HIDDEN, 1.0), (INTER, HIDDEN, 1.0), (HIDDEN, INTER, out_scale)))
+        for f, (r, c), arr in zip((F_EXPERT_GATE, F_EXPERT_UP, F_EXPERT_DOWN),
+                                  ((INTER, HIDDEN), (INTER, HIDDEN), (HIDDEN, INTER)), esets[e]):
+            m.add(f, l, expert_quant, r, c, arr, r * row_bytes(expert_quant, c))
+    m.add(F_TOK_EMBD, -1, weight_quant, embd_rows, HIDDEN, make_matrix(weight_quant, embd_rows, HIDDEN, rng, 1e-3))
+    m.add(F_OUTPUT, -1, weight_quant, vocab, HIDDEN, mat(weight_quant, vocab, HIDDEN, ws))
+    m.add(F_OUTPUT_NORM, -1, FP32, 1, HIDDEN, vec(HIDDEN))
+    return m

@@ -86,3 +86,31 @@ def test_qw6_links_against_dropin_library():
         r = subprocess.run(cmd, capture_output=True, text=True)
         assert r.returncode == 0, r.stderr[-3000:]
         assert exe.exists()
+
+
+@pytest.mark.skipif(not (REF_DIR / "qw6.h").exists(), reason="reference tree absent")
+def test_model_layout_matches_qw6():
+    """qw6_model_abi.h (the pipeline's view of qw6_model_t) has the layout of
+    qw6.h's structs as qw6 is built with QW6_VULKAN: a C file that includes
+    both compiles only if every offset the pipeline reads matches."""
+    fields = ("norm", "post_norm", "attn_q", "attn_k", "attn_v", "attn_o", "attn_q_norm", "attn_k_norm",
+              "attn_gate", "conv1d", "dn_out", "dn_norm", "dn_alpha", "dn_beta", "dn_dt", "dn_a", "moe_router",
+              "shared_router", "expert_gate[0]", "expert_up[17]", "expert_down[255]", "shared_gate", "shared_up",
+              "shared_down")
+    checks = ["_Static_assert(sizeof(qw6_tensor_t) == sizeof(qw6abi_tensor), \"tensor size\");"]
+    for f in ("name", "rows", "cols", "quant", "data", "vk_offset"):
+        checks.append(f"_Static_assert(offsetof(qw6_tensor_t, {f}) == offsetof(qw6abi_tensor, {f}), \"{f}\");")
+    for top in ("tok_embeddings", "output", "output_norm", "max_context"):
+        checks.append(f"_Static_assert(offsetof(qw6_model_t, {top}) == offsetof(qw6abi_model, {top}), \"{top}\");")
+    for layer in (0, 3, 39):
+        for f in fields:
+            p = f"layers[{layer}].{f}"
+            checks.append(f"_Static_assert(offsetof(qw6_model_t, {p}) == offsetof(qw6abi_model, {p}), \"{p}\");")
+    src = ("#define QW6_VULKAN 1\n#include <stddef.h>\n#include \"qw6.h\"\n#include \"qw6_model_abi.h\"\n"
+           + "\n".join(checks) + "\nint main(void) { return 0; }\n")
+    with tempfile.TemporaryDirectory() as td:
+        c = Path(td) / "layout.c"
+        c.write_text(src)
+        r = subprocess.run([shutil.which("gcc") or "gcc", "-std=c11", "-fsyntax-only", "-I", str(REF_DIR), "-I",
+                            str(ROOT / "qw6_b200" / "csrc"), str(c)], capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr[-3000:]
