@@ -17,10 +17,12 @@
 #include "qw6_devcfg.cuh"
 #include "qw6_launch.h"
 #include "qw6_norm.cuh"
+#include "qw6_pdl.cuh"
 
 namespace qw6 {
 
 constexpr int kBlkThreads = 256;
+constexpr int kRowRegs = 16;  // float4 of a router row a lane holds in registers (hidden <= 2048)
 
 // grid (ceil(ne / 8), ntok): CTA (b, t) computes router rows [8b, 8b+8) of
 // token t (warp per row), CTA (0, t) also writes normed[t], and the last CTA
@@ -38,6 +40,20 @@ __global__ void __launch_bounds__(kBlkThreads) k_block_pre(const float* __restri
     extern __shared__ __align__(16) float nrm[];  // [hidden]
     __shared__ float red[kBlkThreads / 32];
     const int t = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // launched with programmatic dependent launch: the warp's router row
+    // (no kernel before this one writes it) is loaded while the previous
+    // kernel finishes, then the wait for x / add
+    pdl_trigger_dependents();
+    const int r = blockIdx.x * (kBlkThreads / 32) + warp;
+    const bool held = r < ne && hidden <= 128 * kRowRegs;
+    float4 wv[kRowRegs];
+#pragma unroll
+    for (int u = 0; u < kRowRegs; u++) {
+        const int c = 4 * lane + 128 * u;
+        wv[u] = held && c < hidden ? __ldg(reinterpret_cast<const float4*>(router + (size_t)r * hidden + c))
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    pdl_grid_wait();
     const float* xt = x + (size_t)t * hidden;
     if (add) {  // x + add into shared memory first, then the norm of the sum
         const float* at = add + (size_t)t * hidden;
@@ -59,16 +75,28 @@ __global__ void __launch_bounds__(kBlkThreads) k_block_pre(const float* __restri
         if (blockIdx.x == 0) normed[(size_t)t * hidden + i] = v;
     }
     __syncthreads();
-    const int r = blockIdx.x * (kBlkThreads / 32) + warp;
     if (r < ne) {
         const float* wr = router + (size_t)r * hidden;
         float acc = 0.f;
-        for (int c = 4 * lane; c < hidden; c += 128) {
-            const float4 w4 = __ldg(reinterpret_cast<const float4*>(wr + c));
-            acc = fmaf(w4.x, nrm[c], acc);
-            acc = fmaf(w4.y, nrm[c + 1], acc);
-            acc = fmaf(w4.z, nrm[c + 2], acc);
-            acc = fmaf(w4.w, nrm[c + 3], acc);
+        if (held) {
+#pragma unroll
+            for (int u = 0; u < kRowRegs; u++) {
+                const int c = 4 * lane + 128 * u;
+                if (c < hidden) {
+                    acc = fmaf(wv[u].x, nrm[c], acc);
+                    acc = fmaf(wv[u].y, nrm[c + 1], acc);
+                    acc = fmaf(wv[u].z, nrm[c + 2], acc);
+                    acc = fmaf(wv[u].w, nrm[c + 3], acc);
+                }
+            }
+        } else {
+            for (int c = 4 * lane; c < hidden; c += 128) {
+                const float4 w4 = __ldg(reinterpret_cast<const float4*>(wr + c));
+                acc = fmaf(w4.x, nrm[c], acc);
+                acc = fmaf(w4.y, nrm[c + 1], acc);
+                acc = fmaf(w4.z, nrm[c + 2], acc);
+                acc = fmaf(w4.w, nrm[c + 3], acc);
+            }
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
@@ -93,6 +121,8 @@ __global__ void __launch_bounds__(kBlkThreads) k_block_pre(const float* __restri
 __global__ void k_block_post(const float* __restrict__ x, const float* __restrict__ ffn, const float* __restrict__ sh,
                              const float* __restrict__ sgate, float* __restrict__ out, int* __restrict__ bad,
                              int hidden, long long n) {
+    pdl_trigger_dependents();
+    pdl_grid_wait();
     bool finite = true;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
         float f = ffn[i];
@@ -118,9 +148,10 @@ extern "C" int qw6k_block_pre(const float* x, const float* add, float* xsum, int
     static DevFlags cfg;
     if (hidden * 4 > 48 * 1024 && smem_optin(cfg, k_block_pre, (int)hidden * 4)) return QW6K_ERR_CUDA;
     const dim3 grid((ne + kBlkThreads / 32 - 1) / (kBlkThreads / 32), ntok);
-    k_block_pre<<<grid, kBlkThreads, (size_t)hidden * 4, st>>>(x, add, xsum, bad, norm_w, router, srouter, normed,
-                                                               logits, sgate, (int)hidden, (int)ne);
-    return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
+    return launch_pdl(k_block_pre, grid, dim3(kBlkThreads), (size_t)hidden * 4, st, x, add, xsum, bad, norm_w, router,
+                      srouter, normed, logits, sgate, (int)hidden, (int)ne) == cudaSuccess
+               ? 0
+               : QW6K_ERR_CUDA;
 }
 
 extern "C" int qw6k_block_post(const float* x, const float* ffn, const float* shared, const float* sgate, float* out,
@@ -128,6 +159,8 @@ extern "C" int qw6k_block_post(const float* x, const float* ffn, const float* sh
     if (!x || !ffn || !out || !ntok || !hidden || (shared && !sgate)) return QW6K_ERR_ARG;
     const long long n = (long long)ntok * hidden;
     const int grid = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
-    k_block_post<<<grid, 256, 0, st>>>(x, ffn, shared, sgate, out, bad, (int)hidden, n);
-    return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
+    return launch_pdl(k_block_post, dim3(grid), dim3(256), 0, st, x, ffn, shared, sgate, out, bad, (int)hidden, n) ==
+                   cudaSuccess
+               ? 0
+               : QW6K_ERR_CUDA;
 }

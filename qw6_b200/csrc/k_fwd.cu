@@ -26,11 +26,17 @@
 //                 qw6.c:2750-2793) and gate with sigmoid(gate) (qw6.c:2419).
 // Element-wise steps use qw6's operations in its order with IEEE rounding
 // (__fmul_rn, __fadd_rn, ...: no contraction); dot products and sums are
-// reductions in another order than qw6's sequential loops.
+// reductions in another order than qw6's sequential loops.  Every kernel is
+// launched with programmatic dependent launch: it lets its successor start,
+// may load weights (written once, at upload), and waits for its predecessor
+// before it reads anything a kernel writes -- the recurrent state and the
+// caches included: reading those before the wait gave wrong results on the
+// B200 although no kernel of the step writes them before.
 #include <cuda_runtime.h>
 
 #include "qw6_launch.h"
 #include "qw6_norm.cuh"
+#include "qw6_pdl.cuh"
 
 namespace qw6 {
 
@@ -60,12 +66,33 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
-// out = rmsnorm(x) * w as qw6_cpu_rmsnorm evaluates it; one CTA.
+// out = rmsnorm(x) * w as qw6_cpu_rmsnorm evaluates it; one CTA of 256
+// threads, dim <= 4096 (each thread keeps its values in registers).
 __global__ void __launch_bounds__(256) k_rmsnorm(const float* __restrict__ x, const float* __restrict__ w,
                                                  float* __restrict__ out, int dim) {
     __shared__ float red[8];
-    const float inv = rms_inv(x, dim, red);
-    for (int i = threadIdx.x; i < dim; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(x[i], inv), w[i]);
+    pdl_trigger_dependents();
+    float wv[16], xv[16];
+#pragma unroll
+    for (int u = 0; u < 16; u++) {
+        const int i = threadIdx.x + 256 * u;
+        wv[u] = i < dim ? w[i] : 0.f;
+    }
+    pdl_grid_wait();
+    float ss = 0.f;
+#pragma unroll
+    for (int u = 0; u < 16; u++) {
+        const int i = threadIdx.x + 256 * u;
+        xv[u] = i < dim ? x[i] : 0.f;
+        ss = fmaf(xv[u], xv[u], ss);
+    }
+    const float t = block_sum(ss, red);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)dim), kRmsEps)));
+#pragma unroll
+    for (int u = 0; u < 16; u++) {
+        const int i = threadIdx.x + 256 * u;
+        if (i < dim) out[i] = __fmul_rn(__fmul_rn(xv[u], inv), wv[u]);
+    }
 }
 
 // grid 64 x 128 threads: CTA b owns channels [128 b, 128 b + 128) of the conv
@@ -75,7 +102,9 @@ __global__ void __launch_bounds__(128) k_dn_conv(const float* __restrict__ proj,
                                                  const float* __restrict__ a, float* __restrict__ conv,
                                                  float* __restrict__ gb) {
     __shared__ float red[4];
+    pdl_trigger_dependents();
     const int c = blockIdx.x * 128 + threadIdx.x;
+    pdl_grid_wait();
     // the window holds the 4 latest qkv rows, oldest first (qw6.c:2327-2331)
     const float s0 = cs[1 * kQKV + c], s1 = cs[2 * kQKV + c], s2 = cs[3 * kQKV + c], s3 = proj[c];
     cs[c] = s0;
@@ -106,16 +135,18 @@ __global__ void __launch_bounds__(512) k_dn_step(const float* __restrict__ conv,
                                                  float* __restrict__ state, float* __restrict__ gated) {
     __shared__ float o[kVD];
     __shared__ float red[16];
+    pdl_trigger_dependents();
     const int vh = blockIdx.x, kh = vh % kKH, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_grid_wait();
+    float4* s = reinterpret_cast<float4*>(state + (size_t)vh * kVD * kVD);
+    float4 row[8];
+#pragma unroll
+    for (int r = 0; r < 8; r++) row[r] = s[(warp * 8 + r) * (kVD / 4) + lane];
     const float4 k4 = reinterpret_cast<const float4*>(conv + kKH * kKD + kh * kKD)[lane];
     const float4 q4 = reinterpret_cast<const float4*>(conv + kh * kKD)[lane];
     const float* v = conv + 2 * kKH * kKD + vh * kVD;
     const float b = gb[vh], decay = expf(gb[kVH + vh]);
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)kVD));
-    float4* s = reinterpret_cast<float4*>(state + (size_t)vh * kVD * kVD);
-    float4 row[8];
-#pragma unroll
-    for (int r = 0; r < 8; r++) row[r] = s[(warp * 8 + r) * (kVD / 4) + lane];
 #pragma unroll
     for (int r = 0; r < 8; r++) {
         const int j = warp * 8 + r;
@@ -154,6 +185,8 @@ __global__ void __launch_bounds__(256) k_fa_prep(const float* __restrict__ proj,
                                                  float* __restrict__ vc, float* __restrict__ qr) {
     __shared__ float y[kHD];
     __shared__ float red[8];
+    pdl_trigger_dependents();
+    pdl_grid_wait();
     const int h = blockIdx.x, d = threadIdx.x;
     const uint32_t pos = step->pos;
     const bool isq = h < kQH;
@@ -192,6 +225,8 @@ __device__ __forceinline__ void fa_chunk(uint32_t seq, int c, uint32_t& c0, uint
 __global__ void __launch_bounds__(256) k_fa_attn(const float* __restrict__ qr, const float* __restrict__ kc,
                                                  const float* __restrict__ vc, const qw6k_step* __restrict__ step,
                                                  float* __restrict__ part) {
+    pdl_trigger_dependents();
+    pdl_grid_wait();
     const uint32_t seq = step->pos + 1;
     uint32_t c0, c1;
     fa_chunk(seq, blockIdx.x, c0, c1);
@@ -256,6 +291,8 @@ __global__ void __launch_bounds__(256) k_fa_attn(const float* __restrict__ qr, c
 // grid 16 (query heads) x 256 (dimensions)
 __global__ void __launch_bounds__(256) k_fa_combine(const float* __restrict__ part, const float* __restrict__ proj,
                                                     const qw6k_step* __restrict__ step, float* __restrict__ attn) {
+    pdl_trigger_dependents();
+    pdl_grid_wait();
     const uint32_t seq = step->pos + 1;
     const int h = blockIdx.x, d = threadIdx.x;
     int nc = 0;
@@ -278,6 +315,8 @@ __global__ void __launch_bounds__(256) k_fa_combine(const float* __restrict__ pa
 }
 
 __global__ void k_check_finite(const float* __restrict__ x, uint32_t n, int* __restrict__ bad) {
+    pdl_trigger_dependents();
+    pdl_grid_wait();
     bool finite = true;
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
         finite = finite && isfinite(x[i]);
@@ -287,6 +326,7 @@ __global__ void k_check_finite(const float* __restrict__ x, uint32_t n, int* __r
 // the step's greedy token (largest packed argmax key: largest logit, lowest
 // index on ties) becomes the next step's input at the next position
 __global__ void k_step_next(qw6k_step* __restrict__ step, const unsigned long long* __restrict__ key) {
+    pdl_grid_wait();
     step->token = ~(uint32_t)(*key & 0xffffffffull);
     step->pos += 1;
 }
@@ -295,37 +335,40 @@ __global__ void k_step_next(qw6k_step* __restrict__ step, const unsigned long lo
 
 using namespace qw6;
 
-static int launched() { return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA; }
-
 extern "C" size_t qw6k_fa_part_floats(void) { return (size_t)kQH * kFaSplit * (2 + kHD); }
 
 extern "C" int qw6k_rmsnorm(const float* x, const float* w, float* out, uint32_t dim, cudaStream_t st) {
     if (!x || !w || !out || !dim) return QW6K_ERR_ARG;
-    k_rmsnorm<<<1, 256, 0, st>>>(x, w, out, (int)dim);
-    return launched();
+    if (dim > 4096) return QW6K_ERR_ARG;
+    return launch_pdl(k_rmsnorm, dim3(1), dim3(256), 0, st, x, w, out, (int)dim) == cudaSuccess ? 0 : QW6K_ERR_CUDA;
 }
 
 extern "C" int qw6k_dn_conv(const float* proj, float* conv_state, const float* conv_w, const float* dt, const float* a,
                             float* conv, float* gb, cudaStream_t st) {
     if (!proj || !conv_state || !conv_w || !dt || !a || !conv || !gb) return QW6K_ERR_ARG;
     if (reinterpret_cast<uintptr_t>(conv_w) & 15u) return QW6K_ERR_ALIGN;
-    k_dn_conv<<<kQKV / 128, 128, 0, st>>>(proj, conv_state, conv_w, dt, a, conv, gb);
-    return launched();
+    return launch_pdl(k_dn_conv, dim3(kQKV / 128), dim3(128), 0, st, proj, conv_state, conv_w, dt, a, conv, gb) ==
+                   cudaSuccess
+               ? 0
+               : QW6K_ERR_CUDA;
 }
 
 extern "C" int qw6k_dn_step(const float* conv, const float* gb, const float* z, const float* dn_norm, float* state,
                             float* gated, cudaStream_t st) {
     if (!conv || !gb || !z || !dn_norm || !state || !gated) return QW6K_ERR_ARG;
     if ((reinterpret_cast<uintptr_t>(conv) | reinterpret_cast<uintptr_t>(state)) & 15u) return QW6K_ERR_ALIGN;
-    k_dn_step<<<kVH, 512, 0, st>>>(conv, gb, z, dn_norm, state, gated);
-    return launched();
+    return launch_pdl(k_dn_step, dim3(kVH), dim3(512), 0, st, conv, gb, z, dn_norm, state, gated) == cudaSuccess
+               ? 0
+               : QW6K_ERR_CUDA;
 }
 
 extern "C" int qw6k_fa_prep(const float* proj, const float* q_norm, const float* k_norm, const float* freq,
                             const qw6k_step* step, float* k_cache, float* v_cache, float* q_rot, cudaStream_t st) {
     if (!proj || !q_norm || !k_norm || !freq || !step || !k_cache || !v_cache || !q_rot) return QW6K_ERR_ARG;
-    k_fa_prep<<<kQH + kKVH, kHD, 0, st>>>(proj, q_norm, k_norm, freq, step, k_cache, v_cache, q_rot);
-    return launched();
+    return launch_pdl(k_fa_prep, dim3(kQH + kKVH), dim3(kHD), 0, st, proj, q_norm, k_norm, freq, step, k_cache,
+                      v_cache, q_rot) == cudaSuccess
+               ? 0
+               : QW6K_ERR_CUDA;
 }
 
 extern "C" int qw6k_fa_attn(const float* q_rot, const float* k_cache, const float* v_cache, const qw6k_step* step,
@@ -334,22 +377,21 @@ extern "C" int qw6k_fa_attn(const float* q_rot, const float* k_cache, const floa
     if ((reinterpret_cast<uintptr_t>(q_rot) | reinterpret_cast<uintptr_t>(k_cache) |
          reinterpret_cast<uintptr_t>(v_cache) | reinterpret_cast<uintptr_t>(part)) & 15u)
         return QW6K_ERR_ALIGN;
-    k_fa_attn<<<dim3(kFaSplit, kKVH), 256, 0, st>>>(q_rot, k_cache, v_cache, step, part);
-    const int rc = launched();
-    if (rc) return rc;
-    k_fa_combine<<<kQH, kHD, 0, st>>>(part, proj, step, attn);
-    return launched();
+    if (launch_pdl(k_fa_attn, dim3(kFaSplit, kKVH), dim3(256), 0, st, q_rot, k_cache, v_cache, step, part) !=
+        cudaSuccess)
+        return QW6K_ERR_CUDA;
+    return launch_pdl(k_fa_combine, dim3(kQH), dim3(kHD), 0, st, part, proj, step, attn) == cudaSuccess
+               ? 0
+               : QW6K_ERR_CUDA;
 }
 
 extern "C" int qw6k_check_finite(const float* x, uint32_t n, int* bad, cudaStream_t st) {
     if (!x || !n || !bad) return QW6K_ERR_ARG;
     const uint32_t grid = (n + 1023) / 1024 < 148 ? (n + 1023) / 1024 : 148;
-    k_check_finite<<<grid, 256, 0, st>>>(x, n, bad);
-    return launched();
+    return launch_pdl(k_check_finite, dim3(grid), dim3(256), 0, st, x, n, bad) == cudaSuccess ? 0 : QW6K_ERR_CUDA;
 }
 
 extern "C" int qw6k_step_next(qw6k_step* step, const unsigned long long* key, cudaStream_t st) {
     if (!step || !key) return QW6K_ERR_ARG;
-    k_step_next<<<1, 1, 0, st>>>(step, key);
-    return launched();
+    return launch_pdl(k_step_next, dim3(1), dim3(1), 0, st, step, key) == cudaSuccess ? 0 : QW6K_ERR_CUDA;
 }

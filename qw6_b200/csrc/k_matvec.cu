@@ -11,6 +11,7 @@
 #include "qw6_devcfg.cuh"
 #include "qw6_grids.cuh"
 #include "qw6_launch.h"
+#include "qw6_pdl.cuh"
 
 namespace qw6 {
 
@@ -183,9 +184,11 @@ __global__ void __launch_bounds__(kThreads, NQ == 1 ? 2 : 1) k_matvec(const MvAr
     };
     auto step_ok = [&](int step) { return step < nsteps && item_mt(step / nbk) < a.mtiles; };
 
+    pdl_trigger();
     typename T::Frag fa, fb, fc;
-    if (step_ok(0)) T::load(fa, tile_ptr(0), lane);
+    if (step_ok(0)) T::load(fa, tile_ptr(0), lane);  // weights: nothing earlier in the stream writes them
     if constexpr (IsIQ<F>::value) IQLut<F>::init(tbl, grid_ptr<F>());
+    pdl_wait();  // x comes from the previous kernel
     xstage_fill(xs, a.x, a.ldx, a.ntok, 4 * NQ, a.cols);
     __syncthreads();
     const XView xv = xs.view();
@@ -419,8 +422,8 @@ static int launch_mv(const uint8_t* w, const float* x, float* y, int rows, int c
     const int wpm = kWarps / ks;
     const long long ngrp = (a.mtiles + wpm - 1) / wpm;
     const int grid = (int)(ngrp < (long long)num_sms() * occ ? ngrp : (long long)num_sms() * occ);
-    k_matvec<F, NQ, KEYS><<<grid, kThreads, smem, st>>>(a);
-    return cudaPeekAtLastError() == cudaSuccess ? 0 : QW6K_ERR_CUDA;
+    return launch_pdl(k_matvec<F, NQ, KEYS>, dim3(grid), dim3(kThreads), smem, st, a) == cudaSuccess ? 0
+                                                                                         : QW6K_ERR_CUDA;
 }
 
 // Token batches: 1-4 and 5-8 tokens in one launch; 9-32 tokens in one launch

@@ -158,6 +158,10 @@ __global__ void __launch_bounds__(kThreads) k_moe_small_gu(const MoeArgs a) {
     using T = Tile<F, 1>;
     constexpr int TB = T::TB;
     __shared__ SmallPlan P;
+    // logits and x come from the previous kernel.  The down kernel routes
+    // from the same logits before its own wait, so it may start only once
+    // this kernel is past its wait (the logits are then complete).
+    pdl_wait();
     pdl_trigger();
     const int nbh = a.hidden / 256, ks = nbh / NBW, mpc = kWarps / ks;
     const int mgroups = (a.inter / 16) / mpc;
@@ -515,7 +519,7 @@ static int launch_small_gu(const MoeArgs& a, cudaStream_t st) {
     static DevFlags cfg;
     if (smem_optin(cfg, k_moe_small_gu<F, NBW>, 200 * 1024)) return QW6K_ERR_CUDA;
     const int ks = a.hidden / 256 / NBW, mgroups = (a.inter / 16) / (kWarps / ks);
-    return launch_ex(k_moe_small_gu<F, NBW>, a.ntok * a.topk * mgroups, kThreads, smem, false, st, a);
+    return launch_ex(k_moe_small_gu<F, NBW>, a.ntok * a.topk * mgroups, kThreads, smem, true, st, a);
 }
 
 template <int F>

@@ -41,6 +41,8 @@ __global__ void k_gather(const float* __restrict__ eo, const float* __restrict__
 __device__ __forceinline__ float silu_ref(float v) { return __fdiv_rn(v, __fadd_rn(1.0f, expf(-v))); }
 
 __global__ void k_silu_mul(const float* __restrict__ g, const float* __restrict__ u, float* __restrict__ o, int n) {
+    pdl_trigger_dependents();
+    pdl_grid_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) o[i] = __fmul_rn(silu_ref(g[i]), u[i]);
 }
@@ -139,8 +141,9 @@ extern "C" int qw6k_moe_gather(const float* eo, const float* w, const float* sha
 
 extern "C" int qw6k_silu_mul(const float* g, const float* u, float* o, uint32_t n, cudaStream_t st) {
     if (!g || !u || !o || !n) return QW6K_ERR_ARG;
-    k_silu_mul<<<(n + 255) / 256, 256, 0, st>>>(g, u, o, (int)n);
-    return launched();
+    return launch_pdl(k_silu_mul, dim3((n + 255) / 256), dim3(256), 0, st, g, u, o, (int)n) == cudaSuccess
+               ? 0
+               : QW6K_ERR_CUDA;
 }
 
 extern "C" int qw6k_argmax(const float* x, uint32_t n, unsigned long long* key64, uint32_t* out_idx, float* out_val,

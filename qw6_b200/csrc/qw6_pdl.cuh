@@ -12,6 +12,9 @@
 namespace qw6 {
 
 __device__ __forceinline__ void pdl_grid_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
@@ -23,7 +26,11 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
     cfg.stream = st;
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+#ifdef QW6_PDL_OFF  // diagnostic builds: plain stream order
+    at[0].val.programmaticStreamSerializationAllowed = 0;
+#else
     at[0].val.programmaticStreamSerializationAllowed = 1;
+#endif
     cfg.attrs = at;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
