@@ -278,12 +278,16 @@ def run_ours(args, rank, local_rank, world):
     if rank == 0 and args.matvec:
         matvec = {"configs": matvec_configs(torch, ctx, stream), "tall_sweep": matvec_sweep(torch, ctx, stream)}
     lmh = lm_head_bench(torch, ctx, stream, rank, world, dist) if args.lm_head else None
+    dstep = decoder_bench(args, ctx, L) if (args.decoder and rank == 0) else None
+    if dist:
+        dist.barrier()
     result = None
     if rank == 0:
         result = report(args, world, head, cpu)
         result["decode"] = dec or None
         result["matvec"] = matvec
         result["lm_head"] = lmh
+        result["decoder"] = dstep
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -804,6 +808,88 @@ def report(args, world, head, cpu):
 
 # --------------------------------------------------------- reference arm --
 
+def decoder_step_bytes(model, pos: int) -> int:
+    """Algorithmic HBM bytes of one decode step at position pos: every weight
+    the step reads once (the 8 routed experts of each layer only), the fp32
+    router, the DeltaNet states and conv windows read and written, the KV
+    cache rows read (pos + 1 per attention layer) and the one written, the
+    embedding row and the logits."""
+    from qw6_b200 import synth as S
+    n, seen = 0, set()
+    for f, l, q, r, c, arr, stride in model.tensors:
+        if f in (S.F_EXPERT_GATE, S.F_EXPERT_UP, S.F_EXPERT_DOWN):
+            n += 8 * r * S.row_bytes(q, c)
+        elif f == S.F_TOK_EMBD:
+            n += S.row_bytes(q, c)
+        else:
+            n += r * S.row_bytes(q, c)
+    for l in range(model.n_layers):
+        if S.is_full_attn(l):
+            n += (pos + 1) * 2 * 512 * 4 + 2 * 512 * 4
+        else:
+            n += 2 * (32 * 128 * 128 * 4 + 4 * 8192 * 4)
+    return n + model.vocab * 4
+
+
+def decoder_bench(args, ctx, L):
+    """The decode-step executor on a full-size synthetic qw6 model (40 layers,
+    distinct weights per layer: IQ2_XXS experts, Q6_K projections, shared
+    expert, embeddings and LM head, 248320-token vocabulary): greedy tokens
+    chained on the device (qw6cu_decoder_generate) and, end to end, one
+    qw6cu_decoder_forward per token with the token id from the host and the
+    pick (and optionally the logits) back.  Replicas only: a step is one
+    token of one sequence; this runs on rank 0."""
+    import torch
+    from qw6_b200 import synth as S
+    t0 = time.perf_counter()
+    m = S.fwd_model(seed=31, n_layers=40, vocab=S.VOCAB, embd_rows=S.VOCAB, attn_period=40, expert_period=40)
+    gen_s = time.perf_counter() - t0
+    n = args.decoder_tokens
+    dec = L.Decoder(ctx, m, max_ctx=max(4096, 2 * n + 64))
+    dev_bytes = dec.device_bytes()
+    step_bytes = [decoder_step_bytes(m, p) for p in range(n)]
+    del m
+    dec.generate(1, 0, 8)  # warm-up
+    dec.reset()
+    hbm, peak_kind = peaks()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    toks = dec.generate(1, 0, n)
+    dt = time.perf_counter() - t0
+    # end to end: host token in, pick back, every step synchronous
+    dec.reset()
+    tok, t1 = 1, time.perf_counter()
+    for p in range(n):
+        _, tok = dec.forward(tok, p, logits=False)
+    e2e = time.perf_counter() - t1
+    dec.reset()
+    tok, t2 = 1, time.perf_counter()
+    for p in range(min(n, 64)):
+        _, tok = dec.forward(tok, p, logits=True)
+    e2e_l = (time.perf_counter() - t2) / min(n, 64)
+    dec.close()
+    avg_bytes = sum(step_bytes) / n
+    gbs = avg_bytes * n / dt / 1e9
+    return {
+        "workload": "decode-step executor: full qw6 forward pass per token (40 layers: 30 Gated DeltaNet + 10 gated "
+                    "attention, MoE 256x top-8 IQ2_XXS + Q6_K shared expert, Q6_K projections / embeddings / LM head "
+                    "248320) on one GPU, greedy, positions 0..n-1 (replicas only)",
+        "data": "synthetic (seeded qw6 model, distinct weights per layer)",
+        "tokens": n, "tokens_s": round(n / dt, 1), "ms_per_token": round(dt / n * 1e3, 4),
+        "timing": "wall clock around qw6cu_decoder_generate (one CUDA graph replay per token, chained on the device, "
+                  "one synchronization at the end)",
+        "algorithmic_bytes_per_token": int(avg_bytes), "device_bytes": int(dev_bytes),
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(gbs / hbm, 4), "peak_kind": peak_kind, "scope": "whole step"},
+        "e2e": {"value": round(n / e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": 16, "d2h_bytes_per_step": 16,
+                "api": "qw6cu_decoder_forward per token (host token id in, greedy pick out, synchronous)",
+                "with_logits_ms_per_token": round(e2e_l * 1e3, 4),
+                "with_logits_d2h_bytes_per_step": S.VOCAB * 4 + 16},
+        "first_tokens": [int(t) for t in toks[:8]],
+        "model_generation_s": round(gen_s, 1),
+    }
+
+
 def run_reference(args, rank, world):
     """qw6's own CPU implementation of config 3's layer (oracle/_ref) on all
     usable host cores: each step runs a bounded sample of the 4096 tokens,
@@ -861,6 +947,9 @@ def main():
     ap.add_argument("--no-lm-head", dest="lm_head", action="store_false")
     ap.add_argument("--no-decode", dest="decode", action="store_false")
     ap.add_argument("--decode-steps", type=int, default=8192)
+    ap.add_argument("--no-decoder", dest="decoder", action="store_false",
+                    help="skip the full-model decode-step executor leg")
+    ap.add_argument("--decoder-tokens", type=int, default=256)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -207,7 +207,8 @@ typedef struct {
  *   ffn = routed experts (qw6cu_moe_decode on normed and logits)
  *         + s * shared_down(silu(shared_gate normed) * shared_up normed),
  *   out = x + ffn.
- * router: fp32 [n_experts x hidden] row-major, 16-byte aligned; norm_w fp32
+ * router (and shared->router): fp32 [n_experts x hidden] row-major, 16-byte
+ * aligned; norm_w fp32
  * [hidden]; shared: NULL for none.  x, out: fp32 [ntok x hidden]; all device
  * pointers, enqueued on the context's stream with no host synchronization
  * (the context workspace is grown on first use, which synchronizes).  The

@@ -21,12 +21,13 @@
 
 namespace qw6 {
 
-constexpr int kBlkThreads = 256;
+constexpr int kBlkThreads = 256;  // 8 router rows per CTA
 constexpr int kRowRegs = 16;  // float4 of a router row a lane holds in registers (hidden <= 2048)
 
-// grid (ceil(ne / 8), ntok): CTA (b, t) computes router rows [8b, 8b+8) of
-// token t (warp per row), CTA (0, t) also writes normed[t], and the last CTA
-// of the token the shared-expert gate sigmoid(shared_router . normed).
+// grid (ceil((ne + 1) / 8), ntok): CTA (b, t) computes rows [8b, 8b+8) of
+// token t (warp per row): rows < ne are the router's, row ne is the shared
+// router (gate sigmoid(shared_router . normed), or 1 without one); CTA (0, t)
+// also writes normed[t].
 // normed[i] = (x[i] * inv) * w[i] as qw6 evaluates it.  With `add` the block
 // input is x + add (the residual add before the FFN, qw6.c:2469-2470), which
 // CTA (0, t) stores to xsum and checks for NaN/Inf (sets *bad, qw6.c:2472).
@@ -45,19 +46,21 @@ __global__ void __launch_bounds__(kBlkThreads) k_block_pre(const float* __restri
     // kernel finishes, then the wait for x / add
     pdl_trigger_dependents();
     const int r = blockIdx.x * (kBlkThreads / 32) + warp;
-    const bool held = r < ne && hidden <= 128 * kRowRegs;
+    // this warp's row: a router row, or the shared router as row ne
+    const float* wr = r < ne ? router + (size_t)r * hidden : (r == ne ? srouter : nullptr);
+    const bool held = wr && hidden <= 128 * kRowRegs;
     float4 wv[kRowRegs];
 #pragma unroll
     for (int u = 0; u < kRowRegs; u++) {
         const int c = 4 * lane + 128 * u;
-        wv[u] = held && c < hidden ? __ldg(reinterpret_cast<const float4*>(router + (size_t)r * hidden + c))
-                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+        wv[u] = held && c < hidden ? __ldg(reinterpret_cast<const float4*>(wr + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     pdl_grid_wait();
     const float* xt = x + (size_t)t * hidden;
     if (add) {  // x + add into shared memory first, then the norm of the sum
         const float* at = add + (size_t)t * hidden;
         bool finite = true;
+#pragma unroll 8
         for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
             const float v = __fadd_rn(xt[i], at[i]);
             nrm[i] = v;
@@ -69,14 +72,14 @@ __global__ void __launch_bounds__(kBlkThreads) k_block_pre(const float* __restri
         xt = nrm;
     }
     const float inv = rms_inv(xt, hidden, red);
+#pragma unroll 8
     for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
         const float v = __fmul_rn(__fmul_rn(xt[i], inv), norm_w[i]);
         nrm[i] = v;  // each thread rewrites only the entries it read
         if (blockIdx.x == 0) normed[(size_t)t * hidden + i] = v;
     }
     __syncthreads();
-    if (r < ne) {
-        const float* wr = router + (size_t)r * hidden;
+    if (wr) {
         float acc = 0.f;
         if (held) {
 #pragma unroll
@@ -100,19 +103,12 @@ __global__ void __launch_bounds__(kBlkThreads) k_block_pre(const float* __restri
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (lane == 0) logits[(size_t)t * ne + r] = acc;
-    }
-    if (blockIdx.x == gridDim.x - 1 && warp == (kBlkThreads / 32) - 1) {
-        float s = 1.0f;  // no shared router: weight 1 (qw6.c:2268)
-        if (srouter) {
-            float acc = 0.f;
-            for (int c = lane; c < hidden; c += 32) acc = fmaf(srouter[c], nrm[c], acc);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-            s = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-acc)));  // qw6_sigmoid (qw6.h:295-297)
+        if (lane == 0) {
+            if (r < ne) logits[(size_t)t * ne + r] = acc;
+            else sgate[t] = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-acc)));  // qw6_sigmoid (qw6.h:295-297)
         }
-        if (lane == 0) sgate[t] = s;
     }
+    if (!srouter && r == ne && lane == 0) sgate[t] = 1.0f;  // no shared router: weight 1 (qw6.c:2268)
 }
 
 // out[t][i] = x[t][i] + (ffn[t][i] + s[t] * sh[t][i])  (sh may be null: no
@@ -134,6 +130,52 @@ __global__ void k_block_post(const float* __restrict__ x, const float* __restric
     if (!finite && bad) atomicOr(bad, 1);
 }
 
+// One token row per CTA (hidden <= 4096): out = x + (ffn + s * sh) as
+// k_block_post, then normed = rmsnorm(out) * w as qw6_cpu_rmsnorm (the next
+// layer's input norm, or the final norm before the LM head, qw6.c:2462,
+// 2493): the residual add and the norm that follows it in one pass.
+__global__ void __launch_bounds__(256) k_post_norm(const float* __restrict__ x, const float* __restrict__ ffn,
+                                                   const float* __restrict__ sh, const float* __restrict__ sgate,
+                                                   float* __restrict__ out, int* __restrict__ bad,
+                                                   const float* __restrict__ w, float* __restrict__ normed,
+                                                   int hidden) {
+    __shared__ float red[8];
+    pdl_trigger_dependents();
+    float wv[16], ov[16];
+#pragma unroll
+    for (int u = 0; u < 16; u++) {
+        const int i = threadIdx.x + 256 * u;
+        wv[u] = i < hidden ? w[i] : 0.f;
+    }
+    pdl_grid_wait();
+    const size_t base = (size_t)blockIdx.x * hidden;
+    const float s = sh ? sgate[blockIdx.x] : 0.f;
+    bool finite = true;
+    float ss = 0.f;
+#pragma unroll
+    for (int u = 0; u < 16; u++) {
+        const int i = threadIdx.x + 256 * u;
+        ov[u] = 0.f;
+        if (i < hidden) {
+            float f = ffn[base + i];
+            if (sh) f = __fadd_rn(f, __fmul_rn(s, sh[base + i]));
+            const float o = __fadd_rn(x[base + i], f);
+            out[base + i] = o;
+            ov[u] = o;
+            finite = finite && isfinite(o);
+            ss = fmaf(o, o, ss);
+        }
+    }
+    if (!finite && bad) atomicOr(bad, 1);
+    const float t = block_sum(ss, red);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)hidden), kRmsEps)));
+#pragma unroll
+    for (int u = 0; u < 16; u++) {
+        const int i = threadIdx.x + 256 * u;
+        if (i < hidden) normed[base + i] = __fmul_rn(__fmul_rn(ov[u], inv), wv[u]);
+    }
+}
+
 }  // namespace qw6
 
 using namespace qw6;
@@ -144,10 +186,12 @@ extern "C" int qw6k_block_pre(const float* x, const float* add, float* xsum, int
     if (!x || !norm_w || !router || !normed || !logits || !sgate || !ntok || ntok > 65535 || !hidden ||
         hidden % 4 || hidden > 16384 || !ne || ne > 256 || (add && !xsum))
         return QW6K_ERR_ARG;
-    if ((reinterpret_cast<uintptr_t>(router) | reinterpret_cast<uintptr_t>(x)) & 15u) return QW6K_ERR_ALIGN;
+    if ((reinterpret_cast<uintptr_t>(router) | reinterpret_cast<uintptr_t>(srouter) | reinterpret_cast<uintptr_t>(x)) &
+        15u)
+        return QW6K_ERR_ALIGN;
     static DevFlags cfg;
     if (hidden * 4 > 48 * 1024 && smem_optin(cfg, k_block_pre, (int)hidden * 4)) return QW6K_ERR_CUDA;
-    const dim3 grid((ne + kBlkThreads / 32 - 1) / (kBlkThreads / 32), ntok);
+    const dim3 grid((ne + 1 + kBlkThreads / 32 - 1) / (kBlkThreads / 32), ntok);
     return launch_pdl(k_block_pre, grid, dim3(kBlkThreads), (size_t)hidden * 4, st, x, add, xsum, bad, norm_w, router,
                       srouter, normed, logits, sgate, (int)hidden, (int)ne) == cudaSuccess
                ? 0
@@ -161,6 +205,18 @@ extern "C" int qw6k_block_post(const float* x, const float* ffn, const float* sh
     const int grid = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
     return launch_pdl(k_block_post, dim3(grid), dim3(256), 0, st, x, ffn, shared, sgate, out, bad, (int)hidden, n) ==
                    cudaSuccess
+               ? 0
+               : QW6K_ERR_CUDA;
+}
+
+extern "C" int qw6k_post_norm(const float* x, const float* ffn, const float* shared, const float* sgate, float* out,
+                              int* bad, const float* norm_w, float* normed, uint32_t ntok, uint32_t hidden,
+                              cudaStream_t st) {
+    if (!x || !ffn || !out || !norm_w || !normed || !ntok || ntok > 65535 || !hidden || hidden > 4096 ||
+        (shared && !sgate))
+        return QW6K_ERR_ARG;
+    return launch_pdl(k_post_norm, dim3(ntok), dim3(256), 0, st, x, ffn, shared, sgate, out, bad, norm_w, normed,
+                      (int)hidden) == cudaSuccess
                ? 0
                : QW6K_ERR_CUDA;
 }

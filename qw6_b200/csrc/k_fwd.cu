@@ -4,15 +4,14 @@
 // step is position-independent and is captured once in a CUDA graph.
 //
 // Gated DeltaNet layer (qw6_apply_linear_attn, qw6.c:2292-2360), after the
-// projections [qkv 8192 | z 4096 | beta 32 | alpha 32] of the normalised row:
-//   k_dn_conv  slide the 4-tap conv window, conv + silu per channel,
-//              l2-normalise the 16 query and 16 key heads (qw6.c:2055-2063),
-//              beta = sigmoid(beta), g = softplus(alpha + dt) * a;
-//   k_dn_step  per value head vh (key head vh % 16, qw6.c:2084): for every
-//              state row j: row *= exp(g); pred = row . k;
-//              row += (v[j] - pred) * beta * k; o[j] = (row . q) / sqrt(128)
-//              (qw6_gated_delta_net_single, qw6.c:2079-2108), then
-//              rmsnorm(o) * silu(z) (qw6.c:2349-2355).
+// projections [qkv 8192 | z 4096 | beta 32 | alpha 32] of the normalised row,
+// in one kernel (k_dn_token): the 4-tap causal conv with silu, the l2 norm
+// of the 16 query and 16 key heads (qw6.c:2055-2063), beta = sigmoid(beta),
+// g = softplus(alpha + dt) * a, then per value head vh (key head vh % 16,
+// qw6.c:2084) for every state row j: row *= exp(g); pred = row . k;
+// row += (v[j] - pred) * beta * k; o[j] = (row . q) / sqrt(128)
+// (qw6_gated_delta_net_single, qw6.c:2079-2108), and rmsnorm(o) * silu(z)
+// (qw6.c:2349-2355).
 // Gated attention layer (qw6_apply_full_attn, qw6.c:2368-2424), after the
 // projections [q|gate per head: 16 x 512 | k 512 | v 512]:
 //   k_fa_prep     rmsnorm per head with q_norm / k_norm, RoPE on the first 64
@@ -95,57 +94,71 @@ __global__ void __launch_bounds__(256) k_rmsnorm(const float* __restrict__ x, co
     }
 }
 
-// grid 64 x 128 threads: CTA b owns channels [128 b, 128 b + 128) of the conv
-// (b < 16: query head b, b < 32: key head b - 16, else values).
-__global__ void __launch_bounds__(128) k_dn_conv(const float* __restrict__ proj, float* __restrict__ cs,
-                                                 const float* __restrict__ cw, const float* __restrict__ dt,
-                                                 const float* __restrict__ a, float* __restrict__ conv,
-                                                 float* __restrict__ gb) {
-    __shared__ float red[4];
-    pdl_trigger_dependents();
-    const int c = blockIdx.x * 128 + threadIdx.x;
-    pdl_grid_wait();
-    // the window holds the 4 latest qkv rows, oldest first (qw6.c:2327-2331)
-    const float s0 = cs[1 * kQKV + c], s1 = cs[2 * kQKV + c], s2 = cs[3 * kQKV + c], s3 = proj[c];
-    cs[c] = s0;
-    cs[1 * kQKV + c] = s1;
-    cs[2 * kQKV + c] = s2;
-    cs[3 * kQKV + c] = s3;
-    const float4 w = reinterpret_cast<const float4*>(cw)[c];
-    float sum = __fmul_rn(s0, w.x);
-    sum = __fadd_rn(sum, __fmul_rn(s1, w.y));
-    sum = __fadd_rn(sum, __fmul_rn(s2, w.z));
-    sum = __fadd_rn(sum, __fmul_rn(s3, w.w));
-    float v = silu_f(sum);
-    if (blockIdx.x < 2 * kKH) {  // l2 norm of a query or key head
-        const float ss = block_sum(v * v, red);
-        v = __fmul_rn(v, __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss, kRmsEps))));
-    }
-    conv[c] = v;
-    if (blockIdx.x == 0 && threadIdx.x < kVH) {
-        const int h = threadIdx.x;
-        gb[h] = sigmoid_f(proj[kQKV + kVDim + h]);
-        gb[kVH + h] = __fmul_rn(softplus_f(__fadd_rn(proj[kQKV + kVDim + kVH + h], dt[h])), a[h]);
-    }
-}
-
-// grid 32 (value heads) x 512 threads; warp w updates state rows [8w, 8w + 8).
-__global__ void __launch_bounds__(512) k_dn_step(const float* __restrict__ conv, const float* __restrict__ gb,
-                                                 const float* __restrict__ z, const float* __restrict__ nw,
-                                                 float* __restrict__ state, float* __restrict__ gated) {
-    __shared__ float o[kVD];
+// One token step of a Gated DeltaNet layer, one CTA per value head vh (key
+// head kh = vh % 16, qw6.c:2084), 512 threads.  Threads 0-127 take query
+// channel kh*128 + i of the causal conv, 128-255 key channel 2048 + kh*128 + i,
+// 256-383 value channel 4096 + vh*128 + i: conv over the 4 latest qkv rows,
+// silu, and the l2 norm of the query and key heads (qw6.c:2324-2343).  The
+// conv window is a ring of 4 rows, row p % 4 holding position p's qkv, so a
+// step reads the three older rows and the new projection and writes only row
+// pos % 4 (qw6 shifts its window instead, qw6.c:2327-2331; the taps meet the
+// same positions): the two value heads that share a key head can both
+// compute its query and key without ordering.  Then the state rows, as
+// qw6_gated_delta_net_single (qw6.c:2079-2108), and rmsnorm(o) * silu(z)
+// (qw6.c:2349-2355).
+__global__ void __launch_bounds__(512) k_dn_token(const float* __restrict__ proj, const qw6k_step* __restrict__ step,
+                                                  float* __restrict__ ring, const float* __restrict__ cw,
+                                                  const float* __restrict__ dt, const float* __restrict__ a,
+                                                  const float* __restrict__ nw, float* __restrict__ state,
+                                                  float* __restrict__ gated) {
+    __shared__ __align__(16) float qk[2][kKD];
+    __shared__ float vs[kVD], o[kVD], gbs[2];
     __shared__ float red[16];
     pdl_trigger_dependents();
-    const int vh = blockIdx.x, kh = vh % kKH, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     pdl_grid_wait();
+    const int vh = blockIdx.x, kh = vh % kKH, tid = threadIdx.x, part = tid >> 7, i = tid & 127;
+    const int warp = tid >> 5, lane = tid & 31;
+    const uint32_t pos = step->pos;
+    // this warp's 8 state rows: independent of the conv, loaded first
     float4* s = reinterpret_cast<float4*>(state + (size_t)vh * kVD * kVD);
     float4 row[8];
 #pragma unroll
     for (int r = 0; r < 8; r++) row[r] = s[(warp * 8 + r) * (kVD / 4) + lane];
-    const float4 k4 = reinterpret_cast<const float4*>(conv + kKH * kKD + kh * kKD)[lane];
-    const float4 q4 = reinterpret_cast<const float4*>(conv + kh * kKD)[lane];
-    const float* v = conv + 2 * kKH * kKD + vh * kVD;
-    const float b = gb[vh], decay = expf(gb[kVH + vh]);
+    float v = 0.f;
+    if (part < 3) {
+        const int c = part == 0 ? kh * kKD + i : part == 1 ? kKH * kKD + kh * kKD + i : 2 * kKH * kKD + vh * kVD + i;
+        const float4 w = reinterpret_cast<const float4*>(cw)[c];
+        const float s3 = proj[c];
+        const float s0 = ring[(size_t)((pos + 1) & 3) * kQKV + c];  // position pos - 3
+        const float s1 = ring[(size_t)((pos + 2) & 3) * kQKV + c];  // pos - 2
+        const float s2 = ring[(size_t)((pos + 3) & 3) * kQKV + c];  // pos - 1
+        float sum = __fmul_rn(s0, w.x);
+        sum = __fadd_rn(sum, __fmul_rn(s1, w.y));
+        sum = __fadd_rn(sum, __fmul_rn(s2, w.z));
+        sum = __fadd_rn(sum, __fmul_rn(s3, w.w));
+        v = silu_f(sum);
+        if (part == 2 || vh < kKH) ring[(size_t)(pos & 3) * kQKV + c] = s3;  // one writer per channel
+    }
+    // l2 norms of the query (part 0) and key (part 1) heads: warps 0-3 and 4-7
+    float sq = part < 2 ? v * v : 0.f;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
+    if (lane == 0) red[warp] = sq;
+    if (tid == 0) {
+        gbs[0] = sigmoid_f(proj[kQKV + kVDim + vh]);
+        gbs[1] = __fmul_rn(softplus_f(__fadd_rn(proj[kQKV + kVDim + kVH + vh], dt[vh])), a[vh]);
+    }
+    __syncthreads();
+    if (part < 2) {
+        const float ss = red[4 * part] + red[4 * part + 1] + red[4 * part + 2] + red[4 * part + 3];
+        qk[part][i] = __fmul_rn(v, __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss, kRmsEps))));
+    } else if (part == 2) {
+        vs[i] = v;
+    }
+    __syncthreads();
+    const float4 q4 = reinterpret_cast<const float4*>(qk[0])[lane];
+    const float4 k4 = reinterpret_cast<const float4*>(qk[1])[lane];
+    const float b = gbs[0], decay = expf(gbs[1]);
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)kVD));
 #pragma unroll
     for (int r = 0; r < 8; r++) {
@@ -156,7 +169,7 @@ __global__ void __launch_bounds__(512) k_dn_step(const float* __restrict__ conv,
         x.z = __fmul_rn(x.z, decay);
         x.w = __fmul_rn(x.w, decay);
         const float pred = warp_sum(fmaf(x.w, k4.w, fmaf(x.z, k4.z, fmaf(x.y, k4.y, x.x * k4.x))));
-        const float delta = __fmul_rn(__fsub_rn(v[j], pred), b);
+        const float delta = __fmul_rn(__fsub_rn(vs[j], pred), b);
         x.x = __fadd_rn(x.x, __fmul_rn(delta, k4.x));
         x.y = __fadd_rn(x.y, __fmul_rn(delta, k4.y));
         x.z = __fadd_rn(x.z, __fmul_rn(delta, k4.z));
@@ -166,13 +179,12 @@ __global__ void __launch_bounds__(512) k_dn_step(const float* __restrict__ conv,
         if (lane == 0) o[j] = __fmul_rn(sum, scale);
     }
     __syncthreads();
-    const int i = threadIdx.x;
-    const float oi = i < kVD ? o[i] : 0.f;
+    const float oi = tid < kVD ? o[tid] : 0.f;
     const float ss = block_sum(oi * oi, red);
-    if (i < kVD) {
+    if (tid < kVD) {
         const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)kVD), kRmsEps)));
-        const float y = __fmul_rn(__fmul_rn(oi, inv), nw[i]);
-        gated[vh * kVD + i] = __fmul_rn(y, silu_f(z[vh * kVD + i]));
+        const float y = __fmul_rn(__fmul_rn(oi, inv), nw[tid]);
+        gated[vh * kVD + tid] = __fmul_rn(y, silu_f(proj[kQKV + vh * kVD + tid]));
     }
 }
 
@@ -343,21 +355,13 @@ extern "C" int qw6k_rmsnorm(const float* x, const float* w, float* out, uint32_t
     return launch_pdl(k_rmsnorm, dim3(1), dim3(256), 0, st, x, w, out, (int)dim) == cudaSuccess ? 0 : QW6K_ERR_CUDA;
 }
 
-extern "C" int qw6k_dn_conv(const float* proj, float* conv_state, const float* conv_w, const float* dt, const float* a,
-                            float* conv, float* gb, cudaStream_t st) {
-    if (!proj || !conv_state || !conv_w || !dt || !a || !conv || !gb) return QW6K_ERR_ARG;
-    if (reinterpret_cast<uintptr_t>(conv_w) & 15u) return QW6K_ERR_ALIGN;
-    return launch_pdl(k_dn_conv, dim3(kQKV / 128), dim3(128), 0, st, proj, conv_state, conv_w, dt, a, conv, gb) ==
-                   cudaSuccess
-               ? 0
-               : QW6K_ERR_CUDA;
-}
-
-extern "C" int qw6k_dn_step(const float* conv, const float* gb, const float* z, const float* dn_norm, float* state,
-                            float* gated, cudaStream_t st) {
-    if (!conv || !gb || !z || !dn_norm || !state || !gated) return QW6K_ERR_ARG;
-    if ((reinterpret_cast<uintptr_t>(conv) | reinterpret_cast<uintptr_t>(state)) & 15u) return QW6K_ERR_ALIGN;
-    return launch_pdl(k_dn_step, dim3(kVH), dim3(512), 0, st, conv, gb, z, dn_norm, state, gated) == cudaSuccess
+extern "C" int qw6k_dn_token(const float* proj, const qw6k_step* step, float* ring, const float* conv_w,
+                             const float* dt, const float* a, const float* dn_norm, float* state, float* gated,
+                             cudaStream_t st) {
+    if (!proj || !step || !ring || !conv_w || !dt || !a || !dn_norm || !state || !gated) return QW6K_ERR_ARG;
+    if ((reinterpret_cast<uintptr_t>(conv_w) | reinterpret_cast<uintptr_t>(state)) & 15u) return QW6K_ERR_ALIGN;
+    return launch_pdl(k_dn_token, dim3(kVH), dim3(512), 0, st, proj, step, ring, conv_w, dt, a, dn_norm, state,
+                      gated) == cudaSuccess
                ? 0
                : QW6K_ERR_CUDA;
 }

@@ -70,7 +70,8 @@ typedef struct {
 
 struct qw6cu_decoder {
     qw6cu_ctx *ctx;
-    cudaStream_t st;
+    cudaStream_t st, st2;        /* st2: the shared expert, beside the routed experts */
+    cudaEvent_t ev_fork, ev_join;
     uint32_t n_layers, max_ctx, vocab, embd_rows, embd_quant;
     const void *embd;
     float *out_norm;
@@ -83,7 +84,7 @@ struct qw6cu_decoder {
     uint8_t *stage;
     size_t stage_n;
     qw6k_step *step, *h_step;
-    float *hid, *hid2, *normed, *proj, *conv, *gb, *gated, *qr, *part, *attn, *attn_out, *rlogits, *sgate, *ffn,
+    float *hid, *hid2, *normed, *proj, *gated, *qr, *part, *attn, *attn_out, *rlogits, *sgate, *ffn,
         *sgu, *smid, *sh, *logits, *freq;
     unsigned long long *keys;
     uint32_t *gen;
@@ -294,11 +295,13 @@ static int upload_group(qw6cu_decoder *d, const qw6cu_model_tensor *const *t, co
     return 0;
 }
 
-static int mv(const qw6cu_decoder *d, const mv_job *j, const float *x, float *y) {
+static int mv_on(cudaStream_t st, const mv_job *j, const float *x, float *y) {
     if (j->quant == QW6F_FP32)
-        return kr(qw6k_matvec_f32((const float *)j->w, x, y + j->y_off, j->rows, j->cols, d->st), "matvec");
-    return kr(qw6k_matvec(j->quant, j->w, x, y + j->y_off, j->rows, j->cols, 1, j->cols, j->rows, d->st), "matvec");
+        return kr(qw6k_matvec_f32((const float *)j->w, x, y + j->y_off, j->rows, j->cols, st), "matvec");
+    return kr(qw6k_matvec(j->quant, j->w, x, y + j->y_off, j->rows, j->cols, 1, j->cols, j->rows, st), "matvec");
 }
+
+static int mv(const qw6cu_decoder *d, const mv_job *j, const float *x, float *y) { return mv_on(d->st, j, x, y); }
 
 static const qw6cu_model_tensor *need(const qw6cu_model_tensor *const *tab, uint32_t field, int layer, uint32_t rows,
                                       uint32_t cols) {
@@ -359,7 +362,7 @@ static int setup_layer(qw6cu_decoder *d, int l, const qw6cu_model_tensor *const 
         if (!(t = need(tab, QW6CU_F_DN_NORM, l, 0, D_VD)) || !(L->dn_norm = upload_f32(d, t, D_VD)))
             return QW6CU_ERR_ARG;
         L->s0_bytes = (size_t)D_VH * D_VD * D_VD * 4;
-        L->s1_bytes = (size_t)4 * D_QKV * 4;
+        L->s1_bytes = (size_t)4 * D_QKV * 4; /* conv window: ring of the 4 latest qkv rows */
     } else {
         if (!(p[0] = need(tab, QW6CU_F_ATTN_Q, l, D_QFULL, D_HID)) || !(p[1] = need(tab, QW6CU_F_ATTN_K, l, D_KV, D_HID)) ||
             !(p[2] = need(tab, QW6CU_F_ATTN_V, l, D_KV, D_HID)))
@@ -422,13 +425,14 @@ static int enqueue_step(qw6cu_decoder *d) {
     int *bad = &d->step->bad;
     int rc = kr(qw6k_dequant_row(d->embd_quant, d->embd, d->embd_rows, D_HID, &d->step->token, d->hid, bad, st),
                 "embedding");
+    /* the first layer's input norm; later ones come with the residual add that precedes them */
+    if (!rc) rc = kr(qw6k_rmsnorm(d->hid, d->L[0].norm, d->normed, D_HID, st), "rmsnorm");
     for (uint32_t l = 0; l < d->n_layers && !rc; l++) {
         dlayer *L = &d->L[l];
-        rc = kr(qw6k_rmsnorm(d->hid, L->norm, d->normed, D_HID, st), "rmsnorm");
         for (int j = 0; j < L->n_in && !rc; j++) rc = mv(d, &L->in[j], d->normed, d->proj);
         if (!rc && !L->full) {
-            rc = kr(qw6k_dn_conv(d->proj, L->s1, L->conv_w, L->dt, L->a, d->conv, d->gb, st), "deltanet");
-            if (!rc) rc = kr(qw6k_dn_step(d->conv, d->gb, d->proj + D_QKV, L->dn_norm, L->s0, d->gated, st), "deltanet");
+            rc = kr(qw6k_dn_token(d->proj, d->step, L->s1, L->conv_w, L->dt, L->a, L->dn_norm, L->s0, d->gated, st),
+                    "deltanet");
             if (!rc) rc = mv(d, &L->out, d->gated, d->attn_out);
         } else if (!rc) {
             rc = kr(qw6k_fa_prep(d->proj, L->q_norm, L->k_norm, d->freq, d->step, L->s0, L->s1, d->qr, st), "attention");
@@ -439,6 +443,7 @@ static int enqueue_step(qw6cu_decoder *d) {
             rc = kr(qw6k_block_pre(d->hid, d->attn_out, d->hid2, bad, L->post_norm, L->router, L->srouter, d->normed,
                                    d->rlogits, d->sgate, 1, D_HID, D_NE, st),
                     "moe block");
+        if (!rc && L->shared) rc = cu(cudaEventRecord(d->ev_fork, st), "fork");
         if (!rc) {
             qw6k_moe_desc m;
             memset(&m, 0, sizeof m);
@@ -450,16 +455,21 @@ static int enqueue_step(qw6cu_decoder *d) {
             const int np = rc ? 0 : qw6k_moe_nphases(&m);
             for (int ph = 0; ph < np && !rc; ph++) rc = kr(qw6k_moe_phase(&m, ph, st), "routed experts");
         }
-        if (!rc && L->shared) {
-            for (int j = 0; j < L->n_sgu && !rc; j++) rc = mv(d, &L->sgu[j], d->normed, d->sgu);
-            if (!rc) rc = kr(qw6k_silu_mul(d->sgu, d->sgu + D_INTER, d->smid, D_INTER, st), "shared expert");
-            if (!rc) rc = mv(d, &L->sdown, d->smid, d->sh);
+        if (!rc && L->shared) { /* the shared expert on the second stream, joined before the residual add */
+            rc = cu(cudaStreamWaitEvent(d->st2, d->ev_fork, 0), "fork");
+            for (int j = 0; j < L->n_sgu && !rc; j++) rc = mv_on(d->st2, &L->sgu[j], d->normed, d->sgu);
+            if (!rc) rc = kr(qw6k_silu_mul(d->sgu, d->sgu + D_INTER, d->smid, D_INTER, d->st2), "shared expert");
+            if (!rc) rc = mv_on(d->st2, &L->sdown, d->smid, d->sh);
+            if (!rc) rc = cu(cudaEventRecord(d->ev_join, d->st2), "join");
+            if (!rc) rc = cu(cudaStreamWaitEvent(st, d->ev_join, 0), "join");
         }
+        /* residual add, then the next layer's input norm (or the final norm) */
+        const float *next_norm = l + 1 < d->n_layers ? d->L[l + 1].norm : d->out_norm;
         if (!rc)
-            rc = kr(qw6k_block_post(d->hid2, d->ffn, L->shared ? d->sh : NULL, d->sgate, d->hid, bad, 1, D_HID, st),
+            rc = kr(qw6k_post_norm(d->hid2, d->ffn, L->shared ? d->sh : NULL, d->sgate, d->hid, bad, next_norm,
+                                   d->normed, 1, D_HID, st),
                     "moe block");
     }
-    if (!rc) rc = kr(qw6k_rmsnorm(d->hid, d->out_norm, d->normed, D_HID, st), "rmsnorm");
     if (!rc)
         rc = kr(qw6k_matvec_argmax(d->lm.quant, d->lm.w, d->normed, d->logits, d->keys, d->vocab, D_HID, 1, D_HID,
                                    d->vocab, 0, st),
@@ -512,7 +522,11 @@ int qw6cu_decoder_create(qw6cu_ctx *ctx, const qw6cu_model_tensor *tensors, uint
     d->ctx = ctx;
     d->n_layers = n_layers;
     d->max_ctx = max_ctx;
-    if ((rc = cu(cudaStreamCreateWithFlags(&d->st, cudaStreamNonBlocking), "stream"))) goto fail;
+    if ((rc = cu(cudaStreamCreateWithFlags(&d->st, cudaStreamNonBlocking), "stream")) ||
+        (rc = cu(cudaStreamCreateWithFlags(&d->st2, cudaStreamNonBlocking), "stream")) ||
+        (rc = cu(cudaEventCreateWithFlags(&d->ev_fork, cudaEventDisableTiming), "event")) ||
+        (rc = cu(cudaEventCreateWithFlags(&d->ev_join, cudaEventDisableTiming), "event")))
+        goto fail;
     rc = QW6CU_ERR_ARG;
     if (!emb || !emb->data || emb->cols != D_HID || !emb->rows || !qw6_row_bytes(emb->quant, D_HID)) {
         qw6h_set_err("qw6cu_decoder_create: token embeddings missing or not [rows x 2048] of a known quant");
@@ -552,8 +566,7 @@ int qw6cu_decoder_create(qw6cu_ctx *ctx, const qw6cu_model_tensor *tensors, uint
     d->moe_ws_bytes = qw6k_moe_ws_bytes(1, D_HID, D_INTER, D_NE, D_TOPK);
     if (!(d->moe_ws = dalloc(d, d->moe_ws_bytes))) goto fail;
 #define F32(ptr, n) if (!((ptr) = dalloc(d, (size_t)(n) * 4))) goto fail
-    F32(d->hid, D_HID); F32(d->hid2, D_HID); F32(d->normed, D_HID); F32(d->proj, D_PROJ); F32(d->conv, D_QKV);
-    F32(d->gb, 2 * D_VH); F32(d->gated, D_Z); F32(d->qr, D_Z); F32(d->part, qw6k_fa_part_floats());
+    F32(d->hid, D_HID); F32(d->hid2, D_HID); F32(d->normed, D_HID); F32(d->proj, D_PROJ); F32(d->gated, D_Z); F32(d->qr, D_Z); F32(d->part, qw6k_fa_part_floats());
     F32(d->attn, D_Z); F32(d->attn_out, D_HID); F32(d->rlogits, D_NE); F32(d->sgate, 64); F32(d->ffn, D_HID);
     F32(d->sgu, 2 * D_INTER); F32(d->smid, D_INTER); F32(d->sh, D_HID); F32(d->logits, d->vocab); F32(d->freq, 32);
 #undef F32
@@ -669,6 +682,10 @@ void qw6cu_decoder_destroy(qw6cu_decoder *d) {
     cudaFree(d->stage);
     cudaFree(d->gen);
     if (d->h_step) cudaFreeHost(d->h_step);
+    if (d->st2) cudaStreamSynchronize(d->st2);
+    if (d->ev_fork) cudaEventDestroy(d->ev_fork);
+    if (d->ev_join) cudaEventDestroy(d->ev_join);
+    if (d->st2) cudaStreamDestroy(d->st2);
     if (d->st) cudaStreamDestroy(d->st);
     free(d->allocs);
     free(d->ups);

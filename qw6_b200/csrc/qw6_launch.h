@@ -129,6 +129,9 @@ int qw6k_block_pre(const float *x, const float *add, float *xsum, int *bad, cons
                    uint32_t ne, cudaStream_t st);
 int qw6k_block_post(const float *x, const float *ffn, const float *shared, const float *sgate, float *out, int *bad,
                     uint32_t ntok, uint32_t hidden, cudaStream_t st);
+/* block_post, then normed = rmsnorm(out) * norm_w (hidden <= 4096) */
+int qw6k_post_norm(const float *x, const float *ffn, const float *shared, const float *sgate, float *out, int *bad,
+                   const float *norm_w, float *normed, uint32_t ntok, uint32_t hidden, cudaStream_t st);
 
 /* Sampling (k_sample.cu): out[r] = qw6_sample's pick (qw6.c:2904-2982) over
  * logits row r (n floats, rows ld apart) with uniform draw u[r]; ws: device
@@ -218,13 +221,11 @@ int qw6k_dequant_row(uint32_t quant, const void *raw, uint32_t rows, uint32_t co
                      float *out, int *bad, cudaStream_t st);
 int qw6k_rmsnorm(const float *x, const float *w, float *out, uint32_t dim, cudaStream_t st);
 /* Gated DeltaNet token step: proj = [qkv 8192 | z 4096 | beta 32 | alpha 32];
- * conv_state [4][8192] (oldest first), conv_w [8192][4], dt/a [32]; conv
- * [8192] and gb [64] (sigmoid(beta), softplus(alpha + dt) * a) are scratch */
-int qw6k_dn_conv(const float *proj, float *conv_state, const float *conv_w, const float *dt, const float *a,
-                 float *conv, float *gb, cudaStream_t st);
-/* state [32][128][128] updated in place; gated [4096] = rmsnorm(o) * silu(z) */
-int qw6k_dn_step(const float *conv, const float *gb, const float *z, const float *dn_norm, float *state,
-                 float *gated, cudaStream_t st);
+ * ring [4][8192]: row p % 4 holds position p's qkv (zero before position
+ * 0); conv_w [8192][4], dt/a [32], dn_norm [128]; state [32][128][128]
+ * updated in place; gated [4096] = rmsnorm(o) * silu(z) */
+int qw6k_dn_token(const float *proj, const qw6k_step *step, float *ring, const float *conv_w, const float *dt,
+                  const float *a, const float *dn_norm, float *state, float *gated, cudaStream_t st);
 /* gated attention: proj = [16 x (q 256 | gate 256) | k 512 | v 512]; caches
  * [max_ctx][2][256]; freq[32] = powf(1e7, i / 64) for even i < 64 */
 int qw6k_fa_prep(const float *proj, const float *q_norm, const float *k_norm, const float *freq,

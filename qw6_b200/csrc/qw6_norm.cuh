@@ -25,6 +25,7 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 // rounding of the sum), the rest is qw6's expression with IEEE operations.
 __device__ __forceinline__ float rms_inv(const float* __restrict__ x, int dim, float* red) {
     float ss = 0.f;
+#pragma unroll 8
     for (int i = threadIdx.x; i < dim; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
     const float t = block_sum(ss, red);
     return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)dim), kRmsEps)));
