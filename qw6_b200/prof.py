@@ -3,6 +3,7 @@
     python -m qw6_b200.prof matvec <quant> <rows> <cols> [reps] [ntok]
     python -m qw6_b200.prof moe_decode <config> [layers] [steps]
     python -m qw6_b200.prof lm_head <ntok> [reps]
+    python -m qw6_b200.prof decoder <tokens>
 
 matvec: `reps` (default 5) launches of the packed quantized matvec
 (qw6cu_matvec) over `ntok` tokens (default 1) on `rows` x `cols` random packed
@@ -18,6 +19,11 @@ weights; 1 copy of config 1 is 0.5 GB, of config 2 0.2 GB.
 
 lm_head: `reps` launches of config 4's fused Q6_K LM head + argmax
 (248320 x 2048) over `ntok` tokens.
+
+decoder: `tokens` greedy steps of the decode-step executor
+(qw6cu_decoder_generate) on a full-size synthetic qw6 model (40 layers with
+distinct weights, 248320-token vocabulary; 10.6 GB on the device, ~16 s to
+generate on the host); each step is one CUDA graph of ~425 launches.
 
 The values are random, so the outputs are meaningless; only the kernels'
 work is real.
@@ -99,6 +105,18 @@ def lm_head(ntok: int, reps: int = 5) -> None:
     print(f"lm_head ntok {ntok}: {reps} launches")
 
 
+def decoder(tokens: int = 3) -> None:
+    from qw6_b200 import lib as L
+    from qw6_b200 import synth as S
+    m = S.fwd_model(seed=31, n_layers=40, vocab=S.VOCAB, embd_rows=S.VOCAB, attn_period=40, expert_period=40)
+    ctx = L.Context(0)
+    dec = L.Decoder(ctx, m, max_ctx=4096)
+    del m
+    print("decoder: picked", list(dec.generate(1, 0, tokens)))
+    dec.close()
+    ctx.close()
+
+
 def main(argv: list[str]) -> int:
     if len(argv) >= 4 and argv[0] == "matvec":
         matvec(argv[1], int(argv[2]), int(argv[3]), *(int(a) for a in argv[4:6]))
@@ -108,6 +126,9 @@ def main(argv: list[str]) -> int:
         return 0
     if len(argv) >= 2 and argv[0] == "lm_head":
         lm_head(*(int(a) for a in argv[1:3]))
+        return 0
+    if len(argv) >= 1 and argv[0] == "decoder":
+        decoder(*(int(a) for a in argv[1:2]))
         return 0
     print(__doc__)
     return 2
