@@ -59,27 +59,12 @@ struct PfArgs {
 };
 
 // ------------------------------------------------------------------ plan --
-
-__global__ void k_pf_route(const PfArgs a) {
-    pdl_grid_wait();
-    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (t >= a.ntok) return;
-    route_token(a.logits + (size_t)t * a.ne, a.ne, a.topk, a.idx + (size_t)t * a.topk, a.w + (size_t)t * a.topk,
-                threadIdx.x & 31);
-}
-
-__global__ void k_pf_count(const PfArgs a) {
-    pdl_grid_wait();
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < a.ntok * a.topk) a.pos[i] = atomicAdd(&a.cnt[a.idx[i]], 1);
-}
-
-// exclusive scans of counts and of 256-token chunks; the work-item list
-__global__ void __launch_bounds__(256) k_pf_offsets(const PfArgs a) {
+// Exclusive scans of the per-expert counts and of their 256-token chunks,
+// and the work-item list; run by one CTA of 256 threads (ne <= 256).
+__device__ __forceinline__ void pf_offsets_cta(const PfArgs& a) {
     __shared__ int wsum[2][8];
-    pdl_grid_wait();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int own = tid < a.ne ? a.cnt[tid] : 0;
+    const int own = tid < a.ne ? __ldcg(a.cnt + tid) : 0;
     int v = own, ch = (own + kPfChunk - 1) / kPfChunk;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -108,7 +93,59 @@ __global__ void __launch_bounds__(256) k_pf_offsets(const PfArgs a) {
             a.items[c0 + c] = make_int4(tid, o0 + c * kPfChunk, min(kPfChunk, own - c * kPfChunk), 0);
 }
 
+// The CTA that finishes last (all counts are in: every CTA fences its
+// atomics before it takes a ticket) runs the scans.  a.nitems[1] is the
+// ticket counter, zeroed before the launch.
+__device__ __forceinline__ void pf_offsets_if_last(const PfArgs& a) {
+    __shared__ bool last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        last = atomicAdd(a.nitems + 1, 1) == (int)gridDim.x - 1;
+    }
+    __syncthreads();
+    if (last) {
+        __threadfence();
+        pf_offsets_cta(a);
+    }
+}
+
+// Route every token (a warp each, qw6.c:2796-2827), count its assignments per
+// expert (their positions within the expert: the order of the atomics, which
+// the results do not depend on), and, in the last CTA, the offsets.
+__global__ void __launch_bounds__(256) k_pf_route_count(const PfArgs a) {
+    pdl_trigger_dependents();
+    pdl_grid_wait();
+    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (t < a.ntok) {
+        route_token(a.logits + (size_t)t * a.ne, a.ne, a.topk, a.idx + (size_t)t * a.topk, a.w + (size_t)t * a.topk,
+                    lane);
+        if (lane < a.topk) {  // the lane reads back the index it wrote
+            const int i = t * a.topk + lane;
+            a.pos[i] = atomicAdd(&a.cnt[a.idx[i]], 1);
+        }
+    }
+    pf_offsets_if_last(a);
+}
+
+// Rows mode (routing given per row): the counts and positions, then the offsets.
+__global__ void __launch_bounds__(256) k_pf_count(const PfArgs a) {
+    pdl_trigger_dependents();
+    pdl_grid_wait();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < a.ntok * a.topk) a.pos[i] = atomicAdd(&a.cnt[a.idx[i]], 1);
+    pf_offsets_if_last(a);
+}
+
+// Sorted mode (counts given): the offsets alone.
+__global__ void __launch_bounds__(256) k_pf_offsets(const PfArgs a) {
+    pdl_trigger_dependents();
+    pdl_grid_wait();
+    pf_offsets_cta(a);
+}
+
 __global__ void k_pf_scatter(const PfArgs a) {
+    pdl_trigger_dependents();
     pdl_grid_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < a.ntok * a.topk) a.order[a.off[a.idx[i]] + a.pos[i]] = i;
@@ -599,6 +636,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfArgs a) {
 // out[t][f] = sum_k w[t,k] * dout[t*topk + k][f], fp32 in slot order k
 // (rows mode: out[r] = w[r] * dout[r]).
 __global__ void k_pf_combine(const PfArgs a) {
+    pdl_trigger_dependents();
     pdl_grid_wait();
     const int t = blockIdx.y, f = (blockIdx.x * blockDim.x + threadIdx.x) * 2;
     if (f >= a.hidden) return;
@@ -714,7 +752,8 @@ extern "C" int qw6k_moe_prefill_check(const qw6k_moe_desc* d, int* err) {
     return pf_args(d, err, a);
 }
 
-/* phases: 0 route, 1 count (after zeroing counts), 2 offsets, 3 scatter,
+/* phases: 0 route + count + offsets, 1 count + offsets (rows mode), 2 offsets
+ * (sorted mode), 3 scatter,
  * 4 gate/up GEMM (+silu), 5 down GEMM (per-assignment outputs), 6 combine */
 extern "C" int qw6k_moe_prefill_phase(const qw6k_moe_desc* d, int* err, int phase, cudaStream_t st) {
     PfArgs a;
@@ -723,16 +762,23 @@ extern "C" int qw6k_moe_prefill_phase(const qw6k_moe_desc* d, int* err, int phas
     const int tk = a.ntok * a.topk;
     const int mi = pf_items_max((uint32_t)tk, (uint32_t)a.ne);
     switch (phase) {
-    case 0:
+    case 0:  // route + count + offsets
         if (!d->logits) return 0;  // rows mode: routing supplied by the caller
-        if (launch_pdl(k_pf_route, dim3((a.ntok + 7) / 8), dim3(256), 0, st, a) != cudaSuccess) return QW6K_ERR_CUDA;
+        if (cudaMemsetAsync(a.cnt, 0, 256 * 4, st) != cudaSuccess ||
+            cudaMemsetAsync(a.nitems + 1, 0, sizeof(int), st) != cudaSuccess)
+            return QW6K_ERR_CUDA;
+        if (launch_pdl(k_pf_route_count, dim3((a.ntok + 7) / 8), dim3(256), 0, st, a) != cudaSuccess)
+            return QW6K_ERR_CUDA;
         break;
-    case 1:
-        if (!a.order) return 0;  // sorted mode: counts supplied
-        if (cudaMemsetAsync(a.cnt, 0, 256 * 4, st) != cudaSuccess) return QW6K_ERR_CUDA;
+    case 1:  // rows mode: count + offsets
+        if (d->logits || !a.order) return 0;  // counted in phase 0, or sorted mode: counts supplied
+        if (cudaMemsetAsync(a.cnt, 0, 256 * 4, st) != cudaSuccess ||
+            cudaMemsetAsync(a.nitems + 1, 0, sizeof(int), st) != cudaSuccess)
+            return QW6K_ERR_CUDA;
         if (launch_pdl(k_pf_count, dim3((tk + 255) / 256), dim3(256), 0, st, a) != cudaSuccess) return QW6K_ERR_CUDA;
         break;
-    case 2:
+    case 2:  // sorted mode: offsets of the given counts
+        if (a.order) return 0;  // done with the counting
         if (launch_pdl(k_pf_offsets, dim3(1), dim3(256), 0, st, a) != cudaSuccess) return QW6K_ERR_CUDA;
         break;
     case 3:
