@@ -174,6 +174,12 @@ __global__ void __launch_bounds__(kThreads, NQ == 1 ? 2 : 1) k_matvec(const MvAr
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ks = a.ks, wpm = kWarps / ks, ms = warp / ks, split = warp % ks, nbk = a.nb / ks;
     const int ngrp = (a.mtiles + wpm - 1) / wpm;
+    // token chunk of this CTA (grid y): tokens [tok0, tok0 + 4 NQ)
+    const int tok0 = (int)blockIdx.y * 4 * NQ;
+    const int ntok = min(a.ntok - tok0, 4 * NQ);
+    const float* xin = a.x + (size_t)tok0 * a.ldx;
+    float* yout = a.y ? a.y + (size_t)tok0 * a.ldy : nullptr;
+    unsigned long long* kout = KEYS ? a.keys + tok0 : nullptr;
     const int n_iter = blockIdx.x < ngrp ? (ngrp - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
     const int nsteps = n_iter * nbk;
 
@@ -189,7 +195,7 @@ __global__ void __launch_bounds__(kThreads, NQ == 1 ? 2 : 1) k_matvec(const MvAr
     if (step_ok(0)) T::load(fa, tile_ptr(0), lane);  // weights: nothing earlier in the stream writes them
     if constexpr (IsIQ<F>::value) IQLut<F>::init(tbl, grid_ptr<F>());
     pdl_wait();  // x comes from the previous kernel
-    xstage_fill(xs, a.x, a.ldx, a.ntok, 4 * NQ, a.cols);
+    xstage_fill(xs, xin, a.ldx, ntok, 4 * NQ, a.cols);
     __syncthreads();
     const XView xv = xs.view();
 
@@ -229,11 +235,11 @@ __global__ void __launch_bounds__(kThreads, NQ == 1 ? 2 : 1) k_matvec(const MvAr
 #pragma unroll
             for (int qt = 0; qt < NQ; qt++) {
                 const int tok = 4 * qt + t;
-                if (tok < a.ntok) {
+                if (tok < ntok) {
                     const int r0 = mt * 16 + g;
-                    if (!KEYS || a.y) {
-                        if (r0 < a.rows) a.y[(size_t)tok * a.ldy + r0] = acc[0][qt];
-                        if (r0 + 8 < a.rows) a.y[(size_t)tok * a.ldy + r0 + 8] = acc[1][qt];
+                    if (!KEYS || yout) {
+                        if (r0 < a.rows) yout[(size_t)tok * a.ldy + r0] = acc[0][qt];
+                        if (r0 + 8 < a.rows) yout[(size_t)tok * a.ldy + r0 + 8] = acc[1][qt];
                     }
                     if (KEYS) {
                         if (r0 < a.rows) {
@@ -292,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, NQ == 1 ? 2 : 1) k_matvec(const MvAr
                 k = v > k ? v : k;
             }
             const int tok = 4 * qt + (lane & 3);
-            if (lane < 4 && tok < a.ntok && k) atomicMax(a.keys + tok, k);
+            if (lane < 4 && tok < ntok && k) atomicMax(kout + tok, k);
         }
     }
 }
@@ -393,7 +399,8 @@ static size_t mv_smem(int cols) {
 
 template <int F, int NQ, bool KEYS>
 static int launch_mv(const uint8_t* w, const float* x, float* y, int rows, int cols, int ntok, int ldx,
-                     int ldy, cudaStream_t st, unsigned long long* keys = nullptr, uint32_t row_offset = 0) {
+                     int ldy, cudaStream_t st, unsigned long long* keys = nullptr, uint32_t row_offset = 0,
+                     int chunks = 1) {
     const size_t smem = mv_smem<F, NQ>(cols);
     if (smem > kMvSmemMax) return QW6K_ERR_ARG;
     static DevFlags configured;
@@ -422,18 +429,32 @@ static int launch_mv(const uint8_t* w, const float* x, float* y, int rows, int c
     const int wpm = kWarps / ks;
     const long long ngrp = (a.mtiles + wpm - 1) / wpm;
     const int grid = (int)(ngrp < (long long)num_sms() * occ ? ngrp : (long long)num_sms() * occ);
-    return launch_pdl(k_matvec<F, NQ, KEYS>, dim3(grid), dim3(kThreads), smem, st, a) == cudaSuccess ? 0
-                                                                                         : QW6K_ERR_CUDA;
+    return launch_pdl(k_matvec<F, NQ, KEYS>, dim3(grid, chunks), dim3(kThreads), smem, st, a) == cudaSuccess
+               ? 0
+               : QW6K_ERR_CUDA;
 }
 
-// Token batches: 1-4 and 5-8 tokens in one launch; 9-32 tokens in one launch
-// when the activation stage of 32 tokens fits in shared memory, else in
-// chunks of 16 tokens (each chunk streams the weights again; only very wide
-// matrices, e.g. 4096 columns, need that).
+// Token batches: 1-4 tokens in one launch.  A small matrix (<= 1024 tile-
+// blocks, IQ formats <= 2048) with more tokens runs as chunks of 4 tokens side
+// by side (grid y), up to 2048 tile-blocks the K formats as chunks of 16: the
+// chunks read the same weights (from L2 after the first), and a CTA stages and
+// multiplies only its chunk's tokens, so a small matrix at batch 32 fills the
+// GPU instead of a few CTAs each staging all 32 tokens (measured on config 0 /
+// 4's projections at batch 32: Q4_K 512x2048 28.6 -> 5.5 us, IQ3_S 2048^2 28.2
+// -> 24.0, IQ2_S 2048x4096 58.1 -> 47.0, Q5_K 4096x2048 34.0 -> 32.0 with
+// 16-token chunks).  Otherwise 5-8 tokens in one launch, 9-32 in one pass when
+// the activation stage of 32 tokens fits in shared memory, else in passes of 16
+// tokens (each pass streams the weights again; only very wide matrices, e.g.
+// 4096 columns, need that).
 template <int F, bool KEYS>
 static int launch_mv_batch(const uint8_t* w, const float* x, float* y, int rows, int cols, int ntok, int ldx,
                            int ldy, cudaStream_t st, unsigned long long* keys, uint32_t row_offset) {
     if (ntok <= 4) return launch_mv<F, 1, KEYS>(w, x, y, rows, cols, ntok, ldx, ldy, st, keys, row_offset);
+    const long long tbs = (long long)((rows + 15) / 16) * (cols / 256);  // tile-blocks
+    if (ntok <= 32 && (tbs <= 1024 || (IsIQ<F>::value && tbs <= 2048)))
+        return launch_mv<F, 1, KEYS>(w, x, y, rows, cols, ntok, ldx, ldy, st, keys, row_offset, (ntok + 3) / 4);
+    if (ntok <= 32 && ntok > 8 && tbs <= 2048 && mv_smem<F, 4>(cols) <= kMvSmemMax)
+        return launch_mv<F, 4, KEYS>(w, x, y, rows, cols, ntok, ldx, ldy, st, keys, row_offset, (ntok + 15) / 16);
     if (ntok <= 8) return launch_mv<F, 2, KEYS>(w, x, y, rows, cols, ntok, ldx, ldy, st, keys, row_offset);
     if (ntok > 32) return QW6K_ERR_ARG;
     if (mv_smem<F, 8>(cols) <= kMvSmemMax)

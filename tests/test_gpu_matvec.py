@@ -169,3 +169,16 @@ def test_host_api_errors():
 def test_selftest_kats():
     """qw6_vk_selftest: the closed-form KATs of qw6's Vulkan self-test."""
     assert L.selftest() == 0
+
+
+@pytest.mark.parametrize("q,rows,cols", [(S.Q5_K, 4096, 2048), (S.Q4_K, 512, 2048), (S.IQ3_S, 2048, 2048)])
+@pytest.mark.parametrize("ntok", [6, 20, 32])
+def test_matvec_token_chunks(q, rows, cols, ntok, cuda, oracle, rng):
+    """Config 0 / 4 shapes at batches above 4, which run as token chunks side
+    by side (4 tokens a chunk, or 16 for mid-sized K-format matrices)."""
+    w = S.make_matrix(q, rows, cols, rng)
+    x = rng.standard_normal((ntok, cols), dtype=np.float32)
+    y = gpu_matvec(cuda, q, w, x, rows, cols)
+    ref = oracle.matvec(q, w, x, rows, cols).reshape(ntok, rows)
+    for t in range(ntok):
+        assert rel_err(y[t], ref[t]) <= TOL, t
