@@ -23,6 +23,7 @@ namespace qw6 {
 
 constexpr int kBlkThreads = 256;  // 8 router rows per CTA
 constexpr int kRowRegs = 16;  // float4 of a router row a lane holds in registers (hidden <= 2048)
+constexpr int kRowVals = 16;  // values of the token row a thread holds in registers (hidden <= 4096)
 
 // grid (ceil((ne + 1) / 8), ntok): CTA (b, t) computes rows [8b, 8b+8) of
 // token t (warp per row): rows < ne are the router's, row ne is the shared
@@ -31,12 +32,11 @@ constexpr int kRowRegs = 16;  // float4 of a router row a lane holds in register
 // normed[i] = (x[i] * inv) * w[i] as qw6 evaluates it.  With `add` the block
 // input is x + add (the residual add before the FFN, qw6.c:2469-2470), which
 // CTA (0, t) stores to xsum and checks for NaN/Inf (sets *bad, qw6.c:2472).
-__global__ void __launch_bounds__(kBlkThreads) k_block_pre(const float* __restrict__ x, const float* __restrict__ add,
-                                                           float* __restrict__ xsum, int* __restrict__ bad,
+__global__ void __launch_bounds__(kBlkThreads) k_block_pre(const float* x, const float* add, float* xsum, int* bad,
                                                            const float* __restrict__ norm_w,
                                                            const float* __restrict__ router,
-                                                           const float* __restrict__ srouter, float* __restrict__ normed,
-                                                           float* __restrict__ logits, float* __restrict__ sgate,
+                                                           const float* __restrict__ srouter, float* normed, float* logits,
+                                                           float* sgate,
                                                            int hidden, int ne) {
     extern __shared__ __align__(16) float nrm[];  // [hidden]
     __shared__ float red[kBlkThreads / 32];
@@ -55,28 +55,73 @@ __global__ void __launch_bounds__(kBlkThreads) k_block_pre(const float* __restri
         const int c = 4 * lane + 128 * u;
         wv[u] = held && c < hidden ? __ldg(reinterpret_cast<const float4*>(wr + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    pdl_grid_wait();
     const float* xt = x + (size_t)t * hidden;
-    if (add) {  // x + add into shared memory first, then the norm of the sum
-        const float* at = add + (size_t)t * hidden;
+    if (hidden <= kBlkThreads * kRowVals) {
+        // the row in registers: every load of a phase is issued before the
+        // first use (a load loop that also stores is issued one load at a time)
+        float nw[kRowVals], xv[kRowVals], av[kRowVals];
+#pragma unroll
+        for (int u = 0; u < kRowVals; u++) {
+            const int i = threadIdx.x + kBlkThreads * u;
+            nw[u] = i < hidden ? norm_w[i] : 0.f;
+        }
+        pdl_grid_wait();
+#pragma unroll
+        for (int u = 0; u < kRowVals; u++) {
+            const int i = threadIdx.x + kBlkThreads * u;
+            xv[u] = i < hidden ? xt[i] : 0.f;
+            av[u] = add && i < hidden ? add[(size_t)t * hidden + i] : 0.f;
+        }
+        float ss = 0.f;
         bool finite = true;
+#pragma unroll
+        for (int u = 0; u < kRowVals; u++) {
+            if (add) xv[u] = __fadd_rn(xv[u], av[u]);  // the residual add (qw6.c:2469-2470)
+            finite = finite && isfinite(xv[u]);
+            ss = fmaf(xv[u], xv[u], ss);
+        }
+        if (add && blockIdx.x == 0) {
+#pragma unroll
+            for (int u = 0; u < kRowVals; u++) {
+                const int i = threadIdx.x + kBlkThreads * u;
+                if (i < hidden) xsum[(size_t)t * hidden + i] = xv[u];
+            }
+            if (!finite && bad) atomicOr(bad, 1);
+        }
+        const float tot = block_sum(ss, red);
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)hidden), kRmsEps)));
+#pragma unroll
+        for (int u = 0; u < kRowVals; u++) {
+            const int i = threadIdx.x + kBlkThreads * u;
+            if (i < hidden) {
+                const float v = __fmul_rn(__fmul_rn(xv[u], inv), nw[u]);
+                nrm[i] = v;
+                if (blockIdx.x == 0) normed[(size_t)t * hidden + i] = v;
+            }
+        }
+    } else {  // hidden > 4096: strided loops
+        pdl_grid_wait();
+        if (add) {  // x + add into shared memory first, then the norm of the sum
+            const float* at = add + (size_t)t * hidden;
+            bool finite = true;
+#pragma unroll 8
+            for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+                const float v = __fadd_rn(xt[i], at[i]);
+                nrm[i] = v;
+                finite = finite && isfinite(v);
+                if (blockIdx.x == 0) xsum[(size_t)t * hidden + i] = v;
+            }
+            if (!finite && blockIdx.x == 0 && bad) atomicOr(bad, 1);
+            __syncthreads();
+            xt = nrm;
+        }
+        const float inv = rms_inv(xt, hidden, red);
 #pragma unroll 8
         for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
-            const float v = __fadd_rn(xt[i], at[i]);
-            nrm[i] = v;
-            finite = finite && isfinite(v);
-            if (blockIdx.x == 0) xsum[(size_t)t * hidden + i] = v;
+            const float v = __fmul_rn(__fmul_rn(xt[i], inv), norm_w[i]);
+            nrm[i] = v;  // each thread rewrites only the entries it read
+            if (blockIdx.x == 0) normed[(size_t)t * hidden + i] = v;
         }
-        if (!finite && blockIdx.x == 0 && bad) atomicOr(bad, 1);
-        __syncthreads();
-        xt = nrm;
-    }
-    const float inv = rms_inv(xt, hidden, red);
-#pragma unroll 8
-    for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
-        const float v = __fmul_rn(__fmul_rn(xt[i], inv), norm_w[i]);
-        nrm[i] = v;  // each thread rewrites only the entries it read
-        if (blockIdx.x == 0) normed[(size_t)t * hidden + i] = v;
     }
     __syncthreads();
     if (wr) {
@@ -114,8 +159,7 @@ __global__ void __launch_bounds__(kBlkThreads) k_block_pre(const float* __restri
 // out[t][i] = x[t][i] + (ffn[t][i] + s[t] * sh[t][i])  (sh may be null: no
 // shared expert), each operation rounded once as qw6's loops do; a NaN/Inf
 // in out sets *bad (qw6.c:2485-2487).
-__global__ void k_block_post(const float* __restrict__ x, const float* __restrict__ ffn, const float* __restrict__ sh,
-                             const float* __restrict__ sgate, float* __restrict__ out, int* __restrict__ bad,
+__global__ void k_block_post(const float* x, const float* ffn, const float* sh, const float* sgate, float* out, int* bad,
                              int hidden, long long n) {
     pdl_trigger_dependents();
     pdl_grid_wait();
@@ -134,10 +178,9 @@ __global__ void k_block_post(const float* __restrict__ x, const float* __restric
 // k_block_post, then normed = rmsnorm(out) * w as qw6_cpu_rmsnorm (the next
 // layer's input norm, or the final norm before the LM head, qw6.c:2462,
 // 2493): the residual add and the norm that follows it in one pass.
-__global__ void __launch_bounds__(256) k_post_norm(const float* __restrict__ x, const float* __restrict__ ffn,
-                                                   const float* __restrict__ sh, const float* __restrict__ sgate,
-                                                   float* __restrict__ out, int* __restrict__ bad,
-                                                   const float* __restrict__ w, float* __restrict__ normed,
+__global__ void __launch_bounds__(256) k_post_norm(const float* x, const float* ffn, const float* sh,
+                                                   const float* sgate, float* out, int* bad,
+                                                   const float* __restrict__ w, float* normed,
                                                    int hidden) {
     __shared__ float red[8];
     pdl_trigger_dependents();
@@ -150,21 +193,32 @@ __global__ void __launch_bounds__(256) k_post_norm(const float* __restrict__ x, 
     pdl_grid_wait();
     const size_t base = (size_t)blockIdx.x * hidden;
     const float s = sh ? sgate[blockIdx.x] : 0.f;
+    float fv[16], hv[16];
+#pragma unroll
+    for (int u = 0; u < 16; u++) {  // every load before the first store
+        const int i = threadIdx.x + 256 * u;
+        ov[u] = i < hidden ? x[base + i] : 0.f;
+        fv[u] = i < hidden ? ffn[base + i] : 0.f;
+        hv[u] = sh && i < hidden ? sh[base + i] : 0.f;
+    }
     bool finite = true;
     float ss = 0.f;
 #pragma unroll
     for (int u = 0; u < 16; u++) {
         const int i = threadIdx.x + 256 * u;
-        ov[u] = 0.f;
         if (i < hidden) {
-            float f = ffn[base + i];
-            if (sh) f = __fadd_rn(f, __fmul_rn(s, sh[base + i]));
-            const float o = __fadd_rn(x[base + i], f);
-            out[base + i] = o;
+            float f = fv[u];
+            if (sh) f = __fadd_rn(f, __fmul_rn(s, hv[u]));
+            const float o = __fadd_rn(ov[u], f);
             ov[u] = o;
             finite = finite && isfinite(o);
             ss = fmaf(o, o, ss);
         }
+    }
+#pragma unroll
+    for (int u = 0; u < 16; u++) {
+        const int i = threadIdx.x + 256 * u;
+        if (i < hidden) out[base + i] = ov[u];
     }
     if (!finite && bad) atomicOr(bad, 1);
     const float t = block_sum(ss, red);

@@ -67,8 +67,8 @@ __device__ __forceinline__ float warp_max(float v) {
 
 // out = rmsnorm(x) * w as qw6_cpu_rmsnorm evaluates it; one CTA of 256
 // threads, dim <= 4096 (each thread keeps its values in registers).
-__global__ void __launch_bounds__(256) k_rmsnorm(const float* __restrict__ x, const float* __restrict__ w,
-                                                 float* __restrict__ out, int dim) {
+__global__ void __launch_bounds__(256) k_rmsnorm(const float* x, const float* __restrict__ w, float* out,
+                                                 int dim) {
     __shared__ float red[8];
     pdl_trigger_dependents();
     float wv[16], xv[16];
@@ -106,11 +106,9 @@ __global__ void __launch_bounds__(256) k_rmsnorm(const float* __restrict__ x, co
 // compute its query and key without ordering.  Then the state rows, as
 // qw6_gated_delta_net_single (qw6.c:2079-2108), and rmsnorm(o) * silu(z)
 // (qw6.c:2349-2355).
-__global__ void __launch_bounds__(512) k_dn_token(const float* __restrict__ proj, const qw6k_step* __restrict__ step,
-                                                  float* __restrict__ ring, const float* __restrict__ cw,
+__global__ void __launch_bounds__(512) k_dn_token(const float* proj, const qw6k_step* step, float* ring, const float* __restrict__ cw,
                                                   const float* __restrict__ dt, const float* __restrict__ a,
-                                                  const float* __restrict__ nw, float* __restrict__ state,
-                                                  float* __restrict__ gated) {
+                                                  const float* __restrict__ nw, float* state, float* gated) {
     __shared__ __align__(16) float qk[2][kKD];
     __shared__ float vs[kVD], o[kVD], gbs[2];
     __shared__ float red[16];
@@ -191,10 +189,9 @@ __global__ void __launch_bounds__(512) k_dn_token(const float* __restrict__ proj
 // grid 18 x 256: CTAs 0-15 the query heads, 16-17 the key/value heads.
 // freq[i/2] = powf(1e7, i / 64) for even i < 64, computed by the host's libm
 // as qw6 computes it, so that theta = pos / freq is qw6's value.
-__global__ void __launch_bounds__(256) k_fa_prep(const float* __restrict__ proj, const float* __restrict__ qn,
+__global__ void __launch_bounds__(256) k_fa_prep(const float* proj, const float* __restrict__ qn,
                                                  const float* __restrict__ kn, const float* __restrict__ freq,
-                                                 const qw6k_step* __restrict__ step, float* __restrict__ kc,
-                                                 float* __restrict__ vc, float* __restrict__ qr) {
+                                                 const qw6k_step* step, float* kc, float* vc, float* qr) {
     __shared__ float y[kHD];
     __shared__ float red[8];
     pdl_trigger_dependents();
@@ -234,9 +231,8 @@ __device__ __forceinline__ void fa_chunk(uint32_t seq, int c, uint32_t& c0, uint
 // grid (kFaSplit, 2 kv heads) x 256: warp w is query head 8 g + w; lane owns
 // dimensions [8 lane, 8 lane + 8).  part: m, l per (head, chunk), then the
 // [head][chunk][256] value sums.
-__global__ void __launch_bounds__(256) k_fa_attn(const float* __restrict__ qr, const float* __restrict__ kc,
-                                                 const float* __restrict__ vc, const qw6k_step* __restrict__ step,
-                                                 float* __restrict__ part) {
+__global__ void __launch_bounds__(256) k_fa_attn(const float* qr, const float* kc, const float* vc,
+                                                 const qw6k_step* step, float* part) {
     pdl_trigger_dependents();
     pdl_grid_wait();
     const uint32_t seq = step->pos + 1;
@@ -301,8 +297,8 @@ __global__ void __launch_bounds__(256) k_fa_attn(const float* __restrict__ qr, c
 }
 
 // grid 16 (query heads) x 256 (dimensions)
-__global__ void __launch_bounds__(256) k_fa_combine(const float* __restrict__ part, const float* __restrict__ proj,
-                                                    const qw6k_step* __restrict__ step, float* __restrict__ attn) {
+__global__ void __launch_bounds__(256) k_fa_combine(const float* part, const float* proj, const qw6k_step* step,
+                                                    float* attn) {
     pdl_trigger_dependents();
     pdl_grid_wait();
     const uint32_t seq = step->pos + 1;
@@ -326,7 +322,7 @@ __global__ void __launch_bounds__(256) k_fa_combine(const float* __restrict__ pa
     attn[h * kHD + d] = __fmul_rn(__fdiv_rn(o, l), sigmoid_f(gate));
 }
 
-__global__ void k_check_finite(const float* __restrict__ x, uint32_t n, int* __restrict__ bad) {
+__global__ void k_check_finite(const float* x, uint32_t n, int* bad) {
     pdl_trigger_dependents();
     pdl_grid_wait();
     bool finite = true;
@@ -337,7 +333,7 @@ __global__ void k_check_finite(const float* __restrict__ x, uint32_t n, int* __r
 
 // the step's greedy token (largest packed argmax key: largest logit, lowest
 // index on ties) becomes the next step's input at the next position
-__global__ void k_step_next(qw6k_step* __restrict__ step, const unsigned long long* __restrict__ key) {
+__global__ void k_step_next(qw6k_step* step, const unsigned long long* key) {
     pdl_grid_wait();
     step->token = ~(uint32_t)(*key & 0xffffffffull);
     step->pos += 1;

@@ -18,8 +18,7 @@
 
 namespace qw6 {
 
-__global__ void k_route(const float* __restrict__ logits, int ntok, int ne, int k, int32_t* __restrict__ idx,
-                        float* __restrict__ w) {
+__global__ void k_route(const float* logits, int ntok, int ne, int k, int32_t* idx, float* w) {
     pdl_grid_wait();
     const int tok = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (tok >= ntok) return;
@@ -40,7 +39,7 @@ __global__ void k_gather(const float* __restrict__ eo, const float* __restrict__
 // ------------------------------------------------------------- silu_mul --
 __device__ __forceinline__ float silu_ref(float v) { return __fdiv_rn(v, __fadd_rn(1.0f, expf(-v))); }
 
-__global__ void k_silu_mul(const float* __restrict__ g, const float* __restrict__ u, float* __restrict__ o, int n) {
+__global__ void k_silu_mul(const float* g, const float* u, float* o, int n) {
     pdl_trigger_dependents();
     pdl_grid_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;

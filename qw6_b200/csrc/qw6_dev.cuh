@@ -380,9 +380,9 @@ __device__ __forceinline__ XStage xstage_carve(uint8_t* base, int ntp, int cols)
     return s;
 }
 
-__device__ __forceinline__ void xstage_fill_warps(const XStage& s, const float* __restrict__ x, int ldx, int ntok,
-                                                  int ntp, int cols, const int32_t* rowsel, int rowdiv,
-                                                  int first_warp, int nwarps);
+__device__ __forceinline__ void xstage_fill_warps(const XStage& s, const float* x, int ldx, int ntok, int ntp,
+                                                  int cols, const int32_t* rowsel, int rowdiv, int first_warp,
+                                                  int nwarps);
 
 // Quantize ntok token rows of x (row stride ldx floats) into the stage;
 // tokens [ntok, ntp) are zero.  Stage row j reads x row j, or row
@@ -390,7 +390,7 @@ __device__ __forceinline__ void xstage_fill_warps(const XStage& s, const float* 
 // negative entry stages a zero row).
 // One warp per (token, 256-block); all threads of the CTA must call it
 // (caller synchronizes afterwards).
-__device__ __forceinline__ void xstage_fill(const XStage& s, const float* __restrict__ x, int ldx,
+__device__ __forceinline__ void xstage_fill(const XStage& s, const float* x, int ldx,
                                             int ntok, int ntp, int cols, const int32_t* rowsel = nullptr,
                                             int rowdiv = 1) {
     xstage_fill_warps(s, x, ldx, ntok, ntp, cols, rowsel, rowdiv, threadIdx.x >> 5, blockDim.x >> 5);
@@ -398,9 +398,9 @@ __device__ __forceinline__ void xstage_fill(const XStage& s, const float* __rest
 
 // Same, executed by warps first_warp, first_warp + nwarps, ... only (no
 // block-wide synchronization inside; a single warp may stage on its own).
-__device__ __forceinline__ void xstage_fill_warps(const XStage& s, const float* __restrict__ x, int ldx, int ntok,
-                                                  int ntp, int cols, const int32_t* rowsel, int rowdiv,
-                                                  int first_warp, int nwarps) {
+__device__ __forceinline__ void xstage_fill_warps(const XStage& s, const float* x, int ldx, int ntok, int ntp,
+                                                  int cols, const int32_t* rowsel, int rowdiv, int first_warp,
+                                                  int nwarps) {
     const int warp = first_warp, lane = threadIdx.x & 31, nw = nwarps;
     const int nb = cols / 256;
     for (int item = warp; item < ntp * nb; item += nw) {

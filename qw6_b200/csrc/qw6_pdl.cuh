@@ -2,7 +2,11 @@
 // stream (also inside CUDA graphs): a kernel launched with launch_pdl may be
 // scheduled while its predecessor still runs, and must call pdl_wait()
 // before it touches anything the predecessor writes (pdl_wait returns at
-// once when the kernel was launched normally).
+// once when the kernel was launched normally).  Such a kernel must not take
+// data that an earlier kernel writes through `const T* __restrict__`: the
+// compiler may then treat it as read-only for the kernel's whole life, read
+// it through the non-coherent path and move the loads above the wait (on the
+// B200 this returned stale rows); weights written once at upload may be.
 #pragma once
 
 #include <cuda_runtime.h>

@@ -22,8 +22,7 @@ __device__ __forceinline__ uint32_t route_key(float v) {
 // -inf, not removed, so when all remaining values are -inf index 0 is chosen
 // (again).  Softmax over the selected logits as qw6 does: max-subtract, expf,
 // sum in selection order, divide.
-__device__ __forceinline__ void route_token(const float* __restrict__ lg, int ne, int k, int32_t* __restrict__ idx,
-                                            float* __restrict__ w, int lane) {
+__device__ __forceinline__ void route_token(const float* lg, int ne, int k, int32_t* idx, float* w, int lane) {
     float v[8];
     uint32_t key[8];
 #pragma unroll

@@ -3,7 +3,7 @@
     python -m qw6_b200.prof matvec <quant> <rows> <cols> [reps] [ntok]
     python -m qw6_b200.prof moe_decode <config> [layers] [steps]
     python -m qw6_b200.prof lm_head <ntok> [reps]
-    python -m qw6_b200.prof decoder <tokens>
+    python -m qw6_b200.prof decoder <tokens> [layers]
 
 matvec: `reps` (default 5) launches of the packed quantized matvec
 (qw6cu_matvec) over `ntok` tokens (default 1) on `rows` x `cols` random packed
@@ -24,6 +24,8 @@ decoder: `tokens` greedy steps of the decode-step executor
 (qw6cu_decoder_generate) on a full-size synthetic qw6 model (40 layers with
 distinct weights, 248320-token vocabulary; 10.6 GB on the device, ~16 s to
 generate on the host); each step is one CUDA graph of ~425 launches.
+`layers` (default 40) fewer layers for captures that replay a kernel
+(4 layers: ~1.2 GB on the device).
 
 The values are random, so the outputs are meaningless; only the kernels'
 work is real.
@@ -105,10 +107,10 @@ def lm_head(ntok: int, reps: int = 5) -> None:
     print(f"lm_head ntok {ntok}: {reps} launches")
 
 
-def decoder(tokens: int = 3) -> None:
+def decoder(tokens: int = 3, layers: int = 40) -> None:
     from qw6_b200 import lib as L
     from qw6_b200 import synth as S
-    m = S.fwd_model(seed=31, n_layers=40, vocab=S.VOCAB, embd_rows=S.VOCAB, attn_period=40, expert_period=40)
+    m = S.fwd_model(seed=31, n_layers=layers, vocab=S.VOCAB, embd_rows=S.VOCAB, attn_period=40, expert_period=40)
     ctx = L.Context(0)
     dec = L.Decoder(ctx, m, max_ctx=4096)
     del m
@@ -128,7 +130,7 @@ def main(argv: list[str]) -> int:
         lm_head(*(int(a) for a in argv[1:3]))
         return 0
     if len(argv) >= 1 and argv[0] == "decoder":
-        decoder(*(int(a) for a in argv[1:2]))
+        decoder(*(int(a) for a in argv[1:3]))
         return 0
     print(__doc__)
     return 2
