@@ -27,10 +27,11 @@
 // (__fmul_rn, __fadd_rn, ...: no contraction); dot products and sums are
 // reductions in another order than qw6's sequential loops.  Every kernel is
 // launched with programmatic dependent launch: it lets its successor start,
-// may load weights (written once, at upload), and waits for its predecessor
-// before it reads anything a kernel writes -- the recurrent state and the
-// caches included: reading those before the wait gave wrong results on the
-// B200 although no kernel of the step writes them before.
+// may load weights (written once, at upload) and its own recurrent state
+// (written only by the same kernel of the previous step), and waits for its
+// predecessor before it reads what that one writes.  Data an earlier kernel
+// writes comes through plain pointers, never `const __restrict__` (see
+// qw6_pdl.cuh).
 #include <cuda_runtime.h>
 
 #include "qw6_launch.h"
@@ -113,15 +114,16 @@ __global__ void __launch_bounds__(512) k_dn_token(const float* proj, const qw6k_
     __shared__ float vs[kVD], o[kVD], gbs[2];
     __shared__ float red[16];
     pdl_trigger_dependents();
-    pdl_grid_wait();
     const int vh = blockIdx.x, kh = vh % kKH, tid = threadIdx.x, part = tid >> 7, i = tid & 127;
     const int warp = tid >> 5, lane = tid & 31;
-    const uint32_t pos = step->pos;
-    // this warp's 8 state rows: independent of the conv, loaded first
+    // this warp's 8 state rows, written only by this kernel in the previous
+    // step: loaded while the projections finish
     float4* s = reinterpret_cast<float4*>(state + (size_t)vh * kVD * kVD);
     float4 row[8];
 #pragma unroll
     for (int r = 0; r < 8; r++) row[r] = s[(warp * 8 + r) * (kVD / 4) + lane];
+    pdl_grid_wait();
+    const uint32_t pos = step->pos;
     float v = 0.f;
     if (part < 3) {
         const int c = part == 0 ? kh * kKD + i : part == 1 ? kKH * kKD + kh * kKD + i : 2 * kKH * kKD + vh * kVD + i;
