@@ -331,11 +331,17 @@ struct Fmt<QW6F_IQ3_S> {
 // H = (X+128) >> 8, L = X - 256 H (both in [-128, 127]), x ~= s*(256H+L).
 // MMA column n of n-tile q is token 4q + n/2, limb n%2, so C columns
 // (2t, 2t+1) of lane t carry the two limbs of token 4q+t.
+// The per-token rows of sx, xsum and nx32 are padded (xs_sx_ld etc.): the
+// four lanes t of a quad read four tokens' entries of the same block at
+// once, and unpadded rows of 2^k bytes would put them in one bank.
+__host__ __device__ constexpr int xs_sx_ld(int nb) { return nb + 1; }   // floats
+__host__ __device__ constexpr int xs_sum_ld(int ns) { return ns + 4; }  // floats (float4 reads)
+__host__ __device__ constexpr int xs_nx_ld(int ns) { return ns + 1; }   // int2
 struct XView {
     const int8_t* q;    // [ntp][2][stride]
-    const float* sx;    // [ntp][nb]
-    const float* xsum;  // [ntp][ns]  fp32 sum of each 32-sub-block (K formats)
-    const int2* nx32;   // [ntp][ns]  (-32*sum H, -32*sum L) per sub-block (Q6_K)
+    const float* sx;    // [ntp][xs_sx_ld(nb)]
+    const float* xsum;  // [ntp][xs_sum_ld(ns)]  fp32 sum of each 32-sub-block (K formats)
+    const int2* nx32;   // [ntp][xs_nx_ld(ns)]   (-32*sum H, -32*sum L) per sub-block (Q6_K)
     int stride, nb, ns;
 
     __device__ __forceinline__ uint2 b64(int qt, int j, int lane) const {
@@ -352,8 +358,8 @@ struct XView {
 __host__ __device__ inline int xstage_stride(int cols) { return cols + 32; }
 __host__ __device__ inline size_t xstage_bytes(int ntp, int cols) {
     const int nb = cols / 256, ns = cols / 32;
-    return (size_t)ntp * 2 * xstage_stride(cols) + (size_t)ntp * nb * 4 + (size_t)ntp * ns * 4 +
-           (size_t)ntp * ns * 8;
+    return (size_t)ntp * 2 * xstage_stride(cols) + (size_t)ntp * xs_sx_ld(nb) * 4 +
+           (size_t)ntp * xs_sum_ld(ns) * 4 + (size_t)ntp * xs_nx_ld(ns) * 8;
 }
 
 struct XStage {
@@ -373,10 +379,10 @@ __device__ __forceinline__ XStage xstage_carve(uint8_t* base, int ntp, int cols)
     s.q = reinterpret_cast<int8_t*>(base);
     uint8_t* p = base + (size_t)ntp * 2 * s.stride;
     s.nx32 = reinterpret_cast<int2*>(p);
-    p += (size_t)ntp * s.ns * 8;
+    p += (size_t)ntp * xs_nx_ld(s.ns) * 8;
+    s.xsum = reinterpret_cast<float*>(p);  // 16-byte aligned for its float4 reads (ntp is a multiple of 4)
+    p += (size_t)ntp * xs_sum_ld(s.ns) * 4;
     s.sx = reinterpret_cast<float*>(p);
-    p += (size_t)ntp * s.nb * 4;
-    s.xsum = reinterpret_cast<float*>(p);
     return s;
 }
 
@@ -411,11 +417,11 @@ __device__ __forceinline__ void xstage_fill_warps(const XStage& s, const float* 
             *reinterpret_cast<uint2*>(s.q + (tok * 2 + 0) * s.stride + 256 * b + 8 * lane) = make_uint2(0u, 0u);
             *reinterpret_cast<uint2*>(s.q + (tok * 2 + 1) * s.stride + 256 * b + 8 * lane) = make_uint2(0u, 0u);
             if ((lane & 3) == 0) {
-                const int j = tok * s.ns + 8 * b + (lane >> 2);
-                s.xsum[j] = 0.f;
-                s.nx32[j] = make_int2(0, 0);
+                const int j = 8 * b + (lane >> 2);
+                s.xsum[tok * xs_sum_ld(s.ns) + j] = 0.f;
+                s.nx32[tok * xs_nx_ld(s.ns) + j] = make_int2(0, 0);
             }
-            if (lane == 0) s.sx[tok * nb + b] = 0.f;
+            if (lane == 0) s.sx[tok * xs_sx_ld(nb) + b] = 0.f;
             continue;
         }
         if (sel >= 0) {
@@ -463,11 +469,11 @@ __device__ __forceinline__ void xstage_fill_warps(const XStage& s, const float* 
             sl += __shfl_xor_sync(0xffffffffu, sl, o);
         }
         if ((lane & 3) == 0) {
-            const int j = tok * s.ns + 8 * b + (lane >> 2);
-            s.xsum[j] = sum;
-            s.nx32[j] = make_int2(-32 * sh, -32 * sl);
+            const int j = 8 * b + (lane >> 2);
+            s.xsum[tok * xs_sum_ld(s.ns) + j] = sum;
+            s.nx32[tok * xs_nx_ld(s.ns) + j] = make_int2(-32 * sh, -32 * sl);
         }
-        if (lane == 0) s.sx[tok * nb + b] = (amax > 0.f || amax != amax) ? amax / 32639.f : 0.f;
+        if (lane == 0) s.sx[tok * xs_sx_ld(nb) + b] = (amax > 0.f || amax != amax) ? amax / 32639.f : 0.f;
     }
 }
 
@@ -495,7 +501,7 @@ __device__ __forceinline__ void finish_block(float (&acc)[2][NQ], const int (&iH
     const int t = lane & 3;
 #pragma unroll
     for (int qt = 0; qt < NQ; qt++) {
-        const float s = xv.sx[(4 * qt + t) * xv.nb + b];
+        const float s = xv.sx[(4 * qt + t) * xs_sx_ld(xv.nb) + b];
 #pragma unroll
         for (int rh = 0; rh < 2; rh++)
             acc[rh][qt] += dfac[rh] * s * fmaf(256.f, (float)iH[rh][qt], (float)iL[rh][qt]);
@@ -571,7 +577,7 @@ struct TileK45 {
         // minimum term: - dmin * sum_j m_j * xsum_j
 #pragma unroll
         for (int qt = 0; qt < NQ; qt++) {
-            const float* xs = xv.xsum + (4 * qt + t) * xv.ns + 8 * b;
+            const float* xs = xv.xsum + (4 * qt + t) * xs_sum_ld(xv.ns) + 8 * b;
             const float4 x0 = *reinterpret_cast<const float4*>(xs);
             const float4 x1 = *reinterpret_cast<const float4*>(xs + 4);
 #pragma unroll
@@ -650,7 +656,7 @@ struct Tile<QW6F_Q6_K, NQ> {
 #pragma unroll
                 for (int qt = 0; qt < NQ; qt++) {
                     const uint2 bb = xv.b64(qt, 8 * b + j, lane);
-                    const int2 nx = xv.nx32[(4 * qt + t) * xv.ns + 8 * b + j];
+                    const int2 nx = xv.nx32[(4 * qt + t) * xs_nx_ld(xv.ns) + 8 * b + j];
                     int d[4];
                     mma_k32(d, a[0][0], a[1][0], a[0][1], a[1][1], bb.x, bb.y, nx.x, nx.y, nx.x, nx.y);
                     iH[0][qt] += s0 * d[0];
