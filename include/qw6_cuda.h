@@ -242,6 +242,22 @@ int qw6cu_moe_prefill(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu
 size_t qw6cu_moe_prefill_workspace_bytes(uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t n_experts,
                                          uint32_t top_k);
 
+/* qw6cu_moe_prefill over n_batches batches of ntok tokens in HOST memory:
+ * batch b reads logits[b] (fp32 [ntok x n_experts]) and x_bf16[b] (bf16
+ * [ntok x hidden]) and writes out[b] (fp32 [ntok x hidden]); entries may
+ * repeat.  Every batch is copied in, run and copied back, pipelined over two
+ * device slots and two copy streams: the copy-in of batch b+1 and the
+ * read-back of batch b-1 run while the experts of batch b run on the context
+ * stream, so a long call streams at the rate of the slowest of the three.
+ * The copies overlap only from page-locked host memory (cudaHostAlloc /
+ * cudaHostRegister); pageable buffers give the same results, serialized.
+ * Synchronous: returns once every out[b] is written (or on the first error).
+ * Each batch's result is bit for bit that of qw6cu_moe_prefill. */
+int qw6cu_moe_prefill_hostio(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
+                             const qw6cu_expert_pack *down, const float *const *logits, const void *const *x_bf16,
+                             float *const *out, uint32_t n_batches, uint32_t ntok, uint32_t hidden, uint32_t inter,
+                             uint32_t n_experts, uint32_t top_k);
+
 /* Expert-parallel building block: the same grouped GEMMs with the routing
  * supplied per row instead of computed from logits.  Row r of x_bf16
  * ([nrows x hidden], device) is sent through expert row_expert[r] (an index

@@ -120,6 +120,13 @@ void qw6cu_destroy(qw6cu_ctx *ctx) {
     if (!ctx) return;
     cudaSetDevice(ctx->device);
     cudaStreamSynchronize(ctx->st);
+    if (ctx->io_ready) {
+        cudaStreamSynchronize(ctx->io_in);
+        cudaStreamSynchronize(ctx->io_out);
+        for (int i = 0; i < 9; i++) cudaEventDestroy(ctx->io_ev[i]);
+        cudaStreamDestroy(ctx->io_in);
+        cudaStreamDestroy(ctx->io_out);
+    }
     prof_free(ctx);
     for (int i = 0; i < QW6H_NBUF; i++) cudaFree(ctx->buf[i].p);
     cudaFreeHost(ctx->pinned);

@@ -18,6 +18,7 @@ enum {
     QW6H_BUF_WS,      /* workspace of the fused MoE / LM-head calls */
     QW6H_BUF_BLOCK,   /* intermediates of the MoE FFN block */
     QW6H_BUF_SAMPLE,  /* per-row histograms of the sampler */
+    QW6H_BUF_IO,      /* the two input/output slots of the pipelined host-buffer prefill */
     QW6H_NBUF
 };
 
@@ -67,6 +68,12 @@ struct qw6cu_ctx {
     /* per-launch event profiler (qw6cu_profile_begin/end) */
     int prof_on, prof_cap, prof_n;
     qw6h_prof_rec *prof;
+    /* copy streams and events of the pipelined host-buffer prefill, created
+     * on its first call: ev[0] start; per slot s: ev[1+s] inputs landed,
+     * ev[3+s] inputs consumed, ev[5+s] output ready, ev[7+s] output read */
+    int io_ready;
+    cudaStream_t io_in, io_out;
+    cudaEvent_t io_ev[9];
 };
 
 void qw6h_set_err(const char *fmt, ...);

@@ -161,15 +161,11 @@ size_t qw6cu_moe_prefill_workspace_bytes(uint32_t ntok, uint32_t hidden, uint32_
     return qw6k_moe_prefill_ws_bytes(ntok, hidden, inter, n_experts, top_k);
 }
 
-int qw6cu_moe_prefill(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
-                      const qw6cu_expert_pack *down, const float *logits, const void *x_bf16, float *out,
-                      uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t n_experts, uint32_t top_k) {
-    int rc = qw6h_use(ctx);
-    if (rc) return rc;
-    if (!gate || !up || !down || gate->quant != up->quant) {
-        qw6h_set_err("qw6cu_moe_prefill: gate and up packs must be given and share one quant type");
-        return QW6CU_ERR_ARG;
-    }
+/* The prefill layer on ctx->st; the workspace and the error word must
+ * already have their full size when the call is part of a pipeline. */
+static int prefill_run(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
+                       const qw6cu_expert_pack *down, const float *logits, const void *x_bf16, float *out,
+                       uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t n_experts, uint32_t top_k) {
     int *err = qw6h_dev_err(ctx);
     if (!err) return QW6CU_ERR_NOMEM;
     qw6k_moe_desc d;
@@ -193,13 +189,122 @@ int qw6cu_moe_prefill(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu
     d.ws_bytes = qw6k_moe_prefill_ws_bytes(ntok, hidden, inter, n_experts, top_k);
     d.ws = qw6h_buf(ctx, QW6H_BUF_WS, d.ws_bytes);
     if (!d.ws) return QW6CU_ERR_NOMEM;
-    rc = qw6h_rc(qw6k_moe_prefill_check(&d, err), "moe_prefill");
+    int rc = qw6h_rc(qw6k_moe_prefill_check(&d, err), "moe_prefill");
     static const int kid[7] = {QW6H_K_PF_PLAN,  QW6H_K_PF_PLAN,  QW6H_K_PF_PLAN, QW6H_K_PF_PLAN,
                                QW6H_K_PF_GEMM1, QW6H_K_PF_GEMM2, QW6H_K_PF_COMBINE};
     for (int ph = 0; ph < 7 && !rc; ph++) {
         const int rec = qw6h_prof_a(ctx, kid[ph]);
         rc = qw6h_rc(qw6k_moe_prefill_phase(&d, err, ph, ctx->st), "moe_prefill");
         qw6h_prof_b(ctx, rec);
+    }
+    return rc;
+}
+
+int qw6cu_moe_prefill(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
+                      const qw6cu_expert_pack *down, const float *logits, const void *x_bf16, float *out,
+                      uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t n_experts, uint32_t top_k) {
+    int rc = qw6h_use(ctx);
+    if (rc) return rc;
+    if (!gate || !up || !down || gate->quant != up->quant) {
+        qw6h_set_err("qw6cu_moe_prefill: gate and up packs must be given and share one quant type");
+        return QW6CU_ERR_ARG;
+    }
+    return prefill_run(ctx, gate, up, down, logits, x_bf16, out, ntok, hidden, inter, n_experts, top_k);
+}
+
+static int io_setup(qw6cu_ctx *ctx) {
+    if (ctx->io_ready) return 0;
+    cudaStream_t s[2];
+    cudaError_t e = cudaSuccess;
+    int ns = 0, ne = 0;
+    for (; ns < 2; ns++)
+        if ((e = cudaStreamCreateWithFlags(&s[ns], cudaStreamNonBlocking)) != cudaSuccess) break;
+    for (; e == cudaSuccess && ne < 9; ne++)
+        if ((e = cudaEventCreateWithFlags(&ctx->io_ev[ne], cudaEventDisableTiming)) != cudaSuccess) break;
+    if (e != cudaSuccess) {
+        for (int i = 0; i < ne; i++) cudaEventDestroy(ctx->io_ev[i]);
+        for (int i = 0; i < ns; i++) cudaStreamDestroy(s[i]);
+        qw6h_set_err("qw6cu_moe_prefill_hostio: creating copy streams/events: %s", cudaGetErrorString(e));
+        return QW6CU_ERR_CUDA;
+    }
+    ctx->io_in = s[0];
+    ctx->io_out = s[1];
+    ctx->io_ready = 1;
+    return 0;
+}
+
+int qw6cu_moe_prefill_hostio(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
+                             const qw6cu_expert_pack *down, const float *const *logits, const void *const *x_bf16,
+                             float *const *out, uint32_t n_batches, uint32_t ntok, uint32_t hidden, uint32_t inter,
+                             uint32_t n_experts, uint32_t top_k) {
+    int rc = qw6h_use(ctx);
+    if (rc) return rc;
+    if (!gate || !up || !down || gate->quant != up->quant) {
+        qw6h_set_err("qw6cu_moe_prefill_hostio: gate and up packs must be given and share one quant type");
+        return QW6CU_ERR_ARG;
+    }
+    if (!n_batches) return 0;
+    if (!logits || !x_bf16 || !out) {
+        qw6h_set_err("qw6cu_moe_prefill_hostio: null host pointer array");
+        return QW6CU_ERR_ARG;
+    }
+    for (uint32_t b = 0; b < n_batches; b++)
+        if (!logits[b] || !x_bf16[b] || !out[b]) {
+            qw6h_set_err("qw6cu_moe_prefill_hostio: null host buffer of batch %u", b);
+            return QW6CU_ERR_ARG;
+        }
+    if ((rc = io_setup(ctx))) return rc;
+    /* every device buffer at its full size before the first copy (growing one
+     * later would synchronize in the middle of the pipeline) */
+    const size_t lb = ((size_t)ntok * n_experts * 4 + 255) & ~(size_t)255;
+    const size_t xb = ((size_t)ntok * hidden * 2 + 255) & ~(size_t)255;
+    const size_t ob = (size_t)ntok * hidden * 4;
+    const size_t slot = lb + xb + ((ob + 255) & ~(size_t)255);
+    uint8_t *io = qw6h_buf(ctx, QW6H_BUF_IO, 2 * slot);
+    if (!io || !qw6h_dev_err(ctx) ||
+        !qw6h_buf(ctx, QW6H_BUF_WS, qw6k_moe_prefill_ws_bytes(ntok, hidden, inter, n_experts, top_k)))
+        return QW6CU_ERR_NOMEM;
+    cudaEvent_t *ev = ctx->io_ev;
+    cudaStream_t cs = ctx->st;
+    /* the copies start after the work already queued on the context stream
+     * (including the zero-fill of freshly grown buffers) */
+    cudaError_t e = cudaEventRecord(ev[0], cs);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(ctx->io_in, ev[0], 0);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(ctx->io_out, ev[0], 0);
+    for (uint32_t b = 0; b < n_batches && e == cudaSuccess && !rc; b++) {
+        const int s = (int)(b & 1);
+        uint8_t *base = io + (size_t)s * slot;
+        float *dl = (float *)base, *dout = (float *)(base + lb + xb);
+        void *dx = base + lb;
+        /* copy in once batch b-2 (same slot) has consumed its inputs */
+        if ((e = cudaStreamWaitEvent(ctx->io_in, ev[3 + s], 0)) != cudaSuccess) break;
+        if ((e = cudaMemcpyAsync(dl, logits[b], (size_t)ntok * n_experts * 4, cudaMemcpyHostToDevice, ctx->io_in)) !=
+            cudaSuccess)
+            break;
+        if ((e = cudaMemcpyAsync(dx, x_bf16[b], (size_t)ntok * hidden * 2, cudaMemcpyHostToDevice, ctx->io_in)) !=
+            cudaSuccess)
+            break;
+        if ((e = cudaEventRecord(ev[1 + s], ctx->io_in)) != cudaSuccess) break;
+        /* run once the inputs landed and batch b-2's output has been read */
+        if ((e = cudaStreamWaitEvent(cs, ev[1 + s], 0)) != cudaSuccess) break;
+        if ((e = cudaStreamWaitEvent(cs, ev[7 + s], 0)) != cudaSuccess) break;
+        rc = prefill_run(ctx, gate, up, down, dl, dx, dout, ntok, hidden, inter, n_experts, top_k);
+        if (rc) break;
+        if ((e = cudaEventRecord(ev[3 + s], cs)) != cudaSuccess) break;
+        if ((e = cudaEventRecord(ev[5 + s], cs)) != cudaSuccess) break;
+        /* read back once the experts wrote it */
+        if ((e = cudaStreamWaitEvent(ctx->io_out, ev[5 + s], 0)) != cudaSuccess) break;
+        if ((e = cudaMemcpyAsync(out[b], dout, ob, cudaMemcpyDeviceToHost, ctx->io_out)) != cudaSuccess) break;
+        if ((e = cudaEventRecord(ev[7 + s], ctx->io_out)) != cudaSuccess) break;
+    }
+    /* drain all three streams, also after an error */
+    cudaError_t e2 = cudaStreamSynchronize(ctx->io_in);
+    cudaError_t e3 = cudaStreamSynchronize(cs);
+    cudaError_t e4 = cudaStreamSynchronize(ctx->io_out);
+    if (e == cudaSuccess) e = e2 != cudaSuccess ? e2 : e3 != cudaSuccess ? e3 : e4;
+    if (!rc && e != cudaSuccess) {
+        qw6h_set_err("qw6cu_moe_prefill_hostio: %s", cudaGetErrorString(e));
+        rc = QW6CU_ERR_CUDA;
     }
     return rc;
 }

@@ -129,6 +129,8 @@ def load() -> C.CDLL:
     lib.qw6cu_moe_decode_hostio.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32]
     lib.qw6cu_moe_decode_noalloc.argtypes = [pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp]
     lib.qw6cu_moe_prefill.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32]
+    _pp = C.POINTER(_vp)
+    lib.qw6cu_moe_prefill_hostio.argtypes = [_vp, pk, pk, pk, _pp, _pp, _pp, _u32, _u32, _u32, _u32, _u32, _u32]
     lib.qw6cu_gguf_open.argtypes = [C.c_char_p, C.POINTER(_vp)]
     lib.qw6cu_gguf_close.argtypes = [_vp]
     lib.qw6cu_gguf_close.restype = None
@@ -353,6 +355,18 @@ class Context:
                     inter, n_experts, top_k):
         _check(self.lib.qw6cu_moe_prefill(self.h, C.byref(gate), C.byref(up), C.byref(down), logits, x_bf16, out,
                                           ntok, hidden, inter, n_experts, top_k), "qw6cu_moe_prefill")
+
+    def moe_prefill_hostio(self, gate: ExpertPack, up: ExpertPack, down: ExpertPack, logits, x_bf16, out, ntok,
+                           hidden, inter, n_experts, top_k):
+        """qw6cu_moe_prefill_hostio: `logits`, `x_bf16`, `out` are equal-length
+        sequences of HOST addresses, one entry per batch of ntok tokens."""
+        n = len(logits)
+        if len(x_bf16) != n or len(out) != n:
+            raise ValueError("moe_prefill_hostio: logits, x_bf16 and out need one host address per batch")
+        arr = lambda v: (_vp * max(n, 1))(*[int(p) for p in v])  # noqa: E731
+        _check(self.lib.qw6cu_moe_prefill_hostio(self.h, C.byref(gate), C.byref(up), C.byref(down), arr(logits),
+                                                 arr(x_bf16), arr(out), n, ntok, hidden, inter, n_experts, top_k),
+               "qw6cu_moe_prefill_hostio")
 
     def moe_expert_rows(self, gate: ExpertPack, up: ExpertPack, down: ExpertPack, x_bf16, row_expert, out_bf16,
                         nrows, hidden, inter, n_experts):

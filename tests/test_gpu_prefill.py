@@ -7,7 +7,7 @@ import pytest
 
 from qw6_b200 import lib as L
 from qw6_b200 import synth as S
-from tests.conftest import rel_err
+from tests.conftest import rel_err, same_bits
 from tests.gpu_util import dev, empty_f32, host, pack, sync
 
 pytestmark = pytest.mark.gpu
@@ -93,3 +93,50 @@ def test_prefill_config3(cuda, oracle, rng):
     ref, _, _ = oracle.moe_layer(S.Q4_K, gate, up, S.Q6_K, down, logits[toks], x32[toks], top_k=8)
     errs32 = [rel_err(out[t], ref[i]) for i, t in enumerate(toks)]
     assert max(errs32) <= TOL, max(errs32)
+
+
+def test_prefill_hostio_pipelined(cuda, oracle, rng):
+    """qw6cu_moe_prefill_hostio: batches in host memory, pipelined over two
+    device slots (copy-in of batch b+1 and read-back of b-1 beside the experts
+    of b).  Five batches from page-locked memory (one repeated, so both slots
+    are reused) and two from pageable numpy arrays: every output is bit for bit
+    qw6cu_moe_prefill's on the same batch, and sampled tokens are within the
+    prefill tolerance of the fp32 oracle."""
+    torch = pytest.importorskip("torch")
+    E, H, I, K, T = 32, 2048, 512, 8, 300
+    gate, up, down = S.moe_weights(rng, E, S.Q4_K, S.Q6_K, H, I)
+    pg, sg = pack(cuda, S.Q4_K, gate, I, H, E)
+    pu, su = pack(cuda, S.Q4_K, up, I, H, E)
+    pd, sd = pack(cuda, S.Q6_K, down, H, I, E)
+    packs = (L.ExpertPack(S.Q4_K, pg.data_ptr(), sg), L.ExpertPack(S.Q4_K, pu.data_ptr(), su),
+             L.ExpertPack(S.Q6_K, pd.data_ptr(), sd))
+    lgs = [rng.standard_normal((T, E), dtype=np.float32) for _ in range(4)]
+    xbs = [S.bf16_round(rng.standard_normal((T, H), dtype=np.float32)) for _ in range(4)]
+    # device reference: one qw6cu_moe_prefill per distinct batch
+    ref = []
+    for lg, xb in zip(lgs, xbs):
+        ld, xd = dev(lg), dev(xb.view(np.int16))
+        o = empty_f32(T, H)
+        sync(cuda)
+        cuda.moe_prefill(*packs, ld.data_ptr(), xd.data_ptr(), o.data_ptr(), T, H, I, E, K)
+        cuda.check_device_errors()
+        ref.append(host(o))
+    order = [0, 1, 2, 3, 1]
+    h_lg = [torch.from_numpy(lg).pin_memory() for lg in lgs]
+    h_x = [torch.from_numpy(xb.view(np.int16)).pin_memory() for xb in xbs]
+    h_out = [torch.full((T, H), float("nan"), dtype=torch.float32).pin_memory() for _ in order]
+    sync(cuda)
+    cuda.moe_prefill_hostio(*packs, [h_lg[b].data_ptr() for b in order], [h_x[b].data_ptr() for b in order],
+                            [o.data_ptr() for o in h_out], T, H, I, E, K)
+    cuda.check_device_errors()
+    for o, b in zip(h_out, order):
+        assert same_bits(o.numpy(), ref[b]), b
+    # pageable host memory: same results, copies serialized
+    p_lg = [np.ascontiguousarray(lgs[b]) for b in (2, 0)]
+    p_x = [np.ascontiguousarray(xbs[b]) for b in (2, 0)]
+    p_out = [np.full((T, H), np.nan, np.float32) for _ in range(2)]
+    cuda.moe_prefill_hostio(*packs, [a.ctypes.data for a in p_lg], [a.ctypes.data for a in p_x],
+                            [a.ctypes.data for a in p_out], T, H, I, E, K)
+    assert same_bits(p_out[0], ref[2]) and same_bits(p_out[1], ref[0])
+    toks = list(rng.choice(T, 24, replace=False))
+    check_tokens(oracle, S.Q4_K, gate, up, S.Q6_K, down, lgs[3], xbs[3], h_out[3].numpy(), toks, K)
