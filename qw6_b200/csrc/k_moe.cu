@@ -153,7 +153,7 @@ __device__ __forceinline__ void small_plan(SmallPlan* P, const MoeArgs& a) {
 }
 
 template <int F, int NBW>
-__global__ void __launch_bounds__(kThreads) k_moe_small_gu(const MoeArgs a) {
+__device__ __forceinline__ void small_gu_body(const MoeArgs& a) {
     extern __shared__ __align__(16) uint8_t smem[];
     using T = Tile<F, 1>;
     constexpr int TB = T::TB;
@@ -229,6 +229,28 @@ __global__ void __launch_bounds__(kThreads) k_moe_small_gu(const MoeArgs a) {
                 m[8] = m1;
             }
     }
+}
+
+// Formats whose gate/up body fits 128 registers with (almost) no spills are
+// compiled for two CTAs per SM: a gate/up CTA and a down CTA (<= 128
+// registers) then share an SM, so the early-launched down kernel's CTAs
+// prefetch their weights beside gate/up instead of waiting for SMs to empty.
+template <int F>
+struct SmallGuPaired {
+    static constexpr bool value = F == QW6F_IQ2_XXS || F == QW6F_Q4_K_M || F == QW6F_Q4_K_S;
+};
+template <int F, int NBW>
+__global__ void __launch_bounds__(kThreads) k_moe_small_gu(const MoeArgs a) {
+    small_gu_body<F, NBW>(a);
+}
+template <int F, int NBW>
+__global__ void __launch_bounds__(kThreads, 2) k_moe_small_gu2(const MoeArgs a) {
+    small_gu_body<F, NBW>(a);
+}
+template <int F, int NBW>
+constexpr void (*small_gu_kernel())(MoeArgs) {
+    if constexpr (SmallGuPaired<F>::value) return k_moe_small_gu2<F, NBW>;
+    else return k_moe_small_gu<F, NBW>;
 }
 
 // Down projection + routing-weighted combine, one CTA per 16 output rows:
@@ -517,9 +539,9 @@ template <int F, int NBW>
 static int launch_small_gu(const MoeArgs& a, cudaStream_t st) {
     const size_t smem = tbl_bytes_of<F>() + xstage_bytes(4, a.hidden) + (size_t)kThreads * 4 * 4;
     static DevFlags cfg;
-    if (smem_optin(cfg, k_moe_small_gu<F, NBW>, 200 * 1024)) return QW6K_ERR_CUDA;
+    if (smem_optin(cfg, small_gu_kernel<F, NBW>(), 200 * 1024)) return QW6K_ERR_CUDA;
     const int ks = a.hidden / 256 / NBW, mgroups = (a.inter / 16) / (kWarps / ks);
-    return launch_ex(k_moe_small_gu<F, NBW>, a.ntok * a.topk * mgroups, kThreads, smem, true, st, a);
+    return launch_ex(small_gu_kernel<F, NBW>(), a.ntok * a.topk * mgroups, kThreads, smem, true, st, a);
 }
 
 template <int F>
@@ -589,10 +611,10 @@ static int small_down_any(uint32_t q, const MoeArgs& a, cudaStream_t st) {
 template <int F>
 static int dec_setup_one() {
     static DevFlags c1, c2, c3, c4, c5, c6;
-    int rc = smem_optin(c1, k_moe_small_gu<F, 1>, 200 * 1024);
+    int rc = smem_optin(c1, small_gu_kernel<F, 1>(), 200 * 1024);
     rc |= smem_optin(c2, k_moe_small_down<F>, 200 * 1024);
     static DevFlags c9;
-    rc |= smem_optin(c9, k_moe_small_gu<F, 2>, 200 * 1024);
+    rc |= smem_optin(c9, small_gu_kernel<F, 2>(), 200 * 1024);
     static DevFlags c7, c8;
     rc |= smem_optin(c3, k_moe_gateup<F, 1, 1>, 200 * 1024);
     rc |= smem_optin(c4, k_moe_gateup<F, 2, 1>, 200 * 1024);
