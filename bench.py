@@ -388,55 +388,22 @@ def ep_bench(args, torch, ctx, L, stream, rank, world, dist, c3):
 
     # end to end: every step copies its logits/x in from pinned host memory
     # and reads its output back, pipelined over two device slots (copy-in of
-    # step s+1 and read-back of step s-1 beside the experts of step s).  N=1:
-    # one qw6cu_moe_prefill_hostio call over all ke steps (the C ABI's
-    # host-buffer entry point); N>1: the same schedule around the
-    # expert-parallel layer with torch copy streams and events.
+    # step s+1 and read-back of step s-1 beside the experts of step s): one
+    # call of the C ABI's host-buffer entry point over all ke steps
+    # (qw6cu_moe_prefill_hostio; N>1 qw6cu_ep_layer_hostio on every rank).
     nh = 4  # distinct page-locked host batches, used in turn
     h_lg = [torch.from_numpy(logits[sl]).pin_memory() for _ in range(nh)]
     h_x = [torch.from_numpy(xbits[sl].view(np.int16)).pin_memory() for _ in range(nh)]
     h_outs = [torch.empty((tpr, HIDDEN), dtype=torch.float32).pin_memory() for _ in range(nh)]
     ke = 128  # enough steps that filling and draining the pipeline (one copy-in, one read-back) is ~1%
-    if pm is None:
-        def e2e_run(n):
-            ctx.set_stream(stream.cuda_stream)
-            ctx.moe_prefill_hostio(*packs[0], [h_lg[s % nh].data_ptr() for s in range(n)],
-                                   [h_x[s % nh].data_ptr() for s in range(n)],
-                                   [h_outs[s % nh].data_ptr() for s in range(n)], tpr, HIDDEN, INTER, NE, TOPK)
-    else:
-        s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
-        d_lg = [torch.empty_like(lg) for _ in range(2)]
-        d_x = [torch.empty_like(x) for _ in range(2)]
-        d_out = [torch.empty_like(out) for _ in range(2)]
 
-        def e2e_run(n):
-            ev = {k: [torch.cuda.Event() for _ in range(2)] for k in ("landed", "used", "ready", "read")}
-            cs = torch.cuda.current_stream()
-            start = torch.cuda.Event()
-            start.record(cs)
-            s_in.wait_event(start)
-            s_out.wait_event(start)
-            for s in range(n):
-                k = s & 1
-                if s >= 2:
-                    s_in.wait_event(ev["used"][k])
-                with torch.cuda.stream(s_in):
-                    d_lg[k].copy_(h_lg[s % nh], non_blocking=True)
-                    d_x[k].copy_(h_x[s % nh], non_blocking=True)
-                    ev["landed"][k].record(s_in)
-                cs.wait_event(ev["landed"][k])
-                if s >= 2:
-                    cs.wait_event(ev["read"][k])
-                step(s, d_lg[k], d_x[k], d_out[k])
-                ev["used"][k].record(cs)
-                ev["ready"][k].record(cs)
-                s_out.wait_event(ev["ready"][k])
-                with torch.cuda.stream(s_out):
-                    h_outs[s % nh].copy_(d_out[k], non_blocking=True)
-                    ev["read"][k].record(s_out)
-            cs.wait_stream(s_in)
-            cs.wait_stream(s_out)
-            cs.synchronize()
+    def e2e_run(n):
+        lgp, xp, op = ([h[s % nh].data_ptr() for s in range(n)] for h in (h_lg, h_x, h_outs))
+        if pm is None:
+            ctx.set_stream(stream.cuda_stream)
+            ctx.moe_prefill_hostio(*packs[0], lgp, xp, op, tpr, HIDDEN, INTER, NE, TOPK)
+        else:
+            pm.hostio(lgp, xp, op, tpr, packs=packs[0])
 
     with torch.cuda.stream(stream):
         e2e_run(3)
@@ -837,8 +804,8 @@ def report(args, world, head, cpu):
         "kernels": {k: {"avg_us": round(v[0] / v[1] * 1e3, 2), "launches_per_step": v[1]} for k, v in prof.items()},
         "e2e": {"value": round(T3 * head["e2e_steps"] / (head["e2e_ms"] / 1e3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": head["h2d"], "d2h_bytes_per_step": head["d2h"],
-                "api": ("qw6_b200.ep.PeerMoE between torch copy streams" if world > 1
-                        else "qw6cu_moe_prefill_hostio (one call over all steps)")
+                "api": ("qw6cu_ep_layer_hostio" if world > 1 else "qw6cu_moe_prefill_hostio")
+                       + " (one call over all steps)"
                        + ": every step copies this rank's logits/x in from pinned host memory and its fp32 output "
                          "back (per-rank bytes), pipelined over two device slots -- step s+1's copy-in and step "
                          "s-1's read-back run beside step s's experts; the timed region ends when the last "

@@ -343,6 +343,15 @@ int qw6cu_ep_set_placement(qw6cu_ep *ep, const uint32_t *experts);
 int qw6cu_ep_layer(qw6cu_ep *ep, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
                    const qw6cu_expert_pack *down, const float *logits, const void *x_bf16, float *out,
                    uint32_t ntok);
+/* qw6cu_ep_layer over n_batches layer steps whose inputs and outputs are
+ * in HOST memory (this rank's tokens; arrays of one host address per step),
+ * pipelined as qw6cu_moe_prefill_hostio: the copy-in of step b+1 and the
+ * read-back of step b-1 run beside step b.  Every rank makes the same call
+ * with the same n_batches.  Synchronous: returns once every out[b] is
+ * written (or on the first error). */
+int qw6cu_ep_layer_hostio(qw6cu_ep *ep, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
+                          const qw6cu_expert_pack *down, const float *const *logits, const void *const *x_bf16,
+                          float *const *out, uint32_t n_batches, uint32_t ntok);
 /* Limit of every cross-GPU wait of this endpoint's later layers, in ms
  * (default 2000): a rank whose peer stops taking part gives up after it,
  * records the wait kind in the context's error word (41 counts, 42 rows,

@@ -337,6 +337,33 @@ int qw6cu_ep_layer(qw6cu_ep *ep, const qw6cu_expert_pack *gate, const qw6cu_expe
     return rc;
 }
 
+typedef struct {
+    qw6cu_ep *ep;
+    const qw6cu_expert_pack *gate, *up, *down;
+    uint32_t ntok;
+} ep_job;
+
+static int ep_job_run(void *arg, const float *logits, const void *x_bf16, float *out) {
+    const ep_job *j = (const ep_job *)arg;
+    return qw6cu_ep_layer(j->ep, j->gate, j->up, j->down, logits, x_bf16, out, j->ntok);
+}
+
+int qw6cu_ep_layer_hostio(qw6cu_ep *ep, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
+                          const qw6cu_expert_pack *down, const float *const *logits, const void *const *x_bf16,
+                          float *const *out, uint32_t n_batches, uint32_t ntok) {
+    if (!ep || !ep->connected || !ntok || ntok > ep->max_tok) {
+        qw6h_set_err("qw6cu_ep_layer_hostio: not connected or ntok outside 1..max_tokens");
+        return QW6CU_ERR_ARG;
+    }
+    int rc = qw6h_use(ep->ctx);
+    if (rc) return rc;
+    if (n_batches && !qw6h_dev_err(ep->ctx)) return QW6CU_ERR_NOMEM;
+    ep_job j = {ep, gate, up, down, ntok};
+    return qw6h_hostio_run(ep->ctx, "qw6cu_ep_layer_hostio", logits, x_bf16, out, n_batches,
+                           (size_t)ntok * ep->ne * 4, (size_t)ntok * ep->hidden * 2, (size_t)ntok * ep->hidden * 4,
+                           ep_job_run, &j);
+}
+
 int qw6cu_ep_last_rows(qw6cu_ep *ep, uint32_t *rows) {
     if (!ep || !rows) {
         qw6h_set_err("qw6cu_ep_last_rows: null argument");

@@ -4,6 +4,7 @@
 #define QW6_HOST_INTERNAL_H
 
 #include <stddef.h>
+#include <stdint.h>
 
 #include <cuda_runtime_api.h>
 
@@ -86,5 +87,12 @@ qw6cu_ctx *qw6h_default_locked(void);
 int qw6h_prof_a(qw6cu_ctx *ctx, int kid);
 int *qw6h_dev_err(qw6cu_ctx *ctx);
 void qw6h_prof_b(qw6cu_ctx *ctx, int rec);
+/* Pipelined host-buffer batches (two device slots, the context's copy
+ * streams): run(arg, logits, x, out) enqueues one batch's layer on ctx->st
+ * with device pointers into the current slot. */
+typedef int (*qw6h_hostio_fn)(void *arg, const float *logits, const void *x_bf16, float *out);
+int qw6h_hostio_run(qw6cu_ctx *ctx, const char *what, const float *const *logits, const void *const *x_bf16,
+                    float *const *out, uint32_t n_batches, size_t lg_bytes, size_t x_bytes, size_t out_bytes,
+                    qw6h_hostio_fn run, void *arg);
 
 #endif /* QW6_HOST_INTERNAL_H */

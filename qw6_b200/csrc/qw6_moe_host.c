@@ -233,37 +233,31 @@ static int io_setup(qw6cu_ctx *ctx) {
     return 0;
 }
 
-int qw6cu_moe_prefill_hostio(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
-                             const qw6cu_expert_pack *down, const float *const *logits, const void *const *x_bf16,
-                             float *const *out, uint32_t n_batches, uint32_t ntok, uint32_t hidden, uint32_t inter,
-                             uint32_t n_experts, uint32_t top_k) {
-    int rc = qw6h_use(ctx);
-    if (rc) return rc;
-    if (!gate || !up || !down || gate->quant != up->quant) {
-        qw6h_set_err("qw6cu_moe_prefill_hostio: gate and up packs must be given and share one quant type");
-        return QW6CU_ERR_ARG;
-    }
+/* The two-slot host-buffer pipeline shared by qw6cu_moe_prefill_hostio and
+ * qw6cu_ep_layer_hostio: batch b's logits/x are copied in on io_in, run(b)
+ * enqueues the layer on the context stream, and its output is read back on
+ * io_out; slot b % 2 is reused only once batch b-2's experts consumed its
+ * inputs and its output was read.  Drains all three streams before it
+ * returns, also after an error. */
+int qw6h_hostio_run(qw6cu_ctx *ctx, const char *what, const float *const *logits, const void *const *x_bf16,
+                    float *const *out, uint32_t n_batches, size_t lg_bytes, size_t x_bytes, size_t out_bytes,
+                    qw6h_hostio_fn run, void *arg) {
     if (!n_batches) return 0;
     if (!logits || !x_bf16 || !out) {
-        qw6h_set_err("qw6cu_moe_prefill_hostio: null host pointer array");
+        qw6h_set_err("%s: null host pointer array", what);
         return QW6CU_ERR_ARG;
     }
     for (uint32_t b = 0; b < n_batches; b++)
         if (!logits[b] || !x_bf16[b] || !out[b]) {
-            qw6h_set_err("qw6cu_moe_prefill_hostio: null host buffer of batch %u", b);
+            qw6h_set_err("%s: null host buffer of batch %u", what, b);
             return QW6CU_ERR_ARG;
         }
-    if ((rc = io_setup(ctx))) return rc;
-    /* every device buffer at its full size before the first copy (growing one
-     * later would synchronize in the middle of the pipeline) */
-    const size_t lb = ((size_t)ntok * n_experts * 4 + 255) & ~(size_t)255;
-    const size_t xb = ((size_t)ntok * hidden * 2 + 255) & ~(size_t)255;
-    const size_t ob = (size_t)ntok * hidden * 4;
-    const size_t slot = lb + xb + ((ob + 255) & ~(size_t)255);
+    int rc = io_setup(ctx);
+    if (rc) return rc;
+    const size_t lb = (lg_bytes + 255) & ~(size_t)255, xb = (x_bytes + 255) & ~(size_t)255;
+    const size_t slot = lb + xb + ((out_bytes + 255) & ~(size_t)255);
     uint8_t *io = qw6h_buf(ctx, QW6H_BUF_IO, 2 * slot);
-    if (!io || !qw6h_dev_err(ctx) ||
-        !qw6h_buf(ctx, QW6H_BUF_WS, qw6k_moe_prefill_ws_bytes(ntok, hidden, inter, n_experts, top_k)))
-        return QW6CU_ERR_NOMEM;
+    if (!io) return QW6CU_ERR_NOMEM;
     cudaEvent_t *ev = ctx->io_ev;
     cudaStream_t cs = ctx->st;
     /* the copies start after the work already queued on the context stream
@@ -278,35 +272,63 @@ int qw6cu_moe_prefill_hostio(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, cons
         void *dx = base + lb;
         /* copy in once batch b-2 (same slot) has consumed its inputs */
         if ((e = cudaStreamWaitEvent(ctx->io_in, ev[3 + s], 0)) != cudaSuccess) break;
-        if ((e = cudaMemcpyAsync(dl, logits[b], (size_t)ntok * n_experts * 4, cudaMemcpyHostToDevice, ctx->io_in)) !=
-            cudaSuccess)
-            break;
-        if ((e = cudaMemcpyAsync(dx, x_bf16[b], (size_t)ntok * hidden * 2, cudaMemcpyHostToDevice, ctx->io_in)) !=
-            cudaSuccess)
-            break;
+        if ((e = cudaMemcpyAsync(dl, logits[b], lg_bytes, cudaMemcpyHostToDevice, ctx->io_in)) != cudaSuccess) break;
+        if ((e = cudaMemcpyAsync(dx, x_bf16[b], x_bytes, cudaMemcpyHostToDevice, ctx->io_in)) != cudaSuccess) break;
         if ((e = cudaEventRecord(ev[1 + s], ctx->io_in)) != cudaSuccess) break;
         /* run once the inputs landed and batch b-2's output has been read */
         if ((e = cudaStreamWaitEvent(cs, ev[1 + s], 0)) != cudaSuccess) break;
         if ((e = cudaStreamWaitEvent(cs, ev[7 + s], 0)) != cudaSuccess) break;
-        rc = prefill_run(ctx, gate, up, down, dl, dx, dout, ntok, hidden, inter, n_experts, top_k);
-        if (rc) break;
+        if ((rc = run(arg, dl, dx, dout))) break;
         if ((e = cudaEventRecord(ev[3 + s], cs)) != cudaSuccess) break;
         if ((e = cudaEventRecord(ev[5 + s], cs)) != cudaSuccess) break;
-        /* read back once the experts wrote it */
+        /* read back once the layer wrote it */
         if ((e = cudaStreamWaitEvent(ctx->io_out, ev[5 + s], 0)) != cudaSuccess) break;
-        if ((e = cudaMemcpyAsync(out[b], dout, ob, cudaMemcpyDeviceToHost, ctx->io_out)) != cudaSuccess) break;
+        if ((e = cudaMemcpyAsync(out[b], dout, out_bytes, cudaMemcpyDeviceToHost, ctx->io_out)) != cudaSuccess) break;
         if ((e = cudaEventRecord(ev[7 + s], ctx->io_out)) != cudaSuccess) break;
     }
-    /* drain all three streams, also after an error */
     cudaError_t e2 = cudaStreamSynchronize(ctx->io_in);
     cudaError_t e3 = cudaStreamSynchronize(cs);
     cudaError_t e4 = cudaStreamSynchronize(ctx->io_out);
     if (e == cudaSuccess) e = e2 != cudaSuccess ? e2 : e3 != cudaSuccess ? e3 : e4;
     if (!rc && e != cudaSuccess) {
-        qw6h_set_err("qw6cu_moe_prefill_hostio: %s", cudaGetErrorString(e));
+        qw6h_set_err("%s: %s", what, cudaGetErrorString(e));
         rc = QW6CU_ERR_CUDA;
     }
     return rc;
+}
+
+typedef struct {
+    qw6cu_ctx *ctx;
+    const qw6cu_expert_pack *gate, *up, *down;
+    uint32_t ntok, hidden, inter, n_experts, top_k;
+} prefill_job;
+
+static int prefill_job_run(void *arg, const float *logits, const void *x_bf16, float *out) {
+    const prefill_job *j = (const prefill_job *)arg;
+    return prefill_run(j->ctx, j->gate, j->up, j->down, logits, x_bf16, out, j->ntok, j->hidden, j->inter,
+                       j->n_experts, j->top_k);
+}
+
+int qw6cu_moe_prefill_hostio(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
+                             const qw6cu_expert_pack *down, const float *const *logits, const void *const *x_bf16,
+                             float *const *out, uint32_t n_batches, uint32_t ntok, uint32_t hidden, uint32_t inter,
+                             uint32_t n_experts, uint32_t top_k) {
+    int rc = qw6h_use(ctx);
+    if (rc) return rc;
+    if (!gate || !up || !down || gate->quant != up->quant) {
+        qw6h_set_err("qw6cu_moe_prefill_hostio: gate and up packs must be given and share one quant type");
+        return QW6CU_ERR_ARG;
+    }
+    /* the workspace and the error word at their full size before the first
+     * copy (growing one later would synchronize inside the pipeline) */
+    if (n_batches &&
+        (!qw6h_dev_err(ctx) ||
+         !qw6h_buf(ctx, QW6H_BUF_WS, qw6k_moe_prefill_ws_bytes(ntok, hidden, inter, n_experts, top_k))))
+        return QW6CU_ERR_NOMEM;
+    prefill_job j = {ctx, gate, up, down, ntok, hidden, inter, n_experts, top_k};
+    return qw6h_hostio_run(ctx, "qw6cu_moe_prefill_hostio", logits, x_bf16, out, n_batches,
+                           (size_t)ntok * n_experts * 4, (size_t)ntok * hidden * 2, (size_t)ntok * hidden * 4,
+                           prefill_job_run, &j);
 }
 
 int qw6cu_moe_expert_rows(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,

@@ -259,6 +259,13 @@ class PeerMoE:
         self.ep.layer(*(packs or self.packs), logits.data_ptr(), x_bf16.data_ptr(), out.data_ptr(), ntok)
         return out
 
+    def hostio(self, logits_host, x_host, out_host, ntok: int, packs: tuple | None = None) -> None:
+        """Layer steps whose inputs and outputs are in host memory (one host
+        address per step in each sequence; qw6cu_ep_layer_hostio): copies
+        pipelined with the steps on the context's stream, synchronous."""
+        self.ctx.set_stream(torch.cuda.current_stream(self.device).cuda_stream or _CUDA_STREAM_LEGACY)
+        self.ep.layer_hostio(*(packs or self.packs), logits_host, x_host, out_host, ntok)
+
     def last_rows(self) -> int:
         return self.ep.last_rows()
 

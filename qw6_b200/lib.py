@@ -168,6 +168,8 @@ def load() -> C.CDLL:
     lib.qw6cu_ep_handle.argtypes = [_vp, _vp]
     lib.qw6cu_ep_connect.argtypes = [_vp, _vp]
     lib.qw6cu_ep_layer.argtypes = [_vp, pk, pk, pk, _vp, _vp, _vp, _u32]
+    lib.qw6cu_ep_layer_hostio.argtypes = [_vp, pk, pk, pk, C.POINTER(_vp), C.POINTER(_vp), C.POINTER(_vp), _u32,
+                                          _u32]
     lib.qw6cu_ep_set_placement.argtypes = [_vp, _vp]
     lib.qw6cu_ep_last_rows.argtypes = [_vp, C.POINTER(_u32)]
     lib.qw6cu_ep_set_wait_limit.argtypes = [_vp, _u32]
@@ -444,6 +446,16 @@ class PeerEP:
     def layer(self, gate: ExpertPack, up: ExpertPack, down: ExpertPack, logits, x_bf16, out, ntok) -> None:
         _check(self.lib.qw6cu_ep_layer(self.h, C.byref(gate), C.byref(up), C.byref(down), logits, x_bf16, out, ntok),
                "qw6cu_ep_layer")
+
+    def layer_hostio(self, gate: ExpertPack, up: ExpertPack, down: ExpertPack, logits, x_bf16, out, ntok) -> None:
+        """qw6cu_ep_layer_hostio: `logits`, `x_bf16`, `out` are equal-length
+        sequences of HOST addresses, one entry per layer step."""
+        n = len(logits)
+        if len(x_bf16) != n or len(out) != n:
+            raise ValueError("layer_hostio: logits, x_bf16 and out need one host address per step")
+        arr = lambda v: (_vp * max(n, 1))(*[int(p) for p in v])  # noqa: E731
+        _check(self.lib.qw6cu_ep_layer_hostio(self.h, C.byref(gate), C.byref(up), C.byref(down), arr(logits),
+                                              arr(x_bf16), arr(out), n, ntok), "qw6cu_ep_layer_hostio")
 
     def set_placement(self, experts) -> None:
         """experts: n_experts routed expert ids, rank r's local experts at

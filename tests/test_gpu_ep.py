@@ -93,6 +93,15 @@ def _rank(rank, world, port, case, q):
         ctx.check_device_errors()
         peer.append(gout.cpu().numpy())
         del g
+        # ... and steps whose inputs and outputs are in host memory, pipelined
+        # over the two device slots (qw6cu_ep_layer_hostio)
+        hl = torch.from_numpy(logits[sl]).pin_memory()
+        hx = torch.from_numpy(xbits[sl].view(np.int16)).pin_memory()
+        ho = [torch.full((tpr, H), float("nan")).pin_memory() for _ in range(3)]
+        torch.cuda.synchronize()
+        pm.hostio([hl.data_ptr()] * 3, [hx.data_ptr()] * 3, [o.data_ptr() for o in ho], tpr)
+        ctx.check_device_errors()
+        peer += [ho[0].numpy().copy(), ho[2].numpy().copy()]
         pm.close()
         # experts placed by a (seeded) permutation instead of contiguous blocks
         pl = np.random.Generator(np.random.PCG64(77)).permutation(E).reshape(world, epr).astype(np.int32)
@@ -156,7 +165,8 @@ def test_ep_prefill_nccl(world, case, oracle):
     out = np.concatenate([got[r][0] for r in range(world)])
     full = got[0][2]
     assert np.array_equal(out.view(np.uint32), full.view(np.uint32)), float(np.max(np.abs(out - full)))
-    for i in range(6):  # three eager peer steps, the graph replay, the permuted placement (peer, NCCL)
+    for i in range(8):  # three eager peer steps, the graph replay, two host-buffer steps, the permuted placement
+        # (peer, NCCL)
         peer = np.concatenate([got[r][1][i] for r in range(world)])
         assert np.array_equal(peer.view(np.uint32), full.view(np.uint32)), (i, float(np.nanmax(np.abs(peer - full))))
     gate, up, down, logits, xbits = _data(case)
