@@ -391,6 +391,7 @@ def ep_bench(args, torch, ctx, L, stream, rank, world, dist, c3):
     # step s+1 and read-back of step s-1 beside the experts of step s): one
     # call of the C ABI's host-buffer entry point over all ke steps
     # (qw6cu_moe_prefill_hostio; N>1 qw6cu_ep_layer_hostio on every rank).
+    host_cpus = bind_host_near_gpu(torch, torch.cuda.current_device())
     nh = 4  # distinct page-locked host batches, used in turn
     h_lg = [torch.from_numpy(logits[sl]).pin_memory() for _ in range(nh)]
     h_x = [torch.from_numpy(xbits[sl].view(np.int16)).pin_memory() for _ in range(nh)]
@@ -421,11 +422,34 @@ def ep_bench(args, torch, ctx, L, stream, rank, world, dist, c3):
     del packs, copies
     torch.cuda.empty_cache()
     return {"ms": ms, "clk": clk, "prof": prof, "rows": rows, "e2e_ms": e2e_ms, "e2e_steps": ke, "graph_steps": G,
-            "h2d": tpr * NE * 4 + tpr * HIDDEN * 2, "d2h": tpr * HIDDEN * 4, "finite": out_ok, "same": same}
+            "h2d": tpr * NE * 4 + tpr * HIDDEN * 2, "d2h": tpr * HIDDEN * 4, "finite": out_ok, "same": same,
+            "host_cpus": len(host_cpus) if host_cpus else None}
 
 
 def local_rank_of(rank):
     return int(os.environ.get("LOCAL_RANK", rank))
+
+
+def bind_host_near_gpu(torch, device):
+    """Run this thread on the CPUs of the GPU's PCIe root (sysfs local_cpulist
+    of the device), so that page-locked buffers allocated afterwards come from
+    that NUMA node's memory: host<->device copies from the other socket's
+    memory run at about half the rate.  Returns the CPU list, or None when
+    sysfs does not say."""
+    p = torch.cuda.get_device_properties(device)
+    path = Path(f"/sys/bus/pci/devices/{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0/local_cpulist")
+    try:
+        cpus = set()
+        for part in path.read_text().strip().split(","):
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        cpus &= os.sched_getaffinity(0)
+        if not cpus:
+            return None
+        os.sched_setaffinity(0, cpus)
+        return sorted(cpus)
+    except (OSError, ValueError):
+        return None
 
 
 IQ2XXS_BYTES_EXPERT = 512 * 8 * 66                            # one IQ2_XXS expert matrix (gate, up or down)
@@ -810,7 +834,9 @@ def report(args, world, head, cpu):
                          "back (per-rank bytes), pipelined over two device slots -- step s+1's copy-in and step "
                          "s-1's read-back run beside step s's experts; the timed region ends when the last "
                          "output is in host memory",
-                "output_finite": head["finite"], "output_equals_device_steps": head["same"]},
+                "output_finite": head["finite"], "output_equals_device_steps": head["same"],
+                "host_binding": (f"page-locked buffers from the NUMA node of the GPU's PCIe root ({head['host_cpus']} "
+                                 "local CPUs)") if head["host_cpus"] else "unbound (no sysfs CPU list)"},
         "gpu_launches": int(launches * K),
         "clocks": head["clk"],
         "cpu_baseline": cpu,

@@ -234,7 +234,7 @@ size_t qw6cu_moe_workspace_bytes(uint32_t ntok, uint32_t hidden, uint32_t inter,
  * writes every assignment's bf16 expert output and a combine sums
  * w_e * output in slot order with fp32 fma, so results do not depend on
  * scheduling.  x_bf16: [ntok x hidden] bf16 (device); out: fp32
- * [ntok x hidden], overwritten.  Tolerance vs the fp32 CPU composition:
+ * [ntok x hidden], overwritten; both 16-byte aligned.  Tolerance vs the fp32 CPU composition:
  * 2e-2.  gate/up/down quant: Q4_K or Q6_K; hidden, inter multiples of 256. */
 int qw6cu_moe_prefill(qw6cu_ctx *ctx, const qw6cu_expert_pack *gate, const qw6cu_expert_pack *up,
                       const qw6cu_expert_pack *down, const float *logits, const void *x_bf16, float *out,

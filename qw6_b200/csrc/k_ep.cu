@@ -417,19 +417,33 @@ __global__ void k_ep_signal_done(const qw6k_ep_desc d) {
 // have written each assignment's bf16 output into this rank's ret
 __global__ void k_ep_combine_ret(const qw6k_ep_desc d) {
     pdl_grid_wait();
-    const int t = blockIdx.y, f = (blockIdx.x * blockDim.x + threadIdx.x) * 2;
+    const int t = blockIdx.y, f = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
     if (f >= (int)d.hidden || *d.abort) return;
     const int topk = (int)d.topk;
     const __nv_bfloat16* ret = reinterpret_cast<const __nv_bfloat16*>(d.peers[d.rank] + d.o_ret);
-    float o0 = 0.f, o1 = 0.f;
-    for (int k = 0; k < topk; k++) {
-        const size_t a = (size_t)t * topk + k;
-        const unsigned int bits = __ldcg(reinterpret_cast<const unsigned int*>(ret + a * d.hidden + f));
-        const float wk = d.w[a];
-        o0 = fmaf(wk, __uint_as_float(bits << 16), o0);
-        o1 = fmaf(wk, __uint_as_float(bits & 0xffff0000u), o1);
+    // 8 features per thread: one 16-byte load per slot, all issued before the sums
+    float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int k0 = 0; k0 < topk; k0 += 8) {
+        uint4 v[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++)
+            if (k0 + k < topk)
+                v[k] = __ldcg(reinterpret_cast<const uint4*>(ret + ((size_t)t * topk + k0 + k) * d.hidden + f));
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            if (k0 + k >= topk) break;
+            const float wk = d.w[(size_t)t * topk + k0 + k];
+            const uint32_t u[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                o[2 * i] = fmaf(wk, __uint_as_float(u[i] << 16), o[2 * i]);
+                o[2 * i + 1] = fmaf(wk, __uint_as_float(u[i] & 0xffff0000u), o[2 * i + 1]);
+            }
+        }
     }
-    *reinterpret_cast<float2*>(d.out + (size_t)t * d.hidden + f) = make_float2(o0, o1);
+    float4* op = reinterpret_cast<float4*>(d.out + (size_t)t * d.hidden + f);
+    op[0] = make_float4(o[0], o[1], o[2], o[3]);
+    op[1] = make_float4(o[4], o[5], o[6], o[7]);
 }
 
 }  // namespace qw6
@@ -479,6 +493,7 @@ extern "C" int qw6k_ep_p2p_phase(const qw6k_ep_desc* d, int phase, cudaStream_t 
         !d->local_cnt || !d->send_row || !d->x || !d->out || !d->cap || !d->nmax || d->ntok * d->topk > d->nmax ||
         !d->ucnt || !d->upos || !d->ubase || !d->eslot)
         return QW6K_ERR_ARG;
+    if (reinterpret_cast<uintptr_t>(d->out) & 15u) return QW6K_ERR_ALIGN;  // 16-byte stores in the combine
     // every phase is launched as a programmatic dependent of the previous
     // kernel on the stream; the counters of phase 6 are zeroed at create and
     // re-zeroed by phase 0 once consumed
@@ -510,7 +525,7 @@ extern "C" int qw6k_ep_p2p_phase(const qw6k_ep_desc* d, int phase, cudaStream_t 
         e = launch_pdl(k_ep_wait, dim3(1), dim3(64), 0, st, *d, (int)QW6K_EP_SIG_DONE);
         break;
     case 5:
-        e = launch_pdl(k_ep_combine_ret, dim3((d->hidden / 2 + 255) / 256, d->ntok), dim3(256), 0, st, *d);
+        e = launch_pdl(k_ep_combine_ret, dim3((d->hidden / 8 + 255) / 256, d->ntok), dim3(256), 0, st, *d);
         break;
     default:
         return QW6K_ERR_ARG;

@@ -634,21 +634,37 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfArgs a) {
 }
 
 // out[t][f] = sum_k w[t,k] * dout[t*topk + k][f], fp32 in slot order k
-// (rows mode: out[r] = w[r] * dout[r]).
+// (rows mode: out[r] = w[r] * dout[r]).  A thread takes 8 features of one
+// token: one 16-byte load per slot, all slots' loads issued before the sums.
+__device__ __forceinline__ void acc_bf16x8(float (&o)[8], float w, const uint4& v) {
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        o[2 * i] = fmaf(w, __uint_as_float(u[i] << 16), o[2 * i]);
+        o[2 * i + 1] = fmaf(w, __uint_as_float(u[i] & 0xffff0000u), o[2 * i + 1]);
+    }
+}
+
 __global__ void k_pf_combine(const PfArgs a) {
     pdl_trigger_dependents();
     pdl_grid_wait();
-    const int t = blockIdx.y, f = (blockIdx.x * blockDim.x + threadIdx.x) * 2;
+    const int t = blockIdx.y, f = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
     if (f >= a.hidden) return;
-    float o0 = 0.f, o1 = 0.f;
-    for (int k = 0; k < a.topk; k++) {
-        const size_t s = (size_t)t * a.topk + k;
-        const float w = a.w[s];
-        const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(a.dout + s * a.hidden + f);
-        o0 = fmaf(w, __bfloat162float(v.x), o0);
-        o1 = fmaf(w, __bfloat162float(v.y), o1);
+    float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const size_t s0 = (size_t)t * a.topk;
+    if (a.topk == 8) {
+        uint4 v[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) v[k] = *reinterpret_cast<const uint4*>(a.dout + (s0 + k) * a.hidden + f);
+#pragma unroll
+        for (int k = 0; k < 8; k++) acc_bf16x8(o, a.w[s0 + k], v[k]);
+    } else {
+        for (int k = 0; k < a.topk; k++)
+            acc_bf16x8(o, a.w[s0 + k], *reinterpret_cast<const uint4*>(a.dout + (s0 + k) * a.hidden + f));
     }
-    *reinterpret_cast<float2*>(a.out + (size_t)t * a.hidden + f) = make_float2(o0, o1);
+    float4* op = reinterpret_cast<float4*>(a.out + (size_t)t * a.hidden + f);
+    op[0] = make_float4(o[0], o[1], o[2], o[3]);
+    op[1] = make_float4(o[4], o[5], o[6], o[7]);
 }
 
 }  // namespace qw6
@@ -681,9 +697,9 @@ static int pf_args(const qw6k_moe_desc* d, int* err, PfArgs& a) {
     if (d->gq != QW6F_Q4_K_M && d->gq != QW6F_Q4_K_S && d->gq != QW6F_Q6_K) return QW6K_ERR_QUANT;
     if (d->dq != QW6F_Q4_K_M && d->dq != QW6F_Q4_K_S && d->dq != QW6F_Q6_K) return QW6K_ERR_QUANT;
     if (d->ws_bytes < qw6k_moe_prefill_ws_bytes(d->ntok, d->hidden, d->inter, d->ne, d->topk)) return QW6K_ERR_ARG;
-    if ((reinterpret_cast<uintptr_t>(d->x) | reinterpret_cast<uintptr_t>(d->gate) |
-         reinterpret_cast<uintptr_t>(d->up) | reinterpret_cast<uintptr_t>(d->down) | d->gstride | d->ustride |
-         d->dstride) & 15u)
+    if ((reinterpret_cast<uintptr_t>(d->x) | reinterpret_cast<uintptr_t>(d->out) |
+         reinterpret_cast<uintptr_t>(d->gate) | reinterpret_cast<uintptr_t>(d->up) |
+         reinterpret_cast<uintptr_t>(d->down) | d->gstride | d->ustride | d->dstride) & 15u)
         return QW6K_ERR_ALIGN;
     a.gate = (const uint8_t*)d->gate;
     a.up = (const uint8_t*)d->up;
@@ -791,7 +807,7 @@ extern "C" int qw6k_moe_prefill_phase(const qw6k_moe_desc* d, int* err, int phas
         return (d->dq == QW6F_Q6_K) ? launch_pf<QW6F_Q6_K, 1>(a, mi, st) : launch_pf<QW6F_Q4_K_M, 1>(a, mi, st);
     case 6: {
         if (!d->logits) return 0;  // rows mode: the caller combines
-        dim3 g((a.hidden / 2 + 255) / 256, a.ntok);
+        dim3 g((a.hidden / 8 + 255) / 256, a.ntok);
         if (launch_pdl(k_pf_combine, g, dim3(256), 0, st, a) != cudaSuccess) return QW6K_ERR_CUDA;
         break;
     }
