@@ -12,7 +12,7 @@
 //               programmatic dependent launch: it routes and prefetches its
 //               weights while gate/up runs);
 //   ntok > 4    four launches: plan (route every token, group the (token,
-//               slot) assignments by expert with a stable counting sort, cut
+//               slot) assignments by expert with a counting sort, cut
 //               each expert's list into work items), gate/up per item,
 //               down per item, slot-order combine (k_moe_plan, k_moe_gateup,
 //               k_moe_down, k_moe_combine).
@@ -49,8 +49,8 @@ struct MoeArgs {
 };
 
 // ------------------------------------------------------------------ plan --
-__global__ void __launch_bounds__(512) k_moe_plan(const MoeArgs a) {
-    __shared__ int cnt[256], off[257], ich[257];
+__global__ void __launch_bounds__(1024) k_moe_plan(const MoeArgs a) {
+    __shared__ int cnt[256], off[257], ich[257], fill[256];
     __shared__ int sidx[4096];  // the routed expert of every assignment (ntok * topk <= 4096)
     pdl_wait();  // logits and the workspace are free to use
     pdl_trigger();
@@ -59,7 +59,7 @@ __global__ void __launch_bounds__(512) k_moe_plan(const MoeArgs a) {
     for (int t = warp; t < a.ntok; t += nw)
         route_token(a.logits + (size_t)t * a.ne, a.ne, a.topk, a.idx + (size_t)t * a.topk, a.w + (size_t)t * a.topk,
                     lane);
-    for (int e = tid; e < 256; e += blockDim.x) cnt[e] = 0;
+    for (int e = tid; e < 256; e += blockDim.x) cnt[e] = fill[e] = 0;
     __syncthreads();
     for (int i = tid; i < TK; i += blockDim.x) {
         const int e = a.idx[i];
@@ -91,12 +91,12 @@ __global__ void __launch_bounds__(512) k_moe_plan(const MoeArgs a) {
         if (tid == 255) { off[256] = bv + v; ich[256] = bc + ch; *a.nitems = bc + ch; }
     }
     __syncthreads();
-    // stable counting sort: rank = earlier assignments with the same expert
+    // counting sort: an assignment's place among its expert's is the order of
+    // the shared-memory atomics.  No value depends on it: every token of an
+    // item is staged, multiplied (its own MMA column) and combined on its own.
     for (int i = tid; i < TK; i += blockDim.x) {
         const int e = sidx[i];
-        int r = 0;
-        for (int j = 0; j < i; j++) r += sidx[j] == e;
-        a.order[off[e] + r] = i;
+        a.order[off[e] + atomicAdd(&fill[e], 1)] = i;
     }
     for (int e = tid; e < a.ne; e += blockDim.x) {
         const int n = cnt[e];
@@ -639,11 +639,19 @@ static int moe_items_max(uint32_t ntok, uint32_t ne, uint32_t topk, uint32_t chu
     return (int)((tk < ne ? tk : ne) + tk / chunk + 1);
 }
 
-static uint32_t moe_chunk(uint32_t ntok) { return ntok <= 4 ? 4u : 8u; }
+// Assignments per work item of the planned path: 4 (one MMA n-tile) while
+// experts average at most 3 assignments (config 2: 512 over 256), else 8.
+// An item's tile-blocks are decoded once for all its tokens, so a larger
+// chunk shares the (instruction-bound) IQ / K decode among more tokens, but
+// costs a second n-tile of MMAs and activation staging for every item,
+// mostly empty when experts see ~2 tokens.
+static uint32_t moe_chunk(uint32_t ntok, uint32_t ne, uint32_t topk) {
+    return (ntok <= 4 || (uint64_t)ntok * topk <= 3ull * ne) ? 4u : 8u;
+}
 
 extern "C" size_t qw6k_moe_ws_bytes(uint32_t ntok, uint32_t hidden, uint32_t inter, uint32_t ne, uint32_t topk) {
     const size_t tk = (size_t)ntok * topk;
-    const int mi = moe_items_max(ntok, ne, topk, moe_chunk(ntok));
+    const int mi = moe_items_max(ntok, ne, topk, moe_chunk(ntok, ne, topk));
     return al256(tk * 4) * 3 + al256((size_t)mi * 16) + 256 + al256(tk * inter * 4) + al256(tk * hidden * 4);
 }
 
@@ -685,7 +693,7 @@ static int moe_args(const qw6k_moe_desc* d, MoeArgs& a) {
     a.inter = (int)d->inter;
     a.ne = (int)d->ne;
     a.topk = (int)d->topk;
-    a.chunk = (int)moe_chunk(d->ntok);
+    a.chunk = (int)moe_chunk(d->ntok, d->ne, d->topk);
     const size_t tk = (size_t)d->ntok * d->topk;
     const int mi = moe_items_max(d->ntok, d->ne, d->topk, (uint32_t)a.chunk);
     uint8_t* p = (uint8_t*)d->ws;
@@ -742,7 +750,7 @@ extern "C" int qw6k_moe_phase(const qw6k_moe_desc* d, int phase, cudaStream_t st
     const int nq = a.chunk / 4;
     switch (phase) {
     case 0:
-        return launch_pdl(k_moe_plan, dim3(1), dim3(512), 0, st, a) == cudaSuccess ? 0 : QW6K_ERR_CUDA;
+        return launch_pdl(k_moe_plan, dim3(1), dim3(1024), 0, st, a) == cudaSuccess ? 0 : QW6K_ERR_CUDA;
     case 1:
         return gateup_any(d->gq, nq, a, mi, st);
     case 2:

@@ -140,3 +140,8 @@ def test_prefill_hostio_pipelined(cuda, oracle, rng):
     assert same_bits(p_out[0], ref[2]) and same_bits(p_out[1], ref[0])
     toks = list(rng.choice(T, 24, replace=False))
     check_tokens(oracle, S.Q4_K, gate, up, S.Q6_K, down, lgs[3], xbs[3], h_out[3].numpy(), toks, K)
+    # no batches: nothing to do; a null host buffer: rejected before any copy
+    cuda.moe_prefill_hostio(*packs, [], [], [], T, H, I, E, K)
+    with pytest.raises(L.Qw6CudaError, match="null host buffer of batch 1"):
+        cuda.moe_prefill_hostio(*packs, [h_lg[0].data_ptr()] * 2, [h_x[0].data_ptr(), 0],
+                                [o.data_ptr() for o in h_out[:2]], T, H, I, E, K)
