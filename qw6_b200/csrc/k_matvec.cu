@@ -425,6 +425,10 @@ static int launch_mv(const uint8_t* w, const float* x, float* y, int rows, int c
     const int slots = num_sms() * occ * kWarps;  // resident warps
     int ks = 1;
     while (ks < 8 && a.nb % (ks * 2) == 0 && (long long)a.mtiles * ks < slots) ks *= 2;
+    // The fused argmax keeps ks = 1: each row's logit is then summed block by
+    // block in one warp, whatever the row count, so row shards of one
+    // vocabulary give the same bits as the whole and combine exactly.
+    if (KEYS) ks = 1;
     a.ks = ks;
     const int wpm = kWarps / ks;
     const long long ngrp = (a.mtiles + wpm - 1) / wpm;

@@ -57,9 +57,11 @@ def test_lm_head_argmax_vs_oracle(q, ntok, cuda, oracle, rng):
         assert idx[t] == int(np.argmax(lg[t]))
 
 
-@pytest.mark.parametrize("shards", [2, 3, 8])
-def test_lm_head_row_shards_combine_exactly(shards, cuda, rng):
-    rows, cols, ntok = 4096, 2048, 5
+@pytest.mark.parametrize("shards,rows", [(2, 4096), (3, 4096), (8, 4096), (2, 37888), (8, 37888)])
+def test_lm_head_row_shards_combine_exactly(shards, rows, cuda, rng):
+    """Row shards give the whole vocabulary's bits; 37888 rows is where a
+    split factor chosen by row count would differ between whole and shards."""
+    cols, ntok = 2048, 5
     w = S.make_matrix(S.Q6_K, rows, cols, rng)
     x = rng.standard_normal((ntok, cols), dtype=np.float32)
     i1, v1, _ = lm_head(cuda, S.Q6_K, w, x, rows, cols, shards=1)
