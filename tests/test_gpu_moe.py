@@ -7,7 +7,7 @@ import pytest
 
 from qw6_b200 import lib as L
 from qw6_b200 import synth as S
-from tests.conftest import rel_err
+from tests.conftest import rel_err, same_bits
 from tests.gpu_util import dev, empty_f32, host, pack, sync
 from tests.test_golden import golden_moe_weights
 
@@ -143,3 +143,32 @@ def test_moe_format_mixes(gq, dq, cuda, oracle, rng):
     ref, _, _ = oracle.moe_layer(gq, gate, up, dq, down, logits, x, top_k=K)
     for t in range(T):
         assert rel_err(out[t], ref[t]) <= TOL, t
+
+
+@pytest.mark.parametrize("ntok", [1, 12])
+def test_moe_decode_hostio(ntok, cuda, oracle, rng):
+    """qw6cu_moe_decode_hostio with host buffers, page-locked and pageable,
+    gives qw6cu_moe_decode's bits on the two-launch path (1 token) and the
+    planned one (12 tokens), also when a call reuses the context's buffers."""
+    torch = pytest.importorskip("torch")
+    E, H, I, K = 32, 2048, 512, 8
+    gate, up, down = S.moe_weights(rng, E, S.Q4_K, S.Q6_K, H, I)
+    logits = rng.standard_normal((ntok, E), dtype=np.float32)
+    x = rng.standard_normal((ntok, H), dtype=np.float32)
+    want = run_moe(cuda, S.Q4_K, gate, up, S.Q6_K, down, logits, x, K)
+    pg, sg = pack(cuda, S.Q4_K, gate, I, H, E)
+    pu, su = pack(cuda, S.Q4_K, up, I, H, E)
+    pd, sd = pack(cuda, S.Q6_K, down, H, I, E)
+    packs = (L.ExpertPack(S.Q4_K, pg.data_ptr(), sg), L.ExpertPack(S.Q4_K, pu.data_ptr(), su),
+             L.ExpertPack(S.Q6_K, pd.data_ptr(), sd))
+    sync(cuda)
+    h_lg, h_x = torch.from_numpy(logits).pin_memory(), torch.from_numpy(x).pin_memory()
+    for _ in range(2):  # the second call reuses the context's buffers
+        h_out = torch.full((ntok, H), float("nan")).pin_memory()
+        cuda.moe_decode_hostio(*packs, h_lg.data_ptr(), h_x.data_ptr(), h_out.data_ptr(), ntok, H, I, E, K)
+        assert same_bits(h_out.numpy(), want)
+    p_out = np.full((ntok, H), np.nan, np.float32)
+    cuda.moe_decode_hostio(*packs, logits.ctypes.data, x.ctypes.data, p_out.ctypes.data, ntok, H, I, E, K)
+    assert same_bits(p_out, want)
+    ref, _, _ = oracle.moe_layer(S.Q4_K, gate, up, S.Q6_K, down, logits, x, top_k=K)
+    assert max(rel_err(want[t], ref[t]) for t in range(ntok)) <= TOL
